@@ -1,0 +1,174 @@
+"""bissimamba_b200 -- B200-native k-mamba scanND / convND hot path.
+
+The product is the C-ABI shared library ``libkmamba_b200.so`` (declared in
+``include/scan_nd.h`` and ``include/convnd.h``).  This module only binds it
+with ctypes, mirroring the reference's C interface (``ScanNDParams``,
+``scannd()``, ``om_scannd_forward/backward``, ``ConvNDParams``, ``convnd()``)
+so Python callers and the tests use the same entry points a C caller links.
+
+There is no CPU fallback: if the library is missing, ``lib()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkmamba_b200.so")
+
+_f = C.POINTER(C.c_float)
+_l = C.POINTER(C.c_long)
+
+
+class ScanNDParams(C.Structure):
+    """Same field order and types as the reference include/scan_nd.h:40-69."""
+    _fields_ = [
+        ("max_ndims", C.c_long), ("max_state", C.c_long), ("use_fast_exp", C.c_int),
+        ("dims", _l), ("ndims", C.c_long), ("D", C.c_long), ("M", C.c_long),
+        ("x", C.c_void_p), ("A", C.c_void_p), ("B", C.c_void_p), ("C", C.c_void_p),
+        ("delta", C.c_void_p), ("h", C.c_void_p), ("y", C.c_void_p),
+        ("theta", C.c_void_p), ("lambda_", C.c_void_p),
+        ("default_lambda", C.c_float), ("use_a_log_clamp", C.c_int), ("a_log_min", C.c_float),
+        ("dA", C.c_void_p), ("dB", C.c_void_p), ("dC", C.c_void_p), ("ddelta", C.c_void_p),
+        ("dlambda", C.c_void_p), ("dtheta", C.c_void_p),
+    ]
+
+
+class ConvNDParams(C.Structure):
+    """Same layout as the reference include/convnd.h:10-23."""
+    _fields_ = [
+        ("input", C.c_void_p), ("kernel", C.c_void_p), ("bias", C.c_void_p),
+        ("output", C.c_void_p), ("dy", C.c_void_p), ("dinput", C.c_void_p),
+        ("dkernel", C.c_void_p), ("dbias", C.c_void_p), ("dims", _l),
+        ("ndims", C.c_long), ("D", C.c_long), ("K", C.c_long),
+    ]
+
+
+CONVND_FORWARD, CONVND_BACKWARD, CONVND_COMPLETE = 1, 2, 3
+
+# every symbol the public headers declare (checked by the CPU tests)
+EXPORTS = [
+    "scannd_validate", "scannd", "scannd_ref_with_plan", "om_scannd_forward", "om_scannd_backward",
+    "scannd_batched", "scannd_backward_batched", "scannd_forward_async", "scannd_backward_async",
+    "convnd_kernel_volume", "convnd_forward_wavefront", "convnd_backward_wavefront", "convnd",
+    "om_convnd_forward", "om_convnd_backward", "convnd_status", "convnd_batched_async",
+    "wavefront_nd_validate_dims", "wavefront_nd_total_points", "wavefront_nd_max_level",
+    "wavefront_nd_row_major_offset", "wavefront_nd_level_size", "wavefront_nd_for_level",
+    "wavefront_nd_for_each_level", "km_wavefront_plan_create", "km_wavefront_plan_free",
+    "km_wavefront_plan_matches_dims", "km_wavefront_plan_level_size", "km_wavefront_plan_level_offsets",
+    "km_wavefront_plan_iter_forward", "km_wavefront_plan_iter_reverse",
+    "kmb_last_error", "kmb_last_forward_path", "kmb_set_force_generic",
+]
+
+_lib = None
+
+
+def lib():
+    """Load libkmamba_b200.so (build it first with ``bissimamba_b200.build``)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m bissimamba_b200.build` "
+                               "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        P = C.POINTER(ScanNDParams)
+        Q = C.POINTER(ConvNDParams)
+        for n in ("scannd_validate", "scannd", "om_scannd_forward", "om_scannd_backward"):
+            getattr(L, n).argtypes = [P]
+            getattr(L, n).restype = C.c_int
+        L.scannd_batched.argtypes = [P, C.c_long]
+        L.scannd_backward_batched.argtypes = [P, C.c_long, C.c_void_p]
+        L.scannd_forward_async.argtypes = [P, C.c_long, C.c_void_p]
+        L.scannd_backward_async.argtypes = [P, C.c_long, C.c_void_p, C.c_void_p]
+        L.scannd_ref_with_plan.argtypes = [P, C.c_void_p]
+        L.convnd.argtypes = [Q, C.c_int]
+        L.convnd.restype = None
+        L.convnd_batched_async.argtypes = [Q, C.c_long, C.c_int, C.c_void_p]
+        L.om_convnd_forward.argtypes = [Q]
+        L.om_convnd_backward.argtypes = [Q]
+        L.convnd_forward_wavefront.argtypes = [Q, C.c_void_p]
+        L.convnd_forward_wavefront.restype = None
+        L.convnd_backward_wavefront.argtypes = [Q, C.c_void_p]
+        L.convnd_backward_wavefront.restype = None
+        L.convnd_kernel_volume.argtypes = [C.c_long, C.c_long]
+        L.convnd_kernel_volume.restype = C.c_long
+        L.kmb_last_error.restype = C.c_char_p
+        L.kmb_set_force_generic.argtypes = [C.c_int]
+        L.kmb_set_force_generic.restype = None
+        L.km_wavefront_plan_create.argtypes = [_l, C.c_long, C.c_long]
+        L.km_wavefront_plan_create.restype = C.c_void_p
+        L.km_wavefront_plan_free.argtypes = [C.c_void_p]
+        L.km_wavefront_plan_level_size.argtypes = [C.c_void_p, C.c_long]
+        L.km_wavefront_plan_level_size.restype = C.c_long
+        L.km_wavefront_plan_level_offsets.argtypes = [C.c_void_p, C.c_long]
+        L.km_wavefront_plan_level_offsets.restype = _l
+        L.wavefront_nd_level_size.argtypes = [_l, C.c_long, C.c_long]
+        L.wavefront_nd_level_size.restype = C.c_long
+        L.wavefront_nd_total_points.argtypes = [_l, C.c_long]
+        L.wavefront_nd_total_points.restype = C.c_long
+        L.wavefront_nd_max_level.argtypes = [_l, C.c_long]
+        L.wavefront_nd_max_level.restype = C.c_long
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().kmb_last_error().decode()
+
+
+def _ptr(t):
+    """Data pointer of a tensor / numpy array / None."""
+    if t is None:
+        return None
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    return t.ctypes.data
+
+
+def dims_array(dims):
+    arr = (C.c_long * len(dims))(*[int(d) for d in dims])
+    return arr
+
+
+def scan_params(dims, D, M, x, A, B, Cm, delta, h, y, theta=None, lam=None, default_lambda=0.5,
+                use_fast_exp=0, use_a_log_clamp=0, a_log_min=-1e-5, grads=None):
+    """Build a ScanNDParams (single-item layout; batched calls use the same
+    struct with contiguous [batch, ...] buffers).  Keeps the dims array alive
+    on the returned object."""
+    p = ScanNDParams()
+    darr = dims_array(dims)
+    p._dims_keep = darr
+    p.max_ndims = 32
+    p.max_state = 0
+    p.use_fast_exp = int(use_fast_exp)
+    p.dims = C.cast(darr, _l)
+    p.ndims = len(dims)
+    p.D, p.M = int(D), int(M)
+    p.x, p.A, p.B, p.C, p.delta = _ptr(x), _ptr(A), _ptr(B), _ptr(Cm), _ptr(delta)
+    p.h, p.y = _ptr(h), _ptr(y)
+    p.theta, p.lambda_ = _ptr(theta), _ptr(lam)
+    p.default_lambda = float(default_lambda)
+    p.use_a_log_clamp = int(use_a_log_clamp)
+    p.a_log_min = float(a_log_min)
+    g = grads or {}
+    for k in ("dA", "dB", "dC", "ddelta", "dlambda", "dtheta"):
+        setattr(p, k, _ptr(g.get(k)))
+    return p
+
+
+def conv_params(dims, D, K, inp=None, kernel=None, bias=None, out=None, dy=None, dinput=None,
+                dkernel=None, dbias=None):
+    p = ConvNDParams()
+    darr = dims_array(dims)
+    p._dims_keep = darr
+    p.input, p.kernel, p.bias, p.output = _ptr(inp), _ptr(kernel), _ptr(bias), _ptr(out)
+    p.dy, p.dinput, p.dkernel, p.dbias = _ptr(dy), _ptr(dinput), _ptr(dkernel), _ptr(dbias)
+    p.dims = C.cast(darr, _l)
+    p.ndims = len(dims)
+    p.D, p.K = int(D), int(K)
+    return p
+
+
+def check(rc: int, what: str = "call"):
+    if rc != 0:
+        raise RuntimeError(f"{what} failed: {last_error()}")

@@ -1,0 +1,215 @@
+// convnd.cu -- dense causal depthwise convND (reference src/convnd.c:396-531).
+//
+// The convolution has no dependence between output points, so the reference's
+// level-by-level wavefront (one OpenMP region / one GPU launch per level) is
+// replaced by a single launch over all (item, point, channel) triples.  The
+// kernel is HBM-bound: 8 bytes per output (read input, write output) with the
+// K^nd taps served from L1/L2.
+//
+// Forward sums taps in ascending kernel-linear order starting from the bias,
+// the reference's order, so fp32 results match the reference bit-for-bit.
+// Backward keeps the reference's overwrite semantics (dinput, dkernel, dbias
+// are zeroed then filled, src/convnd.c:482-484): dinput is a gather with the
+// mirrored taps (no atomics); dkernel/dbias are per-chunk partial sums in
+// registers + shared memory, reduced across chunks in a fixed order
+// (deterministic).
+#include "kmb_common.cuh"
+
+namespace kmb {
+
+struct ConvDesc {
+    int nd, D, K, V;          // V = K^nd
+    long long P, batch;
+    long long dims[KMB_MAXND];
+    long long strides[KMB_MAXND];
+};
+
+__global__ void __launch_bounds__(256) conv_fwd_kernel(ConvDesc c, const float* __restrict__ in,
+                                                       const float* __restrict__ ker,
+                                                       const float* __restrict__ bias,
+                                                       float* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = c.batch * c.P * c.D;
+    if (i >= total) return;
+    const int d = (int)(i % c.D);
+    const long long bp = i / c.D;
+    const long long p = bp % c.P;
+    const long long b = bp / c.P;
+    int oc[KMB_MAXND], kd[KMB_MAXND];
+    for (int a = 0; a < c.nd; a++) {
+        oc[a] = (int)((p / c.strides[a]) % c.dims[a]);
+        kd[a] = 0;
+    }
+    const float* inb = in + b * c.P * c.D;
+    float sum = bias ? bias[d] : 0.0f;
+    for (int kl = 0; kl < c.V; kl++) {
+        long long src = 0;
+        bool ok = true;
+        for (int a = 0; a < c.nd; a++) {
+            const int sc = oc[a] - (c.K - 1 - kd[a]);
+            if (sc < 0) { ok = false; break; }
+            src += (long long)sc * c.strides[a];
+        }
+        if (ok) sum = __fmaf_rn(inb[src * c.D + d], ker[(long long)kl * c.D + d], sum);
+        for (int a = c.nd - 1; a >= 0; a--) {  // kernel-linear increment, last axis fastest
+            if (++kd[a] < c.K) break;
+            kd[a] = 0;
+        }
+    }
+    out[i] = sum;
+}
+
+// dinput[s,d] = sum_k dy[s + (K-1-k), d] * ker[k, d]   (gather form)
+__global__ void __launch_bounds__(256) conv_bwd_input_kernel(ConvDesc c, const float* __restrict__ dy,
+                                                             const float* __restrict__ ker,
+                                                             float* __restrict__ din) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = c.batch * c.P * c.D;
+    if (i >= total) return;
+    const int d = (int)(i % c.D);
+    const long long bp = i / c.D;
+    const long long s = bp % c.P;
+    const long long b = bp / c.P;
+    int sc[KMB_MAXND], kd[KMB_MAXND];
+    for (int a = 0; a < c.nd; a++) {
+        sc[a] = (int)((s / c.strides[a]) % c.dims[a]);
+        kd[a] = 0;
+    }
+    const float* dyb = dy + b * c.P * c.D;
+    float acc = 0.0f;
+    for (int kl = 0; kl < c.V; kl++) {
+        long long o = 0;
+        bool ok = true;
+        for (int a = 0; a < c.nd; a++) {
+            const long long oa = sc[a] + (c.K - 1 - kd[a]);
+            if (oa >= c.dims[a]) { ok = false; break; }
+            o += oa * c.strides[a];
+        }
+        if (ok) acc = __fmaf_rn(dyb[o * c.D + d], ker[(long long)kl * c.D + d], acc);
+        for (int a = c.nd - 1; a >= 0; a--) {
+            if (++kd[a] < c.K) break;
+            kd[a] = 0;
+        }
+    }
+    din[i] = acc;
+}
+
+// Partial dkernel / dbias over a chunk of (item, point) rows for 32 channels.
+// block = 32 channel lanes x 8 row-warps; grid = (ceil(D/32), nchunks).
+// part layout: [nchunks][V+1][D]  (row V holds dbias).
+constexpr int kTapsPerPass = 28;
+
+__global__ void __launch_bounds__(256) conv_bwd_kernel_partial(ConvDesc c, const float* __restrict__ in,
+                                                               const float* __restrict__ dy,
+                                                               float* __restrict__ part,
+                                                               long long rows_per_chunk) {
+    __shared__ float red[8][kTapsPerPass + 1][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int d = blockIdx.x * 32 + lane;
+    const long long r0 = (long long)blockIdx.y * rows_per_chunk;
+    const long long rows = c.batch * c.P;
+    const long long r1 = min(r0 + rows_per_chunk, rows);
+    const int npass = (c.V + kTapsPerPass - 1) / kTapsPerPass;
+    for (int pass = 0; pass < npass; pass++) {
+        const int t0 = pass * kTapsPerPass;
+        const int nt = min(kTapsPerPass, c.V - t0);
+        float acc[kTapsPerPass + 1];
+#pragma unroll
+        for (int t = 0; t <= kTapsPerPass; t++) acc[t] = 0.0f;
+        if (d < c.D) {
+            for (long long r = r0 + w; r < r1; r += 8) {
+                const long long p = r % c.P, b = r / c.P;
+                const float g = dy[r * c.D + d];
+                if (pass == 0) acc[kTapsPerPass] += g;
+                int oc[KMB_MAXND], kd[KMB_MAXND];
+                int tmp = t0;
+                for (int a = c.nd - 1; a >= 0; a--) {
+                    kd[a] = tmp % c.K;
+                    tmp /= c.K;
+                }
+                for (int a = 0; a < c.nd; a++) oc[a] = (int)((p / c.strides[a]) % c.dims[a]);
+                const float* inb = in + b * c.P * c.D;
+#pragma unroll
+                for (int t = 0; t < kTapsPerPass; t++) {
+                    if (t < nt) {
+                        long long src = 0;
+                        bool ok = true;
+                        for (int a = 0; a < c.nd; a++) {
+                            const int sc = oc[a] - (c.K - 1 - kd[a]);
+                            if (sc < 0) { ok = false; break; }
+                            src += (long long)sc * c.strides[a];
+                        }
+                        if (ok) acc[t] = __fmaf_rn(g, inb[src * c.D + d], acc[t]);
+                        for (int a = c.nd - 1; a >= 0; a--) {
+                            if (++kd[a] < c.K) break;
+                            kd[a] = 0;
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t <= kTapsPerPass; t++) red[w][t][lane] = acc[t];
+        __syncthreads();
+        for (int t = w; t <= kTapsPerPass; t += 8) {
+            float s = 0.0f;
+            for (int j = 0; j < 8; j++) s += red[j][t][lane];
+            if (d < c.D) {
+                if (t < nt) part[((long long)blockIdx.y * (c.V + 1) + t0 + t) * c.D + d] = s;
+                else if (t == kTapsPerPass && pass == 0)
+                    part[((long long)blockIdx.y * (c.V + 1) + c.V) * c.D + d] = s;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// out[i] = sum_j part[j*stride + i]  (overwrite)
+__global__ void reduce_rows_set(const float* __restrict__ part, float* __restrict__ out,
+                                long long count, long long n, long long stride) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    float acc = 0.0f;
+    for (long long j = 0; j < n; j++) acc += part[j * stride + i];
+    out[i] = acc;
+}
+
+static inline unsigned cblk(long long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+cudaError_t launch_conv_fwd(const ConvDesc& c, const float* in, const float* ker, const float* bias,
+                            float* out, cudaStream_t st) {
+    conv_fwd_kernel<<<cblk(c.batch * c.P * c.D, 256), 256, 0, st>>>(c, in, ker, bias, out);
+    return cudaGetLastError();
+}
+
+static long long conv_chunks(const ConvDesc& c) {
+    const long long rows = c.batch * c.P;
+    long long n = (rows + 255) / 256;  // >= 256 rows per chunk
+    return n < 1 ? 1 : (n > 1024 ? 1024 : n);
+}
+
+size_t conv_bwd_scratch_bytes(const ConvDesc& c) {
+    return (size_t)conv_chunks(c) * (c.V + 1) * c.D * sizeof(float);
+}
+
+cudaError_t launch_conv_bwd(const ConvDesc& c, const float* in, const float* ker, const float* dy,
+                            float* din, float* dker, float* dbias, void* scratch, cudaStream_t st) {
+    conv_bwd_input_kernel<<<cblk(c.batch * c.P * c.D, 256), 256, 0, st>>>(c, dy, ker, din);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const long long nch = conv_chunks(c);
+    const long long rows = c.batch * c.P;
+    const long long rpc = (rows + nch - 1) / nch;
+    float* part = (float*)scratch;
+    dim3 grid(cblk(c.D, 32), (unsigned)nch);
+    conv_bwd_kernel_partial<<<grid, 256, 0, st>>>(c, in, dy, part, rpc);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const long long cnt = (long long)c.V * c.D;
+    reduce_rows_set<<<cblk(cnt, 256), 256, 0, st>>>(part, dker, cnt, nch, (long long)(c.V + 1) * c.D);
+    if (dbias)
+        reduce_rows_set<<<cblk(c.D, 256), 256, 0, st>>>(part + (long long)c.V * c.D, dbias, c.D, nch,
+                                                       (long long)(c.V + 1) * c.D);
+    return cudaGetLastError();
+}
+
+}  // namespace kmb

@@ -1,0 +1,62 @@
+// kmb_common.cuh -- shared device/host helpers of libkmamba_b200.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define KMB_MAXND 16  // largest ndims the device kernels accept
+
+// Device status codes written by kernels into the caller-visible status word.
+enum KmbStatus : int {
+    KMB_OK = 0,
+    KMB_ERR_TIMEOUT_FULL = 1,   // a consumer gave up waiting for a staged tile
+    KMB_ERR_TIMEOUT_EMPTY = 2,  // the producer gave up waiting for a free stage
+    KMB_ERR_TIMEOUT_Y = 3,      // the reducer gave up waiting for the stage's states
+};
+
+// Scan-A problem description passed by value to the kernels.
+struct ScanDesc {
+    int nd;
+    int D, M;
+    int rope;            // theta != NULL
+    int has_lambda;      // lambda != NULL
+    int fast_exp;
+    int clamp;
+    float a_log_min;
+    float default_lambda;
+    long long P;         // points per item
+    long long batch;
+    long long dims[KMB_MAXND];
+    long long strides[KMB_MAXND];  // row-major point strides
+    const float* x;
+    const float* A;
+    const float* B;
+    const float* C;
+    const float* delta;
+    const float* theta;
+    const float* lambda;
+    float* h;
+    float* y;
+};
+
+// Clamped cubic Taylor exponential of the reference (include/km_topology.h:52-56)
+// or CUDA's accurate expf.
+__device__ __forceinline__ float kmb_exp(float z, int fast) {
+    if (fast) {
+        z = fminf(fmaxf(z, -8.0f), 8.0f);
+        return 1.0f + z + 0.5f * z * z + (1.0f / 6.0f) * z * z * z;
+    }
+    return expf(z);
+}
+
+// d/dz of kmb_exp given e = kmb_exp(z)
+__device__ __forceinline__ float kmb_dexp(float z, float e, int fast) {
+    if (fast) {
+        if (z > 8.0f || z < -8.0f) return 0.0f;
+        return 1.0f + z + 0.5f * z * z;
+    }
+    return e;
+}
+
+__device__ __forceinline__ float kmb_clampA(float a, int clamp, float amin) {
+    return (clamp && a > amin) ? amin : a;
+}

@@ -1,0 +1,18 @@
+/* kmamba_b200.h -- diagnostics of libkmamba_b200.so (no counterpart in the
+ * reference API; the reference reports errors only through return codes). */
+#ifndef KMB200_DIAG_H
+#define KMB200_DIAG_H
+#ifdef __cplusplus
+extern "C" {
+#endif
+/* Text of the last error raised on this host thread ("" if none). */
+const char *kmb_last_error(void);
+/* Which Scan-A forward kernel the last forward call on this thread used:
+ * 1 = persistent TMA kernel (1D/2D fast path), 0 = generic kernel, -1 = none. */
+int kmb_last_forward_path(void);
+/* 1 = route every forward through the generic kernel (tests / comparison). */
+void kmb_set_force_generic(int on);
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,337 @@
+"""TEST INFRASTRUCTURE ONLY -- ctypes access to the CPU checkers.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+--impl reference legs import this module.  It loads:
+
+* ``liboracle.so``           -- my C restatement (scannd_oracle.c, convnd_oracle.c)
+* ``_ref/libkmamba_ref.so``  -- the reference's own CPU sources compiled in place
+                               (built here from the read-only reference checkout;
+                               the built file travels with the repo snapshot).
+
+It also holds the seeded synthetic input generators (numpy), whose
+distributions follow the BASELINE configs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_SO = os.path.join(HERE, "_ref", "libkmamba_ref.so")
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SRC = "/root/reference"
+
+_f = C.POINTER(C.c_float)
+_l = C.POINTER(C.c_long)
+
+
+class ScanNDParams(C.Structure):
+    # identical field order to the reference include/scan_nd.h:40-69
+    _fields_ = [
+        ("max_ndims", C.c_long), ("max_state", C.c_long), ("use_fast_exp", C.c_int),
+        ("dims", _l), ("ndims", C.c_long), ("D", C.c_long), ("M", C.c_long),
+        ("x", _f), ("A", _f), ("B", _f), ("C", _f), ("delta", _f),
+        ("h", _f), ("y", _f), ("theta", _f), ("lambda_", _f),
+        ("default_lambda", C.c_float), ("use_a_log_clamp", C.c_int), ("a_log_min", C.c_float),
+        ("dA", _f), ("dB", _f), ("dC", _f), ("ddelta", _f), ("dlambda", _f), ("dtheta", _f),
+    ]
+
+
+class ConvNDParams(C.Structure):
+    # reference include/convnd.h:10-23
+    _fields_ = [
+        ("input", _f), ("kernel", _f), ("bias", _f), ("output", _f), ("dy", _f),
+        ("dinput", _f), ("dkernel", _f), ("dbias", _f), ("dims", _l),
+        ("ndims", C.c_long), ("D", C.c_long), ("K", C.c_long),
+    ]
+
+
+def build(force: bool = False) -> None:
+    """Build liboracle.so (always possible) and _ref (only where the reference
+    sources exist, i.e. not on the GPU box, which uses the prebuilt file)."""
+    targets = []
+    if force or not os.path.exists(ORACLE_SO):
+        targets.append("oracle")
+    if os.path.isdir(REF_SRC) and (force or not os.path.exists(REF_SO)):
+        targets.append("ref")
+    if targets:
+        subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+
+
+_libs: dict = {}
+
+
+def _lib(name: str):
+    if name not in _libs:
+        build()
+        path = ORACLE_SO if name == "oracle" else REF_SO
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        lib = C.CDLL(path)
+        if name == "oracle":
+            for fn in ("oracle_scannd_fwd", "oracle_scannd_bwd"):
+                getattr(lib, fn).restype = C.c_int
+            lib.oracle_scannd_fwd.argtypes = [C.POINTER(ScanNDParams)]
+            lib.oracle_scannd_bwd.argtypes = [C.POINTER(ScanNDParams), _f]
+            lib.oracle_convnd_fwd.argtypes = [C.POINTER(ConvNDParams)]
+            lib.oracle_convnd_bwd.argtypes = [C.POINTER(ConvNDParams)]
+            lib.oracle_scannd_fwd_f64.restype = C.c_int
+        else:
+            lib.shim_scannd_ref.argtypes = [C.POINTER(ScanNDParams)]
+            lib.shim_scannd_ref_batched.argtypes = [C.POINTER(ScanNDParams), C.c_long]
+            lib.shim_convnd.argtypes = [C.POINTER(ConvNDParams), C.c_int]
+            lib.shim_set_threads.argtypes = [C.c_int]
+            lib.scannd_validate.argtypes = [C.POINTER(ScanNDParams)]
+        _libs[name] = lib
+    return _libs[name]
+
+
+def have_ref() -> bool:
+    try:
+        _lib("ref")
+        return True
+    except (FileNotFoundError, OSError, subprocess.CalledProcessError):
+        return False
+
+
+def set_threads(n: int) -> int:
+    return _lib("ref").shim_set_threads(n)
+
+
+def _fp(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_f)
+
+
+def scan_params(inp: dict, h, y, grads: dict | None = None, keep=None) -> ScanNDParams:
+    """Fill ScanNDParams from a dict of numpy arrays (single item)."""
+    dims = np.ascontiguousarray(inp["dims"], dtype=np.int64)
+    if keep is not None:
+        keep.append(dims)
+    p = ScanNDParams()
+    p.max_ndims = 32
+    p.max_state = 0
+    p.use_fast_exp = int(inp.get("use_fast_exp", 0))
+    p.dims = dims.ctypes.data_as(_l)
+    p.ndims = len(dims)
+    p.D = inp["D"]
+    p.M = inp["M"]
+    p.x, p.A, p.B, p.C, p.delta = (_fp(inp[k]) for k in ("x", "A", "B", "C", "delta"))
+    p.h, p.y = _fp(h), _fp(y)
+    p.theta = _fp(inp.get("theta"))
+    p.lambda_ = _fp(inp.get("lambda"))
+    p.default_lambda = inp.get("default_lambda", 0.5)
+    p.use_a_log_clamp = int(inp.get("use_a_log_clamp", 0))
+    p.a_log_min = inp.get("a_log_min", -1e-5)
+    g = grads or {}
+    for k in ("dA", "dB", "dC", "ddelta", "dlambda", "dtheta"):
+        setattr(p, k, _fp(g.get(k)))
+    return p
+
+
+def _item(inp: dict, b: int) -> dict:
+    """Single batch item view of a batched input dict."""
+    out = dict(inp)
+    for k in ("x", "B", "C", "delta", "lambda"):
+        if inp.get(k) is not None and inp[k].ndim > _base_ndim(k):
+            out[k] = np.ascontiguousarray(inp[k][b])
+    return out
+
+
+def _base_ndim(k):
+    return {"x": 2, "B": 3, "C": 3, "delta": 3, "lambda": 1}[k]
+
+
+def ref_scannd(inp: dict):
+    """Reference scannd_ref (src/scan_nd.c:219-232) on each batch item -> (h, y)."""
+    return _run_fwd(inp, lambda p: _lib("ref").shim_scannd_ref(C.byref(p)))
+
+
+def oracle_scannd(inp: dict):
+    """My fp32 restatement -> (h, y)."""
+    return _run_fwd(inp, lambda p: _lib("oracle").oracle_scannd_fwd(C.byref(p)))
+
+
+def _run_fwd(inp, call):
+    batch = inp.get("batch", 1)
+    P = int(np.prod(inp["dims"]))
+    D, M = inp["D"], inp["M"]
+    hs = np.zeros((batch, P, D, M), np.float32)
+    ys = np.zeros((batch, P, D), np.float32)
+    for b in range(batch):
+        it = _item(inp, b) if batch > 1 or inp["x"].ndim == 3 else inp
+        h = np.zeros((P, D, M), np.float32)
+        y = np.zeros((P, D), np.float32)
+        keep = []
+        p = scan_params(it, h, y, keep=keep)
+        rc = call(p)
+        if rc != 0:
+            raise RuntimeError(f"scan oracle rc={rc}")
+        hs[b], ys[b] = h, y
+    return hs, ys
+
+
+def oracle_scannd_bwd(inp: dict, h, dy):
+    """Exact adjoint (double inside) -> dict of gradients (dA/dtheta summed over batch)."""
+    batch = inp.get("batch", 1)
+    dims = inp["dims"]
+    P = int(np.prod(dims))
+    nd = len(dims)
+    D, M = inp["D"], inp["M"]
+    g = {
+        "dA": np.zeros((nd, D, M), np.float32),
+        "dB": np.zeros((batch, P, D, M), np.float32),
+        "dC": np.zeros((batch, P, D, M), np.float32),
+        "ddelta": np.zeros((batch, nd, P, D), np.float32),
+        "dlambda": np.zeros((batch, P), np.float32),
+        "dtheta": np.zeros((max(D // 2, 1),), np.float32),
+        "dx": np.zeros((batch, P, D), np.float32),
+    }
+    for b in range(batch):
+        it = _item(inp, b) if batch > 1 or inp["x"].ndim == 3 else inp
+        gi = {k: np.zeros_like(g[k][b]) for k in ("dB", "dC", "ddelta", "dlambda")}
+        gi["dA"] = g["dA"]
+        gi["dtheta"] = g["dtheta"] if inp.get("theta") is not None else None
+        hb = np.ascontiguousarray(h[b])
+        dyb = np.ascontiguousarray(dy[b])
+        keep = []
+        p = scan_params(it, hb, dyb, gi, keep=keep)
+        dx = np.zeros((P, D), np.float32)
+        rc = _lib("oracle").oracle_scannd_bwd(C.byref(p), dx.ctypes.data_as(_f))
+        if rc != 0:
+            raise RuntimeError("oracle bwd failed")
+        for k in ("dB", "dC", "ddelta", "dlambda"):
+            g[k][b] = gi[k]
+        g["dx"][b] = dx
+    return g
+
+
+def fwd64(inp: dict, over: dict | None = None):
+    """Double-precision forward of one item, with optional float64 overrides."""
+    d = {k: (None if inp.get(k) is None else np.asarray(inp[k], np.float64))
+         for k in ("x", "A", "B", "C", "delta", "theta", "lambda")}
+    if over:
+        d.update(over)
+    dims = np.ascontiguousarray(inp["dims"], np.int64)
+    P = int(np.prod(dims))
+    D, M = inp["D"], inp["M"]
+    h = np.zeros(P * D * M)
+    y = np.zeros(P * D)
+    dp = C.POINTER(C.c_double)
+
+    def ptr(a):
+        return None if a is None else np.ascontiguousarray(a, np.float64).ctypes.data_as(dp)
+
+    arrs = {k: (None if v is None else np.ascontiguousarray(v, np.float64)) for k, v in d.items()}
+    lib = _lib("oracle")
+    rc = lib.oracle_scannd_fwd_f64(
+        dims.ctypes.data_as(_l), C.c_long(len(dims)), C.c_long(D), C.c_long(M),
+        ptr(arrs["x"]), ptr(arrs["A"]), ptr(arrs["B"]), ptr(arrs["C"]), ptr(arrs["delta"]),
+        ptr(arrs["theta"]), ptr(arrs["lambda"]), C.c_double(inp.get("default_lambda", 0.5)),
+        C.c_int(int(inp.get("use_a_log_clamp", 0))), C.c_double(inp.get("a_log_min", -1e-5)),
+        C.c_int(int(inp.get("use_fast_exp", 0))),
+        h.ctypes.data_as(dp), y.ctypes.data_as(dp))
+    assert rc == 0
+    return h.reshape(P, D, M), y.reshape(P, D)
+
+
+# ----------------------------------------------------------------- generators
+def gen_scan(dims, D, M, batch=1, seed=0, rope=False, lam=False, fast_exp=False,
+             clamp=False, a_log_min=-1e-5, default_lambda=0.5):
+    """Seeded Scan-A inputs with the BASELINE config-0 distributions:
+    x ~ N(0,1); delta = softplus(N(-4, 0.5)); A = -exp(U(0, ln 16));
+    B, C ~ N(0, 1/16) drawn per (p, m) and broadcast over d; theta ~ U(-pi, pi);
+    lambda ~ U(0, 1) when per-point lambda is on."""
+    rng = np.random.default_rng(seed)
+    dims = [int(v) for v in dims]
+    P = int(np.prod(dims))
+    nd = len(dims)
+    f32 = np.float32
+    x = rng.standard_normal((batch, P, D)).astype(f32)
+    delta = np.log1p(np.exp(rng.normal(-4.0, 0.5, (batch, nd, P, D)))).astype(f32)
+    A = (-np.exp(rng.uniform(0.0, np.log(16.0), (nd, D, M)))).astype(f32)
+    Bpm = (rng.standard_normal((batch, P, 1, M)) * 0.25).astype(f32)
+    Cpm = (rng.standard_normal((batch, P, 1, M)) * 0.25).astype(f32)
+    B = np.ascontiguousarray(np.broadcast_to(Bpm, (batch, P, D, M)))
+    Cm = np.ascontiguousarray(np.broadcast_to(Cpm, (batch, P, D, M)))
+    out = dict(dims=dims, D=D, M=M, batch=batch, x=x, delta=delta, A=A, B=B, C=Cm,
+               theta=None, use_fast_exp=int(fast_exp), use_a_log_clamp=int(clamp),
+               a_log_min=a_log_min, default_lambda=default_lambda)
+    out["lambda"] = None
+    if rope:
+        out["theta"] = rng.uniform(-np.pi, np.pi, (D // 2,)).astype(f32)
+    if lam:
+        out["lambda"] = rng.uniform(0.0, 1.0, (batch, P)).astype(f32)
+    return out
+
+
+def gen_conv(dims, D, K, batch=1, seed=0, bias=True):
+    """convnd inputs: input ~ N(0,1); kernel ~ N(0, 1/K^nd); bias ~ N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    P = int(np.prod(dims))
+    V = K ** len(dims)
+    f32 = np.float32
+    return dict(
+        dims=[int(v) for v in dims], D=D, K=K, batch=batch,
+        input=rng.standard_normal((batch, P, D)).astype(f32),
+        kernel=(rng.standard_normal((V, D)) / np.sqrt(V)).astype(f32),
+        bias=(rng.standard_normal(D) * np.sqrt(0.02)).astype(f32) if bias else None,
+        dy=rng.standard_normal((batch, P, D)).astype(f32),
+    )
+
+
+def _conv_params(inp, b, out, dinput=None, dkernel=None, dbias=None, keep=None):
+    dims = np.ascontiguousarray(inp["dims"], np.int64)
+    keep.append(dims)
+    p = ConvNDParams()
+    inb = np.ascontiguousarray(inp["input"][b])
+    keep.append(inb)
+    p.input = _fp(inb)
+    p.kernel = _fp(inp["kernel"])
+    p.bias = _fp(inp.get("bias"))
+    p.output = _fp(out)
+    dyb = np.ascontiguousarray(inp["dy"][b])
+    keep.append(dyb)
+    p.dy = _fp(dyb)
+    p.dinput, p.dkernel, p.dbias = _fp(dinput), _fp(dkernel), _fp(dbias)
+    p.dims = dims.ctypes.data_as(_l)
+    p.ndims = len(dims)
+    p.D = inp["D"]
+    p.K = inp["K"]
+    return p
+
+
+def conv_run(inp, which="oracle", mode=3):
+    """(output, dinput, dkernel summed over batch, dbias summed over batch)."""
+    batch = inp["batch"]
+    P = int(np.prod(inp["dims"]))
+    D = inp["D"]
+    V = inp["K"] ** len(inp["dims"])
+    out = np.zeros((batch, P, D), np.float32)
+    din = np.zeros((batch, P, D), np.float32)
+    dk = np.zeros((V, D), np.float32)
+    db = np.zeros((D,), np.float32)
+    for b in range(batch):
+        o = np.zeros((P, D), np.float32)
+        di = np.zeros((P, D), np.float32)
+        dki = np.zeros((V, D), np.float32)
+        dbi = np.zeros((D,), np.float32)
+        keep = []
+        p = _conv_params(inp, b, o, di, dki, dbi if inp.get("bias") is not None else None, keep)
+        if which == "oracle":
+            lib = _lib("oracle")
+            if mode & 1:
+                assert lib.oracle_convnd_fwd(C.byref(p)) == 0
+            if mode & 2:
+                assert lib.oracle_convnd_bwd(C.byref(p)) == 0
+        else:
+            assert _lib("ref").shim_convnd(C.byref(p), mode) == 0
+        out[b], din[b] = o, di
+        dk += dki
+        db += dbi
+    return out, din, dk, db

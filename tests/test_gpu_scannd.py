@@ -1,0 +1,152 @@
+"""GPU parity of the Scan-A forward/backward through the C ABI.
+
+Forward: against the reference's outputs (golden fixtures made by the
+reference compiled in place) and against the fp32 restatement (bit-equal to
+the reference) on seeded BASELINE-shaped inputs.  Backward: against the
+double-precision exact adjoint (pinned by finite differences)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import make_golden as mg
+from oracle import pyoracle as po
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_both(kmb, cuda, inp, expect_path=None):
+    from gpu_util import scan_fwd, assert_scan_close
+    h, y, path = scan_fwd(inp, cuda)
+    href, yref = po.oracle_scannd(inp)
+    if expect_path is not None:
+        assert path == expect_path, f"forward path {path}, expected {expect_path}"
+    return assert_scan_close(h, y, href, yref, inp["C"])
+
+
+@pytest.mark.parametrize("name", list(mg.SCAN_CASES))
+@pytest.mark.parametrize("generic", [False, True])
+def test_forward_matches_reference_fixture(kmb, cuda, name, generic):
+    from gpu_util import scan_fwd, assert_scan_close
+    kmb.lib().kmb_set_force_generic(1 if generic else 0)
+    try:
+        inp, href, yref = mg.load_scan(name)
+        h, y, path = scan_fwd(inp, cuda)
+        if generic:
+            assert path == 0
+        assert_scan_close(h, y, href, yref, inp["C"])
+    finally:
+        kmb.lib().kmb_set_force_generic(0)
+
+
+def test_config0_1d(kmb, cuda):
+    # dims {1024}, D 64, M 16, batch 1, no RoPE, lambda 0.5
+    inp = po.gen_scan([1024], 64, 16, batch=1, seed=100)
+    _run_both(kmb, cuda, inp, expect_path=1)
+
+
+def test_config1_2d_rope(kmb, cuda):
+    # dims {32,32}, D 64, M 16, batch 8, RoPE on
+    inp = po.gen_scan([32, 32], 64, 16, batch=8, seed=101, rope=True)
+    _run_both(kmb, cuda, inp, expect_path=1)
+
+
+@pytest.mark.parametrize("dims,D,M,flags,path", [
+    ([64, 64], 64, 64, dict(rope=True), 1),          # headline geometry, fewer channels
+    ([64, 64], 32, 64, dict(lam=True), 1),
+    ([16, 80], 32, 32, dict(rope=True, lam=True), 1),  # inner axis 0 (columns)
+    ([80, 16], 16, 16, dict(lam=True, fast_exp=True), 1),
+    ([20, 12], 32, 16, dict(clamp=True, a_log_min=-2.0), 1),   # partial last stage
+    ([100], 16, 16, dict(rope=True), 1),
+    ([4, 6, 5], 6, 3, dict(rope=True, lam=True), 0),  # 3D -> generic
+    ([3, 3, 3, 3], 4, 5, {}, 0),                       # 4D -> generic
+    ([9, 7], 7, 5, dict(rope=True), 0),               # odd sizes -> generic
+])
+def test_forward_shapes(kmb, cuda, dims, D, M, flags, path):
+    inp = po.gen_scan(dims, D, M, batch=2, seed=sum(dims) + D, **flags)
+    _run_both(kmb, cuda, inp, expect_path=path)
+
+
+def test_headline_shape_channel_slice(kmb, cuda):
+    """Headline geometry at full channel count (2D 64x64, D 512, M 64, batch 2):
+    every (item, channel-pair) recurrence is independent, so a 16-channel
+    slice of the oracle must match the same slice of the GPU result."""
+    from gpu_util import scan_fwd, assert_scan_close
+    inp = po.gen_scan([64, 64], 512, 64, batch=2, seed=7, rope=True)
+    h, y, path = scan_fwd(inp, cuda)
+    assert path == 1
+    for b, c0 in ((0, 0), (1, 496)):
+        sl = dict(inp, D=16, batch=1)
+        for k in ("x", "B", "C"):
+            sl[k] = np.ascontiguousarray(inp[k][b:b + 1, :, c0:c0 + 16])
+        sl["delta"] = np.ascontiguousarray(inp["delta"][b:b + 1, :, :, c0:c0 + 16])
+        sl["A"] = np.ascontiguousarray(inp["A"][:, c0:c0 + 16])
+        sl["theta"] = np.ascontiguousarray(inp["theta"][c0 // 2:c0 // 2 + 8])
+        href, yref = po.oracle_scannd(sl)
+        assert_scan_close(h[b:b + 1, :, c0:c0 + 16], y[b:b + 1, :, c0:c0 + 16], href, yref, sl["C"])
+
+
+def test_host_pointer_entry(kmb, cuda):
+    """scannd() with host (numpy) buffers stages through the device."""
+    from gpu_util import assert_scan_close
+    inp = po.gen_scan([6, 5], 6, 4, batch=1, seed=3, rope=True, lam=True)
+    P = 30
+    h = np.zeros((P, 6, 4), np.float32)
+    y = np.zeros((P, 6), np.float32)
+    it = {k: (np.ascontiguousarray(v[0]) if k in ("x", "B", "C", "delta", "lambda") else v)
+          for k, v in inp.items()}
+    p = kmb.scan_params(inp["dims"], 6, 4, it["x"], it["A"], it["B"], it["C"], it["delta"], h, y,
+                        theta=it["theta"], lam=it["lambda"])
+    assert kmb.lib().scannd(C.byref(p)) == 0, kmb.last_error()
+    href, yref = po.oracle_scannd(inp)
+    assert_scan_close(h[None], y[None], href, yref, inp["C"])
+
+
+def test_om_forward_rejects_host_pointers(kmb, cuda):
+    buf = np.zeros(64, np.float32)
+    p = kmb.scan_params([2, 2], 1, 1, buf, buf, buf, buf, buf, buf, buf)
+    assert kmb.lib().om_scannd_forward(C.byref(p)) == -1
+
+
+@pytest.mark.parametrize("dims,D,M,flags", [
+    ([32, 32], 64, 16, dict(rope=True)),             # BASELINE config 1 (batch reduced below)
+    ([6, 5], 6, 4, dict(rope=True, lam=True)),
+    ([5, 7], 5, 3, dict(rope=True)),                  # odd D: last channel unrotated
+    ([3, 4, 2], 4, 4, dict(fast_exp=True, clamp=True, a_log_min=-2.0, lam=True)),
+    ([64], 8, 4, {}),
+])
+def test_backward_matches_exact_adjoint(kmb, cuda, dims, D, M, flags):
+    from gpu_util import scan_bwd, assert_grad_close
+    batch = 2
+    inp = po.gen_scan(dims, D, M, batch=batch, seed=41 + D, **flags)
+    href, _ = po.oracle_scannd(inp)
+    rng = np.random.default_rng(9)
+    P = int(np.prod(dims))
+    dy = rng.standard_normal((batch, P, D)).astype(np.float32)
+    got = scan_bwd(inp, href, dy, cuda)
+    ref = po.oracle_scannd_bwd(inp, href, dy)
+    names = ["dA", "dB", "dC", "ddelta", "dlambda", "dx"] + (["dtheta"] if flags.get("rope") else [])
+    for k in names:
+        r = ref[k] if k != "dtheta" else ref[k][: D // 2]
+        g = got[k] if k != "dtheta" else got[k][: D // 2]
+        assert_grad_close(g, r, k)
+
+
+def test_backward_accumulates(kmb, cuda):
+    """Gradients are accumulated (+=), as the reference's atomicAdd backward does."""
+    from gpu_util import scan_bwd
+    inp = po.gen_scan([6, 5], 6, 4, batch=1, seed=2, rope=True)
+    href, _ = po.oracle_scannd(inp)
+    dy = np.random.default_rng(1).standard_normal((1, 30, 6)).astype(np.float32)
+    g1 = scan_bwd(inp, href, dy, cuda)
+    import torch
+    import bissimamba_b200 as k
+    from gpu_util import to_dev
+    d = to_dev(inp, cuda)
+    ht = torch.from_numpy(href).to(cuda)
+    dyt = torch.from_numpy(dy).to(cuda)
+    dB = torch.ones((1, 30, 6, 4), device=cuda)
+    p = k.scan_params(inp["dims"], 6, 4, d["x"], d["A"], d["B"], d["C"], d["delta"], ht, dyt,
+                      theta=d["theta"], grads={"dB": dB})
+    k.check(k.lib().scannd_backward_batched(C.byref(p), 1, None))
+    np.testing.assert_allclose(dB.cpu().numpy() - 1.0, g1["dB"], rtol=1e-5, atol=1e-5)
