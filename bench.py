@@ -34,11 +34,24 @@ sys.path.insert(0, ROOT)
 
 DIMS = (64, 64)
 D, M, BATCH = 512, 64, 32
-ND = len(DIMS)
-P = DIMS[0] * DIMS[1]
-UPDATES = BATCH * P * D * M                       # per GPU per step
-ALG_BYTES = UPDATES * 12 + BATCH * P * D * (4 + 4 * ND + 4)   # B,C read + h write; x, delta, y
 WORKLOAD = "scannd_fwd_2d64x64_D512_M64_b32"
+
+
+def set_workload(dims, d, m, batch):
+    """Headline by default; --batch/--dims/--D/--M shrink it for profiling runs."""
+    global DIMS, D, M, BATCH, ND, P, UPDATES, ALG_BYTES, WORKLOAD
+    DIMS, D, M, BATCH = tuple(dims), d, m, batch
+    ND = len(DIMS)
+    P = 1
+    for v in DIMS:
+        P *= v
+    UPDATES = BATCH * P * D * M                                   # per GPU per step
+    ALG_BYTES = UPDATES * 12 + BATCH * P * D * (4 + 4 * ND + 4)   # B,C read + h write; x, delta, y
+    if (DIMS, D, M, BATCH) != ((64, 64), 512, 64, 32):
+        WORKLOAD = "scannd_fwd_" + "x".join(map(str, DIMS)) + f"_D{D}_M{M}_b{BATCH} (non-headline)"
+
+
+set_workload(DIMS, D, M, BATCH)
 PROFILE_MD = os.path.join(ROOT, "profiles", "scan_fwd_tma_headline.md")
 
 
@@ -51,7 +64,13 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--batch", type=int, default=BATCH, help="profiling override (default: headline 32)")
+    ap.add_argument("--dims", type=int, nargs="+", default=list(DIMS))
+    ap.add_argument("--D", type=int, default=D)
+    ap.add_argument("--M", type=int, default=M)
+    a = ap.parse_args()
+    set_workload(a.dims, a.D, a.M, a.batch)
+    return a
 
 
 def peaks():
@@ -275,7 +294,7 @@ def main():
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_src,
                 "traffic": (tpu * UPDATES if tpu else None),
-                "alg_bytes_per_launch": ALG_BYTES, "kernel": "scan_fwd_tma" if path == 1 else "scan_fwd_generic"}
+                "alg_bytes_per_launch": ALG_BYTES, "kernel": ("scan_fwd_strips" if len(DIMS) == 2 else "scan_fwd_tma") if path == 1 else "scan_fwd_generic"}
 
     # ------------------------------------------------------------- e2e
     e2e = None
@@ -322,7 +341,7 @@ def main():
                 "config": {"workload": WORKLOAD, "dims": list(DIMS), "D": D, "M": M, "batch_per_gpu": BATCH,
                            "global_batch": BATCH * world, "rope": False, "lambda": "default 0.5",
                            "parallelism": f"dp{world} (batch shards, no collective)",
-                           "l2": "inputs 52.6 GB/GPU >> 126 MB L2, no flush"},
+                           "l2": f"inputs {ALG_BYTES / 1e9:.1f} GB/GPU >> 126 MB L2, no flush"},
                 "hbm_gbs": round(achieved, 1),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": args.steps, "clocks": clk,

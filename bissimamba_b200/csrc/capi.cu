@@ -29,6 +29,7 @@
 namespace kmb {
 cudaError_t launch_scan_fwd_generic(const ScanDesc& s, cudaStream_t st);
 cudaError_t launch_scan_fwd_tma(const ScanDesc& s, int* status, cudaStream_t st);
+cudaError_t launch_scan_fwd_strips(const ScanDesc& s, int* status, cudaStream_t st);
 size_t scan_bwd_generic_scratch_bytes(const ScanDesc& s);
 cudaError_t launch_scan_bwd_generic(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC,
                                     float* ddelta, float* dlambda, float* dtheta, float* dx, void* scratch,
@@ -171,12 +172,12 @@ int run_scan_fwd(const ScanDesc& s, cudaStream_t st) {
         int* status = status_word();
         if (!status) return fail("workspace allocation failed");
         if ((e = cudaMemsetAsync(status, 0, sizeof(int), st)) != cudaSuccess) return fail_cuda("memset", e);
-        e = launch_scan_fwd_tma(s, status, st);
+        e = (s.nd == 2) ? launch_scan_fwd_strips(s, status, st) : launch_scan_fwd_tma(s, status, st);
         if (e == cudaSuccess) {
             tl_fast_path = 1;
             return 0;
         }
-        if (e != cudaErrorNotSupported) return fail_cuda("scan_fwd_tma", e);
+        if (e != cudaErrorNotSupported) return fail_cuda("scan_fwd (TMA path)", e);
         cudaGetLastError();
     }
     tl_fast_path = 0;

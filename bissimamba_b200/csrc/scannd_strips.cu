@@ -1,0 +1,535 @@
+// scannd_strips.cu -- Scan-A forward for 2D grids on sm_100a: a systolic
+// column-strip pipeline (the headline path: 2D 64x64, D=512, M=64, batch 32).
+//
+// The grid is walked row by row (outer o, inner q, inner extent Q <= 64).  A
+// CTA owns a tile (item b, CH consecutive channels, all M states) and splits
+// the inner axis into S <= 8 column strips of Wc <= 8 columns.  Warp (w, h)
+// owns strip w for the lane half h (M=64 needs two warps per channel).  Each
+// thread owns one state index m for CPT channels (2 when RoPE pairs channels,
+// so the rotation needs no shuffle) and keeps, per column of its strip, the
+// rotated state R h and the B*x product of the previous row in registers
+// (ring of Wc slots).  The value left of its first column comes from strip
+// w-1 through a shared-memory handoff slot guarded by mbarriers; strips run
+// one row apart, like a systolic array, so all warps stay busy.
+//
+// Data: per strip a ring of NSS stages, each one row of the strip: TMA boxes
+// of B and C [Wc][CH][M], x and delta [.][Wc][4] (4-channel boxes, aligned),
+// lambda; issued by lane 0 of the strip's first warp, NSS-1 rows ahead.  Only
+// B, C, x, delta, lambda are read (once) and h, y written (once): 12 B per
+// state update + 16 B per (point, channel).
+// y[p, d] = sum_m C h: each warp reduces its 8 points x CPT channels across
+// its lanes with a transposed butterfly; with two lane halves (M = 64) the two
+// partials are added into a zeroed y with red.add (two addends in either order
+// give the same fp32 sum, so the result is deterministic).
+#include <cuda.h>
+#include "kmb_common.cuh"
+#include "kmb_sync.cuh"
+#include <type_traits>
+
+namespace kmb {
+
+constexpr int SW_NSS_MAX = 4;  // stages per strip (fewer when shared memory is short)
+constexpr int SW_K = 4;        // handoff slots per strip boundary
+constexpr int SW_WC = 8;       // max columns per strip
+
+struct StripDesc {
+    int D, nd;
+    int Q, O, Wc, S;        // inner extent, outer extent, columns per strip, strips
+    int k_in;               // axis of the inner dimension
+    int lam_inner_fast;     // lambda box (Wc,1,1) at (q0,o,b) vs (4,Wc,1) at (o&~3,q0,b)
+    int clamp;
+    float amin, deflam;
+    long long qstride, ostride;  // point strides of the inner / outer dims
+    long long P;
+    int ntd;                // channel tiles per item
+    long long ntiles;
+    int nss;                // stages per strip
+    int st_bytes, offC, offX, offD, offL;
+    unsigned tx_bytes;
+    int red_y;              // 1: y is accumulated with red.add (two lane halves)
+    const float* A;
+    const float* theta;
+    float* h;
+    float* y;
+    int* status;
+};
+
+template <int MT, bool ROPE>
+struct StripGeom {
+    static constexpr int CPT = ROPE ? 2 : 1;              // channels per thread
+    static constexpr int SPW = MT >= 32 ? 1 : 32 / MT;    // channel sets per warp
+    static constexpr int HW = MT >= 32 ? MT / 32 : 1;     // warps per strip
+    static constexpr int CH = SPW * CPT;                  // channels per tile
+    static constexpr int GS = MT >= 32 ? 32 : MT;         // lanes summed for y
+};
+
+// Transposed butterfly: v[NV] per lane -> lane holds the sum over its GS-lane
+// group of value index idx_of(lane).  NV is a power of two <= GS.
+template <int N>
+struct Log2 {
+    static constexpr int value = 1 + Log2<N / 2>::value;
+};
+template <>
+struct Log2<1> {
+    static constexpr int value = 0;
+};
+
+template <int NV, int GS>
+__device__ __forceinline__ float butterfly(float (&v)[NV], int lane) {
+    constexpr int LV = Log2<NV>::value, LG = Log2<GS>::value;
+#pragma unroll
+    for (int lvl = 0; lvl < LV; lvl++) {
+        const int half = NV >> (lvl + 1);
+        const int off = GS >> (lvl + 1);
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < NV / 2; i++) {
+            if (i < half) {
+                const float send = up ? v[i] : v[i + half];
+                const float keep = up ? v[i + half] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int lvl = LV; lvl < LG; lvl++) r += __shfl_xor_sync(0xffffffffu, r, GS >> (lvl + 1));
+    return r;
+}
+// value index held by `lane` after butterfly<NV, GS>
+template <int NV, int GS>
+__device__ __forceinline__ int butterfly_index(int lane) {
+    int idx = 0, n = NV, off = GS / 2;
+    while (n > 1) {
+        n >>= 1;
+        if (lane & off) idx += n;
+        off >>= 1;
+    }
+    return idx;
+}
+
+template <int MT, bool ROPE>
+struct StripLayout {
+    using Gm = StripGeom<MT, ROPE>;
+    static constexpr int BBOX = MT * Gm::CH * SW_WC * 4;   // bytes of one B / C box
+    static constexpr int offC = BBOX;
+    static constexpr int offX = 2 * BBOX;                  // x box [WC][4]
+    static constexpr int offD = offX + 128;                // delta box [2][WC][4]
+    static constexpr int offL = offD + 256;                // lambda box [WC] or [WC][4]
+    static constexpr int bytes = offL + 128;
+};
+
+template <int MT, bool ROPE, bool LAMB, bool KIN0>
+__global__ void __launch_bounds__(512, 1)
+scan_fwd_strips(const __grid_constant__ StripDesc f,
+                const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mC,
+                const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mD,
+                const __grid_constant__ CUtensorMap mL) {
+    using Gm = StripGeom<MT, ROPE>;
+    using Ly = StripLayout<MT, ROPE>;
+    constexpr int CPT = Gm::CPT, HW = Gm::HW, CH = Gm::CH, GS = Gm::GS;
+    constexpr int WC = SW_WC;
+    constexpr int ST = Ly::bytes;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
+    const int w = wi / HW, hh = wi % HW;  // strip, lane half
+    // parameters held in registers
+    const int S = f.S, NSS = f.nss, D = f.D, O = f.O, Q = f.Q, ntd = f.ntd;
+    const long long ntiles = f.ntiles, P = f.P, qstride = f.qstride, ostride = f.ostride;
+    const float deflam = f.deflam;
+    const int red_y = f.red_y;
+    // smem map: stages [S][NSS] | handoff values [S][HW][K][2][32*CPT] | barriers
+    unsigned char* stages = smem;
+    const int hv = 32 * CPT;
+    float* hand = (float*)(smem + (size_t)S * NSS * ST);
+    uint64_t* bars = (uint64_t*)(hand + (size_t)S * HW * SW_K * 2 * hv);
+    uint64_t* b_full = bars;                          // [S][NSS]
+    uint64_t* b_empty = bars + S * NSS;               // [S][NSS]
+    uint64_t* b_hfull = bars + 2 * S * NSS;           // [S][HW][K]
+    uint64_t* b_hempty = b_hfull + S * HW * SW_K;     // [S][HW][K]
+    if (tid == 0) {
+        for (int i = 0; i < S * NSS; i++) {
+            mbar_init(smem_u32(&b_full[i]), 1);
+            mbar_init(smem_u32(&b_empty[i]), HW);
+        }
+        for (int i = 0; i < S * HW * SW_K; i++) {
+            mbar_init(smem_u32(&b_hfull[i]), 1);
+            mbar_init(smem_u32(&b_hempty[i]), 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (w >= S) return;
+
+    // ---- lane geometry
+    const int m = MT >= 32 ? hh * 32 + lane : lane % MT;
+    const int cl0 = MT >= 32 ? 0 : (lane / MT) * CPT;   // first local channel of this thread
+    const long long DM = (long long)D * MT;
+    const long long hq = qstride * DM;
+    const int q0 = w * WC;
+    const int ncol = min(WC, Q - q0);
+    unsigned char* my_stages = stages + (size_t)w * NSS * ST;
+    const bool issuer = (hh == 0 && lane == 0);
+    const long long tiles_mine = (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x;
+    const long long total_rows = tiles_mine * O;
+    long long next_issue = 0;
+
+    auto issue = [&](long long t) {
+        const long long ti = t / O;
+        const int o = (int)(t - ti * O);
+        const long long tile = blockIdx.x + ti * gridDim.x;
+        const int b = (int)(tile / ntd);
+        const int d0 = (int)(tile - (long long)b * ntd) * CH;
+        const int slot = (int)(t % NSS);
+        unsigned char* st = my_stages + (size_t)slot * ST;
+        const uint32_t full = smem_u32(&b_full[w * NSS + slot]);
+        mbar_expect_tx(full, f.tx_bytes);
+        tma_load_5d(smem_u32(st), &mB, full, 0, d0, q0, o, b);
+        tma_load_5d(smem_u32(st + Ly::offC), &mC, full, 0, d0, q0, o, b);
+        tma_load_4d(smem_u32(st + Ly::offX), &mX, full, d0 & ~3, q0, o, b);
+        tma_load_5d(smem_u32(st + Ly::offD), &mD, full, d0 & ~3, q0, o, 0, b);
+        if (LAMB) {
+            if (!KIN0) tma_load_3d(smem_u32(st + Ly::offL), &mL, full, q0, o, b);
+            else tma_load_3d(smem_u32(st + Ly::offL), &mL, full, o & ~3, q0, b);
+        }
+    };
+    auto top_up = [&](long long cur) -> bool {
+        while (next_issue < total_rows && next_issue < cur + NSS) {
+            const long long t = next_issue;
+            if (t >= NSS) {
+                const uint32_t eb = smem_u32(&b_empty[w * NSS + (int)(t % NSS)]);
+                const uint32_t ph = (uint32_t)(((t / NSS) - 1) & 1);
+                if (t <= cur) {
+                    if (!mbar_wait(eb, ph)) return false;
+                } else if (!mbar_try(eb, ph)) {
+                    break;
+                }
+            }
+            issue(t);
+            next_issue++;
+        }
+        return true;
+    };
+    auto drain = [&]() {
+        if (!issuer) return;
+        for (long long j = (next_issue > NSS ? next_issue - NSS : 0); j < next_issue; j++)
+            mbar_wait(smem_u32(&b_full[w * NSS + (int)(j % NSS)]), (uint32_t)((j / NSS) & 1));
+    };
+
+    float* my_hand_in = hand + ((size_t)(w * HW + hh) * SW_K) * 2 * hv;           // written by strip w-1
+    float* my_hand_out = hand + ((size_t)((w + 1) * HW + hh) * SW_K) * 2 * hv;    // read by strip w+1
+    const int hl = lane * CPT;
+    // per-thread offsets inside a stage
+    const int bofs = (cl0 * MT + m) * 4;                 // B / C box: [j][CH][MT]
+    const int xofs = cl0;                                // x / delta box column (+ (d0 & 3))
+    long long row = 0;
+
+    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int b = (int)(tile / ntd);
+        const int d0 = (int)(tile - (long long)b * ntd) * CH;
+        float AI[CPT], AO[CPT], cth = 1.0f, sth = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CPT; c++) {
+            const int d = d0 + cl0 + c;
+            AI[c] = kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + m], f.clamp, f.amin);
+            AO[c] = kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + m], f.clamp, f.amin);
+        }
+        if (ROPE) {
+            const float th = f.theta[(d0 + cl0) >> 1];
+            cth = cosf(th);
+            sth = sinf(th);
+        }
+        float* const hbase = f.h + (long long)b * P * DM + (long long)(d0 + cl0) * MT + m + (long long)q0 * hq;
+        float* const ybase = f.y + (long long)b * P * D + d0;
+        const int xo = (d0 & 3) + xofs;
+        float ring_h[WC][CPT], ring_b[WC][CPT];
+
+        // one row of this strip; HASO: the row above exists (o > 0)
+        auto do_row = [&](auto hasO_c, int o) -> bool {
+            constexpr bool HASO = decltype(hasO_c)::value;
+            const int slot = (int)(row % NSS);
+            const uint32_t ph = (uint32_t)((row / NSS) & 1);
+            if (issuer && !top_up(row)) {
+                set_status(f.status, KMB_ERR_TIMEOUT_EMPTY);
+                drain();
+                return false;
+            }
+            __syncwarp();
+            if (!mbar_wait(smem_u32(&b_full[w * NSS + slot]), ph)) {
+                set_status(f.status, KMB_ERR_TIMEOUT_FULL);
+                drain();
+                return false;
+            }
+            const unsigned char* st = my_stages + (size_t)slot * ST;
+            const float* Bs = (const float*)(st + bofs);
+            const float* Cs = (const float*)(st + Ly::offC + bofs);
+            const float* Xs = (const float*)(st + Ly::offX) + xo;
+            const float* DsI = (const float*)(st + Ly::offD) + (KIN0 ? 0 : WC * 4) + xo;
+            const float* DsO = (const float*)(st + Ly::offD) + (KIN0 ? WC * 4 : 0) + xo;
+            const float* Ls = (const float*)(st + Ly::offL) + (KIN0 ? (o & 3) : 0);
+            const int hs = (int)(row % SW_K);
+            const uint32_t hph = (uint32_t)((row / SW_K) & 1);
+            float lh[CPT], lb[CPT];
+            if (w > 0) {
+                if (!mbar_wait(smem_u32(&b_hfull[(w * HW + hh) * SW_K + hs]), hph)) {
+                    set_status(f.status, KMB_ERR_TIMEOUT_Y);
+                    drain();
+                    return false;
+                }
+                const float* src = my_hand_in + (size_t)hs * 2 * hv;
+#pragma unroll
+                for (int c = 0; c < CPT; c++) {
+                    lh[c] = src[hl + c];
+                    lb[c] = src[hv + hl + c];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&b_hempty[(w * HW + hh) * SW_K + hs]));
+            }
+            float prod[WC][CPT];
+            float lastH[CPT], lastB[CPT];
+            float* hp = hbase + (long long)o * ostride * DM;
+#pragma unroll
+            for (int j = 0; j < WC; j++) {
+                const float lam = LAMB ? Ls[j * (KIN0 ? 4 : 1)] : deflam;
+                float hn[CPT];
+#pragma unroll
+                for (int c = 0; c < CPT; c++) {
+                    const float x = Xs[j * 4 + c];
+                    const float dI = DsI[j * 4 + c];
+                    const float dO = DsO[j * 4 + c];
+                    const float Bv = Bs[j * CH * MT + c * MT];
+                    const float dt = __fadd_rn(dI, dO);
+                    const float bu = __fmul_rn(Bv, x);
+                    const float aI = kmb_exp(__fmul_rn(dI, AI[c]), 0);
+                    float buacc, dacc, hacc, inv;
+                    // inner predecessor: the previous column (strip w-1's last column when j == 0)
+                    const float hatI = (j == 0) ? lh[c] : ring_h[j == 0 ? 0 : j - 1][c];
+                    const float buI = (j == 0) ? lb[c] : ring_b[j == 0 ? 0 : j - 1][c];
+                    if (HASO) {
+                        const float aO = kmb_exp(__fmul_rn(dO, AO[c]), 0);
+                        if (j > 0 || w > 0) {
+                            buacc = __fadd_rn(buI, ring_b[j][c]);
+                            dacc = __fadd_rn(aI, aO);
+                            hacc = KIN0 ? __fmaf_rn(aO, ring_h[j][c], __fmul_rn(aI, hatI))
+                                        : __fmaf_rn(aI, hatI, __fmul_rn(aO, ring_h[j][c]));
+                            inv = 0.5f;
+                        } else {
+                            buacc = ring_b[j][c];
+                            dacc = aO;
+                            hacc = __fmul_rn(aO, ring_h[j][c]);
+                            inv = 1.0f;
+                        }
+                    } else {
+                        if (j > 0 || w > 0) {
+                            buacc = buI;
+                            dacc = aI;
+                            hacc = __fmul_rn(aI, hatI);
+                            inv = 1.0f;
+                        } else {
+                            buacc = 0.0f;
+                            dacc = 0.0f;
+                            hacc = 0.0f;
+                            inv = 0.0f;
+                        }
+                    }
+                    const float beta = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), __fmul_rn(dacc, inv));
+                    const float gamma = __fmul_rn(lam, dt);
+                    hn[c] = __fadd_rn(__fmaf_rn(bu, gamma, __fmul_rn(__fmul_rn(buacc, inv), beta)), hacc);
+                    ring_b[j][c] = bu;
+                    if (j < ncol) __stcs(hp + (long long)c * MT, hn[c]);
+                    prod[j][c] = __fmul_rn(Cs[j * CH * MT + c * MT], hn[c]);
+                }
+                if (ROPE) {
+                    ring_h[j][0] = __fmaf_rn(cth, hn[0], -__fmul_rn(sth, hn[1]));
+                    ring_h[j][1] = __fmaf_rn(sth, hn[0], __fmul_rn(cth, hn[1]));
+                } else {
+                    ring_h[j][0] = hn[0];
+                }
+                if (j == 0 || j < ncol) {
+#pragma unroll
+                    for (int c = 0; c < CPT; c++) {
+                        lastH[c] = ring_h[j][c];
+                        lastB[c] = ring_b[j][c];
+                    }
+                }
+                hp += hq;
+            }
+            // right boundary to strip w+1
+            if (w + 1 < S) {
+                if (row >= SW_K &&
+                    !mbar_wait(smem_u32(&b_hempty[((w + 1) * HW + hh) * SW_K + hs]), hph ^ 1)) {
+                    set_status(f.status, KMB_ERR_TIMEOUT_Y);
+                    drain();
+                    return false;
+                }
+                float* dst = my_hand_out + (size_t)hs * 2 * hv;
+#pragma unroll
+                for (int c = 0; c < CPT; c++) {
+                    dst[hl + c] = lastH[c];
+                    dst[hv + hl + c] = lastB[c];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&b_hfull[((w + 1) * HW + hh) * SW_K + hs]));
+            }
+            // y: reduce the warp's WC x CPT products across its GS-lane groups
+            {
+                constexpr int NV = WC * CPT;
+                float v[NV];
+#pragma unroll
+                for (int j = 0; j < WC; j++)
+#pragma unroll
+                    for (int c = 0; c < CPT; c++) v[j * CPT + c] = prod[j][c];
+                const float sum = butterfly<NV, GS>(v, lane);
+                constexpr int LPV = GS / NV;
+                const int gl = lane & (GS - 1);
+                if (LPV <= 1 || (gl % LPV) == 0) {
+                    const int idx = butterfly_index<NV, GS>(gl);
+                    const int j = idx / CPT, c = idx % CPT;
+                    if (j < ncol) {
+                        const int cl = (MT >= 32 ? 0 : (lane / MT) * CPT) + c;
+                        float* yp = ybase + ((long long)o * ostride + (long long)(q0 + j) * qstride) * D + cl;
+                        if (red_y) atomicAdd(yp, sum);
+                        else *yp = sum;
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&b_empty[w * NSS + slot]));
+            row++;
+            return true;
+        };
+
+        if (!do_row(std::integral_constant<bool, false>(), 0)) return;
+#pragma unroll 1
+        for (int o = 1; o < O; o++)
+            if (!do_row(std::integral_constant<bool, true>(), o)) return;
+    }
+}
+
+// ------------------------------------------------------------------ host side
+bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long long* dims,
+                 const unsigned long long* strides_bytes, const unsigned* box);
+
+
+template <int MT, bool ROPE, bool LAMB, bool KIN0>
+static cudaError_t strips_inst(const StripDesc& f, const CUtensorMap* maps, int smem, int threads, cudaStream_t st) {
+    auto k = scan_fwd_strips<MT, ROPE, LAMB, KIN0>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int dev, sms, per = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, threads, smem);
+    if (per < 1) return cudaErrorNotSupported;
+    long long grid = (long long)sms * per;
+    if (grid > f.ntiles) grid = f.ntiles;
+    k<<<(unsigned)grid, threads, smem, st>>>(f, maps[0], maps[1], maps[2], maps[3], maps[4]);
+    return cudaGetLastError();
+}
+
+template <int MT, bool ROPE>
+static cudaError_t strips_flags(const ScanDesc& s, const StripDesc& f, const CUtensorMap* maps, int smem,
+                                int threads, cudaStream_t st) {
+    const bool k0 = f.k_in == 0;
+    if (s.has_lambda)
+        return k0 ? strips_inst<MT, ROPE, true, true>(f, maps, smem, threads, st)
+                  : strips_inst<MT, ROPE, true, false>(f, maps, smem, threads, st);
+    return k0 ? strips_inst<MT, ROPE, false, true>(f, maps, smem, threads, st)
+              : strips_inst<MT, ROPE, false, false>(f, maps, smem, threads, st);
+}
+
+template <int MT, bool ROPE>
+static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st) {
+    using Gm = StripGeom<MT, ROPE>;
+    const int CH = Gm::CH, HW = Gm::HW, CPT = Gm::CPT;
+    const int D = s.D;
+    if (D % CH != 0) return cudaErrorNotSupported;
+    const long long H = s.dims[0], W = s.dims[1];
+    StripDesc f{};
+    f.D = D;
+    f.nd = 2;
+    if (W <= 64) {
+        f.Q = (int)W; f.O = (int)H; f.k_in = 1; f.qstride = 1; f.ostride = W; f.lam_inner_fast = 1;
+    } else if (H <= 64) {
+        f.Q = (int)H; f.O = (int)W; f.k_in = 0; f.qstride = W; f.ostride = 1; f.lam_inner_fast = 0;
+    } else {
+        return cudaErrorNotSupported;
+    }
+    if (s.has_lambda && (W % 4) != 0) return cudaErrorNotSupported;
+    f.Wc = SW_WC;
+    f.S = (f.Q + f.Wc - 1) / f.Wc;
+    f.clamp = s.clamp; f.amin = s.a_log_min; f.deflam = s.default_lambda;
+    f.P = s.P;
+    f.ntd = D / CH;
+    f.ntiles = s.batch * f.ntd;
+    using Ly = StripLayout<MT, ROPE>;
+    const int bbox = Ly::BBOX;
+    f.offC = Ly::offC;
+    f.offX = Ly::offX;
+    f.offD = Ly::offD;
+    f.offL = Ly::offL;
+    f.st_bytes = Ly::bytes;
+    f.tx_bytes = (unsigned)(2 * bbox + 16 * f.Wc + 2 * 16 * f.Wc +
+                            (s.has_lambda ? (f.lam_inner_fast ? 4 * f.Wc : 16 * f.Wc) : 0));
+    f.red_y = HW > 1;
+    f.A = s.A; f.theta = s.theta; f.h = s.h; f.y = s.y; f.status = status;
+    const unsigned long long P = s.P, Bn = s.batch, DM = (unsigned long long)D * MT;
+    const unsigned long long qs = f.qstride, os = f.ostride;
+    CUtensorMap maps[5];
+    memset(maps, 0, sizeof(maps));
+    {
+        const unsigned long long dims[5] = {(unsigned long long)MT, (unsigned long long)D, (unsigned long long)f.Q,
+                                            (unsigned long long)f.O, Bn};
+        const unsigned long long str[4] = {(unsigned long long)MT * 4, qs * DM * 4, os * DM * 4, P * DM * 4};
+        const unsigned box[5] = {(unsigned)MT, (unsigned)CH, (unsigned)f.Wc, 1, 1};
+        if (!tmap_encode(&maps[0], s.B, 5, dims, str, box)) return cudaErrorNotSupported;
+        if (!tmap_encode(&maps[1], s.C, 5, dims, str, box)) return cudaErrorNotSupported;
+    }
+    {
+        const unsigned long long dims[4] = {(unsigned long long)D, (unsigned long long)f.Q, (unsigned long long)f.O, Bn};
+        const unsigned long long str[3] = {qs * D * 4, os * D * 4, P * D * 4};
+        const unsigned box[4] = {4, (unsigned)f.Wc, 1, 1};
+        if (!tmap_encode(&maps[2], s.x, 4, dims, str, box)) return cudaErrorNotSupported;
+    }
+    {
+        const unsigned long long dims[5] = {(unsigned long long)D, (unsigned long long)f.Q, (unsigned long long)f.O, 2, Bn};
+        const unsigned long long str[4] = {qs * D * 4, os * D * 4, P * D * 4, 2 * P * D * 4};
+        const unsigned box[5] = {4, (unsigned)f.Wc, 1, 2, 1};
+        if (!tmap_encode(&maps[3], s.delta, 5, dims, str, box)) return cudaErrorNotSupported;
+    }
+    if (s.has_lambda) {
+        const unsigned long long dims[3] = {(unsigned long long)W, (unsigned long long)H, Bn};
+        const unsigned long long str[2] = {(unsigned long long)W * 4, P * 4};
+        const unsigned box[3] = {f.lam_inner_fast ? (unsigned)f.Wc : 4u, f.lam_inner_fast ? 1u : (unsigned)f.Wc, 1};
+        if (!tmap_encode(&maps[4], s.lambda, 3, dims, str, box)) return cudaErrorNotSupported;
+    } else {
+        maps[4] = maps[2];
+    }
+    const int threads = f.S * HW * 32;
+    const int hv = 32 * CPT;
+    const int fixed = f.S * HW * SW_K * 2 * hv * 4 + (2 * f.S * SW_NSS_MAX + 2 * f.S * HW * SW_K) * 8;
+    f.nss = SW_NSS_MAX;
+    while (f.nss > 2 && fixed + f.S * f.nss * f.st_bytes > 227 * 1024) f.nss--;
+    const int smem = fixed + f.S * f.nss * f.st_bytes;
+    if (smem > 227 * 1024) return cudaErrorNotSupported;
+    if (f.red_y) {
+        cudaError_t e = cudaMemsetAsync(s.y, 0, (size_t)s.batch * s.P * D * sizeof(float), st);
+        if (e != cudaSuccess) return e;
+    }
+    return strips_flags<MT, ROPE>(s, f, maps, smem, threads, st);
+}
+
+// 2D grids with an inner extent <= 64 and M in {16, 32, 64}.
+cudaError_t launch_scan_fwd_strips(const ScanDesc& s, int* status, cudaStream_t st) {
+    if (s.nd != 2 || s.fast_exp) return cudaErrorNotSupported;
+    if (s.batch > 0x7fffffff || s.P > 0x7fffffffLL) return cudaErrorNotSupported;
+    if (s.D % 4 != 0) return cudaErrorNotSupported;
+    switch (s.M) {
+        case 16: return s.rope ? strips_launch<16, true>(s, status, st) : strips_launch<16, false>(s, status, st);
+        case 32: return s.rope ? strips_launch<32, true>(s, status, st) : strips_launch<32, false>(s, status, st);
+        case 64: return s.rope ? strips_launch<64, true>(s, status, st) : strips_launch<64, false>(s, status, st);
+        default: return cudaErrorNotSupported;
+    }
+}
+
+}  // namespace kmb

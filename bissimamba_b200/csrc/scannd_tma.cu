@@ -1,5 +1,6 @@
-// scannd_tma.cu -- persistent, warp-specialised Scan-A forward for 1D and 2D
-// grids on sm_100a (the headline path: 2D 64x64, D=512, M=64, batch 32).
+// scannd_tma.cu -- persistent Scan-A forward for 1D grids on sm_100a (2D grids
+// use the column-strip pipeline of scannd_strips.cu).  This file also holds the
+// host-side TMA descriptor encoder shared by both kernels.
 //
 // Work decomposition
 //   tile   = (item b, channel tile [d0, d0+DT)), DT*M = 256 recurrence lanes.
@@ -31,6 +32,7 @@
 //            the status word and returns (the issuer first drains its copies).
 #include <cuda.h>
 #include "kmb_common.cuh"
+#include "kmb_sync.cuh"
 
 namespace kmb {
 
@@ -38,7 +40,6 @@ constexpr int TG = 8;      // points per stage
 constexpr int TNS = 6;     // stages in the ring
 constexpr int TNCW = 8;    // consumer warps
 constexpr int TTHREADS = TNCW * 32;
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 struct FastDesc {
     int M, DT, D, nd;
@@ -52,77 +53,13 @@ struct FastDesc {
     int ntd;                // channel tiles per item (D / DT)
     long long ntiles;       // batch * ntd
     int sq_count;           // ceil(Q / G)
-    unsigned tx_bytes;      // TMA bytes per stage      // TMA bytes per stage
+    unsigned tx_bytes;      // TMA bytes per stage
     const float* A;
     const float* theta;
     float* h;
     float* y;
     int* status;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-// Bounded wait on an mbarrier phase.  false = gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    if (mbar_try(bar, parity)) return true;
-    const unsigned long long t0 = gtimer();
-    while (!mbar_try(bar, parity)) {
-        if (gtimer() - t0 > kWaitLimitNs) return false;
-    }
-    return true;
-}
-
-__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2, int c3, int c4) {
-    asm volatile(
-        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
-        ::"r"(dst), "l"((unsigned long long)map), "r"(bar),
-          "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4) : "memory");
-}
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2, int c3) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6}], [%2];"
-        ::"r"(dst), "l"((unsigned long long)map), "r"(bar),
-          "r"(c0), "r"(c1), "r"(c2), "r"(c3) : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5}], [%2];"
-        ::"r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2) : "memory");
-}
-
-__device__ __forceinline__ void set_status(int* st, int code) {
-    if (st) atomicCAS(st, 0, code);
-}
 
 // One state update of lane (d, m) at inner position q of outer row o.
 // hasI/hasO: inner / outer predecessor present.  Returns h; writes the rotated
@@ -442,7 +379,7 @@ static PFN_encodeTiled get_encode() {
     return fn;
 }
 
-static bool encode(CUtensorMap* m, const void* base, int rank, const unsigned long long* dims,
+bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long long* dims,
                    const unsigned long long* strides_bytes, const unsigned* box) {
     PFN_encodeTiled fn = get_encode();
     if (!fn) return false;
@@ -481,17 +418,14 @@ static cudaError_t launch_inst(const FastDesc& f, const CUtensorMap* maps, cudaS
 template <int MT>
 static cudaError_t dispatch_nd(const ScanDesc& s, const FastDesc& f, const CUtensorMap* maps, int QT,
                                cudaStream_t st) {
-    if (s.nd == 1)
-        return s.rope ? launch_inst<1, true, 1, MT>(f, maps, st) : launch_inst<1, false, 1, MT>(f, maps, st);
-    if (QT == 32)
-        return s.rope ? launch_inst<2, true, 32, MT>(f, maps, st) : launch_inst<2, false, 32, MT>(f, maps, st);
-    return s.rope ? launch_inst<2, true, 64, MT>(f, maps, st) : launch_inst<2, false, 64, MT>(f, maps, st);
+    (void)QT;
+    return s.rope ? launch_inst<1, true, 1, MT>(f, maps, st) : launch_inst<1, false, 1, MT>(f, maps, st);
 }
 
 // Returns cudaErrorNotSupported when the shape is outside the fast path's
 // envelope (the caller then uses the generic kernels).
 cudaError_t launch_scan_fwd_tma(const ScanDesc& s, int* status, cudaStream_t st) {
-    if (s.nd < 1 || s.nd > 2) return cudaErrorNotSupported;
+    if (s.nd != 1) return cudaErrorNotSupported;
     const int M = s.M, D = s.D;
     if (M != 16 && M != 32 && M != 64) return cudaErrorNotSupported;
     const int DT = 256 / M;
@@ -539,15 +473,15 @@ cudaError_t launch_scan_fwd_tma(const ScanDesc& s, int* status, cudaStream_t st)
                                             (unsigned long long)f.Q, (unsigned long long)f.O, Bn};
         const unsigned long long str[4] = {(unsigned long long)M * 4, qs * DM * 4, os * DM * 4, P * DM * 4};
         const unsigned box[5] = {(unsigned)M, (unsigned)DT, (unsigned)TG, 1, 1};
-        if (!encode(&maps[0], s.B, 5, dims, str, box)) return cudaErrorNotSupported;
-        if (!encode(&maps[1], s.C, 5, dims, str, box)) return cudaErrorNotSupported;
+        if (!tmap_encode(&maps[0], s.B, 5, dims, str, box)) return cudaErrorNotSupported;
+        if (!tmap_encode(&maps[1], s.C, 5, dims, str, box)) return cudaErrorNotSupported;
     }
     {
         const unsigned long long dims[4] = {(unsigned long long)D, (unsigned long long)f.Q,
                                             (unsigned long long)f.O, Bn};
         const unsigned long long str[3] = {qs * D * 4, os * D * 4, P * D * 4};
         const unsigned box[4] = {(unsigned)DT, (unsigned)TG, 1, 1};
-        if (!encode(&maps[2], s.x, 4, dims, str, box)) return cudaErrorNotSupported;
+        if (!tmap_encode(&maps[2], s.x, 4, dims, str, box)) return cudaErrorNotSupported;
     }
     {
         const unsigned long long dims[5] = {(unsigned long long)D, (unsigned long long)f.Q,
@@ -555,7 +489,7 @@ cudaError_t launch_scan_fwd_tma(const ScanDesc& s, int* status, cudaStream_t st)
         const unsigned long long str[4] = {qs * D * 4, os * D * 4, P * D * 4,
                                            (unsigned long long)s.nd * P * D * 4};
         const unsigned box[5] = {(unsigned)DT, (unsigned)TG, 1, (unsigned)s.nd, 1};
-        if (!encode(&maps[3], s.delta, 5, dims, str, box)) return cudaErrorNotSupported;
+        if (!tmap_encode(&maps[3], s.delta, 5, dims, str, box)) return cudaErrorNotSupported;
     }
     if (s.has_lambda) {
         const unsigned long long dims[3] = {(unsigned long long)W, (unsigned long long)(s.nd == 2 ? H : 1), Bn};
@@ -564,7 +498,7 @@ cudaError_t launch_scan_fwd_tma(const ScanDesc& s, int* status, cudaStream_t st)
         (void)dims;
         const unsigned long long str[2] = {d0 * 4, P * 4};
         const unsigned box[3] = {f.lam_inner_fast ? (unsigned)TG : 4u, f.lam_inner_fast ? 1u : (unsigned)TG, 1};
-        if (!encode(&maps[4], s.lambda, 3, dims1, str, box)) return cudaErrorNotSupported;
+        if (!tmap_encode(&maps[4], s.lambda, 3, dims1, str, box)) return cudaErrorNotSupported;
     } else {
         maps[4] = maps[2];
     }

@@ -37,4 +37,28 @@ int oracle_scannd_bwd(const ScanNDParams *p, float *dx);
 int oracle_convnd_fwd(const ConvNDParams *p);
 int oracle_convnd_bwd(const ConvNDParams *p);
 
+/* Mamba-3 block scan (Scan-B), one batch item.  B, C: [L, R*N] (index
+ * r*N + n), u: [L, R], dt / lam: [L], A: [N] (A_log used as A), theta: [N/2].
+ * ndims = 0 or 1 selects the reference's 1D recurrence, >= 2 the ND one. */
+typedef struct {
+    long ndims;
+    const long *dims;
+    long L;                 /* used when ndims == 0 */
+    long N, R;
+    const float *u, *dt, *lam, *B, *C, *A, *theta;
+    float default_lambda;
+    int fast_exp;
+    float *h, *Bu, *y;      /* outputs [L,N], [L,N], [L,R] */
+} BlockScanArgs;
+
+typedef struct {
+    float *dB, *dC, *du, *ddt, *dlam, *dA, *dtheta;
+} BlockScanGrads;
+
+int oracle_blockscan_fwd(const BlockScanArgs *a);
+int oracle_blockscan_bwd(const BlockScanArgs *a, const float *dy, BlockScanGrads *g);
+int oracle_blockscan_fwd64(long ndims, const long *dims, long N, long R, const double *u, const double *dt,
+                           const double *lam, const double *B, const double *C, const double *A,
+                           const double *theta, double default_lambda, int fast, double *h, double *y);
+
 #endif

@@ -79,6 +79,10 @@ def _lib(name: str):
             lib.oracle_convnd_fwd.argtypes = [C.POINTER(ConvNDParams)]
             lib.oracle_convnd_bwd.argtypes = [C.POINTER(ConvNDParams)]
             lib.oracle_scannd_fwd_f64.restype = C.c_int
+            lib.oracle_blockscan_fwd.argtypes = [C.POINTER(BlockScanArgs)]
+            lib.oracle_blockscan_bwd.argtypes = [C.POINTER(BlockScanArgs), _f, C.POINTER(BlockScanGrads)]
+            lib.oracle_scannd_bound.argtypes = [C.POINTER(ScanNDParams), C.POINTER(C.c_double),
+                                                C.POINTER(C.c_double)]
         else:
             lib.shim_scannd_ref.argtypes = [C.POINTER(ScanNDParams)]
             lib.shim_scannd_ref_batched.argtypes = [C.POINTER(ScanNDParams), C.c_long]
@@ -174,6 +178,30 @@ def _run_fwd(inp, call):
             raise RuntimeError(f"scan oracle rc={rc}")
         hs[b], ys[b] = h, y
     return hs, ys
+
+
+def scannd_bound(inp: dict):
+    """(Hb, Yb) float64 magnitude bounds of h and y (see oracle_scannd_bound)."""
+    batch = inp.get("batch", 1)
+    P = int(np.prod(inp["dims"]))
+    D, M = inp["D"], inp["M"]
+    Hb = np.zeros((batch, P, D, M))
+    Yb = np.zeros((batch, P, D))
+    lib = _lib("oracle")
+    dp = C.POINTER(C.c_double)
+    for b in range(batch):
+        it = _item(inp, b) if batch > 1 or inp["x"].ndim == 3 else inp
+        h = np.zeros((P, D, M), np.float32)
+        y = np.zeros((P, D), np.float32)
+        keep = []
+        p = scan_params(it, h, y, keep=keep)
+        hb = np.zeros((P, D, M))
+        yb = np.zeros((P, D))
+        rc = lib.oracle_scannd_bound(C.byref(p), hb.ctypes.data_as(dp), yb.ctypes.data_as(dp))
+        if rc != 0:
+            raise RuntimeError("bound failed")
+        Hb[b], Yb[b] = hb, yb
+    return Hb, Yb
 
 
 def oracle_scannd_bwd(inp: dict, h, dy):
@@ -335,3 +363,148 @@ def conv_run(inp, which="oracle", mode=3):
         dk += dki
         db += dbi
     return out, din, dk, db
+
+
+# ------------------------------------------------------------- block scan (Scan-B)
+class BlockScanArgs(C.Structure):
+    _fields_ = [("ndims", C.c_long), ("dims", _l), ("L", C.c_long), ("N", C.c_long), ("R", C.c_long),
+                ("u", _f), ("dt", _f), ("lam", _f), ("B", _f), ("C", _f), ("A", _f), ("theta", _f),
+                ("default_lambda", C.c_float), ("fast_exp", C.c_int),
+                ("h", _f), ("Bu", _f), ("y", _f)]
+
+
+class BlockScanGrads(C.Structure):
+    _fields_ = [(k, _f) for k in ("dB", "dC", "du", "ddt", "dlam", "dA", "dtheta")]
+
+
+def gen_blockscan(dims, N, R, batch=1, seed=0, lam=True, fast_exp=False):
+    """Scan-B inputs shaped like the block produces them: u = silu(.),
+    dt in [dt_min, dt_max], lambda = sigmoid(.), B/C projections, A_log = -1
+    plus noise, theta in [0, 2 pi / N)."""
+    rng = np.random.default_rng(seed)
+    L = int(np.prod(dims))
+    f32 = np.float32
+    z = rng.standard_normal((batch, L, R))
+    out = dict(dims=[int(d) for d in dims], N=N, R=R, batch=batch, fast_exp=int(fast_exp),
+               default_lambda=0.5,
+               u=(z / (1 + np.exp(-z))).astype(f32),
+               dt=np.clip(np.log1p(np.exp(rng.normal(-3.0, 1.0, (batch, L)))), 1e-3, 0.1).astype(f32),
+               B=(rng.standard_normal((batch, L, R * N)) * 0.5).astype(f32),
+               C=(rng.standard_normal((batch, L, R * N)) * 0.5).astype(f32),
+               A=(-1.0 + 0.1 * rng.standard_normal(N)).astype(f32),
+               theta=rng.uniform(0, 2 * np.pi / N, max(N // 2, 1)).astype(f32))
+    out["lam"] = (1 / (1 + np.exp(-rng.standard_normal((batch, L))))).astype(f32) if lam else None
+    return out
+
+
+def _bs_args(inp, b, h, Bu, y, keep):
+    dims = np.ascontiguousarray(inp["dims"], np.int64)
+    keep.append(dims)
+    a = BlockScanArgs()
+    a.ndims = len(dims) if len(dims) > 1 else 1
+    a.dims = dims.ctypes.data_as(_l)
+    a.L = int(np.prod(dims))
+    a.N, a.R = inp["N"], inp["R"]
+    for k in ("u", "dt", "lam", "B", "C"):
+        v = inp.get(k)
+        if v is not None:
+            v = np.ascontiguousarray(v[b])
+            keep.append(v)
+        setattr(a, k, _fp(v))
+    a.A = _fp(inp["A"])
+    a.theta = _fp(inp["theta"])
+    a.default_lambda = inp.get("default_lambda", 0.5)
+    a.fast_exp = inp.get("fast_exp", 0)
+    a.h, a.Bu, a.y = _fp(h), _fp(Bu), _fp(y)
+    return a
+
+
+def oracle_blockscan(inp):
+    """(h[b,L,N], Bu[b,L,N], y[b,L,R]) from the fp32 restatement."""
+    lib = _lib("oracle")
+    batch, L, N, R = inp["batch"], int(np.prod(inp["dims"])), inp["N"], inp["R"]
+    H = np.zeros((batch, L, N), np.float32)
+    BU = np.zeros((batch, L, N), np.float32)
+    Y = np.zeros((batch, L, R), np.float32)
+    for b in range(batch):
+        keep = []
+        a = _bs_args(inp, b, H[b], BU[b], Y[b], keep)
+        assert lib.oracle_blockscan_fwd(C.byref(a)) == 0
+    return H, BU, Y
+
+
+def oracle_blockscan_bwd(inp, h, Bu, dy):
+    """Exact adjoint (double inside); dA / dtheta summed over the batch."""
+    lib = _lib("oracle")
+    batch, L, N, R = inp["batch"], int(np.prod(inp["dims"])), inp["N"], inp["R"]
+    g = dict(dB=np.zeros((batch, L, R * N), np.float32), dC=np.zeros((batch, L, R * N), np.float32),
+             du=np.zeros((batch, L, R), np.float32), ddt=np.zeros((batch, L), np.float32),
+             dlam=np.zeros((batch, L), np.float32), dA=np.zeros(N, np.float32),
+             dtheta=np.zeros(max(N // 2, 1), np.float32))
+    for b in range(batch):
+        keep = []
+        hb, bub = np.ascontiguousarray(h[b]), np.ascontiguousarray(Bu[b])
+        a = _bs_args(inp, b, hb, bub, np.zeros((L, R), np.float32), keep)
+        gg = BlockScanGrads()
+        tmp = {k: np.ascontiguousarray(g[k][b]) for k in ("dB", "dC", "du", "ddt", "dlam")}
+        for k, v in tmp.items():
+            setattr(gg, k, _fp(v))
+        gg.dA, gg.dtheta = _fp(g["dA"]), _fp(g["dtheta"])
+        dyb = np.ascontiguousarray(dy[b], np.float32)
+        assert lib.oracle_blockscan_bwd(C.byref(a), dyb.ctypes.data_as(_f), C.byref(gg)) == 0
+        for k, v in tmp.items():
+            g[k][b] = v
+    return g
+
+
+def blockscan_fwd64(inp, b=0, over=None):
+    lib = _lib("oracle")
+    d = {k: (None if inp.get(k) is None else np.asarray(inp[k], np.float64)) for k in ("u", "dt", "lam", "B", "C")}
+    d = {k: (None if v is None else np.ascontiguousarray(v[b])) for k, v in d.items()}
+    d["A"] = np.asarray(inp["A"], np.float64)
+    d["theta"] = np.asarray(inp["theta"], np.float64)
+    if over:
+        d.update({k: np.ascontiguousarray(v, np.float64) for k, v in over.items()})
+    dims = np.ascontiguousarray(inp["dims"], np.int64)
+    L, N, R = int(np.prod(dims)), inp["N"], inp["R"]
+    h = np.zeros(L * N)
+    y = np.zeros(L * R)
+    dp = C.POINTER(C.c_double)
+    ptr = lambda a: None if a is None else a.ctypes.data_as(dp)
+    rc = lib.oracle_blockscan_fwd64(C.c_long(len(dims)), dims.ctypes.data_as(_l), C.c_long(N), C.c_long(R),
+                                    ptr(d["u"]), ptr(d["dt"]), ptr(d["lam"]), ptr(d["B"]), ptr(d["C"]),
+                                    ptr(d["A"]), ptr(d["theta"]), C.c_double(inp.get("default_lambda", 0.5)),
+                                    C.c_int(inp.get("fast_exp", 0)), h.ctypes.data_as(dp), y.ctypes.data_as(dp))
+    assert rc == 0
+    return h.reshape(L, N), y.reshape(L, R)
+
+
+def ref_block_run(dims, dim, N, R, params, x, dt_min=1e-3, dt_max=0.1, default_lambda=0.5, fast_exp=0, dy=None):
+    """The reference MambaBlock forward (and backward when dy is given) on one
+    item: returns (out, ws dict, grads dict)."""
+    lib = _lib("ref")
+    L = int(np.prod(dims))
+    NR = N * R
+    dims_a = np.ascontiguousarray(dims, np.int64)
+    order = ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "lambda_proj", "b_B", "b_C", "theta")
+    parr = [np.ascontiguousarray(params[k], np.float32) for k in order]
+    pp = (_f * 10)(*[a.ctypes.data_as(_f) for a in parr])
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros((L, dim), np.float32)
+    ws = {k: np.zeros(s, np.float32) for k, s in (("u", (L, R)), ("dt", (L,)), ("lam", (L,)), ("B", (L, NR)),
+                                                   ("C", (L, NR)), ("h", (L, N)), ("Bu", (L, N)), ("y", (L, R)))}
+    wsp = (_f * 8)(*[ws[k].ctypes.data_as(_f) for k in ("u", "dt", "lam", "B", "C", "h", "Bu", "y")])
+    gnames = ("g_A_log", "g_theta", "d_scan_B", "d_scan_C", "d_delta", "d_lambda", "g_W_out", "g_W_B",
+              "g_W_C", "g_b_B", "g_b_C", "g_delta_proj", "g_lambda_proj")
+    gshapes = ((N,), (max(N // 2, 1),), (L, NR), (L, NR), (L,), (L,), (dim, R), (NR, dim), (NR, dim), (NR,),
+               (NR,), (dim,), (dim,))
+    grads = {k: np.zeros(s, np.float32) for k, s in zip(gnames, gshapes)} if dy is not None else {}
+    gp = (_f * 13)(*[grads[k].ctypes.data_as(_f) for k in gnames]) if dy is not None else None
+    dyp = np.ascontiguousarray(dy, np.float32).ctypes.data_as(_f) if dy is not None else None
+    lib.shim_block_run.restype = C.c_int
+    rc = lib.shim_block_run(dims_a.ctypes.data_as(_l), C.c_long(len(dims)), C.c_long(dim), C.c_long(N), C.c_long(R),
+                            pp, C.c_float(dt_min), C.c_float(dt_max), C.c_float(default_lambda), C.c_int(fast_exp),
+                            x.ctypes.data_as(_f), out.ctypes.data_as(_f), wsp, dyp, gp)
+    if rc != 0:
+        raise RuntimeError("reference block run failed")
+    return out, ws, grads

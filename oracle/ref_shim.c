@@ -80,3 +80,88 @@ int shim_set_threads(int n) {
     if (n > 0) omp_set_num_threads(n);
     return omp_get_max_threads();
 }
+
+/* ------------------------------------------------------------------------
+ * Reference MambaBlock (src/mamba_block.c) driven through its public API.
+ * params: W_in[R,dim], W_out[dim,R], A_log[N], W_B[NR,dim], W_C[NR,dim],
+ * delta_proj[dim], lambda_proj[dim], b_B[NR], b_C[NR], theta[N/2].
+ * Runs mamba_block_forward_ws on one item (src/mamba_block.c:509-528) and
+ * exports the workspace: u[L,R], dt[L], lam[L], scan_B/C[L,NR], h[L,N],
+ * Bu[L,N], y_rank[L,R] and the block output out[L,dim].  When dy != NULL it
+ * then runs mamba_backward_ws (src/mamba_block.c:746-773) and exports the
+ * reference's gradients (grads: g_A_log[N], g_theta[N/2], d_scan_B[L,NR],
+ * d_scan_C[L,NR], d_delta[L], d_lambda[L], g_W_out[dim,R], g_W_B, g_W_C,
+ * g_b_B, g_b_C, g_delta_proj, g_lambda_proj; NULL entries are skipped).
+ */
+#include "kmamba.h"
+
+static MambaBlock *shim_block_make(const long *dims, long ndims, long dim, long N, long R,
+                                   const float *const *params, float dt_min, float dt_max,
+                                   float default_lambda, int use_fast_exp) {
+    MBConfig cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    long L = 1;
+    for (long i = 0; i < ndims; i++) L *= dims[i];
+    cfg.max_ndims = 8;
+    cfg.max_state = N;
+    cfg.use_fast_exp = use_fast_exp;
+    cfg.dim = (size_t)dim;
+    cfg.state_size = (size_t)N;
+    cfg.seq_len = (size_t)L;
+    cfg.mimo_rank = (size_t)R;
+    cfg.dt_scale = 1.0f;
+    cfg.dt_min = dt_min;
+    cfg.dt_max = dt_max;
+    cfg.default_lambda = default_lambda;
+    cfg.use_a_log_clamp = 1;
+    cfg.a_log_min = -1e-5f;
+    cfg.spatial_ndims = ndims;
+    for (long i = 0; i < ndims; i++) cfg.spatial_dims[i] = dims[i];
+    MambaBlock *blk = mamba_block_create(&cfg);
+    if (!blk) return NULL;
+    const size_t NR = (size_t)N * R, TS = N / 2 > 0 ? N / 2 : 1;
+    memcpy(blk->W_in.data, params[0], sizeof(float) * R * dim);
+    memcpy(blk->W_out.data, params[1], sizeof(float) * dim * R);
+    memcpy(blk->A_log.data, params[2], sizeof(float) * N);
+    memcpy(blk->W_B.data, params[3], sizeof(float) * NR * dim);
+    memcpy(blk->W_C.data, params[4], sizeof(float) * NR * dim);
+    memcpy(blk->delta_proj.data, params[5], sizeof(float) * dim);
+    memcpy(blk->lambda_proj.data, params[6], sizeof(float) * dim);
+    memcpy(blk->b_B, params[7], sizeof(float) * NR);
+    memcpy(blk->b_C, params[8], sizeof(float) * NR);
+    memcpy(blk->theta, params[9], sizeof(float) * TS);
+    return blk;
+}
+
+int shim_block_run(const long *dims, long ndims, long dim, long N, long R, const float *const *params,
+                   float dt_min, float dt_max, float default_lambda, int use_fast_exp,
+                   const float *x, float *out, float *const *ws_out, const float *dy, float *const *grads) {
+    MambaBlock *blk = shim_block_make(dims, ndims, dim, N, R, params, dt_min, dt_max, default_lambda, use_fast_exp);
+    if (!blk) return -1;
+    MambaBlockWorkspace *ws = mamba_block_workspace_create(blk);
+    if (!ws) { mamba_block_free(blk); return -1; }
+    const size_t L = blk->config.seq_len, NR = (size_t)N * R;
+    mamba_block_forward_ws(blk, ws, out, x, 1);
+    const float *src[8] = {ws->u_seq, ws->delta, ws->lambda_seq, ws->scan_B, ws->scan_C, ws->h_seq, ws->Bu_seq, ws->y_rank};
+    const size_t n[8] = {L * R, L, L, L * NR, L * NR, L * N, L * N, L * R};
+    for (int i = 0; i < 8; i++) if (ws_out && ws_out[i]) memcpy(ws_out[i], src[i], sizeof(float) * n[i]);
+    if (dy) {
+        MBOptimConfig oc;
+        memset(&oc, 0, sizeof(oc));
+        mamba_attach_optimizer(blk, OPTIMIZER_ADAMW, &oc);
+        mamba_zero_grads(blk);
+        float *dinp = (float *)malloc(sizeof(float) * L * dim);
+        mamba_backward_ws(blk, ws, dy, x, dinp, 0);
+        free(dinp);
+        MBOptimState *g = blk->opt_state;
+        const size_t TS = N / 2 > 0 ? N / 2 : 1;
+        const float *gs[13] = {g->g_A_log, g->g_theta, ws->d_scan_B, ws->d_scan_C, ws->d_delta, ws->d_lambda,
+                               g->g_W_out, g->g_W_B, g->g_W_C, g->g_b_B, g->g_b_C, g->g_delta_proj, g->g_lambda_proj};
+        const size_t gn[13] = {(size_t)N, TS, L * NR, L * NR, L, L, (size_t)dim * R, NR * dim, NR * dim, NR, NR,
+                               (size_t)dim, (size_t)dim};
+        for (int i = 0; i < 13; i++) if (grads && grads[i]) memcpy(grads[i], gs[i], sizeof(float) * gn[i]);
+    }
+    mamba_block_workspace_free(ws);
+    mamba_block_free(blk);
+    return 0;
+}

@@ -140,6 +140,16 @@ static double o_hat64(const double *h, long base, long D, long M, long d, long m
     return (d & 1) ? s * h0 + c * h1 : c * h0 - s * h1;
 }
 
+/* |R| h for the magnitude bound (all entries non-negative). */
+static double o_hatabs64(const double *h, long base, long D, long M, long d, long m,
+                         const double *cs, const double *sn) {
+    if (!cs) return h[base + d * M + m];
+    if ((D & 1) && d == D - 1) return h[base + d * M + m];
+    long d0 = d & ~1L;
+    double h0 = h[base + d0 * M + m], h1 = h[base + (d0 + 1) * M + m];
+    return cs[d0 >> 1] * ((d & 1) ? h1 : h0) + sn[d0 >> 1] * ((d & 1) ? h0 : h1);
+}
+
 int oracle_scannd_fwd_f64(const long *dims, long nd, long D, long M,
                           const double *x, const double *A, const double *B,
                           const double *C, const double *delta,
@@ -316,4 +326,58 @@ int oracle_scannd_bwd(const ScanNDParams *p, float *dx) {
 fail:
     free(acc_hat); free(acc_bu); free(hd); free(gA); free(gth);
     return -1;
+}
+
+/* Magnitude bound of the forward: the same recurrence evaluated in double on
+ * absolute values (|x|, |B|, |C|, |cos|, |sin|; alpha, beta, gamma >= 0 for
+ * lambda in [0,1]).  Hb(p) bounds the sum of the absolute values of every
+ * term that contributes to h(p), so fp32 rounding in any evaluation order is
+ * O(eps * Hb); the parity tests scale their tolerance by it. */
+int oracle_scannd_bound(const ScanNDParams *p, double *Hb, double *Yb) {
+    if (!o_valid(p)) return -1;
+    const long nd = p->ndims, D = p->D, M = p->M;
+    const long P = o_points(p->dims, nd);
+    long st[MAXND], idx[MAXND];
+    o_strides(p->dims, nd, st);
+    double *cs = NULL, *sn = NULL;
+    if (p->theta) {
+        cs = (double *)malloc(sizeof(double) * (D / 2 + 1));
+        sn = (double *)malloc(sizeof(double) * (D / 2 + 1));
+        for (long i = 0; i < D / 2; i++) { cs[i] = fabs(cos((double)p->theta[i])); sn[i] = fabs(sin((double)p->theta[i])); }
+    }
+    for (long off = 0; off < P; off++) {
+        o_unravel(off, p->dims, st, nd, idx);
+        double lam = p->lambda ? p->lambda[off] : p->default_lambda;
+        double lam1 = fabs(1.0 - lam);
+        lam = fabs(lam);
+        for (long d = 0; d < D; d++) {
+            double xv = fabs(p->x[off * D + d]), dt = 0.0, yacc = 0.0;
+            for (long a = 0; a < nd; a++) dt += fabs(p->delta[(a * P + off) * D + d]);
+            for (long m = 0; m < M; m++) {
+                long pdm = off * D * M + d * M + m;
+                double but = fabs(p->B[pdm]) * xv, buacc = 0, dacc = 0, hacc = 0;
+                int n = 0;
+                for (long a = 0; a < nd; a++) {
+                    if (idx[a] > 0) {
+                        long q = off - st[a];
+                        double av = p->A[(a * D + d) * M + m];
+                        if (p->use_a_log_clamp && av > p->a_log_min) av = p->a_log_min;
+                        double al = fabs(o_exp64(p->delta[(a * P + off) * D + d] * av, p->use_fast_exp));
+                        buacc += fabs(p->B[q * D * M + d * M + m]) * fabs(p->x[q * D + d]);
+                        dacc += al;
+                        hacc += al * o_hatabs64(Hb, q * D * M, D, M, d, m, cs, sn);
+                        n++;
+                    }
+                }
+                double hn = but * lam * dt + hacc;
+                if (n > 0) hn += (buacc / n) * lam1 * dt * (dacc / n);
+                Hb[pdm] = hn;
+                yacc += fabs(p->C[pdm]) * hn;
+            }
+            Yb[off * D + d] = yacc;
+        }
+    }
+    free(cs);
+    free(sn);
+    return 0;
 }

@@ -64,25 +64,63 @@ def scan_bwd(inp, h, dy, dev, with_dx=True):
     return out
 
 
-def assert_scan_close(h, y, href, yref, Cm, rtol=1e-4, atol=1e-5):
-    """Parity criterion: identical non-finite masks; on finite entries
-    |h - h_ref| <= atol + rtol |h_ref| and |y - y_ref| <= atol + rtol * sum_m |C h_ref|
-    (the y bound uses the magnitude of the summed terms: y is a sum over M
-    states whose rounding error scales with sum |C h|, not with |y|)."""
+EPS32 = 2.0 ** -24
+
+
+def _item(inp, b):
+    out = dict(inp, batch=1)
+    for k in ("x", "B", "C", "delta", "lambda"):
+        if inp.get(k) is not None:
+            out[k] = np.ascontiguousarray(inp[k][b:b + 1])
+    return out
+
+
+def assert_scan_close(h, y, inp, href=None, yref=None, rtol=1e-4, atol=1e-5, kappa=64.0):
+    """Parity criterion for the Scan-A forward (h and y), per batch item:
+
+    1. identical non-finite masks against the fp32 reference;
+    2. elementwise: |g - ref| <= atol + rtol*|ref| + kappa*eps32*Hb, where Hb is
+       the recurrence evaluated on absolute values (oracle_scannd_bound): the
+       magnitude of every term feeding that entry, i.e. what fp32 rounding in
+       any evaluation order scales with (cancellation makes |ref| << Hb);
+    3. normwise against the exact double-precision result:
+       ||g - exact|| <= max(4 ||ref - exact||, 1e-5 ||exact||): the GPU result is
+       within 1e-5 normwise relative of the exact value (10x inside the 1e-4
+       parity tolerance), or as accurate as the reference's own fp32
+       evaluation up to a factor 4 (CUDA expf is a 2-ulp function, glibc's is
+       sub-ulp, and the recurrence compounds that over every level).
+    Returns (worst elementwise ratio, worst normwise ratio)."""
+    from oracle import pyoracle as po
+    if href is None:
+        href, yref = po.oracle_scannd(inp)
+    Hb, Yb = po.scannd_bound(inp)
     assert np.array_equal(np.isfinite(h), np.isfinite(href)), "non-finite mask of h differs"
     assert np.array_equal(np.isfinite(y), np.isfinite(yref)), "non-finite mask of y differs"
-    fh = np.isfinite(href)
-    err_h = np.abs(h[fh].astype(np.float64) - href[fh])
-    bound_h = atol + rtol * np.abs(href[fh].astype(np.float64))
-    worst = float((err_h / bound_h).max()) if err_h.size else 0.0
-    assert worst <= 1.0, f"h exceeds tolerance: worst err/bound {worst:.3g}"
-    scale = np.abs(Cm.astype(np.float64) * href.astype(np.float64)).sum(-1)
-    fy = np.isfinite(yref) & np.isfinite(scale)
-    err_y = np.abs(y[fy].astype(np.float64) - yref[fy])
-    bound_y = atol + rtol * scale[fy]
-    worst_y = float((err_y / bound_y).max()) if err_y.size else 0.0
-    assert worst_y <= 1.0, f"y exceeds tolerance: worst err/bound {worst_y:.3g}"
-    return worst, worst_y
+    worst_e, worst_n = 0.0, 0.0
+    for g, r, bnd, name in ((h, href, Hb, "h"), (y, yref, Yb, "y")):
+        f = np.isfinite(r) & np.isfinite(bnd)
+        err = np.abs(g[f].astype(np.float64) - r[f])
+        bound = atol + rtol * np.abs(r[f].astype(np.float64)) + kappa * EPS32 * bnd[f]
+        if err.size:
+            ratio = err / bound
+            k = int(ratio.argmax())
+            worst_e = max(worst_e, float(ratio[k]))
+            assert ratio[k] <= 1.0, (f"{name}: elementwise err/bound {ratio[k]:.3g} at flat index {k}: "
+                                     f"got {g[f][k]!r} ref {r[f][k]!r} bound-scale {bnd[f][k]:.3g}")
+    batch = h.shape[0]
+    for b in range(batch):
+        one = _item(inp, b)
+        if not np.isfinite(href[b]).all():
+            continue
+        h64, y64 = po.fwd64(one)
+        for g, r, ex, name in ((h[b], href[b], h64, "h"), (y[b], yref[b], y64, "y")):
+            e_g = np.linalg.norm(g.astype(np.float64).ravel() - ex.ravel())
+            e_r = np.linalg.norm(r.astype(np.float64).ravel() - ex.ravel())
+            lim = max(4.0 * e_r, 1e-5 * np.linalg.norm(ex.ravel())) + 1e-30
+            worst_n = max(worst_n, e_g / lim)
+            assert e_g <= lim, (f"{name}[item {b}]: ||gpu-exact|| {e_g:.3g} > max(4||ref-exact|| "
+                                f"{e_r:.3g}, 1e-5||exact||)")
+    return worst_e, worst_n
 
 
 def assert_grad_close(got, ref, name, rtol=1e-3):

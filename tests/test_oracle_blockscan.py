@@ -1,0 +1,67 @@
+"""CPU tests pinning the Mamba-3 block-scan (Scan-B) oracle.
+
+* The fp32 restatement reproduces, bit for bit, the scan states and rank
+  outputs the reference MambaBlock forward leaves in its workspace
+  (src/mamba_block.c:384-470 via mamba_block_forward_ws, driven through the
+  reference's public API in oracle/_ref) for 1D, 2D and 3D grids.
+* The double-precision adjoint matches central finite differences of the
+  double forward (the reference's own block backward averages predecessors
+  and is not an exact gradient, src/mamba_block.c:640-695).
+"""
+import numpy as np
+import pytest
+
+from oracle import pyoracle as po
+
+
+def _block_params(rng, dim, N, R):
+    NR = N * R
+    return dict(W_in=rng.uniform(-.3, .3, (R, dim)), W_out=rng.uniform(-.3, .3, (dim, R)), A_log=-np.ones(N),
+                W_B=rng.uniform(-.3, .3, (NR, dim)), W_C=rng.uniform(-.3, .3, (NR, dim)),
+                delta_proj=rng.normal(0, .5, dim), lambda_proj=rng.normal(0, .02, dim),
+                b_B=rng.normal(0, .1, NR), b_C=rng.normal(0, .1, NR), theta=rng.uniform(0, 2 * np.pi / N, N // 2))
+
+
+@pytest.mark.skipif(not po.have_ref(), reason="reference build not available")
+@pytest.mark.parametrize("dims,N,R", [([6, 5], 8, 2), ([24], 8, 2), ([3, 4, 2], 6, 3), ([8, 8], 16, 4)])
+def test_blockscan_restatement_bit_equal_reference(dims, N, R):
+    rng = np.random.default_rng(sum(dims) + N)
+    dim = 16
+    params = _block_params(rng, dim, N, R)
+    x = rng.standard_normal((int(np.prod(dims)), dim)).astype(np.float32)
+    _, ws, _ = po.ref_block_run(dims, dim, N, R, params, x)
+    inp = dict(dims=dims, N=N, R=R, batch=1, fast_exp=0, default_lambda=0.5, u=ws["u"][None], dt=ws["dt"][None],
+               lam=ws["lam"][None], B=ws["B"][None], C=ws["C"][None], A=params["A_log"].astype(np.float32),
+               theta=params["theta"].astype(np.float32))
+    h, Bu, y = po.oracle_blockscan(inp)
+    np.testing.assert_array_equal(h[0], ws["h"])
+    np.testing.assert_array_equal(Bu[0], ws["Bu"])
+    np.testing.assert_array_equal(y[0], ws["y"])
+
+
+@pytest.mark.parametrize("dims,fast", [([4, 3], False), ([5], False), ([2, 3, 2], True)])
+def test_blockscan_adjoint_matches_finite_differences(dims, fast):
+    N, R = 6, 2
+    inp = po.gen_blockscan(dims, N, R, batch=1, seed=3, fast_exp=fast)
+    L = int(np.prod(dims))
+    h64, _ = po.blockscan_fwd64(inp)
+    _, Bu, _ = po.oracle_blockscan(inp)
+    dy = np.random.default_rng(1).standard_normal((1, L, R)).astype(np.float32)
+    g = po.oracle_blockscan_bwd(inp, h64[None].astype(np.float32), Bu, dy)
+
+    def loss(over):
+        _, yy = po.blockscan_fwd64(inp, 0, over)
+        return float((yy * dy[0]).sum())
+
+    eps = 1e-6
+    for name, gname, src in (("u", "du", inp["u"][0]), ("dt", "ddt", inp["dt"][0]), ("lam", "dlam", inp["lam"][0]),
+                             ("B", "dB", inp["B"][0]), ("C", "dC", inp["C"][0]), ("A", "dA", inp["A"]),
+                             ("theta", "dtheta", inp["theta"])):
+        base = src.astype(np.float64)
+        gg = g[gname] if gname in ("dA", "dtheta") else g[gname][0]
+        for idx in list(np.ndindex(base.shape))[::max(1, base.size // 9)]:
+            pp, mm = base.copy(), base.copy()
+            pp[idx] += eps
+            mm[idx] -= eps
+            fd = (loss({name: pp}) - loss({name: mm})) / (2 * eps)
+            assert abs(fd - gg[idx]) <= 1e-4 * (abs(fd) + 1e-2), (name, idx, fd, gg[idx])
