@@ -54,7 +54,7 @@ def test_config1_2d_rope(kmb, cuda):
     ([64, 64], 64, 64, dict(rope=True), 1),          # headline geometry, fewer channels
     ([64, 64], 32, 64, dict(lam=True), 1),
     ([16, 80], 32, 32, dict(rope=True, lam=True), 1),  # inner axis 0 (columns)
-    ([80, 16], 16, 16, dict(lam=True, fast_exp=True), 1),
+    ([80, 16], 16, 16, dict(lam=True, fast_exp=True), 0),  # fast exp -> generic
     ([20, 12], 32, 16, dict(clamp=True, a_log_min=-2.0), 1),   # partial last stage
     ([100], 16, 16, dict(rope=True), 1),
     ([4, 6, 5], 6, 3, dict(rope=True, lam=True), 0),  # 3D -> generic
