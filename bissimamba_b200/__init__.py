@@ -52,6 +52,7 @@ EXPORTS = [
     "scannd_batched", "scannd_backward_batched", "scannd_forward_async", "scannd_backward_async",
     "convnd_kernel_volume", "convnd_forward_wavefront", "convnd_backward_wavefront", "convnd",
     "om_convnd_forward", "om_convnd_backward", "convnd_status", "convnd_batched_async",
+    "convnd_backward_noalloc", "convnd_backward_noalloc_error",
     "wavefront_nd_validate_dims", "wavefront_nd_total_points", "wavefront_nd_max_level",
     "wavefront_nd_row_major_offset", "wavefront_nd_level_size", "wavefront_nd_for_level",
     "wavefront_nd_for_each_level", "km_wavefront_plan_create", "km_wavefront_plan_free",
@@ -85,6 +86,8 @@ def lib():
         L.convnd.restype = None
         L.convnd_batched_async.argtypes = [Q, C.c_long, C.c_int, C.c_void_p]
         L.om_convnd_forward.argtypes = [Q]
+        L.convnd_backward_noalloc.argtypes = [Q, C.c_long, C.c_void_p]
+        L.convnd_backward_noalloc_error.restype = C.c_char_p
         L.om_convnd_backward.argtypes = [Q]
         L.convnd_forward_wavefront.argtypes = [Q, C.c_void_p]
         L.convnd_forward_wavefront.restype = None

@@ -212,4 +212,138 @@ cudaError_t launch_conv_bwd(const ConvDesc& c, const float* in, const float* ker
     return cudaGetLastError();
 }
 
+
+
+// ---------------------------------------------------------------------------
+// convnd backward without any allocation.
+//
+// Some callers cannot allocate device memory: code that runs where
+// cudaMalloc is forbidden or unsafe (inside a caller-owned memory pool or
+// arena that must not grow, allocator hooks, real-time paths that may not
+// take the allocator's locks).  For them the dkernel/dbias partial sums live
+// in one fixed device array that is part of the loaded library.
+//
+// Limit: the partial-sum array holds kNoAllocScratchFloats floats (4 MiB);
+// a call needs (K^ndims + 1) * D floats per row chunk and at least one chunk,
+// so it is rejected when (K^ndims + 1) * D > kNoAllocScratchFloats.
+// The array is shared by every call on a device and keeps the last call's
+// contents; the kernels overwrite every entry they read, so nothing needs
+// clearing.  Calls whose work overlaps on the GPU (different streams, or
+// host threads without ordering) race on the array.
+// ---------------------------------------------------------------------------
+constexpr long long kNoAllocScratchFloats = 1 << 20;
+static __device__ __align__(256) float g_conv_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+static float* g_noalloc_ptr[kNoAllocMaxDevices];
+
+// Device address of the array on the current device.  The first call on a
+// device resolves it (cudaGetSymbolAddress); make that first call before any
+// stream capture.
+static cudaError_t noalloc_scratch_ptr(float** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+    float* p = __atomic_load_n(&g_noalloc_ptr[dev], __ATOMIC_ACQUIRE);
+    if (!p) {
+        e = cudaGetSymbolAddress((void**)&p, g_conv_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        __atomic_store_n(&g_noalloc_ptr[dev], p, __ATOMIC_RELEASE);
+    }
+    *out = p;
+    return cudaSuccess;
+}
+
+static cudaError_t launch_conv_bwd_noalloc(const ConvDesc& c, const float* in, const float* ker, const float* dy,
+                                           float* din, float* dker, float* dbias, cudaStream_t st) {
+    const long long per_chunk = (long long)(c.V + 1) * c.D;
+    if (per_chunk > kNoAllocScratchFloats) return cudaErrorInvalidValue;
+    float* part = nullptr;
+    cudaError_t e = noalloc_scratch_ptr(&part);
+    if (e != cudaSuccess) return e;
+    long long nch = conv_chunks(c);
+    if (nch > kNoAllocScratchFloats / per_chunk) nch = kNoAllocScratchFloats / per_chunk;
+    const long long rows = c.batch * c.P;
+    const long long rpc = (rows + nch - 1) / nch;
+    conv_bwd_input_kernel<<<cblk(c.batch * c.P * c.D, 256), 256, 0, st>>>(c, dy, ker, din);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    dim3 grid(cblk(c.D, 32), (unsigned)nch);
+    conv_bwd_kernel_partial<<<grid, 256, 0, st>>>(c, in, dy, part, rpc);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const long long cnt = (long long)c.V * c.D;
+    reduce_rows_set<<<cblk(cnt, 256), 256, 0, st>>>(part, dker, cnt, nch, per_chunk);
+    if (dbias) reduce_rows_set<<<cblk(c.D, 256), 256, 0, st>>>(part + cnt, dbias, c.D, nch, per_chunk);
+    return cudaGetLastError();
+}
+
 }  // namespace kmb
+
+#include <cstdio>
+#include <cstring>
+#include "../../include/convnd.h"
+
+static thread_local char tl_noalloc_err[160];
+
+static bool noalloc_is_device(const void* p) {
+    if (!p) return true;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+extern "C" const char* convnd_backward_noalloc_error(void) { return tl_noalloc_err; }
+
+extern "C" int convnd_backward_noalloc(ConvNDParams* p, long batch, void* stream) {
+    tl_noalloc_err[0] = 0;
+    if (!p || !p->dims || p->ndims <= 0 || p->ndims > KMB_MAXND || p->D <= 0 || p->K <= 0 || batch < 1 ||
+        !p->input || !p->kernel || !p->dy || !p->dinput || !p->dkernel) {
+        snprintf(tl_noalloc_err, sizeof tl_noalloc_err, "invalid ConvNDParams");
+        return -1;
+    }
+    const void* ptrs[] = {p->input, p->kernel, p->dy, p->dinput, p->dkernel, p->dbias};
+    for (const void* q : ptrs)
+        if (!noalloc_is_device(q)) {
+            snprintf(tl_noalloc_err, sizeof tl_noalloc_err, "convnd_backward_noalloc needs device pointers");
+            return -1;
+        }
+    kmb::ConvDesc c;
+    memset(&c, 0, sizeof c);
+    c.nd = (int)p->ndims;
+    c.D = (int)p->D;
+    c.K = (int)p->K;
+    long long v = 1, P = 1;
+    for (long i = 0; i < p->ndims; i++) {
+        if (p->dims[i] <= 0) {
+            snprintf(tl_noalloc_err, sizeof tl_noalloc_err, "invalid dims");
+            return -1;
+        }
+        v *= p->K;
+        P *= p->dims[i];
+    }
+    c.V = (int)v;
+    c.P = P;
+    c.batch = batch;
+    long long st = 1;
+    for (int a = c.nd - 1; a >= 0; a--) {
+        c.dims[a] = p->dims[a];
+        c.strides[a] = st;
+        st *= p->dims[a];
+    }
+    if ((long long)(c.V + 1) * c.D > kmb::kNoAllocScratchFloats) {
+        snprintf(tl_noalloc_err, sizeof tl_noalloc_err,
+                 "convnd_backward_noalloc: (K^ndims + 1) * D = %lld exceeds the %lld-float scratch limit",
+                 (long long)(c.V + 1) * c.D, kmb::kNoAllocScratchFloats);
+        return -1;
+    }
+    cudaError_t e = kmb::launch_conv_bwd_noalloc(c, p->input, p->kernel, p->dy, p->dinput, p->dkernel, p->dbias,
+                                                 (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        snprintf(tl_noalloc_err, sizeof tl_noalloc_err, "convnd_backward_noalloc: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
