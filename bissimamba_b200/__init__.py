@@ -44,6 +44,19 @@ class ConvNDParams(C.Structure):
     ]
 
 
+class KMBlockScanParams(C.Structure):
+    """include/kmamba_block.h"""
+    _fields_ = [("ndims", C.c_long), ("dims", _l), ("L", C.c_long), ("N", C.c_long), ("R", C.c_long),
+                ("u", C.c_void_p), ("dt", C.c_void_p), ("lambda_", C.c_void_p), ("B", C.c_void_p),
+                ("C", C.c_void_p), ("A_log", C.c_void_p), ("theta", C.c_void_p),
+                ("default_lambda", C.c_float), ("use_fast_exp", C.c_int),
+                ("h", C.c_void_p), ("Bu", C.c_void_p), ("y", C.c_void_p)]
+
+
+class KMBlockScanGrads(C.Structure):
+    _fields_ = [(k, C.c_void_p) for k in ("dB", "dC", "du", "ddt", "dlambda", "dA_log", "dtheta")]
+
+
 CONVND_FORWARD, CONVND_BACKWARD, CONVND_COMPLETE = 1, 2, 3
 
 # every symbol the public headers declare (checked by the CPU tests)
@@ -59,6 +72,7 @@ EXPORTS = [
     "km_wavefront_plan_matches_dims", "km_wavefront_plan_level_size", "km_wavefront_plan_level_offsets",
     "km_wavefront_plan_iter_forward", "km_wavefront_plan_iter_reverse",
     "kmb_last_error", "kmb_last_forward_path", "kmb_set_force_generic",
+    "kmb_blockscan_forward", "kmb_blockscan_backward",
 ]
 
 _lib = None
@@ -96,6 +110,9 @@ def lib():
         L.convnd_kernel_volume.argtypes = [C.c_long, C.c_long]
         L.convnd_kernel_volume.restype = C.c_long
         L.kmb_last_error.restype = C.c_char_p
+        L.kmb_blockscan_forward.argtypes = [C.POINTER(KMBlockScanParams), C.c_long, C.c_void_p]
+        L.kmb_blockscan_backward.argtypes = [C.POINTER(KMBlockScanParams), C.c_long, C.c_void_p,
+                                             C.POINTER(KMBlockScanGrads), C.c_void_p]
         L.kmb_set_force_generic.argtypes = [C.c_int]
         L.kmb_set_force_generic.restype = None
         L.km_wavefront_plan_create.argtypes = [_l, C.c_long, C.c_long]
@@ -175,3 +192,21 @@ def conv_params(dims, D, K, inp=None, kernel=None, bias=None, out=None, dy=None,
 def check(rc: int, what: str = "call"):
     if rc != 0:
         raise RuntimeError(f"{what} failed: {last_error()}")
+
+
+def blockscan_params(dims, N, R, u, dt, lam, B, Cm, A_log, theta, h, Bu, y, default_lambda=0.5, use_fast_exp=0):
+    p = KMBlockScanParams()
+    darr = dims_array(dims)
+    p._dims_keep = darr
+    p.ndims = len(dims)
+    p.dims = C.cast(darr, _l)
+    L = 1
+    for d in dims:
+        L *= int(d)
+    p.L, p.N, p.R = L, int(N), int(R)
+    p.u, p.dt, p.lambda_, p.B, p.C = _ptr(u), _ptr(dt), _ptr(lam), _ptr(B), _ptr(Cm)
+    p.A_log, p.theta = _ptr(A_log), _ptr(theta)
+    p.default_lambda = float(default_lambda)
+    p.use_fast_exp = int(use_fast_exp)
+    p.h, p.Bu, p.y = _ptr(h), _ptr(Bu), _ptr(y)
+    return p

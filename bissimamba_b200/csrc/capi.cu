@@ -74,7 +74,7 @@ bool force_generic() {
 }
 
 // ---------------------------------------------------------------- workspace
-enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 3 };
+enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 8 };  // 3, 4: blockscan
 struct Ws {
     void* p = nullptr;
     size_t n = 0;
@@ -100,6 +100,16 @@ void* ws_get(int slot, size_t bytes) {
 }
 
 int* status_word() { return (int*)ws_get(WS_STATUS, 256); }
+
+}  // namespace
+
+namespace kmb {
+void* workspace(int slot, size_t bytes) { return ws_get(slot, bytes); }
+int set_error(const char* msg) { return fail(msg); }
+int set_cuda_error(const char* where, cudaError_t e) { return fail_cuda(where, e); }
+}  // namespace kmb
+
+namespace {
 
 // ----------------------------------------------------------- pointer kinds
 enum PtrKind { PK_NULL = 0, PK_HOST = 1, PK_DEVICE = 2, PK_OTHER_DEVICE = 3 };
