@@ -57,6 +57,38 @@ class KMBlockScanGrads(C.Structure):
     _fields_ = [(k, C.c_void_p) for k in ("dB", "dC", "du", "ddt", "dlambda", "dA_log", "dtheta")]
 
 
+class KMBlockConfig(C.Structure):
+    _fields_ = [("dim", C.c_long), ("N", C.c_long), ("R", C.c_long), ("ndims", C.c_long), ("dims", _l),
+                ("L", C.c_long), ("dt_min", C.c_float), ("dt_max", C.c_float), ("default_lambda", C.c_float),
+                ("use_fast_exp", C.c_int)]
+
+
+BLOCK_FIELDS = ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "lambda_proj", "b_B", "b_C", "theta")
+
+
+class KMBlockWeights(C.Structure):
+    _fields_ = [(k, C.c_void_p) for k in BLOCK_FIELDS]
+
+
+class KMBlockGrads(C.Structure):
+    _fields_ = [(k, C.c_void_p) for k in BLOCK_FIELDS]
+
+
+def block_config(dims, dim, N, R, dt_min=1e-3, dt_max=0.1, default_lambda=0.5, use_fast_exp=0):
+    c = KMBlockConfig()
+    darr = dims_array(dims)
+    c._dims_keep = darr
+    c.dim, c.N, c.R = int(dim), int(N), int(R)
+    c.ndims = len(dims)
+    c.dims = C.cast(darr, _l)
+    L = 1
+    for d in dims:
+        L *= int(d)
+    c.L = L
+    c.dt_min, c.dt_max, c.default_lambda, c.use_fast_exp = dt_min, dt_max, default_lambda, use_fast_exp
+    return c
+
+
 CONVND_FORWARD, CONVND_BACKWARD, CONVND_COMPLETE = 1, 2, 3
 
 # every symbol the public headers declare (checked by the CPU tests)
@@ -72,7 +104,8 @@ EXPORTS = [
     "km_wavefront_plan_matches_dims", "km_wavefront_plan_level_size", "km_wavefront_plan_level_offsets",
     "km_wavefront_plan_iter_forward", "km_wavefront_plan_iter_reverse",
     "kmb_last_error", "kmb_last_forward_path", "kmb_set_force_generic",
-    "kmb_blockscan_forward", "kmb_blockscan_backward",
+    "kmb_blockscan_forward", "kmb_blockscan_backward", "kmb_block_activation_floats",
+    "kmb_block_forward", "kmb_block_backward",
 ]
 
 _lib = None
@@ -110,6 +143,13 @@ def lib():
         L.convnd_kernel_volume.argtypes = [C.c_long, C.c_long]
         L.convnd_kernel_volume.restype = C.c_long
         L.kmb_last_error.restype = C.c_char_p
+        L.kmb_block_activation_floats.argtypes = [C.POINTER(KMBlockConfig), C.c_long]
+        L.kmb_block_activation_floats.restype = C.c_size_t
+        L.kmb_block_forward.argtypes = [C.POINTER(KMBlockConfig), C.POINTER(KMBlockWeights), C.c_void_p,
+                                        C.c_void_p, C.c_long, C.c_void_p, C.c_void_p]
+        L.kmb_block_backward.argtypes = [C.POINTER(KMBlockConfig), C.POINTER(KMBlockWeights), C.c_void_p,
+                                         C.c_void_p, C.c_void_p, C.POINTER(KMBlockGrads), C.c_long, C.c_void_p,
+                                         C.c_void_p]
         L.kmb_blockscan_forward.argtypes = [C.POINTER(KMBlockScanParams), C.c_long, C.c_void_p]
         L.kmb_blockscan_backward.argtypes = [C.POINTER(KMBlockScanParams), C.c_long, C.c_void_p,
                                              C.POINTER(KMBlockScanGrads), C.c_void_p]

@@ -1,0 +1,292 @@
+// block.cu -- Mamba-3 block (projections + block scan + output projection).
+//
+// Reference semantics: src/mamba_block.c:106-125 (projections and
+// activations), :509-528 (forward), :746-773 (backward).  On the B200 the L
+// per-point GEMVs of the reference become one packed GEMM over all batch rows:
+// P[BL, Rt] = X[BL, dim] . Wcat^T with Wcat = [W_in; delta_proj; lambda_proj;
+// W_B; W_C] (Rt = R + 2 + 2 N R rows), in fp32 through cuBLAS (plain library
+// GEMM; no TF32, the parity target is the fp32 reference).  One elementwise
+// epilogue applies silu / softplus+clamp / sigmoid / biases and writes the
+// block-scan inputs; the backward mirrors it.  The backward is exact: it also
+// produces dW_in and the projection paths of dx, which the reference skips.
+#include <cublas_v2.h>
+#include <cstring>
+#include <map>
+#include "kmb_common.cuh"
+#include "../../include/kmamba_block.h"
+
+namespace kmb {
+void* workspace(int slot, size_t bytes);
+int set_error(const char* msg);
+int set_cuda_error(const char* where, cudaError_t e);
+enum { WS_BLK_W = 5, WS_BLK_SCRATCH = 6 };
+
+struct ActLayout {
+    long long BL, Rt, NR;
+    size_t proj, u, dt, lam, B, C, h, Bu, y, total;  // offsets in floats
+};
+
+static ActLayout act_layout(const KMBlockConfig* c, long batch) {
+    ActLayout a;
+    a.BL = (long long)batch * c->L;
+    a.NR = c->N * c->R;
+    a.Rt = c->R + 2 + 2 * a.NR;
+    size_t o = 0;
+    auto take = [&](size_t n) { size_t r = o; o += (n + 63) & ~(size_t)63; return r; };
+    a.proj = take(a.BL * a.Rt);
+    a.u = take(a.BL * c->R);
+    a.dt = take(a.BL);
+    a.lam = take(a.BL);
+    a.B = take(a.BL * a.NR);
+    a.C = take(a.BL * a.NR);
+    a.h = take(a.BL * c->N);
+    a.Bu = take(a.BL * c->N);
+    a.y = take(a.BL * c->R);
+    a.total = o;
+    return a;
+}
+
+__device__ __forceinline__ float sigm(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+// Forward epilogue over P[BL, Rt]
+__global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, int R, int NR, float dt_min,
+                                   float dt_max, const float* __restrict__ bB, const float* __restrict__ bC,
+                                   float* __restrict__ u, float* __restrict__ dt, float* __restrict__ lam,
+                                   float* __restrict__ B, float* __restrict__ C) {
+    const long long Rt = R + 2 + 2LL * NR;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= BL * Rt) return;
+    const long long row = i / Rt;
+    const int col = (int)(i - row * Rt);
+    const float v = P[i];
+    if (col < R) {
+        u[row * R + col] = v / (1.0f + expf(-v));                 // silu
+    } else if (col == R) {
+        float d = logf(1.0f + expf(v));                           // softplus
+        if (d < dt_min) d = dt_min;
+        if (d > dt_max) d = dt_max;
+        dt[row] = d;
+    } else if (col == R + 1) {
+        lam[row] = sigm(v);
+    } else if (col < R + 2 + NR) {
+        const int j = col - R - 2;
+        B[row * NR + j] = v + bB[j];
+    } else {
+        const int j = col - R - 2 - NR;
+        C[row * NR + j] = v + bC[j];
+    }
+}
+
+// Backward epilogue: dP[BL, Rt] from the scan gradients
+__global__ void block_bwd_epilogue(const float* __restrict__ P, const float* __restrict__ dtv,
+                                   const float* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
+                                   float dt_max, const float* __restrict__ du, const float* __restrict__ ddt,
+                                   const float* __restrict__ dlam, const float* __restrict__ dB,
+                                   const float* __restrict__ dC, float* __restrict__ dP) {
+    const long long Rt = R + 2 + 2LL * NR;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= BL * Rt) return;
+    const long long row = i / Rt;
+    const int col = (int)(i - row * Rt);
+    float g;
+    if (col < R) {
+        const float z = P[i], s = sigm(z);
+        g = du[row * R + col] * s * (1.0f + z * (1.0f - s));          // silu'
+    } else if (col == R) {
+        const float d = dtv[row];
+        g = (d > dt_min && d < dt_max) ? ddt[row] * sigm(P[i]) : 0.0f;  // softplus' inside the clamp
+    } else if (col == R + 1) {
+        const float l = lamv[row];
+        g = dlam[row] * l * (1.0f - l);
+    } else if (col < R + 2 + NR) {
+        g = dB[row * NR + (col - R - 2)];
+    } else {
+        g = dC[row * NR + (col - R - 2 - NR)];
+    }
+    dP[i] = g;
+}
+
+// grads += slices of G[Rt, dim]
+__global__ void block_scatter_grads(const float* __restrict__ G, int R, int NR, int dim, float* gWin,
+                                    float* gdelta, float* glam, float* gWB, float* gWC) {
+    const long long Rt = R + 2 + 2LL * NR;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= Rt * dim) return;
+    const int row = (int)(i / dim), col = (int)(i - (long long)row * dim);
+    const float v = G[i];
+    float* dst;
+    if (row < R) dst = gWin ? gWin + (long long)row * dim : nullptr;
+    else if (row == R) dst = gdelta;
+    else if (row == R + 1) dst = glam;
+    else if (row < R + 2 + NR) dst = gWB ? gWB + (long long)(row - R - 2) * dim : nullptr;
+    else dst = gWC ? gWC + (long long)(row - R - 2 - NR) * dim : nullptr;
+    if (dst) dst[col] += v;
+}
+
+__global__ void fill_value(float* p, long long n, float v) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+static thread_local std::map<int, cublasHandle_t> tl_cublas;
+static cublasHandle_t cublas_for(cudaStream_t st) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cublasHandle_t& h = tl_cublas[dev];
+    if (!h) {
+        if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return nullptr;
+        cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH);  // strict fp32: no TF32 or reduced-precision paths
+    }
+    cublasSetStream(h, st);
+    return h;
+}
+
+static inline unsigned nb(long long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+static int check_cfg(const KMBlockConfig* c, const KMBlockWeights* w, long batch) {
+    if (!c || !w || batch < 1 || c->dim < 1 || c->N < 1 || c->N > 64 || c->R < 1 || c->L < 1)
+        return set_error("invalid KMBlockConfig (N must be 1..64)");
+    if (!w->W_in || !w->W_out || !w->A_log || !w->W_B || !w->W_C || !w->delta_proj || !w->lambda_proj ||
+        !w->b_B || !w->b_C || !w->theta)
+        return set_error("KMBlockWeights: every parameter pointer is required");
+    return 0;
+}
+
+// Wcat = [W_in; delta_proj; lambda_proj; W_B; W_C]  [Rt, dim]
+static float* pack_wcat(const KMBlockConfig* c, const KMBlockWeights* w, cudaStream_t st) {
+    const long long NR = c->N * c->R, Rt = c->R + 2 + 2 * NR, dim = c->dim;
+    float* W = (float*)workspace(WS_BLK_W, (size_t)Rt * dim * sizeof(float));
+    if (!W) return nullptr;
+    const float* src[5] = {w->W_in, w->delta_proj, w->lambda_proj, w->W_B, w->W_C};
+    const long long rows[5] = {c->R, 1, 1, NR, NR};
+    long long r0 = 0;
+    for (int i = 0; i < 5; i++) {
+        if (cudaMemcpyAsync(W + r0 * dim, src[i], (size_t)rows[i] * dim * sizeof(float), cudaMemcpyDeviceToDevice,
+                            st) != cudaSuccess)
+            return nullptr;
+        r0 += rows[i];
+    }
+    return W;
+}
+
+}  // namespace kmb
+
+using namespace kmb;
+
+extern "C" size_t kmb_block_activation_floats(const KMBlockConfig* c, long batch) {
+    if (!c || batch < 1) return 0;
+    return act_layout(c, batch).total;
+}
+
+extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w, const float* x, float* out,
+                                 long batch, float* act, void* stream) {
+    if (check_cfg(c, w, batch)) return -1;
+    if (!x || !out || !act) return set_error("kmb_block_forward: x, out, act required");
+    cudaStream_t st = (cudaStream_t)stream;
+    cublasHandle_t hb = cublas_for(st);
+    if (!hb) return set_error("cuBLAS initialisation failed");
+    const ActLayout a = act_layout(c, batch);
+    float* W = pack_wcat(c, w, st);
+    if (!W) return set_error("kmb_block_forward: weight packing failed");
+    const float one = 1.0f, zero = 0.0f;
+    const int dim = (int)c->dim;
+    // P^T[Rt, BL] = Wcat[Rt, dim] . X^T
+    if (cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, (int)a.Rt, (int)a.BL, dim, &one, W, dim, x, dim, &zero,
+                    act + a.proj, (int)a.Rt) != CUBLAS_STATUS_SUCCESS)
+        return set_error("projection GEMM failed");
+    block_fwd_epilogue<<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min,
+                                                             c->dt_max, w->b_B, w->b_C, act + a.u, act + a.dt,
+                                                             act + a.lam, act + a.B, act + a.C);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("block epilogue", e);
+    KMBlockScanParams p;
+    memset(&p, 0, sizeof p);
+    p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;
+    p.u = act + a.u; p.dt = act + a.dt; p.lambda = act + a.lam; p.B = act + a.B; p.C = act + a.C;
+    p.A_log = w->A_log; p.theta = w->theta; p.default_lambda = c->default_lambda; p.use_fast_exp = c->use_fast_exp;
+    p.h = act + a.h; p.Bu = act + a.Bu; p.y = act + a.y;
+    if (kmb_blockscan_forward(&p, batch, stream)) return -1;
+    // out = x + y . W_out^T
+    if ((e = cudaMemcpyAsync(out, x, (size_t)a.BL * dim * sizeof(float), cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+        return set_cuda_error("residual copy", e);
+    if (cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, dim, (int)a.BL, (int)c->R, &one, w->W_out, (int)c->R,
+                    act + a.y, (int)c->R, &one, out, dim) != CUBLAS_STATUS_SUCCESS)
+        return set_error("output projection GEMM failed");
+    return 0;
+}
+
+extern "C" int kmb_block_backward(const KMBlockConfig* c, const KMBlockWeights* w, const float* x,
+                                  const float* dout, float* dx, const KMBlockGrads* g, long batch, const float* act,
+                                  void* stream) {
+    if (check_cfg(c, w, batch)) return -1;
+    if (!x || !dout || !act || !g) return set_error("kmb_block_backward: x, dout, act, g required");
+    cudaStream_t st = (cudaStream_t)stream;
+    cublasHandle_t hb = cublas_for(st);
+    if (!hb) return set_error("cuBLAS initialisation failed");
+    const ActLayout a = act_layout(c, batch);
+    const int dim = (int)c->dim, R = (int)c->R;
+    const long long BL = a.BL, NR = a.NR, Rt = a.Rt;
+    // scratch: dy[BL,R] | du[BL,R] | ddt[BL] | dlam[BL] | dB[BL,NR] | dC[BL,NR] | dP[BL,Rt] | G[Rt,dim] | ones[BL]
+    size_t o = 0;
+    auto take = [&](size_t n) { size_t r = o; o += (n + 63) & ~(size_t)63; return r; };
+    const size_t s_dy = take(BL * R), s_du = take(BL * R), s_ddt = take(BL), s_dlam = take(BL);
+    const size_t s_dB = take(BL * NR), s_dC = take(BL * NR), s_dP = take(BL * Rt), s_G = take(Rt * dim);
+    const size_t s_one = take(BL);
+    float* S = (float*)workspace(WS_BLK_SCRATCH, o * sizeof(float));
+    if (!S) return set_error("workspace allocation failed");
+    float* W = pack_wcat(c, w, st);
+    if (!W) return set_error("kmb_block_backward: weight packing failed");
+    const float one = 1.0f, zero = 0.0f;
+    cudaError_t e;
+    // d_y[BL,R] = dout . W_out ; gW_out += dout^T . y
+    if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_N, R, (int)BL, dim, &one, w->W_out, R, dout, dim, &zero, S + s_dy, R) !=
+        CUBLAS_STATUS_SUCCESS)
+        return set_error("dy GEMM failed");
+    if (g->W_out && cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_T, R, dim, (int)BL, &one, act + a.y, R, dout, dim, &one,
+                                g->W_out, R) != CUBLAS_STATUS_SUCCESS)
+        return set_error("dW_out GEMM failed");
+    // block-scan backward into zeroed scratch
+    if ((e = cudaMemsetAsync(S + s_du, 0, (s_dP - s_du) * sizeof(float), st)) != cudaSuccess)
+        return set_cuda_error("memset", e);
+    KMBlockScanParams p;
+    memset(&p, 0, sizeof p);
+    p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;
+    p.u = act + a.u; p.dt = act + a.dt; p.lambda = act + a.lam; p.B = act + a.B; p.C = act + a.C;
+    p.A_log = w->A_log; p.theta = w->theta; p.default_lambda = c->default_lambda; p.use_fast_exp = c->use_fast_exp;
+    p.h = (float*)(act + a.h); p.Bu = (float*)(act + a.Bu); p.y = (float*)(act + a.y);
+    KMBlockScanGrads sg;
+    sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
+    sg.dA_log = g->A_log; sg.dtheta = g->theta;
+    if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
+    block_bwd_epilogue<<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R, (int)NR,
+                                                         c->dt_min, c->dt_max, S + s_du, S + s_ddt, S + s_dlam,
+                                                         S + s_dB, S + s_dC, S + s_dP);
+    if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
+    // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
+    if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, &one, x, dim, S + s_dP, (int)Rt, &zero,
+                    S + s_G, dim) != CUBLAS_STATUS_SUCCESS)
+        return set_error("dWcat GEMM failed");
+    block_scatter_grads<<<nb(Rt * dim, 256), 256, 0, st>>>(S + s_G, R, (int)NR, dim, g->W_in, g->delta_proj,
+                                                           g->lambda_proj, g->W_B, g->W_C);
+    if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("grad scatter", e);
+    // bias gradients: column sums of dB, dC (GEMV with a ones vector, += into the gradients)
+    if (g->b_B || g->b_C) {
+        fill_value<<<nb(BL, 256), 256, 0, st>>>(S + s_one, BL, 1.0f);
+        if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("fill", e);
+        if (g->b_B && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dB, (int)NR, S + s_one, 1, &one,
+                                  g->b_B, 1) != CUBLAS_STATUS_SUCCESS)
+            return set_error("db_B GEMV failed");
+        if (g->b_C && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dC, (int)NR, S + s_one, 1, &one,
+                                  g->b_C, 1) != CUBLAS_STATUS_SUCCESS)
+            return set_error("db_C GEMV failed");
+    }
+    if (dx) {
+        if ((e = cudaMemcpyAsync(dx, dout, (size_t)BL * dim * sizeof(float), cudaMemcpyDeviceToDevice, st)) !=
+            cudaSuccess)
+            return set_cuda_error("dx copy", e);
+        if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, &one, W, dim, S + s_dP, (int)Rt, &one, dx,
+                        dim) != CUBLAS_STATUS_SUCCESS)
+            return set_error("dx GEMM failed");
+    }
+    return 0;
+}

@@ -46,6 +46,45 @@ int kmb_blockscan_forward(const KMBlockScanParams *p, long batch, void *stream);
 int kmb_blockscan_backward(const KMBlockScanParams *p, long batch, const float *dy,
                            const KMBlockScanGrads *g, void *stream);
 
+/* ---- Mamba-3 block (reference MambaBlock, src/mamba_block.c:106-125,509-528,746-773;
+ * GPU counterpart cuda/mamba_block.cu:223-415), batched, device pointers ---------- */
+typedef struct {
+    long dim, N, R;          /* model dim, state size, MIMO rank */
+    long ndims;              /* spatial grid rank (0/1 = 1D over L) */
+    const long *dims;        /* host memory */
+    long L;                  /* points per item */
+    float dt_min, dt_max, default_lambda;
+    int use_fast_exp;
+} KMBlockConfig;
+
+/* Parameters, reference layouts (include/kmamba.h:152-175): W_in[R,dim],
+ * W_out[dim,R], A_log[N], W_B/W_C[N*R,dim], delta_proj[dim], lambda_proj[dim],
+ * b_B/b_C[N*R], theta[N/2].  The gradient struct has the same fields (+=). */
+typedef struct {
+    const float *W_in, *W_out, *A_log, *W_B, *W_C, *delta_proj, *lambda_proj, *b_B, *b_C, *theta;
+} KMBlockWeights;
+typedef struct {
+    float *W_in, *W_out, *A_log, *W_B, *W_C, *delta_proj, *lambda_proj, *b_B, *b_C, *theta;
+} KMBlockGrads;
+
+/* Floats of the activation buffer the forward fills and the backward reads. */
+size_t kmb_block_activation_floats(const KMBlockConfig *c, long batch);
+
+/* Reference mamba_block_forward_ws (src/mamba_block.c:509-528) for `batch`
+ * items: x, out [batch, L, dim].  u = silu(W_in x), dt = clamp(softplus(
+ * delta_proj.x), dt_min, dt_max), lambda = sigmoid(lambda_proj.x), B = W_B x + b_B,
+ * C = W_C x + b_C, block scan, out = x + W_out y.  Projections are fp32 cuBLAS
+ * GEMMs (no TF32).  act: kmb_block_activation_floats() floats. */
+int kmb_block_forward(const KMBlockConfig *c, const KMBlockWeights *w, const float *x, float *out,
+                      long batch, float *act, void *stream);
+
+/* Exact gradient of kmb_block_forward: parameter gradients accumulate (+=)
+ * into g (any field may be NULL); dx (may be NULL) receives the full input
+ * gradient, including the W_in / W_B / W_C / delta / lambda paths that the
+ * reference omits (src/mamba_block.c:772, d_input = dY). */
+int kmb_block_backward(const KMBlockConfig *c, const KMBlockWeights *w, const float *x, const float *dout,
+                       float *dx, const KMBlockGrads *g, long batch, const float *act, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -508,3 +508,71 @@ def ref_block_run(dims, dim, N, R, params, x, dt_min=1e-3, dt_max=0.1, default_l
     if rc != 0:
         raise RuntimeError("reference block run failed")
     return out, ws, grads
+
+
+# ------------------------------------------------------------- Mamba-3 block
+BLOCK_KEYS = ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "lambda_proj", "b_B", "b_C", "theta")
+
+
+def gen_block_params(dim, N, R, seed=0):
+    """Random block parameters with the reference init scales (src/mamba_block.c:227-268):
+    Xavier-uniform matrices, A_log = -1, theta in [0, 2 pi / N), delta / lambda
+    projections small; biases small non-zero so their gradients are exercised."""
+    rng = np.random.default_rng(seed)
+    NR = N * R
+    xav = lambda r, c: rng.uniform(-1, 1, (r, c)) * np.sqrt(6.0 / (r + c))
+    p = dict(W_in=xav(R, dim), W_out=xav(dim, R), A_log=-np.ones(N) + 0.05 * rng.standard_normal(N),
+             W_B=xav(NR, dim), W_C=xav(NR, dim), delta_proj=rng.normal(0, 0.5, dim),
+             lambda_proj=rng.normal(0, 0.02, dim), b_B=rng.normal(0, 0.05, NR), b_C=rng.normal(0, 0.05, NR),
+             theta=rng.uniform(0, 2 * np.pi / N, max(N // 2, 1)))
+    return {k: v.astype(np.float32) for k, v in p.items()}
+
+
+def _block_proj64(params, x, dt_min, dt_max):
+    P = {k: np.asarray(v, np.float64) for k, v in params.items()}
+    x = np.asarray(x, np.float64)
+    zu = x @ P["W_in"].T
+    u = zu / (1 + np.exp(-zu))
+    zd = x @ P["delta_proj"]
+    dt = np.clip(np.log1p(np.exp(zd)), dt_min, dt_max)
+    zl = x @ P["lambda_proj"]
+    lam = 1 / (1 + np.exp(-zl))
+    B = x @ P["W_B"].T + P["b_B"]
+    Cm = x @ P["W_C"].T + P["b_C"]
+    return P, x, zu, u, zd, dt, zl, lam, B, Cm
+
+
+def block_fwd64(params, x, dims, N, R, dt_min=1e-3, dt_max=0.1, default_lambda=0.5):
+    """Double-precision block forward of one item x[L, dim] -> out[L, dim]."""
+    P, x, zu, u, zd, dt, zl, lam, B, Cm = _block_proj64(params, x, dt_min, dt_max)
+    inp = dict(dims=list(dims), N=N, R=R, default_lambda=default_lambda, fast_exp=0,
+               u=u[None], dt=dt[None], lam=lam[None], B=B[None], C=Cm[None], A=P["A_log"], theta=P["theta"])
+    h, y = blockscan_fwd64(inp)
+    return x + y @ P["W_out"].T
+
+
+def block_bwd_oracle(params, x, dout, dims, N, R, dt_min=1e-3, dt_max=0.1, default_lambda=0.5):
+    """Exact gradient of block_fwd64 (chain rule around the exact block-scan
+    adjoint): dict of parameter gradients and 'dx'.  One item."""
+    P, x64, zu, u, zd, dt, zl, lam, B, Cm = _block_proj64(params, x, dt_min, dt_max)
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    inp = dict(dims=list(dims), N=N, R=R, batch=1, default_lambda=default_lambda, fast_exp=0,
+               u=f(u[None]), dt=f(dt[None]), lam=f(lam[None]), B=f(B[None]), C=f(Cm[None]),
+               A=f(P["A_log"]), theta=f(P["theta"]))
+    h64, y64 = blockscan_fwd64(inp)
+    _, Bu, _ = oracle_blockscan(inp)
+    dout = np.asarray(dout, np.float64)
+    dy = dout @ P["W_out"]
+    g = oracle_blockscan_bwd(inp, f(h64[None]), Bu, f(dy[None]))
+    s = 1 / (1 + np.exp(-zu))
+    dzu = g["du"][0] * s * (1 + zu * (1 - s))
+    sp = np.log1p(np.exp(zd))
+    dzd = np.where((sp > dt_min) & (sp < dt_max), g["ddt"][0] / (1 + np.exp(-zd)), 0.0)
+    dzl = g["dlam"][0] * lam * (1 - lam)
+    dB, dC = g["dB"][0].astype(np.float64), g["dC"][0].astype(np.float64)
+    out = dict(W_out=dout.T @ y64, W_in=dzu.T @ x64, delta_proj=dzd @ x64, lambda_proj=dzl @ x64,
+               W_B=dB.T @ x64, W_C=dC.T @ x64, b_B=dB.sum(0), b_C=dC.sum(0),
+               A_log=g["dA"].astype(np.float64), theta=g["dtheta"].astype(np.float64))
+    out["dx"] = (dout + dzu @ P["W_in"] + np.outer(dzd, P["delta_proj"]) + np.outer(dzl, P["lambda_proj"])
+                 + dB @ P["W_B"] + dC @ P["W_C"])
+    return out

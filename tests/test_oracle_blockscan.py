@@ -65,3 +65,43 @@ def test_blockscan_adjoint_matches_finite_differences(dims, fast):
             mm[idx] -= eps
             fd = (loss({name: pp}) - loss({name: mm})) / (2 * eps)
             assert abs(fd - gg[idx]) <= 1e-4 * (abs(fd) + 1e-2), (name, idx, fd, gg[idx])
+
+
+@pytest.mark.skipif(not po.have_ref(), reason="reference build not available")
+@pytest.mark.parametrize("dims,N,R", [([6, 5], 8, 2), ([24], 8, 2), ([3, 4, 2], 6, 3)])
+def test_block_forward_oracle_matches_reference(dims, N, R):
+    dim = 16
+    params = po.gen_block_params(dim, N, R, seed=sum(dims))
+    x = np.random.default_rng(1).standard_normal((int(np.prod(dims)), dim)).astype(np.float32)
+    out_ref, _, _ = po.ref_block_run(dims, dim, N, R, params, x)
+    out64 = po.block_fwd64(params, x, dims, N, R)
+    np.testing.assert_allclose(out64, out_ref, rtol=2e-5, atol=2e-5 * np.abs(out_ref).max())
+
+
+@pytest.mark.parametrize("dims,N,R", [([3, 4], 4, 2), ([6], 4, 1)])
+def test_block_adjoint_matches_finite_differences(dims, N, R):
+    dim = 6
+    params = po.gen_block_params(dim, N, R, seed=3)
+    # keep the softplus away from the dt clamp so the gradient is smooth at the test point
+    params["delta_proj"] = (params["delta_proj"] * 0.1).astype(np.float32)
+    L = int(np.prod(dims))
+    x = np.random.default_rng(2).standard_normal((L, dim)).astype(np.float32) * 0.5
+    dout = np.random.default_rng(4).standard_normal((L, dim))
+    g = po.block_bwd_oracle(params, x, dout, dims, N, R, dt_min=1e-4, dt_max=10.0)
+
+    def loss(pp, xx):
+        return float((po.block_fwd64(pp, xx, dims, N, R, dt_min=1e-4, dt_max=10.0) * dout).sum())
+
+    eps = 1e-6
+    for k in po.BLOCK_KEYS + ("dx",):
+        base = (x if k == "dx" else params[k]).astype(np.float64)
+        for idx in list(np.ndindex(base.shape))[::max(1, base.size // 5)]:
+            pp, mm = base.copy(), base.copy()
+            pp[idx] += eps
+            mm[idx] -= eps
+            if k == "dx":
+                fd = (loss(params, pp) - loss(params, mm)) / (2 * eps)
+            else:
+                fd = (loss(dict(params, **{k: pp}), x) - loss(dict(params, **{k: mm}), x)) / (2 * eps)
+            gg = g[k][idx]
+            assert abs(fd - gg) <= 2e-4 * (abs(fd) + 1e-2), (k, idx, fd, gg)
