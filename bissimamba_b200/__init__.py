@@ -89,6 +89,27 @@ def block_config(dims, dim, N, R, dt_min=1e-3, dt_max=0.1, default_lambda=0.5, u
     return c
 
 
+MAX_NDIMS = 32
+
+
+class KMambaConfig(C.Structure):
+    """Same layout as the reference include/kmamba.h:238-278."""
+    _fields_ = [("max_ndims", C.c_long), ("max_state", C.c_long), ("use_fast_exp", C.c_int),
+                ("vocab_size", C.c_size_t), ("dim", C.c_size_t), ("state_size", C.c_size_t),
+                ("seq_len", C.c_size_t), ("n_layers", C.c_size_t), ("mimo_rank", C.c_size_t),
+                ("dt_scale", C.c_float), ("dt_min", C.c_float), ("dt_max", C.c_float),
+                ("default_lambda", C.c_float), ("use_a_log_clamp", C.c_int), ("a_log_min", C.c_float),
+                ("spatial_ndims", C.c_long), ("spatial_dims", C.c_long * MAX_NDIMS),
+                ("use_convnd", C.c_int), ("use_convnd_bias", C.c_int), ("convnd_K", C.c_long),
+                ("convnd_ndims", C.c_long), ("pad_left", C.c_long * MAX_NDIMS), ("pad_right", C.c_long * MAX_NDIMS),
+                ("d_conv", C.c_uint32), ("expand_factor", C.c_float), ("model_name", C.c_char * 64),
+                ("vocab_data", C.c_void_p), ("gpu_device", C.c_int), ("weight_tying", C.c_int)]
+
+
+class MBOptimConfig(C.Structure):
+    _fields_ = [(k, C.c_float) for k in ("lr", "mu", "beta2", "eps", "clip_norm", "weight_decay")]
+
+
 CONVND_FORWARD, CONVND_BACKWARD, CONVND_COMPLETE = 1, 2, 3
 
 # every symbol the public headers declare (checked by the CPU tests)
@@ -106,6 +127,10 @@ EXPORTS = [
     "kmb_last_error", "kmb_last_forward_path", "kmb_set_force_generic",
     "kmb_blockscan_forward", "kmb_blockscan_backward", "kmb_block_activation_floats",
     "kmb_block_forward", "kmb_block_backward",
+    "kmamba_config_set_defaults", "kmamba_optim_config_set_defaults", "kmamba_create", "kmamba_free",
+    "kmamba_init", "kmamba_enable_training", "kmamba_forward", "kmamba_train_batch", "kmamba_train_step",
+    "kmamba_get_config", "kmamba_step_count", "kmamba_update_lr", "kmamba_get_tensor", "kmamba_set_tensor",
+    "kmb_model_forward_backward", "kmb_model_optimizer_step", "kmb_model_grad_arena", "kmb_model_param_arena", "kmb_model_tensor_offset",
 ]
 
 _lib = None
@@ -143,6 +168,39 @@ def lib():
         L.convnd_kernel_volume.argtypes = [C.c_long, C.c_long]
         L.convnd_kernel_volume.restype = C.c_long
         L.kmb_last_error.restype = C.c_char_p
+        KC = C.POINTER(KMambaConfig)
+        L.kmamba_config_set_defaults.argtypes = [KC]
+        L.kmamba_config_set_defaults.restype = None
+        L.kmamba_optim_config_set_defaults.argtypes = [C.POINTER(MBOptimConfig)]
+        L.kmamba_optim_config_set_defaults.restype = None
+        L.kmamba_create.argtypes = [KC]
+        L.kmamba_create.restype = C.c_void_p
+        L.kmamba_free.argtypes = [C.c_void_p]
+        L.kmamba_free.restype = None
+        L.kmamba_init.argtypes = [C.c_void_p, C.c_uint32]
+        L.kmamba_enable_training.argtypes = [C.c_void_p, C.POINTER(MBOptimConfig), C.c_float, C.c_float]
+        L.kmamba_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
+        L.kmamba_train_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
+        L.kmamba_train_batch.restype = C.c_float
+        L.kmamba_train_step.argtypes = [C.c_void_p, C.c_void_p]
+        L.kmamba_train_step.restype = C.c_float
+        L.kmamba_get_tensor.argtypes = [C.c_void_p, C.c_char_p]
+        L.kmamba_get_tensor.restype = _f
+        L.kmamba_set_tensor.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p]
+        L.kmamba_step_count.argtypes = [C.c_void_p]
+        L.kmamba_step_count.restype = C.c_size_t
+        L.kmamba_update_lr.argtypes = [C.c_void_p, C.c_float, C.c_float]
+        L.kmamba_update_lr.restype = None
+        L.kmamba_get_config.argtypes = [C.c_void_p]
+        L.kmamba_get_config.restype = KC
+        L.kmb_model_forward_backward.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
+        L.kmb_model_forward_backward.restype = C.c_float
+        L.kmb_model_optimizer_step.argtypes = [C.c_void_p, C.c_void_p]
+        L.kmb_model_grad_arena.argtypes = [C.c_void_p, C.POINTER(C.c_size_t)]
+        L.kmb_model_grad_arena.restype = C.c_void_p
+        L.kmb_model_tensor_offset.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+        L.kmb_model_param_arena.argtypes = [C.c_void_p, C.POINTER(C.c_size_t)]
+        L.kmb_model_param_arena.restype = C.c_void_p
         L.kmb_block_activation_floats.argtypes = [C.POINTER(KMBlockConfig), C.c_long]
         L.kmb_block_activation_floats.restype = C.c_size_t
         L.kmb_block_forward.argtypes = [C.POINTER(KMBlockConfig), C.POINTER(KMBlockWeights), C.c_void_p,
@@ -250,3 +308,27 @@ def blockscan_params(dims, N, R, u, dt, lam, B, Cm, A_log, theta, h, Bu, y, defa
     p.use_fast_exp = int(use_fast_exp)
     p.h, p.Bu, p.y = _ptr(h), _ptr(Bu), _ptr(y)
     return p
+
+
+def model_config(dims, vocab, dim, N, R, n_layers):
+    """KMambaConfig with the reference defaults and the given shape."""
+    c = KMambaConfig()
+    lib().kmamba_config_set_defaults(C.byref(c))
+    L = 1
+    for d in dims:
+        L *= int(d)
+    c.vocab_size, c.dim, c.state_size, c.seq_len = vocab, dim, N, L
+    c.n_layers, c.mimo_rank = n_layers, R
+    c.spatial_ndims = len(dims)
+    for i, d in enumerate(dims):
+        c.spatial_dims[i] = int(d)
+    return c
+
+
+class DeviceArray:
+    """Minimal __cuda_array_interface__ view of a library-owned device buffer
+    (float32), so torch.as_tensor can read it without copying."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": "<f4", "data": (int(ptr), False),
+                                         "version": 3}

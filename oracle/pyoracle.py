@@ -576,3 +576,87 @@ def block_bwd_oracle(params, x, dout, dims, N, R, dt_min=1e-3, dt_max=0.1, defau
     out["dx"] = (dout + dzu @ P["W_in"] + np.outer(dzd, P["delta_proj"]) + np.outer(dzl, P["lambda_proj"])
                  + dB @ P["W_B"] + dC @ P["W_C"])
     return out
+
+
+# ------------------------------------------------------------- model (config 4)
+def model_tensor_names(nl):
+    names = ["embedding", "head"]
+    for i in range(nl):
+        names += [f"layers.{i}.{k}" for k in BLOCK_KEYS]
+    return names
+
+
+def gen_model_params(V, dim, N, R, nl, seed=0):
+    rng = np.random.default_rng(seed)
+    lim_e = np.sqrt(6.0 / (V + dim))
+    p = {"embedding": rng.uniform(-lim_e, lim_e, (V, dim)).astype(np.float32),
+         "head": rng.uniform(-lim_e, lim_e, (dim, V)).astype(np.float32)}
+    for i in range(nl):
+        for k, v in gen_block_params(dim, N, R, seed=seed + 1 + i).items():
+            p[f"layers.{i}.{k}"] = v
+    return p
+
+
+def ref_model_forward(dims, V, dim, N, R, nl, params, tokens):
+    """Reference kmamba_forward (CPU) logits[L, V] for one token sequence."""
+    lib = _lib("ref")
+    dims_a = np.ascontiguousarray(dims, np.int64)
+    names = model_tensor_names(nl)
+    arrs = [np.ascontiguousarray(params[n], np.float32) for n in names]
+    cn = (C.c_char_p * len(names))(*[n.encode() for n in names])
+    cd = (_f * len(names))(*[a.ctypes.data_as(_f) for a in arrs])
+    L = int(np.prod(dims))
+    tok = np.ascontiguousarray(tokens, np.uint32)
+    logits = np.zeros((L, V), np.float32)
+    lib.shim_model_forward.restype = C.c_int
+    rc = lib.shim_model_forward(dims_a.ctypes.data_as(_l), C.c_long(len(dims)), C.c_long(V), C.c_long(dim),
+                                C.c_long(N), C.c_long(R), C.c_long(nl), cn, cd, C.c_long(len(names)),
+                                tok.ctypes.data_as(C.POINTER(C.c_uint32)), logits.ctypes.data_as(_f))
+    if rc != 0:
+        raise RuntimeError(f"reference model forward failed ({rc})")
+    return logits
+
+
+def model_loss_and_grads(dims, V, dim, N, R, nl, params, batch_tokens, dt_min=1e-3, dt_max=0.1):
+    """Mean cross-entropy over batch and positions and its exact gradient
+    (double precision; embedding / blocks / head).  batch_tokens[B, L+1]."""
+    B = batch_tokens.shape[0]
+    L = int(np.prod(dims))
+    grads = {k: np.zeros(v.shape) for k, v in params.items()}
+    total = 0.0
+    emb = params["embedding"].astype(np.float64)
+    head = params["head"].astype(np.float64)
+    for b in range(B):
+        tin = batch_tokens[b, :L].astype(np.int64)
+        tin = np.where(tin >= V, 0, tin)
+        tgt = batch_tokens[b, 1:L + 1].astype(np.int64)
+        hs = [emb[tin]]
+        for i in range(nl):
+            lp = {k: params[f"layers.{i}.{k}"] for k in BLOCK_KEYS}
+            hs.append(block_fwd64(lp, hs[-1], dims, N, R, dt_min, dt_max))
+        logits = hs[-1] @ head
+        mx = logits.max(1, keepdims=True)
+        lse = mx[:, 0] + np.log(np.exp(logits - mx).sum(1))
+        total += float((lse - logits[np.arange(L), tgt]).sum())
+        p = np.exp(logits - lse[:, None])
+        p[np.arange(L), tgt] -= 1.0
+        dl = p / (B * L)
+        grads["head"] += hs[-1].T @ dl
+        dh = dl @ head.T
+        for i in reversed(range(nl)):
+            lp = {k: params[f"layers.{i}.{k}"] for k in BLOCK_KEYS}
+            g = block_bwd_oracle(lp, hs[i], dh, dims, N, R, dt_min, dt_max)
+            for k in BLOCK_KEYS:
+                grads[f"layers.{i}.{k}"] += g[k]
+            dh = g["dx"]
+        np.add.at(grads["embedding"], tin, dh)
+    return total / (B * L), grads
+
+
+def adamw_ref(p, g, m, v, lr, b1, b2, eps, wd, t):
+    """reference kernels/optimizer_f32.c:82-105 in double."""
+    m = b1 * m + (1 - b1) * g
+    v = b2 * v + (1 - b2) * g * g
+    mh = m / (1 - b1 ** t)
+    vh = v / (1 - b2 ** t)
+    return p * (1 - lr * wd) - lr * mh / (np.sqrt(vh) + eps), m, v

@@ -93,6 +93,7 @@ int shim_set_threads(int n) {
  * d_scan_C[L,NR], d_delta[L], d_lambda[L], g_W_out[dim,R], g_W_B, g_W_C,
  * g_b_B, g_b_C, g_delta_proj, g_lambda_proj; NULL entries are skipped).
  */
+#include <stdio.h>
 #include "kmamba.h"
 
 static MambaBlock *shim_block_make(const long *dims, long ndims, long dim, long N, long R,
@@ -164,4 +165,58 @@ int shim_block_run(const long *dims, long ndims, long dim, long N, long R, const
     mamba_block_workspace_free(ws);
     mamba_block_free(blk);
     return 0;
+}
+
+/* Reference KMamba (src/kmamba.c) forward through its public API: create,
+ * set every named tensor, kmamba_forward (CPU path, src/kmamba.c:626-660). */
+size_t shim_sizeof_kmamba_config(void) { return sizeof(KMambaConfig); }
+size_t shim_sizeof_mboptim_config(void) { return sizeof(MBOptimConfig); }
+
+int shim_model_forward(const long *dims, long ndims, long V, long dim, long N, long R, long nl,
+                       const char *const *names, const float *const *data, long ntensors,
+                       const uint32_t *tokens, float *logits) {
+    KMambaConfig cfg;
+    kmamba_config_set_defaults(&cfg);
+    long L = 1;
+    for (long i = 0; i < ndims; i++) L *= dims[i];
+    cfg.vocab_size = (size_t)V;
+    cfg.dim = (size_t)dim;
+    cfg.state_size = (size_t)N;
+    cfg.seq_len = (size_t)L;
+    cfg.n_layers = (size_t)nl;
+    cfg.mimo_rank = (size_t)R;
+    cfg.spatial_ndims = ndims;
+    for (long i = 0; i < ndims; i++) cfg.spatial_dims[i] = dims[i];
+    KMamba *m = kmamba_create(&cfg);
+    if (!m) return -1;
+    /* The reference kmamba_set_tensor cannot be used here: its name matching
+     * (src/kmamba.c:693-702) accepts any "layers.<i>.*" as W_in because
+     * sscanf returns 1 once the index is converted.  Write the tensors
+     * through the reference's structs instead, with strict names. */
+    const size_t D = (size_t)dim, NR = (size_t)N * R, TS = N / 2 > 0 ? N / 2 : 1;
+    for (long i = 0; i < ntensors; i++) {
+        float *dst = NULL;
+        size_t n = 0, li;
+        char field[32];
+        if (!strcmp(names[i], "embedding")) { dst = m->embedding; n = (size_t)V * D; }
+        else if (!strcmp(names[i], "head")) { dst = m->head; n = D * (size_t)V; }
+        else if (sscanf(names[i], "layers.%zu.%31s", &li, field) == 2 && li < (size_t)nl) {
+            MambaBlock *b = m->layers[li];
+            if (!strcmp(field, "W_in")) { dst = b->W_in.data; n = (size_t)R * D; }
+            else if (!strcmp(field, "W_out")) { dst = b->W_out.data; n = D * (size_t)R; }
+            else if (!strcmp(field, "A_log")) { dst = b->A_log.data; n = (size_t)N; }
+            else if (!strcmp(field, "W_B")) { dst = b->W_B.data; n = NR * D; }
+            else if (!strcmp(field, "W_C")) { dst = b->W_C.data; n = NR * D; }
+            else if (!strcmp(field, "delta_proj")) { dst = b->delta_proj.data; n = D; }
+            else if (!strcmp(field, "lambda_proj")) { dst = b->lambda_proj.data; n = D; }
+            else if (!strcmp(field, "b_B")) { dst = b->b_B; n = NR; }
+            else if (!strcmp(field, "b_C")) { dst = b->b_C; n = NR; }
+            else if (!strcmp(field, "theta")) { dst = b->theta; n = TS; }
+        }
+        if (!dst) { kmamba_free(m); return -2; }
+        memcpy(dst, data[i], n * sizeof(float));
+    }
+    int rc = kmamba_forward(m, tokens, logits);
+    kmamba_free(m);
+    return rc;
 }

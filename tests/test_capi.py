@@ -99,3 +99,16 @@ def test_plan_matches_reference_plan(kmb, dims):
 def test_kernel_volume(kmb):
     assert kmb.lib().convnd_kernel_volume(3, 3) == 27
     assert kmb.lib().convnd_kernel_volume(2, 2) == 4
+
+
+def test_model_config_layout_matches_reference(kmb):
+    if not po.have_ref():
+        pytest.skip("reference build not available")
+    ref = po._lib("ref")
+    ref.shim_sizeof_kmamba_config.restype = C.c_size_t
+    ref.shim_sizeof_mboptim_config.restype = C.c_size_t
+    assert C.sizeof(kmb.KMambaConfig) == ref.shim_sizeof_kmamba_config()
+    assert C.sizeof(kmb.MBOptimConfig) == ref.shim_sizeof_mboptim_config()
+    c = kmb.KMambaConfig()
+    kmb.lib().kmamba_config_set_defaults(C.byref(c))
+    assert (c.dim, c.state_size, c.seq_len, c.n_layers, c.vocab_size) == (512, 64, 1024, 12, 32768)

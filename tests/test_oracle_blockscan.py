@@ -105,3 +105,18 @@ def test_block_adjoint_matches_finite_differences(dims, N, R):
                 fd = (loss(dict(params, **{k: pp}), x) - loss(dict(params, **{k: mm}), x)) / (2 * eps)
             gg = g[k][idx]
             assert abs(fd - gg) <= 2e-4 * (abs(fd) + 1e-2), (k, idx, fd, gg)
+
+
+@pytest.mark.skipif(not po.have_ref(), reason="reference build not available")
+@pytest.mark.parametrize("dims,V,dim,N,R,nl", [([4, 8], 16, 16, 8, 2, 2), ([2, 3, 4], 24, 16, 6, 4, 2)])
+def test_model_forward_oracle_matches_reference(dims, V, dim, N, R, nl):
+    """The double composition (embedding -> blocks -> head) used as the model
+    oracle reproduces the reference kmamba_forward (src/kmamba.c:626-660)."""
+    params = po.gen_model_params(V, dim, N, R, nl, seed=3)
+    tok = np.random.default_rng(1).integers(0, V, int(np.prod(dims))).astype(np.uint32)
+    ref = po.ref_model_forward(dims, V, dim, N, R, nl, params, tok)
+    h = params["embedding"].astype(np.float64)[tok]
+    for i in range(nl):
+        h = po.block_fwd64({k: params[f"layers.{i}.{k}"] for k in po.BLOCK_KEYS}, h, dims, N, R)
+    logits = h @ params["head"].astype(np.float64)
+    np.testing.assert_allclose(logits, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
