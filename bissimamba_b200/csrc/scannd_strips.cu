@@ -170,19 +170,20 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     const int ncol = min(WC, Q - q0);
     unsigned char* my_stages = stages + (size_t)w * NSS * ST;
     const bool issuer = (hh == 0 && lane == 0);
-    const long long tiles_mine = (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x;
-    const long long total_rows = tiles_mine * O;
-    long long next_issue = 0;
+    const int tiles_mine = (int)((ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x);
+    const int total_rows = tiles_mine * O;
+    // issuer state: next row to issue, its (tile, o) and ring (slot, phase),
+    // all maintained incrementally (no runtime divisions per row)
+    int next_issue = 0, is_o = 0, is_slot = 0;
+    uint32_t is_phase = 0;
+    long long is_tile = blockIdx.x;
 
-    auto issue = [&](long long t) {
-        const long long ti = t / O;
-        const int o = (int)(t - ti * O);
-        const long long tile = blockIdx.x + ti * gridDim.x;
-        const int b = (int)(tile / ntd);
-        const int d0 = (int)(tile - (long long)b * ntd) * CH;
-        const int slot = (int)(t % NSS);
-        unsigned char* st = my_stages + (size_t)slot * ST;
-        const uint32_t full = smem_u32(&b_full[w * NSS + slot]);
+    auto issue = [&]() {
+        const int b = (int)(is_tile / ntd);
+        const int d0 = (int)(is_tile - (long long)b * ntd) * CH;
+        const int o = is_o;
+        unsigned char* st = my_stages + (size_t)is_slot * ST;
+        const uint32_t full = smem_u32(&b_full[w * NSS + is_slot]);
         mbar_expect_tx(full, f.tx_bytes);
         tma_load_5d(smem_u32(st), &mB, full, 0, d0, q0, o, b);
         tma_load_5d(smem_u32(st + Ly::offC), &mC, full, 0, d0, q0, o, b);
@@ -193,27 +194,33 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             else tma_load_3d(smem_u32(st + Ly::offL), &mL, full, o & ~3, q0, b);
         }
     };
-    auto top_up = [&](long long cur) -> bool {
+    auto advance_issue = [&]() {
+        next_issue++;
+        if (++is_o == O) { is_o = 0; is_tile += gridDim.x; }
+        if (++is_slot == NSS) { is_slot = 0; is_phase ^= 1u; }
+    };
+    // Keep up to NSS rows in flight; block only for the row about to be consumed.
+    auto top_up = [&](int cur) -> bool {
         while (next_issue < total_rows && next_issue < cur + NSS) {
-            const long long t = next_issue;
-            if (t >= NSS) {
-                const uint32_t eb = smem_u32(&b_empty[w * NSS + (int)(t % NSS)]);
-                const uint32_t ph = (uint32_t)(((t / NSS) - 1) & 1);
-                if (t <= cur) {
+            if (next_issue >= NSS) {
+                // the slot's previous use (row next_issue - NSS) must have been released
+                const uint32_t eb = smem_u32(&b_empty[w * NSS + is_slot]);
+                const uint32_t ph = is_phase ^ 1u;
+                if (next_issue <= cur) {
                     if (!mbar_wait(eb, ph)) return false;
                 } else if (!mbar_try(eb, ph)) {
                     break;
                 }
             }
-            issue(t);
-            next_issue++;
+            issue();
+            advance_issue();
         }
         return true;
     };
     auto drain = [&]() {
         if (!issuer) return;
-        for (long long j = (next_issue > NSS ? next_issue - NSS : 0); j < next_issue; j++)
-            mbar_wait(smem_u32(&b_full[w * NSS + (int)(j % NSS)]), (uint32_t)((j / NSS) & 1));
+        for (int j = (next_issue > NSS ? next_issue - NSS : 0); j < next_issue; j++)
+            mbar_wait(smem_u32(&b_full[w * NSS + j % NSS]), (uint32_t)((j / NSS) & 1));
     };
 
     float* my_hand_in = hand + ((size_t)(w * HW + hh) * SW_K) * 2 * hv;           // written by strip w-1
@@ -222,7 +229,8 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     // per-thread offsets inside a stage
     const int bofs = (cl0 * MT + m) * 4;                 // B / C box: [j][CH][MT]
     const int xofs = cl0;                                // x / delta box column (+ (d0 & 3))
-    long long row = 0;
+    int row = 0, slot = 0;  // consumer row counter and its stage slot / phase
+    uint32_t ph = 0;
 
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int b = (int)(tile / ntd);
@@ -247,8 +255,6 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
         // one row of this strip; HASO: the row above exists (o > 0)
         auto do_row = [&](auto hasO_c, int o) -> bool {
             constexpr bool HASO = decltype(hasO_c)::value;
-            const int slot = (int)(row % NSS);
-            const uint32_t ph = (uint32_t)((row / NSS) & 1);
             if (issuer && !top_up(row)) {
                 set_status(f.status, KMB_ERR_TIMEOUT_EMPTY);
                 drain();
@@ -267,7 +273,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             const float* DsI = (const float*)(st + Ly::offD) + (KIN0 ? 0 : WC * 4) + xo;
             const float* DsO = (const float*)(st + Ly::offD) + (KIN0 ? WC * 4 : 0) + xo;
             const float* Ls = (const float*)(st + Ly::offL) + (KIN0 ? (o & 3) : 0);
-            const int hs = (int)(row % SW_K);
+            const int hs = row & (SW_K - 1);
             const uint32_t hph = (uint32_t)((row / SW_K) & 1);
             float lh[CPT], lb[CPT];
             if (w > 0) {
@@ -300,13 +306,13 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     const float Bv = Bs[j * CH * MT + c * MT];
                     const float dt = __fadd_rn(dI, dO);
                     const float bu = __fmul_rn(Bv, x);
-                    const float aI = kmb_exp(__fmul_rn(dI, AI[c]), 0);
+                    const float aI = kmb_exp2c(__fmul_rn(dI, AI[c]));
                     float buacc, dacc, hacc, inv;
                     // inner predecessor: the previous column (strip w-1's last column when j == 0)
                     const float hatI = (j == 0) ? lh[c] : ring_h[j == 0 ? 0 : j - 1][c];
                     const float buI = (j == 0) ? lb[c] : ring_b[j == 0 ? 0 : j - 1][c];
                     if (HASO) {
-                        const float aO = kmb_exp(__fmul_rn(dO, AO[c]), 0);
+                        const float aO = kmb_exp2c(__fmul_rn(dO, AO[c]));
                         if (j > 0 || w > 0) {
                             buacc = __fadd_rn(buI, ring_b[j][c]);
                             dacc = __fadd_rn(aI, aO);
@@ -396,6 +402,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&b_empty[w * NSS + slot]));
             row++;
+            if (++slot == NSS) { slot = 0; ph ^= 1u; }
             return true;
         };
 
