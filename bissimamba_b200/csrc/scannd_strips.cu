@@ -119,7 +119,7 @@ struct StripLayout {
     static constexpr int bytes = offL + 128;
 };
 
-template <int MT, bool ROPE, bool LAMB, bool KIN0>
+template <int MT, bool ROPE, bool LAMB, bool KIN0, bool FULL>
 __global__ void __launch_bounds__(512, 1)
 scan_fwd_strips(const __grid_constant__ StripDesc f,
                 const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mC,
@@ -137,6 +137,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     const int S = f.S, NSS = f.nss, D = f.D, O = f.O, Q = f.Q, ntd = f.ntd;
     const long long ntiles = f.ntiles, P = f.P, qstride = f.qstride, ostride = f.ostride;
     const float deflam = f.deflam;
+    const float omlq = __fmul_rn(__fsub_rn(1.0f, deflam), 0.25f);  // (1 - lambda) / 4 when lambda is constant
     const int red_y = f.red_y;
     // smem map: stages [S][NSS] | handoff values [S][HW][K][2][32*CPT] | barriers
     unsigned char* stages = smem;
@@ -167,7 +168,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     const long long DM = (long long)D * MT;
     const long long hq = qstride * DM;
     const int q0 = w * WC;
-    const int ncol = min(WC, Q - q0);
+    const int ncol = FULL ? WC : min(WC, Q - q0);  // FULL: every strip has WC columns
     unsigned char* my_stages = stages + (size_t)w * NSS * ST;
     const bool issuer = (hh == 0 && lane == 0);
     const int tiles_mine = (int)((ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x);
@@ -314,11 +315,17 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     if (HASO) {
                         const float aO = kmb_exp2c(__fmul_rn(dO, AO[c]));
                         if (j > 0 || w > 0) {
+                            // two predecessors: mean of two = sum * 0.5 (exact), so
+                            // ((1-lam) dt (dacc/2)) (buacc/2) == (((1-lam) dt / 4) dacc) buacc bit for bit
                             buacc = __fadd_rn(buI, ring_b[j][c]);
                             dacc = __fadd_rn(aI, aO);
                             hacc = KIN0 ? __fmaf_rn(aO, ring_h[j][c], __fmul_rn(aI, hatI))
                                         : __fmaf_rn(aI, hatI, __fmul_rn(aO, ring_h[j][c]));
-                            inv = 0.5f;
+                            const float omdtq = LAMB ? __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), 0.25f)
+                                                     : __fmul_rn(omlq, dt);
+                            const float gamma2 = __fmul_rn(lam, dt);
+                            hn[c] = __fadd_rn(__fmaf_rn(bu, gamma2, __fmul_rn(__fmul_rn(omdtq, dacc), buacc)), hacc);
+                            goto have_h;
                         } else {
                             buacc = ring_b[j][c];
                             dacc = aO;
@@ -338,9 +345,12 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                             inv = 0.0f;
                         }
                     }
-                    const float beta = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), __fmul_rn(dacc, inv));
-                    const float gamma = __fmul_rn(lam, dt);
-                    hn[c] = __fadd_rn(__fmaf_rn(bu, gamma, __fmul_rn(__fmul_rn(buacc, inv), beta)), hacc);
+                    {
+                        const float beta = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), __fmul_rn(dacc, inv));
+                        const float gamma = __fmul_rn(lam, dt);
+                        hn[c] = __fadd_rn(__fmaf_rn(bu, gamma, __fmul_rn(__fmul_rn(buacc, inv), beta)), hacc);
+                    }
+                have_h:
                     ring_b[j][c] = bu;
                     if (j < ncol) __stcs(hp + (long long)c * MT, hn[c]);
                     prod[j][c] = __fmul_rn(Cs[j * CH * MT + c * MT], hn[c]);
@@ -420,7 +430,7 @@ bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long
 
 template <int MT, bool ROPE, bool LAMB, bool KIN0>
 static cudaError_t strips_inst(const StripDesc& f, const CUtensorMap* maps, int smem, int threads, cudaStream_t st) {
-    auto k = scan_fwd_strips<MT, ROPE, LAMB, KIN0>;
+    auto k = (f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true> : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int dev, sms, per = 0;
