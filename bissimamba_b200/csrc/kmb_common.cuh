@@ -64,6 +64,15 @@ __device__ __forceinline__ float kmb_exp2c(float z) {
     return __fmaf_rn(e, __fmul_rn(tl, 0.693147180559945309f), e);
 }
 
+// exp(z) as one hardware base-2 exponential of the rounded product
+// z * log2(e): 2 instructions; adds up to ~|z log2 e| * 2^-24 relative error
+// from the rounded product on top of ex2.approx's own (a few ulp for |z| < 4).
+__device__ __forceinline__ float kmb_exp2r(float z) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(z, 1.44269502162933349609375f)));
+    return e;
+}
+
 // d/dz of kmb_exp given e = kmb_exp(z)
 __device__ __forceinline__ float kmb_dexp(float z, float e, int fast) {
     if (fast) {

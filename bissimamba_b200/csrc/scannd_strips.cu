@@ -307,13 +307,13 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     const float Bv = Bs[j * CH * MT + c * MT];
                     const float dt = __fadd_rn(dI, dO);
                     const float bu = __fmul_rn(Bv, x);
-                    const float aI = kmb_exp2c(__fmul_rn(dI, AI[c]));
+                    const float aI = kmb_exp2r(__fmul_rn(dI, AI[c]));
                     float buacc, dacc, hacc, inv;
                     // inner predecessor: the previous column (strip w-1's last column when j == 0)
                     const float hatI = (j == 0) ? lh[c] : ring_h[j == 0 ? 0 : j - 1][c];
                     const float buI = (j == 0) ? lb[c] : ring_b[j == 0 ? 0 : j - 1][c];
                     if (HASO) {
-                        const float aO = kmb_exp2c(__fmul_rn(dO, AO[c]));
+                        const float aO = kmb_exp2r(__fmul_rn(dO, AO[c]));
                         if (j > 0 || w > 0) {
                             // two predecessors: mean of two = sum * 0.5 (exact), so
                             // ((1-lam) dt (dacc/2)) (buacc/2) == (((1-lam) dt / 4) dacc) buacc bit for bit
