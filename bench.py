@@ -52,13 +52,13 @@ def set_workload(dims, d, m, batch):
 
 
 set_workload(DIMS, D, M, BATCH)
-PROFILE_MD = os.path.join(ROOT, "profiles", "scan_fwd_tma_headline.md")
+PROFILE_MD = os.path.join(ROOT, "profiles", "scan_fwd_strips_headline.md")
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2)
@@ -103,7 +103,7 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", dev_uuid, f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
