@@ -29,6 +29,8 @@ import sys
 import tempfile
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -68,6 +70,9 @@ def parse():
     ap.add_argument("--dims", type=int, nargs="+", default=list(DIMS))
     ap.add_argument("--D", type=int, default=D)
     ap.add_argument("--M", type=int, default=M)
+    ap.add_argument("--workload", default="scan_fwd",
+                    choices=["scan_fwd", "scan_bwd", "convnd", "block", "model"],
+                    help="scan_fwd = the headline line; the others measure the other BASELINE configs")
     a = ap.parse_args()
     set_workload(a.dims, a.D, a.M, a.batch)
     return a
@@ -225,6 +230,9 @@ def main():
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return
+    if args.workload != "scan_fwd":
+        run_other_workload(args, rank, world)
+        return
 
     import torch
     import torch.distributed as dist
@@ -354,6 +362,160 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- other configs
+def _timed(step, steps, warmup, stream):
+    """CUDA-event time (ms) of `steps` calls after `warmup` calls."""
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+def run_other_workload(args, rank, world):
+    """BASELINE configs 1-4 on one GPU (per rank; weak scaling like the headline)."""
+    import torch
+    import torch.distributed as dist
+    import bissimamba_b200 as kmb
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    lib = kmb.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    rn = lambda *s: torch.randn(s, generator=g, device=dev)
+    steps, warm = max(args.steps // 6, 5), max(args.warmup, 3)
+    peak, peak_src = peaks()
+    line = {"n_gpus": world, "steps": steps, "warmup": warm, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions), on device"}
+
+    if args.workload == "scan_bwd":
+        # BASELINE config 1 backward: 2D 32x32, D 64, M 16, batch 8, RoPE, dy ~ N(0,1)
+        dims, D_, M_, B_ = (32, 32), 64, 16, 8
+        P_ = 1024
+        x, dl = rn(B_, P_, D_), torch.nn.functional.softplus(rn(B_, 2, P_, D_) * 0.5 - 4.0)
+        A = -torch.exp(torch.rand((2, D_, M_), generator=g, device=dev) * torch.log(torch.tensor(16.0)))
+        Bm = (rn(B_, P_, 1, M_) * 0.25).expand(B_, P_, D_, M_).contiguous()
+        Cm = (rn(B_, P_, 1, M_) * 0.25).expand(B_, P_, D_, M_).contiguous()
+        th = torch.rand(D_ // 2, generator=g, device=dev) * 6.283 - 3.1416
+        h, y = torch.empty(B_, P_, D_, M_, device=dev), torch.empty(B_, P_, D_, device=dev)
+        p = kmb.scan_params(list(dims), D_, M_, x, A, Bm, Cm, dl, h, y, theta=th)
+        kmb.check(lib.scannd_forward_async(C.byref(p), B_, sp))
+        dy = rn(B_, P_, D_)
+        gr = {k: torch.zeros(s, device=dev) for k, s in (("dA", (2, D_, M_)), ("dB", (B_, P_, D_, M_)),
+                                                           ("dC", (B_, P_, D_, M_)), ("ddelta", (B_, 2, P_, D_)),
+                                                           ("dlambda", (B_, P_)), ("dtheta", (D_ // 2,)))}
+        dx = torch.zeros(B_, P_, D_, device=dev)
+        pb = kmb.scan_params(list(dims), D_, M_, x, A, Bm, Cm, dl, h, dy, theta=th, grads=gr)
+        ms = _timed(lambda: kmb.check(lib.scannd_backward_async(C.byref(pb), B_, dx.data_ptr(), sp)), steps, warm,
+                    stream)
+        upd = B_ * P_ * D_ * M_
+        alg = upd * 20 + B_ * P_ * D_ * 4 * 7
+        t = ms / steps / 1e3
+        line.update(metric="scanND backward state-updates/sec", value=upd * world / t, unit="state-updates/s",
+                    ms_per_step=ms / steps, config={"workload": "scannd_bwd_2d32x32_D64_M16_b8_rope (config 1)"},
+                    roofline={"bound": "hbm", "achieved": round(alg / t / 1e9, 1), "peak": peak, "unit": "GB/s",
+                              "frac": round(alg / t / 1e9 / peak, 4), "peak_source": peak_src},
+                    gpu_launches=steps * 4)
+    elif args.workload == "convnd":
+        # BASELINE config 2: dims {32,32} and {16,16,16}, D 256, K 3, batch 16, forward + backward
+        res = {}
+        for dims in ((32, 32), (16, 16, 16)):
+            D_, K_, B_ = 256, 3, 16
+            P_ = int(np.prod(dims)) if False else (dims[0] * dims[1] * (dims[2] if len(dims) > 2 else 1))
+            V_ = K_ ** len(dims)
+            xi, dy = rn(B_, P_, D_), rn(B_, P_, D_)
+            ker, bias = rn(V_, D_) / V_ ** 0.5, rn(D_) * 0.14
+            out, din = torch.empty(B_, P_, D_, device=dev), torch.empty(B_, P_, D_, device=dev)
+            dk, db = torch.empty(V_, D_, device=dev), torch.empty(D_, device=dev)
+            p = kmb.conv_params(list(dims), D_, K_, xi, ker, bias, out, dy, din, dk, db)
+            ms = _timed(lambda: kmb.check(lib.convnd_batched_async(C.byref(p), B_, 3, sp)), steps, warm, stream)
+            t = ms / steps / 1e3
+            alg = B_ * P_ * D_ * 20
+            res["x".join(map(str, dims))] = {"outputs_per_s": B_ * P_ * D_ * world / t, "ms_per_step": ms / steps,
+                                             "hbm_gbs": round(alg / t / 1e9, 1),
+                                             "frac": round(alg / t / 1e9 / peak, 4)}
+        line.update(metric="convND fwd+bwd outputs/sec (config 2, 2D and 3D)",
+                    value=res["32x32"]["outputs_per_s"], unit="outputs/s", ms_per_step=res["32x32"]["ms_per_step"],
+                    config={"workload": "convnd_D256_K3_b16 (config 2)", "per_shape": res}, gpu_launches=None)
+    elif args.workload == "block":
+        # BASELINE config 3: Mamba-3 block, dim 512, N 64, R 2, 2D 64x64, batch 32, forward + backward (fp32)
+        dims, dim, N_, R_, B_ = (64, 64), 512, 64, 2, 32
+        L_ = 4096
+        from oracle import pyoracle as po  # parameter init only (seeded numpy), not a compute path
+        params = po.gen_block_params(dim, N_, R_, seed=42)
+        W = {k: torch.from_numpy(v).to(dev) for k, v in params.items()}
+        cfg = kmb.block_config(list(dims), dim, N_, R_)
+        w = kmb.KMBlockWeights(**{k: W[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+        G = {k: torch.zeros_like(v) for k, v in W.items()}
+        gw = kmb.KMBlockGrads(**{k: G[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+        act = torch.empty(lib.kmb_block_activation_floats(C.byref(cfg), B_), device=dev)
+        x, dout = rn(B_, L_, dim), rn(B_, L_, dim)
+        out, dx = torch.empty_like(x), torch.empty_like(x)
+
+        def step():
+            kmb.check(lib.kmb_block_forward(C.byref(cfg), C.byref(w), x.data_ptr(), out.data_ptr(), B_,
+                                            act.data_ptr(), sp))
+            kmb.check(lib.kmb_block_backward(C.byref(cfg), C.byref(w), x.data_ptr(), dout.data_ptr(), dx.data_ptr(),
+                                             C.byref(gw), B_, act.data_ptr(), sp))
+        ms = _timed(step, steps, warm, stream)
+        t = ms / steps / 1e3
+        line.update(metric="Mamba-3 block fwd+bwd tokens/sec (config 3)", value=B_ * L_ * world / t,
+                    unit="tokens/s", ms_per_step=ms / steps,
+                    config={"workload": "block_dim512_N64_R2_2d64x64_b32 (config 3, fp32 storage)"},
+                    scan_updates_per_s=B_ * L_ * N_ * R_ * world / t)
+    else:
+        # BASELINE config 4: 12-layer model, dim 512, N 64, R 4, 3D {16,32,32}, batch 64, vocab 256, AdamW
+        dims, V_, dim, N_, R_, nl, B_ = (16, 32, 32), 256, 512, 64, 4, 12, 64
+        B_ = int(os.environ.get("KMB_BENCH_MODEL_BATCH", B_))
+        cfgm = kmb.model_config(list(dims), V_, dim, N_, R_, nl)
+        m = lib.kmamba_create(C.byref(cfgm))
+        if not m:
+            raise RuntimeError(kmb.last_error())
+        lib.kmamba_init(m, 42)
+        opt = kmb.MBOptimConfig()
+        lib.kmamba_optim_config_set_defaults(C.byref(opt))
+        lib.kmamba_enable_training(m, C.byref(opt), 1e-3, 0.01)
+        L_ = 16384
+        tok = torch.randint(0, V_, (B_, L_ + 1), generator=g, device=dev, dtype=torch.int32)
+        losses = []
+
+        def step():
+            # NaN is a legitimate value here (the recurrence overflows fp32 at this scale, as the
+            # reference's does); an error leaves a message in kmb_last_error()
+            loss = lib.kmb_model_forward_backward(m, tok.data_ptr(), B_, sp)
+            if loss != loss and kmb.last_error():
+                raise RuntimeError(kmb.last_error())
+            kmb.check(lib.kmb_model_optimizer_step(m, sp))
+            losses.append(loss if loss == loss else None)
+        steps = max(2, min(steps, 3))
+        ms = _timed(step, steps, 2, stream)
+        t = ms / steps / 1e3
+        line.update(metric="k-mamba train step tokens/sec (config 4)", value=B_ * L_ * world / t, unit="tokens/s",
+                    ms_per_step=ms / steps, steps=steps, warmup=2,
+                    config={"workload": f"model_12x512_N64_R4_3d16x32x32_b{B_}_vocab256 (config 4)"},
+                    loss_first_last=[losses[0], losses[-1]])
+        lib.kmamba_free(m)
+    if world > 1:
+        t = torch.tensor([line["ms_per_step"]], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        line["ms_per_step"] = float(t.item())
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

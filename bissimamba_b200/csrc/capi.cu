@@ -106,6 +106,7 @@ int* status_word() { return (int*)ws_get(WS_STATUS, 256); }
 namespace kmb {
 void* workspace(int slot, size_t bytes) { return ws_get(slot, bytes); }
 int set_error(const char* msg) { return fail(msg); }
+void clear_error() { tl_err.clear(); }
 int set_cuda_error(const char* where, cudaError_t e) { return fail_cuda(where, e); }
 }  // namespace kmb
 

@@ -175,9 +175,200 @@ __global__ void reduce_rows_set(const float* __restrict__ part, float* __restric
 }
 
 static inline unsigned cblk(long long n, int t) { return (unsigned)((n + t - 1) / t); }
+// ---------------------------------------------------------------------------
+// Specialised kernels for ndims in {1,2,3}, K in {2,3,4}, D % 4 == 0: taps
+// unrolled at compile time, four channels per thread (float4), tap validity
+// from per-axis shift tests.  Same tap order as above (ascending kernel-linear
+// index), so the forward stays bit-identical to the reference.
+template <int ND, int K>
+struct Taps {
+    static constexpr int V = ND == 1 ? K : (ND == 2 ? K * K : K * K * K);
+    // digit of axis a (0 = outermost) of kernel-linear index kl, last axis fastest
+    __host__ __device__ static constexpr int digit(int kl, int a) {
+        return ND == 1 ? kl : (ND == 2 ? (a == 0 ? kl / K : kl % K)
+                                       : (a == 0 ? kl / (K * K) : (a == 1 ? (kl / K) % K : kl % K)));
+    }
+};
+
+__device__ __forceinline__ void fma4(float4& acc, const float4 a, const float4 b) {
+    acc.x = __fmaf_rn(a.x, b.x, acc.x);
+    acc.y = __fmaf_rn(a.y, b.y, acc.y);
+    acc.z = __fmaf_rn(a.z, b.z, acc.z);
+    acc.w = __fmaf_rn(a.w, b.w, acc.w);
+}
+
+template <int ND, int K, bool BWD>
+__global__ void __launch_bounds__(256) conv_tap_kernel(ConvDesc c, const float4* __restrict__ src,
+                                                       const float4* __restrict__ ker,
+                                                       const float4* __restrict__ bias, float4* __restrict__ dst) {
+    // forward: dst[o] = bias + sum_k src[o - shift_k] * ker[k]
+    // backward (dinput): dst[s] = sum_k src[s + shift_k] * ker[k]  (src = dy)
+    using T = Taps<ND, K>;
+    const int D4 = c.D >> 2;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= c.batch * c.P * D4) return;
+    const int d4 = (int)(i % D4);
+    const long long bp = i / D4;
+    const long long p = bp % c.P;
+    int oc[3];
+    long long st[3];
+#pragma unroll
+    for (int a = 0; a < ND; a++) {
+        st[a] = c.strides[a];
+        oc[a] = (int)((p / st[a]) % c.dims[a]);
+    }
+    float4 acc = BWD ? make_float4(0.f, 0.f, 0.f, 0.f) : (bias ? bias[d4] : make_float4(0.f, 0.f, 0.f, 0.f));
+    const float4* s = src + (bp - p) * D4;  // item base
+#pragma unroll
+    for (int kl = 0; kl < T::V; kl++) {
+        bool ok = true;
+        long long off = p;
+#pragma unroll
+        for (int a = 0; a < ND; a++) {
+            const int sh = K - 1 - T::digit(kl, a);
+            if (BWD) {
+                ok = ok && (oc[a] + sh < c.dims[a]);
+                off += sh * st[a];
+            } else {
+                ok = ok && (oc[a] >= sh);
+                off -= sh * st[a];
+            }
+        }
+        if (ok) fma4(acc, s[off * D4 + d4], ker[(long long)kl * D4 + d4]);
+    }
+    dst[i] = acc;
+}
+
+// dkernel / dbias partial sums: block = 32 float4 channel lanes x 8 row groups,
+// grid = (ceil(D4 / 32), nchunks); part[chunk][V + 1][D].
+template <int ND, int K>
+__global__ void __launch_bounds__(256) conv_dk_tap_kernel(ConvDesc c, const float4* __restrict__ in,
+                                                          const float4* __restrict__ dy, float4* __restrict__ part,
+                                                          long long rows_per_chunk) {
+    // taps are processed in passes of TP = K^(ND-1) (one value of the outermost
+    // kernel digit per pass) to bound the register accumulators; pass 0 also
+    // accumulates dbias
+    using T = Taps<ND, K>;
+    constexpr int NPASS = T::V > 16 ? K : 1;   // split only when the accumulators would not fit
+    constexpr int TP = T::V / NPASS;
+    __shared__ float4 red[8][32];
+    const int D4 = c.D >> 2;
+    const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+    const int d4 = blockIdx.x * 32 + lane;
+    const long long r0 = (long long)blockIdx.y * rows_per_chunk;
+    const long long rows = c.batch * c.P;
+    const long long r1 = min(r0 + rows_per_chunk, rows);
+    long long st[3];
+#pragma unroll
+    for (int a = 0; a < ND; a++) st[a] = c.strides[a];
+#pragma unroll 1
+    for (int pass = 0; pass < NPASS; pass++) {
+        float4 acc[TP + 1];
+#pragma unroll
+        for (int t = 0; t <= TP; t++) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (d4 < D4) {
+            for (long long r = r0 + grp; r < r1; r += 8) {
+                const long long p = r % c.P;
+                int oc[3];
+#pragma unroll
+                for (int a = 0; a < ND; a++) oc[a] = (int)((p / st[a]) % c.dims[a]);
+                const float4 g = dy[r * D4 + d4];
+                if (pass == 0) {
+                    acc[TP].x += g.x; acc[TP].y += g.y; acc[TP].z += g.z; acc[TP].w += g.w;
+                }
+                const float4* s = in + (r - p) * D4;
+                const int sh0 = K - 1 - pass;  // shift of the outermost axis (NPASS == K)
+                if (NPASS > 1 && oc[0] < sh0) continue;
+#pragma unroll
+                for (int t = 0; t < TP; t++) {
+                    const int kl = pass * TP + t;
+                    bool ok = true;
+                    long long off = NPASS > 1 ? p - (long long)sh0 * st[0] : p;
+#pragma unroll
+                    for (int a = (NPASS > 1 ? 1 : 0); a < ND; a++) {
+                        const int sh = K - 1 - T::digit(kl, a);
+                        ok = ok && (oc[a] >= sh);
+                        off -= sh * st[a];
+                    }
+                    if (ok) fma4(acc[t], g, s[off * D4 + d4]);
+                }
+            }
+        }
+        for (int t = 0; t <= TP; t++) {
+            if (t == TP && pass != 0) break;
+            red[grp][lane] = acc[t];
+            __syncthreads();
+            if (grp == 0 && d4 < D4) {
+                float4 v = red[0][lane];
+                for (int j = 1; j < 8; j++) {
+                    const float4 u = red[j][lane];
+                    v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+                }
+                const int slot = (t == TP) ? T::V : pass * TP + t;
+                part[((long long)blockIdx.y * (T::V + 1) + slot) * D4 + d4] = v;
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <int ND, int K>
+static cudaError_t conv_fast_impl(const ConvDesc& c, bool fwd, const float* in, const float* ker, const float* bias,
+                                  float* out, const float* dy, float* din, float* dker, float* dbias, float* scratch,
+                                  long long nch_max, cudaStream_t st) {
+    const long long n4 = c.batch * c.P * (c.D / 4);
+    const unsigned g4 = (unsigned)((n4 + 255) / 256);
+    if (fwd) {
+        conv_tap_kernel<ND, K, false><<<g4, 256, 0, st>>>(c, (const float4*)in, (const float4*)ker,
+                                                          (const float4*)bias, (float4*)out);
+        return cudaGetLastError();
+    }
+    conv_tap_kernel<ND, K, true><<<g4, 256, 0, st>>>(c, (const float4*)dy, (const float4*)ker, nullptr,
+                                                     (float4*)din);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const long long rows = c.batch * c.P;
+    const int D4 = c.D / 4;
+    const int dtiles = (D4 + 31) / 32;
+    long long nch = (2LL * 148 * 4 + dtiles - 1) / dtiles;  // ~4 blocks per SM pair
+    if (nch > rows) nch = rows;
+    if (nch > nch_max) nch = nch_max;
+    if (nch < 1) nch = 1;
+    const long long rpc = (rows + nch - 1) / nch;
+    dim3 grid(dtiles, (unsigned)nch);
+    conv_dk_tap_kernel<ND, K><<<grid, 256, 0, st>>>(c, (const float4*)in, (const float4*)dy, (float4*)scratch, rpc);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const long long V = Taps<ND, K>::V, cnt = V * c.D;
+    reduce_rows_set<<<(unsigned)((cnt + 255) / 256), 256, 0, st>>>(scratch, dker, cnt, nch, (V + 1) * c.D);
+    if (dbias)
+        reduce_rows_set<<<(unsigned)((c.D + 255) / 256), 256, 0, st>>>(scratch + V * c.D, dbias, c.D, nch,
+                                                                      (V + 1) * c.D);
+    return cudaGetLastError();
+}
+
+// cudaErrorNotSupported when (ndims, K, D) is outside the specialised set.
+static cudaError_t conv_fast(const ConvDesc& c, bool fwd, const float* in, const float* ker, const float* bias,
+                             float* out, const float* dy, float* din, float* dker, float* dbias, float* scratch,
+                             long long nch_max, cudaStream_t st) {
+    if (c.D % 4 != 0) return cudaErrorNotSupported;
+    const uintptr_t al = (uintptr_t)in | (uintptr_t)ker | (uintptr_t)(fwd ? out : din) | (uintptr_t)(fwd ? in : dy) |
+                         (uintptr_t)(bias ? bias : ker);
+    if (al & 15) return cudaErrorNotSupported;
+#define KMB_CONV_CASE(ND_, K_) \
+    if (c.nd == ND_ && c.K == K_) \
+        return conv_fast_impl<ND_, K_>(c, fwd, in, ker, bias, out, dy, din, dker, dbias, scratch, nch_max, st);
+    KMB_CONV_CASE(1, 2) KMB_CONV_CASE(1, 3) KMB_CONV_CASE(1, 4)
+    KMB_CONV_CASE(2, 2) KMB_CONV_CASE(2, 3) KMB_CONV_CASE(2, 4)
+    KMB_CONV_CASE(3, 2) KMB_CONV_CASE(3, 3) KMB_CONV_CASE(3, 4)
+#undef KMB_CONV_CASE
+    return cudaErrorNotSupported;
+}
+
 
 cudaError_t launch_conv_fwd(const ConvDesc& c, const float* in, const float* ker, const float* bias,
                             float* out, cudaStream_t st) {
+    cudaError_t ef = conv_fast(c, true, in, ker, bias, out, nullptr, nullptr, nullptr, nullptr, nullptr, 0, st);
+    if (ef != cudaErrorNotSupported) return ef;
     conv_fwd_kernel<<<cblk(c.batch * c.P * c.D, 256), 256, 0, st>>>(c, in, ker, bias, out);
     return cudaGetLastError();
 }
@@ -194,6 +385,9 @@ size_t conv_bwd_scratch_bytes(const ConvDesc& c) {
 
 cudaError_t launch_conv_bwd(const ConvDesc& c, const float* in, const float* ker, const float* dy,
                             float* din, float* dker, float* dbias, void* scratch, cudaStream_t st) {
+    cudaError_t ef = conv_fast(c, false, in, ker, nullptr, nullptr, dy, din, dker, dbias, (float*)scratch,
+                               conv_chunks(c), st);
+    if (ef != cudaErrorNotSupported) return ef;
     conv_bwd_input_kernel<<<cblk(c.batch * c.P * c.D, 256), 256, 0, st>>>(c, dy, ker, din);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;

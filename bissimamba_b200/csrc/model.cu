@@ -22,6 +22,7 @@
 namespace kmb {
 int set_error(const char* msg);
 int set_cuda_error(const char* where, cudaError_t e);
+void clear_error();
 }
 using namespace kmb;
 
@@ -351,7 +352,11 @@ int kmamba_forward(KMamba* m, const uint32_t* tokens, float* logits_out) {
 }
 
 float kmb_model_forward_backward(KMamba* m, const uint32_t* d_tokens, size_t batch, void* stream) {
-    if (!m || !d_tokens || batch == 0) return NAN;
+    clear_error();
+    if (!m || !d_tokens || batch == 0) {
+        set_error("kmb_model_forward_backward: invalid arguments");
+        return NAN;
+    }
     cudaSetDevice(m->dev);
     if (ensure_batch(m, batch)) return NAN;
     cudaStream_t st = (cudaStream_t)stream;

@@ -94,7 +94,9 @@ int kmamba_set_tensor(KMamba *m, const char *name, const float *data);
 
 /* ---- extensions (no counterpart in the reference API) ---- */
 /* Device-token variants split for data parallelism: forward + backward into
- * the gradient arena (zeroed first); returns the mean loss, or NaN on error. */
+ * the gradient arena (zeroed first); returns the mean loss.  On error it
+ * returns NaN and kmb_last_error() is non-empty (a NaN loss with an empty
+ * error string is a numerical result: the recurrence overflowed fp32). */
 float kmb_model_forward_backward(KMamba *m, const uint32_t *d_batch_tokens, size_t batch_size, void *stream);
 /* AdamW over the whole arena (one launch). */
 int kmb_model_optimizer_step(KMamba *m, void *stream);
