@@ -318,42 +318,44 @@ namespace kmb {
 void* workspace(int slot, size_t bytes);
 int set_error(const char* msg);
 int set_cuda_error(const char* where, cudaError_t e);
-enum { WS_BS_PLAN = 3, WS_BS_SCRATCH = 4 };
+enum { WS_BS_SCRATCH = 4 };
 
-// Device copy of the wavefront plan of `dims` (level starts + points), cached
-// per host thread and device for the last shape used.
-struct PlanCache {
-    std::vector<long> dims;
+// Device copy of the wavefront plan of `dims` (level starts [nlev + 1], then the
+// points of every level [L]), cached per host thread, device and shape.
+// Shared with the Scan-A backward (scannd_bwd.cu).
+struct PlanEntry {
     int nlev = 0;
     int* dev = nullptr;
 };
-static thread_local std::map<int, PlanCache> tl_plans;
+static thread_local std::map<int, std::map<std::vector<long>, PlanEntry>> tl_plans;
 
-static int bs_plan(const std::vector<long>& dims, long L, int** out, int* nlev, cudaStream_t st) {
+int device_plan(const std::vector<long>& dims, long L, int** out, int* nlev, cudaStream_t st) {
     int devid = 0;
     cudaGetDevice(&devid);
-    PlanCache& pc = tl_plans[devid];
-    if (pc.dev && pc.dims == dims) {
-        *out = pc.dev;
-        *nlev = pc.nlev;
+    PlanEntry& pe = tl_plans[devid][dims];
+    if (pe.dev) {
+        *out = pe.dev;
+        *nlev = pe.nlev;
         return 0;
     }
     KMWavefrontPlan* pl = km_wavefront_plan_create(dims.data(), (long)dims.size(), 0);
-    if (!pl) return set_error("blockscan: cannot build the wavefront plan");
+    if (!pl) return set_error("cannot build the wavefront plan");
     const int nl = (int)pl->max_level + 1;
     std::vector<int> host(nl + 1 + L);
     for (int i = 0; i <= nl; i++) host[i] = (int)pl->level_starts[i];
     for (long i = 0; i < L; i++) host[nl + 1 + i] = (int)pl->level_offsets[i];
     km_wavefront_plan_free(pl);
-    int* d = (int*)workspace(WS_BS_PLAN, host.size() * sizeof(int));
-    if (!d) return set_error("workspace allocation failed");
-    cudaError_t e = cudaMemcpyAsync(d, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
-    if (e != cudaSuccess) return set_cuda_error("plan upload", e);
-    e = cudaStreamSynchronize(st);  // host vector goes out of scope
-    if (e != cudaSuccess) return set_cuda_error("plan upload", e);
-    pc.dims = dims;
-    pc.nlev = nl;
-    pc.dev = d;
+    int* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, host.size() * sizeof(int));  // one allocation per shape, kept for reuse
+    if (e != cudaSuccess) return set_cuda_error("plan allocation", e);
+    e = cudaMemcpyAsync(d, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // the host vector goes out of scope
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return set_cuda_error("plan upload", e);
+    }
+    pe.dev = d;
+    pe.nlev = nl;
     *out = d;
     *nlev = nl;
     return 0;
@@ -395,7 +397,7 @@ static int bs_desc(const KMBlockScanParams* p, long batch, BSDesc* s, cudaStream
     }
     if (p->ndims <= 1) s->nd = 1;
     int* plan = nullptr;
-    if (bs_plan(dims, p->L, &plan, &s->nlev, st)) return -1;
+    if (device_plan(dims, p->L, &plan, &s->nlev, st)) return -1;
     s->lev_start = plan;
     s->lev_pts = plan + s->nlev + 1;
     s->u = p->u; s->dt = p->dt; s->lam = p->lambda; s->B = p->B; s->C = p->C; s->A = p->A_log;

@@ -31,6 +31,9 @@ cudaError_t launch_scan_fwd_generic(const ScanDesc& s, cudaStream_t st);
 cudaError_t launch_scan_fwd_tma(const ScanDesc& s, int* status, cudaStream_t st);
 cudaError_t launch_scan_fwd_strips(const ScanDesc& s, int* status, cudaStream_t st);
 size_t scan_bwd_generic_scratch_bytes(const ScanDesc& s);
+size_t scan_bwd_wave_scratch_bytes(const ScanDesc& s);
+cudaError_t launch_scan_bwd_wave(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC, float* ddelta,
+                                 float* dlambda, float* dtheta, float* dx, void* scratch, cudaStream_t st);
 cudaError_t launch_scan_bwd_generic(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC,
                                     float* ddelta, float* dlambda, float* dtheta, float* dx, void* scratch,
                                     cudaStream_t st);
@@ -317,6 +320,15 @@ int scannd_backward_async(ScanNDParams* p, long batch, float* dx, void* stream) 
     if (common_kind(ptrs, 16) != PK_DEVICE) return fail("scannd backward needs device pointers");
     ScanDesc s;
     if (!fill_desc(p, batch, &s)) return fail("unsupported ndims / sizes");
+    if (!force_generic()) {
+        void* ws = ws_get(WS_SCRATCH, scan_bwd_wave_scratch_bytes(s));
+        if (!ws) return fail("workspace allocation failed");
+        cudaError_t ew = launch_scan_bwd_wave(s, p->y, p->dA, p->dB, p->dC, p->ddelta, p->dlambda,
+                                              p->theta ? p->dtheta : nullptr, dx, ws, (cudaStream_t)stream);
+        if (ew == cudaSuccess) return 0;
+        if (ew != cudaErrorNotSupported) return fail_cuda("scan_bwd_wave", ew);
+        cudaGetLastError();
+    }
     void* scratch = ws_get(WS_SCRATCH, scan_bwd_generic_scratch_bytes(s));
     if (!scratch) return fail("workspace allocation failed");
     cudaError_t e = launch_scan_bwd_generic(s, p->y, p->dA, p->dB, p->dC, p->ddelta, p->dlambda,

@@ -113,7 +113,17 @@ def test_om_forward_rejects_host_pointers(kmb, cuda):
     ([3, 4, 2], 4, 4, dict(fast_exp=True, clamp=True, a_log_min=-2.0, lam=True)),
     ([64], 8, 4, {}),
 ])
-def test_backward_matches_exact_adjoint(kmb, cuda, dims, D, M, flags):
+@pytest.mark.parametrize("generic", [False, True])
+def test_backward_matches_exact_adjoint(kmb, cuda, dims, D, M, flags, generic):
+    from gpu_util import scan_bwd, assert_grad_close
+    kmb.lib().kmb_set_force_generic(1 if generic else 0)
+    try:
+        _check_backward(dims, D, M, flags, cuda)
+    finally:
+        kmb.lib().kmb_set_force_generic(0)
+
+
+def _check_backward(dims, D, M, flags, cuda):
     from gpu_util import scan_bwd, assert_grad_close
     batch = 2
     inp = po.gen_scan(dims, D, M, batch=batch, seed=41 + D, **flags)
