@@ -73,6 +73,7 @@ def parse():
     ap.add_argument("--workload", default="scan_fwd",
                     choices=["scan_fwd", "scan_bwd", "convnd", "block", "model"],
                     help="scan_fwd = the headline line; the others measure the other BASELINE configs")
+    ap.add_argument("--bf16", action="store_true", help="block workload: bf16 storage, fp32 state (config 3)")
     a = ap.parse_args()
     set_workload(a.dims, a.D, a.M, a.batch)
     return a
@@ -458,12 +459,14 @@ def run_other_workload(args, rank, world):
         from oracle import pyoracle as po  # parameter init only (seeded numpy), not a compute path
         params = po.gen_block_params(dim, N_, R_, seed=42)
         W = {k: torch.from_numpy(v).to(dev) for k, v in params.items()}
-        cfg = kmb.block_config(list(dims), dim, N_, R_)
+        cfg = kmb.block_config(list(dims), dim, N_, R_, bf16=args.bf16)
         w = kmb.KMBlockWeights(**{k: W[k].data_ptr() for k in kmb.BLOCK_FIELDS})
         G = {k: torch.zeros_like(v) for k, v in W.items()}
         gw = kmb.KMBlockGrads(**{k: G[k].data_ptr() for k in kmb.BLOCK_FIELDS})
         act = torch.empty(lib.kmb_block_activation_floats(C.byref(cfg), B_), device=dev)
         x, dout = rn(B_, L_, dim), rn(B_, L_, dim)
+        if args.bf16:
+            x, dout = x.to(torch.bfloat16), dout.to(torch.bfloat16)
         out, dx = torch.empty_like(x), torch.empty_like(x)
 
         def step():
@@ -475,7 +478,9 @@ def run_other_workload(args, rank, world):
         t = ms / steps / 1e3
         line.update(metric="Mamba-3 block fwd+bwd tokens/sec (config 3)", value=B_ * L_ * world / t,
                     unit="tokens/s", ms_per_step=ms / steps,
-                    config={"workload": "block_dim512_N64_R2_2d64x64_b32 (config 3, fp32 storage)"},
+                    config={"workload": "block_dim512_N64_R2_2d64x64_b32 (config 3, "
+                                        + ("bf16 storage, fp32 state)" if args.bf16 else "fp32 storage)")},
+                    dtype="bf16 storage / f32 state" if args.bf16 else "f32",
                     scan_updates_per_s=B_ * L_ * N_ * R_ * world / t)
     else:
         # 12-layer model, dim 512, N 64, R 4, 3D {16,32,32}, batch 64, vocab 256, AdamW

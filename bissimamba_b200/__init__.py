@@ -50,7 +50,7 @@ class KMBlockScanParams(C.Structure):
                 ("u", C.c_void_p), ("dt", C.c_void_p), ("lambda_", C.c_void_p), ("B", C.c_void_p),
                 ("C", C.c_void_p), ("A_log", C.c_void_p), ("theta", C.c_void_p),
                 ("default_lambda", C.c_float), ("use_fast_exp", C.c_int),
-                ("h", C.c_void_p), ("Bu", C.c_void_p), ("y", C.c_void_p)]
+                ("h", C.c_void_p), ("Bu", C.c_void_p), ("y", C.c_void_p), ("inputs_bf16", C.c_int)]
 
 
 class KMBlockScanGrads(C.Structure):
@@ -60,7 +60,7 @@ class KMBlockScanGrads(C.Structure):
 class KMBlockConfig(C.Structure):
     _fields_ = [("dim", C.c_long), ("N", C.c_long), ("R", C.c_long), ("ndims", C.c_long), ("dims", _l),
                 ("L", C.c_long), ("dt_min", C.c_float), ("dt_max", C.c_float), ("default_lambda", C.c_float),
-                ("use_fast_exp", C.c_int)]
+                ("use_fast_exp", C.c_int), ("bf16_storage", C.c_int)]
 
 
 BLOCK_FIELDS = ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "lambda_proj", "b_B", "b_C", "theta")
@@ -74,7 +74,7 @@ class KMBlockGrads(C.Structure):
     _fields_ = [(k, C.c_void_p) for k in BLOCK_FIELDS]
 
 
-def block_config(dims, dim, N, R, dt_min=1e-3, dt_max=0.1, default_lambda=0.5, use_fast_exp=0):
+def block_config(dims, dim, N, R, dt_min=1e-3, dt_max=0.1, default_lambda=0.5, use_fast_exp=0, bf16=False):
     c = KMBlockConfig()
     darr = dims_array(dims)
     c._dims_keep = darr
@@ -86,6 +86,7 @@ def block_config(dims, dim, N, R, dt_min=1e-3, dt_max=0.1, default_lambda=0.5, u
         L *= int(d)
     c.L = L
     c.dt_min, c.dt_max, c.default_lambda, c.use_fast_exp = dt_min, dt_max, default_lambda, use_fast_exp
+    c.bf16_storage = int(bf16)
     return c
 
 

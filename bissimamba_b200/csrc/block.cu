@@ -10,6 +10,7 @@
 // block-scan inputs; the backward mirrors it.  The backward is exact: it also
 // produces dW_in and the projection paths of dx, which the reference skips.
 #include <cublas_v2.h>
+#include <cuda_bf16.h>
 #include <cstring>
 #include <map>
 #include "kmb_common.cuh"
@@ -19,7 +20,7 @@ namespace kmb {
 void* workspace(int slot, size_t bytes);
 int set_error(const char* msg);
 int set_cuda_error(const char* where, cudaError_t e);
-enum { WS_BLK_W = 5, WS_BLK_SCRATCH = 6 };
+enum { WS_BLK_W = 5, WS_BLK_SCRATCH = 6, WS_BLK_WBF = 7 };
 
 struct ActLayout {
     long long BL, Rt, NR;
@@ -34,11 +35,13 @@ static ActLayout act_layout(const KMBlockConfig* c, long batch) {
     size_t o = 0;
     auto take = [&](size_t n) { size_t r = o; o += (n + 63) & ~(size_t)63; return r; };
     a.proj = take(a.BL * a.Rt);
-    a.u = take(a.BL * c->R);
-    a.dt = take(a.BL);
-    a.lam = take(a.BL);
-    a.B = take(a.BL * a.NR);
-    a.C = take(a.BL * a.NR);
+    // scan inputs: bf16 (half a float each) when bf16_storage
+    auto in = [&](size_t n) { return take(c->bf16_storage ? (n + 1) / 2 : n); };
+    a.u = in(a.BL * c->R);
+    a.dt = in(a.BL);
+    a.lam = in(a.BL);
+    a.B = in(a.BL * a.NR);
+    a.C = in(a.BL * a.NR);
     a.h = take(a.BL * c->N);
     a.Bu = take(a.BL * c->N);
     a.y = take(a.BL * c->R);
@@ -48,11 +51,17 @@ static ActLayout act_layout(const KMBlockConfig* c, long batch) {
 
 __device__ __forceinline__ float sigm(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-// Forward epilogue over P[BL, Rt]
+__device__ __forceinline__ void stv(float* p, float v) { *p = v; }
+__device__ __forceinline__ void stv(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ float ldv(const float* p) { return *p; }
+__device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+// Forward epilogue over P[BL, Rt]; T = storage type of the scan inputs
+template <typename T>
 __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, int R, int NR, float dt_min,
                                    float dt_max, const float* __restrict__ bB, const float* __restrict__ bC,
-                                   float* __restrict__ u, float* __restrict__ dt, float* __restrict__ lam,
-                                   float* __restrict__ B, float* __restrict__ C) {
+                                   T* __restrict__ u, T* __restrict__ dt, T* __restrict__ lam,
+                                   T* __restrict__ B, T* __restrict__ C) {
     const long long Rt = R + 2 + 2LL * NR;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= BL * Rt) return;
@@ -60,26 +69,27 @@ __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, in
     const int col = (int)(i - row * Rt);
     const float v = P[i];
     if (col < R) {
-        u[row * R + col] = v / (1.0f + expf(-v));                 // silu
+        stv(u + row * R + col, v / (1.0f + expf(-v)));          // silu
     } else if (col == R) {
         float d = logf(1.0f + expf(v));                           // softplus
         if (d < dt_min) d = dt_min;
         if (d > dt_max) d = dt_max;
-        dt[row] = d;
+        stv(dt + row, d);
     } else if (col == R + 1) {
-        lam[row] = sigm(v);
+        stv(lam + row, sigm(v));
     } else if (col < R + 2 + NR) {
         const int j = col - R - 2;
-        B[row * NR + j] = v + bB[j];
+        stv(B + row * NR + j, v + bB[j]);
     } else {
         const int j = col - R - 2 - NR;
-        C[row * NR + j] = v + bC[j];
+        stv(C + row * NR + j, v + bC[j]);
     }
 }
 
 // Backward epilogue: dP[BL, Rt] from the scan gradients
-__global__ void block_bwd_epilogue(const float* __restrict__ P, const float* __restrict__ dtv,
-                                   const float* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
+template <typename T>
+__global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restrict__ dtv,
+                                   const T* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
                                    float dt_max, const float* __restrict__ du, const float* __restrict__ ddt,
                                    const float* __restrict__ dlam, const float* __restrict__ dB,
                                    const float* __restrict__ dC, float* __restrict__ dP) {
@@ -93,10 +103,12 @@ __global__ void block_bwd_epilogue(const float* __restrict__ P, const float* __r
         const float z = P[i], s = sigm(z);
         g = du[row * R + col] * s * (1.0f + z * (1.0f - s));          // silu'
     } else if (col == R) {
-        const float d = dtv[row];
+        // clamp test on the unrounded softplus (identical to the stored dt in fp32 mode)
+        const float d = fminf(fmaxf(logf(1.0f + expf(P[i])), dt_min), dt_max);
+        (void)dtv;
         g = (d > dt_min && d < dt_max) ? ddt[row] * sigm(P[i]) : 0.0f;  // softplus' inside the clamp
     } else if (col == R + 1) {
-        const float l = lamv[row];
+        const float l = ldv(lamv + row);
         g = dlam[row] * l * (1.0f - l);
     } else if (col < R + 2 + NR) {
         g = dB[row * NR + (col - R - 2)];
@@ -121,6 +133,27 @@ __global__ void block_scatter_grads(const float* __restrict__ G, int R, int NR, 
     else if (row < R + 2 + NR) dst = gWB ? gWB + (long long)(row - R - 2) * dim : nullptr;
     else dst = gWC ? gWC + (long long)(row - R - 2 - NR) * dim : nullptr;
     if (dst) dst[col] += v;
+}
+
+__global__ void to_bf16(const float* __restrict__ a, __nv_bfloat16* __restrict__ b, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) b[i] = __float2bfloat16_rn(a[i]);
+}
+__global__ void to_f32(const __nv_bfloat16* __restrict__ a, float* __restrict__ b, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) b[i] = __bfloat162float(a[i]);
+}
+// out[row, d] = bf16(x[row, d] + sum_r y[row, r] W_out[d, r])   (bf16 residual stream)
+__global__ void block_out_bf16(const __nv_bfloat16* __restrict__ x, const float* __restrict__ y,
+                               const float* __restrict__ Wout, long long BL, int dim, int R,
+                               __nv_bfloat16* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= BL * dim) return;
+    const long long row = i / dim;
+    const int d = (int)(i - row * dim);
+    float acc = 0.0f;
+    for (int r = 0; r < R; r++) acc = __fmaf_rn(y[row * R + r], Wout[(long long)d * R + r], acc);
+    out[i] = __float2bfloat16_rn(__bfloat162float(x[i]) + acc);
 }
 
 __global__ void fill_value(float* p, long long n, float v) {
@@ -190,14 +223,31 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     if (!W) return set_error("kmb_block_forward: weight packing failed");
     const float one = 1.0f, zero = 0.0f;
     const int dim = (int)c->dim;
-    // P^T[Rt, BL] = Wcat[Rt, dim] . X^T
-    if (cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, (int)a.Rt, (int)a.BL, dim, &one, W, dim, x, dim, &zero,
-                    act + a.proj, (int)a.Rt) != CUBLAS_STATUS_SUCCESS)
-        return set_error("projection GEMM failed");
-    block_fwd_epilogue<<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min,
-                                                             c->dt_max, w->b_B, w->b_C, act + a.u, act + a.dt,
-                                                             act + a.lam, act + a.B, act + a.C);
-    cudaError_t e = cudaGetLastError();
+    const bool bf = c->bf16_storage != 0;
+    cudaError_t e;
+    if (bf) {
+        // bf16 x bf16 -> fp32 projection GEMM (tensor cores through cuBLAS)
+        __nv_bfloat16* Wb = (__nv_bfloat16*)workspace(WS_BLK_WBF, (size_t)a.Rt * dim * sizeof(__nv_bfloat16));
+        if (!Wb) return set_error("workspace allocation failed");
+        to_bf16<<<nb(a.Rt * dim, 256), 256, 0, st>>>(W, Wb, a.Rt * dim);
+        if (cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, (int)a.Rt, (int)a.BL, dim, &one, Wb, CUDA_R_16BF, dim, x,
+                         CUDA_R_16BF, dim, &zero, act + a.proj, CUDA_R_32F, (int)a.Rt, CUBLAS_COMPUTE_32F,
+                         CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+            return set_error("bf16 projection GEMM failed");
+        typedef __nv_bfloat16 H;
+        block_fwd_epilogue<H><<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(
+            act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, (H*)(act + a.u),
+            (H*)(act + a.dt), (H*)(act + a.lam), (H*)(act + a.B), (H*)(act + a.C));
+    } else {
+        // P^T[Rt, BL] = Wcat[Rt, dim] . X^T
+        if (cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, (int)a.Rt, (int)a.BL, dim, &one, W, dim, x, dim, &zero,
+                        act + a.proj, (int)a.Rt) != CUBLAS_STATUS_SUCCESS)
+            return set_error("projection GEMM failed");
+        block_fwd_epilogue<float><<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(
+            act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, act + a.u, act + a.dt,
+            act + a.lam, act + a.B, act + a.C);
+    }
+    e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("block epilogue", e);
     KMBlockScanParams p;
     memset(&p, 0, sizeof p);
@@ -205,7 +255,14 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     p.u = act + a.u; p.dt = act + a.dt; p.lambda = act + a.lam; p.B = act + a.B; p.C = act + a.C;
     p.A_log = w->A_log; p.theta = w->theta; p.default_lambda = c->default_lambda; p.use_fast_exp = c->use_fast_exp;
     p.h = act + a.h; p.Bu = act + a.Bu; p.y = act + a.y;
+    p.inputs_bf16 = bf;
     if (kmb_blockscan_forward(&p, batch, stream)) return -1;
+    if (bf) {
+        block_out_bf16<<<nb(a.BL * dim, 256), 256, 0, st>>>((const __nv_bfloat16*)x, act + a.y, w->W_out, a.BL, dim,
+                                                           (int)c->R, (__nv_bfloat16*)out);
+        e = cudaGetLastError();
+        return e == cudaSuccess ? 0 : set_cuda_error("bf16 output", e);
+    }
     // out = x + y . W_out^T
     if ((e = cudaMemcpyAsync(out, x, (size_t)a.BL * dim * sizeof(float), cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
         return set_cuda_error("residual copy", e);
@@ -215,11 +272,10 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     return 0;
 }
 
-extern "C" int kmb_block_backward(const KMBlockConfig* c, const KMBlockWeights* w, const float* x,
-                                  const float* dout, float* dx, const KMBlockGrads* g, long batch, const float* act,
-                                  void* stream) {
-    if (check_cfg(c, w, batch)) return -1;
-    if (!x || !dout || !act || !g) return set_error("kmb_block_backward: x, dout, act, g required");
+// fp32 backward body; in bf16 mode x / dout / dx are fp32 copies and the stored
+// scan inputs are read as bf16
+static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, const float* x, const float* dout,
+                              float* dx, const KMBlockGrads* g, long batch, const float* act, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
     cublasHandle_t hb = cublas_for(st);
     if (!hb) return set_error("cuBLAS initialisation failed");
@@ -254,13 +310,20 @@ extern "C" int kmb_block_backward(const KMBlockConfig* c, const KMBlockWeights* 
     p.u = act + a.u; p.dt = act + a.dt; p.lambda = act + a.lam; p.B = act + a.B; p.C = act + a.C;
     p.A_log = w->A_log; p.theta = w->theta; p.default_lambda = c->default_lambda; p.use_fast_exp = c->use_fast_exp;
     p.h = (float*)(act + a.h); p.Bu = (float*)(act + a.Bu); p.y = (float*)(act + a.y);
+    p.inputs_bf16 = c->bf16_storage;
     KMBlockScanGrads sg;
     sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
     if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
-    block_bwd_epilogue<<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R, (int)NR,
-                                                         c->dt_min, c->dt_max, S + s_du, S + s_ddt, S + s_dlam,
-                                                         S + s_dB, S + s_dC, S + s_dP);
+    if (c->bf16_storage)
+        block_bwd_epilogue<__nv_bfloat16><<<nb(BL * Rt, 256), 256, 0, st>>>(
+            act + a.proj, (const __nv_bfloat16*)(act + a.dt), (const __nv_bfloat16*)(act + a.lam), BL, R, (int)NR,
+            c->dt_min, c->dt_max, S + s_du, S + s_ddt, S + s_dlam, S + s_dB, S + s_dC, S + s_dP);
+    else
+        block_bwd_epilogue<float><<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
+                                                                    (int)NR, c->dt_min, c->dt_max, S + s_du,
+                                                                    S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
+                                                                    S + s_dP);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
     // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
     if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, &one, x, dim, S + s_dP, (int)Rt, &zero,
@@ -289,4 +352,24 @@ extern "C" int kmb_block_backward(const KMBlockConfig* c, const KMBlockWeights* 
             return set_error("dx GEMM failed");
     }
     return 0;
+}
+
+extern "C" int kmb_block_backward(const KMBlockConfig* c, const KMBlockWeights* w, const float* x,
+                                  const float* dout, float* dx, const KMBlockGrads* g, long batch, const float* act,
+                                  void* stream) {
+    if (check_cfg(c, w, batch)) return -1;
+    if (!x || !dout || !act || !g) return set_error("kmb_block_backward: x, dout, act, g required");
+    if (!c->bf16_storage) return block_backward_f32(c, w, x, dout, dx, g, batch, act, stream);
+    // bf16 storage: widen x and dout, run the fp32 body, narrow dx
+    cudaStream_t st = (cudaStream_t)stream;
+    const long long n = (long long)batch * c->L * c->dim;
+    float* buf = (float*)workspace(WS_BLK_WBF + 1, (size_t)n * 3 * sizeof(float));
+    if (!buf) return set_error("workspace allocation failed");
+    float *x32 = buf, *d32 = buf + n, *dx32 = buf + 2 * n;
+    to_f32<<<nb(n, 256), 256, 0, st>>>((const __nv_bfloat16*)x, x32, n);
+    to_f32<<<nb(n, 256), 256, 0, st>>>((const __nv_bfloat16*)dout, d32, n);
+    if (block_backward_f32(c, w, x32, d32, dx ? dx32 : nullptr, g, batch, act, stream)) return -1;
+    if (dx) to_bf16<<<nb(n, 256), 256, 0, st>>>(dx32, (__nv_bfloat16*)dx, n);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : set_cuda_error("bf16 backward", e);
 }

@@ -12,6 +12,7 @@
 // The backward stores every point's state adjoint g_h in a scratch array and
 // pulls its successors' values (no atomics); dA_log and dtheta are reduced
 // from per-item partials in a fixed order.
+#include <cuda_bf16.h>
 #include "kmb_common.cuh"
 #include "../../include/kmamba_block.h"
 
@@ -19,15 +20,19 @@ namespace kmb {
 
 constexpr int BS_MAXND = 8;
 
+__device__ __forceinline__ float ldv(const float* p) { return *p; }
+__device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
 struct BSDesc {
-    int nd, N, R, P2, fast;
+    int nd, N, R, P2, fast, bf16;
     float deflam;
     long long L, batch;
     int dims[BS_MAXND], strides[BS_MAXND];
     int nlev;
     const int* lev_start;   // [nlev + 1]
     const int* lev_pts;     // [L]
-    const float *u, *dt, *lam, *B, *C, *A, *theta;
+    const void *u, *dt, *lam, *B, *C;  // float, or __nv_bfloat16 when bf16
+    const float *A, *theta;
     float *h, *Bu, *y;
 };
 
@@ -41,6 +46,7 @@ __device__ __forceinline__ void bs_unravel(const BSDesc& s, int t, int* idx) {
     for (int k = 0; k < s.nd; k++) idx[k] = (t / s.strides[k]) % s.dims[k];
 }
 
+template <typename T>
 __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
     const int b = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -54,11 +60,11 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
         sth = sinf(s.theta[lane]);
     }
     const long long L = s.L;
-    const float* u = s.u + b * L * R;
-    const float* dtp = s.dt + b * L;
-    const float* lamp = s.lam ? s.lam + b * L : nullptr;
-    const float* Bp = s.B + b * L * NR;
-    const float* Cp = s.C + b * L * NR;
+    const T* u = (const T*)s.u + b * L * R;
+    const T* dtp = (const T*)s.dt + b * L;
+    const T* lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* Bp = (const T*)s.B + b * L * NR;
+    const T* Cp = (const T*)s.C + b * L * NR;
     float* h = s.h + b * L * N;
     float* Bu = s.Bu + b * L * N;
     float* y = s.y + b * L * R;
@@ -66,13 +72,13 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
         const int beg = s.lev_start[lev], end = s.lev_start[lev + 1];
         for (int i = beg + warp; i < end; i += nw) {
             const int t = s.lev_pts[i];
-            const float dt = dtp[t];
-            const float lam = lamp ? lamp[t] : s.deflam;
+            const float dt = ldv(dtp + t);
+            const float lam = lamp ? ldv(lamp + t) : s.deflam;
             float bu0 = 0.0f, bu1 = 0.0f;
             for (int r = 0; r < R; r++) {
-                const float ur = u[(long long)t * R + r];
-                if (h0ok) bu0 = __fmaf_rn(Bp[(long long)t * NR + r * N + n0], ur, bu0);
-                if (h1ok) bu1 = __fmaf_rn(Bp[(long long)t * NR + r * N + n1], ur, bu1);
+                const float ur = ldv(u + (long long)t * R + r);
+                if (h0ok) bu0 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n0), ur, bu0);
+                if (h1ok) bu1 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n1), ur, bu1);
             }
             const float al0 = kmb_exp(dt * A0, s.fast), al1 = kmb_exp(dt * A1, s.fast);
             float hn0, hn1;
@@ -123,8 +129,8 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
             if (h1ok) { h[o + n1] = hn1; Bu[o + n1] = bu1; }
             for (int r = 0; r < R; r++) {
                 float part = 0.0f;
-                if (h0ok) part = Cp[(long long)t * NR + r * N + n0] * hn0;
-                if (h1ok) part = __fmaf_rn(Cp[(long long)t * NR + r * N + n1], hn1, part);
+                if (h0ok) part = ldv(Cp + (long long)t * NR + r * N + n0) * hn0;
+                if (h1ok) part = __fmaf_rn(ldv(Cp + (long long)t * NR + r * N + n1), hn1, part);
                 part = warp_sum(part);
                 if (lane == 0) y[(long long)t * R + r] = part;
             }
@@ -141,6 +147,7 @@ struct BSGrad {
     float* pth;   // scratch [batch, 32]
 };
 
+template <typename T>
 __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) {
     const int b = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -154,11 +161,11 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
         sth = sinf(s.theta[lane]);
     }
     const long long L = s.L;
-    const float* u = s.u + b * L * R;
-    const float* dtp = s.dt + b * L;
-    const float* lamp = s.lam ? s.lam + b * L : nullptr;
-    const float* Bp = s.B + b * L * NR;
-    const float* Cp = s.C + b * L * NR;
+    const T* u = (const T*)s.u + b * L * R;
+    const T* dtp = (const T*)s.dt + b * L;
+    const T* lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* Bp = (const T*)s.B + b * L * NR;
+    const T* Cp = (const T*)s.C + b * L * NR;
     const float* h = s.h + b * L * N;
     const float* Bu = s.Bu + b * L * N;
     const float* dy = g.dy + b * L * R;
@@ -181,15 +188,15 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 idx[k] = (t / strides[k]) % dims[k];
                 npt += idx[k] > 0;
             }
-            const float dt = dtp[t];
-            const float lam = lamp ? lamp[t] : s.deflam;
+            const float dt = ldv(dtp + t);
+            const float lam = lamp ? ldv(lamp + t) : s.deflam;
             // pull from successors s = t + e_k
             float a0 = 0.0f, a1 = 0.0f, ab0 = 0.0f, ab1 = 0.0f;
             for (int k = 0; k < nd; k++) {
                 if (idx[k] >= dims[k] - 1) continue;
                 const int sp = t + strides[k];
-                const float dts = dtp[sp];
-                const float lams = lamp ? lamp[sp] : s.deflam;
+                const float dts = ldv(dtp + sp);
+                const float lams = lamp ? ldv(lamp + sp) : s.deflam;
                 const int nps = npt + (idx[k] == 0 ? 1 : 0);
                 const float al0 = kmb_exp(dts * A0, s.fast), al1 = kmb_exp(dts * A1, s.fast);
                 const float coef = (1.0f - lams) * dts / (float)nps;
@@ -212,11 +219,11 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 const float dyr = dy[(long long)t * R + r];
                 const long long c0 = (long long)t * NR + r * N;
                 if (h0ok) {
-                    gh0 += Cp[c0 + n0] * dyr;
+                    gh0 += ldv(Cp + c0 + n0) * dyr;
                     g.dC[b * L * NR + c0 + n0] += dyr * ht0;
                 }
                 if (h1ok) {
-                    gh1 += Cp[c0 + n1] * dyr;
+                    gh1 += ldv(Cp + c0 + n1) * dyr;
                     g.dC[b * L * NR + c0 + n1] += dyr * ht1;
                 }
             }
@@ -226,16 +233,16 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
             const float gam = lam * dt;
             const float gbu0 = gam * gh0 + ab0, gbu1 = gam * gh1 + ab1;
             for (int r = 0; r < R; r++) {
-                const float ur = u[(long long)t * R + r];
+                const float ur = ldv(u + (long long)t * R + r);
                 const long long c0 = (long long)t * NR + r * N;
                 float part = 0.0f;
                 if (h0ok) {
                     g.dB[b * L * NR + c0 + n0] += gbu0 * ur;
-                    part += gbu0 * Bp[c0 + n0];
+                    part += gbu0 * ldv(Bp + c0 + n0);
                 }
                 if (h1ok) {
                     g.dB[b * L * NR + c0 + n1] += gbu1 * ur;
-                    part += gbu1 * Bp[c0 + n1];
+                    part += gbu1 * ldv(Bp + c0 + n1);
                 }
                 part = warp_sum(part);
                 if (lane == 0) g.du[b * L * R + (long long)t * R + r] += part;
@@ -400,6 +407,7 @@ static int bs_desc(const KMBlockScanParams* p, long batch, BSDesc* s, cudaStream
     if (device_plan(dims, p->L, &plan, &s->nlev, st)) return -1;
     s->lev_start = plan;
     s->lev_pts = plan + s->nlev + 1;
+    s->bf16 = p->inputs_bf16 != 0;
     s->u = p->u; s->dt = p->dt; s->lam = p->lambda; s->B = p->B; s->C = p->C; s->A = p->A_log;
     s->theta = p->theta; s->h = p->h; s->Bu = p->Bu; s->y = p->y;
     return 0;
@@ -421,7 +429,8 @@ extern "C" int kmb_blockscan_forward(const KMBlockScanParams* p, long batch, voi
     cudaStream_t st = (cudaStream_t)stream;
     BSDesc s;
     if (bs_desc(p, batch, &s, st)) return -1;
-    blockscan_fwd_kernel<<<(unsigned)batch, bs_threads(s), 0, st>>>(s);
+    if (s.bf16) blockscan_fwd_kernel<__nv_bfloat16><<<(unsigned)batch, bs_threads(s), 0, st>>>(s);
+    else blockscan_fwd_kernel<float><<<(unsigned)batch, bs_threads(s), 0, st>>>(s);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("blockscan_fwd", e);
 }
@@ -442,7 +451,8 @@ extern "C" int kmb_blockscan_backward(const KMBlockScanParams* p, long batch, co
     g.G = (float*)w;
     g.pA = g.G + nG;
     g.pth = g.pA + (size_t)batch * s.N;
-    blockscan_bwd_kernel<<<(unsigned)batch, bs_threads(s), 0, st>>>(s, g);
+    if (s.bf16) blockscan_bwd_kernel<__nv_bfloat16><<<(unsigned)batch, bs_threads(s), 0, st>>>(s, g);
+    else blockscan_bwd_kernel<float><<<(unsigned)batch, bs_threads(s), 0, st>>>(s, g);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("blockscan_bwd", e);
     if (gr->dA_log) bs_reduce_add<<<1, 64, 0, st>>>(g.pA, gr->dA_log, s.N, batch, s.N);

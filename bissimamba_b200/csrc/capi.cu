@@ -77,7 +77,7 @@ bool force_generic() {
 }
 
 // ---------------------------------------------------------------- workspace
-enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 8 };  // 3, 4: blockscan
+enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 10 };  // 4: blockscan, 5-8: block
 struct Ws {
     void* p = nullptr;
     size_t n = 0;

@@ -30,6 +30,7 @@ typedef struct {
     float default_lambda;   /* used when lambda == NULL */
     int use_fast_exp;
     float *h, *Bu, *y;      /* forward outputs; read back by the backward */
+    int inputs_bf16;        /* 1: u, dt, lambda, B, C are bf16 arrays (state and outputs stay fp32) */
 } KMBlockScanParams;
 
 typedef struct {
@@ -55,6 +56,10 @@ typedef struct {
     long L;                  /* points per item */
     float dt_min, dt_max, default_lambda;
     int use_fast_exp;
+    int bf16_storage;        /* 1: x, out, dout, dx and the stored scan inputs are bf16;
+                                projections run as bf16 x bf16 -> fp32 GEMMs; state, parameters
+                                and their gradients stay fp32 (no counterpart in the reference,
+                                whose use_bf16 flag is never read, include/kmamba.h:47-48) */
 } KMBlockConfig;
 
 /* Parameters, reference layouts (include/kmamba.h:152-175): W_in[R,dim],

@@ -75,3 +75,53 @@ def test_block_backward(kmb, cuda, dims, dim, N, R):
     for k in kmb.BLOCK_FIELDS:
         assert_grad_close(G[k].cpu().numpy(), ref[k], k)
     assert_grad_close(dx.cpu().numpy(), np.stack(dxs), "dx")
+
+
+def _bf16_round(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+@pytest.mark.parametrize("dims,dim,N,R", [([6, 5], 32, 8, 2), ([16, 16], 64, 64, 2), ([64, 64], 512, 64, 2)])
+def test_block_bf16_storage(kmb, cuda, dims, dim, N, R):
+    """bf16 storage, fp32 state: against the double-precision
+    block on bf16-rounded inputs and projection weights, 2e-2 normwise relative on
+    the block's own contribution (out - x) and on every gradient."""
+    import torch
+    batch = 2 if np.prod(dims) <= 256 else 1
+    params = po.gen_block_params(dim, N, R, seed=21)
+    L = int(np.prod(dims))
+    x = np.random.default_rng(22).standard_normal((batch, L, dim)).astype(np.float32)
+    xb = torch.from_numpy(x).to(cuda).to(torch.bfloat16)
+    W = {k: torch.from_numpy(v).to(cuda) for k, v in params.items()}
+    cfg = kmb.block_config(dims, dim, N, R, bf16=True)
+    w = kmb.KMBlockWeights(**{k: W[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+    act = torch.empty(kmb.lib().kmb_block_activation_floats(C.byref(cfg), batch), device=cuda)
+    out = torch.empty_like(xb)
+    kmb.check(kmb.lib().kmb_block_forward(C.byref(cfg), C.byref(w), xb.data_ptr(), out.data_ptr(), batch,
+                                          act.data_ptr(), None), "bf16 block forward")
+    dout = np.random.default_rng(23).standard_normal((batch, L, dim)).astype(np.float32)
+    db = torch.from_numpy(dout).to(cuda).to(torch.bfloat16)
+    G = {k: torch.zeros_like(v) for k, v in W.items()}
+    g = kmb.KMBlockGrads(**{k: G[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+    dx = torch.empty_like(xb)
+    kmb.check(kmb.lib().kmb_block_backward(C.byref(cfg), C.byref(w), xb.data_ptr(), db.data_ptr(), dx.data_ptr(),
+                                           C.byref(g), batch, act.data_ptr(), None), "bf16 block backward")
+    torch.cuda.synchronize()
+    rp = dict(params)
+    for k in ("W_in", "W_B", "W_C", "delta_proj", "lambda_proj"):
+        rp[k] = _bf16_round(params[k])
+    xr = xb.float().cpu().numpy()
+    dr = db.float().cpu().numpy()
+    outg = out.float().cpu().numpy()
+    rel = lambda a, b: np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30)
+    ref_g = {k: 0.0 for k in kmb.BLOCK_FIELDS}
+    for b in range(batch):
+        ex = po.block_fwd64(rp, xr[b], dims, N, R)
+        assert rel(outg[b] - xr[b], ex - xr[b]) <= 2e-2
+        r = po.block_bwd_oracle(rp, xr[b], dr[b], dims, N, R)
+        for k in kmb.BLOCK_FIELDS:
+            ref_g[k] = ref_g[k] + r[k]
+        assert rel(dx[b].float().cpu().numpy(), r["dx"]) <= 2e-2
+    for k in kmb.BLOCK_FIELDS:
+        assert rel(G[k].cpu().numpy(), ref_g[k]) <= 2e-2, k
