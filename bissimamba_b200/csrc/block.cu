@@ -19,6 +19,7 @@
 namespace kmb {
 void* workspace(int slot, size_t bytes);
 int set_error(const char* msg);
+void clear_error();
 int set_cuda_error(const char* where, cudaError_t e);
 enum { WS_BLK_W = 5, WS_BLK_SCRATCH = 6, WS_BLK_WBF = 7 };
 
@@ -344,7 +345,8 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
             return set_error("db_C GEMV failed");
     }
     if (dx) {
-        if ((e = cudaMemcpyAsync(dx, dout, (size_t)BL * dim * sizeof(float), cudaMemcpyDeviceToDevice, st)) !=
+        // dx may alias dout (the reference model passes one buffer for both): dout is last read above
+        if (dx != dout && (e = cudaMemcpyAsync(dx, dout, (size_t)BL * dim * sizeof(float), cudaMemcpyDeviceToDevice, st)) !=
             cudaSuccess)
             return set_cuda_error("dx copy", e);
         if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, &one, W, dim, S + s_dP, (int)Rt, &one, dx,
@@ -372,4 +374,137 @@ extern "C" int kmb_block_backward(const KMBlockConfig* c, const KMBlockWeights* 
     if (dx) to_bf16<<<nb(n, 256), 256, 0, st>>>(dx32, (__nv_bfloat16*)dx, n);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("bf16 backward", e);
+}
+
+// ---------------------------------------------------------------------------
+// The reference's cuda_block_forward / cuda_block_backward signatures, served by
+// the kernels above.  The packed activation buffer is rebuilt from / copied to
+// the caller's named workspace buffers (one sequence per call, like the
+// reference).
+namespace {
+__global__ void gather_proj(const float* P, long long L, int Rt, int R, float* u_raw, float* dt_raw, float* lam_raw) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= L) return;
+    for (int r = 0; r < R; r++) u_raw[t * R + r] = P[t * Rt + r];
+    dt_raw[t] = P[t * Rt + R];
+    lam_raw[t] = P[t * Rt + R + 1];
+}
+__global__ void scatter_proj(float* P, long long L, int Rt, int R, int NR, const float* u_raw, const float* dt_raw,
+                             const float* lam_raw, const float* Bx, const float* Cx) {
+    const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= L) return;
+    for (int r = 0; r < R; r++) P[t * Rt + r] = u_raw[t * R + r];
+    P[t * Rt + R] = dt_raw[t];
+    P[t * Rt + R + 1] = lam_raw ? lam_raw[t] : 0.0f;
+    for (int j = 0; j < NR; j++) {
+        P[t * Rt + R + 2 + j] = Bx[t * NR + j];
+        P[t * Rt + R + 2 + NR + j] = Cx[t * NR + j];
+    }
+}
+
+// Bu[t, n] = sum_r B[t, r N + n] u[t, r] in the forward scan's fma order, for callers that keep
+// no copy of it (the reference passes NULL for dt_exp).
+__global__ void rebuild_bu(const float* B, const float* u, long long L, int N, int R, float* Bu) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= L * N) return;
+    const long long t = i / N;
+    const int n = (int)(i - t * N);
+    float acc = 0.0f;
+    for (int r = 0; r < R; r++) acc = __fmaf_rn(B[t * (long long)N * R + r * N + n], u[t * R + r], acc);
+    Bu[i] = acc;
+}
+
+KMBlockConfig ref_cfg(int L, int state, int dim, int R, int nd, const long* dims) {
+    KMBlockConfig c;
+    memset(&c, 0, sizeof c);
+    c.dim = dim; c.N = state; c.R = R < 1 ? 1 : R; c.ndims = nd; c.dims = dims; c.L = L;
+    c.dt_min = 0.001f; c.dt_max = 0.1f; c.default_lambda = 0.5f;  // reference GPU kernels hard-code these
+    return c;
+}
+}  // namespace
+
+extern "C" void cuda_block_forward(void* cublas, const float* d_W_in, const float* d_W_out, const float* d_A_log,
+                                   const float* d_W_B, const float* d_W_C, const float* d_delta_proj,
+                                   const float* d_theta, const float* d_lambda_proj, const float* d_x, float* d_y,
+                                   float* d_u_raw, float* d_u, float* d_dt_raw, float* d_dt, float* d_B_exp,
+                                   float* d_C_exp, float* d_dt_exp, float* d_h_store, float* d_y_scan,
+                                   float* d_y_proj, float* d_lambda_raw, float* d_lambda, int L, int state, int dim,
+                                   int R, int spatial_ndims, const long* spatial_dims) {
+    (void)cublas;
+    clear_error();
+    KMBlockConfig c = ref_cfg(L, state, dim, R, spatial_ndims, spatial_dims);
+    const long long NR = (long long)state * c.R;
+    float* zeros = (float*)workspace(WS_BLK_WBF + 2, (size_t)NR * sizeof(float) * 2);
+    const size_t nact = kmb_block_activation_floats(&c, 1);
+    float* act = (float*)workspace(WS_BLK_WBF + 3, nact * sizeof(float));
+    if (!zeros || !act) { set_error("workspace allocation failed"); return; }
+    cudaMemsetAsync(zeros, 0, (size_t)NR * sizeof(float) * 2, 0);
+    KMBlockWeights w = {d_W_in, d_W_out, d_A_log, d_W_B, d_W_C, d_delta_proj, d_lambda_proj, zeros, zeros + NR, d_theta};
+    if (kmb_block_forward(&c, &w, d_x, d_y, 1, act, nullptr)) return;
+    const ActLayout a = act_layout(&c, 1);
+    gather_proj<<<nb(L, 256), 256>>>(act + a.proj, L, (int)a.Rt, (int)c.R, d_u_raw, d_dt_raw, d_lambda_raw);
+    const size_t f = sizeof(float);
+    cudaMemcpyAsync(d_u, act + a.u, (size_t)L * c.R * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(d_dt, act + a.dt, (size_t)L * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(d_lambda, act + a.lam, (size_t)L * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(d_B_exp, act + a.B, (size_t)L * NR * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(d_C_exp, act + a.C, (size_t)L * NR * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(d_h_store, act + a.h, (size_t)L * state * f, cudaMemcpyDeviceToDevice, 0);
+    if (d_dt_exp) cudaMemcpyAsync(d_dt_exp, act + a.Bu, (size_t)L * state * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(d_y_scan, act + a.y, (size_t)L * c.R * f, cudaMemcpyDeviceToDevice, 0);
+    if (d_y_proj) {  // y_proj = y - x
+        cudaMemcpyAsync(d_y_proj, d_y, (size_t)L * dim * f, cudaMemcpyDeviceToDevice, 0);
+        const float m1 = -1.0f;
+        cublasHandle_t hb = cublas_for(0);
+        if (hb) cublasSaxpy(hb, L * dim, &m1, d_x, 1, d_y_proj, 1);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) set_cuda_error("cuda_block_forward", e);
+}
+
+extern "C" void cuda_block_backward(void* cublas, const float* d_W_in, const float* d_W_out, const float* d_A_log,
+                                    const float* d_W_B, const float* d_W_C, const float* d_delta_proj,
+                                    const float* d_theta, const float* d_lambda_proj, const float* d_x,
+                                    const float* d_u_raw, const float* d_u, const float* d_dt_raw, const float* d_dt,
+                                    const float* d_B_exp, const float* d_C_exp, const float* d_dt_exp,
+                                    const float* d_h_store, const float* d_y_scan, const float* d_lambda,
+                                    const float* d_dy, float* d_dW_in, float* d_dW_out, float* d_dA_log,
+                                    float* d_dW_B, float* d_dW_C, float* d_ddelta_proj, float* d_g_theta,
+                                    float* d_g_lambda_proj, float* d_dx, float* d_dy_scan, float* d_du,
+                                    float* d_du_raw, float* d_ddt, float* d_ddt_raw, float* d_dB_scan,
+                                    float* d_dC_scan, float* d_ddt_scan, float* d_dA_tmp, float* d_dlambda,
+                                    float* d_dlambda_raw, int L, int state, int dim, int R, int spatial_ndims,
+                                    const long* spatial_dims) {
+    (void)cublas; (void)d_dy_scan; (void)d_du; (void)d_du_raw; (void)d_ddt; (void)d_ddt_raw; (void)d_dB_scan;
+    (void)d_dC_scan; (void)d_ddt_scan; (void)d_dA_tmp; (void)d_dlambda; (void)d_dlambda_raw;
+    clear_error();
+    KMBlockConfig c = ref_cfg(L, state, dim, R, spatial_ndims, spatial_dims);
+    const long long NR = (long long)state * c.R;
+    float* zeros = (float*)workspace(WS_BLK_WBF + 2, (size_t)NR * sizeof(float) * 2);
+    const size_t nact = kmb_block_activation_floats(&c, 1);
+    float* act = (float*)workspace(WS_BLK_WBF + 3, nact * sizeof(float));
+    if (!zeros || !act) { set_error("workspace allocation failed"); return; }
+    cudaMemsetAsync(zeros, 0, (size_t)NR * sizeof(float) * 2, 0);
+    const ActLayout a = act_layout(&c, 1);
+    // rebuild the packed activations: P columns from the raw buffers (B / C columns are only
+    // copied for completeness; the backward reads u_raw, dt_raw from P and the rest from the arrays)
+    // lambda_raw is not passed to the reference backward; P's lambda column is unused by the backward.
+    scatter_proj<<<nb(L, 256), 256>>>(act + a.proj, L, (int)a.Rt, (int)c.R, (int)NR, d_u_raw, d_dt_raw, nullptr,
+                                      d_B_exp, d_C_exp);
+    const size_t f = sizeof(float);
+    cudaMemcpyAsync(act + a.u, d_u, (size_t)L * c.R * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(act + a.dt, d_dt, (size_t)L * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(act + a.lam, d_lambda, (size_t)L * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(act + a.B, d_B_exp, (size_t)L * NR * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(act + a.C, d_C_exp, (size_t)L * NR * f, cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(act + a.h, d_h_store, (size_t)L * state * f, cudaMemcpyDeviceToDevice, 0);
+    if (d_dt_exp)
+        cudaMemcpyAsync(act + a.Bu, d_dt_exp, (size_t)L * state * f, cudaMemcpyDeviceToDevice, 0);
+    else
+        rebuild_bu<<<nb((long long)L * state, 256), 256>>>(d_B_exp, d_u, L, state, (int)c.R, act + a.Bu);
+    cudaMemcpyAsync(act + a.y, d_y_scan, (size_t)L * c.R * f, cudaMemcpyDeviceToDevice, 0);
+    KMBlockWeights w = {d_W_in, d_W_out, d_A_log, d_W_B, d_W_C, d_delta_proj, d_lambda_proj, zeros, zeros + NR, d_theta};
+    KMBlockGrads g = {d_dW_in, d_dW_out, d_dA_log, d_dW_B, d_dW_C, d_ddelta_proj, d_g_lambda_proj, nullptr, nullptr,
+                      d_g_theta};
+    kmb_block_backward(&c, &w, d_x, d_dy, d_dx, &g, 1, act, nullptr);
 }

@@ -77,7 +77,7 @@ bool force_generic() {
 }
 
 // ---------------------------------------------------------------- workspace
-enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 10 };  // 4: blockscan, 5-8: block
+enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 12 };  // 4: blockscan, 5-10: block
 struct Ws {
     void* p = nullptr;
     size_t n = 0;
@@ -86,6 +86,7 @@ thread_local std::map<int, Ws> tl_ws[WS_NSLOTS];
 
 void* ws_get(int slot, size_t bytes) {
     int dev = 0;
+    if (slot < 0 || slot >= WS_NSLOTS) return nullptr;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     Ws& w = tl_ws[slot][dev];
     if (w.n < bytes) {
@@ -233,6 +234,7 @@ bool scan_sizes(const ScanNDParams* p, long batch, size_t* sz /*[9]*/) {
 extern "C" {
 
 const char* kmb_last_error(void) { return tl_err.c_str(); }
+void kmb_clear_error(void) { tl_err.clear(); }
 int kmb_last_forward_path(void) { return tl_fast_path; }
 void kmb_set_force_generic(int on) { g_force_generic = on ? 1 : 0; }
 

@@ -7,6 +7,8 @@ extern "C" {
 #endif
 /* Text of the last error raised on this host thread ("" if none). */
 const char *kmb_last_error(void);
+/* Empty the last-error text of this host thread. */
+void kmb_clear_error(void);
 /* Which Scan-A forward kernel the last forward call on this thread used:
  * 1 = persistent TMA kernel (1D/2D fast path), 0 = generic kernel, -1 = none. */
 int kmb_last_forward_path(void);

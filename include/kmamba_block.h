@@ -90,6 +90,43 @@ int kmb_block_forward(const KMBlockConfig *c, const KMBlockWeights *w, const flo
 int kmb_block_backward(const KMBlockConfig *c, const KMBlockWeights *w, const float *x, const float *dout,
                        float *dx, const KMBlockGrads *g, long batch, const float *act, void *stream);
 
+/* ---- the reference's GPU block entry points, same argument lists -------------
+ * cuda/mamba_block.cu:223-244 and :306-346 (the prototype of the definition;
+ * src/kmamba.c:36-51 declares a different argument order for the backward --
+ * this one follows the definition).  All pointers are device pointers for one
+ * sequence of L points; `cublas` is accepted and ignored.  The reference's GPU
+ * block has no B / C biases, so none are applied.  The caller's workspace
+ * buffers receive what the reference stores in them (u_raw, u, dt_raw, dt,
+ * B_exp, C_exp, h_store, y_scan, y_proj, lambda_raw, lambda).  dt_exp may be
+ * NULL, as the reference passes it; when given ([L, state] floats) it receives
+ * the B*u products, and the backward reads them instead of recomputing them.
+ * The backward accumulates the exact gradients (+=) and writes d_dx; its
+ * scratch arguments (dy_scan .. dlambda_raw) are unused and may be NULL.
+ * The computation is the CPU MambaBlock's (src/mamba_block.c), the same as
+ * kmb_block_forward with zero B / C biases, dt in [1e-3, 0.1] and default
+ * lambda 0.5.  The reference's GPU body instead runs the Scan-A kernel with
+ * D = state, M = 1 over u[L, R] (cuda/mamba_block.cu:271-291), which reads past
+ * u whenever state > R; that is not reproduced.  d_dx may alias d_dy, as the
+ * reference model passes it (src/kmamba.c:567-568).
+ * There is no error channel in these void functions: kmb_last_error() is set. */
+void cuda_block_forward(void *cublas, const float *d_W_in, const float *d_W_out, const float *d_A_log,
+                        const float *d_W_B, const float *d_W_C, const float *d_delta_proj, const float *d_theta,
+                        const float *d_lambda_proj, const float *d_x, float *d_y, float *d_u_raw, float *d_u,
+                        float *d_dt_raw, float *d_dt, float *d_B_exp, float *d_C_exp, float *d_dt_exp,
+                        float *d_h_store, float *d_y_scan, float *d_y_proj, float *d_lambda_raw, float *d_lambda,
+                        int L, int state, int dim, int R, int spatial_ndims, const long *spatial_dims);
+void cuda_block_backward(void *cublas, const float *d_W_in, const float *d_W_out, const float *d_A_log,
+                         const float *d_W_B, const float *d_W_C, const float *d_delta_proj, const float *d_theta,
+                         const float *d_lambda_proj, const float *d_x, const float *d_u_raw, const float *d_u,
+                         const float *d_dt_raw, const float *d_dt, const float *d_B_exp, const float *d_C_exp,
+                         const float *d_dt_exp, const float *d_h_store, const float *d_y_scan,
+                         const float *d_lambda, const float *d_dy, float *d_dW_in, float *d_dW_out,
+                         float *d_dA_log, float *d_dW_B, float *d_dW_C, float *d_ddelta_proj, float *d_g_theta,
+                         float *d_g_lambda_proj, float *d_dx, float *d_dy_scan, float *d_du, float *d_du_raw,
+                         float *d_ddt, float *d_ddt_raw, float *d_dB_scan, float *d_dC_scan, float *d_ddt_scan,
+                         float *d_dA_tmp, float *d_dlambda, float *d_dlambda_raw, int L, int state, int dim, int R,
+                         int spatial_ndims, const long *spatial_dims);
+
 #ifdef __cplusplus
 }
 #endif

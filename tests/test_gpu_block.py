@@ -125,3 +125,70 @@ def test_block_bf16_storage(kmb, cuda, dims, dim, N, R):
         assert rel(dx[b].float().cpu().numpy(), r["dx"]) <= 2e-2
     for k in kmb.BLOCK_FIELDS:
         assert rel(G[k].cpu().numpy(), ref_g[k]) <= 2e-2, k
+
+
+@pytest.mark.parametrize("dims,dim,N,R,keep_bu,alias", [([6, 5], 16, 8, 2, False, True), ([24], 16, 8, 1, True, False),
+                                                        ([4, 4, 3], 32, 16, 2, False, False)])
+def test_reference_block_abi(kmb, cuda, dims, dim, N, R, keep_bu, alias):
+    """cuda_block_forward / cuda_block_backward (the reference's argument lists,
+    cuda/mamba_block.cu:223-346) agree bit for bit with kmb_block_forward /
+    kmb_block_backward at batch 1 with zero B / C biases, whether dt_exp is NULL
+    (the reference's call) or kept, and with d_dx aliasing d_dy."""
+    import torch
+    params = po.gen_block_params(dim, N, R, seed=dim + N)
+    params["b_B"] = np.zeros_like(params["b_B"])
+    params["b_C"] = np.zeros_like(params["b_C"])
+    L = int(np.prod(dims))
+    NR = N * R
+    rng = np.random.default_rng(3)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(cuda)
+    W = {k: t(v) for k, v in params.items()}
+    x = t(rng.standard_normal((L, dim)))
+    dy = t(rng.standard_normal((L, dim)))
+    lib = kmb.lib()
+    # own ABI
+    cfg = kmb.block_config(dims, dim, N, R)
+    w = kmb.KMBlockWeights(**{k: W[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+    act = torch.empty(lib.kmb_block_activation_floats(C.byref(cfg), 1), device=cuda)
+    y_own = torch.empty_like(x)
+    kmb.check(lib.kmb_block_forward(C.byref(cfg), C.byref(w), x.data_ptr(), y_own.data_ptr(), 1, act.data_ptr(),
+                                    None), "block forward")
+    G_own = {k: torch.zeros_like(v) for k, v in W.items()}
+    g = kmb.KMBlockGrads(**{k: G_own[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+    dx_own = torch.empty_like(x)
+    kmb.check(lib.kmb_block_backward(C.byref(cfg), C.byref(w), x.data_ptr(), dy.data_ptr(), dx_own.data_ptr(),
+                                     C.byref(g), 1, act.data_ptr(), None), "block backward")
+    # reference ABI
+    z = lambda *s: torch.zeros(*s, device=cuda)
+    ws = dict(u_raw=z(L, R), u=z(L, R), dt_raw=z(L), dt=z(L), B_exp=z(L, NR), C_exp=z(L, NR),
+              dt_exp=z(L, N) if keep_bu else None, h=z(L, N), y_scan=z(L, R), y_proj=z(L, dim), lam_raw=z(L),
+              lam=z(L))
+    p = lambda a: None if a is None else C.c_void_p(a.data_ptr())
+    darr = kmb.dims_array(dims)
+    y_ref = torch.empty_like(x)
+    lib.cuda_block_forward.restype = None
+    lib.cuda_block_forward(None, *[p(W[k]) for k in ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "theta",
+                                                     "lambda_proj")],
+                           p(x), p(y_ref), p(ws["u_raw"]), p(ws["u"]), p(ws["dt_raw"]), p(ws["dt"]), p(ws["B_exp"]),
+                           p(ws["C_exp"]), p(ws["dt_exp"]), p(ws["h"]), p(ws["y_scan"]), p(ws["y_proj"]),
+                           p(ws["lam_raw"]), p(ws["lam"]), L, N, dim, R, len(dims), C.cast(darr, C.POINTER(C.c_long)))
+    torch.cuda.synchronize()
+    assert kmb.last_error() == "", kmb.last_error()
+    assert torch.equal(y_ref, y_own)
+    torch.testing.assert_close(ws["y_proj"], y_own - x, rtol=0, atol=0)
+    G_ref = {k: torch.zeros_like(v) for k, v in W.items()}
+    dbuf = dy.clone()
+    dx_ref = dbuf if alias else torch.empty_like(x)
+    lib.cuda_block_backward.restype = None
+    lib.cuda_block_backward(None, *[p(W[k]) for k in ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "theta",
+                                                      "lambda_proj")],
+                            p(x), p(ws["u_raw"]), p(ws["u"]), p(ws["dt_raw"]), p(ws["dt"]), p(ws["B_exp"]),
+                            p(ws["C_exp"]), p(ws["dt_exp"]), p(ws["h"]), p(ws["y_scan"]), p(ws["lam"]), p(dbuf),
+                            *[p(G_ref[k]) for k in ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "theta",
+                                                    "lambda_proj")],
+                            p(dx_ref), *([None] * 11), L, N, dim, R, len(dims), C.cast(darr, C.POINTER(C.c_long)))
+    torch.cuda.synchronize()
+    assert kmb.last_error() == "", kmb.last_error()
+    for k in ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "theta", "lambda_proj"):
+        assert torch.equal(G_ref[k], G_own[k]), k
+    assert torch.equal(dx_ref, dx_own)
