@@ -48,30 +48,18 @@ __device__ __forceinline__ float kmb_exp(float z, int fast) {
     return expf(z);
 }
 
-// exp(z) = 2^(z log2 e) on the hardware base-2 exponential, with the rounding
-// error of the product z * log2(e) recovered exactly by an FMA (plus the tail
-// of log2 e beyond float precision) and applied as a first-order correction
-// 2^(t + tl) ~ 2^t (1 + tl ln 2).  5 instructions, no branches; the error is
-// that of ex2.approx (a couple of ulp), like expf's.  Results below 2^-126 are
-// flushed to zero.
-__device__ __forceinline__ float kmb_exp2c(float z) {
-    const float kL2eHi = 1.44269502162933349609375f;   // float(log2 e)
-    const float kL2eLo = 1.925963033500011e-08f;       // log2 e - kL2eHi
-    const float t = __fmul_rn(z, kL2eHi);
-    const float tl = __fmaf_rn(z, kL2eLo, __fmaf_rn(z, kL2eHi, -t));
+// 2^w as one hardware base-2 exponential (ex2.approx, a few ulp for |w| < 4;
+// results below 2^-126 flush to zero).  exp(delta * A) is evaluated as
+// kmb_ex2(delta * (A log2 e)) with A log2 e rounded once per channel, so the
+// argument carries ~|delta A log2 e| * 2^-23 relative error from two roundings:
+// one multiply and one ex2 per exponential instead of expf's range-reduction
+// sequence.
+__device__ __forceinline__ float kmb_ex2(float w) {
     float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
-    return __fmaf_rn(e, __fmul_rn(tl, 0.693147180559945309f), e);
-}
-
-// exp(z) as one hardware base-2 exponential of the rounded product
-// z * log2(e): 2 instructions; adds up to ~|z log2 e| * 2^-24 relative error
-// from the rounded product on top of ex2.approx's own (a few ulp for |z| < 4).
-__device__ __forceinline__ float kmb_exp2r(float z) {
-    float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(z, 1.44269502162933349609375f)));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(w));
     return e;
 }
+constexpr float kKmbLog2e = 1.44269502162933349609375f;  // log2(e) rounded to float
 
 // d/dz of kmb_exp given e = kmb_exp(z)
 __device__ __forceinline__ float kmb_dexp(float z, float e, int fast) {

@@ -230,6 +230,18 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     // per-thread offsets inside a stage
     const int bofs = (cl0 * MT + m) * 4;                 // B / C box: [j][CH][MT]
     const int xofs = cl0;                                // x / delta box column (+ (d0 & 3))
+    // y: after the butterfly, lane gl of a GS-lane group holds the sum of value
+    // index butterfly_index(gl) = (column j, channel c); fixed per lane
+    bool y_lane;
+    long long y_col;
+    {
+        constexpr int NV = WC * CPT, LPV = GS / NV;
+        const int gl = lane & (GS - 1);
+        const int idx = butterfly_index<NV, GS>(gl);
+        const int j = idx / CPT, c = idx % CPT;
+        y_lane = (LPV <= 1 || (gl % LPV) == 0) && j < ncol;
+        y_col = (long long)(q0 + j) * qstride * D + cl0 + c;
+    }
     int row = 0, slot = 0;  // consumer row counter and its stage slot / phase
     uint32_t ph = 0;
 
@@ -240,8 +252,9 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
 #pragma unroll
         for (int c = 0; c < CPT; c++) {
             const int d = d0 + cl0 + c;
-            AI[c] = kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + m], f.clamp, f.amin);
-            AO[c] = kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + m], f.clamp, f.amin);
+            // A log2 e: alpha = 2^(delta * A log2 e) is one multiply and one ex2 per update
+            AI[c] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + m], f.clamp, f.amin), kKmbLog2e);
+            AO[c] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + m], f.clamp, f.amin), kKmbLog2e);
         }
         if (ROPE) {
             const float th = f.theta[(d0 + cl0) >> 1];
@@ -249,7 +262,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             sth = sinf(th);
         }
         float* const hbase = f.h + (long long)b * P * DM + (long long)(d0 + cl0) * MT + m + (long long)q0 * hq;
-        float* const ybase = f.y + (long long)b * P * D + d0;
+        float* const ybase = f.y + (long long)b * P * D + d0 + y_col;
         const int xo = (d0 & 3) + xofs;
         float ring_h[WC][CPT], ring_b[WC][CPT];
 
@@ -307,16 +320,17 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     const float Bv = Bs[j * CH * MT + c * MT];
                     const float dt = __fadd_rn(dI, dO);
                     const float bu = __fmul_rn(Bv, x);
-                    const float aI = kmb_exp2r(__fmul_rn(dI, AI[c]));
+                    const float aI = kmb_ex2(__fmul_rn(dI, AI[c]));
                     float buacc, dacc, hacc, inv;
                     // inner predecessor: the previous column (strip w-1's last column when j == 0)
                     const float hatI = (j == 0) ? lh[c] : ring_h[j == 0 ? 0 : j - 1][c];
                     const float buI = (j == 0) ? lb[c] : ring_b[j == 0 ? 0 : j - 1][c];
                     if (HASO) {
-                        const float aO = kmb_exp2r(__fmul_rn(dO, AO[c]));
+                        const float aO = kmb_ex2(__fmul_rn(dO, AO[c]));
                         if (j > 0 || w > 0) {
-                            // two predecessors: mean of two = sum * 0.5 (exact), so
-                            // ((1-lam) dt (dacc/2)) (buacc/2) == (((1-lam) dt / 4) dacc) buacc bit for bit
+                            // two predecessors: mean of two = sum * 0.5 (exact), so the
+                            // coefficient (1-lam) dt (dacc/2) (buacc/2) is ((1-lam) dt / 4) (dacc buacc);
+                            // h = (A-part + that) + gamma bu, as two fused multiply-adds
                             buacc = __fadd_rn(buI, ring_b[j][c]);
                             dacc = __fadd_rn(aI, aO);
                             hacc = KIN0 ? __fmaf_rn(aO, ring_h[j][c], __fmul_rn(aI, hatI))
@@ -324,7 +338,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                             const float omdtq = LAMB ? __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), 0.25f)
                                                      : __fmul_rn(omlq, dt);
                             const float gamma2 = __fmul_rn(lam, dt);
-                            hn[c] = __fadd_rn(__fmaf_rn(bu, gamma2, __fmul_rn(__fmul_rn(omdtq, dacc), buacc)), hacc);
+                            hn[c] = __fmaf_rn(gamma2, bu, __fmaf_rn(omdtq, __fmul_rn(dacc, buacc), hacc));
                             goto have_h;
                         } else {
                             buacc = ring_b[j][c];
@@ -396,17 +410,10 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
 #pragma unroll
                     for (int c = 0; c < CPT; c++) v[j * CPT + c] = prod[j][c];
                 const float sum = butterfly<NV, GS>(v, lane);
-                constexpr int LPV = GS / NV;
-                const int gl = lane & (GS - 1);
-                if (LPV <= 1 || (gl % LPV) == 0) {
-                    const int idx = butterfly_index<NV, GS>(gl);
-                    const int j = idx / CPT, c = idx % CPT;
-                    if (j < ncol) {
-                        const int cl = (MT >= 32 ? 0 : (lane / MT) * CPT) + c;
-                        float* yp = ybase + ((long long)o * ostride + (long long)(q0 + j) * qstride) * D + cl;
-                        if (red_y) atomicAdd(yp, sum);
-                        else *yp = sum;
-                    }
+                if (y_lane) {
+                    float* yp = ybase + (long long)o * ostride * D;
+                    if (red_y) atomicAdd(yp, sum);
+                    else *yp = sum;
                 }
             }
             __syncwarp();
