@@ -177,11 +177,12 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     // all maintained incrementally (no runtime divisions per row)
     int next_issue = 0, is_o = 0, is_slot = 0;
     uint32_t is_phase = 0;
-    long long is_tile = blockIdx.x;
+    // issuer's tile as (item, channel tile), advanced without divisions
+    int is_b = (int)(blockIdx.x / ntd), is_dt = (int)(blockIdx.x - (long long)is_b * ntd);
 
     auto issue = [&]() {
-        const int b = (int)(is_tile / ntd);
-        const int d0 = (int)(is_tile - (long long)b * ntd) * CH;
+        const int b = is_b;
+        const int d0 = is_dt * CH;
         const int o = is_o;
         unsigned char* st = my_stages + (size_t)is_slot * ST;
         const uint32_t full = smem_u32(&b_full[w * NSS + is_slot]);
@@ -197,7 +198,10 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     };
     auto advance_issue = [&]() {
         next_issue++;
-        if (++is_o == O) { is_o = 0; is_tile += gridDim.x; }
+        if (++is_o == O) {
+            is_o = 0;
+            for (is_dt += gridDim.x; is_dt >= ntd; is_dt -= ntd) is_b++;
+        }
         if (++is_slot == NSS) { is_slot = 0; is_phase ^= 1u; }
     };
     // Keep up to NSS rows in flight; block only for the row about to be consumed.
@@ -242,6 +246,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
         y_lane = (LPV <= 1 || (gl % LPV) == 0) && j < ncol;
         y_col = (long long)(q0 + j) * qstride * D + cl0 + c;
     }
+    const long long h_ostep = ostride * DM, y_ostep = ostride * D;  // one outer step in h / y
     int row = 0, slot = 0;  // consumer row counter and its stage slot / phase
     uint32_t ph = 0;
 
@@ -261,8 +266,9 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             cth = cosf(th);
             sth = sinf(th);
         }
-        float* const hbase = f.h + (long long)b * P * DM + (long long)(d0 + cl0) * MT + m + (long long)q0 * hq;
-        float* const ybase = f.y + (long long)b * P * D + d0 + y_col;
+        // h and y of the current row, advanced by one outer step per row
+        float* hrow = f.h + (long long)b * P * DM + (long long)(d0 + cl0) * MT + m + (long long)q0 * hq;
+        float* yrow = f.y + (long long)b * P * D + d0 + y_col;
         const int xo = (d0 & 3) + xofs;
         float ring_h[WC][CPT], ring_b[WC][CPT];
 
@@ -307,7 +313,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             }
             float prod[WC][CPT];
             float lastH[CPT], lastB[CPT];
-            float* hp = hbase + (long long)o * ostride * DM;
+            float* hp = hrow;
 #pragma unroll
             for (int j = 0; j < WC; j++) {
                 const float lam = LAMB ? Ls[j * (KIN0 ? 4 : 1)] : deflam;
@@ -411,15 +417,16 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     for (int c = 0; c < CPT; c++) v[j * CPT + c] = prod[j][c];
                 const float sum = butterfly<NV, GS>(v, lane);
                 if (y_lane) {
-                    float* yp = ybase + (long long)o * ostride * D;
-                    if (red_y) atomicAdd(yp, sum);
-                    else *yp = sum;
+                    if (red_y) atomicAdd(yrow, sum);
+                    else *yrow = sum;
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&b_empty[w * NSS + slot]));
             row++;
             if (++slot == NSS) { slot = 0; ph ^= 1u; }
+            hrow += h_ostep;
+            yrow += y_ostep;
             return true;
         };
 
