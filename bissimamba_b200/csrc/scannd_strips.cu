@@ -3,24 +3,26 @@
 //
 // The grid is walked row by row (outer o, inner q, inner extent Q <= 64).  A
 // CTA owns a tile (item b, CH consecutive channels, all M states) and splits
-// the inner axis into S <= 8 column strips of Wc <= 8 columns.  Warp (w, h)
-// owns strip w for the lane half h (M=64 needs two warps per channel).  Each
-// thread owns one state index m for CPT channels (2 when RoPE pairs channels,
-// so the rotation needs no shuffle) and keeps, per column of its strip, the
-// rotated state R h and the B*x product of the previous row in registers
-// (ring of Wc slots).  The value left of its first column comes from strip
-// w-1 through a shared-memory handoff slot guarded by mbarriers; strips run
-// one row apart, like a systolic array, so all warps stay busy.
+// the inner axis into S <= 8 column strips of Wc <= 8 columns; warp w owns
+// strip w.  Each lane carries CPT = 2 channels (the RoPE pair, so the rotation
+// needs no shuffle, or two independent channels) and SPT state slots (m, and
+// m + 32 when M = 64): up to four independent state chains per lane, which
+// amortises the per-row and per-point work and gives the scheduler ILP.  Per
+// column of its strip a lane keeps the rotated state R h and the B*x product
+// of the previous row in registers (ring of Wc slots).  The value left of its
+// first column comes from strip w-1 through a shared-memory handoff slot
+// guarded by mbarriers; strips run one row apart, like a systolic array.
+// (The HW > 1 lane-half split, with y accumulated by red.add into a zeroed y,
+// remains for geometries where one warp cannot cover M; the supported M of
+// 16, 32 and 64 all use HW = 1.)
 //
 // Data: per strip a ring of NSS stages, each one row of the strip: TMA boxes
 // of B and C [Wc][CH][M], x and delta [.][Wc][4] (4-channel boxes, aligned),
-// lambda; issued by lane 0 of the strip's first warp, NSS-1 rows ahead.  Only
+// lambda; issued by lane 0 of the strip's warp, NSS-1 rows ahead.  Only
 // B, C, x, delta, lambda are read (once) and h, y written (once): 12 B per
 // state update + 16 B per (point, channel).
-// y[p, d] = sum_m C h: each warp reduces its 8 points x CPT channels across
-// its lanes with a transposed butterfly; with two lane halves (M = 64) the two
-// partials are added into a zeroed y with red.add (two addends in either order
-// give the same fp32 sum, so the result is deterministic).
+// y[p, d] = sum_m C h: each lane first adds its state slots, then the warp
+// reduces its 8 points x CPT channels across lanes with a transposed butterfly.
 #include <cuda.h>
 #include "kmb_common.cuh"
 #include "kmb_sync.cuh"
@@ -56,11 +58,19 @@ struct StripDesc {
 
 template <int MT, bool ROPE>
 struct StripGeom {
-    static constexpr int CPT = ROPE ? 2 : 1;              // channels per thread
+    // Each thread carries CPT = 2 channels (the RoPE pair, or two independent
+    // channels) and, for M = 64, SPT = 2 states (m and m + 32), so one warp
+    // covers a strip and the per-row and per-point work (waits, handoff, TMA
+    // issue, x / delta / lambda, coefficients) serves up to four independent
+    // state chains, which also gives the scheduler four-way ILP per lane.
+    static constexpr int CPT = 2;                         // channels per thread
+    static constexpr int SPT = MT == 64 ? 2 : 1;          // states per thread
+    static constexpr int U = CPT * SPT;                   // (channel, state) units per thread
     static constexpr int SPW = MT >= 32 ? 1 : 32 / MT;    // channel sets per warp
-    static constexpr int HW = MT >= 32 ? MT / 32 : 1;     // warps per strip
+    static constexpr int HW = MT >= 32 ? MT / (32 * SPT) : 1;  // warps per strip
     static constexpr int CH = SPW * CPT;                  // channels per tile
     static constexpr int GS = MT >= 32 ? 32 : MT;         // lanes summed for y
+    static constexpr int MAXT = 8 * HW * 32;              // threads of the largest CTA (8 strips)
 };
 
 // Transposed butterfly: v[NV] per lane -> lane holds the sum over its GS-lane
@@ -120,14 +130,14 @@ struct StripLayout {
 };
 
 template <int MT, bool ROPE, bool LAMB, bool KIN0, bool FULL>
-__global__ void __launch_bounds__(512, 1)
+__global__ void __launch_bounds__(StripGeom<MT, ROPE>::MAXT, 1)
 scan_fwd_strips(const __grid_constant__ StripDesc f,
                 const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mC,
                 const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mD,
                 const __grid_constant__ CUtensorMap mL) {
     using Gm = StripGeom<MT, ROPE>;
     using Ly = StripLayout<MT, ROPE>;
-    constexpr int CPT = Gm::CPT, HW = Gm::HW, CH = Gm::CH, GS = Gm::GS;
+    constexpr int CPT = Gm::CPT, HW = Gm::HW, CH = Gm::CH, GS = Gm::GS, U = Gm::U;
     constexpr int WC = SW_WC;
     constexpr int ST = Ly::bytes;
     extern __shared__ __align__(1024) unsigned char smem[];
@@ -139,9 +149,9 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     const float deflam = f.deflam;
     const float omlq = __fmul_rn(__fsub_rn(1.0f, deflam), 0.25f);  // (1 - lambda) / 4 when lambda is constant
     const int red_y = f.red_y;
-    // smem map: stages [S][NSS] | handoff values [S][HW][K][2][32*CPT] | barriers
+    // smem map: stages [S][NSS] | handoff values [S][HW][K][2][32*U] | barriers
     unsigned char* stages = smem;
-    const int hv = 32 * CPT;
+    const int hv = 32 * U;
     float* hand = (float*)(smem + (size_t)S * NSS * ST);
     uint64_t* bars = (uint64_t*)(hand + (size_t)S * HW * SW_K * 2 * hv);
     uint64_t* b_full = bars;                          // [S][NSS]
@@ -230,7 +240,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
 
     float* my_hand_in = hand + ((size_t)(w * HW + hh) * SW_K) * 2 * hv;           // written by strip w-1
     float* my_hand_out = hand + ((size_t)((w + 1) * HW + hh) * SW_K) * 2 * hv;    // read by strip w+1
-    const int hl = lane * CPT;
+    const int hl = lane * U;
     // per-thread offsets inside a stage
     const int bofs = (cl0 * MT + m) * 4;                 // B / C box: [j][CH][MT]
     const int xofs = cl0;                                // x / delta box column (+ (d0 & 3))
@@ -253,13 +263,13 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int b = (int)(tile / ntd);
         const int d0 = (int)(tile - (long long)b * ntd) * CH;
-        float AI[CPT], AO[CPT], cth = 1.0f, sth = 0.0f;
+        float AI[U], AO[U], cth = 1.0f, sth = 0.0f;
 #pragma unroll
-        for (int c = 0; c < CPT; c++) {
-            const int d = d0 + cl0 + c;
+        for (int u = 0; u < U; u++) {
+            const int d = d0 + cl0 + u % CPT, mu = m + 32 * (u / CPT);
             // A log2 e: alpha = 2^(delta * A log2 e) is one multiply and one ex2 per update
-            AI[c] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + m], f.clamp, f.amin), kKmbLog2e);
-            AO[c] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + m], f.clamp, f.amin), kKmbLog2e);
+            AI[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + mu], f.clamp, f.amin), kKmbLog2e);
+            AO[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + mu], f.clamp, f.amin), kKmbLog2e);
         }
         if (ROPE) {
             const float th = f.theta[(d0 + cl0) >> 1];
@@ -270,7 +280,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
         float* hrow = f.h + (long long)b * P * DM + (long long)(d0 + cl0) * MT + m + (long long)q0 * hq;
         float* yrow = f.y + (long long)b * P * D + d0 + y_col;
         const int xo = (d0 & 3) + xofs;
-        float ring_h[WC][CPT], ring_b[WC][CPT];
+        float ring_h[WC][U], ring_b[WC][U];
 
         // one row of this strip; HASO: the row above exists (o > 0)
         auto do_row = [&](auto hasO_c, int o) -> bool {
@@ -295,7 +305,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             const float* Ls = (const float*)(st + Ly::offL) + (KIN0 ? (o & 3) : 0);
             const int hs = row & (SW_K - 1);
             const uint32_t hph = (uint32_t)((row / SW_K) & 1);
-            float lh[CPT], lb[CPT];
+            float lh[U], lb[U];
             if (w > 0) {
                 if (!mbar_wait(smem_u32(&b_hfull[(w * HW + hh) * SW_K + hs]), hph)) {
                     set_status(f.status, KMB_ERR_TIMEOUT_Y);
@@ -304,52 +314,53 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                 }
                 const float* src = my_hand_in + (size_t)hs * 2 * hv;
 #pragma unroll
-                for (int c = 0; c < CPT; c++) {
-                    lh[c] = src[hl + c];
-                    lb[c] = src[hv + hl + c];
+                for (int u = 0; u < U; u++) {
+                    lh[u] = src[hl + u];
+                    lb[u] = src[hv + hl + u];
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&b_hempty[(w * HW + hh) * SW_K + hs]));
             }
             float prod[WC][CPT];
-            float lastH[CPT], lastB[CPT];
+            float lastH[U], lastB[U];
             float* hp = hrow;
 #pragma unroll
             for (int j = 0; j < WC; j++) {
                 const float lam = LAMB ? Ls[j * (KIN0 ? 4 : 1)] : deflam;
-                float hn[CPT];
+                float hn[U];
 #pragma unroll
-                for (int c = 0; c < CPT; c++) {
+                for (int u = 0; u < U; u++) {
+                    const int c = u % CPT, sofs = 32 * (u / CPT);  // channel, state offset
                     const float x = Xs[j * 4 + c];
                     const float dI = DsI[j * 4 + c];
                     const float dO = DsO[j * 4 + c];
-                    const float Bv = Bs[j * CH * MT + c * MT];
+                    const float Bv = Bs[j * CH * MT + c * MT + sofs];
                     const float dt = __fadd_rn(dI, dO);
                     const float bu = __fmul_rn(Bv, x);
-                    const float aI = kmb_ex2(__fmul_rn(dI, AI[c]));
+                    const float aI = kmb_ex2(__fmul_rn(dI, AI[u]));
                     float buacc, dacc, hacc, inv;
                     // inner predecessor: the previous column (strip w-1's last column when j == 0)
-                    const float hatI = (j == 0) ? lh[c] : ring_h[j == 0 ? 0 : j - 1][c];
-                    const float buI = (j == 0) ? lb[c] : ring_b[j == 0 ? 0 : j - 1][c];
+                    const float hatI = (j == 0) ? lh[u] : ring_h[j == 0 ? 0 : j - 1][u];
+                    const float buI = (j == 0) ? lb[u] : ring_b[j == 0 ? 0 : j - 1][u];
                     if (HASO) {
-                        const float aO = kmb_ex2(__fmul_rn(dO, AO[c]));
+                        const float aO = kmb_ex2(__fmul_rn(dO, AO[u]));
                         if (j > 0 || w > 0) {
                             // two predecessors: mean of two = sum * 0.5 (exact), so the
                             // coefficient (1-lam) dt (dacc/2) (buacc/2) is ((1-lam) dt / 4) (dacc buacc);
                             // h = (A-part + that) + gamma bu, as two fused multiply-adds
-                            buacc = __fadd_rn(buI, ring_b[j][c]);
+                            buacc = __fadd_rn(buI, ring_b[j][u]);
                             dacc = __fadd_rn(aI, aO);
-                            hacc = KIN0 ? __fmaf_rn(aO, ring_h[j][c], __fmul_rn(aI, hatI))
-                                        : __fmaf_rn(aI, hatI, __fmul_rn(aO, ring_h[j][c]));
+                            hacc = KIN0 ? __fmaf_rn(aO, ring_h[j][u], __fmul_rn(aI, hatI))
+                                        : __fmaf_rn(aI, hatI, __fmul_rn(aO, ring_h[j][u]));
                             const float omdtq = LAMB ? __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), 0.25f)
                                                      : __fmul_rn(omlq, dt);
                             const float gamma2 = __fmul_rn(lam, dt);
-                            hn[c] = __fmaf_rn(gamma2, bu, __fmaf_rn(omdtq, __fmul_rn(dacc, buacc), hacc));
+                            hn[u] = __fmaf_rn(gamma2, bu, __fmaf_rn(omdtq, __fmul_rn(dacc, buacc), hacc));
                             goto have_h;
                         } else {
-                            buacc = ring_b[j][c];
+                            buacc = ring_b[j][u];
                             dacc = aO;
-                            hacc = __fmul_rn(aO, ring_h[j][c]);
+                            hacc = __fmul_rn(aO, ring_h[j][u]);
                             inv = 1.0f;
                         }
                     } else {
@@ -368,24 +379,31 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     {
                         const float beta = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), __fmul_rn(dacc, inv));
                         const float gamma = __fmul_rn(lam, dt);
-                        hn[c] = __fadd_rn(__fmaf_rn(bu, gamma, __fmul_rn(__fmul_rn(buacc, inv), beta)), hacc);
+                        hn[u] = __fadd_rn(__fmaf_rn(bu, gamma, __fmul_rn(__fmul_rn(buacc, inv), beta)), hacc);
                     }
                 have_h:
-                    ring_b[j][c] = bu;
-                    if (j < ncol) __stcs(hp + (long long)c * MT, hn[c]);
-                    prod[j][c] = __fmul_rn(Cs[j * CH * MT + c * MT], hn[c]);
+                    ring_b[j][u] = bu;
+                    if (j < ncol) __stcs(hp + (long long)c * MT + sofs, hn[u]);
+                    const float cy = __fmul_rn(Cs[j * CH * MT + c * MT + sofs], hn[u]);
+                    prod[j][c] = sofs == 0 ? cy : __fadd_rn(prod[j][c], cy);
                 }
                 if (ROPE) {
-                    ring_h[j][0] = __fmaf_rn(cth, hn[0], -__fmul_rn(sth, hn[1]));
-                    ring_h[j][1] = __fmaf_rn(sth, hn[0], __fmul_rn(cth, hn[1]));
+                    // the pair (2i, 2i+1) of state slot s is units (s CPT, s CPT + 1)
+#pragma unroll
+                    for (int s = 0; s < Gm::SPT; s++) {
+                        const float h0 = hn[s * CPT], h1 = hn[s * CPT + 1];
+                        ring_h[j][s * CPT] = __fmaf_rn(cth, h0, -__fmul_rn(sth, h1));
+                        ring_h[j][s * CPT + 1] = __fmaf_rn(sth, h0, __fmul_rn(cth, h1));
+                    }
                 } else {
-                    ring_h[j][0] = hn[0];
+#pragma unroll
+                    for (int u = 0; u < U; u++) ring_h[j][u] = hn[u];
                 }
                 if (j == 0 || j < ncol) {
 #pragma unroll
-                    for (int c = 0; c < CPT; c++) {
-                        lastH[c] = ring_h[j][c];
-                        lastB[c] = ring_b[j][c];
+                    for (int u = 0; u < U; u++) {
+                        lastH[u] = ring_h[j][u];
+                        lastB[u] = ring_b[j][u];
                     }
                 }
                 hp += hq;
@@ -400,9 +418,9 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                 }
                 float* dst = my_hand_out + (size_t)hs * 2 * hv;
 #pragma unroll
-                for (int c = 0; c < CPT; c++) {
-                    dst[hl + c] = lastH[c];
-                    dst[hv + hl + c] = lastB[c];
+                for (int u = 0; u < U; u++) {
+                    dst[hl + u] = lastH[u];
+                    dst[hv + hl + u] = lastB[u];
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&b_hfull[((w + 1) * HW + hh) * SW_K + hs]));
@@ -472,7 +490,7 @@ static cudaError_t strips_flags(const ScanDesc& s, const StripDesc& f, const CUt
 template <int MT, bool ROPE>
 static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st) {
     using Gm = StripGeom<MT, ROPE>;
-    const int CH = Gm::CH, HW = Gm::HW, CPT = Gm::CPT;
+    const int CH = Gm::CH, HW = Gm::HW;
     const int D = s.D;
     if (D % CH != 0) return cudaErrorNotSupported;
     const long long H = s.dims[0], W = s.dims[1];
@@ -537,7 +555,7 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
         maps[4] = maps[2];
     }
     const int threads = f.S * HW * 32;
-    const int hv = 32 * CPT;
+    const int hv = 32 * Gm::U;
     const int fixed = f.S * HW * SW_K * 2 * hv * 4 + (2 * f.S * SW_NSS_MAX + 2 * f.S * HW * SW_K) * 8;
     f.nss = SW_NSS_MAX;
     while (f.nss > 2 && fixed + f.S * f.nss * f.st_bytes > 227 * 1024) f.nss--;
