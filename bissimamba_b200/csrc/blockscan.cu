@@ -25,6 +25,7 @@ __device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat16
 
 struct BSDesc {
     int nd, N, R, P2, fast, bf16;
+    int GP, NG;             // pairs per group, groups (CTAs per item)
     float deflam;
     long long L, batch;
     int dims[BS_MAXND], strides[BS_MAXND];
@@ -34,6 +35,7 @@ struct BSDesc {
     const void *u, *dt, *lam, *B, *C;  // float, or __nv_bfloat16 when bf16
     const float *A, *theta;
     float *h, *Bu, *y;
+    float* part;            // NG > 1: per-group partials of y [NG][batch][L][R]
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -46,18 +48,53 @@ __device__ __forceinline__ void bs_unravel(const BSDesc& s, int t, int* idx) {
     for (int k = 0; k < s.nd; k++) idx[k] = (t / s.strides[k]) % s.dims[k];
 }
 
-template <typename T>
+// Lane geometry shared by the forward and the backward.  The state pairs are
+// split into NG groups of GP pairs; CTA (item b, group g) owns group g of item
+// b, and a warp works on PPW = 32 / GP points of a level at once: lane =
+// (point slot ps, pair pl).  Sums over the states of a point are shuffles
+// inside the GP-lane group; with NG > 1 each group writes its partial of
+// every such sum to scratch and bs_group_reduce adds the NG partials in group
+// order (deterministic).
+template <int GP>
+struct BSLanes {
+    static constexpr int PPW = 32 / GP;
+    int b, g, ps, pl, n0, n1;
+    bool h0ok, h1ok, pair;
+    __device__ BSLanes(const BSDesc& s) {
+        b = blockIdx.x / s.NG;
+        g = blockIdx.x - b * s.NG;
+        const int lane = threadIdx.x & 31;
+        ps = lane / GP;
+        pl = lane % GP;
+        const int p = g * GP + pl;
+        n0 = 2 * p;
+        n1 = 2 * p + 1;
+        h0ok = n0 < s.N;
+        h1ok = n1 < s.N;
+        pair = h1ok;
+    }
+};
+
+template <int GP>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int o = GP / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <typename T, int GP>
 __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
-    const int b = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    using Ln = BSLanes<GP>;
+    const Ln ln(s);
+    const int b = ln.b, n0 = ln.n0, n1 = ln.n1;
+    const bool h0ok = ln.h0ok, h1ok = ln.h1ok, pair = ln.pair;
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int N = s.N, R = s.R, NR = N * R;
-    const int n0 = 2 * lane, n1 = 2 * lane + 1;
-    const bool h0ok = n0 < N, h1ok = n1 < N, pair = h1ok;
     const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (pair) {
-        cth = cosf(s.theta[lane]);
-        sth = sinf(s.theta[lane]);
+        cth = cosf(s.theta[n0 >> 1]);
+        sth = sinf(s.theta[n0 >> 1]);
     }
     const long long L = s.L;
     const T* u = (const T*)s.u + b * L * R;
@@ -67,11 +104,15 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
     const T* Cp = (const T*)s.C + b * L * NR;
     float* h = s.h + b * L * N;
     float* Bu = s.Bu + b * L * N;
-    float* y = s.y + b * L * R;
+    // y, or this group's partial of y
+    float* y = (s.NG == 1 ? s.y : s.part + (long long)ln.g * s.batch * L * R) + b * L * R;
     for (int lev = 0; lev < s.nlev; lev++) {
         const int beg = s.lev_start[lev], end = s.lev_start[lev + 1];
-        for (int i = beg + warp; i < end; i += nw) {
-            const int t = s.lev_pts[i];
+        // warp-uniform trip count: the group shuffles need the whole warp
+        for (int base = beg + warp * Ln::PPW; base < end; base += nw * Ln::PPW) {
+            const bool act = base + ln.ps < end;
+            const int t = s.lev_pts[act ? base + ln.ps : base];
+            const bool w0 = act && h0ok, w1 = act && h1ok;
             const float dt = ldv(dtp + t);
             const float lam = lamp ? ldv(lamp + t) : s.deflam;
             float bu0 = 0.0f, bu1 = 0.0f;
@@ -106,9 +147,9 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                     hn0 = __fmaf_rn(bs * al0, bacc0, hn0);
                     hn1 = __fmaf_rn(bs * al1, bacc1, hn1);
                 }
-                const float g = lam * dt;
-                hn0 = __fmaf_rn(g, bu0, hn0);
-                hn1 = __fmaf_rn(g, bu1, hn1);
+                const float gm = lam * dt;
+                hn0 = __fmaf_rn(gm, bu0, hn0);
+                hn1 = __fmaf_rn(gm, bu1, hn1);
             } else {
                 // 1D recurrence (reference src/mamba_block.c:384-393)
                 float p0 = 0.0f, p1 = 0.0f, pb0 = 0.0f, pb1 = 0.0f;
@@ -120,19 +161,19 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                 const float r0 = pair ? cth * p0 - sth * p1 : p0;
                 const float r1 = sth * p0 + cth * p1;
                 const float beta0 = (1.0f - lam) * dt * al0, beta1 = (1.0f - lam) * dt * al1;
-                const float g = lam * dt;
-                hn0 = __fmaf_rn(g, bu0, __fmaf_rn(beta0, pb0, al0 * r0));
-                hn1 = __fmaf_rn(g, bu1, __fmaf_rn(beta1, pb1, al1 * r1));
+                const float gm = lam * dt;
+                hn0 = __fmaf_rn(gm, bu0, __fmaf_rn(beta0, pb0, al0 * r0));
+                hn1 = __fmaf_rn(gm, bu1, __fmaf_rn(beta1, pb1, al1 * r1));
             }
             const long long o = (long long)t * N;
-            if (h0ok) { h[o + n0] = hn0; Bu[o + n0] = bu0; }
-            if (h1ok) { h[o + n1] = hn1; Bu[o + n1] = bu1; }
+            if (w0) { h[o + n0] = hn0; Bu[o + n0] = bu0; }
+            if (w1) { h[o + n1] = hn1; Bu[o + n1] = bu1; }
             for (int r = 0; r < R; r++) {
                 float part = 0.0f;
                 if (h0ok) part = ldv(Cp + (long long)t * NR + r * N + n0) * hn0;
                 if (h1ok) part = __fmaf_rn(ldv(Cp + (long long)t * NR + r * N + n1), hn1, part);
-                part = warp_sum(part);
-                if (lane == 0) y[(long long)t * R + r] = part;
+                part = group_sum<GP>(part);
+                if (act && ln.pl == 0) y[(long long)t * R + r] = part;
             }
         }
         __syncthreads();
@@ -145,20 +186,23 @@ struct BSGrad {
     float* G;     // scratch [batch, L, N]
     float* pA;    // scratch [batch, N]
     float* pth;   // scratch [batch, 32]
+    // NG > 1: per-group partials [NG][batch][L][R] and [NG][batch][L] (x2)
+    float *pdu, *pddt, *pdlam;
 };
 
-template <typename T>
+template <typename T, int GP>
 __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) {
-    const int b = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    using Ln = BSLanes<GP>;
+    const Ln ln(s);
+    const int b = ln.b, n0 = ln.n0, n1 = ln.n1;
+    const bool h0ok = ln.h0ok, h1ok = ln.h1ok, pair = ln.pair;
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int N = s.N, R = s.R, NR = N * R, nd = s.nd < 1 ? 1 : s.nd;
-    const int n0 = 2 * lane, n1 = 2 * lane + 1;
-    const bool h0ok = n0 < N, h1ok = n1 < N, pair = h1ok;
     const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (pair) {
-        cth = cosf(s.theta[lane]);
-        sth = sinf(s.theta[lane]);
+        cth = cosf(s.theta[n0 >> 1]);
+        sth = sinf(s.theta[n0 >> 1]);
     }
     const long long L = s.L;
     const T* u = (const T*)s.u + b * L * R;
@@ -170,6 +214,12 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
     const float* Bu = s.Bu + b * L * N;
     const float* dy = g.dy + b * L * R;
     float* G = g.G + b * L * N;
+    // du / ddt / dlambda: accumulate in place (one group), or this group's partials
+    const bool direct = s.NG == 1;
+    const long long gofs = (long long)ln.g * s.batch;
+    float* du = direct ? g.du + b * L * R : g.pdu + (gofs + b) * L * R;
+    float* ddt = direct ? (g.ddt ? g.ddt + b * L : nullptr) : g.pddt + (gofs + b) * L;
+    float* dlam = direct ? (g.dlam ? g.dlam + b * L : nullptr) : g.pdlam + (gofs + b) * L;
     float gA0 = 0.0f, gA1 = 0.0f, gth = 0.0f;
     int dims[BS_MAXND], strides[BS_MAXND];
     if (s.nd >= 1) {
@@ -180,8 +230,11 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
     }
     for (int lev = s.nlev - 1; lev >= 0; lev--) {
         const int beg = s.lev_start[lev], end = s.lev_start[lev + 1];
-        for (int i = beg + warp; i < end; i += nw) {
-            const int t = s.lev_pts[i];
+        for (int base = beg + warp * Ln::PPW; base < end; base += nw * Ln::PPW) {
+            const bool act = base + ln.ps < end;
+            const int t = s.lev_pts[act ? base + ln.ps : base];
+            // inactive point slots compute on a duplicate point and store nothing
+            const bool x0 = act && h0ok, x1 = act && h1ok;
             int idx[BS_MAXND];
             int npt = 0;
             for (int k = 0; k < nd; k++) {
@@ -211,7 +264,7 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
             float gh1 = -sth * a0 + cth * a1;
             const long long o = (long long)t * N;
             const float ht0 = h0ok ? h[o + n0] : 0.0f, ht1 = h1ok ? h[o + n1] : 0.0f;
-            if (pair) {
+            if (pair && act) {
                 const float hat0 = cth * ht0 - sth * ht1, hat1 = sth * ht0 + cth * ht1;
                 gth += -a0 * hat1 + a1 * hat0;
             }
@@ -220,15 +273,15 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 const long long c0 = (long long)t * NR + r * N;
                 if (h0ok) {
                     gh0 += ldv(Cp + c0 + n0) * dyr;
-                    g.dC[b * L * NR + c0 + n0] += dyr * ht0;
+                    if (act) g.dC[b * L * NR + c0 + n0] += dyr * ht0;
                 }
                 if (h1ok) {
                     gh1 += ldv(Cp + c0 + n1) * dyr;
-                    g.dC[b * L * NR + c0 + n1] += dyr * ht1;
+                    if (act) g.dC[b * L * NR + c0 + n1] += dyr * ht1;
                 }
             }
-            if (h0ok) G[o + n0] = gh0;
-            if (h1ok) G[o + n1] = gh1;
+            if (x0) G[o + n0] = gh0;
+            if (x1) G[o + n1] = gh1;
             const float bu0 = h0ok ? Bu[o + n0] : 0.0f, bu1 = h1ok ? Bu[o + n1] : 0.0f;
             const float gam = lam * dt;
             const float gbu0 = gam * gh0 + ab0, gbu1 = gam * gh1 + ab1;
@@ -237,15 +290,18 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 const long long c0 = (long long)t * NR + r * N;
                 float part = 0.0f;
                 if (h0ok) {
-                    g.dB[b * L * NR + c0 + n0] += gbu0 * ur;
+                    if (act) g.dB[b * L * NR + c0 + n0] += gbu0 * ur;
                     part += gbu0 * ldv(Bp + c0 + n0);
                 }
                 if (h1ok) {
-                    g.dB[b * L * NR + c0 + n1] += gbu1 * ur;
+                    if (act) g.dB[b * L * NR + c0 + n1] += gbu1 * ur;
                     part += gbu1 * ldv(Bp + c0 + n1);
                 }
-                part = warp_sum(part);
-                if (lane == 0) g.du[b * L * R + (long long)t * R + r] += part;
+                part = group_sum<GP>(part);
+                if (act && ln.pl == 0) {
+                    if (direct) du[(long long)t * R + r] += part;
+                    else du[(long long)t * R + r] = part;
+                }
             }
             float gdt = lam * (bu0 * gh0 + bu1 * gh1);
             float glam = dt * (bu0 * gh0 + bu1 * gh1);
@@ -268,39 +324,60 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 const float dz0 = h0ok ? kmb_dexp(z0, al0, s.fast) * dal0 : 0.0f;
                 const float dz1 = h1ok ? kmb_dexp(z1, al1, s.fast) * dal1 : 0.0f;
                 gdt += dz0 * A0 + dz1 * A1;
-                gA0 += dz0 * dt;
-                gA1 += dz1 * dt;
+                if (act) {
+                    gA0 += dz0 * dt;
+                    gA1 += dz1 * dt;
+                }
                 const float ds = al0 * sb0 * gh0 + al1 * sb1 * gh1;
                 gdt += (1.0f - lam) * inv * ds;
                 glam -= dt * inv * ds;
             }
-            gdt = warp_sum(gdt);
-            glam = warp_sum(glam);
-            if (lane == 0) {
-                if (g.ddt) g.ddt[b * L + t] += gdt;
-                if (g.dlam) g.dlam[b * L + t] += glam;
+            gdt = group_sum<GP>(gdt);
+            glam = group_sum<GP>(glam);
+            if (act && ln.pl == 0) {
+                if (direct) {
+                    if (ddt) ddt[t] += gdt;
+                    if (dlam) dlam[t] += glam;
+                } else {
+                    ddt[t] = gdt;
+                    dlam[t] = glam;
+                }
             }
         }
         __syncthreads();
     }
-    // per-item partials: sum the warps' accumulators in a fixed order
-    __shared__ float sA[16][64];
-    __shared__ float sT[16][32];
-    sA[warp][n0 & 63] = gA0;
-    sA[warp][n1 & 63] = gA1;
-    sT[warp][lane] = gth;
+    // per-(item, group) partials of dA and dtheta: sum the warps' and point
+    // slots' accumulators in a fixed order
+    __shared__ float sA[16 * 32][2];
+    __shared__ float sT[16 * 32];
+    const int tid = threadIdx.x;
+    sA[tid][0] = gA0;
+    sA[tid][1] = gA1;
+    sT[tid] = gth;
     __syncthreads();
-    if (warp == 0) {
+    if (tid < GP) {
         float t0 = 0.0f, t1 = 0.0f, tt = 0.0f;
-        for (int w = 0; w < nw; w++) {
-            t0 += sA[w][n0 & 63];
-            t1 += sA[w][n1 & 63];
-            tt += sT[w][lane];
+        for (int j = 0; j < nw * Ln::PPW; j++) {
+            const int src = (j / Ln::PPW) * 32 + (j % Ln::PPW) * GP + tid;  // (warp, point slot, pair tid)
+            t0 += sA[src][0];
+            t1 += sA[src][1];
+            tt += sT[src];
         }
-        if (h0ok) g.pA[(long long)b * N + n0] = t0;
-        if (h1ok) g.pA[(long long)b * N + n1] = t1;
-        g.pth[(long long)b * 32 + lane] = tt;
+        const int p = ln.g * GP + tid;
+        if (2 * p < N) g.pA[(long long)b * N + 2 * p] = t0;
+        if (2 * p + 1 < N) g.pA[(long long)b * N + 2 * p + 1] = t1;
+        if (p < 32) g.pth[(long long)b * 32 + p] = tt;
     }
+}
+
+// out[i] (+)= sum_g part[g * n + i], g = 0 .. NG-1 in order
+__global__ void bs_group_reduce(const float* __restrict__ part, float* __restrict__ out, long long n, int ng,
+                                int accumulate) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float acc = 0.0f;
+    for (int j = 0; j < ng; j++) acc += part[(long long)j * n + i];
+    out[i] = accumulate ? out[i] + acc : acc;
 }
 
 // out[i] += sum_j part[j*stride + i]
@@ -325,7 +402,7 @@ namespace kmb {
 void* workspace(int slot, size_t bytes);
 int set_error(const char* msg);
 int set_cuda_error(const char* where, cudaError_t e);
-enum { WS_BS_SCRATCH = 4 };
+enum { WS_BS_FWD = 3, WS_BS_SCRATCH = 4 };
 
 // Device copy of the wavefront plan of `dims` (level starts [nlev + 1], then the
 // points of every level [L]), cached per host thread, device and shape.
@@ -392,6 +469,9 @@ static int bs_desc(const KMBlockScanParams* p, long batch, BSDesc* s, cudaStream
     s->N = (int)p->N;
     s->R = (int)p->R;
     s->P2 = (s->N + 1) / 2;
+    s->GP = 1;
+    while (s->GP < 8 && s->GP < s->P2) s->GP *= 2;
+    s->NG = (s->P2 + s->GP - 1) / s->GP;
     s->fast = p->use_fast_exp != 0;
     s->deflam = p->default_lambda;
     s->L = p->L;
@@ -421,6 +501,36 @@ static int bs_threads(const BSDesc& s) {
     return 512;
 }
 
+template <typename T, int GP>
+static void bs_fwd_launch(const BSDesc& s, cudaStream_t st) {
+    blockscan_fwd_kernel<T, GP><<<(unsigned)(s.batch * s.NG), bs_threads(s), 0, st>>>(s);
+}
+template <typename T, int GP>
+static void bs_bwd_launch(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
+    blockscan_bwd_kernel<T, GP><<<(unsigned)(s.batch * s.NG), bs_threads(s), 0, st>>>(s, g);
+}
+template <typename T>
+static void bs_fwd_dispatch(const BSDesc& s, cudaStream_t st) {
+    switch (s.GP) {
+        case 1: bs_fwd_launch<T, 1>(s, st); break;
+        case 2: bs_fwd_launch<T, 2>(s, st); break;
+        case 4: bs_fwd_launch<T, 4>(s, st); break;
+        default: bs_fwd_launch<T, 8>(s, st); break;
+    }
+}
+template <typename T>
+static void bs_bwd_dispatch(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
+    switch (s.GP) {
+        case 1: bs_bwd_launch<T, 1>(s, g, st); break;
+        case 2: bs_bwd_launch<T, 2>(s, g, st); break;
+        case 4: bs_bwd_launch<T, 4>(s, g, st); break;
+        default: bs_bwd_launch<T, 8>(s, g, st); break;
+    }
+}
+static void group_reduce(const float* part, float* out, long long n, int ng, int accumulate, cudaStream_t st) {
+    bs_group_reduce<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, out, n, ng, accumulate);
+}
+
 }  // namespace kmb
 
 using namespace kmb;
@@ -429,8 +539,14 @@ extern "C" int kmb_blockscan_forward(const KMBlockScanParams* p, long batch, voi
     cudaStream_t st = (cudaStream_t)stream;
     BSDesc s;
     if (bs_desc(p, batch, &s, st)) return -1;
-    if (s.bf16) blockscan_fwd_kernel<__nv_bfloat16><<<(unsigned)batch, bs_threads(s), 0, st>>>(s);
-    else blockscan_fwd_kernel<float><<<(unsigned)batch, bs_threads(s), 0, st>>>(s);
+    const long long ny = (long long)batch * s.L * s.R;
+    if (s.NG > 1) {
+        s.part = (float*)workspace(WS_BS_FWD, (size_t)s.NG * ny * sizeof(float));
+        if (!s.part) return set_error("workspace allocation failed");
+    }
+    if (s.bf16) bs_fwd_dispatch<__nv_bfloat16>(s, st);
+    else bs_fwd_dispatch<float>(s, st);
+    if (s.NG > 1) group_reduce(s.part, s.y, ny, s.NG, 0, st);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("blockscan_fwd", e);
 }
@@ -442,7 +558,9 @@ extern "C" int kmb_blockscan_backward(const KMBlockScanParams* p, long batch, co
     BSDesc s;
     if (bs_desc(p, batch, &s, st)) return -1;
     const size_t nG = (size_t)batch * s.L * s.N;
-    const size_t bytes = (nG + (size_t)batch * s.N + (size_t)batch * 32) * sizeof(float) + 512;
+    const size_t ny = (size_t)batch * s.L * s.R, nl = (size_t)batch * s.L;
+    const size_t npart = s.NG > 1 ? (size_t)s.NG * (ny + 2 * nl) : 0;
+    const size_t bytes = (nG + (size_t)batch * s.N + (size_t)batch * 32 + npart) * sizeof(float) + 512;
     char* w = (char*)workspace(WS_BS_SCRATCH, bytes);
     if (!w) return set_error("workspace allocation failed");
     BSGrad g;
@@ -451,10 +569,18 @@ extern "C" int kmb_blockscan_backward(const KMBlockScanParams* p, long batch, co
     g.G = (float*)w;
     g.pA = g.G + nG;
     g.pth = g.pA + (size_t)batch * s.N;
-    if (s.bf16) blockscan_bwd_kernel<__nv_bfloat16><<<(unsigned)batch, bs_threads(s), 0, st>>>(s, g);
-    else blockscan_bwd_kernel<float><<<(unsigned)batch, bs_threads(s), 0, st>>>(s, g);
+    g.pdu = g.pth + (size_t)batch * 32;
+    g.pddt = g.pdu + (size_t)s.NG * ny;
+    g.pdlam = g.pddt + (size_t)s.NG * nl;
+    if (s.bf16) bs_bwd_dispatch<__nv_bfloat16>(s, g, st);
+    else bs_bwd_dispatch<float>(s, g, st);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("blockscan_bwd", e);
+    if (s.NG > 1) {
+        group_reduce(g.pdu, gr->du, (long long)ny, s.NG, 1, st);
+        if (gr->ddt) group_reduce(g.pddt, gr->ddt, (long long)nl, s.NG, 1, st);
+        if (gr->dlambda) group_reduce(g.pdlam, gr->dlambda, (long long)nl, s.NG, 1, st);
+    }
     if (gr->dA_log) bs_reduce_add<<<1, 64, 0, st>>>(g.pA, gr->dA_log, s.N, batch, s.N);
     if (gr->dtheta && s.N >= 2) bs_reduce_add<<<1, 32, 0, st>>>(g.pth, gr->dtheta, s.N / 2, batch, 32);
     e = cudaGetLastError();
