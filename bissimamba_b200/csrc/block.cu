@@ -66,7 +66,8 @@ __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, in
     const long long Rt = R + 2 + 2LL * NR;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= BL * Rt) return;
-    const long long row = i / Rt;
+    // 32-bit division when the index fits (the common case), 64-bit otherwise
+    const long long row = BL * Rt <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)Rt) : i / Rt;
     const int col = (int)(i - row * Rt);
     const float v = P[i];
     if (col < R) {
@@ -87,17 +88,19 @@ __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, in
     }
 }
 
-// Backward epilogue: dP[BL, Rt] from the scan gradients
-template <typename T>
+// Backward epilogue: dP[BL, Rt] from the scan gradients (O = float, or bf16
+// as the operand of the bf16 tensor-core gradient GEMMs)
+template <typename T, typename O>
 __global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restrict__ dtv,
                                    const T* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
                                    float dt_max, const float* __restrict__ du, const float* __restrict__ ddt,
                                    const float* __restrict__ dlam, const float* __restrict__ dB,
-                                   const float* __restrict__ dC, float* __restrict__ dP) {
+                                   const float* __restrict__ dC, O* __restrict__ dP) {
     const long long Rt = R + 2 + 2LL * NR;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= BL * Rt) return;
-    const long long row = i / Rt;
+    // 32-bit division when the index fits (the common case), 64-bit otherwise
+    const long long row = BL * Rt <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)Rt) : i / Rt;
     const int col = (int)(i - row * Rt);
     float g;
     if (col < R) {
@@ -116,7 +119,7 @@ __global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restr
     } else {
         g = dC[row * NR + (col - R - 2 - NR)];
     }
-    dP[i] = g;
+    stv(dP + i, g);
 }
 
 // grads += slices of G[Rt, dim]
@@ -140,11 +143,25 @@ __global__ void to_bf16(const float* __restrict__ a, __nv_bfloat16* __restrict__
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) b[i] = __float2bfloat16_rn(a[i]);
 }
-__global__ void to_f32(const __nv_bfloat16* __restrict__ a, float* __restrict__ b, long long n) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) b[i] = __bfloat162float(a[i]);
+// out[row, d] = bf16(x[row, d] + sum_r y[row, r] W_out[d, r])   (bf16 residual stream),
+// 8 channels (16 bytes) per thread; dim % 8 == 0 and 16-byte aligned x / out
+__global__ void block_out_bf16_v8(const uint4* __restrict__ x, const float* __restrict__ y,
+                                  const float* __restrict__ Wout, unsigned rows, unsigned dim8, int R,
+                                  uint4* __restrict__ out) {
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * dim8) return;
+    const unsigned row = i / dim8, d0 = (i - row * dim8) * 8;
+    uint4 xv = x[i];
+    __nv_bfloat16* xe = (__nv_bfloat16*)&xv;
+    const float* yr = y + (size_t)row * R;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float acc = 0.0f;
+        for (int r = 0; r < R; r++) acc = __fmaf_rn(yr[r], Wout[(size_t)(d0 + e) * R + r], acc);
+        xe[e] = __float2bfloat16_rn(__bfloat162float(xe[e]) + acc);
+    }
+    out[i] = xv;
 }
-// out[row, d] = bf16(x[row, d] + sum_r y[row, r] W_out[d, r])   (bf16 residual stream)
 __global__ void block_out_bf16(const __nv_bfloat16* __restrict__ x, const float* __restrict__ y,
                                const float* __restrict__ Wout, long long BL, int dim, int R,
                                __nv_bfloat16* __restrict__ out) {
@@ -259,8 +276,13 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     p.inputs_bf16 = bf;
     if (kmb_blockscan_forward(&p, batch, stream)) return -1;
     if (bf) {
-        block_out_bf16<<<nb(a.BL * dim, 256), 256, 0, st>>>((const __nv_bfloat16*)x, act + a.y, w->W_out, a.BL, dim,
-                                                           (int)c->R, (__nv_bfloat16*)out);
+        if (dim % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0 && a.BL * dim / 8 < (1LL << 31))
+            block_out_bf16_v8<<<nb(a.BL * dim / 8, 256), 256, 0, st>>>((const uint4*)x, act + a.y, w->W_out,
+                                                                      (unsigned)a.BL, (unsigned)(dim / 8), (int)c->R,
+                                                                      (uint4*)out);
+        else
+            block_out_bf16<<<nb(a.BL * dim, 256), 256, 0, st>>>((const __nv_bfloat16*)x, act + a.y, w->W_out, a.BL,
+                                                               dim, (int)c->R, (__nv_bfloat16*)out);
         e = cudaGetLastError();
         return e == cudaSuccess ? 0 : set_cuda_error("bf16 output", e);
     }
@@ -273,8 +295,7 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     return 0;
 }
 
-// fp32 backward body; in bf16 mode x / dout / dx are fp32 copies and the stored
-// scan inputs are read as bf16
+// fp32-storage backward
 static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, const float* x, const float* dout,
                               float* dx, const KMBlockGrads* g, long batch, const float* act, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
@@ -311,17 +332,11 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     p.u = act + a.u; p.dt = act + a.dt; p.lambda = act + a.lam; p.B = act + a.B; p.C = act + a.C;
     p.A_log = w->A_log; p.theta = w->theta; p.default_lambda = c->default_lambda; p.use_fast_exp = c->use_fast_exp;
     p.h = (float*)(act + a.h); p.Bu = (float*)(act + a.Bu); p.y = (float*)(act + a.y);
-    p.inputs_bf16 = c->bf16_storage;
     KMBlockScanGrads sg;
     sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
     if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
-    if (c->bf16_storage)
-        block_bwd_epilogue<__nv_bfloat16><<<nb(BL * Rt, 256), 256, 0, st>>>(
-            act + a.proj, (const __nv_bfloat16*)(act + a.dt), (const __nv_bfloat16*)(act + a.lam), BL, R, (int)NR,
-            c->dt_min, c->dt_max, S + s_du, S + s_ddt, S + s_dlam, S + s_dB, S + s_dC, S + s_dP);
-    else
-        block_bwd_epilogue<float><<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
+    block_bwd_epilogue<float, float><<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
                                                                     (int)NR, c->dt_min, c->dt_max, S + s_du,
                                                                     S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
                                                                     S + s_dP);
@@ -356,24 +371,109 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     return 0;
 }
 
+// dx = bf16(dout + D)   (bf16 residual stream; dx may alias dout)
+__global__ void residual_bf16(const __nv_bfloat16* dout, const float* __restrict__ D, __nv_bfloat16* dx, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dx[i] = __float2bfloat16_rn(__bfloat162float(dout[i]) + D[i]);
+}
+
+static cublasStatus_t gemm_bf16(cublasHandle_t hb, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                                const void* A, int lda, const void* B, int ldb, float beta, float* C, int ldc) {
+    const float one = 1.0f;
+    return cublasGemmEx(hb, ta, tb, m, n, k, &one, A, CUDA_R_16BF, lda, B, CUDA_R_16BF, ldb, &beta, C, CUDA_R_32F,
+                        ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+// bf16-storage backward: x, dout, dx bf16; the four gradient GEMMs run as
+// bf16 x bf16 -> fp32 on the tensor cores (dP and the small operands y, W_out
+// rounded to bf16), the scan backward and every gradient accumulate in fp32.
+static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, const __nv_bfloat16* x,
+                               const __nv_bfloat16* dout, __nv_bfloat16* dx, const KMBlockGrads* g, long batch,
+                               const float* act, void* stream) {
+    typedef __nv_bfloat16 H;
+    cudaStream_t st = (cudaStream_t)stream;
+    cublasHandle_t hb = cublas_for(st);
+    if (!hb) return set_error("cuBLAS initialisation failed");
+    const ActLayout a = act_layout(c, batch);
+    const int dim = (int)c->dim, R = (int)c->R;
+    const long long BL = a.BL, NR = a.NR, Rt = a.Rt;
+    // scratch (floats): dy | du | ddt | dlam | dB | dC | G[Rt,dim] | ones | D[BL,dim] | bf16: dP | y | W_out | Wcat
+    size_t o = 0;
+    auto take = [&](size_t n) { size_t r = o; o += (n + 63) & ~(size_t)63; return r; };
+    const size_t s_dy = take(BL * R), s_du = take(BL * R), s_ddt = take(BL), s_dlam = take(BL);
+    const size_t s_dB = take(BL * NR), s_dC = take(BL * NR), s_G = take(Rt * dim), s_one = take(BL);
+    const size_t s_D = dx ? take(BL * dim) : 0;
+    const size_t s_dP = take((BL * Rt + 1) / 2), s_yb = take((BL * R + 1) / 2), s_wo = take((dim * R + 1) / 2);
+    const size_t s_wb = take((Rt * dim + 1) / 2);
+    float* S = (float*)workspace(WS_BLK_SCRATCH, o * sizeof(float));
+    if (!S) return set_error("workspace allocation failed");
+    H *dPb = (H*)(S + s_dP), *yb = (H*)(S + s_yb), *wob = (H*)(S + s_wo), *Wb = (H*)(S + s_wb);
+    cudaError_t e;
+    to_bf16<<<nb(BL * R, 256), 256, 0, st>>>(act + a.y, yb, BL * R);
+    to_bf16<<<nb((long long)dim * R, 256), 256, 0, st>>>(w->W_out, wob, (long long)dim * R);
+    // d_y[BL,R] = dout . W_out ; gW_out += dout^T . y
+    if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_N, R, (int)BL, dim, wob, R, dout, dim, 0.0f, S + s_dy, R) !=
+        CUBLAS_STATUS_SUCCESS)
+        return set_error("dy GEMM failed");
+    if (g->W_out && gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, R, dim, (int)BL, yb, R, dout, dim, 1.0f, g->W_out, R) !=
+                        CUBLAS_STATUS_SUCCESS)
+        return set_error("dW_out GEMM failed");
+    if ((e = cudaMemsetAsync(S + s_du, 0, (s_G - s_du) * sizeof(float), st)) != cudaSuccess)
+        return set_cuda_error("memset", e);
+    KMBlockScanParams p;
+    memset(&p, 0, sizeof p);
+    p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;
+    p.u = act + a.u; p.dt = act + a.dt; p.lambda = act + a.lam; p.B = act + a.B; p.C = act + a.C;
+    p.A_log = w->A_log; p.theta = w->theta; p.default_lambda = c->default_lambda; p.use_fast_exp = c->use_fast_exp;
+    p.h = (float*)(act + a.h); p.Bu = (float*)(act + a.Bu); p.y = (float*)(act + a.y);
+    p.inputs_bf16 = 1;
+    KMBlockScanGrads sg;
+    sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
+    sg.dA_log = g->A_log; sg.dtheta = g->theta;
+    if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
+    block_bwd_epilogue<H, H><<<nb(BL * Rt, 256), 256, 0, st>>>(
+        act + a.proj, (const H*)(act + a.dt), (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max,
+        S + s_du, S + s_ddt, S + s_dlam, S + s_dB, S + s_dC, dPb);
+    if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
+    // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
+    if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, x, dim, dPb, (int)Rt, 0.0f, S + s_G, dim) !=
+        CUBLAS_STATUS_SUCCESS)
+        return set_error("dWcat GEMM failed");
+    block_scatter_grads<<<nb(Rt * dim, 256), 256, 0, st>>>(S + s_G, R, (int)NR, dim, g->W_in, g->delta_proj,
+                                                           g->lambda_proj, g->W_B, g->W_C);
+    if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("grad scatter", e);
+    const float one = 1.0f;
+    if (g->b_B || g->b_C) {
+        fill_value<<<nb(BL, 256), 256, 0, st>>>(S + s_one, BL, 1.0f);
+        if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("fill", e);
+        if (g->b_B && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dB, (int)NR, S + s_one, 1, &one,
+                                  g->b_B, 1) != CUBLAS_STATUS_SUCCESS)
+            return set_error("db_B GEMV failed");
+        if (g->b_C && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dC, (int)NR, S + s_one, 1, &one,
+                                  g->b_C, 1) != CUBLAS_STATUS_SUCCESS)
+            return set_error("db_C GEMV failed");
+    }
+    if (dx) {
+        float* W = pack_wcat(c, w, st);
+        if (!W) return set_error("kmb_block_backward: weight packing failed");
+        to_bf16<<<nb(Rt * dim, 256), 256, 0, st>>>(W, Wb, Rt * dim);
+        if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, Wb, dim, dPb, (int)Rt, 0.0f, S + s_D,
+                      dim) != CUBLAS_STATUS_SUCCESS)
+            return set_error("dx GEMM failed");
+        residual_bf16<<<nb(BL * dim, 256), 256, 0, st>>>(dout, S + s_D, dx, BL * dim);
+    }
+    e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : set_cuda_error("bf16 backward", e);
+}
+
 extern "C" int kmb_block_backward(const KMBlockConfig* c, const KMBlockWeights* w, const float* x,
                                   const float* dout, float* dx, const KMBlockGrads* g, long batch, const float* act,
                                   void* stream) {
     if (check_cfg(c, w, batch)) return -1;
     if (!x || !dout || !act || !g) return set_error("kmb_block_backward: x, dout, act, g required");
     if (!c->bf16_storage) return block_backward_f32(c, w, x, dout, dx, g, batch, act, stream);
-    // bf16 storage: widen x and dout, run the fp32 body, narrow dx
-    cudaStream_t st = (cudaStream_t)stream;
-    const long long n = (long long)batch * c->L * c->dim;
-    float* buf = (float*)workspace(WS_BLK_WBF + 1, (size_t)n * 3 * sizeof(float));
-    if (!buf) return set_error("workspace allocation failed");
-    float *x32 = buf, *d32 = buf + n, *dx32 = buf + 2 * n;
-    to_f32<<<nb(n, 256), 256, 0, st>>>((const __nv_bfloat16*)x, x32, n);
-    to_f32<<<nb(n, 256), 256, 0, st>>>((const __nv_bfloat16*)dout, d32, n);
-    if (block_backward_f32(c, w, x32, d32, dx ? dx32 : nullptr, g, batch, act, stream)) return -1;
-    if (dx) to_bf16<<<nb(n, 256), 256, 0, st>>>(dx32, (__nv_bfloat16*)dx, n);
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? 0 : set_cuda_error("bf16 backward", e);
+    return block_backward_bf16(c, w, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dout, (__nv_bfloat16*)dx, g,
+                               batch, act, stream);
 }
 
 // ---------------------------------------------------------------------------
