@@ -82,7 +82,19 @@ __device__ __forceinline__ float group_sum(float v) {
     return v;
 }
 
-template <typename T, int GP>
+// Per-point inputs of the forward that do not depend on the recurrence (RM >= R
+// ranks held; RM = 0: loaded at use).  A lane loads the next point's set while
+// it computes the current one, across the level barrier, so the level loop
+// waits only on the predecessor states.
+template <int RM>
+struct BSIn {
+    static constexpr int K = RM > 0 ? RM : 1;
+    int t;
+    bool act;
+    float dt, lam, u[K], b0[K], b1[K], c0[K], c1[K];
+};
+
+template <typename T, int GP, int RM>
 __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
     using Ln = BSLanes<GP>;
     const Ln ln(s);
@@ -97,29 +109,71 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
         sth = sinf(s.theta[n0 >> 1]);
     }
     const long long L = s.L;
-    const T* u = (const T*)s.u + b * L * R;
-    const T* dtp = (const T*)s.dt + b * L;
-    const T* lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
-    const T* Bp = (const T*)s.B + b * L * NR;
-    const T* Cp = (const T*)s.C + b * L * NR;
+    const T* __restrict__ u = (const T*)s.u + b * L * R;
+    const T* __restrict__ dtp = (const T*)s.dt + b * L;
+    const T* __restrict__ lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* __restrict__ Bp = (const T*)s.B + b * L * NR;
+    const T* __restrict__ Cp = (const T*)s.C + b * L * NR;
     float* h = s.h + b * L * N;
     float* Bu = s.Bu + b * L * N;
     // y, or this group's partial of y
     float* y = (s.NG == 1 ? s.y : s.part + (long long)ln.g * s.batch * L * R) + b * L * R;
+    const int step = nw * Ln::PPW;
+    auto load = [&](int lvl, int base, BSIn<RM>& d) {
+        d.act = base + ln.ps < s.lev_start[lvl + 1];
+        const int t = s.lev_pts[d.act ? base + ln.ps : base];
+        d.t = t;
+        d.dt = ldv(dtp + t);
+        d.lam = lamp ? ldv(lamp + t) : s.deflam;
+        if constexpr (RM > 0) {
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                if (r < R) {
+                    const long long c = (long long)t * NR + r * N;
+                    d.u[r] = ldv(u + (long long)t * R + r);
+                    d.b0[r] = h0ok ? ldv(Bp + c + n0) : 0.0f;
+                    d.b1[r] = h1ok ? ldv(Bp + c + n1) : 0.0f;
+                    d.c0[r] = h0ok ? ldv(Cp + c + n0) : 0.0f;
+                    d.c1[r] = h1ok ? ldv(Cp + c + n1) : 0.0f;
+                }
+            }
+        }
+    };
+    // this warp's next task: level nl, first point nb (nl == nlev: none left)
+    int nl = 0, nb = s.lev_start[0] + warp * Ln::PPW;
+    auto seek = [&]() {
+        while (nl < s.nlev && nb >= s.lev_start[nl + 1]) {
+            nl++;
+            if (nl < s.nlev) nb = s.lev_start[nl] + warp * Ln::PPW;
+        }
+    };
+    seek();
+    BSIn<RM> nx;
+    if (nl < s.nlev) load(nl, nb, nx);
     for (int lev = 0; lev < s.nlev; lev++) {
-        const int beg = s.lev_start[lev], end = s.lev_start[lev + 1];
-        // warp-uniform trip count: the group shuffles need the whole warp
-        for (int base = beg + warp * Ln::PPW; base < end; base += nw * Ln::PPW) {
-            const bool act = base + ln.ps < end;
-            const int t = s.lev_pts[act ? base + ln.ps : base];
-            const bool w0 = act && h0ok, w1 = act && h1ok;
-            const float dt = ldv(dtp + t);
-            const float lam = lamp ? ldv(lamp + t) : s.deflam;
+        while (nl == lev) {
+            const BSIn<RM> cur = nx;
+            nb += step;
+            seek();
+            if (nl < s.nlev) load(nl, nb, nx);
+            const int t = cur.t;
+            const bool act = cur.act, w0 = act && h0ok, w1 = act && h1ok;
+            const float dt = cur.dt, lam = cur.lam;
             float bu0 = 0.0f, bu1 = 0.0f;
-            for (int r = 0; r < R; r++) {
-                const float ur = ldv(u + (long long)t * R + r);
-                if (h0ok) bu0 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n0), ur, bu0);
-                if (h1ok) bu1 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n1), ur, bu1);
+            if constexpr (RM > 0) {
+#pragma unroll
+                for (int r = 0; r < RM; r++) {
+                    if (r < R) {
+                        bu0 = __fmaf_rn(cur.b0[r], cur.u[r], bu0);
+                        bu1 = __fmaf_rn(cur.b1[r], cur.u[r], bu1);
+                    }
+                }
+            } else {
+                for (int r = 0; r < R; r++) {
+                    const float ur = ldv(u + (long long)t * R + r);
+                    if (h0ok) bu0 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n0), ur, bu0);
+                    if (h1ok) bu1 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n1), ur, bu1);
+                }
             }
             const float al0 = kmb_exp(dt * A0, s.fast), al1 = kmb_exp(dt * A1, s.fast);
             float hn0, hn1;
@@ -168,12 +222,21 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
             const long long o = (long long)t * N;
             if (w0) { h[o + n0] = hn0; Bu[o + n0] = bu0; }
             if (w1) { h[o + n1] = hn1; Bu[o + n1] = bu1; }
-            for (int r = 0; r < R; r++) {
+            auto emit_y = [&](int r, float c0v, float c1v) {
                 float part = 0.0f;
-                if (h0ok) part = ldv(Cp + (long long)t * NR + r * N + n0) * hn0;
-                if (h1ok) part = __fmaf_rn(ldv(Cp + (long long)t * NR + r * N + n1), hn1, part);
+                if (h0ok) part = c0v * hn0;
+                if (h1ok) part = __fmaf_rn(c1v, hn1, part);
                 part = group_sum<GP>(part);
                 if (act && ln.pl == 0) y[(long long)t * R + r] = part;
+            };
+            if constexpr (RM > 0) {
+#pragma unroll
+                for (int r = 0; r < RM; r++)
+                    if (r < R) emit_y(r, cur.c0[r], cur.c1[r]);
+            } else {
+                for (int r = 0; r < R; r++)
+                    emit_y(r, h0ok ? ldv(Cp + (long long)t * NR + r * N + n0) : 0.0f,
+                           h1ok ? ldv(Cp + (long long)t * NR + r * N + n1) : 0.0f);
             }
         }
         __syncthreads();
@@ -191,7 +254,7 @@ struct BSGrad {
 };
 
 template <typename T, int GP>
-__global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) {
+__global__ void __launch_bounds__(512) blockscan_bwd_generic(BSDesc s, BSGrad g) {
     using Ln = BSLanes<GP>;
     const Ln ln(s);
     const int b = ln.b, n0 = ln.n0, n1 = ln.n1;
@@ -370,6 +433,215 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
     }
 }
 
+// Backward for grids of NDT <= 3 dimensions and rank R <= RM <= 4: every load
+// of a point (successors' adjoints and steps, predecessors' states, its own
+// inputs and the old gradient values it accumulates into) is issued before
+// any store, so a point costs one memory round trip instead of several.
+template <typename T, int GP, int RM, int NDT>
+__global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) {
+    using Ln = BSLanes<GP>;
+    const Ln ln(s);
+    const int b = ln.b, n0 = ln.n0, n1 = ln.n1;
+    const bool h0ok = ln.h0ok, h1ok = ln.h1ok, pair = ln.pair;
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int N = s.N, R = s.R, NR = N * R;
+    const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
+    float cth = 1.0f, sth = 0.0f;
+    if (pair) {
+        cth = cosf(s.theta[n0 >> 1]);
+        sth = sinf(s.theta[n0 >> 1]);
+    }
+    const long long L = s.L;
+    const T* __restrict__ u = (const T*)s.u + b * L * R;
+    const T* __restrict__ dtp = (const T*)s.dt + b * L;
+    const T* __restrict__ lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* __restrict__ Bp = (const T*)s.B + b * L * NR;
+    const T* __restrict__ Cp = (const T*)s.C + b * L * NR;
+    const float* __restrict__ h = s.h + b * L * N;
+    const float* __restrict__ Bu = s.Bu + b * L * N;
+    const float* __restrict__ dy = g.dy + b * L * R;
+    float* G = g.G + b * L * N;
+    float* dB = g.dB + b * L * NR;
+    float* dC = g.dC + b * L * NR;
+    const bool direct = s.NG == 1;
+    const long long gofs = (long long)ln.g * s.batch;
+    float* du = direct ? g.du + b * L * R : g.pdu + (gofs + b) * L * R;
+    float* ddt = direct ? (g.ddt ? g.ddt + b * L : nullptr) : g.pddt + (gofs + b) * L;
+    float* dlam = direct ? (g.dlam ? g.dlam + b * L : nullptr) : g.pdlam + (gofs + b) * L;
+    float gA0 = 0.0f, gA1 = 0.0f, gth = 0.0f;
+    int dims[NDT], strides[NDT];
+#pragma unroll
+    for (int k = 0; k < NDT; k++) {
+        dims[k] = NDT == 1 ? (int)L : s.dims[k];
+        strides[k] = NDT == 1 ? 1 : s.strides[k];
+    }
+    for (int lev = s.nlev - 1; lev >= 0; lev--) {
+        const int beg = s.lev_start[lev], end = s.lev_start[lev + 1];
+        for (int base = beg + warp * Ln::PPW; base < end; base += nw * Ln::PPW) {
+            const bool act = base + ln.ps < end;
+            const int t = s.lev_pts[act ? base + ln.ps : base];
+            const bool x0 = act && h0ok, x1 = act && h1ok;
+            int idx[NDT];
+            int npt = 0;
+#pragma unroll
+            for (int k = 0; k < NDT; k++) {
+                idx[k] = (t / strides[k]) % dims[k];
+                npt += idx[k] > 0;
+            }
+            // ---- loads
+            const float dt = ldv(dtp + t);
+            const float lam = lamp ? ldv(lamp + t) : s.deflam;
+            bool hs[NDT], hp[NDT];
+            float sdt[NDT], slam[NDT], sG0[NDT], sG1[NDT], ph0[NDT], ph1[NDT], pb0[NDT], pb1[NDT];
+#pragma unroll
+            for (int k = 0; k < NDT; k++) {
+                hs[k] = idx[k] < dims[k] - 1;
+                const int sp = hs[k] ? t + strides[k] : t;
+                sdt[k] = ldv(dtp + sp);
+                slam[k] = lamp ? ldv(lamp + sp) : s.deflam;
+                sG0[k] = h0ok && hs[k] ? G[(long long)sp * N + n0] : 0.0f;
+                sG1[k] = h1ok && hs[k] ? G[(long long)sp * N + n1] : 0.0f;
+                hp[k] = idx[k] > 0;
+                const long long q = (long long)(hp[k] ? t - strides[k] : t) * N;
+                ph0[k] = h0ok ? h[q + n0] : 0.0f;
+                ph1[k] = h1ok ? h[q + n1] : 0.0f;
+                pb0[k] = h0ok ? Bu[q + n0] : 0.0f;
+                pb1[k] = h1ok ? Bu[q + n1] : 0.0f;
+            }
+            const long long o = (long long)t * N;
+            const float ht0 = h0ok ? h[o + n0] : 0.0f, ht1 = h1ok ? h[o + n1] : 0.0f;
+            const float bu0 = h0ok ? Bu[o + n0] : 0.0f, bu1 = h1ok ? Bu[o + n1] : 0.0f;
+            float dyv[RM], uu[RM], c0[RM], c1[RM], b0[RM], b1[RM], odB0[RM], odB1[RM], odC0[RM], odC1[RM];
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                const bool rr = r < R;
+                const long long c = (long long)t * NR + (rr ? r : 0) * N;
+                dyv[r] = rr ? dy[(long long)t * R + r] : 0.0f;
+                uu[r] = rr ? ldv(u + (long long)t * R + r) : 0.0f;
+                c0[r] = rr && h0ok ? ldv(Cp + c + n0) : 0.0f;
+                c1[r] = rr && h1ok ? ldv(Cp + c + n1) : 0.0f;
+                b0[r] = rr && h0ok ? ldv(Bp + c + n0) : 0.0f;
+                b1[r] = rr && h1ok ? ldv(Bp + c + n1) : 0.0f;
+                odB0[r] = rr && x0 ? dB[c + n0] : 0.0f;
+                odB1[r] = rr && x1 ? dB[c + n1] : 0.0f;
+                odC0[r] = rr && x0 ? dC[c + n0] : 0.0f;
+                odC1[r] = rr && x1 ? dC[c + n1] : 0.0f;
+            }
+            // ---- pull from successors s = t + e_k
+            float a0 = 0.0f, a1 = 0.0f, ab0 = 0.0f, ab1 = 0.0f;
+#pragma unroll
+            for (int k = 0; k < NDT; k++) {
+                if (!hs[k]) continue;
+                const int nps = npt + (idx[k] == 0 ? 1 : 0);
+                const float al0 = kmb_exp(sdt[k] * A0, s.fast), al1 = kmb_exp(sdt[k] * A1, s.fast);
+                const float coef = (1.0f - slam[k]) * sdt[k] / (float)nps;
+                a0 += al0 * sG0[k];
+                a1 += al1 * sG1[k];
+                ab0 += coef * al0 * sG0[k];
+                ab1 += coef * al1 * sG1[k];
+            }
+            float gh0 = pair ? cth * a0 + sth * a1 : a0;
+            float gh1 = -sth * a0 + cth * a1;
+            if (pair && act) {
+                const float hat0 = cth * ht0 - sth * ht1, hat1 = sth * ht0 + cth * ht1;
+                gth += -a0 * hat1 + a1 * hat0;
+            }
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                if (r >= R) continue;
+                if (h0ok) gh0 += c0[r] * dyv[r];
+                if (h1ok) gh1 += c1[r] * dyv[r];
+            }
+            const float gam = lam * dt;
+            const float gbu0 = gam * gh0 + ab0, gbu1 = gam * gh1 + ab1;
+            float gdt = lam * (bu0 * gh0 + bu1 * gh1);
+            float glam = dt * (bu0 * gh0 + bu1 * gh1);
+            if (npt > 0) {
+                float sh0 = 0.0f, sh1 = 0.0f, sb0 = 0.0f, sb1 = 0.0f;
+#pragma unroll
+                for (int k = 0; k < NDT; k++) {
+                    if (!hp[k]) continue;
+                    sh0 += pair ? cth * ph0[k] - sth * ph1[k] : ph0[k];
+                    sh1 += sth * ph0[k] + cth * ph1[k];
+                    sb0 += pb0[k];
+                    sb1 += pb1[k];
+                }
+                const float inv = 1.0f / (float)npt;
+                const float sc = (1.0f - lam) * dt * inv;
+                const float z0 = dt * A0, z1 = dt * A1;
+                const float al0 = kmb_exp(z0, s.fast), al1 = kmb_exp(z1, s.fast);
+                const float dal0 = (sh0 + sc * sb0) * gh0, dal1 = (sh1 + sc * sb1) * gh1;
+                const float dz0 = h0ok ? kmb_dexp(z0, al0, s.fast) * dal0 : 0.0f;
+                const float dz1 = h1ok ? kmb_dexp(z1, al1, s.fast) * dal1 : 0.0f;
+                gdt += dz0 * A0 + dz1 * A1;
+                if (act) {
+                    gA0 += dz0 * dt;
+                    gA1 += dz1 * dt;
+                }
+                const float ds = al0 * sb0 * gh0 + al1 * sb1 * gh1;
+                gdt += (1.0f - lam) * inv * ds;
+                glam -= dt * inv * ds;
+            }
+            // ---- stores
+            if (x0) G[o + n0] = gh0;
+            if (x1) G[o + n1] = gh1;
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                if (r >= R) continue;
+                const long long c = (long long)t * NR + r * N;
+                if (x0) {
+                    dC[c + n0] = odC0[r] + dyv[r] * ht0;
+                    dB[c + n0] = odB0[r] + gbu0 * uu[r];
+                }
+                if (x1) {
+                    dC[c + n1] = odC1[r] + dyv[r] * ht1;
+                    dB[c + n1] = odB1[r] + gbu1 * uu[r];
+                }
+                float part = 0.0f;
+                if (h0ok) part += gbu0 * b0[r];
+                if (h1ok) part += gbu1 * b1[r];
+                part = group_sum<GP>(part);
+                if (act && ln.pl == 0) {
+                    if (direct) du[(long long)t * R + r] += part;
+                    else du[(long long)t * R + r] = part;
+                }
+            }
+            gdt = group_sum<GP>(gdt);
+            glam = group_sum<GP>(glam);
+            if (act && ln.pl == 0) {
+                if (direct) {
+                    if (ddt) ddt[t] += gdt;
+                    if (dlam) dlam[t] += glam;
+                } else {
+                    ddt[t] = gdt;
+                    dlam[t] = glam;
+                }
+            }
+        }
+        __syncthreads();
+    }
+    __shared__ float sA[16 * 32][2];
+    __shared__ float sT[16 * 32];
+    const int tid = threadIdx.x;
+    sA[tid][0] = gA0;
+    sA[tid][1] = gA1;
+    sT[tid] = gth;
+    __syncthreads();
+    if (tid < GP) {
+        float t0 = 0.0f, t1 = 0.0f, tt = 0.0f;
+        for (int j = 0; j < nw * Ln::PPW; j++) {
+            const int src = (j / Ln::PPW) * 32 + (j % Ln::PPW) * GP + tid;
+            t0 += sA[src][0];
+            t1 += sA[src][1];
+            tt += sT[src];
+        }
+        const int p = ln.g * GP + tid;
+        if (2 * p < N) g.pA[(long long)b * N + 2 * p] = t0;
+        if (2 * p + 1 < N) g.pA[(long long)b * N + 2 * p + 1] = t1;
+        if (p < 32) g.pth[(long long)b * 32 + p] = tt;
+    }
+}
+
 // out[i] (+)= sum_g part[g * n + i], g = 0 .. NG-1 in order
 __global__ void bs_group_reduce(const float* __restrict__ part, float* __restrict__ out, long long n, int ng,
                                 int accumulate) {
@@ -503,11 +775,28 @@ static int bs_threads(const BSDesc& s) {
 
 template <typename T, int GP>
 static void bs_fwd_launch(const BSDesc& s, cudaStream_t st) {
-    blockscan_fwd_kernel<T, GP><<<(unsigned)(s.batch * s.NG), bs_threads(s), 0, st>>>(s);
+    const dim3 grid((unsigned)(s.batch * s.NG));
+    const int th = bs_threads(s);
+    if (s.R <= 1) blockscan_fwd_kernel<T, GP, 1><<<grid, th, 0, st>>>(s);
+    else if (s.R <= 2) blockscan_fwd_kernel<T, GP, 2><<<grid, th, 0, st>>>(s);
+    else if (s.R <= 4) blockscan_fwd_kernel<T, GP, 4><<<grid, th, 0, st>>>(s);
+    else blockscan_fwd_kernel<T, GP, 0><<<grid, th, 0, st>>>(s);
+}
+template <typename T, int GP, int RM>
+static void bs_bwd_launch_r(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
+    const dim3 grid((unsigned)(s.batch * s.NG));
+    const int th = bs_threads(s);
+    if (s.nd <= 1) blockscan_bwd_kernel<T, GP, RM, 1><<<grid, th, 0, st>>>(s, g);
+    else if (s.nd == 2) blockscan_bwd_kernel<T, GP, RM, 2><<<grid, th, 0, st>>>(s, g);
+    else if (s.nd == 3) blockscan_bwd_kernel<T, GP, RM, 3><<<grid, th, 0, st>>>(s, g);
+    else blockscan_bwd_generic<T, GP><<<grid, th, 0, st>>>(s, g);
 }
 template <typename T, int GP>
 static void bs_bwd_launch(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
-    blockscan_bwd_kernel<T, GP><<<(unsigned)(s.batch * s.NG), bs_threads(s), 0, st>>>(s, g);
+    if (s.R <= 1) bs_bwd_launch_r<T, GP, 1>(s, g, st);
+    else if (s.R <= 2) bs_bwd_launch_r<T, GP, 2>(s, g, st);
+    else if (s.R <= 4) bs_bwd_launch_r<T, GP, 4>(s, g, st);
+    else blockscan_bwd_generic<T, GP><<<(unsigned)(s.batch * s.NG), bs_threads(s), 0, st>>>(s, g);
 }
 template <typename T>
 static void bs_fwd_dispatch(const BSDesc& s, cudaStream_t st) {
