@@ -11,6 +11,7 @@
 // produces dW_in and the projection paths of dx, which the reference skips.
 #include <cublas_v2.h>
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include "kmb_common.cuh"
@@ -143,24 +144,37 @@ __global__ void to_bf16(const float* __restrict__ a, __nv_bfloat16* __restrict__
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) b[i] = __float2bfloat16_rn(a[i]);
 }
-// out[row, d] = bf16(x[row, d] + sum_r y[row, r] W_out[d, r])   (bf16 residual stream),
-// 8 channels (16 bytes) per thread; dim % 8 == 0 and 16-byte aligned x / out
-__global__ void block_out_bf16_v8(const uint4* __restrict__ x, const float* __restrict__ y,
-                                  const float* __restrict__ Wout, unsigned rows, unsigned dim8, int R,
-                                  uint4* __restrict__ out) {
-    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= rows * dim8) return;
-    const unsigned row = i / dim8, d0 = (i - row * dim8) * 8;
-    uint4 xv = x[i];
-    __nv_bfloat16* xe = (__nv_bfloat16*)&xv;
-    const float* yr = y + (size_t)row * R;
+// out[row, d] = bf16(x[row, d] + sum_r y[row, r] W_out[d, r])   (bf16 residual stream).
+// A thread owns an 8-channel column chunk (16 bytes), keeps its W_out slice in
+// registers and walks rows; dim % 8 == 0, 16-byte aligned x / out, R <= RM.
+template <int RM>
+__global__ void block_out_bf16_cols(const uint4* __restrict__ x, const float* __restrict__ y,
+                                    const float* __restrict__ Wout, long long rows, int dim8, int R,
+                                    uint4* __restrict__ out) {
+    const int c = threadIdx.x % dim8, rpb = blockDim.x / dim8;
+    const int d0 = c * 8;
+    if ((int)threadIdx.x >= rpb * dim8) return;
+    float w[8][RM];
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-        float acc = 0.0f;
-        for (int r = 0; r < R; r++) acc = __fmaf_rn(yr[r], Wout[(size_t)(d0 + e) * R + r], acc);
-        xe[e] = __float2bfloat16_rn(__bfloat162float(xe[e]) + acc);
+    for (int e = 0; e < 8; e++)
+#pragma unroll
+        for (int r = 0; r < RM; r++) w[e][r] = r < R ? Wout[(long long)(d0 + e) * R + r] : 0.0f;
+    for (long long row = (long long)blockIdx.x * rpb + threadIdx.x / dim8; row < rows; row += (long long)gridDim.x * rpb) {
+        float yr[RM];
+#pragma unroll
+        for (int r = 0; r < RM; r++) yr[r] = r < R ? y[row * R + r] : 0.0f;
+        const long long i = row * dim8 + c;
+        uint4 xv = x[i];
+        __nv_bfloat16* xe = (__nv_bfloat16*)&xv;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int r = 0; r < RM; r++) acc = __fmaf_rn(yr[r], w[e][r], acc);
+            xe[e] = __float2bfloat16_rn(__bfloat162float(xe[e]) + acc);
+        }
+        out[i] = xv;
     }
-    out[i] = xv;
 }
 __global__ void block_out_bf16(const __nv_bfloat16* __restrict__ x, const float* __restrict__ y,
                                const float* __restrict__ Wout, long long BL, int dim, int R,
@@ -276,11 +290,17 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     p.inputs_bf16 = bf;
     if (kmb_blockscan_forward(&p, batch, stream)) return -1;
     if (bf) {
-        if (dim % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0 && a.BL * dim / 8 < (1LL << 31))
-            block_out_bf16_v8<<<nb(a.BL * dim / 8, 256), 256, 0, st>>>((const uint4*)x, act + a.y, w->W_out,
-                                                                      (unsigned)a.BL, (unsigned)(dim / 8), (int)c->R,
-                                                                      (uint4*)out);
-        else
+        const int dim8 = dim / 8;
+        if (dim % 8 == 0 && dim8 <= 256 && c->R <= 4 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+            const int rpb = 256 / dim8;
+            const unsigned grid = (unsigned)std::min<long long>((a.BL + rpb - 1) / rpb, 148LL * 8);
+            if (c->R <= 2)
+                block_out_bf16_cols<2><<<grid, 256, 0, st>>>((const uint4*)x, act + a.y, w->W_out, a.BL, dim8,
+                                                             (int)c->R, (uint4*)out);
+            else
+                block_out_bf16_cols<4><<<grid, 256, 0, st>>>((const uint4*)x, act + a.y, w->W_out, a.BL, dim8,
+                                                             (int)c->R, (uint4*)out);
+        } else
             block_out_bf16<<<nb(a.BL * dim, 256), 256, 0, st>>>((const __nv_bfloat16*)x, act + a.y, w->W_out, a.BL,
                                                                dim, (int)c->R, (__nv_bfloat16*)out);
         e = cudaGetLastError();
@@ -371,10 +391,20 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     return 0;
 }
 
-// dx = bf16(dout + D)   (bf16 residual stream; dx may alias dout)
+// dx = bf16(dout + D)   (bf16 residual stream; dx may alias dout), 8 elements per thread
 __global__ void residual_bf16(const __nv_bfloat16* dout, const float* __restrict__ D, __nv_bfloat16* dx, long long n) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) dx[i] = __float2bfloat16_rn(__bfloat162float(dout[i]) + D[i]);
+    const long long i8 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (i8 + 8 <= n && (((uintptr_t)dout | (uintptr_t)dx) & 15) == 0 && ((uintptr_t)D & 15) == 0) {
+        uint4 v = *(const uint4*)(dout + i8);
+        const float4 a = *(const float4*)(D + i8), b = *(const float4*)(D + i8 + 4);
+        __nv_bfloat16* e = (__nv_bfloat16*)&v;
+        const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int j = 0; j < 8; j++) e[j] = __float2bfloat16_rn(__bfloat162float(e[j]) + f[j]);
+        *(uint4*)(dx + i8) = v;
+    } else {
+        for (long long i = i8; i < i8 + 8 && i < n; i++) dx[i] = __float2bfloat16_rn(__bfloat162float(dout[i]) + D[i]);
+    }
 }
 
 static cublasStatus_t gemm_bf16(cublasHandle_t hb, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
@@ -460,7 +490,7 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
         if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, Wb, dim, dPb, (int)Rt, 0.0f, S + s_D,
                       dim) != CUBLAS_STATUS_SUCCESS)
             return set_error("dx GEMM failed");
-        residual_bf16<<<nb(BL * dim, 256), 256, 0, st>>>(dout, S + s_D, dx, BL * dim);
+        residual_bf16<<<nb((BL * dim + 7) / 8, 256), 256, 0, st>>>(dout, S + s_D, dx, BL * dim);
     }
     e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("bf16 backward", e);

@@ -32,6 +32,9 @@ struct BSDesc {
     int nlev;
     const int* lev_start;   // [nlev + 1]
     const int* lev_pts;     // [L]
+    const int* lev_pos;     // [L] position of a point inside its level
+    const int* nbr;         // [L] bit k: predecessor along k, bit 8 + k: successor along k
+    int wmax;               // widest level
     const void *u, *dt, *lam, *B, *C;  // float, or __nv_bfloat16 when bf16
     const float *A, *theta;
     float *h, *Bu, *y;
@@ -237,6 +240,166 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                 for (int r = 0; r < R; r++)
                     emit_y(r, h0ok ? ldv(Cp + (long long)t * NR + r * N + n0) : 0.0f,
                            h1ok ? ldv(Cp + (long long)t * NR + r * N + n1) : 0.0f);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Forward for NDT <= 3 dimensions, R <= RM <= 4: the previous level's states
+// and B*u products of this CTA's pairs live in a two-level shared-memory ring
+// ([2][wmax][GP][2] each), so a point reads its predecessors in shared memory;
+// the next point's inputs (B, C, u, dt, lambda, neighbour mask, predecessor
+// positions) are prefetched into registers across the level barrier.
+template <int RM, int NDT>
+struct BSInR {
+    int t, nb, pos, ppos[NDT];
+    bool act;
+    float dt, lam, u[RM], b0[RM], b1[RM], c0[RM], c1[RM];
+};
+
+template <typename T, int GP, int RM, int NDT>
+__global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
+    using Ln = BSLanes<GP>;
+    extern __shared__ float bs_ring[];
+    const Ln ln(s);
+    const int b = ln.b, n0 = ln.n0, n1 = ln.n1, pl = ln.pl;
+    const bool h0ok = ln.h0ok, h1ok = ln.h1ok, pair = ln.pair;
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int N = s.N, R = s.R, NR = N * R, wmax = s.wmax;
+    const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
+    float cth = 1.0f, sth = 0.0f;
+    if (pair) {
+        cth = cosf(s.theta[n0 >> 1]);
+        sth = sinf(s.theta[n0 >> 1]);
+    }
+    int strides[NDT];
+#pragma unroll
+    for (int k = 0; k < NDT; k++) strides[k] = NDT == 1 ? 1 : s.strides[k];
+    const long long L = s.L;
+    const T* __restrict__ u = (const T*)s.u + b * L * R;
+    const T* __restrict__ dtp = (const T*)s.dt + b * L;
+    const T* __restrict__ lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* __restrict__ Bp = (const T*)s.B + b * L * NR;
+    const T* __restrict__ Cp = (const T*)s.C + b * L * NR;
+    float* h = s.h + b * L * N;
+    float* Bu = s.Bu + b * L * N;
+    float* y = (s.NG == 1 ? s.y : s.part + (long long)ln.g * s.batch * L * R) + b * L * R;
+    float* ring_h = bs_ring;                          // [2][wmax][GP][2]
+    float* ring_b = bs_ring + 2 * (size_t)wmax * GP * 2;
+    auto rix = [&](int buf, int pos) { return ((size_t)(buf * wmax + pos) * GP + pl) * 2; };
+    const int step = nw * Ln::PPW;
+    auto load = [&](int lvl, int base, BSInR<RM, NDT>& d) {
+        const int beg = s.lev_start[lvl];
+        d.act = base + ln.ps < s.lev_start[lvl + 1];
+        const int i = d.act ? base + ln.ps : base;
+        const int t = s.lev_pts[i];
+        d.t = t;
+        d.pos = i - beg;
+        d.nb = s.nbr[t];
+#pragma unroll
+        for (int k = 0; k < NDT; k++) d.ppos[k] = (d.nb >> k) & 1 ? s.lev_pos[t - strides[k]] : 0;
+        d.dt = ldv(dtp + t);
+        d.lam = lamp ? ldv(lamp + t) : s.deflam;
+#pragma unroll
+        for (int r = 0; r < RM; r++) {
+            const bool rr = r < R;
+            const long long c = (long long)t * NR + (rr ? r : 0) * N;
+            d.u[r] = rr ? ldv(u + (long long)t * R + r) : 0.0f;
+            d.b0[r] = rr && h0ok ? ldv(Bp + c + n0) : 0.0f;
+            d.b1[r] = rr && h1ok ? ldv(Bp + c + n1) : 0.0f;
+            d.c0[r] = rr && h0ok ? ldv(Cp + c + n0) : 0.0f;
+            d.c1[r] = rr && h1ok ? ldv(Cp + c + n1) : 0.0f;
+        }
+    };
+    int nl = 0, nbase = s.lev_start[0] + warp * Ln::PPW;
+    auto seek = [&]() {
+        while (nl < s.nlev && nbase >= s.lev_start[nl + 1]) {
+            nl++;
+            if (nl < s.nlev) nbase = s.lev_start[nl] + warp * Ln::PPW;
+        }
+    };
+    seek();
+    BSInR<RM, NDT> nx;
+    if (nl < s.nlev) load(nl, nbase, nx);
+    for (int lev = 0; lev < s.nlev; lev++) {
+        const int cb = lev & 1, pb = cb ^ 1;
+        while (nl == lev) {
+            const BSInR<RM, NDT> cur = nx;
+            nbase += step;
+            seek();
+            if (nl < s.nlev) load(nl, nbase, nx);
+            const int t = cur.t;
+            const bool act = cur.act;
+            const float dt = cur.dt, lam = cur.lam;
+            float bu0 = 0.0f, bu1 = 0.0f;
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                bu0 = __fmaf_rn(cur.b0[r], cur.u[r], bu0);
+                bu1 = __fmaf_rn(cur.b1[r], cur.u[r], bu1);
+            }
+            const float al0 = kmb_exp(dt * A0, s.fast), al1 = kmb_exp(dt * A1, s.fast);
+            float hn0, hn1;
+            if (NDT >= 2) {
+                float bacc0 = 0.0f, bacc1 = 0.0f;
+                hn0 = 0.0f;
+                hn1 = 0.0f;
+                int np = 0;
+#pragma unroll
+                for (int k = 0; k < NDT; k++) {
+                    if (!((cur.nb >> k) & 1)) continue;
+                    const size_t q = rix(pb, cur.ppos[k]);
+                    const float p0 = ring_h[q], p1 = ring_h[q + 1];
+                    const float r0 = pair ? cth * p0 - sth * p1 : p0;
+                    const float r1 = sth * p0 + cth * p1;
+                    hn0 = __fmaf_rn(al0, r0, hn0);
+                    hn1 = __fmaf_rn(al1, r1, hn1);
+                    bacc0 += ring_b[q];
+                    bacc1 += ring_b[q + 1];
+                    np++;
+                }
+                if (np > 0) {
+                    const float bs = (1.0f - lam) * dt / (float)np;
+                    hn0 = __fmaf_rn(bs * al0, bacc0, hn0);
+                    hn1 = __fmaf_rn(bs * al1, bacc1, hn1);
+                }
+                const float gm = lam * dt;
+                hn0 = __fmaf_rn(gm, bu0, hn0);
+                hn1 = __fmaf_rn(gm, bu1, hn1);
+            } else {
+                // 1D recurrence (reference src/mamba_block.c:384-393)
+                float p0 = 0.0f, p1 = 0.0f, pb0 = 0.0f, pb1 = 0.0f;
+                if (cur.nb & 1) {
+                    const size_t q = rix(pb, cur.ppos[0]);
+                    p0 = ring_h[q]; p1 = ring_h[q + 1];
+                    pb0 = ring_b[q]; pb1 = ring_b[q + 1];
+                }
+                const float r0 = pair ? cth * p0 - sth * p1 : p0;
+                const float r1 = sth * p0 + cth * p1;
+                const float beta0 = (1.0f - lam) * dt * al0, beta1 = (1.0f - lam) * dt * al1;
+                const float gm = lam * dt;
+                hn0 = __fmaf_rn(gm, bu0, __fmaf_rn(beta0, pb0, al0 * r0));
+                hn1 = __fmaf_rn(gm, bu1, __fmaf_rn(beta1, pb1, al1 * r1));
+            }
+            // states of absent states (odd N, padding pairs) stay 0 in the ring
+            if (!h0ok) { hn0 = 0.0f; bu0 = 0.0f; }
+            if (!h1ok) { hn1 = 0.0f; bu1 = 0.0f; }
+            if (act) {
+                const size_t q = rix(cb, cur.pos);
+                ring_h[q] = hn0; ring_h[q + 1] = hn1;
+                ring_b[q] = bu0; ring_b[q + 1] = bu1;
+                const long long o = (long long)t * N;
+                if (h0ok) { h[o + n0] = hn0; Bu[o + n0] = bu0; }
+                if (h1ok) { h[o + n1] = hn1; Bu[o + n1] = bu1; }
+            }
+#pragma unroll
+            for (int r = 0; r < RM; r++) {
+                if (r >= R) break;
+                float part = 0.0f;
+                if (h0ok) part = cur.c0[r] * hn0;
+                if (h1ok) part = __fmaf_rn(cur.c1[r], hn1, part);
+                part = group_sum<GP>(part);
+                if (act && ln.pl == 0) y[(long long)t * R + r] = part;
             }
         }
         __syncthreads();
@@ -665,6 +828,7 @@ __global__ void bs_reduce_add(const float* __restrict__ part, float* __restrict_
 }  // namespace kmb
 
 // ------------------------------------------------------------------ host side
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <vector>
@@ -680,41 +844,70 @@ enum { WS_BS_FWD = 3, WS_BS_SCRATCH = 4 };
 // points of every level [L]), cached per host thread, device and shape.
 // Shared with the Scan-A backward (scannd_bwd.cu).
 struct PlanEntry {
-    int nlev = 0;
+    int nlev = 0, wmax = 0;
     int* dev = nullptr;
 };
 static thread_local std::map<int, std::map<std::vector<long>, PlanEntry>> tl_plans;
 
-int device_plan(const std::vector<long>& dims, long L, int** out, int* nlev, cudaStream_t st) {
+// Device layout: level starts [nlev + 1] | points of every level [L] | position
+// of every point inside its level [L] | neighbour mask of every point [L]
+// (bit k: a predecessor along axis k, bit 8 + k: a successor along axis k).
+int device_plan_ex(const std::vector<long>& dims, long L, int** out, int* nlev, int* wmax, cudaStream_t st) {
     int devid = 0;
     cudaGetDevice(&devid);
     PlanEntry& pe = tl_plans[devid][dims];
-    if (pe.dev) {
-        *out = pe.dev;
-        *nlev = pe.nlev;
-        return 0;
+    if (!pe.dev) {
+        KMWavefrontPlan* pl = km_wavefront_plan_create(dims.data(), (long)dims.size(), 0);
+        if (!pl) return set_error("cannot build the wavefront plan");
+        const int nl = (int)pl->max_level + 1;
+        std::vector<int> host(nl + 1 + 3 * (size_t)L);
+        int* starts = host.data();
+        int* pts = starts + nl + 1;
+        int* pos = pts + L;
+        int* mask = pos + L;
+        int wm = 0;
+        for (int i = 0; i <= nl; i++) starts[i] = (int)pl->level_starts[i];
+        for (int l = 0; l < nl; l++) {
+            wm = std::max(wm, starts[l + 1] - starts[l]);
+            for (int i = starts[l]; i < starts[l + 1]; i++) {
+                pts[i] = (int)pl->level_offsets[i];
+                pos[pts[i]] = i - starts[l];
+            }
+        }
+        km_wavefront_plan_free(pl);
+        const int nd = (int)dims.size();
+        for (long t = 0; t < L; t++) {
+            long rem = t;
+            int m = 0;
+            for (int k = nd - 1; k >= 0; k--) {
+                const long ik = rem % dims[k];
+                rem /= dims[k];
+                if (ik > 0) m |= 1 << k;
+                if (ik < dims[k] - 1) m |= 1 << (8 + k);
+            }
+            mask[t] = m;
+        }
+        int* d = nullptr;
+        cudaError_t e = cudaMalloc(&d, host.size() * sizeof(int));  // one allocation per shape, kept for reuse
+        if (e != cudaSuccess) return set_cuda_error("plan allocation", e);
+        e = cudaMemcpyAsync(d, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // the host vector goes out of scope
+        if (e != cudaSuccess) {
+            cudaFree(d);
+            return set_cuda_error("plan upload", e);
+        }
+        pe.dev = d;
+        pe.nlev = nl;
+        pe.wmax = wm;
     }
-    KMWavefrontPlan* pl = km_wavefront_plan_create(dims.data(), (long)dims.size(), 0);
-    if (!pl) return set_error("cannot build the wavefront plan");
-    const int nl = (int)pl->max_level + 1;
-    std::vector<int> host(nl + 1 + L);
-    for (int i = 0; i <= nl; i++) host[i] = (int)pl->level_starts[i];
-    for (long i = 0; i < L; i++) host[nl + 1 + i] = (int)pl->level_offsets[i];
-    km_wavefront_plan_free(pl);
-    int* d = nullptr;
-    cudaError_t e = cudaMalloc(&d, host.size() * sizeof(int));  // one allocation per shape, kept for reuse
-    if (e != cudaSuccess) return set_cuda_error("plan allocation", e);
-    e = cudaMemcpyAsync(d, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // the host vector goes out of scope
-    if (e != cudaSuccess) {
-        cudaFree(d);
-        return set_cuda_error("plan upload", e);
-    }
-    pe.dev = d;
-    pe.nlev = nl;
-    *out = d;
-    *nlev = nl;
+    *out = pe.dev;
+    *nlev = pe.nlev;
+    if (wmax) *wmax = pe.wmax;
     return 0;
+}
+
+int device_plan(const std::vector<long>& dims, long L, int** out, int* nlev, cudaStream_t st) {
+    return device_plan_ex(dims, L, out, nlev, nullptr, st);
 }
 
 static int bs_desc(const KMBlockScanParams* p, long batch, BSDesc* s, cudaStream_t st) {
@@ -756,9 +949,11 @@ static int bs_desc(const KMBlockScanParams* p, long batch, BSDesc* s, cudaStream
     }
     if (p->ndims <= 1) s->nd = 1;
     int* plan = nullptr;
-    if (device_plan(dims, p->L, &plan, &s->nlev, st)) return -1;
+    if (device_plan_ex(dims, p->L, &plan, &s->nlev, &s->wmax, st)) return -1;
     s->lev_start = plan;
     s->lev_pts = plan + s->nlev + 1;
+    s->lev_pos = s->lev_pts + p->L;
+    s->nbr = s->lev_pos + p->L;
     s->bf16 = p->inputs_bf16 != 0;
     s->u = p->u; s->dt = p->dt; s->lam = p->lambda; s->B = p->B; s->C = p->C; s->A = p->A_log;
     s->theta = p->theta; s->h = p->h; s->Bu = p->Bu; s->y = p->y;
@@ -773,10 +968,34 @@ static int bs_threads(const BSDesc& s) {
     return 512;
 }
 
+// shared memory of the ring kernels (two levels of GP pairs, two arrays)
+static size_t ring_bytes(const BSDesc& s) { return (size_t)2 * 2 * s.wmax * s.GP * 2 * sizeof(float); }
+static bool ring_ok(const BSDesc& s) { return s.nd <= 3 && s.R <= 4 && ring_bytes(s) <= 200 * 1024; }
+
+template <typename T, int GP, int RM>
+static void bs_fwd_ring_r(const BSDesc& s, cudaStream_t st) {
+    const dim3 grid((unsigned)(s.batch * s.NG));
+    const int th = bs_threads(s);
+    const size_t sm = ring_bytes(s);
+    auto go = [&](auto kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        kern<<<grid, th, sm, st>>>(s);
+    };
+    if (s.nd <= 1) go(blockscan_fwd_ring<T, GP, RM, 1>);
+    else if (s.nd == 2) go(blockscan_fwd_ring<T, GP, RM, 2>);
+    else go(blockscan_fwd_ring<T, GP, RM, 3>);
+}
+
 template <typename T, int GP>
 static void bs_fwd_launch(const BSDesc& s, cudaStream_t st) {
     const dim3 grid((unsigned)(s.batch * s.NG));
     const int th = bs_threads(s);
+    if (ring_ok(s)) {
+        if (s.R <= 1) bs_fwd_ring_r<T, GP, 1>(s, st);
+        else if (s.R <= 2) bs_fwd_ring_r<T, GP, 2>(s, st);
+        else bs_fwd_ring_r<T, GP, 4>(s, st);
+        return;
+    }
     if (s.R <= 1) blockscan_fwd_kernel<T, GP, 1><<<grid, th, 0, st>>>(s);
     else if (s.R <= 2) blockscan_fwd_kernel<T, GP, 2><<<grid, th, 0, st>>>(s);
     else if (s.R <= 4) blockscan_fwd_kernel<T, GP, 4><<<grid, th, 0, st>>>(s);
