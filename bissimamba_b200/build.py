@@ -8,7 +8,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libkmamba_b200.so")
-SOURCES = ["capi.cu", "scannd_generic.cu", "scannd_tma.cu", "scannd_strips.cu", "scannd_bwd.cu", "convnd.cu", "blockscan.cu", "block.cu", "model.cu", "wavefront.cpp"]
+SOURCES = ["capi.cu", "scannd_generic.cu", "scannd_tma.cu", "scannd_strips.cu", "scannd_bwd.cu", "convnd.cu", "blockscan.cu", "block.cu", "proj_tc.cu", "model.cu", "wavefront.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC,-O3", "-shared", "--expt-relaxed-constexpr", "-ccbin", "/usr/bin/g++"]

@@ -193,6 +193,16 @@ __global__ void fill_value(float* p, long long n, float v) {
     if (i < n) p[i] = v;
 }
 
+int* device_status();
+cudaError_t launch_proj_fwd_tc(const __nv_bfloat16* X, const float* Win, const float* dp, const float* lp,
+                               const float* WB, const float* WC, __nv_bfloat16* W, long long BL, int dim, int R,
+                               int NR, float dt_min, float dt_max, const float* bB, const float* bC, float* P,
+                               __nv_bfloat16* u, __nv_bfloat16* dt, __nv_bfloat16* lam, __nv_bfloat16* B,
+                               __nv_bfloat16* C, int* status, cudaStream_t st);
+// 1: route the bf16 projections through cuBLAS + separate epilogues (tests / comparison)
+static thread_local int tl_no_tc = 0;
+static thread_local int tl_proj_path = -1;  // projection of the last bf16 forward: 1 tensor cores, 0 cuBLAS
+
 static thread_local std::map<int, cublasHandle_t> tl_cublas;
 static cublasHandle_t cublas_for(cudaStream_t st) {
     int dev = 0;
@@ -243,6 +253,9 @@ extern "C" size_t kmb_block_activation_floats(const KMBlockConfig* c, long batch
     return act_layout(c, batch).total;
 }
 
+extern "C" void kmb_block_set_tensor_cores(int on) { tl_no_tc = on ? 0 : 1; }
+extern "C" int kmb_block_last_projection_path(void) { return tl_proj_path; }
+
 extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w, const float* x, float* out,
                                  long batch, float* act, void* stream) {
     if (check_cfg(c, w, batch)) return -1;
@@ -261,12 +274,27 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
         // bf16 x bf16 -> fp32 projection GEMM (tensor cores through cuBLAS)
         __nv_bfloat16* Wb = (__nv_bfloat16*)workspace(WS_BLK_WBF, (size_t)a.Rt * dim * sizeof(__nv_bfloat16));
         if (!Wb) return set_error("workspace allocation failed");
+        typedef __nv_bfloat16 H;
+        // tensor-core projection with the epilogue fused (tcgen05); cuBLAS + epilogue otherwise
+        int* status = device_status();
+        if (status && !tl_no_tc) {
+            cudaMemsetAsync(status, 0, sizeof(int), st);
+            e = launch_proj_fwd_tc((const H*)x, w->W_in, w->delta_proj, w->lambda_proj, w->W_B, w->W_C, Wb, a.BL,
+                                   dim, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, act + a.proj,
+                                   (H*)(act + a.u), (H*)(act + a.dt), (H*)(act + a.lam), (H*)(act + a.B),
+                                   (H*)(act + a.C), status, st);
+            if (e != cudaSuccess && e != cudaErrorNotSupported) return set_cuda_error("tensor-core projection", e);
+        } else {
+            e = cudaErrorNotSupported;
+        }
+        tl_proj_path = e == cudaSuccess ? 1 : 0;
+        if (e == cudaSuccess) goto scan;
+        cudaGetLastError();
         to_bf16<<<nb(a.Rt * dim, 256), 256, 0, st>>>(W, Wb, a.Rt * dim);
         if (cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, (int)a.Rt, (int)a.BL, dim, &one, Wb, CUDA_R_16BF, dim, x,
                          CUDA_R_16BF, dim, &zero, act + a.proj, CUDA_R_32F, (int)a.Rt, CUBLAS_COMPUTE_32F,
                          CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
             return set_error("bf16 projection GEMM failed");
-        typedef __nv_bfloat16 H;
         block_fwd_epilogue<H><<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(
             act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, (H*)(act + a.u),
             (H*)(act + a.dt), (H*)(act + a.lam), (H*)(act + a.B), (H*)(act + a.C));
@@ -281,6 +309,7 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("block epilogue", e);
+scan:
     KMBlockScanParams p;
     memset(&p, 0, sizeof p);
     p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;

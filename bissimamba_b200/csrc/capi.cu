@@ -104,6 +104,14 @@ void* ws_get(int slot, size_t bytes) {
 }
 
 int* status_word() { return (int*)ws_get(WS_STATUS, 256); }
+}  // namespace
+
+namespace kmb {
+// the device status word of this host thread and device (kernels record bounded-wait timeouts in it)
+int* device_status() { return status_word(); }
+}  // namespace kmb
+
+namespace {
 
 }  // namespace
 
@@ -235,6 +243,16 @@ extern "C" {
 
 const char* kmb_last_error(void) { return tl_err.c_str(); }
 void kmb_clear_error(void) { tl_err.clear(); }
+
+int kmb_device_status(void* stream) {
+    int* status = status_word();
+    if (!status) return -1;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return -1;
+    int v = 0;
+    if (cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (v != 0) cudaMemset(status, 0, sizeof(int));
+    return v;
+}
 int kmb_last_forward_path(void) { return tl_fast_path; }
 void kmb_set_force_generic(int on) { g_force_generic = on ? 1 : 0; }
 

@@ -1,0 +1,286 @@
+// proj_tc.cu -- the bf16 block projection on the sm_100a tensor cores (tcgen05),
+// with the block's input epilogue fused in.
+//
+// Q[row, c] = sum_k X[row, k] Wtc[c, k]   (X [BL, dim] bf16, Wtc [Rt, dim] bf16,
+// both K-major), with the projection rows in the order Wtc = [W_B; W_C; W_in;
+// delta_proj; lambda_proj] so that 16-column accumulator chunks map onto whole
+// 32-byte pieces of B and C rows (N R % 16 == 0).  Then per column (reference
+// project_controller_full, src/mamba_block.c:106-125): B = Q + b_B and C = Q +
+// b_C, u = silu(Q), dt = clamp(softplus(Q)), lambda = sigmoid(Q).  u, dt,
+// lambda, B, C are written as bf16 straight from the accumulator (B and C as
+// 16-byte vectors); the fp32 pre-activations of u, dt, lambda are also kept in
+// the block's P layout (row stride Rt, columns 0 .. R+1), which is all the
+// backward epilogue reads of P.
+//
+// One CTA per 128-row tile of X and up to 512 columns of Wcat (grid.y covers
+// more): warp 0 issues the TMA loads (128B-swizzled K-major tiles, 64 K-elements
+// per stage, a ring of S stages), warp 1 owns the TMEM accumulator (128 lanes x
+// up to 512 fp32 columns) and issues tcgen05.mma (M = 128, N = 256 and the
+// remainder, K = 16 per instruction), warps 2-5 read TMEM rows back with
+// tcgen05.ld and run the epilogue.  Every wait is bounded; on a timeout the
+// kernel records a status, drains its copies and still frees its TMEM.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include "kmb_common.cuh"
+#include "kmb_sync.cuh"
+
+namespace kmb {
+
+struct ProjTCDesc {
+    long long BL;
+    int dim, R, NR, Rt, ncols_max;   // ncols_max: columns one CTA covers (<= 512, multiple of 16)
+    int stages, stage_bytes, x_bytes;
+    float dt_min, dt_max;
+    const float *bB, *bC;
+    float* P;                         // fp32 pre-activations, [BL, Rt] (columns < R + 2 written)
+    __nv_bfloat16 *u, *dt, *lam, *B, *C;
+    int* status;
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(c0), "r"(c1) : "memory");
+}
+
+// K-major, 128-byte-swizzled operand tile: rows of 64 bf16 (128 B), 8-row groups
+// 1024 B apart; start must be 1024-byte aligned (+ 32 B per K step of 16).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    const uint64_t lo = (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16);   // start, LBO = 16 B (unused)
+    const uint64_t hi = (uint64_t)(1024 >> 4) | ((uint64_t)1 << 14) | ((uint64_t)2 << 29);  // SBO, version 1, SW128
+    return lo | (hi << 32);
+}
+// kind::f16 instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, M = 128
+__device__ __forceinline__ uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)acc) : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+constexpr int PTC_THREADS = 192;
+constexpr int PTC_WROWS = 16;   // rows of Wcat per TMA box
+
+__global__ void __launch_bounds__(PTC_THREADS, 1)
+proj_fwd_tc(const __grid_constant__ ProjTCDesc d, const __grid_constant__ CUtensorMap mX,
+            const __grid_constant__ CUtensorMap mW) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte alignment for the swizzled tiles
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int S = d.stages;
+    uint64_t* full = (uint64_t*)(smem + (size_t)S * d.stage_bytes);
+    uint64_t* empty = full + S;
+    uint64_t* done = empty + S;
+    uint32_t* tmem_slot = (uint32_t*)(done + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long m0 = (long long)blockIdx.x * 128;
+    const int n0 = blockIdx.y * d.ncols_max;
+    const int ncols = min(d.ncols_max, ((d.Rt + 15) & ~15) - n0);   // multiple of 16
+    const int nch0 = min(ncols, 256), nch1 = ncols - nch0;
+    const int nkb = d.dim / 64;
+    const int tcols = ncols <= 32 ? 32 : ncols <= 64 ? 64 : ncols <= 128 ? 128 : ncols <= 256 ? 256 : 512;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) {
+            mbar_init(smem_u32(&full[i]), 1);
+            mbar_init(smem_u32(&empty[i]), 1);
+        }
+        mbar_init(smem_u32(done), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(tcols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const unsigned wbytes = (unsigned)ncols * 128;
+            int issued = 0;
+            for (int kb = 0; kb < nkb && ok; kb++) {
+                const int s = kb % S;
+                if (kb >= S && !mbar_wait(smem_u32(&empty[s]), (uint32_t)(((kb / S) - 1) & 1))) {
+                    set_status(d.status, KMB_ERR_TIMEOUT_EMPTY);
+                    ok = false;
+                    break;
+                }
+                unsigned char* st = smem + (size_t)s * d.stage_bytes;
+                const uint32_t fb = smem_u32(&full[s]);
+                mbar_expect_tx(fb, (unsigned)d.x_bytes + wbytes);
+                tma_load_2d(smem_u32(st), &mX, fb, kb * 64, (int)m0);
+                for (int r = 0; r < ncols; r += PTC_WROWS)
+                    tma_load_2d(smem_u32(st + d.x_bytes + r * 128), &mW, fb, kb * 64, n0 + r);
+                issued = kb + 1;
+            }
+            // copies still in flight must land before the CTA can leave
+            for (int kb = (issued > S ? issued - S : 0); kb < issued; kb++)
+                mbar_wait(smem_u32(&full[kb % S]), (uint32_t)((kb / S) & 1));
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t id0 = idesc_bf16(nch0), id1 = nch1 > 0 ? idesc_bf16(nch1) : 0u;
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % S;
+                if (!mbar_wait(smem_u32(&full[s]), (uint32_t)((kb / S) & 1))) {
+                    set_status(d.status, KMB_ERR_TIMEOUT_FULL);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t xa = smem_u32(smem + (size_t)s * d.stage_bytes);
+                const uint32_t wa = xa + d.x_bytes;
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++) {
+                    const bool acc = kb > 0 || ks > 0;
+                    umma_bf16(tmem, sw128_desc(xa + ks * 32), sw128_desc(wa + ks * 32), id0, acc);
+                    if (nch1 > 0)
+                        umma_bf16(tmem + 256, sw128_desc(xa + ks * 32), sw128_desc(wa + 256 * 128 + ks * 32), id1, acc);
+                }
+                umma_commit(smem_u32(&empty[s]));   // the stage is free once these MMAs have read it
+            }
+            umma_commit(smem_u32(done));            // accumulator complete (or as far as it got)
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile
+        const int q = warp & 3;
+        const long long row = m0 + q * 32 + lane;
+        const bool got = mbar_wait(smem_u32(done), 0);
+        if (!got) set_status(d.status, KMB_ERR_TIMEOUT_Y);
+        tc_fence_after();
+        const int R = d.R, NR = d.NR, Rt = d.Rt;
+        for (int c = 0; c < ncols; c += 16) {
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+            if (!got || row >= d.BL) continue;
+            const int col = n0 + c;
+            if (col < 2 * NR) {
+                // 16 columns of B or C: bias, round, two 16-byte stores
+                const bool isB = col < NR;
+                const int jj = isB ? col : col - NR;
+                const float* bias = (isB ? d.bB : d.bC) + jj;
+                __nv_bfloat16* dst = (isB ? d.B : d.C) + row * NR + jj;
+                uint4 pk[2];
+                __nv_bfloat16* e = (__nv_bfloat16*)pk;
+#pragma unroll
+                for (int j = 0; j < 16; j++) e[j] = __float2bfloat16_rn(v[j] + bias[j]);
+                ((uint4*)dst)[0] = pk[0];
+                ((uint4*)dst)[1] = pk[1];
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int k = col + j - 2 * NR;  // 0 .. R-1: u, R: dt, R+1: lambda
+                    if (k > R + 1) break;
+                    const float z = v[j];
+                    d.P[row * Rt + k] = z;
+                    if (k < R) {
+                        d.u[row * R + k] = __float2bfloat16_rn(z / (1.0f + expf(-z)));
+                    } else if (k == R) {
+                        float t = logf(1.0f + expf(z));
+                        t = fminf(fmaxf(t, d.dt_min), d.dt_max);
+                        d.dt[row] = __float2bfloat16_rn(t);
+                    } else {
+                        d.lam[row] = __float2bfloat16_rn(1.0f / (1.0f + expf(-z)));
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+}
+
+// Wtc[Rt, dim] bf16 = [W_B; W_C; W_in; delta_proj; lambda_proj]
+__global__ void pack_wtc(const float* __restrict__ Win, const float* __restrict__ dp, const float* __restrict__ lp,
+                         const float* __restrict__ WB, const float* __restrict__ WC, int R, int NR, int dim,
+                         __nv_bfloat16* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long Rt = R + 2 + 2LL * NR;
+    if (i >= Rt * dim) return;
+    const int row = (int)(i / dim), col = (int)(i - (long long)row * dim);
+    float v;
+    if (row < NR) v = WB[(long long)row * dim + col];
+    else if (row < 2 * NR) v = WC[(long long)(row - NR) * dim + col];
+    else if (row < 2 * NR + R) v = Win[(long long)(row - 2 * NR) * dim + col];
+    else if (row == 2 * NR + R) v = dp[col];
+    else v = lp[col];
+    out[i] = __float2bfloat16_rn(v);
+}
+
+bool tmap_encode_ex(CUtensorMap* m, const void* base, int dtype, int rank, const unsigned long long* dims,
+                    const unsigned long long* strides_bytes, const unsigned* box, int swizzle);
+
+// Returns cudaErrorNotSupported when the shapes do not fit this kernel.
+// W: bf16 scratch of Rt x dim for the reordered weights.
+cudaError_t launch_proj_fwd_tc(const __nv_bfloat16* X, const float* Win, const float* dp, const float* lp,
+                               const float* WB, const float* WC, __nv_bfloat16* W, long long BL, int dim, int R,
+                               int NR, float dt_min, float dt_max, const float* bB, const float* bC, float* P,
+                               __nv_bfloat16* u, __nv_bfloat16* dt, __nv_bfloat16* lam, __nv_bfloat16* B,
+                               __nv_bfloat16* C, int* status, cudaStream_t st) {
+    const int Rt = R + 2 + 2 * NR;
+    if (dim % 64 != 0 || NR % 16 != 0 || R + 2 > 16 || ((uintptr_t)X & 15) || ((uintptr_t)W & 15) ||
+        ((uintptr_t)B & 15) || ((uintptr_t)C & 15) || BL < 1)
+        return cudaErrorNotSupported;
+    pack_wtc<<<(unsigned)(((long long)Rt * dim + 255) / 256), 256, 0, st>>>(Win, dp, lp, WB, WC, R, NR, dim, W);
+    ProjTCDesc d{};
+    d.BL = BL; d.dim = dim; d.R = R; d.NR = NR; d.Rt = Rt;
+    const int rt_pad = (Rt + 15) & ~15;
+    d.ncols_max = rt_pad <= 512 ? rt_pad : 512;
+    d.x_bytes = 128 * 128;
+    d.stage_bytes = d.x_bytes + d.ncols_max * 128;
+    d.stages = (200 * 1024) / d.stage_bytes;
+    if (d.stages > 4) d.stages = 4;
+    if (d.stages < 2) return cudaErrorNotSupported;
+    d.dt_min = dt_min; d.dt_max = dt_max; d.bB = bB; d.bC = bC; d.P = P;
+    d.u = u; d.dt = dt; d.lam = lam; d.B = B; d.C = C; d.status = status;
+    CUtensorMap mX, mW;
+    {
+        const unsigned long long dims[2] = {(unsigned long long)dim, (unsigned long long)BL};
+        const unsigned long long str[1] = {(unsigned long long)dim * 2};
+        const unsigned box[2] = {64, 128};
+        if (!tmap_encode_ex(&mX, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorNotSupported;
+    }
+    {
+        const unsigned long long dims[2] = {(unsigned long long)dim, (unsigned long long)Rt};
+        const unsigned long long str[1] = {(unsigned long long)dim * 2};
+        const unsigned box[2] = {64, PTC_WROWS};
+        if (!tmap_encode_ex(&mW, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorNotSupported;
+    }
+    const int smem = 1024 + d.stages * d.stage_bytes + (2 * d.stages + 1) * 8 + 16;
+    cudaError_t e = cudaFuncSetAttribute(proj_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((unsigned)((BL + 127) / 128), (unsigned)((rt_pad + d.ncols_max - 1) / d.ncols_max));
+    proj_fwd_tc<<<grid, PTC_THREADS, smem, st>>>(d, mX, mW);
+    return cudaGetLastError();
+}
+
+}  // namespace kmb

@@ -379,8 +379,9 @@ static PFN_encodeTiled get_encode() {
     return fn;
 }
 
-bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long long* dims,
-                   const unsigned long long* strides_bytes, const unsigned* box) {
+// Tiled tensor map of any element type and swizzle (no interleave; OOB elements read as zero)
+bool tmap_encode_ex(CUtensorMap* m, const void* base, int dtype, int rank, const unsigned long long* dims,
+                    const unsigned long long* strides_bytes, const unsigned* box, int swizzle) {
     PFN_encodeTiled fn = get_encode();
     if (!fn) return false;
     cuuint64_t gd[5], gs[4];
@@ -391,10 +392,16 @@ bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long
         es[i] = 1;
         if (i < rank - 1) gs[i] = strides_bytes[i];
     }
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx,
-                    es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(m, (CUtensorMapDataType)dtype, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long long* dims,
+                 const unsigned long long* strides_bytes, const unsigned* box) {
+    return tmap_encode_ex(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, dims, strides_bytes, box,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 

@@ -80,6 +80,13 @@ size_t kmb_block_activation_floats(const KMBlockConfig *c, long batch);
  * delta_proj.x), dt_min, dt_max), lambda = sigmoid(lambda_proj.x), B = W_B x + b_B,
  * C = W_C x + b_C, block scan, out = x + W_out y.  Projections are fp32 cuBLAS
  * GEMMs (no TF32).  act: kmb_block_activation_floats() floats. */
+/* bf16 storage: 1 (default) = block projections on the tensor cores with the
+ * input epilogue fused (tcgen05); 0 = cuBLAS GEMMs and separate epilogues.
+ * Per host thread; for comparison and tests. */
+void kmb_block_set_tensor_cores(int on);
+/* Projection used by this thread's last bf16 block forward: 1 = tensor cores,
+ * 0 = cuBLAS, -1 = none yet. */
+int kmb_block_last_projection_path(void);
 int kmb_block_forward(const KMBlockConfig *c, const KMBlockWeights *w, const float *x, float *out,
                       long batch, float *act, void *stream);
 

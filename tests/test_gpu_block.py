@@ -192,3 +192,47 @@ def test_reference_block_abi(kmb, cuda, dims, dim, N, R, keep_bu, alias):
     for k in ("W_in", "W_out", "A_log", "W_B", "W_C", "delta_proj", "theta", "lambda_proj"):
         assert torch.equal(G_ref[k], G_own[k]), k
     assert torch.equal(dx_ref, dx_own)
+
+
+@pytest.mark.parametrize("dims,dim,N,R,batch", [([64, 64], 512, 64, 2, 2), ([5, 7], 64, 64, 2, 3),
+                                                ([16, 16], 128, 64, 4, 2), ([4, 6], 64, 8, 1, 1)])
+def test_block_tensor_core_projection(kmb, cuda, dims, dim, N, R, batch):
+    """bf16 block forward: the tcgen05 projection with the fused epilogue against
+    the cuBLAS bf16 GEMM + separate epilogue (same bf16 operands, fp32
+    accumulation; only the summation order differs).  Covers a partial last
+    row tile (BL % 128 != 0), the 256 + 16 column split (Rt = 260), two
+    column ranges per row tile (Rt = 518 > 512), and the cuBLAS fallback when
+    N R is not a multiple of 16."""
+    import torch
+    params = po.gen_block_params(dim, N, R, seed=5)
+    L = int(np.prod(dims))
+    x = torch.from_numpy(np.random.default_rng(6).standard_normal((batch, L, dim)).astype(np.float32))
+    xb = x.to(cuda).to(torch.bfloat16)
+    W = {k: torch.from_numpy(v).to(cuda) for k, v in params.items()}
+    cfg = kmb.block_config(dims, dim, N, R, bf16=True)
+    w = kmb.KMBlockWeights(**{k: W[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+    lib = kmb.lib()
+    nact = lib.kmb_block_activation_floats(C.byref(cfg), batch)
+    res = {}
+    for tc in (1, 0):
+        lib.kmb_block_set_tensor_cores(tc)
+        act = torch.zeros(nact, device=cuda)
+        out = torch.empty_like(xb)
+        kmb.check(lib.kmb_block_forward(C.byref(cfg), C.byref(w), xb.data_ptr(), out.data_ptr(), batch,
+                                        act.data_ptr(), None), "bf16 block forward")
+        torch.cuda.synchronize()
+        assert lib.kmb_device_status(None) == 0
+        # N R % 16 != 0 has no tensor-core layout: the cuBLAS path runs either way
+        assert lib.kmb_block_last_projection_path() == (tc if (N * R) % 16 == 0 else 0)
+        res[tc] = (out.float().cpu(), act.cpu())
+    lib.kmb_block_set_tensor_cores(1)
+    o1, a1 = res[1]
+    o0, a0 = res[0]
+    BL, Rt, NR = batch * L, R + 2 + 2 * N * R, N * R
+    # pre-activations of the u / dt / lambda columns (fp32, summation order only)
+    P1 = a1[:BL * Rt].view(BL, Rt)[:, :R + 2]
+    P0 = a0[:BL * Rt].view(BL, Rt)[:, :R + 2]
+    torch.testing.assert_close(P1, P0, rtol=1e-4, atol=1e-4)
+    # the bf16 scan inputs and the block output: within one bf16 rounding step
+    torch.testing.assert_close(o1, o0, rtol=1.6e-2, atol=1e-2)
+    assert torch.isfinite(o1).all()
