@@ -96,22 +96,28 @@ __global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restr
                                    const T* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
                                    float dt_max, const float* __restrict__ du, const float* __restrict__ ddt,
                                    const float* __restrict__ dlam, const float* __restrict__ dB,
-                                   const float* __restrict__ dC, O* __restrict__ dP) {
+                                   const float* __restrict__ dC, O* __restrict__ dP, int ldo) {
+    // dP rows have ldo >= Rt columns; columns Rt .. ldo-1 are written as zero
     const long long Rt = R + 2 + 2LL * NR;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= BL * Rt) return;
+    if (i >= BL * ldo) return;
     // 32-bit division when the index fits (the common case), 64-bit otherwise
-    const long long row = BL * Rt <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)Rt) : i / Rt;
-    const int col = (int)(i - row * Rt);
+    const long long row = BL * ldo <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)ldo) : i / ldo;
+    const int col = (int)(i - row * ldo);
+    if (col >= Rt) {
+        stv(dP + i, 0.0f);
+        return;
+    }
+    const long long ip = row * Rt + col;   // index into P
     float g;
     if (col < R) {
-        const float z = P[i], s = sigm(z);
+        const float z = P[ip], s = sigm(z);
         g = du[row * R + col] * s * (1.0f + z * (1.0f - s));          // silu'
     } else if (col == R) {
         // clamp test on the unrounded softplus (identical to the stored dt in fp32 mode)
-        const float d = fminf(fmaxf(logf(1.0f + expf(P[i])), dt_min), dt_max);
+        const float d = fminf(fmaxf(logf(1.0f + expf(P[ip])), dt_min), dt_max);
         (void)dtv;
-        g = (d > dt_min && d < dt_max) ? ddt[row] * sigm(P[i]) : 0.0f;  // softplus' inside the clamp
+        g = (d > dt_min && d < dt_max) ? ddt[row] * sigm(P[ip]) : 0.0f;  // softplus' inside the clamp
     } else if (col == R + 1) {
         const float l = ldv(lamv + row);
         g = dlam[row] * l * (1.0f - l);
@@ -202,6 +208,10 @@ cudaError_t launch_proj_fwd_tc(const __nv_bfloat16* X, const float* Win, const f
 // 1: route the bf16 projections through cuBLAS + separate epilogues (tests / comparison)
 static thread_local int tl_no_tc = 0;
 static thread_local int tl_proj_path = -1;  // projection of the last bf16 forward: 1 tensor cores, 0 cuBLAS
+static thread_local int tl_dx_path = -1;    // dx GEMM of the last bf16 backward: 1 tensor cores, 0 cuBLAS
+cudaError_t launch_dx_tc(const __nv_bfloat16* dP, int ldp, const float* Win, const float* dp, const float* lp,
+                         const float* WB, const float* WC, __nv_bfloat16* Wt, long long BL, int dim, int R, int NR,
+                         const __nv_bfloat16* dout, __nv_bfloat16* dx, int* status, cudaStream_t st);
 
 static thread_local std::map<int, cublasHandle_t> tl_cublas;
 static cublasHandle_t cublas_for(cudaStream_t st) {
@@ -255,6 +265,7 @@ extern "C" size_t kmb_block_activation_floats(const KMBlockConfig* c, long batch
 
 extern "C" void kmb_block_set_tensor_cores(int on) { tl_no_tc = on ? 0 : 1; }
 extern "C" int kmb_block_last_projection_path(void) { return tl_proj_path; }
+extern "C" int kmb_block_last_dx_path(void) { return tl_dx_path; }
 
 extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w, const float* x, float* out,
                                  long batch, float* act, void* stream) {
@@ -388,7 +399,7 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     block_bwd_epilogue<float, float><<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
                                                                     (int)NR, c->dt_min, c->dt_max, S + s_du,
                                                                     S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
-                                                                    S + s_dP);
+                                                                    S + s_dP, (int)Rt);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
     // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
     if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, &one, x, dim, S + s_dP, (int)Rt, &zero,
@@ -461,9 +472,10 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     auto take = [&](size_t n) { size_t r = o; o += (n + 63) & ~(size_t)63; return r; };
     const size_t s_dy = take(BL * R), s_du = take(BL * R), s_ddt = take(BL), s_dlam = take(BL);
     const size_t s_dB = take(BL * NR), s_dC = take(BL * NR), s_G = take(Rt * dim), s_one = take(BL);
+    const int ldp = (int)((Rt + 15) & ~15LL);   // dP row stride (16-byte rows, zero padding) for TMA
     const size_t s_D = dx ? take(BL * dim) : 0;
-    const size_t s_dP = take((BL * Rt + 1) / 2), s_yb = take((BL * R + 1) / 2), s_wo = take((dim * R + 1) / 2);
-    const size_t s_wb = take((Rt * dim + 1) / 2);
+    const size_t s_dP = take((BL * ldp + 1) / 2), s_yb = take((BL * R + 1) / 2), s_wo = take((dim * R + 1) / 2);
+    const size_t s_wb = take(((size_t)ldp * dim + 1) / 2);
     float* S = (float*)workspace(WS_BLK_SCRATCH, o * sizeof(float));
     if (!S) return set_error("workspace allocation failed");
     H *dPb = (H*)(S + s_dP), *yb = (H*)(S + s_yb), *wob = (H*)(S + s_wo), *Wb = (H*)(S + s_wb);
@@ -490,12 +502,12 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
     if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
-    block_bwd_epilogue<H, H><<<nb(BL * Rt, 256), 256, 0, st>>>(
+    block_bwd_epilogue<H, H><<<nb(BL * ldp, 256), 256, 0, st>>>(
         act + a.proj, (const H*)(act + a.dt), (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max,
-        S + s_du, S + s_ddt, S + s_dlam, S + s_dB, S + s_dC, dPb);
+        S + s_du, S + s_ddt, S + s_dlam, S + s_dB, S + s_dC, dPb, ldp);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
     // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
-    if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, x, dim, dPb, (int)Rt, 0.0f, S + s_G, dim) !=
+    if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, x, dim, dPb, ldp, 0.0f, S + s_G, dim) !=
         CUBLAS_STATUS_SUCCESS)
         return set_error("dWcat GEMM failed");
     block_scatter_grads<<<nb(Rt * dim, 256), 256, 0, st>>>(S + s_G, R, (int)NR, dim, g->W_in, g->delta_proj,
@@ -513,13 +525,27 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
             return set_error("db_C GEMV failed");
     }
     if (dx) {
-        float* W = pack_wcat(c, w, st);
-        if (!W) return set_error("kmb_block_backward: weight packing failed");
-        to_bf16<<<nb(Rt * dim, 256), 256, 0, st>>>(W, Wb, Rt * dim);
-        if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, Wb, dim, dPb, (int)Rt, 0.0f, S + s_D,
-                      dim) != CUBLAS_STATUS_SUCCESS)
-            return set_error("dx GEMM failed");
-        residual_bf16<<<nb((BL * dim + 7) / 8, 256), 256, 0, st>>>(dout, S + s_D, dx, BL * dim);
+        // dx = dout + dP Wcat: tensor cores with the residual fused (tcgen05), else cuBLAS + residual kernel
+        int* status = device_status();
+        if (status && !tl_no_tc) {
+            cudaMemsetAsync(status, 0, sizeof(int), st);
+            e = launch_dx_tc(dPb, ldp, w->W_in, w->delta_proj, w->lambda_proj, w->W_B, w->W_C, Wb, BL, dim, R,
+                             (int)NR, dout, dx, status, st);
+            if (e != cudaSuccess && e != cudaErrorNotSupported) return set_cuda_error("tensor-core dx", e);
+        } else {
+            e = cudaErrorNotSupported;
+        }
+        tl_dx_path = e == cudaSuccess ? 1 : 0;
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            float* W = pack_wcat(c, w, st);
+            if (!W) return set_error("kmb_block_backward: weight packing failed");
+            to_bf16<<<nb(Rt * dim, 256), 256, 0, st>>>(W, Wb, Rt * dim);
+            if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, Wb, dim, dPb, ldp, 0.0f, S + s_D,
+                          dim) != CUBLAS_STATUS_SUCCESS)
+                return set_error("dx GEMM failed");
+            residual_bf16<<<nb((BL * dim + 7) / 8, 256), 256, 0, st>>>(dout, S + s_D, dx, BL * dim);
+        }
     }
     e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("bf16 backward", e);

@@ -26,9 +26,15 @@
 
 namespace kmb {
 
+// D[row, c] = sum_k A[row, k] Bm[c, k] over K, for N output columns, then one of
+// two epilogues: EPI 0 = the block's input projection (above), EPI 1 = the
+// input gradient of the block, dx = bf16(dout + D) (row stride N).
 struct ProjTCDesc {
     long long BL;
-    int dim, R, NR, Rt, ncols_max;   // ncols_max: columns one CTA covers (<= 512, multiple of 16)
+    int K, N;                         // reduction length, output columns
+    int R, NR, Rt, ncols_max;         // ncols_max: columns one CTA covers (<= 512, multiple of 16)
+    const __nv_bfloat16* dout;        // EPI 1
+    __nv_bfloat16* dx;
     int stages, stage_bytes, x_bytes;
     float dt_min, dt_max;
     const float *bB, *bC;
@@ -81,6 +87,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 constexpr int PTC_THREADS = 192;
 constexpr int PTC_WROWS = 16;   // rows of Wcat per TMA box
 
+template <int EPI>
 __global__ void __launch_bounds__(PTC_THREADS, 1)
 proj_fwd_tc(const __grid_constant__ ProjTCDesc d, const __grid_constant__ CUtensorMap mX,
             const __grid_constant__ CUtensorMap mW) {
@@ -95,9 +102,9 @@ proj_fwd_tc(const __grid_constant__ ProjTCDesc d, const __grid_constant__ CUtens
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long m0 = (long long)blockIdx.x * 128;
     const int n0 = blockIdx.y * d.ncols_max;
-    const int ncols = min(d.ncols_max, ((d.Rt + 15) & ~15) - n0);   // multiple of 16
+    const int ncols = min(d.ncols_max, ((d.N + 15) & ~15) - n0);   // multiple of 16
     const int nch0 = min(ncols, 256), nch1 = ncols - nch0;
-    const int nkb = d.dim / 64;
+    const int nkb = (d.K + 63) / 64;
     const int tcols = ncols <= 32 ? 32 : ncols <= 64 ? 64 : ncols <= 128 ? 128 : ncols <= 256 ? 256 : 512;
 
     if (threadIdx.x == 0) {
@@ -179,6 +186,19 @@ proj_fwd_tc(const __grid_constant__ ProjTCDesc d, const __grid_constant__ CUtens
             tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
             if (!got || row >= d.BL) continue;
             const int col = n0 + c;
+            if constexpr (EPI == 1) {
+                // dx = bf16(dout + D): 16 columns, two 16-byte loads and stores (dx may alias dout)
+                const long long o = row * d.N + col;
+                uint4 pk[2];
+                pk[0] = ((const uint4*)(d.dout + o))[0];
+                pk[1] = ((const uint4*)(d.dout + o))[1];
+                __nv_bfloat16* e = (__nv_bfloat16*)pk;
+#pragma unroll
+                for (int j = 0; j < 16; j++) e[j] = __float2bfloat16_rn(__bfloat162float(e[j]) + v[j]);
+                ((uint4*)(d.dx + o))[0] = pk[0];
+                ((uint4*)(d.dx + o))[1] = pk[1];
+                continue;
+            }
             if (col < 2 * NR) {
                 // 16 columns of B or C: bias, round, two 16-byte stores
                 const bool isB = col < NR;
@@ -238,6 +258,75 @@ bool tmap_encode_ex(CUtensorMap* m, const void* base, int dtype, int rank, const
                     const unsigned long long* strides_bytes, const unsigned* box, int swizzle);
 
 // Returns cudaErrorNotSupported when the shapes do not fit this kernel.
+// Wt[dim, ldp] bf16 = Wcat^T (Wcat = [W_in; delta_proj; lambda_proj; W_B; W_C], [Rt, dim]); columns
+// Rt .. ldp-1 are zero
+__global__ void pack_wcat_t(const float* __restrict__ Win, const float* __restrict__ dp, const float* __restrict__ lp,
+                            const float* __restrict__ WB, const float* __restrict__ WC, int R, int NR, int dim,
+                            int ldp, __nv_bfloat16* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)dim * ldp) return;
+    const int n = (int)(i / ldp), c = (int)(i - (long long)n * ldp);
+    float v = 0.0f;
+    if (c < R) v = Win[(long long)c * dim + n];
+    else if (c == R) v = dp[n];
+    else if (c == R + 1) v = lp[n];
+    else if (c < R + 2 + NR) v = WB[(long long)(c - R - 2) * dim + n];
+    else if (c < R + 2 + 2 * NR) v = WC[(long long)(c - R - 2 - NR) * dim + n];
+    out[i] = __float2bfloat16_rn(v);
+}
+
+// Stage sizing, tensor maps and launch shared by both epilogues.  A [M, K] and
+// Bm [N, K] are bf16, K-major, with row strides lda / ldb elements.
+template <int EPI>
+static cudaError_t tc_launch(ProjTCDesc& d, const __nv_bfloat16* A, int lda, const __nv_bfloat16* Bm, int ldb,
+                             cudaStream_t st) {
+    if (((uintptr_t)A & 15) || ((uintptr_t)Bm & 15) || (lda % 8) || (ldb % 8) || d.BL < 1 || d.K < 1 || d.N < 16)
+        return cudaErrorNotSupported;
+    const int npad = (d.N + 15) & ~15;
+    d.ncols_max = npad <= 512 ? npad : 512;
+    d.x_bytes = 128 * 128;
+    d.stage_bytes = d.x_bytes + d.ncols_max * 128;
+    d.stages = (200 * 1024) / d.stage_bytes;
+    if (d.stages > 4) d.stages = 4;
+    if (d.stages < 2) return cudaErrorNotSupported;
+    CUtensorMap mA, mB;
+    {
+        const unsigned long long dims[2] = {(unsigned long long)d.K, (unsigned long long)d.BL};
+        const unsigned long long str[1] = {(unsigned long long)lda * 2};
+        const unsigned box[2] = {64, 128};
+        if (!tmap_encode_ex(&mA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorNotSupported;
+    }
+    {
+        const unsigned long long dims[2] = {(unsigned long long)d.K, (unsigned long long)d.N};
+        const unsigned long long str[1] = {(unsigned long long)ldb * 2};
+        const unsigned box[2] = {64, PTC_WROWS};
+        if (!tmap_encode_ex(&mB, Bm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorNotSupported;
+    }
+    const int smem = 1024 + d.stages * d.stage_bytes + (2 * d.stages + 1) * 8 + 16;
+    cudaError_t e = cudaFuncSetAttribute(proj_fwd_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((unsigned)((d.BL + 127) / 128), (unsigned)((npad + d.ncols_max - 1) / d.ncols_max));
+    proj_fwd_tc<EPI><<<grid, PTC_THREADS, smem, st>>>(d, mA, mB);
+    return cudaGetLastError();
+}
+
+// dx[BL, dim] = bf16(dout + dP Wcat) for the bf16 block backward.  dP is [BL, ldp]
+// bf16 with zero columns Rt .. ldp-1; Wt is bf16 scratch of dim x ldp.
+cudaError_t launch_dx_tc(const __nv_bfloat16* dP, int ldp, const float* Win, const float* dp, const float* lp,
+                         const float* WB, const float* WC, __nv_bfloat16* Wt, long long BL, int dim, int R, int NR,
+                         const __nv_bfloat16* dout, __nv_bfloat16* dx, int* status, cudaStream_t st) {
+    if (dim % 16 != 0 || ((uintptr_t)dout & 15) || ((uintptr_t)dx & 15) || ((uintptr_t)Wt & 15))
+        return cudaErrorNotSupported;
+    ProjTCDesc d{};
+    d.BL = BL; d.K = ldp; d.N = dim; d.R = R; d.NR = NR; d.Rt = R + 2 + 2 * NR;
+    d.dout = dout; d.dx = dx; d.status = status;
+    pack_wcat_t<<<(unsigned)(((long long)dim * ldp + 255) / 256), 256, 0, st>>>(Win, dp, lp, WB, WC, R, NR, dim, ldp,
+                                                                               Wt);
+    return tc_launch<1>(d, dP, ldp, Wt, ldp, st);
+}
+
 // W: bf16 scratch of Rt x dim for the reordered weights.
 cudaError_t launch_proj_fwd_tc(const __nv_bfloat16* X, const float* Win, const float* dp, const float* lp,
                                const float* WB, const float* WC, __nv_bfloat16* W, long long BL, int dim, int R,
@@ -245,42 +334,15 @@ cudaError_t launch_proj_fwd_tc(const __nv_bfloat16* X, const float* Win, const f
                                __nv_bfloat16* u, __nv_bfloat16* dt, __nv_bfloat16* lam, __nv_bfloat16* B,
                                __nv_bfloat16* C, int* status, cudaStream_t st) {
     const int Rt = R + 2 + 2 * NR;
-    if (dim % 64 != 0 || NR % 16 != 0 || R + 2 > 16 || ((uintptr_t)X & 15) || ((uintptr_t)W & 15) ||
+    if (NR % 16 != 0 || R + 2 > 16 || ((uintptr_t)X & 15) || ((uintptr_t)W & 15) ||
         ((uintptr_t)B & 15) || ((uintptr_t)C & 15) || BL < 1)
         return cudaErrorNotSupported;
     pack_wtc<<<(unsigned)(((long long)Rt * dim + 255) / 256), 256, 0, st>>>(Win, dp, lp, WB, WC, R, NR, dim, W);
     ProjTCDesc d{};
-    d.BL = BL; d.dim = dim; d.R = R; d.NR = NR; d.Rt = Rt;
-    const int rt_pad = (Rt + 15) & ~15;
-    d.ncols_max = rt_pad <= 512 ? rt_pad : 512;
-    d.x_bytes = 128 * 128;
-    d.stage_bytes = d.x_bytes + d.ncols_max * 128;
-    d.stages = (200 * 1024) / d.stage_bytes;
-    if (d.stages > 4) d.stages = 4;
-    if (d.stages < 2) return cudaErrorNotSupported;
+    d.BL = BL; d.K = dim; d.N = Rt; d.R = R; d.NR = NR; d.Rt = Rt;
     d.dt_min = dt_min; d.dt_max = dt_max; d.bB = bB; d.bC = bC; d.P = P;
     d.u = u; d.dt = dt; d.lam = lam; d.B = B; d.C = C; d.status = status;
-    CUtensorMap mX, mW;
-    {
-        const unsigned long long dims[2] = {(unsigned long long)dim, (unsigned long long)BL};
-        const unsigned long long str[1] = {(unsigned long long)dim * 2};
-        const unsigned box[2] = {64, 128};
-        if (!tmap_encode_ex(&mX, X, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
-            return cudaErrorNotSupported;
-    }
-    {
-        const unsigned long long dims[2] = {(unsigned long long)dim, (unsigned long long)Rt};
-        const unsigned long long str[1] = {(unsigned long long)dim * 2};
-        const unsigned box[2] = {64, PTC_WROWS};
-        if (!tmap_encode_ex(&mW, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
-            return cudaErrorNotSupported;
-    }
-    const int smem = 1024 + d.stages * d.stage_bytes + (2 * d.stages + 1) * 8 + 16;
-    cudaError_t e = cudaFuncSetAttribute(proj_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    const dim3 grid((unsigned)((BL + 127) / 128), (unsigned)((rt_pad + d.ncols_max - 1) / d.ncols_max));
-    proj_fwd_tc<<<grid, PTC_THREADS, smem, st>>>(d, mX, mW);
-    return cudaGetLastError();
+    return tc_launch<0>(d, X, dim, W, dim, st);
 }
 
 }  // namespace kmb

@@ -87,6 +87,9 @@ void kmb_block_set_tensor_cores(int on);
 /* Projection used by this thread's last bf16 block forward: 1 = tensor cores,
  * 0 = cuBLAS, -1 = none yet. */
 int kmb_block_last_projection_path(void);
+/* dx GEMM of this thread's last bf16 block backward: 1 = tensor cores (residual
+ * fused), 0 = cuBLAS, -1 = none yet. */
+int kmb_block_last_dx_path(void);
 int kmb_block_forward(const KMBlockConfig *c, const KMBlockWeights *w, const float *x, float *out,
                       long batch, float *act, void *stream);
 

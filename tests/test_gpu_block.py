@@ -224,10 +224,25 @@ def test_block_tensor_core_projection(kmb, cuda, dims, dim, N, R, batch):
         assert lib.kmb_device_status(None) == 0
         # N R % 16 != 0 has no tensor-core layout: the cuBLAS path runs either way
         assert lib.kmb_block_last_projection_path() == (tc if (N * R) % 16 == 0 else 0)
-        res[tc] = (out.float().cpu(), act.cpu())
+        # backward: dx = dout + dP Wcat on the tensor cores (residual fused) or through cuBLAS
+        dout = torch.from_numpy(np.random.default_rng(7).standard_normal((batch, L, dim)).astype(np.float32))
+        db = dout.to(cuda).to(torch.bfloat16)
+        G = {k: torch.zeros_like(v) for k, v in W.items()}
+        g = kmb.KMBlockGrads(**{k: G[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+        dx = torch.empty_like(xb)
+        kmb.check(lib.kmb_block_backward(C.byref(cfg), C.byref(w), xb.data_ptr(), db.data_ptr(), dx.data_ptr(),
+                                         C.byref(g), batch, act.data_ptr(), None), "bf16 block backward")
+        torch.cuda.synchronize()
+        assert lib.kmb_device_status(None) == 0
+        assert lib.kmb_block_last_dx_path() == tc
+        res[tc] = (out.float().cpu(), act.cpu(), dx.float().cpu(), {k: v.cpu() for k, v in G.items()})
     lib.kmb_block_set_tensor_cores(1)
-    o1, a1 = res[1]
-    o0, a0 = res[0]
+    o1, a1, dx1, G1 = res[1]
+    o0, a0, dx0, G0 = res[0]
+    torch.testing.assert_close(dx1, dx0, rtol=1.6e-2, atol=1e-2)
+    for k in kmb.BLOCK_FIELDS:
+        rel = float(torch.linalg.norm(G1[k] - G0[k]) / max(float(torch.linalg.norm(G0[k])), 1e-30))
+        assert rel <= 2e-2, (k, rel)
     BL, Rt, NR = batch * L, R + 2 + 2 * N * R, N * R
     # pre-activations of the u / dt / lambda columns (fp32, summation order only)
     P1 = a1[:BL * Rt].view(BL, Rt)[:, :R + 2]
