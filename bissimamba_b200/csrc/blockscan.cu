@@ -132,8 +132,8 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
 #pragma unroll
             for (int r = 0; r < RM; r++) {
                 if (r < R) {
-                    const long long c = (long long)t * NR + r * N;
-                    d.u[r] = ldv(u + (long long)t * R + r);
+                    const int c = t * NR + r * N;
+                    d.u[r] = ldv(u + t * R + r);
                     d.b0[r] = h0ok ? ldv(Bp + c + n0) : 0.0f;
                     d.b1[r] = h1ok ? ldv(Bp + c + n1) : 0.0f;
                     d.c0[r] = h0ok ? ldv(Cp + c + n0) : 0.0f;
@@ -173,9 +173,9 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                 }
             } else {
                 for (int r = 0; r < R; r++) {
-                    const float ur = ldv(u + (long long)t * R + r);
-                    if (h0ok) bu0 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n0), ur, bu0);
-                    if (h1ok) bu1 = __fmaf_rn(ldv(Bp + (long long)t * NR + r * N + n1), ur, bu1);
+                    const float ur = ldv(u + t * R + r);
+                    if (h0ok) bu0 = __fmaf_rn(ldv(Bp + t * NR + r * N + n0), ur, bu0);
+                    if (h1ok) bu1 = __fmaf_rn(ldv(Bp + t * NR + r * N + n1), ur, bu1);
                 }
             }
             const float al0 = kmb_exp(dt * A0, s.fast), al1 = kmb_exp(dt * A1, s.fast);
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                 int np = 0;
                 for (int k = 0; k < s.nd; k++) {
                     if (idx[k] == 0) continue;
-                    const long long q = (long long)(t - s.strides[k]) * N;
+                    const int q = (t - s.strides[k]) * N;
                     const float p0 = h0ok ? h[q + n0] : 0.0f, p1 = h1ok ? h[q + n1] : 0.0f;
                     const float r0 = pair ? cth * p0 - sth * p1 : p0;
                     const float r1 = sth * p0 + cth * p1;
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                 // 1D recurrence (reference src/mamba_block.c:384-393)
                 float p0 = 0.0f, p1 = 0.0f, pb0 = 0.0f, pb1 = 0.0f;
                 if (t > 0) {
-                    const long long q = (long long)(t - 1) * N;
+                    const int q = (t - 1) * N;
                     if (h0ok) { p0 = h[q + n0]; pb0 = Bu[q + n0]; }
                     if (h1ok) { p1 = h[q + n1]; pb1 = Bu[q + n1]; }
                 }
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                 hn0 = __fmaf_rn(gm, bu0, __fmaf_rn(beta0, pb0, al0 * r0));
                 hn1 = __fmaf_rn(gm, bu1, __fmaf_rn(beta1, pb1, al1 * r1));
             }
-            const long long o = (long long)t * N;
+            const int o = t * N;
             if (w0) { h[o + n0] = hn0; Bu[o + n0] = bu0; }
             if (w1) { h[o + n1] = hn1; Bu[o + n1] = bu1; }
             auto emit_y = [&](int r, float c0v, float c1v) {
@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                 if (h0ok) part = c0v * hn0;
                 if (h1ok) part = __fmaf_rn(c1v, hn1, part);
                 part = group_sum<GP>(part);
-                if (act && ln.pl == 0) y[(long long)t * R + r] = part;
+                if (act && ln.pl == 0) y[t * R + r] = part;
             };
             if constexpr (RM > 0) {
 #pragma unroll
@@ -238,8 +238,8 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
                     if (r < R) emit_y(r, cur.c0[r], cur.c1[r]);
             } else {
                 for (int r = 0; r < R; r++)
-                    emit_y(r, h0ok ? ldv(Cp + (long long)t * NR + r * N + n0) : 0.0f,
-                           h1ok ? ldv(Cp + (long long)t * NR + r * N + n1) : 0.0f);
+                    emit_y(r, h0ok ? ldv(Cp + t * NR + r * N + n0) : 0.0f,
+                           h1ok ? ldv(Cp + t * NR + r * N + n1) : 0.0f);
             }
         }
         __syncthreads();
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
     float* y = (s.NG == 1 ? s.y : s.part + (long long)ln.g * s.batch * L * R) + b * L * R;
     float* ring_h = bs_ring;                          // [2][wmax][GP][2]
     float* ring_b = bs_ring + 2 * (size_t)wmax * GP * 2;
-    auto rix = [&](int buf, int pos) { return ((size_t)(buf * wmax + pos) * GP + pl) * 2; };
+    auto rix = [&](int buf, int pos) { return ((buf * wmax + pos) * GP + pl) * 2; };
     const int step = nw * Ln::PPW;
     auto load = [&](int lvl, int base, BSInR<RM, NDT>& d) {
         const int beg = s.lev_start[lvl];
@@ -304,8 +304,8 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
 #pragma unroll
         for (int r = 0; r < RM; r++) {
             const bool rr = r < R;
-            const long long c = (long long)t * NR + (rr ? r : 0) * N;
-            d.u[r] = rr ? ldv(u + (long long)t * R + r) : 0.0f;
+            const int c = t * NR + (rr ? r : 0) * N;
+            d.u[r] = rr ? ldv(u + t * R + r) : 0.0f;
             d.b0[r] = rr && h0ok ? ldv(Bp + c + n0) : 0.0f;
             d.b1[r] = rr && h1ok ? ldv(Bp + c + n1) : 0.0f;
             d.c0[r] = rr && h0ok ? ldv(Cp + c + n0) : 0.0f;
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
 #pragma unroll
                 for (int k = 0; k < NDT; k++) {
                     if (!((cur.nb >> k) & 1)) continue;
-                    const size_t q = rix(pb, cur.ppos[k]);
+                    const int q = rix(pb, cur.ppos[k]);
                     const float p0 = ring_h[q], p1 = ring_h[q + 1];
                     const float r0 = pair ? cth * p0 - sth * p1 : p0;
                     const float r1 = sth * p0 + cth * p1;
@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
                 // 1D recurrence (reference src/mamba_block.c:384-393)
                 float p0 = 0.0f, p1 = 0.0f, pb0 = 0.0f, pb1 = 0.0f;
                 if (cur.nb & 1) {
-                    const size_t q = rix(pb, cur.ppos[0]);
+                    const int q = rix(pb, cur.ppos[0]);
                     p0 = ring_h[q]; p1 = ring_h[q + 1];
                     pb0 = ring_b[q]; pb1 = ring_b[q + 1];
                 }
@@ -385,10 +385,10 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
             if (!h0ok) { hn0 = 0.0f; bu0 = 0.0f; }
             if (!h1ok) { hn1 = 0.0f; bu1 = 0.0f; }
             if (act) {
-                const size_t q = rix(cb, cur.pos);
+                const int q = rix(cb, cur.pos);
                 ring_h[q] = hn0; ring_h[q + 1] = hn1;
                 ring_b[q] = bu0; ring_b[q + 1] = bu1;
-                const long long o = (long long)t * N;
+                const int o = t * N;
                 if (h0ok) { h[o + n0] = hn0; Bu[o + n0] = bu0; }
                 if (h1ok) { h[o + n1] = hn1; Bu[o + n1] = bu1; }
             }
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
                 if (h0ok) part = cur.c0[r] * hn0;
                 if (h1ok) part = __fmaf_rn(cur.c1[r], hn1, part);
                 part = group_sum<GP>(part);
-                if (act && ln.pl == 0) y[(long long)t * R + r] = part;
+                if (act && ln.pl == 0) y[t * R + r] = part;
             }
         }
         __syncthreads();
@@ -440,6 +440,8 @@ __global__ void __launch_bounds__(512) blockscan_bwd_generic(BSDesc s, BSGrad g)
     const float* Bu = s.Bu + b * L * N;
     const float* dy = g.dy + b * L * R;
     float* G = g.G + b * L * N;
+    float* dBi = g.dB + b * L * NR;
+    float* dCi = g.dC + b * L * NR;
     // du / ddt / dlambda: accumulate in place (one group), or this group's partials
     const bool direct = s.NG == 1;
     const long long gofs = (long long)ln.g * s.batch;
@@ -479,8 +481,8 @@ __global__ void __launch_bounds__(512) blockscan_bwd_generic(BSDesc s, BSGrad g)
                 const int nps = npt + (idx[k] == 0 ? 1 : 0);
                 const float al0 = kmb_exp(dts * A0, s.fast), al1 = kmb_exp(dts * A1, s.fast);
                 const float coef = (1.0f - lams) * dts / (float)nps;
-                const float G0 = h0ok ? G[(long long)sp * N + n0] : 0.0f;
-                const float G1 = h1ok ? G[(long long)sp * N + n1] : 0.0f;
+                const float G0 = h0ok ? G[sp * N + n0] : 0.0f;
+                const float G1 = h1ok ? G[sp * N + n1] : 0.0f;
                 a0 += al0 * G0;
                 a1 += al1 * G1;
                 ab0 += coef * al0 * G0;
@@ -488,22 +490,22 @@ __global__ void __launch_bounds__(512) blockscan_bwd_generic(BSDesc s, BSGrad g)
             }
             float gh0 = pair ? cth * a0 + sth * a1 : a0;
             float gh1 = -sth * a0 + cth * a1;
-            const long long o = (long long)t * N;
+            const int o = t * N;
             const float ht0 = h0ok ? h[o + n0] : 0.0f, ht1 = h1ok ? h[o + n1] : 0.0f;
             if (pair && act) {
                 const float hat0 = cth * ht0 - sth * ht1, hat1 = sth * ht0 + cth * ht1;
                 gth += -a0 * hat1 + a1 * hat0;
             }
             for (int r = 0; r < R; r++) {
-                const float dyr = dy[(long long)t * R + r];
-                const long long c0 = (long long)t * NR + r * N;
+                const float dyr = dy[t * R + r];
+                const int c0 = t * NR + r * N;
                 if (h0ok) {
                     gh0 += ldv(Cp + c0 + n0) * dyr;
-                    if (act) g.dC[b * L * NR + c0 + n0] += dyr * ht0;
+                    if (act) dCi[c0 + n0] += dyr * ht0;
                 }
                 if (h1ok) {
                     gh1 += ldv(Cp + c0 + n1) * dyr;
-                    if (act) g.dC[b * L * NR + c0 + n1] += dyr * ht1;
+                    if (act) dCi[c0 + n1] += dyr * ht1;
                 }
             }
             if (x0) G[o + n0] = gh0;
@@ -512,21 +514,21 @@ __global__ void __launch_bounds__(512) blockscan_bwd_generic(BSDesc s, BSGrad g)
             const float gam = lam * dt;
             const float gbu0 = gam * gh0 + ab0, gbu1 = gam * gh1 + ab1;
             for (int r = 0; r < R; r++) {
-                const float ur = ldv(u + (long long)t * R + r);
-                const long long c0 = (long long)t * NR + r * N;
+                const float ur = ldv(u + t * R + r);
+                const int c0 = t * NR + r * N;
                 float part = 0.0f;
                 if (h0ok) {
-                    if (act) g.dB[b * L * NR + c0 + n0] += gbu0 * ur;
+                    if (act) dBi[c0 + n0] += gbu0 * ur;
                     part += gbu0 * ldv(Bp + c0 + n0);
                 }
                 if (h1ok) {
-                    if (act) g.dB[b * L * NR + c0 + n1] += gbu1 * ur;
+                    if (act) dBi[c0 + n1] += gbu1 * ur;
                     part += gbu1 * ldv(Bp + c0 + n1);
                 }
                 part = group_sum<GP>(part);
                 if (act && ln.pl == 0) {
-                    if (direct) du[(long long)t * R + r] += part;
-                    else du[(long long)t * R + r] = part;
+                    if (direct) du[t * R + r] += part;
+                    else du[t * R + r] = part;
                 }
             }
             float gdt = lam * (bu0 * gh0 + bu1 * gh1);
@@ -662,25 +664,25 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 const int sp = hs[k] ? t + strides[k] : t;
                 sdt[k] = ldv(dtp + sp);
                 slam[k] = lamp ? ldv(lamp + sp) : s.deflam;
-                sG0[k] = h0ok && hs[k] ? G[(long long)sp * N + n0] : 0.0f;
-                sG1[k] = h1ok && hs[k] ? G[(long long)sp * N + n1] : 0.0f;
+                sG0[k] = h0ok && hs[k] ? G[sp * N + n0] : 0.0f;
+                sG1[k] = h1ok && hs[k] ? G[sp * N + n1] : 0.0f;
                 hp[k] = idx[k] > 0;
-                const long long q = (long long)(hp[k] ? t - strides[k] : t) * N;
+                const int q = (hp[k] ? t - strides[k] : t) * N;
                 ph0[k] = h0ok ? h[q + n0] : 0.0f;
                 ph1[k] = h1ok ? h[q + n1] : 0.0f;
                 pb0[k] = h0ok ? Bu[q + n0] : 0.0f;
                 pb1[k] = h1ok ? Bu[q + n1] : 0.0f;
             }
-            const long long o = (long long)t * N;
+            const int o = t * N;
             const float ht0 = h0ok ? h[o + n0] : 0.0f, ht1 = h1ok ? h[o + n1] : 0.0f;
             const float bu0 = h0ok ? Bu[o + n0] : 0.0f, bu1 = h1ok ? Bu[o + n1] : 0.0f;
             float dyv[RM], uu[RM], c0[RM], c1[RM], b0[RM], b1[RM], odB0[RM], odB1[RM], odC0[RM], odC1[RM];
 #pragma unroll
             for (int r = 0; r < RM; r++) {
                 const bool rr = r < R;
-                const long long c = (long long)t * NR + (rr ? r : 0) * N;
-                dyv[r] = rr ? dy[(long long)t * R + r] : 0.0f;
-                uu[r] = rr ? ldv(u + (long long)t * R + r) : 0.0f;
+                const int c = t * NR + (rr ? r : 0) * N;
+                dyv[r] = rr ? dy[t * R + r] : 0.0f;
+                uu[r] = rr ? ldv(u + t * R + r) : 0.0f;
                 c0[r] = rr && h0ok ? ldv(Cp + c + n0) : 0.0f;
                 c1[r] = rr && h1ok ? ldv(Cp + c + n1) : 0.0f;
                 b0[r] = rr && h0ok ? ldv(Bp + c + n0) : 0.0f;
@@ -751,7 +753,7 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
 #pragma unroll
             for (int r = 0; r < RM; r++) {
                 if (r >= R) continue;
-                const long long c = (long long)t * NR + r * N;
+                const int c = t * NR + r * N;
                 if (x0) {
                     dC[c + n0] = odC0[r] + dyv[r] * ht0;
                     dB[c + n0] = odB0[r] + gbu0 * uu[r];
@@ -765,8 +767,8 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 if (h1ok) part += gbu1 * b1[r];
                 part = group_sum<GP>(part);
                 if (act && ln.pl == 0) {
-                    if (direct) du[(long long)t * R + r] += part;
-                    else du[(long long)t * R + r] = part;
+                    if (direct) du[t * R + r] += part;
+                    else du[t * R + r] = part;
                 }
             }
             gdt = group_sum<GP>(gdt);
@@ -928,7 +930,8 @@ static int bs_desc(const KMBlockScanParams* p, long batch, BSDesc* s, cudaStream
         }
         if (prod != p->L) return set_error("blockscan: product of dims != L");
     }
-    if (p->L > 0x7fffffffL) return set_error("blockscan: L too large");
+    if (p->L > 0x7fffffffL || (long long)p->L * p->N * p->R >= (1LL << 31))
+        return set_error("blockscan: L * N * R must be below 2^31 per item (32-bit indexing inside an item)");
     memset(s, 0, sizeof(*s));
     s->nd = p->ndims <= 1 ? 1 : (int)p->ndims;
     s->N = (int)p->N;
