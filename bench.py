@@ -338,7 +338,7 @@ def main():
         e2e = {"value": (UPDATES // BATCH) * eb * world * args.e2e_steps / dt, "unit": "state-updates/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                "ms_per_step": 1e3 * dt / args.e2e_steps, "batch_per_gpu": eb,
-               "path": "scannd_batched() with pinned host buffers (H2D inputs, kernel, D2H h and y)"}
+               "path": "scannd_batched() with pinned host buffers: H2D inputs, kernel, D2H h and y, pipelined by item chunks over three streams (PCIe-bound)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -274,6 +274,132 @@ int scannd_forward_async(ScanNDParams* p, long batch, void* stream) {
     return run_scan_fwd(s, (cudaStream_t)stream);
 }
 
+// Host-pointer batches of more than kPipeMinBytes: the batch is cut into chunks of
+// whole items and three device slots rotate over three streams, so the
+// host-to-device copy of chunk i+1, the kernel on chunk i and the device-to-host
+// copy of chunk i-1 run at the same time (the two copy directions use separate
+// copy engines).  Returns 1 when the call is too small to gain from it.
+static const size_t kPipeMinBytes = (size_t)256 << 20;
+struct PipeStreams {
+    cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
+    cudaEvent_t in[3] = {}, done[3] = {}, out[3] = {};
+    bool ok = false;
+};
+static thread_local std::map<int, PipeStreams> tl_pipe;
+
+static PipeStreams* pipe_streams() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    PipeStreams& ps = tl_pipe[dev];
+    if (!ps.ok) {
+        if (cudaStreamCreateWithFlags(&ps.h2d, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&ps.comp, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&ps.d2h, cudaStreamNonBlocking) != cudaSuccess)
+            return nullptr;
+        for (int i = 0; i < 3; i++)
+            if (cudaEventCreateWithFlags(&ps.in[i], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&ps.done[i], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&ps.out[i], cudaEventDisableTiming) != cudaSuccess)
+                return nullptr;
+        ps.ok = true;
+    }
+    return &ps;
+}
+
+static int scan_host_pipelined(ScanNDParams* p, long batch, const ScanDesc& s0) {
+    size_t one[9];
+    scan_sizes(p, 1, one);   // floats per item (A and theta are shared)
+    const size_t per_item = (one[0] + one[2] + one[3] + one[4] + one[5] + one[6] + one[8]) * 4;
+    if (batch < 2 || per_item * (size_t)batch < kPipeMinBytes) return 1;
+    // chunk: ~1/8 of the batch, at most ~2 GB of inputs and outputs, at least one item
+    long cb = batch / 8 > 0 ? batch / 8 : 1;
+    while (cb > 1 && per_item * (size_t)cb > ((size_t)2 << 30)) cb--;
+    PipeStreams* ps = pipe_streams();
+    if (!ps) return fail("stream creation failed");
+    // device: shared A / theta, then 3 slots of [x | B | C | delta | lambda | h | y] for cb items
+    const int in_ids[5] = {0, 2, 3, 4, 8}, out_ids[2] = {5, 6};
+    size_t soff[9] = {}, slot_bytes = 0;
+    for (int k : in_ids) { soff[k] = slot_bytes; slot_bytes += (one[k] * cb * 4 + 255) & ~(size_t)255; }
+    for (int k : out_ids) { soff[k] = slot_bytes; slot_bytes += (one[k] * cb * 4 + 255) & ~(size_t)255; }
+    const size_t shared_bytes = ((one[1] * 4 + 255) & ~(size_t)255) + ((one[7] * 4 + 255) & ~(size_t)255);
+    char* w = (char*)ws_get(WS_STAGE, shared_bytes + 3 * slot_bytes);
+    if (!w) return fail("workspace allocation failed");
+    float* dA = (float*)w;
+    float* dth = (float*)(w + ((one[1] * 4 + 255) & ~(size_t)255));
+    char* slots = w + shared_bytes;
+    cudaError_t e;
+    if ((e = cudaMemcpyAsync(dA, p->A, one[1] * 4, cudaMemcpyHostToDevice, ps->h2d)) != cudaSuccess)
+        return fail_cuda("H2D A", e);
+    if (p->theta && (e = cudaMemcpyAsync(dth, p->theta, one[7] * 4, cudaMemcpyHostToDevice, ps->h2d)) != cudaSuccess)
+        return fail_cuda("H2D theta", e);
+    int* status = status_word();
+    if (!status) return fail("workspace allocation failed");
+    if ((e = cudaMemsetAsync(status, 0, sizeof(int), ps->h2d)) != cudaSuccess) return fail_cuda("memset", e);
+    const void* hin[9] = {p->x, nullptr, p->B, p->C, p->delta, nullptr, nullptr, nullptr, p->lambda};
+    void* hout[9] = {nullptr, nullptr, nullptr, nullptr, nullptr, p->h, p->y, nullptr, nullptr};
+    const long nch = (batch + cb - 1) / cb;
+    int fast = -1;
+    for (long i = 0; i < nch; i++) {
+        const int sl = (int)(i % 3);
+        const long b0 = i * cb, nb = (b0 + cb <= batch) ? cb : batch - b0;
+        char* base = slots + (size_t)sl * slot_bytes;
+        // inputs: the slot is free once its previous results have left
+        if (i >= 3 && (e = cudaStreamWaitEvent(ps->h2d, ps->out[sl], 0)) != cudaSuccess) return fail_cuda("wait", e);
+        for (int k : in_ids) {
+            if (!hin[k] || !one[k]) continue;
+            if ((e = cudaMemcpyAsync(base + soff[k], (const char*)hin[k] + one[k] * 4 * b0, one[k] * 4 * nb,
+                                     cudaMemcpyHostToDevice, ps->h2d)) != cudaSuccess)
+                return fail_cuda("H2D", e);
+        }
+        if ((e = cudaEventRecord(ps->in[sl], ps->h2d)) != cudaSuccess) return fail_cuda("event", e);
+        // kernel
+        if ((e = cudaStreamWaitEvent(ps->comp, ps->in[sl], 0)) != cudaSuccess) return fail_cuda("wait", e);
+        ScanDesc s = s0;
+        s.batch = nb;
+        s.x = (const float*)(base + soff[0]);
+        s.A = dA;
+        s.B = (const float*)(base + soff[2]);
+        s.C = (const float*)(base + soff[3]);
+        s.delta = (const float*)(base + soff[4]);
+        s.lambda = p->lambda ? (const float*)(base + soff[8]) : nullptr;
+        s.theta = p->theta ? dth : nullptr;
+        s.h = (float*)(base + soff[5]);
+        s.y = (float*)(base + soff[6]);
+        cudaError_t ek = cudaErrorNotSupported;
+        if (!force_generic())
+            ek = (s.nd == 2) ? launch_scan_fwd_strips(s, status, ps->comp) : launch_scan_fwd_tma(s, status, ps->comp);
+        if (ek == cudaSuccess) {
+            fast = fast < 0 ? 1 : fast;
+        } else {
+            if (ek != cudaErrorNotSupported) return fail_cuda("scan_fwd (TMA path)", ek);
+            cudaGetLastError();
+            fast = 0;
+            if ((e = launch_scan_fwd_generic(s, ps->comp)) != cudaSuccess) return fail_cuda("scan_fwd_generic", e);
+        }
+        if ((e = cudaEventRecord(ps->done[sl], ps->comp)) != cudaSuccess) return fail_cuda("event", e);
+        // outputs
+        if ((e = cudaStreamWaitEvent(ps->d2h, ps->done[sl], 0)) != cudaSuccess) return fail_cuda("wait", e);
+        for (int k : out_ids) {
+            if ((e = cudaMemcpyAsync((char*)hout[k] + one[k] * 4 * b0, base + soff[k], one[k] * 4 * nb,
+                                     cudaMemcpyDeviceToHost, ps->d2h)) != cudaSuccess)
+                return fail_cuda("D2H", e);
+        }
+        if ((e = cudaEventRecord(ps->out[sl], ps->d2h)) != cudaSuccess) return fail_cuda("event", e);
+    }
+    if ((e = cudaStreamSynchronize(ps->d2h)) != cudaSuccess) return fail_cuda("synchronize", e);
+    if ((e = cudaStreamSynchronize(ps->comp)) != cudaSuccess) return fail_cuda("synchronize", e);
+    tl_fast_path = fast < 0 ? 0 : fast;
+    if (tl_fast_path == 1) {
+        int v = 0;
+        if (cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && v != 0) {
+            char buf[96];
+            snprintf(buf, sizeof buf, "device wait limit exceeded (status %d)", v);
+            return fail(buf);
+        }
+    }
+    return 0;
+}
+
 int scannd_batched(ScanNDParams* p, long batch) {
     if (!scannd_validate(p) || batch < 1) return fail("invalid ScanNDParams");
     const void* ptrs[] = {p->x, p->A, p->B, p->C, p->delta, p->h, p->y, p->theta, p->lambda};
@@ -286,6 +412,11 @@ int scannd_batched(ScanNDParams* p, long batch) {
         return sync_and_check(st);
     }
     if (kind != PK_HOST) return fail("mixed host/device pointers");
+    {
+        // large host batches: pipeline the copies against the kernel (and each other)
+        const int r = scan_host_pipelined(p, batch, s);
+        if (r != 1) return r;
+    }
     // host buffers: stage through the device workspace
     size_t sz[9];
     scan_sizes(p, batch, sz);

@@ -158,3 +158,36 @@ def test_backward_accumulates(kmb, cuda):
                       theta=d["theta"], grads={"dB": dB})
     k.check(k.lib().scannd_backward_batched(C.byref(p), 1, None))
     np.testing.assert_allclose(dB.cpu().numpy() - 1.0, g1["dB"], rtol=1e-5, atol=1e-5)
+
+
+def test_host_pointer_pipelined(kmb, cuda):
+    """A host-pointer batch above the pipelining threshold (4 items, ~0.8 GB) runs
+    as chunks over three device slots and streams (copy in / kernel / copy out
+    overlapped); h and y equal the device-pointer path bit for bit."""
+    import torch
+    g = torch.Generator().manual_seed(11)
+    b, H, W, D, M = 4, 64, 64, 64, 64
+    P = H * W
+    x = torch.randn(b, P, D, generator=g)
+    A = -torch.exp(torch.rand(2, D, M, generator=g) * np.log(16.0))
+    Bm = torch.randn(b, P, D, M, generator=g) / 4
+    Cm = torch.randn(b, P, D, M, generator=g) / 4
+    delta = torch.nn.functional.softplus(torch.randn(b, 2, P, D, generator=g) * 0.5 - 4)
+    theta = (torch.rand(D // 2, generator=g) * 2 - 1) * np.pi
+    lam = torch.sigmoid(torch.randn(b, P, generator=g))
+    host = {k: v.contiguous().pin_memory() for k, v in dict(x=x, A=A, B=Bm, C=Cm, delta=delta, theta=theta,
+                                                              lam=lam).items()}
+    hh = torch.zeros(b, P, D, M).pin_memory()
+    yh = torch.zeros(b, P, D).pin_memory()
+    p = kmb.scan_params([H, W], D, M, host["x"], host["A"], host["B"], host["C"], host["delta"], hh, yh,
+                        theta=host["theta"], lam=host["lam"])
+    assert kmb.lib().scannd_batched(C.byref(p), b) == 0, kmb.last_error()
+    assert kmb.lib().kmb_last_forward_path() == 1
+    dev = {k: v.to(cuda) for k, v in host.items()}
+    hd = torch.empty(b, P, D, M, device=cuda)
+    yd = torch.empty(b, P, D, device=cuda)
+    pd = kmb.scan_params([H, W], D, M, dev["x"], dev["A"], dev["B"], dev["C"], dev["delta"], hd, yd,
+                         theta=dev["theta"], lam=dev["lam"])
+    assert kmb.lib().scannd_batched(C.byref(pd), b) == 0, kmb.last_error()
+    assert torch.equal(hh, hd.cpu())
+    assert torch.equal(yh, yd.cpu())
