@@ -163,7 +163,7 @@ def cpu_reference_rate(target_s=3.0, max_total_s=25.0):
     full 64x64 grid and M, a channel slice sized to ~target_s per call."""
     import numpy as np
     from oracle import pyoracle as po
-    threads = po.set_threads(os.cpu_count() or 1)
+    threads = po.set_threads(len(os.sched_getaffinity(0)) or os.cpu_count() or 1)
     d_s = 16
     t = None
     while True:
@@ -192,7 +192,7 @@ def run_reference_arm(args, rank, world):
         return
     import numpy as np
     from oracle import pyoracle as po
-    threads = po.set_threads(os.cpu_count() or 1)
+    threads = po.set_threads(len(os.sched_getaffinity(0)) or os.cpu_count() or 1)
     d_s = 64
     inp = po.gen_scan(list(DIMS), d_s, M, batch=1, seed=3)
     t0 = time.perf_counter()
