@@ -41,8 +41,11 @@ struct WaveBwd {
     float *G, *pA, *pth, *plam;
 };
 
+// Two CTAs per SM (64 registers): the (item, channel-group) CTAs of a call are
+// resident at once instead of running in two waves, and each SM hides twice the
+// latency; the small register spill costs less than that gains.
 template <int ND, bool ROPE>
-__global__ void __launch_bounds__(512) scan_bwd_wave(WaveBwd w) {
+__global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
     const int D = w.D, M = w.M;
     const int ngroups = ROPE ? (D + 1) / 2 : D;
     const int b = blockIdx.x / ngroups, g = blockIdx.x % ngroups;
