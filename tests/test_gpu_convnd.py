@@ -74,3 +74,30 @@ def test_convnd_host_entry(kmb, cuda):
     np.testing.assert_allclose(out, ref["output"][0], rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(din, ref["dinput"][0], rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(dk, ref["dkernel"][0], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("dims,D,K,bias", [([1, 8], 8, 3, True), ([8, 1], 4, 3, False), ([1], 4, 3, True),
+                                           ([2, 3], 8, 4, True), ([2, 2, 2, 2], 4, 2, True), ([5, 6], 7, 3, True),
+                                           ([3, 3, 3], 4, 5, False), ([33], 12, 4, True)])
+def test_conv_degenerate_shapes(kmb, cuda, dims, D, K, bias):
+    """Size-1 axes, kernels wider than the grid (every tap out of range somewhere),
+    four dimensions, odd channel counts (generic kernels) and missing bias,
+    forward and backward against the restatement."""
+    inp = po.gen_conv(dims, D, K, batch=2, seed=len(dims) + K + D, bias=bias)
+    o, di, dk, db = _gpu_conv(kmb, cuda, inp)
+    ro, rdi, rdk, rdb = po.conv_run(inp, "oracle")
+    np.testing.assert_allclose(o, ro, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(di, rdi, rtol=1e-4, atol=1e-5)
+    scale = max(np.abs(rdk).max(), 1e-30)
+    np.testing.assert_allclose(dk, rdk, rtol=1e-4, atol=1e-5 * scale)
+    if bias:
+        np.testing.assert_allclose(db, rdb, rtol=1e-4, atol=1e-5 * max(np.abs(rdb).max(), 1e-30))
+
+
+def test_conv_rejects_invalid(kmb, cuda):
+    """Zero-sized axes, K = 0 and an empty batch are invalid arguments."""
+    import torch
+    z = torch.zeros(16, device=cuda)
+    for dims, K, batch in (([4, 0], 3, 1), ([4, 4], 0, 1), ([4, 4], 3, 0)):
+        p = kmb.conv_params(dims, 1, K, z, z, None, z, z, z, z, None)
+        assert kmb.lib().convnd_batched_async(C.byref(p), batch, 3, None) == -1

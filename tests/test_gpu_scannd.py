@@ -191,3 +191,77 @@ def test_host_pointer_pipelined(kmb, cuda):
     assert kmb.lib().scannd_batched(C.byref(pd), b) == 0, kmb.last_error()
     assert torch.equal(hh, hd.cpu())
     assert torch.equal(yh, yd.cpu())
+
+
+def test_headline_full_size(kmb, cuda):
+    """The full headline workload (2D 64x64, D 512, M 64, batch 32: 35 GB of
+    inputs, 17 GB of outputs) in one call.  Size-independent properties: every
+    (item, channel) recurrence is independent, so items recomputed alone equal
+    the same items of the batched call bit for bit; and the last channel tile
+    of the last item matches the oracle."""
+    import torch
+    from gpu_util import assert_scan_close
+    if torch.cuda.get_device_properties(0).total_memory < 80 * 2 ** 30:
+        pytest.skip("needs the B200's memory")
+    g = torch.Generator(device=cuda).manual_seed(5)
+    b, H, W, D, M = 32, 64, 64, 512, 64
+    P = H * W
+    rn = lambda *s: torch.randn(*s, generator=g, device=cuda)
+    x = rn(b, P, D)
+    delta = torch.nn.functional.softplus(rn(b, 2, P, D) * 0.5 - 4.0)
+    A = -torch.exp(torch.rand(2, D, M, generator=g, device=cuda) * np.log(16.0))
+    Bm = (rn(b, P, 1, M) * 0.25).expand(b, P, D, M).contiguous()
+    Cm = (rn(b, P, 1, M) * 0.25).expand(b, P, D, M).contiguous()
+    h = torch.empty(b, P, D, M, device=cuda)
+    y = torch.empty(b, P, D, device=cuda)
+    p = kmb.scan_params([H, W], D, M, x, A, Bm, Cm, delta, h, y)
+    kmb.check(kmb.lib().scannd_batched(C.byref(p), b), "full headline")
+    assert kmb.lib().kmb_last_forward_path() == 1
+    assert torch.isfinite(y).all()
+    for it in (0, 17, 31):
+        h1 = torch.empty(1, P, D, M, device=cuda)
+        y1 = torch.empty(1, P, D, device=cuda)
+        p1 = kmb.scan_params([H, W], D, M, x[it:it + 1], A, Bm[it:it + 1], Cm[it:it + 1], delta[it:it + 1], h1, y1)
+        kmb.check(kmb.lib().scannd_batched(C.byref(p1), 1), "single item")
+        assert torch.equal(h1[0], h[it]) and torch.equal(y1[0], y[it])
+    c0, it = 508, 31
+    sl = dict(dims=[H, W], D=4, M=M, batch=1, theta=None, use_fast_exp=0, use_a_log_clamp=0, a_log_min=-1e-5,
+              default_lambda=0.5)
+    sl["lambda"] = None
+    sl["x"] = x[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy()
+    sl["B"] = Bm[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy()
+    sl["C"] = Cm[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy()
+    sl["delta"] = delta[it:it + 1, :, :, c0:c0 + 4].contiguous().cpu().numpy()
+    sl["A"] = A[:, c0:c0 + 4].contiguous().cpu().numpy()
+    assert_scan_close(h[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy(),
+                      y[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy(), sl)
+
+
+@pytest.mark.parametrize("dims,D,M,flags", [([1, 64], 8, 16, {}), ([64, 1], 8, 16, dict(rope=True)),
+                                            ([1, 1], 4, 16, {}), ([1], 4, 8, dict(lam=True)),
+                                            ([2, 1, 3], 4, 4, dict(rope=True)), ([2, 2, 2, 2, 2], 4, 4, dict(lam=True)),
+                                            ([3, 70], 8, 16, {})])
+def test_degenerate_and_high_rank_shapes(kmb, cuda, dims, D, M, flags):
+    """Size-1 axes, a single point, five dimensions and an inner extent above 64
+    (generic kernel): forward against the oracle, backward against the exact adjoint."""
+    from gpu_util import scan_fwd, assert_scan_close
+    inp = po.gen_scan(dims, D, M, batch=2, seed=len(dims) * 7 + D, **flags)
+    h, y, _ = scan_fwd(inp, cuda)
+    assert_scan_close(h, y, inp)
+    _check_backward(dims, D, M, flags, cuda)
+
+
+def test_rejects_empty_and_zero_dims(kmb, cuda):
+    """Empty batches and zero-sized axes are invalid arguments (-1, message set), never a launch."""
+    import torch
+    inp = po.gen_scan([4, 4], 4, 4, batch=1, seed=1)
+    from gpu_util import to_dev
+    d = to_dev(inp, cuda)
+    h = torch.empty(1, 16, 4, 4, device=cuda)
+    y = torch.empty(1, 16, 4, device=cuda)
+    p = kmb.scan_params([4, 4], 4, 4, d["x"], d["A"], d["B"], d["C"], d["delta"], h, y)
+    assert kmb.lib().scannd_batched(C.byref(p), 0) == -1
+    assert kmb.last_error()
+    pz = kmb.scan_params([4, 0], 4, 4, d["x"], d["A"], d["B"], d["C"], d["delta"], h, y)
+    assert kmb.lib().scannd_validate(C.byref(pz)) == 0
+    assert kmb.lib().scannd_batched(C.byref(pz), 1) == -1
