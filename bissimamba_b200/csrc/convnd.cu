@@ -203,29 +203,89 @@ __global__ void __launch_bounds__(256) conv_tap_kernel(ConvDesc c, const float4*
                                                        const float4* __restrict__ bias, float4* __restrict__ dst) {
     // forward: dst[o] = bias + sum_k src[o - shift_k] * ker[k]
     // backward (dinput): dst[s] = sum_k src[s + shift_k] * ker[k]  (src = dy)
+    // 32-bit index arithmetic: batch * P * D/4 < 2^31 (checked by the launcher)
     using T = Taps<ND, K>;
-    const int D4 = c.D >> 2;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= c.batch * c.P * D4) return;
-    const int d4 = (int)(i % D4);
-    const long long bp = i / D4;
-    const long long p = bp % c.P;
+    const unsigned D4 = (unsigned)c.D >> 2, Pp = (unsigned)c.P;
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (unsigned)(c.batch * c.P) * D4) return;
+    const unsigned d4 = i % D4;
+    const unsigned bp = i / D4;
+    const unsigned p = bp % Pp;
     int oc[3];
-    long long st[3];
+    unsigned st[3];
 #pragma unroll
     for (int a = 0; a < ND; a++) {
-        st[a] = c.strides[a];
-        oc[a] = (int)((p / st[a]) % c.dims[a]);
+        st[a] = (unsigned)c.strides[a];
+        oc[a] = (int)((p / st[a]) % (unsigned)c.dims[a]);
     }
     float4 acc = BWD ? make_float4(0.f, 0.f, 0.f, 0.f) : (bias ? bias[d4] : make_float4(0.f, 0.f, 0.f, 0.f));
-    const float4* s = src + (bp - p) * D4;  // item base
+    const float4* s = src + (size_t)(bp - p) * D4;  // item base
 #pragma unroll
     for (int kl = 0; kl < T::V; kl++) {
         bool ok = true;
-        long long off = p;
+        int off = (int)p;
 #pragma unroll
         for (int a = 0; a < ND; a++) {
             const int sh = K - 1 - T::digit(kl, a);
+            if (BWD) {
+                ok = ok && (oc[a] + sh < (int)c.dims[a]);
+                off += sh * (int)st[a];
+            } else {
+                ok = ok && (oc[a] >= sh);
+                off -= sh * (int)st[a];
+            }
+        }
+        if (ok) fma4(acc, s[(unsigned)off * D4 + d4], ker[kl * D4 + d4]);
+    }
+    dst[i] = acc;
+}
+
+// Streaming stencil along the outermost axis (V = K^ND <= 27): thread = (item,
+// chunk of CH planes of axis 0, point of the remaining axes, 4 channels).  The K^ND
+// kernel taps of the thread's channels sit in registers; each plane of the input
+// (forward) or dy (backward, walked downwards) is loaded once as its K^(ND-1)
+// neighbours and added into K rotating accumulators, the outputs of the K planes
+// it reaches.  Loads per output fall from K^ND to K^(ND-1); the K-1 planes before
+// a chunk are read to warm the accumulators up.  Summation order per output:
+// by plane, then the remaining taps; fp32.
+template <int ND, int K, bool BWD, int CH>
+__global__ void __launch_bounds__(128) conv_stream_kernel(ConvDesc c, const float4* __restrict__ src,
+                                                          const float4* __restrict__ ker,
+                                                          const float4* __restrict__ bias, float4* __restrict__ dst,
+                                                          int nchunks) {
+    using T = Taps<ND, K>;
+    constexpr int TR = T::V / K;   // taps of the remaining axes
+    const int D4 = c.D >> 2;
+    const int P0 = (int)c.dims[0];
+    const long long Prest = c.P / P0;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= c.batch * nchunks * Prest * D4) return;
+    const int d4 = (int)(i % D4);
+    long long r = i / D4;
+    const long long pr = r % Prest;
+    r /= Prest;
+    const int chunk = (int)(r % nchunks);
+    const long long b = r / nchunks;
+    int oc[3] = {0, 0, 0}, st[3] = {1, 1, 1};
+#pragma unroll
+    for (int a = 1; a < ND; a++) {
+        st[a] = (int)c.strides[a];
+        oc[a] = (int)((pr / st[a]) % c.dims[a]);
+    }
+    float4 kv[T::V];
+#pragma unroll
+    for (int kl = 0; kl < T::V; kl++) kv[kl] = ker[(long long)kl * D4 + d4];
+    const float4 b0 = (!BWD && bias) ? bias[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    // the remaining-axes neighbour offsets of this point (in points), and which exist
+    int roff[TR];   // points per item < 2^31 (checked by the launcher)
+    bool rok[TR];
+#pragma unroll
+    for (int tr = 0; tr < TR; tr++) {
+        int off = (int)pr;
+        bool ok = true;
+#pragma unroll
+        for (int a = 1; a < ND; a++) {
+            const int sh = K - 1 - T::digit(tr, a);   // digit of the remaining axes (axis 0 digit is 0 here)
             if (BWD) {
                 ok = ok && (oc[a] + sh < c.dims[a]);
                 off += sh * st[a];
@@ -234,9 +294,36 @@ __global__ void __launch_bounds__(256) conv_tap_kernel(ConvDesc c, const float4*
                 off -= sh * st[a];
             }
         }
-        if (ok) fma4(acc, s[off * D4 + d4], ker[(long long)kl * D4 + d4]);
+        roff[tr] = ok ? off : 0;
+        rok[tr] = ok;
     }
-    dst[i] = acc;
+    const float4* s = src + b * c.P * D4;
+    float4* o = dst + b * c.P * D4;
+    const int lo = chunk * CH, hi = min(lo + CH, P0);   // outputs [lo, hi) of axis 0
+    float4 acc[K];
+#pragma unroll
+    for (int j = 0; j < K; j++) acc[j] = b0;
+    // forward walks planes lo-(K-1) .. hi-1 upwards; backward walks hi-1+(K-1) .. lo downwards
+    const int first = BWD ? min(hi - 1 + (K - 1), P0 - 1) : max(lo - (K - 1), 0);
+    const int last = BWD ? lo : hi - 1;
+    const int step = BWD ? -1 : 1;
+    for (int p0 = first;; p0 += step) {
+        const long long pbase = (long long)p0 * Prest;
+#pragma unroll
+        for (int tr = 0; tr < TR; tr++) {
+            if (!rok[tr]) continue;
+            const float4 v = s[(pbase + roff[tr]) * D4 + d4];
+#pragma unroll
+            for (int sh0 = 0; sh0 < K; sh0++) fma4(acc[sh0], v, kv[(K - 1 - sh0) * TR + tr]);
+        }
+        // the output on this plane is complete
+        const bool mine = BWD ? (p0 < hi) : (p0 >= lo);
+        if (mine) o[((long long)p0 * Prest + pr) * D4 + d4] = acc[0];
+#pragma unroll
+        for (int j = 0; j < K - 1; j++) acc[j] = acc[j + 1];
+        acc[K - 1] = b0;
+        if (p0 == last) break;
+    }
 }
 
 // dkernel / dbias partial sums: block = 32 float4 channel lanes x 8 row groups,
@@ -255,42 +342,43 @@ __global__ void __launch_bounds__(256) conv_dk_tap_kernel(ConvDesc c, const floa
     const int D4 = c.D >> 2;
     const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
     const int d4 = blockIdx.x * 32 + lane;
-    const long long r0 = (long long)blockIdx.y * rows_per_chunk;
-    const long long rows = c.batch * c.P;
-    const long long r1 = min(r0 + rows_per_chunk, rows);
-    long long st[3];
+    // 32-bit index arithmetic: batch * P * D/4 < 2^31 (checked by the launcher)
+    const unsigned r0 = (unsigned)(blockIdx.y * rows_per_chunk);
+    const unsigned rows = (unsigned)(c.batch * c.P), Pp = (unsigned)c.P;
+    const unsigned r1 = min(r0 + (unsigned)rows_per_chunk, rows);
+    unsigned st[3];
 #pragma unroll
-    for (int a = 0; a < ND; a++) st[a] = c.strides[a];
+    for (int a = 0; a < ND; a++) st[a] = (unsigned)c.strides[a];
 #pragma unroll 1
     for (int pass = 0; pass < NPASS; pass++) {
         float4 acc[TP + 1];
 #pragma unroll
         for (int t = 0; t <= TP; t++) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (d4 < D4) {
-            for (long long r = r0 + grp; r < r1; r += 8) {
-                const long long p = r % c.P;
+            for (unsigned r = r0 + grp; r < r1; r += 8) {
+                const unsigned p = r % Pp;
                 int oc[3];
 #pragma unroll
-                for (int a = 0; a < ND; a++) oc[a] = (int)((p / st[a]) % c.dims[a]);
+                for (int a = 0; a < ND; a++) oc[a] = (int)((p / st[a]) % (unsigned)c.dims[a]);
                 const float4 g = dy[r * D4 + d4];
                 if (pass == 0) {
                     acc[TP].x += g.x; acc[TP].y += g.y; acc[TP].z += g.z; acc[TP].w += g.w;
                 }
-                const float4* s = in + (r - p) * D4;
+                const float4* s = in + (size_t)(r - p) * D4;
                 const int sh0 = K - 1 - pass;  // shift of the outermost axis (NPASS == K)
                 if (NPASS > 1 && oc[0] < sh0) continue;
 #pragma unroll
                 for (int t = 0; t < TP; t++) {
                     const int kl = pass * TP + t;
                     bool ok = true;
-                    long long off = NPASS > 1 ? p - (long long)sh0 * st[0] : p;
+                    int off = NPASS > 1 ? (int)p - sh0 * (int)st[0] : (int)p;
 #pragma unroll
                     for (int a = (NPASS > 1 ? 1 : 0); a < ND; a++) {
                         const int sh = K - 1 - T::digit(kl, a);
                         ok = ok && (oc[a] >= sh);
-                        off -= sh * st[a];
+                        off -= sh * (int)st[a];
                     }
-                    if (ok) fma4(acc[t], g, s[off * D4 + d4]);
+                    if (ok) fma4(acc[t], g, s[(unsigned)off * D4 + d4]);
                 }
             }
         }
@@ -318,13 +406,28 @@ static cudaError_t conv_fast_impl(const ConvDesc& c, bool fwd, const float* in, 
                                   long long nch_max, cudaStream_t st) {
     const long long n4 = c.batch * c.P * (c.D / 4);
     const unsigned g4 = (unsigned)((n4 + 255) / 256);
+    // streaming along axis 0 for 1D / 2D; 3D keeps the per-output gather (measured faster there)
+    constexpr bool STREAM = ND <= 2 && Taps<ND, K>::V <= 27;
+    if (c.batch * c.P * (c.D / 4) >= (1LL << 31)) return cudaErrorNotSupported;   // 32-bit indexing
+    constexpr int CH = 8;   // planes of the outermost axis per thread
+    const int nchunks = (int)((c.dims[0] + CH - 1) / CH);
+    const long long ns = c.batch * nchunks * (c.P / c.dims[0]) * (c.D / 4);
+    const unsigned gs = (unsigned)((ns + 127) / 128);
     if (fwd) {
-        conv_tap_kernel<ND, K, false><<<g4, 256, 0, st>>>(c, (const float4*)in, (const float4*)ker,
-                                                          (const float4*)bias, (float4*)out);
+        if constexpr (STREAM)
+            conv_stream_kernel<ND, K, false, CH><<<gs, 128, 0, st>>>(c, (const float4*)in, (const float4*)ker,
+                                                                     (const float4*)bias, (float4*)out, nchunks);
+        else
+            conv_tap_kernel<ND, K, false><<<g4, 256, 0, st>>>(c, (const float4*)in, (const float4*)ker,
+                                                              (const float4*)bias, (float4*)out);
         return cudaGetLastError();
     }
-    conv_tap_kernel<ND, K, true><<<g4, 256, 0, st>>>(c, (const float4*)dy, (const float4*)ker, nullptr,
-                                                     (float4*)din);
+    if constexpr (STREAM)
+        conv_stream_kernel<ND, K, true, CH><<<gs, 128, 0, st>>>(c, (const float4*)dy, (const float4*)ker, nullptr,
+                                                                (float4*)din, nchunks);
+    else
+        conv_tap_kernel<ND, K, true><<<g4, 256, 0, st>>>(c, (const float4*)dy, (const float4*)ker, nullptr,
+                                                         (float4*)din);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const long long rows = c.batch * c.P;
