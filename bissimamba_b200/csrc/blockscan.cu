@@ -289,13 +289,25 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
     float* ring_b = bs_ring + 2 * (size_t)wmax * GP * 2;
     auto rix = [&](int buf, int pos) { return ((buf * wmax + pos) * GP + pl) * 2; };
     const int step = nw * Ln::PPW;
-    auto load = [&](int lvl, int base, BSInR<RM, NDT>& d) {
+    const int Lp = (int)L;
+    // Two-deep prefetch: the point id of the task after next is read one task
+    // earlier than its data, so no load in the loop waits on another load.
+    struct Pt {
+        int t, i;
+    };
+    auto point_of = [&](int lvl, int base) {
+        Pt q;
+        q.i = base + ln.ps;
+        q.t = s.lev_pts[min(q.i, Lp - 1)];
+        return q;
+    };
+    auto load = [&](int lvl, const Pt& q, BSInR<RM, NDT>& d) {
         const int beg = s.lev_start[lvl];
-        d.act = base + ln.ps < s.lev_start[lvl + 1];
-        const int i = d.act ? base + ln.ps : base;
-        const int t = s.lev_pts[i];
+        d.act = q.i < s.lev_start[lvl + 1];
+        // inactive slots compute on some valid point (clamped id) and store nothing
+        const int t = q.t;
         d.t = t;
-        d.pos = i - beg;
+        d.pos = q.i - beg;
         d.nb = s.nbr[t];
 #pragma unroll
         for (int k = 0; k < NDT; k++) d.ppos[k] = (d.nb >> k) & 1 ? s.lev_pos[t - strides[k]] : 0;
@@ -312,23 +324,30 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
             d.c1[r] = rr && h1ok ? ldv(Cp + c + n1) : 0.0f;
         }
     };
-    int nl = 0, nbase = s.lev_start[0] + warp * Ln::PPW;
-    auto seek = [&]() {
-        while (nl < s.nlev && nbase >= s.lev_start[nl + 1]) {
-            nl++;
-            if (nl < s.nlev) nbase = s.lev_start[nl] + warp * Ln::PPW;
+    auto seek = [&](int& l, int& base) {
+        while (l < s.nlev && base >= s.lev_start[l + 1]) {
+            l++;
+            if (l < s.nlev) base = s.lev_start[l] + warp * Ln::PPW;
         }
     };
-    seek();
+    // task k+1 (data in nx) at (nl, nbase); task k+2 (point id in p2) at (nl2, nb2)
+    int nl = 0, nbase = s.lev_start[0] + warp * Ln::PPW;
+    seek(nl, nbase);
     BSInR<RM, NDT> nx;
-    if (nl < s.nlev) load(nl, nbase, nx);
+    if (nl < s.nlev) load(nl, point_of(nl, nbase), nx);
+    int nl2 = nl, nb2 = nbase + step;
+    seek(nl2, nb2);
+    Pt p2 = nl2 < s.nlev ? point_of(nl2, nb2) : Pt{0, 0};
     for (int lev = 0; lev < s.nlev; lev++) {
         const int cb = lev & 1, pb = cb ^ 1;
         while (nl == lev) {
             const BSInR<RM, NDT> cur = nx;
-            nbase += step;
-            seek();
-            if (nl < s.nlev) load(nl, nbase, nx);
+            nl = nl2;
+            nbase = nb2;
+            if (nl < s.nlev) load(nl, p2, nx);
+            nb2 = nbase + step;
+            seek(nl2, nb2);
+            if (nl2 < s.nlev) p2 = point_of(nl2, nb2);
             const int t = cur.t;
             const bool act = cur.act;
             const float dt = cur.dt, lam = cur.lam;
