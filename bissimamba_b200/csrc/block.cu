@@ -129,6 +129,46 @@ __global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restr
     stv(dP + i, g);
 }
 
+// The bf16 form of block_bwd_epilogue: 8 consecutive dP columns of one row per
+// thread (one index division per 8 elements, one 16-byte store); ldo % 8 == 0 and
+// a 16-byte-aligned dP.  Same per-element arithmetic.
+template <typename T>
+__global__ void block_bwd_epilogue_v8(const float* __restrict__ P, const T* __restrict__ lamv, long long BL, int R,
+                                      int NR, float dt_min, float dt_max, const float* __restrict__ du,
+                                      const float* __restrict__ ddt, const float* __restrict__ dlam,
+                                      const float* __restrict__ dB, const float* __restrict__ dC,
+                                      __nv_bfloat16* __restrict__ dP, int ldo) {
+    const int Rt = R + 2 + 2 * NR, ch = ldo >> 3;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= BL * ch) return;
+    const long long row = BL * ch <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)ch) : i / ch;
+    const int c0 = (int)(i - row * ch) * 8;
+    uint4 pk;
+    __nv_bfloat16* e = (__nv_bfloat16*)&pk;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int col = c0 + j;
+        float g;
+        if (col >= Rt) {
+            g = 0.0f;
+        } else if (col >= R + 2) {
+            g = col < R + 2 + NR ? dB[row * NR + (col - R - 2)] : dC[row * NR + (col - R - 2 - NR)];
+        } else if (col < R) {
+            const float z = P[row * Rt + col], s = sigm(z);
+            g = du[row * R + col] * s * (1.0f + z * (1.0f - s));
+        } else if (col == R) {
+            const float z = P[row * Rt + col];
+            const float d = fminf(fmaxf(logf(1.0f + expf(z)), dt_min), dt_max);
+            g = (d > dt_min && d < dt_max) ? ddt[row] * sigm(z) : 0.0f;
+        } else {
+            const float l = ldv(lamv + row);
+            g = dlam[row] * l * (1.0f - l);
+        }
+        e[j] = __float2bfloat16_rn(g);
+    }
+    *(uint4*)(dP + row * ldo + c0) = pk;
+}
+
 // grads += slices of G[Rt, dim]
 __global__ void block_scatter_grads(const float* __restrict__ G, int R, int NR, int dim, float* gWin,
                                     float* gdelta, float* glam, float* gWB, float* gWC) {
@@ -502,9 +542,10 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
     if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
-    block_bwd_epilogue<H, H><<<nb(BL * ldp, 256), 256, 0, st>>>(
-        act + a.proj, (const H*)(act + a.dt), (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max,
-        S + s_du, S + s_ddt, S + s_dlam, S + s_dB, S + s_dC, dPb, ldp);
+    // ldp is a multiple of 16 and dPb 256-byte aligned: the 8-column form applies
+    block_bwd_epilogue_v8<H><<<nb(BL * (ldp / 8), 256), 256, 0, st>>>(
+        act + a.proj, (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max, S + s_du, S + s_ddt,
+        S + s_dlam, S + s_dB, S + s_dC, dPb, ldp);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
     // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
     if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, x, dim, dPb, ldp, 0.0f, S + s_G, dim) !=
