@@ -14,6 +14,8 @@
 // from per-item partials in a fixed order.
 #include <cuda_bf16.h>
 #include "kmb_common.cuh"
+#include "kmb_sync.cuh"
+#include "kmb_butterfly.cuh"
 #include "../../include/kmamba_block.h"
 
 namespace kmb {
@@ -422,6 +424,286 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
             }
         }
         __syncthreads();
+    }
+}
+
+// Forward for 2D grids with an inner extent W <= 64, N <= 64, R in {1, 2, 4}: a
+// systolic column-strip pipeline instead of level barriers.  CTA = item; warp w
+// owns columns 8w .. 8w+7 of every row; lane p owns the state pair (2p, 2p+1).
+// For each of its columns a lane keeps the previous row's rotated state R(theta)h
+// and its B*u product in registers; the left neighbour of its first column comes
+// from warp w-1 through shared-memory slots guarded by mbarriers (bounded waits),
+// so warps run one row apart and predecessor states never touch memory.  Per point
+// the arithmetic is the same as blockscan_fwd_ring's (outer predecessor, then
+// inner); y is a transposed butterfly over the 32 pairs.  STAGED: each warp keeps
+// its next NSS rows of B, C, u, dt, lambda in flight in shared memory with bulk
+// copies (W % 8 == 0, N % 8 == 0: every piece is a whole run of 16-byte units);
+// otherwise a row's inputs are loaded at the start of the row.
+constexpr int BSS_WC = 8, BSS_K = 4, BSS_NSS = 3;
+
+// Bulk (non-tensor, no multicast) copy global -> this CTA's shared memory, completion on an mbarrier.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, unsigned bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+// Byte layout of one staged row of a strip: B [8][R][N] | C [8][R][N] | u [8][R] | dt [8] | lambda [8],
+// each piece rounded up to 16 bytes.
+template <typename T>
+struct BSStage {
+    int offC, offU, offD, offL, bytes;
+    __host__ __device__ BSStage(int R, int N, bool has_lam) {
+        const int bc = BSS_WC * R * N * (int)sizeof(T);
+        auto up = [](int v) { return (v + 15) & ~15; };
+        offC = up(bc);
+        offU = offC + up(bc);
+        offD = offU + up(BSS_WC * R * (int)sizeof(T));
+        offL = offD + up(BSS_WC * (int)sizeof(T));
+        bytes = offL + (has_lam ? up(BSS_WC * (int)sizeof(T)) : 0);
+    }
+};
+
+template <typename T, int RP, bool STAGED>
+__global__ void __launch_bounds__(256, 1) blockscan_fwd_strips(BSDesc s, int* status) {
+    extern __shared__ __align__(16) unsigned char bss_smem[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, S = blockDim.x >> 5;
+    const int b = blockIdx.x;
+    const int H = s.dims[0], W = s.dims[1];
+    const int N = s.N, R = s.R, NR = N * R;
+    const int n0 = 2 * lane, n1 = 2 * lane + 1;
+    const bool h0ok = n0 < N, h1ok = n1 < N, pair = h1ok;
+    const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
+    float cth = 1.0f, sth = 0.0f;
+    if (pair) {
+        cth = cosf(s.theta[lane]);
+        sth = sinf(s.theta[lane]);
+    }
+    const long long L = s.L;
+    const T* __restrict__ u = (const T*)s.u + b * L * R;
+    const T* __restrict__ dtp = (const T*)s.dt + b * L;
+    const T* __restrict__ lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* __restrict__ Bp = (const T*)s.B + b * L * NR;
+    const T* __restrict__ Cp = (const T*)s.C + b * L * NR;
+    float* h = s.h + b * L * N;
+    float* Bu = s.Bu + b * L * N;
+    float* y = s.y + b * L * R;
+    // handoff slots [S][K][4][32] (rotated h pair, B*u pair), their barriers, stage barriers, stages
+    float* hand = (float*)bss_smem;
+    uint64_t* hfull = (uint64_t*)(hand + (size_t)S * BSS_K * 4 * 32);
+    uint64_t* hempty = hfull + S * BSS_K;
+    uint64_t* sfull = hempty + S * BSS_K;                            // [S][NSS]
+    const BSStage<T> sl(R, N, lamp != nullptr);
+    // [S][NSS][sl.bytes], 128-byte aligned (bulk copies need 16-byte aligned destinations)
+    unsigned char* stages = (unsigned char*)(((uintptr_t)(sfull + S * BSS_NSS) + 127) & ~(uintptr_t)127);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S * BSS_K; i++) {
+            mbar_init(smem_u32(&hfull[i]), 1);
+            mbar_init(smem_u32(&hempty[i]), 1);
+        }
+        for (int i = 0; i < S * BSS_NSS; i++) mbar_init(smem_u32(&sfull[i]), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const int q0 = w * BSS_WC;
+    const int ncol = min(BSS_WC, W - q0);
+    auto issue = [&](int orow) {
+        const int slot = orow % BSS_NSS;
+        unsigned char* st = stages + ((size_t)w * BSS_NSS + slot) * sl.bytes;
+        const uint32_t fb = smem_u32(&sfull[w * BSS_NSS + slot]);
+        const int t0 = orow * W + q0;
+        const unsigned bcb = BSS_WC * R * N * sizeof(T), ub = BSS_WC * R * sizeof(T), db = BSS_WC * sizeof(T);
+        mbar_expect_tx(fb, 2 * bcb + ub + db + (lamp ? db : 0));
+        bulk_load(smem_u32(st), Bp + (size_t)t0 * NR, bcb, fb);
+        bulk_load(smem_u32(st + sl.offC), Cp + (size_t)t0 * NR, bcb, fb);
+        bulk_load(smem_u32(st + sl.offU), u + (size_t)t0 * R, ub, fb);
+        bulk_load(smem_u32(st + sl.offD), dtp + t0, db, fb);
+        if (lamp) bulk_load(smem_u32(st + sl.offL), lamp + t0, db, fb);
+    };
+    int issued = 0;
+    if (STAGED && lane == 0)
+        for (; issued < BSS_NSS && issued < H; issued++) issue(issued);
+    // leaving early: copies in flight must land first (bounded)
+    auto drain = [&]() {
+        if constexpr (STAGED) {
+            if (lane != 0) return;
+            for (int j = (issued > BSS_NSS ? issued - BSS_NSS : 0); j < issued; j++)
+                mbar_wait(smem_u32(&sfull[w * BSS_NSS + j % BSS_NSS]), (uint32_t)((j / BSS_NSS) & 1));
+        }
+    };
+    // y: lane gl holds value butterfly_index = (column j, rank r) after the reduction
+    constexpr int NV = BSS_WC * RP, LPV = 32 / NV;
+    const int yidx = butterfly_index<NV, 32>(lane);
+    const int yj = yidx / RP, yr = yidx % RP;
+    const bool y_lane = (LPV <= 1 || (lane % LPV) == 0) && yj < ncol && yr < R;
+    float rh0[BSS_WC], rh1[BSS_WC], rb0[BSS_WC], rb1[BSS_WC];
+#pragma unroll
+    for (int j = 0; j < BSS_WC; j++) rh0[j] = rh1[j] = rb0[j] = rb1[j] = 0.0f;
+    for (int o = 0; o < H; o++) {
+        // ---- inputs of the row
+        float uu[BSS_WC][RP], bb0[BSS_WC][RP], bb1[BSS_WC][RP], cc0[BSS_WC][RP], cc1[BSS_WC][RP];
+        float dtv[BSS_WC], lmv[BSS_WC];
+        if constexpr (STAGED) {
+            const int slot = o % BSS_NSS;
+            if (!mbar_wait(smem_u32(&sfull[w * BSS_NSS + slot]), (uint32_t)((o / BSS_NSS) & 1))) {
+                set_status(status, KMB_ERR_TIMEOUT_FULL);
+                drain();
+                return;
+            }
+            const unsigned char* st = stages + ((size_t)w * BSS_NSS + slot) * sl.bytes;
+            const T* sB = (const T*)st;
+            const T* sC = (const T*)(st + sl.offC);
+            const T* sU = (const T*)(st + sl.offU);
+            const T* sD = (const T*)(st + sl.offD);
+            const T* sL = (const T*)(st + sl.offL);
+#pragma unroll
+            for (int j = 0; j < BSS_WC; j++) {
+                dtv[j] = ldv(sD + j);
+                lmv[j] = lamp ? ldv(sL + j) : s.deflam;
+#pragma unroll
+                for (int r = 0; r < RP; r++) {
+                    const bool rr = r < R;
+                    const int c = j * NR + (rr ? r : 0) * N;
+                    uu[j][r] = rr ? ldv(sU + j * R + r) : 0.0f;
+                    bb0[j][r] = rr && h0ok ? ldv(sB + c + n0) : 0.0f;
+                    bb1[j][r] = rr && h1ok ? ldv(sB + c + n1) : 0.0f;
+                    cc0[j][r] = rr && h0ok ? ldv(sC + c + n0) : 0.0f;
+                    cc1[j][r] = rr && h1ok ? ldv(sC + c + n1) : 0.0f;
+                }
+            }
+            // the stage is read: refill it with row o + NSS
+            __syncwarp();
+            if (lane == 0 && o + BSS_NSS < H) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(o + BSS_NSS);
+                issued = o + BSS_NSS + 1;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < BSS_WC; j++) {
+                const int t = o * W + q0 + (j < ncol ? j : 0);
+                dtv[j] = ldv(dtp + t);
+                lmv[j] = lamp ? ldv(lamp + t) : s.deflam;
+#pragma unroll
+                for (int r = 0; r < RP; r++) {
+                    const bool rr = r < R;
+                    const int c = t * NR + (rr ? r : 0) * N;
+                    uu[j][r] = rr ? ldv(u + t * R + r) : 0.0f;
+                    bb0[j][r] = rr && h0ok ? ldv(Bp + c + n0) : 0.0f;
+                    bb1[j][r] = rr && h1ok ? ldv(Bp + c + n1) : 0.0f;
+                    cc0[j][r] = rr && h0ok ? ldv(Cp + c + n0) : 0.0f;
+                    cc1[j][r] = rr && h1ok ? ldv(Cp + c + n1) : 0.0f;
+                }
+            }
+        }
+        // ---- left neighbour of the first column, from warp w-1
+        const int hs = o & (BSS_K - 1);
+        const uint32_t hph = (uint32_t)((o / BSS_K) & 1);
+        float lh0 = 0.0f, lh1 = 0.0f, lb0 = 0.0f, lb1 = 0.0f;
+        if (w > 0) {
+            if (!mbar_wait(smem_u32(&hfull[w * BSS_K + hs]), hph)) {
+                set_status(status, KMB_ERR_TIMEOUT_Y);
+                drain();
+                return;
+            }
+            const float* src = hand + ((size_t)w * BSS_K + hs) * 128;
+            lh0 = src[lane];
+            lh1 = src[32 + lane];
+            lb0 = src[64 + lane];
+            lb1 = src[96 + lane];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&hempty[w * BSS_K + hs]));
+        }
+        float prod[BSS_WC][RP];
+#pragma unroll
+        for (int j = 0; j < BSS_WC; j++) {
+#pragma unroll
+            for (int r = 0; r < RP; r++) prod[j][r] = 0.0f;
+            if (j >= ncol) continue;
+            const int t = o * W + q0 + j;
+            const float dt = dtv[j], lam = lmv[j];
+            float bu0 = 0.0f, bu1 = 0.0f;
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                bu0 = __fmaf_rn(bb0[j][r], uu[j][r], bu0);
+                bu1 = __fmaf_rn(bb1[j][r], uu[j][r], bu1);
+            }
+            const float al0 = kmb_exp(dt * A0, s.fast), al1 = kmb_exp(dt * A1, s.fast);
+            float hn0 = 0.0f, hn1 = 0.0f, bacc0 = 0.0f, bacc1 = 0.0f;
+            int np = 0;
+            if (o > 0) {   // outer predecessor (o-1, q): this column's ring entry (previous row)
+                hn0 = __fmaf_rn(al0, rh0[j], hn0);
+                hn1 = __fmaf_rn(al1, rh1[j], hn1);
+                bacc0 += rb0[j];
+                bacc1 += rb1[j];
+                np++;
+            }
+            if (q0 + j > 0) {   // inner predecessor (o, q-1): the previous column (this row)
+                const float p0 = j == 0 ? lh0 : rh0[j == 0 ? 0 : j - 1];
+                const float p1 = j == 0 ? lh1 : rh1[j == 0 ? 0 : j - 1];
+                const float q0b = j == 0 ? lb0 : rb0[j == 0 ? 0 : j - 1];
+                const float q1b = j == 0 ? lb1 : rb1[j == 0 ? 0 : j - 1];
+                hn0 = __fmaf_rn(al0, p0, hn0);
+                hn1 = __fmaf_rn(al1, p1, hn1);
+                bacc0 += q0b;
+                bacc1 += q1b;
+                np++;
+            }
+            if (np > 0) {
+                const float bs = (1.0f - lam) * dt / (float)np;
+                hn0 = __fmaf_rn(bs * al0, bacc0, hn0);
+                hn1 = __fmaf_rn(bs * al1, bacc1, hn1);
+            }
+            const float gm = lam * dt;
+            hn0 = __fmaf_rn(gm, bu0, hn0);
+            hn1 = __fmaf_rn(gm, bu1, hn1);
+            if (!h0ok) { hn0 = 0.0f; bu0 = 0.0f; }
+            if (!h1ok) { hn1 = 0.0f; bu1 = 0.0f; }
+            const int ot = t * N;
+            if (h0ok) { h[ot + n0] = hn0; Bu[ot + n0] = bu0; }
+            if (h1ok) { h[ot + n1] = hn1; Bu[ot + n1] = bu1; }
+            // the predecessor form read by the next row / column: R(theta) h and B*u
+            rh0[j] = pair ? cth * hn0 - sth * hn1 : hn0;
+            rh1[j] = sth * hn0 + cth * hn1;
+            rb0[j] = bu0;
+            rb1[j] = bu1;
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                float part = 0.0f;
+                if (h0ok) part = cc0[j][r] * hn0;
+                if (h1ok) part = __fmaf_rn(cc1[j][r], hn1, part);
+                prod[j][r] = part;
+            }
+        }
+        // ---- right boundary to warp w+1
+        if (w + 1 < S) {
+            if (o >= BSS_K && !mbar_wait(smem_u32(&hempty[(w + 1) * BSS_K + hs]), hph ^ 1)) {
+                set_status(status, KMB_ERR_TIMEOUT_Y);
+                drain();
+                return;
+            }
+            float* dst = hand + ((size_t)(w + 1) * BSS_K + hs) * 128;
+            const int lj = ncol - 1;
+            float a0 = 0.0f, a1 = 0.0f, c0 = 0.0f, c1 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < BSS_WC; j++)
+                if (j == lj) { a0 = rh0[j]; a1 = rh1[j]; c0 = rb0[j]; c1 = rb1[j]; }
+            dst[lane] = a0;
+            dst[32 + lane] = a1;
+            dst[64 + lane] = c0;
+            dst[96 + lane] = c1;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&hfull[(w + 1) * BSS_K + hs]));
+        }
+        // ---- y[t, r] = sum over the states
+        {
+            float v[NV];
+#pragma unroll
+            for (int j = 0; j < BSS_WC; j++)
+#pragma unroll
+                for (int r = 0; r < RP; r++) v[j * RP + r] = prod[j][r];
+            const float sum = butterfly<NV, 32>(v, lane);
+            if (y_lane) y[(o * W + q0 + yj) * R + yr] = sum;
+        }
     }
 }
 
@@ -860,6 +1142,10 @@ void* workspace(int slot, size_t bytes);
 int set_error(const char* msg);
 int set_cuda_error(const char* where, cudaError_t e);
 enum { WS_BS_FWD = 3, WS_BS_SCRATCH = 4 };
+int* device_status();
+// forward choice of this host thread: strips (with staged rows where possible), strips loading rows
+// directly, or the level kernels; and the path of the last forward
+static thread_local int tl_bs_no_strips = 0, tl_bs_no_staging = 0, tl_bs_path = -1;
 
 // Device copy of the wavefront plan of `dims` (level starts [nlev + 1], then the
 // points of every level [L]), cached per host thread, device and shape.
@@ -1065,6 +1351,12 @@ static void group_reduce(const float* part, float* out, long long n, int ng, int
 
 using namespace kmb;
 
+extern "C" void kmb_blockscan_set_strips(int mode) {
+    tl_bs_no_strips = mode == 0 ? 1 : 0;
+    tl_bs_no_staging = mode == 2 ? 1 : 0;
+}
+extern "C" int kmb_blockscan_last_forward_path(void) { return tl_bs_path; }
+
 extern "C" int kmb_blockscan_forward(const KMBlockScanParams* p, long batch, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
     BSDesc s;
@@ -1074,6 +1366,45 @@ extern "C" int kmb_blockscan_forward(const KMBlockScanParams* p, long batch, voi
         s.part = (float*)workspace(WS_BS_FWD, (size_t)s.NG * ny * sizeof(float));
         if (!s.part) return set_error("workspace allocation failed");
     }
+    // 2D grids with an inner extent <= 64: the systolic strip kernel (one CTA per item)
+    if (s.nd == 2 && s.dims[1] <= 64 && s.N <= 64 && (s.R == 1 || s.R == 2 || s.R == 4) && !tl_bs_no_strips) {
+        int* status = device_status();
+        if (status) {
+            const int S = (s.dims[1] + BSS_WC - 1) / BSS_WC;
+            const int sb = s.bf16 ? BSStage<__nv_bfloat16>(s.R, s.N, s.lam != nullptr).bytes
+                                  : BSStage<float>(s.R, s.N, s.lam != nullptr).bytes;
+            const size_t sm_base =
+                (size_t)S * BSS_K * 4 * 32 * sizeof(float) + (2 * S * BSS_K + S * BSS_NSS) * sizeof(uint64_t);
+            const size_t sm_staged = sm_base + 128 + (size_t)S * BSS_NSS * sb;   // + alignment of the stages
+            // staged rows (bulk copies of whole 16-byte pieces) when every strip is full, N % 8 == 0
+            // and the stages fit
+            const bool staged = s.dims[1] % BSS_WC == 0 && s.N % 8 == 0 && !tl_bs_no_staging &&
+                                sm_staged <= 200 * 1024;
+            const size_t sm = staged ? sm_staged : sm_base;
+            auto go = [&](auto kern) {
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+                kern<<<(unsigned)batch, S * 32, sm, st>>>(s, status);
+            };
+#define KMB_BSS_GO(TT, ST)                                              \
+    do {                                                                \
+        if (s.R == 1) go(blockscan_fwd_strips<TT, 1, ST>);              \
+        else if (s.R == 2) go(blockscan_fwd_strips<TT, 2, ST>);         \
+        else go(blockscan_fwd_strips<TT, 4, ST>);                       \
+    } while (0)
+            if (s.bf16) {
+                if (staged) KMB_BSS_GO(__nv_bfloat16, true);
+                else KMB_BSS_GO(__nv_bfloat16, false);
+            } else {
+                if (staged) KMB_BSS_GO(float, true);
+                else KMB_BSS_GO(float, false);
+            }
+#undef KMB_BSS_GO
+            tl_bs_path = staged ? 2 : 1;
+            cudaError_t e = cudaGetLastError();
+            return e == cudaSuccess ? 0 : set_cuda_error("blockscan_fwd_strips", e);
+        }
+    }
+    tl_bs_path = 0;
     if (s.bf16) bs_fwd_dispatch<__nv_bfloat16>(s, st);
     else bs_fwd_dispatch<float>(s, st);
     if (s.NG > 1) group_reduce(s.part, s.y, ny, s.NG, 0, st);

@@ -41,6 +41,14 @@ typedef struct {
     float *dtheta;          /* [N/2]  += summed over the batch */
 } KMBlockScanGrads;
 
+/* Forward kernel choice, per host thread (for tests and comparison).  mode 1
+ * (default): 2D grids with an inner extent <= 64, N <= 64, R in {1, 2, 4} use the
+ * systolic strip kernel, with rows staged through shared memory by bulk copies
+ * when the inner extent and N are multiples of 8; 2: the strip kernel always
+ * loads rows directly; 0: always the level-synchronous kernels.  The last
+ * forward's path: 2 staged strips, 1 strips, 0 level kernels, -1 none yet. */
+void kmb_blockscan_set_strips(int mode);
+int kmb_blockscan_last_forward_path(void);
 /* No counterpart in the reference API (see above): batched Scan-B forward. */
 int kmb_blockscan_forward(const KMBlockScanParams *p, long batch, void *stream);
 /* No counterpart in the reference API: exact Scan-B backward; dy is [batch, L, R]. */

@@ -80,3 +80,40 @@ def test_blockscan_backward(kmb, cuda, dims, N, R, fl):
     names = {"dB": "dB", "dC": "dC", "du": "du", "ddt": "ddt", "dlambda": "dlam", "dA_log": "dA", "dtheta": "dtheta"}
     for k, rk in names.items():
         assert_grad_close(g[k].cpu().numpy(), ref[rk], k)
+
+
+@pytest.mark.parametrize("dims,N,R", [([64, 64], 64, 2), ([9, 13], 12, 1), ([16, 64], 64, 4), ([3, 8], 7, 2),
+                                      ([8, 16], 16, 4), ([5, 8], 16, 2)])
+def test_blockscan_strips_path(kmb, cuda, dims, N, R):
+    """2D grids with an inner extent <= 64 run the systolic strip forward (rows staged
+    through shared memory where the shape allows, else loaded directly): the path is
+    taken, and h and Bu equal the level-synchronous kernels bit for bit (same
+    per-point arithmetic); y agrees to rounding (its sum over the states is ordered
+    differently)."""
+    import torch
+    inp = po.gen_blockscan(dims, N, R, batch=2, seed=N + R)
+    lib = kmb.lib()
+    staged_ok = dims[1] % 8 == 0 and N % 8 == 0   # fp32 inputs at 64 x 64, N 64 exceed the stage budget
+    out = {}
+    try:
+        for mode in (1, 2, 0):
+            lib.kmb_blockscan_set_strips(mode)
+            h, Bu, y, _, _ = _fwd(kmb, cuda, inp)
+            path = lib.kmb_blockscan_last_forward_path()
+            assert lib.kmb_device_status(None) == 0
+            if mode == 0:
+                assert path == 0
+            elif mode == 2:
+                assert path == 1
+            else:
+                # staged when the shape allows and three staged rows per strip fit in shared memory
+                assert path == (2 if dims in ([8, 16], [5, 8]) else 1 if not staged_ok else path) and path in (1, 2)
+            out[mode] = (h.cpu(), Bu.cpu(), y.cpu())
+    finally:
+        lib.kmb_blockscan_set_strips(1)
+    h0, b0, y0 = out[0]
+    for mode in (1, 2):
+        h1, b1, y1 = out[mode]
+        assert torch.equal(b1, b0)
+        assert torch.equal(h1, h0)
+        torch.testing.assert_close(y1, y0, rtol=1e-5, atol=1e-5 * float(y0.abs().max()))
