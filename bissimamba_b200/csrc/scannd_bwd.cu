@@ -36,6 +36,7 @@ struct WaveBwd {
     int nlev;
     const int* lev_start;
     const int* lev_pts;
+    const int* nbr;   // per point: bit k = predecessor along axis k, bit 8 + k = successor along axis k
     const float *x, *A, *B, *C, *delta, *theta, *lambda, *h, *dy;
     float *dB, *dC, *ddelta, *dx;
     float *G, *pA, *pth, *plam;
@@ -54,15 +55,17 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
     const bool rot = ROPE && nc == 2;
     const int tid = threadIdx.x, m = tid % M, slot = tid / M;
     const int nslots = blockDim.x / M;
+    // item bases in 64-bit; indices inside an item in 32-bit (P * D * M < 2^31, checked by the launcher)
     const long long P = w.P, DM = (long long)D * M;
-    const float* x = w.x + b * P * D;
-    const float* Bp = w.B + b * P * DM;
-    const float* Cp = w.C + b * P * DM;
-    const float* hp = w.h + b * P * DM;
-    const float* dl = w.delta + b * ND * P * D;
-    const float* dyp = w.dy + b * P * D;
-    const float* lamp = w.has_lambda ? w.lambda + b * P : nullptr;
-    float* G = w.G + b * P * DM;
+    const int Pi = (int)P, DMi = D * M;
+    const float* __restrict__ x = w.x + b * P * D;
+    const float* __restrict__ Bp = w.B + b * P * DM;
+    const float* __restrict__ Cp = w.C + b * P * DM;
+    const float* __restrict__ hp = w.h + b * P * DM;
+    const float* __restrict__ dl = w.delta + b * ND * P * D;
+    const float* __restrict__ dyp = w.dy + b * P * D;
+    const float* __restrict__ lamp = w.has_lambda ? w.lambda + b * P : nullptr;
+    float* __restrict__ G = w.G + b * P * DM;
     float* dBp = w.dB ? w.dB + b * P * DM : nullptr;
     float* dCp = w.dC ? w.dC + b * P * DM : nullptr;
     float* ddp = w.ddelta ? w.ddelta + b * ND * P * D : nullptr;
@@ -93,13 +96,9 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
             const int i = base + slot;
             const bool active = i < end;
             const int p = active ? w.lev_pts[i] : 0;
-            int idx[ND];
-            int npred = 0;
-#pragma unroll
-            for (int k = 0; k < ND; k++) {
-                idx[k] = (p / w.strides[k]) % w.dims[k];
-                npred += idx[k] > 0;
-            }
+            // neighbour mask from the plan: no divisions per point
+            const int nb = w.nbr[p];
+            const int npred = __popc(nb & 0xff);
             float gdel[ND][2], gdt[2] = {0.f, 0.f}, gx[2] = {0.f, 0.f}, glam = 0.0f;
 #pragma unroll
             for (int k = 0; k < ND; k++) gdel[k][0] = gdel[k][1] = 0.0f;
@@ -109,9 +108,9 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
                 float ah[2] = {0.f, 0.f}, ab[2] = {0.f, 0.f};
 #pragma unroll
                 for (int k = 0; k < ND; k++) {
-                    if (idx[k] >= w.dims[k] - 1) continue;
+                    if (!((nb >> (8 + k)) & 1)) continue;
                     const int s = p + w.strides[k];
-                    const int ns = npred + (idx[k] == 0 ? 1 : 0);
+                    const int ns = npred + (((nb >> k) & 1) ? 0 : 1);
                     const float lams = lamp ? lamp[s] : w.deflam;
 #pragma unroll
                     for (int c = 0; c < 2; c++) {
@@ -119,23 +118,23 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
                         float dts = 0.0f, sal = 0.0f, alk = 0.0f;
 #pragma unroll
                         for (int k2 = 0; k2 < ND; k2++) {
-                            const float dv = dl[((long long)k2 * P + s) * D + c0 + c];
+                            const float dv = dl[(k2 * Pi + s) * D + c0 + c];
                             dts += dv;
-                            const bool has = (k2 == k) || (idx[k2] > 0);   // successor's predecessor axes
+                            const bool has = (k2 == k) || ((nb >> k2) & 1);   // successor's predecessor axes
                             if (has) {
                                 const float a = kmb_exp(dv * Ak[k2][c], w.fast);
                                 sal += a;
                                 if (k2 == k) alk = a;
                             }
                         }
-                        const float Gs = G[(long long)s * DM + (long long)(c0 + c) * M + m];
+                        const float Gs = G[s * DMi + (c0 + c) * M + m];
                         const float beta = (1.0f - lams) * dts * (sal / (float)ns);
                         ah[c] += alk * Gs;
                         ab[c] += beta / (float)ns * Gs;
                     }
                 }
                 float gh[2];
-                const long long o = (long long)p * DM + (long long)c0 * M + m;
+                const int o = p * DMi + c0 * M + m;
                 const float h0 = hp[o], h1 = rot ? hp[o + M] : 0.0f;
                 if (rot) {
                     gh[0] = cth * ah[0] + sth * ah[1];
@@ -149,25 +148,25 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     if (c >= nc) continue;
-                    const long long oc = o + (long long)c * M;
+                    const int oc = o + c * M;
                     const int d = c0 + c;
-                    const float dyv = dyp[(long long)p * D + d];
+                    const float dyv = dyp[p * D + d];
                     const float hv = c ? h1 : h0;
                     gh[c] += Cp[oc] * dyv;
-                    if (dCp) dCp[oc] += dyv * hv;
+                    if (dCp) atomicAdd(&dCp[oc], dyv * hv);   // one addition: old + value
                     G[oc] = gh[c];
-                    const float xv = x[(long long)p * D + d];
+                    const float xv = x[p * D + d];
                     float dt = 0.0f;
                     float dk[ND];
 #pragma unroll
                     for (int k = 0; k < ND; k++) {
-                        dk[k] = dl[((long long)k * P + p) * D + d];
+                        dk[k] = dl[(k * Pi + p) * D + d];
                         dt += dk[k];
                     }
                     const float bv = Bp[oc];
                     const float bu = bv * xv;
                     const float gbu = lam * dt * gh[c] + ab[c];
-                    if (dBp) dBp[oc] += gbu * xv;
+                    if (dBp) atomicAdd(&dBp[oc], gbu * xv);
                     gx[c] = gbu * bv;
                     gdt[c] = lam * bu * gh[c];
                     glam += dt * bu * gh[c];
@@ -177,12 +176,12 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
                         for (int k = 0; k < ND; k++) {
                             al[k] = 0.0f;
                             hat[k] = 0.0f;
-                            if (idx[k] == 0) continue;
+                            if (!((nb >> k) & 1)) continue;
                             const int q = p - w.strides[k];
-                            const long long oq = (long long)q * DM + (long long)c0 * M + m;
+                            const int oq = q * DMi + c0 * M + m;
                             al[k] = kmb_exp(dk[k] * Ak[k][c], w.fast);
                             sal += al[k];
-                            sbu += Bp[oq + (long long)c * M] * x[(long long)q * D + d];
+                            sbu += Bp[oq + c * M] * x[q * D + d];
                             if (rot) {
                                 const float q0 = hp[oq], q1 = hp[oq + M];
                                 hat[k] = c ? sth * q0 + cth * q1 : cth * q0 - sth * q1;
@@ -197,7 +196,7 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
                         glam -= dt * sal * inv * gbeta;
 #pragma unroll
                         for (int k = 0; k < ND; k++) {
-                            if (idx[k] == 0) continue;
+                            if (!((nb >> k) & 1)) continue;
                             const float z = dk[k] * Ak[k][c];
                             const float dz = kmb_dexp(z, al[k], w.fast) * (hat[k] * gh[c] + gsal);
                             gdel[k][c] += dz * Ak[k][c];
@@ -226,8 +225,8 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
                     const int d = c0 + c;
                     if (ddp)
 #pragma unroll
-                        for (int k = 0; k < ND; k++) ddp[((long long)k * P + p) * D + d] += gdel[k][c] + gdt[c];
-                    if (dxp) dxp[(long long)p * D + d] += gx[c];
+                        for (int k = 0; k < ND; k++) atomicAdd(&ddp[(k * Pi + p) * D + d], gdel[k][c] + gdt[c]);
+                    if (dxp) atomicAdd(&dxp[p * D + d], gx[c]);
                 }
                 w.plam[((long long)b * ngroups + g) * P + p] = glam;
             }
@@ -278,7 +277,8 @@ size_t scan_bwd_wave_scratch_bytes(const ScanDesc& s) {
 // cudaErrorNotSupported when the shape is outside the kernel's envelope.
 cudaError_t launch_scan_bwd_wave(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC, float* ddelta,
                                  float* dlambda, float* dtheta, float* dx, void* scratch, cudaStream_t st) {
-    if (s.nd < 1 || s.nd > 4 || s.M > 32 || (s.M & (s.M - 1)) != 0 || s.P > 0x7fffffffLL || s.batch * s.D > 0x7fffffffLL)
+    if (s.nd < 1 || s.nd > 4 || s.M > 32 || (s.M & (s.M - 1)) != 0 || s.P > 0x7fffffffLL || s.batch * s.D > 0x7fffffffLL ||
+        s.P * s.D * s.M * s.nd >= (1LL << 31))   // 32-bit indexing inside an item
         return cudaErrorNotSupported;
     std::vector<long> dims(s.dims, s.dims + s.nd);
     int* plan = nullptr;
@@ -290,6 +290,7 @@ cudaError_t launch_scan_bwd_wave(const ScanDesc& s, const float* dy, float* dA, 
     w.amin = s.a_log_min; w.deflam = s.default_lambda; w.P = s.P;
     for (int k = 0; k < s.nd; k++) { w.dims[k] = (int)s.dims[k]; w.strides[k] = (int)s.strides[k]; }
     w.nlev = nlev; w.lev_start = plan; w.lev_pts = plan + nlev + 1;
+    w.nbr = w.lev_pts + 2 * s.P;   // after the points and their in-level positions
     w.x = s.x; w.A = s.A; w.B = s.B; w.C = s.C; w.delta = s.delta; w.theta = s.theta; w.lambda = s.lambda;
     w.h = s.h; w.dy = dy; w.dB = dB; w.dC = dC; w.ddelta = ddelta; w.dx = dx;
     const long long ngroups = s.rope ? (s.D + 1) / 2 : s.D;
