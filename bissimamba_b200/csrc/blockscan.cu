@@ -947,13 +947,9 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
             const bool act = base + ln.ps < end;
             const int t = s.lev_pts[act ? base + ln.ps : base];
             const bool x0 = act && h0ok, x1 = act && h1ok;
-            int idx[NDT];
-            int npt = 0;
-#pragma unroll
-            for (int k = 0; k < NDT; k++) {
-                idx[k] = (t / strides[k]) % dims[k];
-                npt += idx[k] > 0;
-            }
+            // neighbour mask from the plan (bit k: predecessor along k, bit 8 + k: successor)
+            const int nbm = s.nbr[t];
+            const int npt = __popc(nbm & 0xff);
             // ---- loads
             const float dt = ldv(dtp + t);
             const float lam = lamp ? ldv(lamp + t) : s.deflam;
@@ -961,13 +957,13 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
             float sdt[NDT], slam[NDT], sG0[NDT], sG1[NDT], ph0[NDT], ph1[NDT], pb0[NDT], pb1[NDT];
 #pragma unroll
             for (int k = 0; k < NDT; k++) {
-                hs[k] = idx[k] < dims[k] - 1;
+                hs[k] = (nbm >> (8 + k)) & 1;
                 const int sp = hs[k] ? t + strides[k] : t;
                 sdt[k] = ldv(dtp + sp);
                 slam[k] = lamp ? ldv(lamp + sp) : s.deflam;
                 sG0[k] = h0ok && hs[k] ? G[sp * N + n0] : 0.0f;
                 sG1[k] = h1ok && hs[k] ? G[sp * N + n1] : 0.0f;
-                hp[k] = idx[k] > 0;
+                hp[k] = (nbm >> k) & 1;
                 const int q = (hp[k] ? t - strides[k] : t) * N;
                 ph0[k] = h0ok ? h[q + n0] : 0.0f;
                 ph1[k] = h1ok ? h[q + n1] : 0.0f;
@@ -977,7 +973,7 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
             const int o = t * N;
             const float ht0 = h0ok ? h[o + n0] : 0.0f, ht1 = h1ok ? h[o + n1] : 0.0f;
             const float bu0 = h0ok ? Bu[o + n0] : 0.0f, bu1 = h1ok ? Bu[o + n1] : 0.0f;
-            float dyv[RM], uu[RM], c0[RM], c1[RM], b0[RM], b1[RM], odB0[RM], odB1[RM], odC0[RM], odC1[RM];
+            float dyv[RM], uu[RM], c0[RM], c1[RM], b0[RM], b1[RM];
 #pragma unroll
             for (int r = 0; r < RM; r++) {
                 const bool rr = r < R;
@@ -988,17 +984,13 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 c1[r] = rr && h1ok ? ldv(Cp + c + n1) : 0.0f;
                 b0[r] = rr && h0ok ? ldv(Bp + c + n0) : 0.0f;
                 b1[r] = rr && h1ok ? ldv(Bp + c + n1) : 0.0f;
-                odB0[r] = rr && x0 ? dB[c + n0] : 0.0f;
-                odB1[r] = rr && x1 ? dB[c + n1] : 0.0f;
-                odC0[r] = rr && x0 ? dC[c + n0] : 0.0f;
-                odC1[r] = rr && x1 ? dC[c + n1] : 0.0f;
             }
             // ---- pull from successors s = t + e_k
             float a0 = 0.0f, a1 = 0.0f, ab0 = 0.0f, ab1 = 0.0f;
 #pragma unroll
             for (int k = 0; k < NDT; k++) {
                 if (!hs[k]) continue;
-                const int nps = npt + (idx[k] == 0 ? 1 : 0);
+                const int nps = npt + (((nbm >> k) & 1) ? 0 : 1);
                 const float al0 = kmb_exp(sdt[k] * A0, s.fast), al1 = kmb_exp(sdt[k] * A1, s.fast);
                 const float coef = (1.0f - slam[k]) * sdt[k] / (float)nps;
                 a0 += al0 * sG0[k];
@@ -1056,12 +1048,13 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
                 if (r >= R) continue;
                 const int c = t * NR + r * N;
                 if (x0) {
-                    dC[c + n0] = odC0[r] + dyv[r] * ht0;
-                    dB[c + n0] = odB0[r] + gbu0 * uu[r];
+                    // one addition each (old + value): no read of the old value in the chain
+                    atomicAdd(&dC[c + n0], dyv[r] * ht0);
+                    atomicAdd(&dB[c + n0], gbu0 * uu[r]);
                 }
                 if (x1) {
-                    dC[c + n1] = odC1[r] + dyv[r] * ht1;
-                    dB[c + n1] = odB1[r] + gbu1 * uu[r];
+                    atomicAdd(&dC[c + n1], dyv[r] * ht1);
+                    atomicAdd(&dB[c + n1], gbu1 * uu[r]);
                 }
                 float part = 0.0f;
                 if (h0ok) part += gbu0 * b0[r];
