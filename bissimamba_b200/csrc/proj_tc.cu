@@ -12,11 +12,11 @@
 // the block's P layout (row stride Rt, columns 0 .. R+1), which is all the
 // backward epilogue reads of P.
 //
-// One CTA per 128-row tile of X and up to 512 columns of Wcat (grid.y covers
-// more): warp 0 issues the TMA loads (128B-swizzled K-major tiles, 64 K-elements
-// per stage, a ring of S stages), warp 1 owns the TMEM accumulator (128 lanes x
-// up to 512 fp32 columns) and issues tcgen05.mma (M = 128, N = 256 and the
-// remainder, K = 16 per instruction), warps 2-5 read TMEM rows back with
+// One CTA per 128-row tile of X and up to 256 columns of Wcat (grid.y covers
+// more; two CTAs per SM): warp 0 issues the TMA loads (128B-swizzled K-major
+// tiles, 64 K-elements per stage, a ring of S stages), warp 1 owns the TMEM
+// accumulator (128 lanes x up to 256 fp32 columns) and issues tcgen05.mma
+// (M = 128, N <= 256, K = 16 per instruction), warps 2-5 read TMEM rows back with
 // tcgen05.ld and run the epilogue.  Every wait is bounded; on a timeout the
 // kernel records a status, drains its copies and still frees its TMEM.
 #include <cuda.h>
@@ -283,10 +283,12 @@ static cudaError_t tc_launch(ProjTCDesc& d, const __nv_bfloat16* A, int lda, con
     if (((uintptr_t)A & 15) || ((uintptr_t)Bm & 15) || (lda % 8) || (ldb % 8) || d.BL < 1 || d.K < 1 || d.N < 16)
         return cudaErrorNotSupported;
     const int npad = (d.N + 15) & ~15;
-    d.ncols_max = npad <= 512 ? npad : 512;
+    // 256-column ranges and <= 110 KB of stages: two CTAs (and two 256-column TMEM
+    // accumulators) per SM, so one tile's epilogue overlaps another's loads and MMAs
+    d.ncols_max = npad <= 256 ? npad : 256;
     d.x_bytes = 128 * 128;
     d.stage_bytes = d.x_bytes + d.ncols_max * 128;
-    d.stages = (200 * 1024) / d.stage_bytes;
+    d.stages = (110 * 1024) / d.stage_bytes;
     if (d.stages > 4) d.stages = 4;
     if (d.stages < 2) return cudaErrorNotSupported;
     CUtensorMap mA, mB;
