@@ -126,7 +126,8 @@ EXPORTS = [
     "km_wavefront_plan_matches_dims", "km_wavefront_plan_level_size", "km_wavefront_plan_level_offsets",
     "km_wavefront_plan_iter_forward", "km_wavefront_plan_iter_reverse",
     "kmb_last_error", "kmb_clear_error", "kmb_device_status", "kmb_last_forward_path", "kmb_set_force_generic",
-    "kmb_blockscan_forward", "kmb_blockscan_set_strips", "kmb_blockscan_last_forward_path", "kmb_blockscan_backward", "kmb_block_activation_floats",
+    "kmb_blockscan_forward", "kmb_blockscan_set_strips", "kmb_blockscan_last_forward_path", "kmb_blockscan_set_backward_strips",
+    "kmb_blockscan_last_backward_path", "kmb_blockscan_backward", "kmb_blockscan_backward_ex", "kmb_block_activation_floats",
     "kmb_block_forward", "kmb_block_backward", "kmb_block_set_tensor_cores", "kmb_block_last_projection_path", "kmb_block_last_dx_path", "cuda_block_forward", "cuda_block_backward",
     "kmamba_config_set_defaults", "kmamba_optim_config_set_defaults", "kmamba_create", "kmamba_free",
     "kmamba_init", "kmamba_enable_training", "kmamba_forward", "kmamba_train_batch", "kmamba_train_step",
@@ -212,6 +213,10 @@ def lib():
         L.kmb_blockscan_forward.argtypes = [C.POINTER(KMBlockScanParams), C.c_long, C.c_void_p]
         L.kmb_blockscan_backward.argtypes = [C.POINTER(KMBlockScanParams), C.c_long, C.c_void_p,
                                              C.POINTER(KMBlockScanGrads), C.c_void_p]
+        L.kmb_blockscan_backward_ex.argtypes = [C.POINTER(KMBlockScanParams), C.c_long, C.c_void_p,
+                                                C.POINTER(KMBlockScanGrads), C.c_int, C.c_void_p]
+        L.kmb_blockscan_set_backward_strips.argtypes = [C.c_int]
+        L.kmb_blockscan_set_backward_strips.restype = None
         L.kmb_set_force_generic.argtypes = [C.c_int]
         L.kmb_set_force_generic.restype = None
         L.km_wavefront_plan_create.argtypes = [_l, C.c_long, C.c_long]

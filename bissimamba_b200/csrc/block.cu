@@ -423,9 +423,6 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     if (g->W_out && cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_T, R, dim, (int)BL, &one, act + a.y, R, dout, dim, &one,
                                 g->W_out, R) != CUBLAS_STATUS_SUCCESS)
         return set_error("dW_out GEMM failed");
-    // block-scan backward into zeroed scratch
-    if ((e = cudaMemsetAsync(S + s_du, 0, (s_dP - s_du) * sizeof(float), st)) != cudaSuccess)
-        return set_cuda_error("memset", e);
     KMBlockScanParams p;
     memset(&p, 0, sizeof p);
     p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;
@@ -435,7 +432,8 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     KMBlockScanGrads sg;
     sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
-    if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
+    // du, ddt, dlambda, dB, dC are assigned (no clearing of the scratch first)
+    if (kmb_blockscan_backward_ex(&p, batch, S + s_dy, &sg, 1, stream)) return -1;
     block_bwd_epilogue<float, float><<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
                                                                     (int)NR, c->dt_min, c->dt_max, S + s_du,
                                                                     S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
@@ -529,8 +527,6 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     if (g->W_out && gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, R, dim, (int)BL, yb, R, dout, dim, 1.0f, g->W_out, R) !=
                         CUBLAS_STATUS_SUCCESS)
         return set_error("dW_out GEMM failed");
-    if ((e = cudaMemsetAsync(S + s_du, 0, (s_G - s_du) * sizeof(float), st)) != cudaSuccess)
-        return set_cuda_error("memset", e);
     KMBlockScanParams p;
     memset(&p, 0, sizeof p);
     p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;
@@ -541,7 +537,8 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     KMBlockScanGrads sg;
     sg.dB = S + s_dB; sg.dC = S + s_dC; sg.du = S + s_du; sg.ddt = S + s_ddt; sg.dlambda = S + s_dlam;
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
-    if (kmb_blockscan_backward(&p, batch, S + s_dy, &sg, stream)) return -1;
+    // du, ddt, dlambda, dB, dC are assigned (no clearing of the scratch first)
+    if (kmb_blockscan_backward_ex(&p, batch, S + s_dy, &sg, 1, stream)) return -1;
     // ldp is a multiple of 16 and dPb 256-byte aligned: the 8-column form applies
     block_bwd_epilogue_v8<H><<<nb(BL * (ldp / 8), 256), 256, 0, st>>>(
         act + a.proj, (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max, S + s_du, S + s_ddt,

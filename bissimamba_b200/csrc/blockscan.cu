@@ -715,6 +715,7 @@ struct BSGrad {
     float* pth;   // scratch [batch, 32]
     // NG > 1: per-group partials [NG][batch][L][R] and [NG][batch][L] (x2)
     float *pdu, *pddt, *pdlam;
+    int overwrite;   // 1: dB, dC, du, ddt, dlambda are assigned, not accumulated (strip backward only)
 };
 
 template <typename T, int GP>
@@ -1101,6 +1102,316 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
     }
 }
 
+// Backward for 2D grids, R in {1, 2, 4}: a systolic reverse column-strip
+// pipeline, the mirror of blockscan_fwd_strips, with the state pairs split
+// into groups as in the level kernels (CTA = (item, group of GP pairs)).
+// Strips of CW columns are numbered from the right; a warp carries SPW = 32 /
+// GP strips at once (lane = (slot, pair)), slot ss working one row behind slot
+// ss - 1, rows bottom to top and columns right to left.  What a point hands to
+// its predecessors -- alpha * g_h and coef * alpha * g_h per state, the exact
+// terms the level kernel pulls from a successor -- stays in registers for the
+// outer axis (same column, next row), moves along the strip in registers, to
+// the next slot by a shuffle, and to the next warp through mbarrier-guarded
+// shared-memory slots (bounded waits).  So the state adjoints never touch
+// memory; h and B*u of a point and its predecessors are read back from the
+// forward, and the next row's loads are issued before the current row's
+// arithmetic.  Per point the arithmetic is the level kernel's.
+constexpr int BSB_K = 4;
+
+__device__ __forceinline__ float2 ld2(const float* p) { return *(const float2*)p; }
+__device__ __forceinline__ float2 ld2(const __nv_bfloat16* p) {
+    return __bfloat1622float2(*(const __nv_bfloat162*)p);
+}
+
+// One column's loads for a row: own h and B*u, the outer predecessor's, the inner
+// predecessor's (last column of the strip only; the others take the next
+// column's own values), and the point's inputs.  Pairs are one vector load each.
+template <int RP>
+struct BSBCol {
+    float dt, lam;
+    float2 ht, bu, uh, ub, lh, lb;
+    float dy[RP], u[RP];
+    float2 b[RP], c[RP];
+};
+
+template <typename T, int GP, int RP, int CW>
+__global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad g, int* status) {
+    extern __shared__ __align__(16) unsigned char bsb_smem[];
+    constexpr int SPW = 32 / GP;
+    using Ln = BSLanes<GP>;
+    const Ln ln(s);
+    const int b = ln.b, n0 = ln.n0;
+    const bool hok = ln.h0ok;   // N is even: a pair is whole or absent
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int ss = ln.ps, pl = ln.pl;
+    const int H = s.dims[0], W = s.dims[1];
+    const int N = s.N, R = s.R, NR = N * R;
+    const int nstrips = (W + CW - 1) / CW;
+    const int st = w * SPW + ss;
+    const int qb = W - 1 - st * CW;   // rightmost column of the strip
+    const float A0 = hok ? s.A[n0] : 0.0f, A1 = hok ? s.A[n0 + 1] : 0.0f;
+    float cth = 1.0f, sth = 0.0f;
+    if (hok) {
+        cth = cosf(s.theta[n0 >> 1]);
+        sth = sinf(s.theta[n0 >> 1]);
+    }
+    const long long L = s.L;
+    const T* __restrict__ u = (const T*)s.u + b * L * R;
+    const T* __restrict__ dtp = (const T*)s.dt + b * L;
+    const T* __restrict__ lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* __restrict__ Bp = (const T*)s.B + b * L * NR + n0;
+    const T* __restrict__ Cp = (const T*)s.C + b * L * NR + n0;
+    const float* __restrict__ h = s.h + b * L * N + n0;
+    const float* __restrict__ Bu = s.Bu + b * L * N + n0;
+    const float* __restrict__ dy = g.dy + b * L * R;
+    float* dB = g.dB + b * L * NR + n0;
+    float* dC = g.dC + b * L * NR + n0;
+    const bool direct = s.NG == 1, ovw = g.overwrite != 0;
+    const long long gofs = (long long)ln.g * s.batch;
+    float* du = direct ? g.du + b * L * R : g.pdu + (gofs + b) * L * R;
+    float* ddt = direct ? (g.ddt ? g.ddt + b * L : nullptr) : g.pddt + (gofs + b) * L;
+    float* dlam = direct ? (g.dlam ? g.dlam + b * L : nullptr) : g.pdlam + (gofs + b) * L;
+    const bool assign = !direct || ovw;
+
+    // handoff slots [nw][K][4][GP] (P pair, Q pair of a strip's leftmost column), then their barriers
+    float* hand = (float*)bsb_smem;
+    uint64_t* hfull = (uint64_t*)(hand + (size_t)nw * BSB_K * 4 * GP);
+    uint64_t* hempty = hfull + nw * BSB_K;
+    float* red = (float*)(hempty + nw * BSB_K);   // [nw * 32][3]: dA pair and dtheta partials
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nw * BSB_K; i++) {
+            mbar_init(smem_u32(&hfull[i]), 1);
+            mbar_init(smem_u32(&hempty[i]), 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const float2 z2 = make_float2(0.0f, 0.0f);
+    auto load_row = [&](BSBCol<RP>* c, int rr) {
+        const bool rok = st < nstrips && rr >= 0 && rr < H;
+        const int o = rok ? H - 1 - rr : 0;
+#pragma unroll
+        for (int j = 0; j < CW; j++) {
+            const int q = qb - j;
+            const bool ok = rok && q >= 0;
+            const int t = ok ? o * W + q : 0;
+            BSBCol<RP>& x = c[j];
+            x.dt = ldv(dtp + t);
+            x.lam = lamp ? ldv(lamp + t) : s.deflam;
+            const int tu = ok && o > 0 ? t - W : t;
+            x.ht = hok ? ld2(h + t * N) : z2;
+            x.bu = hok ? ld2(Bu + t * N) : z2;
+            x.uh = hok ? ld2(h + tu * N) : z2;
+            x.ub = hok ? ld2(Bu + tu * N) : z2;
+            if (j == CW - 1) {
+                const int tl = ok && q > 0 ? t - 1 : t;
+                x.lh = hok ? ld2(h + tl * N) : z2;
+                x.lb = hok ? ld2(Bu + tl * N) : z2;
+            }
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                const bool rk = r < R;
+                const int cc = t * NR + (rk ? r : 0) * N;
+                x.dy[r] = rk ? dy[t * R + r] : 0.0f;
+                x.u[r] = rk ? ldv(u + t * R + r) : 0.0f;
+                x.b[r] = rk && hok ? ld2(Bp + cc) : z2;
+                x.c[r] = rk && hok ? ld2(Cp + cc) : z2;
+            }
+        }
+    };
+
+    float PO0[CW], PO1[CW], QO0[CW], QO1[CW];   // from the outer successor (same column, row below)
+#pragma unroll
+    for (int j = 0; j < CW; j++) PO0[j] = PO1[j] = QO0[j] = QO1[j] = 0.0f;
+    float ob0 = 0.0f, ob1 = 0.0f, oq0 = 0.0f, oq1 = 0.0f;   // this slot's output to the strip on its left
+    float gA0 = 0.0f, gA1 = 0.0f, gth = 0.0f;
+    BSBCol<RP> cur[CW], nxt[CW];
+    load_row(cur, -ss);
+    const int nsteps = H + SPW - 1;
+    for (int i = 0; i < nsteps; i++) {
+        const int rr = i - ss;
+        const bool act = st < nstrips && rr >= 0 && rr < H;
+        const int o = H - 1 - rr;
+        load_row(nxt, rr + 1);
+        // ---- inner successor of the rightmost column: the strip on the right, same row
+        float ip0 = __shfl_up_sync(0xffffffffu, ob0, GP);
+        float ip1 = __shfl_up_sync(0xffffffffu, ob1, GP);
+        float iq0 = __shfl_up_sync(0xffffffffu, oq0, GP);
+        float iq1 = __shfl_up_sync(0xffffffffu, oq1, GP);
+        if (ss == 0) ip0 = ip1 = iq0 = iq1 = 0.0f;
+        if (w > 0 && i < H) {   // warp-uniform: slot 0 takes row i of warp w - 1's last strip
+            const int hs = i & (BSB_K - 1);
+            if (!mbar_wait(smem_u32(&hfull[w * BSB_K + hs]), (uint32_t)((i / BSB_K) & 1))) {
+                set_status(status, KMB_ERR_TIMEOUT_Y);
+                return;
+            }
+            if (ss == 0) {
+                const float* src = hand + ((size_t)w * BSB_K + hs) * 4 * GP;
+                ip0 = src[pl];
+                ip1 = src[GP + pl];
+                iq0 = src[2 * GP + pl];
+                iq1 = src[3 * GP + pl];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&hempty[w * BSB_K + hs]));
+        }
+#pragma unroll
+        for (int j = 0; j < CW; j++) {
+            const int q = qb - j;
+            const bool pa = act && q >= 0;
+            const BSBCol<RP>& x = cur[j];
+            const int t = pa ? o * W + q : 0;
+            const bool up = o > 0, lf = q > 0;
+            const int npt = (int)up + (int)lf;
+            const float ht0 = x.ht.x, ht1 = x.ht.y;
+            // ---- successors: outer (row below) first, then inner (column to the right)
+            const float a0 = PO0[j] + ip0, a1 = PO1[j] + ip1;
+            const float ab0 = QO0[j] + iq0, ab1 = QO1[j] + iq1;
+            float gh0 = cth * a0 + sth * a1;
+            float gh1 = -sth * a0 + cth * a1;
+            if (pa) {
+                const float hat0 = cth * ht0 - sth * ht1, hat1 = sth * ht0 + cth * ht1;
+                gth += -a0 * hat1 + a1 * hat0;
+            }
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                if (r >= R) continue;
+                gh0 += x.c[r].x * x.dy[r];
+                gh1 += x.c[r].y * x.dy[r];
+            }
+            const float dt = x.dt, lam = x.lam;
+            const float bu0 = x.bu.x, bu1 = x.bu.y;
+            const float gam = lam * dt;
+            const float gbu0 = gam * gh0 + ab0, gbu1 = gam * gh1 + ab1;
+            float gdt = lam * (bu0 * gh0 + bu1 * gh1);
+            float glam = dt * (bu0 * gh0 + bu1 * gh1);
+            float np0 = 0.0f, np1 = 0.0f, nq0 = 0.0f, nq1 = 0.0f;
+            if (npt > 0) {
+                // the inner predecessor's h and B*u: the next column's own values, or loaded for the last
+                const float2 lh = j + 1 < CW ? cur[j + 1 < CW ? j + 1 : j].ht : x.lh;
+                const float2 lb = j + 1 < CW ? cur[j + 1 < CW ? j + 1 : j].bu : x.lb;
+                float sh0 = 0.0f, sh1 = 0.0f, sb0 = 0.0f, sb1 = 0.0f;
+                if (up) {
+                    sh0 += cth * x.uh.x - sth * x.uh.y;
+                    sh1 += sth * x.uh.x + cth * x.uh.y;
+                    sb0 += x.ub.x;
+                    sb1 += x.ub.y;
+                }
+                if (lf) {
+                    sh0 += cth * lh.x - sth * lh.y;
+                    sh1 += sth * lh.x + cth * lh.y;
+                    sb0 += lb.x;
+                    sb1 += lb.y;
+                }
+                const float inv = 1.0f / (float)npt;
+                const float sc = (1.0f - lam) * dt * inv;
+                const float z0 = dt * A0, z1 = dt * A1;
+                const float al0 = kmb_exp(z0, s.fast), al1 = kmb_exp(z1, s.fast);
+                const float dal0 = (sh0 + sc * sb0) * gh0, dal1 = (sh1 + sc * sb1) * gh1;
+                const float dz0 = hok ? kmb_dexp(z0, al0, s.fast) * dal0 : 0.0f;
+                const float dz1 = hok ? kmb_dexp(z1, al1, s.fast) * dal1 : 0.0f;
+                gdt += dz0 * A0 + dz1 * A1;
+                if (pa) {
+                    gA0 += dz0 * dt;
+                    gA1 += dz1 * dt;
+                }
+                const float ds = al0 * sb0 * gh0 + al1 * sb1 * gh1;
+                gdt += (1.0f - lam) * inv * ds;
+                glam -= dt * inv * ds;
+                // what the predecessors pull from this point
+                const float coef = (1.0f - lam) * dt / (float)npt;
+                np0 = al0 * gh0;
+                np1 = al1 * gh1;
+                nq0 = coef * al0 * gh0;
+                nq1 = coef * al1 * gh1;
+            }
+            if (!hok) np0 = np1 = nq0 = nq1 = 0.0f;
+            if (pa) {
+                PO0[j] = np0; PO1[j] = np1; QO0[j] = nq0; QO1[j] = nq1;
+            }
+            ip0 = np0; ip1 = np1; iq0 = nq0; iq1 = nq1;
+            // ---- stores
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                if (r >= R) continue;
+                const int c = t * NR + r * N;
+                if (pa && hok) {
+                    const float2 vc = make_float2(x.dy[r] * ht0, x.dy[r] * ht1);
+                    const float2 vb = make_float2(gbu0 * x.u[r], gbu1 * x.u[r]);
+                    if (ovw) {
+                        *(float2*)(dC + c) = vc;
+                        *(float2*)(dB + c) = vb;
+                    } else {
+                        // one addition each (old + value): no read of the old value in the chain
+                        atomicAdd(dC + c, vc.x);
+                        atomicAdd(dC + c + 1, vc.y);
+                        atomicAdd(dB + c, vb.x);
+                        atomicAdd(dB + c + 1, vb.y);
+                    }
+                }
+                float part = gbu0 * x.b[r].x + gbu1 * x.b[r].y;
+                part = group_sum<GP>(part);
+                if (pa && pl == 0) {
+                    if (assign) du[t * R + r] = part;
+                    else du[t * R + r] += part;
+                }
+            }
+            gdt = group_sum<GP>(gdt);
+            glam = group_sum<GP>(glam);
+            if (pa && pl == 0) {
+                if (assign) {
+                    if (ddt) ddt[t] = gdt;
+                    if (dlam) dlam[t] = glam;
+                } else {
+                    if (ddt) ddt[t] += gdt;
+                    if (dlam) dlam[t] += glam;
+                }
+            }
+            // the strip's leftmost processed column feeds the strip on the left
+            if (q >= 0) { ob0 = ip0; ob1 = ip1; oq0 = iq0; oq1 = iq1; }
+        }
+        // ---- the last slot's output goes to warp w + 1 (row i - (SPW - 1))
+        const int ro = i - (SPW - 1);
+        if (w + 1 < nw && ro >= 0 && ro < H) {   // warp-uniform
+            const int hs = ro & (BSB_K - 1);
+            if (ro >= BSB_K && !mbar_wait(smem_u32(&hempty[(w + 1) * BSB_K + hs]), (uint32_t)(((ro / BSB_K) & 1) ^ 1))) {
+                set_status(status, KMB_ERR_TIMEOUT_Y);
+                return;
+            }
+            if (ss == SPW - 1) {
+                float* dst = hand + ((size_t)(w + 1) * BSB_K + hs) * 4 * GP;
+                dst[pl] = ob0;
+                dst[GP + pl] = ob1;
+                dst[2 * GP + pl] = oq0;
+                dst[3 * GP + pl] = oq1;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&hfull[(w + 1) * BSB_K + hs]));
+        }
+#pragma unroll
+        for (int j = 0; j < CW; j++) cur[j] = nxt[j];
+    }
+    // ---- dA_log and dtheta partials of this CTA's pairs, in a fixed order
+    red[threadIdx.x * 3 + 0] = gA0;
+    red[threadIdx.x * 3 + 1] = gA1;
+    red[threadIdx.x * 3 + 2] = gth;
+    __syncthreads();
+    if (threadIdx.x < GP) {
+        float t0 = 0.0f, t1 = 0.0f, tt = 0.0f;
+        for (int j = 0; j < nw * SPW; j++) {
+            const int src = (j / SPW) * 32 + (j % SPW) * GP + threadIdx.x;
+            t0 += red[src * 3 + 0];
+            t1 += red[src * 3 + 1];
+            tt += red[src * 3 + 2];
+        }
+        const int p = ln.g * GP + threadIdx.x;
+        if (2 * p < N) g.pA[(long long)b * N + 2 * p] = t0;
+        if (2 * p + 1 < N) g.pA[(long long)b * N + 2 * p + 1] = t1;
+        if (p < 32) g.pth[(long long)b * 32 + p] = tt;
+    }
+}
+
 // out[i] (+)= sum_g part[g * n + i], g = 0 .. NG-1 in order
 __global__ void bs_group_reduce(const float* __restrict__ part, float* __restrict__ out, long long n, int ng,
                                 int accumulate) {
@@ -1139,6 +1450,8 @@ int* device_status();
 // forward choice of this host thread: strips (with staged rows where possible), strips loading rows
 // directly, or the level kernels; and the path of the last forward
 static thread_local int tl_bs_no_strips = 0, tl_bs_no_staging = 0, tl_bs_path = -1;
+// backward choice (1: strips where the shape allows, 0: level kernels) and the path of the last backward
+static thread_local int tl_bs_bwd_strips = 1, tl_bs_bwd_path = -1;
 
 // Device copy of the wavefront plan of `dims` (level starts [nlev + 1], then the
 // points of every level [L]), cached per host thread, device and shape.
@@ -1336,6 +1649,43 @@ static void bs_bwd_dispatch(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
         default: bs_bwd_launch<T, 8>(s, g, st); break;
     }
 }
+// The systolic backward for 2D grids, R in {1, 2, 4}, N even, when the strips fit in 8 warps.  false: not taken.
+constexpr int BSB_CW = 2;
+static bool bs_bwd_strips_launch(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
+    if (!tl_bs_bwd_strips || s.nd != 2 || !(s.R == 1 || s.R == 2 || s.R == 4) || s.N % 2) return false;
+    const int spw = 32 / s.GP;
+    const int nstrips = (s.dims[1] + BSB_CW - 1) / BSB_CW;
+    const int nw = (nstrips + spw - 1) / spw;
+    if (nw > 8) return false;
+    int* status = device_status();
+    if (!status) return false;
+    const size_t sm = (size_t)nw * BSB_K * 4 * s.GP * sizeof(float) + 2 * nw * BSB_K * sizeof(uint64_t) +
+                      (size_t)nw * 32 * 3 * sizeof(float);
+    const dim3 grid((unsigned)(s.batch * s.NG));
+    auto go = [&](auto kern) { kern<<<grid, nw * 32, sm, st>>>(s, g, status); };
+#define KMB_BSB_R(TT, GPV)                                                  \
+    do {                                                                    \
+        if (s.R == 1) go(blockscan_bwd_strips<TT, GPV, 1, BSB_CW>);         \
+        else if (s.R == 2) go(blockscan_bwd_strips<TT, GPV, 2, BSB_CW>);    \
+        else go(blockscan_bwd_strips<TT, GPV, 4, BSB_CW>);                  \
+    } while (0)
+#define KMB_BSB_GP(TT)                          \
+    do {                                        \
+        switch (s.GP) {                         \
+            case 1: KMB_BSB_R(TT, 1); break;    \
+            case 2: KMB_BSB_R(TT, 2); break;    \
+            case 4: KMB_BSB_R(TT, 4); break;    \
+            default: KMB_BSB_R(TT, 8); break;   \
+        }                                       \
+    } while (0)
+    if (s.bf16) KMB_BSB_GP(__nv_bfloat16);
+    else KMB_BSB_GP(float);
+#undef KMB_BSB_GP
+#undef KMB_BSB_R
+    tl_bs_bwd_path = 1;
+    return true;
+}
+
 static void group_reduce(const float* part, float* out, long long n, int ng, int accumulate, cudaStream_t st) {
     bs_group_reduce<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, out, n, ng, accumulate);
 }
@@ -1349,6 +1699,8 @@ extern "C" void kmb_blockscan_set_strips(int mode) {
     tl_bs_no_staging = mode == 2 ? 1 : 0;
 }
 extern "C" int kmb_blockscan_last_forward_path(void) { return tl_bs_path; }
+extern "C" void kmb_blockscan_set_backward_strips(int on) { tl_bs_bwd_strips = on ? 1 : 0; }
+extern "C" int kmb_blockscan_last_backward_path(void) { return tl_bs_bwd_path; }
 
 extern "C" int kmb_blockscan_forward(const KMBlockScanParams* p, long batch, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
@@ -1405,8 +1757,8 @@ extern "C" int kmb_blockscan_forward(const KMBlockScanParams* p, long batch, voi
     return e == cudaSuccess ? 0 : set_cuda_error("blockscan_fwd", e);
 }
 
-extern "C" int kmb_blockscan_backward(const KMBlockScanParams* p, long batch, const float* dy,
-                                      const KMBlockScanGrads* gr, void* stream) {
+extern "C" int kmb_blockscan_backward_ex(const KMBlockScanParams* p, long batch, const float* dy,
+                                         const KMBlockScanGrads* gr, int overwrite, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
     if (!dy || !gr || !gr->dB || !gr->dC || !gr->du) return set_error("blockscan backward: dy, dB, dC, du required");
     BSDesc s;
@@ -1426,17 +1778,38 @@ extern "C" int kmb_blockscan_backward(const KMBlockScanParams* p, long batch, co
     g.pdu = g.pth + (size_t)batch * 32;
     g.pddt = g.pdu + (size_t)s.NG * ny;
     g.pdlam = g.pddt + (size_t)s.NG * nl;
-    if (s.bf16) bs_bwd_dispatch<__nv_bfloat16>(s, g, st);
-    else bs_bwd_dispatch<float>(s, g, st);
+    g.overwrite = overwrite ? 1 : 0;
+    if (!bs_bwd_strips_launch(s, g, st)) {
+        tl_bs_bwd_path = 0;
+        if (overwrite) {   // the level kernels accumulate: clear the outputs first
+            cudaError_t e = cudaSuccess;
+            const size_t nbc = ny * s.N * sizeof(float);
+            if (e == cudaSuccess) e = cudaMemsetAsync(gr->dB, 0, nbc, st);
+            if (e == cudaSuccess) e = cudaMemsetAsync(gr->dC, 0, nbc, st);
+            if (e == cudaSuccess) e = cudaMemsetAsync(gr->du, 0, ny * sizeof(float), st);
+            if (e == cudaSuccess && gr->ddt) e = cudaMemsetAsync(gr->ddt, 0, nl * sizeof(float), st);
+            if (e == cudaSuccess && gr->dlambda) e = cudaMemsetAsync(gr->dlambda, 0, nl * sizeof(float), st);
+            if (e != cudaSuccess) return set_cuda_error("blockscan backward memset", e);
+            g.overwrite = 0;
+        }
+        if (s.bf16) bs_bwd_dispatch<__nv_bfloat16>(s, g, st);
+        else bs_bwd_dispatch<float>(s, g, st);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("blockscan_bwd", e);
     if (s.NG > 1) {
-        group_reduce(g.pdu, gr->du, (long long)ny, s.NG, 1, st);
-        if (gr->ddt) group_reduce(g.pddt, gr->ddt, (long long)nl, s.NG, 1, st);
-        if (gr->dlambda) group_reduce(g.pdlam, gr->dlambda, (long long)nl, s.NG, 1, st);
+        const int acc = g.overwrite ? 0 : 1;
+        group_reduce(g.pdu, gr->du, (long long)ny, s.NG, acc, st);
+        if (gr->ddt) group_reduce(g.pddt, gr->ddt, (long long)nl, s.NG, acc, st);
+        if (gr->dlambda) group_reduce(g.pdlam, gr->dlambda, (long long)nl, s.NG, acc, st);
     }
     if (gr->dA_log) bs_reduce_add<<<1, 64, 0, st>>>(g.pA, gr->dA_log, s.N, batch, s.N);
     if (gr->dtheta && s.N >= 2) bs_reduce_add<<<1, 32, 0, st>>>(g.pth, gr->dtheta, s.N / 2, batch, 32);
     e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("blockscan reduce", e);
+}
+
+extern "C" int kmb_blockscan_backward(const KMBlockScanParams* p, long batch, const float* dy,
+                                      const KMBlockScanGrads* gr, void* stream) {
+    return kmb_blockscan_backward_ex(p, batch, dy, gr, 0, stream);
 }

@@ -49,11 +49,22 @@ typedef struct {
  * forward's path: 2 staged strips, 1 strips, 0 level kernels, -1 none yet. */
 void kmb_blockscan_set_strips(int mode);
 int kmb_blockscan_last_forward_path(void);
+/* Backward kernel choice, per host thread: on (default) 2D grids with R in
+ * {1, 2, 4} whose column strips fit in 8 warps use the systolic strip backward;
+ * off: always the level-synchronous kernels.  The last backward's path: 1
+ * strips, 0 level kernels, -1 none yet. */
+void kmb_blockscan_set_backward_strips(int on);
+int kmb_blockscan_last_backward_path(void);
 /* No counterpart in the reference API (see above): batched Scan-B forward. */
 int kmb_blockscan_forward(const KMBlockScanParams *p, long batch, void *stream);
 /* No counterpart in the reference API: exact Scan-B backward; dy is [batch, L, R]. */
 int kmb_blockscan_backward(const KMBlockScanParams *p, long batch, const float *dy,
                            const KMBlockScanGrads *g, void *stream);
+/* No counterpart in the reference API: the same backward; overwrite = 1 assigns
+ * dB, dC, du, ddt and dlambda instead of accumulating into them (dA_log and
+ * dtheta still accumulate), so the caller need not clear them first. */
+int kmb_blockscan_backward_ex(const KMBlockScanParams *p, long batch, const float *dy,
+                              const KMBlockScanGrads *g, int overwrite, void *stream);
 
 /* ---- Mamba-3 block (reference MambaBlock, src/mamba_block.c:106-125,509-528,746-773;
  * GPU counterpart cuda/mamba_block.cu:223-415), batched, device pointers ---------- */

@@ -117,3 +117,51 @@ def test_blockscan_strips_path(kmb, cuda, dims, N, R):
         assert torch.equal(b1, b0)
         assert torch.equal(h1, h0)
         torch.testing.assert_close(y1, y0, rtol=1e-5, atol=1e-5 * float(y0.abs().max()))
+
+
+@pytest.mark.parametrize("dims,N,R", [([64, 64], 64, 2), ([9, 13], 12, 1), ([16, 64], 64, 4), ([3, 8], 7, 2),
+                                      ([5, 80], 8, 2), ([4, 3], 2, 1), ([2, 130], 64, 1), ([7, 1], 16, 2),
+                                      ([1, 9], 64, 2)])
+def test_blockscan_backward_strips_path(kmb, cuda, dims, N, R):
+    """2D grids whose column strips fit in 8 warps take the systolic strip backward
+    (others the level kernels); its gradients match the level kernels' to rounding
+    (the per-point arithmetic is the same, the successor terms are summed in a
+    different association)."""
+    import torch
+    batch = 2
+    inp = po.gen_blockscan(dims, N, R, batch=batch, seed=N + 3 * R)
+    lib = kmb.lib()
+    L = int(np.prod(dims))
+    dy = torch.from_numpy(np.random.default_rng(5).standard_normal((batch, L, R)).astype(np.float32)).to(cuda)
+    gp = 1
+    while gp < 8 and gp < (N + 1) // 2:
+        gp *= 2
+    strips_ok = N % 2 == 0 and (((dims[1] + 1) // 2) + 32 // gp - 1) // (32 // gp) <= 8
+    out = {}
+    try:
+        for on in (1, 0):
+            lib.kmb_blockscan_set_backward_strips(on)
+            h, Bu, y, p, d = _fwd(kmb, cuda, inp)
+            res = {}
+            for ovw in (0, 1):
+                # overwrite: the per-point outputs start as NaN and must be assigned, not accumulated
+                z = lambda *s: torch.zeros(s, device=cuda)
+                f = (lambda *s: torch.full(s, float("nan"), device=cuda)) if ovw else z
+                g = dict(dB=f(batch, L, R * N), dC=f(batch, L, R * N), du=f(batch, L, R), ddt=f(batch, L),
+                         dlambda=f(batch, L), dA_log=z(N), dtheta=z(max(N // 2, 1)))
+                gr = kmb.KMBlockScanGrads(**{k: v.data_ptr() for k, v in g.items()})
+                kmb.check(lib.kmb_blockscan_backward_ex(C.byref(p), batch, dy.data_ptr(), C.byref(gr), ovw, None),
+                          "bwd")
+                torch.cuda.synchronize()
+                assert lib.kmb_device_status(None) == 0
+                assert lib.kmb_blockscan_last_backward_path() == (1 if on and strips_ok else 0)
+                res[ovw] = {k: v.cpu() for k, v in g.items()}
+            for k in res[0]:
+                assert torch.equal(res[0][k], res[1][k]), k
+            out[on] = res[0]
+    finally:
+        lib.kmb_blockscan_set_backward_strips(1)
+    for k in out[0]:
+        ref = out[0][k]
+        torch.testing.assert_close(out[1][k], ref, rtol=1e-4, atol=1e-5 * max(float(ref.abs().max()), 1e-30),
+                                   msg=lambda m: f"{k}: {m}")
