@@ -1134,7 +1134,7 @@ struct BSBCol {
     float2 b[RP], c[RP];
 };
 
-template <typename T, int GP, int RP, int CW>
+template <typename T, int GP, int RP, int CW, bool OVW>
 __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad g, int* status) {
     extern __shared__ __align__(16) unsigned char bsb_smem[];
     constexpr int SPW = 32 / GP;
@@ -1145,7 +1145,8 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int ss = ln.ps, pl = ln.pl;
     const int H = s.dims[0], W = s.dims[1];
-    const int N = s.N, R = s.R, NR = N * R;
+    constexpr int R = RP;   // the rank is a template parameter here
+    const int N = s.N, NR = N * R;
     const int nstrips = (W + CW - 1) / CW;
     const int st = w * SPW + ss;
     const int qb = W - 1 - st * CW;   // rightmost column of the strip
@@ -1166,12 +1167,12 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
     const float* __restrict__ dy = g.dy + b * L * R;
     float* dB = g.dB + b * L * NR + n0;
     float* dC = g.dC + b * L * NR + n0;
-    const bool direct = s.NG == 1, ovw = g.overwrite != 0;
+    const bool direct = s.NG == 1;
     const long long gofs = (long long)ln.g * s.batch;
     float* du = direct ? g.du + b * L * R : g.pdu + (gofs + b) * L * R;
     float* ddt = direct ? (g.ddt ? g.ddt + b * L : nullptr) : g.pddt + (gofs + b) * L;
     float* dlam = direct ? (g.dlam ? g.dlam + b * L : nullptr) : g.pdlam + (gofs + b) * L;
-    const bool assign = !direct || ovw;
+    const bool assign = !direct || OVW;
 
     // handoff slots [nw][K][4][GP] (P pair, Q pair of a strip's leftmost column), then their barriers
     float* hand = (float*)bsb_smem;
@@ -1188,35 +1189,45 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
     __syncthreads();
 
     const float2 z2 = make_float2(0.0f, 0.0f);
+    // Rows and columns outside the grid (pipeline fill and drain, a partial last strip) are clamped
+    // into it: their loads are valid and their results are never stored.  An absent predecessor
+    // loads as zeros, so the sums over predecessors need no branch.
     auto load_row = [&](BSBCol<RP>* c, int rr) {
-        const bool rok = st < nstrips && rr >= 0 && rr < H;
-        const int o = rok ? H - 1 - rr : 0;
+        const int o = min(max(H - 1 - rr, 0), H - 1);
 #pragma unroll
         for (int j = 0; j < CW; j++) {
-            const int q = qb - j;
-            const bool ok = rok && q >= 0;
-            const int t = ok ? o * W + q : 0;
+            const int q = max(qb - j, 0);
+            const int t = o * W + q;
             BSBCol<RP>& x = c[j];
             x.dt = ldv(dtp + t);
             x.lam = lamp ? ldv(lamp + t) : s.deflam;
-            const int tu = ok && o > 0 ? t - W : t;
-            x.ht = hok ? ld2(h + t * N) : z2;
-            x.bu = hok ? ld2(Bu + t * N) : z2;
-            x.uh = hok ? ld2(h + tu * N) : z2;
-            x.ub = hok ? ld2(Bu + tu * N) : z2;
+            const float* hp = h + t * N;
+            const float* bp = Bu + t * N;
+            x.ht = hok ? ld2(hp) : z2;
+            x.bu = hok ? ld2(bp) : z2;
+            x.uh = hok && o > 0 ? ld2(hp - W * N) : z2;
+            x.ub = hok && o > 0 ? ld2(bp - W * N) : z2;
             if (j == CW - 1) {
-                const int tl = ok && q > 0 ? t - 1 : t;
-                x.lh = hok ? ld2(h + tl * N) : z2;
-                x.lb = hok ? ld2(Bu + tl * N) : z2;
+                x.lh = hok && q > 0 ? ld2(hp - N) : z2;
+                x.lb = hok && q > 0 ? ld2(bp - N) : z2;
+            }
+            if constexpr (RP == 1) {
+                x.dy[0] = dy[t];
+                x.u[0] = ldv(u + t);
+            } else {
+#pragma unroll
+                for (int r = 0; r < RP; r += 2) {
+                    const float2 d2 = ld2(dy + t * R + r), u2 = ld2(u + t * R + r);
+                    x.dy[r] = d2.x;
+                    x.dy[r + 1] = d2.y;
+                    x.u[r] = u2.x;
+                    x.u[r + 1] = u2.y;
+                }
             }
 #pragma unroll
             for (int r = 0; r < RP; r++) {
-                const bool rk = r < R;
-                const int cc = t * NR + (rk ? r : 0) * N;
-                x.dy[r] = rk ? dy[t * R + r] : 0.0f;
-                x.u[r] = rk ? ldv(u + t * R + r) : 0.0f;
-                x.b[r] = rk && hok ? ld2(Bp + cc) : z2;
-                x.c[r] = rk && hok ? ld2(Cp + cc) : z2;
+                x.b[r] = hok ? ld2(Bp + t * NR + r * N) : z2;
+                x.c[r] = hok ? ld2(Cp + t * NR + r * N) : z2;
             }
         }
     };
@@ -1276,7 +1287,6 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
             }
 #pragma unroll
             for (int r = 0; r < RP; r++) {
-                if (r >= R) continue;
                 gh0 += x.c[r].x * x.dy[r];
                 gh1 += x.c[r].y * x.dy[r];
             }
@@ -1286,46 +1296,38 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
             const float gbu0 = gam * gh0 + ab0, gbu1 = gam * gh1 + ab1;
             float gdt = lam * (bu0 * gh0 + bu1 * gh1);
             float glam = dt * (bu0 * gh0 + bu1 * gh1);
-            float np0 = 0.0f, np1 = 0.0f, nq0 = 0.0f, nq1 = 0.0f;
-            if (npt > 0) {
-                // the inner predecessor's h and B*u: the next column's own values, or loaded for the last
-                const float2 lh = j + 1 < CW ? cur[j + 1 < CW ? j + 1 : j].ht : x.lh;
-                const float2 lb = j + 1 < CW ? cur[j + 1 < CW ? j + 1 : j].bu : x.lb;
-                float sh0 = 0.0f, sh1 = 0.0f, sb0 = 0.0f, sb1 = 0.0f;
-                if (up) {
-                    sh0 += cth * x.uh.x - sth * x.uh.y;
-                    sh1 += sth * x.uh.x + cth * x.uh.y;
-                    sb0 += x.ub.x;
-                    sb1 += x.ub.y;
-                }
-                if (lf) {
-                    sh0 += cth * lh.x - sth * lh.y;
-                    sh1 += sth * lh.x + cth * lh.y;
-                    sb0 += lb.x;
-                    sb1 += lb.y;
-                }
-                const float inv = 1.0f / (float)npt;
-                const float sc = (1.0f - lam) * dt * inv;
-                const float z0 = dt * A0, z1 = dt * A1;
-                const float al0 = kmb_exp(z0, s.fast), al1 = kmb_exp(z1, s.fast);
-                const float dal0 = (sh0 + sc * sb0) * gh0, dal1 = (sh1 + sc * sb1) * gh1;
-                const float dz0 = hok ? kmb_dexp(z0, al0, s.fast) * dal0 : 0.0f;
-                const float dz1 = hok ? kmb_dexp(z1, al1, s.fast) * dal1 : 0.0f;
-                gdt += dz0 * A0 + dz1 * A1;
-                if (pa) {
-                    gA0 += dz0 * dt;
-                    gA1 += dz1 * dt;
-                }
-                const float ds = al0 * sb0 * gh0 + al1 * sb1 * gh1;
-                gdt += (1.0f - lam) * inv * ds;
-                glam -= dt * inv * ds;
-                // what the predecessors pull from this point
-                const float coef = (1.0f - lam) * dt / (float)npt;
-                np0 = al0 * gh0;
-                np1 = al1 * gh1;
-                nq0 = coef * al0 * gh0;
-                nq1 = coef * al1 * gh1;
+            // predecessors (absent ones are zeros; with none, every term below is zero)
+            const float2 lh = !lf ? z2 : j + 1 < CW ? cur[j + 1 < CW ? j + 1 : j].ht : x.lh;
+            const float2 lb = !lf ? z2 : j + 1 < CW ? cur[j + 1 < CW ? j + 1 : j].bu : x.lb;
+            float sh0 = 0.0f, sh1 = 0.0f, sb0 = 0.0f, sb1 = 0.0f;
+            sh0 += cth * x.uh.x - sth * x.uh.y;
+            sh1 += sth * x.uh.x + cth * x.uh.y;
+            sb0 += x.ub.x;
+            sb1 += x.ub.y;
+            sh0 += cth * lh.x - sth * lh.y;
+            sh1 += sth * lh.x + cth * lh.y;
+            sb0 += lb.x;
+            sb1 += lb.y;
+            const float fnp = (float)max(npt, 1);
+            const float inv = 1.0f / fnp;
+            const float sc = (1.0f - lam) * dt * inv;
+            const float z0 = dt * A0, z1 = dt * A1;
+            const float al0 = kmb_exp(z0, s.fast), al1 = kmb_exp(z1, s.fast);
+            const float dal0 = (sh0 + sc * sb0) * gh0, dal1 = (sh1 + sc * sb1) * gh1;
+            const float dz0 = hok ? kmb_dexp(z0, al0, s.fast) * dal0 : 0.0f;
+            const float dz1 = hok ? kmb_dexp(z1, al1, s.fast) * dal1 : 0.0f;
+            gdt += dz0 * A0 + dz1 * A1;
+            if (pa) {
+                gA0 += dz0 * dt;
+                gA1 += dz1 * dt;
             }
+            const float ds = al0 * sb0 * gh0 + al1 * sb1 * gh1;
+            gdt += (1.0f - lam) * inv * ds;
+            glam -= dt * inv * ds;
+            // what the predecessors pull from this point
+            const float coef = (1.0f - lam) * dt / fnp;
+            float np0 = al0 * gh0, np1 = al1 * gh1;
+            float nq0 = coef * al0 * gh0, nq1 = coef * al1 * gh1;
             if (!hok) np0 = np1 = nq0 = nq1 = 0.0f;
             if (pa) {
                 PO0[j] = np0; PO1[j] = np1; QO0[j] = nq0; QO1[j] = nq1;
@@ -1334,12 +1336,11 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
             // ---- stores
 #pragma unroll
             for (int r = 0; r < RP; r++) {
-                if (r >= R) continue;
                 const int c = t * NR + r * N;
                 if (pa && hok) {
                     const float2 vc = make_float2(x.dy[r] * ht0, x.dy[r] * ht1);
                     const float2 vb = make_float2(gbu0 * x.u[r], gbu1 * x.u[r]);
-                    if (ovw) {
+                    if constexpr (OVW) {
                         *(float2*)(dC + c) = vc;
                         *(float2*)(dB + c) = vb;
                     } else {
@@ -1650,7 +1651,7 @@ static void bs_bwd_dispatch(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
     }
 }
 // The systolic backward for 2D grids, R in {1, 2, 4}, N even, when the strips fit in 8 warps.  false: not taken.
-constexpr int BSB_CW = 2;
+constexpr int BSB_CW = 2;   // columns per strip (4 measured slower: fewer warps, longer serial steps)
 static bool bs_bwd_strips_launch(const BSDesc& s, const BSGrad& g, cudaStream_t st) {
     if (!tl_bs_bwd_strips || s.nd != 2 || !(s.R == 1 || s.R == 2 || s.R == 4) || s.N % 2) return false;
     const int spw = 32 / s.GP;
@@ -1663,11 +1664,16 @@ static bool bs_bwd_strips_launch(const BSDesc& s, const BSGrad& g, cudaStream_t 
                       (size_t)nw * 32 * 3 * sizeof(float);
     const dim3 grid((unsigned)(s.batch * s.NG));
     auto go = [&](auto kern) { kern<<<grid, nw * 32, sm, st>>>(s, g, status); };
-#define KMB_BSB_R(TT, GPV)                                                  \
-    do {                                                                    \
-        if (s.R == 1) go(blockscan_bwd_strips<TT, GPV, 1, BSB_CW>);         \
-        else if (s.R == 2) go(blockscan_bwd_strips<TT, GPV, 2, BSB_CW>);    \
-        else go(blockscan_bwd_strips<TT, GPV, 4, BSB_CW>);                  \
+#define KMB_BSB_O(TT, GPV, RV)                                                      \
+    do {                                                                            \
+        if (g.overwrite) go(blockscan_bwd_strips<TT, GPV, RV, BSB_CW, true>);       \
+        else go(blockscan_bwd_strips<TT, GPV, RV, BSB_CW, false>);                  \
+    } while (0)
+#define KMB_BSB_R(TT, GPV)                                  \
+    do {                                                    \
+        if (s.R == 1) KMB_BSB_O(TT, GPV, 1);                \
+        else if (s.R == 2) KMB_BSB_O(TT, GPV, 2);           \
+        else KMB_BSB_O(TT, GPV, 4);                         \
     } while (0)
 #define KMB_BSB_GP(TT)                          \
     do {                                        \
@@ -1682,6 +1688,7 @@ static bool bs_bwd_strips_launch(const BSDesc& s, const BSGrad& g, cudaStream_t 
     else KMB_BSB_GP(float);
 #undef KMB_BSB_GP
 #undef KMB_BSB_R
+#undef KMB_BSB_O
     tl_bs_bwd_path = 1;
     return true;
 }
