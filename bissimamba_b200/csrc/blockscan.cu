@@ -1413,6 +1413,210 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
     }
 }
 
+// Forward for 2D grids, R in {1, 2, 4}, N even: the systolic strip pipeline of
+// blockscan_bwd_strips run forwards (rows top to bottom, columns left to
+// right), with the state pairs split into groups (CTA = (item, group of GP
+// pairs)) so that an item runs on NG CTAs.  Strips of CW columns are numbered
+// from the left; lane = (slot, pair), slot ss one row behind slot ss - 1.  The
+// predecessor form R(theta) h and B*u of a point stays in registers for the
+// next row (same column), moves along the strip in registers, to the next slot
+// by a shuffle and to the next warp through mbarrier-guarded shared-memory
+// slots (bounded waits).  Per point the arithmetic is blockscan_fwd_strips',
+// so h and B*u are bit-identical to it; y is summed over the GP pairs of the
+// group by shuffles and, with NG > 1, over the groups by bs_group_reduce in
+// group order.
+template <int RP>
+struct BSFCol {
+    float dt, lam, u[RP];
+    float2 b[RP], c[RP];
+};
+
+template <typename T, int GP, int RP, int CW>
+__global__ void __launch_bounds__(256, 1) blockscan_fwd_gstrips(BSDesc s, int* status) {
+    extern __shared__ __align__(16) unsigned char bsf_smem[];
+    constexpr int SPW = 32 / GP;
+    constexpr int R = RP;
+    using Ln = BSLanes<GP>;
+    const Ln ln(s);
+    const int b = ln.b, n0 = ln.n0;
+    const bool hok = ln.h0ok;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int ss = ln.ps, pl = ln.pl;
+    const int H = s.dims[0], W = s.dims[1];
+    const int N = s.N, NR = N * R;
+    const int nstrips = (W + CW - 1) / CW;
+    const int st = w * SPW + ss;
+    const int qa = st * CW;   // leftmost column of the strip
+    const float A0 = hok ? s.A[n0] : 0.0f, A1 = hok ? s.A[n0 + 1] : 0.0f;
+    float cth = 1.0f, sth = 0.0f;
+    if (hok) {
+        cth = cosf(s.theta[n0 >> 1]);
+        sth = sinf(s.theta[n0 >> 1]);
+    }
+    const long long L = s.L;
+    const T* __restrict__ u = (const T*)s.u + b * L * R;
+    const T* __restrict__ dtp = (const T*)s.dt + b * L;
+    const T* __restrict__ lamp = s.lam ? (const T*)s.lam + b * L : nullptr;
+    const T* __restrict__ Bp = (const T*)s.B + b * L * NR + n0;
+    const T* __restrict__ Cp = (const T*)s.C + b * L * NR + n0;
+    float* h = s.h + b * L * N + n0;
+    float* Bu = s.Bu + b * L * N + n0;
+    float* y = s.NG == 1 ? s.y + b * L * R : s.part + ((long long)ln.g * s.batch + b) * L * R;
+
+    float* hand = (float*)bsf_smem;   // [nw][K][4][GP]
+    uint64_t* hfull = (uint64_t*)(hand + (size_t)nw * BSB_K * 4 * GP);
+    uint64_t* hempty = hfull + nw * BSB_K;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nw * BSB_K; i++) {
+            mbar_init(smem_u32(&hfull[i]), 1);
+            mbar_init(smem_u32(&hempty[i]), 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const float2 z2 = make_float2(0.0f, 0.0f);
+    // rows and columns outside the grid (pipeline fill and drain, a partial last strip) are clamped
+    // into it: their loads are valid and their results are never stored
+    auto load_row = [&](BSFCol<RP>* c, int o) {
+        o = min(max(o, 0), H - 1);
+#pragma unroll
+        for (int j = 0; j < CW; j++) {
+            const int t = o * W + min(qa + j, W - 1);
+            BSFCol<RP>& x = c[j];
+            x.dt = ldv(dtp + t);
+            x.lam = lamp ? ldv(lamp + t) : s.deflam;
+            if constexpr (RP == 1) {
+                x.u[0] = ldv(u + t);
+            } else {
+#pragma unroll
+                for (int r = 0; r < RP; r += 2) {
+                    const float2 u2 = ld2(u + t * R + r);
+                    x.u[r] = u2.x;
+                    x.u[r + 1] = u2.y;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                x.b[r] = hok ? ld2(Bp + t * NR + r * N) : z2;
+                x.c[r] = hok ? ld2(Cp + t * NR + r * N) : z2;
+            }
+        }
+    };
+
+    float rh0[CW], rh1[CW], rb0[CW], rb1[CW];   // previous row of this strip's columns: R(theta) h, B*u
+#pragma unroll
+    for (int j = 0; j < CW; j++) rh0[j] = rh1[j] = rb0[j] = rb1[j] = 0.0f;
+    float ob0 = 0.0f, ob1 = 0.0f, oc0 = 0.0f, oc1 = 0.0f;   // this slot's output to the strip on its right
+    BSFCol<RP> cur[CW], nxt[CW];
+    load_row(cur, -ss);
+    const int nsteps = H + SPW - 1;
+    for (int i = 0; i < nsteps; i++) {
+        const int o = i - ss;
+        const bool act = st < nstrips && o >= 0 && o < H;
+        load_row(nxt, o + 1);
+        // ---- inner predecessor of the leftmost column: the strip on the left, same row
+        float lh0 = __shfl_up_sync(0xffffffffu, ob0, GP);
+        float lh1 = __shfl_up_sync(0xffffffffu, ob1, GP);
+        float lb0 = __shfl_up_sync(0xffffffffu, oc0, GP);
+        float lb1 = __shfl_up_sync(0xffffffffu, oc1, GP);
+        if (ss == 0) lh0 = lh1 = lb0 = lb1 = 0.0f;
+        if (w > 0 && i < H) {   // warp-uniform: slot 0 takes row i of warp w - 1's last strip
+            const int hs = i & (BSB_K - 1);
+            if (!mbar_wait(smem_u32(&hfull[w * BSB_K + hs]), (uint32_t)((i / BSB_K) & 1))) {
+                set_status(status, KMB_ERR_TIMEOUT_Y);
+                return;
+            }
+            if (ss == 0) {
+                const float* src = hand + ((size_t)w * BSB_K + hs) * 4 * GP;
+                lh0 = src[pl];
+                lh1 = src[GP + pl];
+                lb0 = src[2 * GP + pl];
+                lb1 = src[3 * GP + pl];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&hempty[w * BSB_K + hs]));
+        }
+#pragma unroll
+        for (int j = 0; j < CW; j++) {
+            const int q = qa + j;
+            const bool pa = act && q < W;
+            const BSFCol<RP>& x = cur[j];
+            const int t = pa ? o * W + q : 0;
+            const float dt = x.dt, lam = x.lam;
+            float bu0 = 0.0f, bu1 = 0.0f;
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                bu0 = __fmaf_rn(x.b[r].x, x.u[r], bu0);
+                bu1 = __fmaf_rn(x.b[r].y, x.u[r], bu1);
+            }
+            const float al0 = kmb_exp(dt * A0, s.fast), al1 = kmb_exp(dt * A1, s.fast);
+            float hn0 = 0.0f, hn1 = 0.0f, bacc0 = 0.0f, bacc1 = 0.0f;
+            int np = 0;
+            if (o > 0) {   // outer predecessor (o-1, q): this column's previous row
+                hn0 = __fmaf_rn(al0, rh0[j], hn0);
+                hn1 = __fmaf_rn(al1, rh1[j], hn1);
+                bacc0 += rb0[j];
+                bacc1 += rb1[j];
+                np++;
+            }
+            if (q > 0) {   // inner predecessor (o, q-1): the previous column of this row
+                hn0 = __fmaf_rn(al0, lh0, hn0);
+                hn1 = __fmaf_rn(al1, lh1, hn1);
+                bacc0 += lb0;
+                bacc1 += lb1;
+                np++;
+            }
+            if (np > 0) {
+                const float bs = (1.0f - lam) * dt / (float)np;
+                hn0 = __fmaf_rn(bs * al0, bacc0, hn0);
+                hn1 = __fmaf_rn(bs * al1, bacc1, hn1);
+            }
+            const float gm = lam * dt;
+            hn0 = __fmaf_rn(gm, bu0, hn0);
+            hn1 = __fmaf_rn(gm, bu1, hn1);
+            if (pa && hok) {
+                *(float2*)(h + t * N) = make_float2(hn0, hn1);
+                *(float2*)(Bu + t * N) = make_float2(bu0, bu1);
+            }
+            const float r0 = cth * hn0 - sth * hn1, r1 = sth * hn0 + cth * hn1;
+            if (pa) {
+                rh0[j] = r0; rh1[j] = r1; rb0[j] = bu0; rb1[j] = bu1;
+            }
+            lh0 = r0; lh1 = r1; lb0 = bu0; lb1 = bu1;
+            if (q < W) { ob0 = r0; ob1 = r1; oc0 = bu0; oc1 = bu1; }
+#pragma unroll
+            for (int r = 0; r < RP; r++) {
+                float part = x.c[r].x * hn0;
+                part = __fmaf_rn(x.c[r].y, hn1, part);
+                part = group_sum<GP>(hok ? part : 0.0f);
+                if (pa && pl == 0) y[t * R + r] = part;
+            }
+        }
+        // ---- the last slot's output goes to warp w + 1 (row i - (SPW - 1))
+        const int ro = i - (SPW - 1);
+        if (w + 1 < nw && ro >= 0 && ro < H) {   // warp-uniform
+            const int hs = ro & (BSB_K - 1);
+            if (ro >= BSB_K &&
+                !mbar_wait(smem_u32(&hempty[(w + 1) * BSB_K + hs]), (uint32_t)(((ro / BSB_K) & 1) ^ 1))) {
+                set_status(status, KMB_ERR_TIMEOUT_Y);
+                return;
+            }
+            if (ss == SPW - 1) {
+                float* dst = hand + ((size_t)(w + 1) * BSB_K + hs) * 4 * GP;
+                dst[pl] = ob0;
+                dst[GP + pl] = ob1;
+                dst[2 * GP + pl] = oc0;
+                dst[3 * GP + pl] = oc1;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&hfull[(w + 1) * BSB_K + hs]));
+        }
+#pragma unroll
+        for (int j = 0; j < CW; j++) cur[j] = nxt[j];
+    }
+}
+
 // out[i] (+)= sum_g part[g * n + i], g = 0 .. NG-1 in order
 __global__ void bs_group_reduce(const float* __restrict__ part, float* __restrict__ out, long long n, int ng,
                                 int accumulate) {
@@ -1448,9 +1652,8 @@ int set_error(const char* msg);
 int set_cuda_error(const char* where, cudaError_t e);
 enum { WS_BS_FWD = 3, WS_BS_SCRATCH = 4 };
 int* device_status();
-// forward choice of this host thread: strips (with staged rows where possible), strips loading rows
-// directly, or the level kernels; and the path of the last forward
-static thread_local int tl_bs_no_strips = 0, tl_bs_no_staging = 0, tl_bs_path = -1;
+// forward choice of this host thread (kmb_blockscan_set_strips modes 0-3) and the path of the last forward
+static thread_local int tl_bs_mode = 1, tl_bs_no_strips = 0, tl_bs_no_staging = 0, tl_bs_path = -1;
 // backward choice (1: strips where the shape allows, 0: level kernels) and the path of the last backward
 static thread_local int tl_bs_bwd_strips = 1, tl_bs_bwd_path = -1;
 
@@ -1693,6 +1896,40 @@ static bool bs_bwd_strips_launch(const BSDesc& s, const BSGrad& g, cudaStream_t 
     return true;
 }
 
+// The grouped strip forward for 2D grids, R in {1, 2, 4}, N even, when the strips fit in 8 warps.
+static bool bs_fwd_gstrips_launch(const BSDesc& s, cudaStream_t st) {
+    if (tl_bs_mode != 1 || s.nd != 2 || !(s.R == 1 || s.R == 2 || s.R == 4) || s.N % 2) return false;
+    const int spw = 32 / s.GP;
+    const int nstrips = (s.dims[1] + BSB_CW - 1) / BSB_CW;
+    const int nw = (nstrips + spw - 1) / spw;
+    if (nw > 8) return false;
+    int* status = device_status();
+    if (!status) return false;
+    const size_t sm = (size_t)nw * BSB_K * 4 * s.GP * sizeof(float) + 2 * nw * BSB_K * sizeof(uint64_t);
+    const dim3 grid((unsigned)(s.batch * s.NG));
+    auto go = [&](auto kern) { kern<<<grid, nw * 32, sm, st>>>(s, status); };
+#define KMB_BSF_R(TT, GPV)                                                    \
+    do {                                                                      \
+        if (s.R == 1) go(blockscan_fwd_gstrips<TT, GPV, 1, BSB_CW>);          \
+        else if (s.R == 2) go(blockscan_fwd_gstrips<TT, GPV, 2, BSB_CW>);     \
+        else go(blockscan_fwd_gstrips<TT, GPV, 4, BSB_CW>);                   \
+    } while (0)
+#define KMB_BSF_GP(TT)                          \
+    do {                                        \
+        switch (s.GP) {                         \
+            case 1: KMB_BSF_R(TT, 1); break;    \
+            case 2: KMB_BSF_R(TT, 2); break;    \
+            case 4: KMB_BSF_R(TT, 4); break;    \
+            default: KMB_BSF_R(TT, 8); break;   \
+        }                                       \
+    } while (0)
+    if (s.bf16) KMB_BSF_GP(__nv_bfloat16);
+    else KMB_BSF_GP(float);
+#undef KMB_BSF_GP
+#undef KMB_BSF_R
+    return true;
+}
+
 static void group_reduce(const float* part, float* out, long long n, int ng, int accumulate, cudaStream_t st) {
     bs_group_reduce<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, out, n, ng, accumulate);
 }
@@ -1702,6 +1939,7 @@ static void group_reduce(const float* part, float* out, long long n, int ng, int
 using namespace kmb;
 
 extern "C" void kmb_blockscan_set_strips(int mode) {
+    tl_bs_mode = mode;
     tl_bs_no_strips = mode == 0 ? 1 : 0;
     tl_bs_no_staging = mode == 2 ? 1 : 0;
 }
@@ -1717,6 +1955,13 @@ extern "C" int kmb_blockscan_forward(const KMBlockScanParams* p, long batch, voi
     if (s.NG > 1) {
         s.part = (float*)workspace(WS_BS_FWD, (size_t)s.NG * ny * sizeof(float));
         if (!s.part) return set_error("workspace allocation failed");
+    }
+    // 2D grids, N even: the grouped systolic strip kernel (NG CTAs per item)
+    if (bs_fwd_gstrips_launch(s, st)) {
+        tl_bs_path = 3;
+        if (s.NG > 1) group_reduce(s.part, s.y, ny, s.NG, 0, st);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? 0 : set_cuda_error("blockscan_fwd_gstrips", e);
     }
     // 2D grids with an inner extent <= 64: the systolic strip kernel (one CTA per item)
     if (s.nd == 2 && s.dims[1] <= 64 && s.N <= 64 && (s.R == 1 || s.R == 2 || s.R == 4) && !tl_bs_no_strips) {

@@ -42,11 +42,15 @@ typedef struct {
 } KMBlockScanGrads;
 
 /* Forward kernel choice, per host thread (for tests and comparison).  mode 1
- * (default): 2D grids with an inner extent <= 64, N <= 64, R in {1, 2, 4} use the
- * systolic strip kernel, with rows staged through shared memory by bulk copies
- * when the inner extent and N are multiples of 8; 2: the strip kernel always
- * loads rows directly; 0: always the level-synchronous kernels.  The last
- * forward's path: 2 staged strips, 1 strips, 0 level kernels, -1 none yet. */
+ * (default): 2D grids with N even, R in {1, 2, 4} whose column strips fit in 8
+ * warps use the grouped systolic strip kernel (the state pairs split over
+ * several CTAs per item); other 2D grids with an inner extent <= 64, N <= 64,
+ * R in {1, 2, 4} use the one-CTA-per-item strip kernel, with rows staged
+ * through shared memory by bulk copies when the inner extent and N are
+ * multiples of 8; 3: skip the grouped kernel; 2: the one-CTA-per-item strip
+ * kernel always loads rows directly; 0: always the level-synchronous kernels.
+ * The last forward's path: 3 grouped strips, 2 staged strips, 1 strips, 0 level
+ * kernels, -1 none yet. */
 void kmb_blockscan_set_strips(int mode);
 int kmb_blockscan_last_forward_path(void);
 /* Backward kernel choice, per host thread: on (default) 2D grids with R in

@@ -83,20 +83,22 @@ def test_blockscan_backward(kmb, cuda, dims, N, R, fl):
 
 
 @pytest.mark.parametrize("dims,N,R", [([64, 64], 64, 2), ([9, 13], 12, 1), ([16, 64], 64, 4), ([3, 8], 7, 2),
-                                      ([8, 16], 16, 4), ([5, 8], 16, 2)])
+                                      ([8, 16], 16, 4), ([5, 8], 16, 2), ([4, 3], 2, 1), ([1, 9], 64, 2),
+                                      ([7, 1], 16, 2), ([5, 40], 8, 4)])
 def test_blockscan_strips_path(kmb, cuda, dims, N, R):
-    """2D grids with an inner extent <= 64 run the systolic strip forward (rows staged
-    through shared memory where the shape allows, else loaded directly): the path is
-    taken, and h and Bu equal the level-synchronous kernels bit for bit (same
-    per-point arithmetic); y agrees to rounding (its sum over the states is ordered
-    differently)."""
+    """2D grids run a systolic strip forward: the grouped one (several CTAs per item)
+    when N is even, else (and in mode 3) the one-CTA-per-item kernel, with rows
+    staged through shared memory where the shape allows, else loaded directly.  The
+    path is taken, and h and Bu equal the level-synchronous kernels bit for bit
+    (same per-point arithmetic); y agrees to rounding (its sum over the states is
+    ordered differently)."""
     import torch
     inp = po.gen_blockscan(dims, N, R, batch=2, seed=N + R)
     lib = kmb.lib()
     staged_ok = dims[1] % 8 == 0 and N % 8 == 0   # fp32 inputs at 64 x 64, N 64 exceed the stage budget
     out = {}
     try:
-        for mode in (1, 2, 0):
+        for mode in (1, 3, 2, 0):
             lib.kmb_blockscan_set_strips(mode)
             h, Bu, y, _, _ = _fwd(kmb, cuda, inp)
             path = lib.kmb_blockscan_last_forward_path()
@@ -105,6 +107,8 @@ def test_blockscan_strips_path(kmb, cuda, dims, N, R):
                 assert path == 0
             elif mode == 2:
                 assert path == 1
+            elif mode == 1 and N % 2 == 0:
+                assert path == 3
             else:
                 # staged when the shape allows and three staged rows per strip fit in shared memory
                 assert path == (2 if dims in ([8, 16], [5, 8]) else 1 if not staged_ok else path) and path in (1, 2)
@@ -112,7 +116,7 @@ def test_blockscan_strips_path(kmb, cuda, dims, N, R):
     finally:
         lib.kmb_blockscan_set_strips(1)
     h0, b0, y0 = out[0]
-    for mode in (1, 2):
+    for mode in (1, 3, 2):
         h1, b1, y1 = out[mode]
         assert torch.equal(b1, b0)
         assert torch.equal(h1, h0)
