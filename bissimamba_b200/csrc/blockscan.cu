@@ -1237,10 +1237,11 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
     for (int j = 0; j < CW; j++) PO0[j] = PO1[j] = QO0[j] = QO1[j] = 0.0f;
     float ob0 = 0.0f, ob1 = 0.0f, oq0 = 0.0f, oq1 = 0.0f;   // this slot's output to the strip on its left
     float gA0 = 0.0f, gA1 = 0.0f, gth = 0.0f;
-    BSBCol<RP> cur[CW], nxt[CW];
-    load_row(cur, -ss);
+    // two row buffers used in turn (no register copy that would wait for the prefetch to land)
+    BSBCol<RP> bufA[CW], bufB[CW];
+    load_row(bufA, -ss);
     const int nsteps = H + SPW - 1;
-    for (int i = 0; i < nsteps; i++) {
+    auto step = [&](const int i, BSBCol<RP>* cur, BSBCol<RP>* nxt) -> bool {
         const int rr = i - ss;
         const bool act = st < nstrips && rr >= 0 && rr < H;
         const int o = H - 1 - rr;
@@ -1255,7 +1256,7 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
             const int hs = i & (BSB_K - 1);
             if (!mbar_wait(smem_u32(&hfull[w * BSB_K + hs]), (uint32_t)((i / BSB_K) & 1))) {
                 set_status(status, KMB_ERR_TIMEOUT_Y);
-                return;
+                return false;
             }
             if (ss == 0) {
                 const float* src = hand + ((size_t)w * BSB_K + hs) * 4 * GP;
@@ -1378,7 +1379,7 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
             const int hs = ro & (BSB_K - 1);
             if (ro >= BSB_K && !mbar_wait(smem_u32(&hempty[(w + 1) * BSB_K + hs]), (uint32_t)(((ro / BSB_K) & 1) ^ 1))) {
                 set_status(status, KMB_ERR_TIMEOUT_Y);
-                return;
+                return false;
             }
             if (ss == SPW - 1) {
                 float* dst = hand + ((size_t)(w + 1) * BSB_K + hs) * 4 * GP;
@@ -1390,8 +1391,11 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&hfull[(w + 1) * BSB_K + hs]));
         }
-#pragma unroll
-        for (int j = 0; j < CW; j++) cur[j] = nxt[j];
+        return true;
+    };
+    for (int i = 0; i < nsteps; i += 2) {
+        if (!step(i, bufA, bufB)) return;
+        if (i + 1 < nsteps && !step(i + 1, bufB, bufA)) return;
     }
     // ---- dA_log and dtheta partials of this CTA's pairs, in a fixed order
     red[threadIdx.x * 3 + 0] = gA0;
@@ -1508,10 +1512,11 @@ __global__ void __launch_bounds__(256, 1) blockscan_fwd_gstrips(BSDesc s, int* s
 #pragma unroll
     for (int j = 0; j < CW; j++) rh0[j] = rh1[j] = rb0[j] = rb1[j] = 0.0f;
     float ob0 = 0.0f, ob1 = 0.0f, oc0 = 0.0f, oc1 = 0.0f;   // this slot's output to the strip on its right
-    BSFCol<RP> cur[CW], nxt[CW];
-    load_row(cur, -ss);
+    // two row buffers used in turn (no register copy that would wait for the prefetch to land)
+    BSFCol<RP> bufA[CW], bufB[CW];
+    load_row(bufA, -ss);
     const int nsteps = H + SPW - 1;
-    for (int i = 0; i < nsteps; i++) {
+    auto step = [&](const int i, BSFCol<RP>* cur, BSFCol<RP>* nxt) -> bool {
         const int o = i - ss;
         const bool act = st < nstrips && o >= 0 && o < H;
         load_row(nxt, o + 1);
@@ -1525,7 +1530,7 @@ __global__ void __launch_bounds__(256, 1) blockscan_fwd_gstrips(BSDesc s, int* s
             const int hs = i & (BSB_K - 1);
             if (!mbar_wait(smem_u32(&hfull[w * BSB_K + hs]), (uint32_t)((i / BSB_K) & 1))) {
                 set_status(status, KMB_ERR_TIMEOUT_Y);
-                return;
+                return false;
             }
             if (ss == 0) {
                 const float* src = hand + ((size_t)w * BSB_K + hs) * 4 * GP;
@@ -1600,7 +1605,7 @@ __global__ void __launch_bounds__(256, 1) blockscan_fwd_gstrips(BSDesc s, int* s
             if (ro >= BSB_K &&
                 !mbar_wait(smem_u32(&hempty[(w + 1) * BSB_K + hs]), (uint32_t)(((ro / BSB_K) & 1) ^ 1))) {
                 set_status(status, KMB_ERR_TIMEOUT_Y);
-                return;
+                return false;
             }
             if (ss == SPW - 1) {
                 float* dst = hand + ((size_t)(w + 1) * BSB_K + hs) * 4 * GP;
@@ -1612,8 +1617,11 @@ __global__ void __launch_bounds__(256, 1) blockscan_fwd_gstrips(BSDesc s, int* s
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&hfull[(w + 1) * BSB_K + hs]));
         }
-#pragma unroll
-        for (int j = 0; j < CW; j++) cur[j] = nxt[j];
+        return true;
+    };
+    for (int i = 0; i < nsteps; i += 2) {
+        if (!step(i, bufA, bufB)) return;
+        if (i + 1 < nsteps && !step(i + 1, bufB, bufA)) return;
     }
 }
 
