@@ -1436,7 +1436,7 @@ struct BSFCol {
 };
 
 template <typename T, int GP, int RP, int CW>
-__global__ void __launch_bounds__(256, 1) blockscan_fwd_gstrips(BSDesc s, int* status) {
+__global__ void __launch_bounds__(CW == 1 ? 512 : 256, 1) blockscan_fwd_gstrips(BSDesc s, int* status) {
     extern __shared__ __align__(16) unsigned char bsf_smem[];
     constexpr int SPW = 32 / GP;
     constexpr int R = RP;
@@ -1905,12 +1905,14 @@ static bool bs_bwd_strips_launch(const BSDesc& s, const BSGrad& g, cudaStream_t 
 }
 
 // The grouped strip forward for 2D grids, R in {1, 2, 4}, N even, when the strips fit in 8 warps.
+// columns per forward strip (one column, in 16-warp CTAs, measured 1 % slower per block step)
+constexpr int BSF_CW = 2;
 static bool bs_fwd_gstrips_launch(const BSDesc& s, cudaStream_t st) {
     if (tl_bs_mode != 1 || s.nd != 2 || !(s.R == 1 || s.R == 2 || s.R == 4) || s.N % 2) return false;
     const int spw = 32 / s.GP;
-    const int nstrips = (s.dims[1] + BSB_CW - 1) / BSB_CW;
+    const int nstrips = (s.dims[1] + BSF_CW - 1) / BSF_CW;
     const int nw = (nstrips + spw - 1) / spw;
-    if (nw > 8) return false;
+    if (nw > (BSF_CW == 1 ? 16 : 8)) return false;
     int* status = device_status();
     if (!status) return false;
     const size_t sm = (size_t)nw * BSB_K * 4 * s.GP * sizeof(float) + 2 * nw * BSB_K * sizeof(uint64_t);
@@ -1918,9 +1920,9 @@ static bool bs_fwd_gstrips_launch(const BSDesc& s, cudaStream_t st) {
     auto go = [&](auto kern) { kern<<<grid, nw * 32, sm, st>>>(s, status); };
 #define KMB_BSF_R(TT, GPV)                                                    \
     do {                                                                      \
-        if (s.R == 1) go(blockscan_fwd_gstrips<TT, GPV, 1, BSB_CW>);          \
-        else if (s.R == 2) go(blockscan_fwd_gstrips<TT, GPV, 2, BSB_CW>);     \
-        else go(blockscan_fwd_gstrips<TT, GPV, 4, BSB_CW>);                   \
+        if (s.R == 1) go(blockscan_fwd_gstrips<TT, GPV, 1, BSF_CW>);          \
+        else if (s.R == 2) go(blockscan_fwd_gstrips<TT, GPV, 2, BSF_CW>);     \
+        else go(blockscan_fwd_gstrips<TT, GPV, 4, BSF_CW>);                   \
     } while (0)
 #define KMB_BSF_GP(TT)                          \
     do {                                        \
