@@ -1134,14 +1134,15 @@ struct BSBCol {
     float2 b[RP], c[RP];
 };
 
-template <typename T, int GP, int RP, int CW, bool OVW>
+template <typename T, int GP, int RP, int CW, bool OVW, bool FULL>
 __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad g, int* status) {
     extern __shared__ __align__(16) unsigned char bsb_smem[];
     constexpr int SPW = 32 / GP;
     using Ln = BSLanes<GP>;
     const Ln ln(s);
     const int b = ln.b, n0 = ln.n0;
-    const bool hok = ln.h0ok;   // N is even: a pair is whole or absent
+    // N is even: a pair is whole or absent; FULL (N a multiple of 2 GP): every lane has one
+    const bool hok = FULL || ln.h0ok;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int ss = ln.ps, pl = ln.pl;
     const int H = s.dims[0], W = s.dims[1];
@@ -1435,7 +1436,7 @@ struct BSFCol {
     float2 b[RP], c[RP];
 };
 
-template <typename T, int GP, int RP, int CW>
+template <typename T, int GP, int RP, int CW, bool FULL>
 __global__ void __launch_bounds__(CW == 1 ? 512 : 256, 1) blockscan_fwd_gstrips(BSDesc s, int* status) {
     extern __shared__ __align__(16) unsigned char bsf_smem[];
     constexpr int SPW = 32 / GP;
@@ -1443,7 +1444,7 @@ __global__ void __launch_bounds__(CW == 1 ? 512 : 256, 1) blockscan_fwd_gstrips(
     using Ln = BSLanes<GP>;
     const Ln ln(s);
     const int b = ln.b, n0 = ln.n0;
-    const bool hok = ln.h0ok;
+    const bool hok = FULL || ln.h0ok;   // FULL: N is a multiple of 2 GP, every lane has a pair
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int ss = ln.ps, pl = ln.pl;
     const int H = s.dims[0], W = s.dims[1];
@@ -1875,24 +1876,27 @@ static bool bs_bwd_strips_launch(const BSDesc& s, const BSGrad& g, cudaStream_t 
                       (size_t)nw * 32 * 3 * sizeof(float);
     const dim3 grid((unsigned)(s.batch * s.NG));
     auto go = [&](auto kern) { kern<<<grid, nw * 32, sm, st>>>(s, g, status); };
-#define KMB_BSB_O(TT, GPV, RV)                                                      \
+#define KMB_BSB_O(TT, GPV, RV, FL)                                                    \
     do {                                                                            \
-        if (g.overwrite) go(blockscan_bwd_strips<TT, GPV, RV, BSB_CW, true>);       \
-        else go(blockscan_bwd_strips<TT, GPV, RV, BSB_CW, false>);                  \
+        if (g.overwrite) go(blockscan_bwd_strips<TT, GPV, RV, BSB_CW, true, FL>);   \
+        else go(blockscan_bwd_strips<TT, GPV, RV, BSB_CW, false, FL>);              \
     } while (0)
-#define KMB_BSB_R(TT, GPV)                                  \
+#define KMB_BSB_R(TT, GPV, FL)                                \
     do {                                                    \
-        if (s.R == 1) KMB_BSB_O(TT, GPV, 1);                \
-        else if (s.R == 2) KMB_BSB_O(TT, GPV, 2);           \
-        else KMB_BSB_O(TT, GPV, 4);                         \
+        if (s.R == 1) KMB_BSB_O(TT, GPV, 1, FL);             \
+        else if (s.R == 2) KMB_BSB_O(TT, GPV, 2, FL);        \
+        else KMB_BSB_O(TT, GPV, 4, FL);                      \
     } while (0)
 #define KMB_BSB_GP(TT)                          \
     do {                                        \
         switch (s.GP) {                         \
-            case 1: KMB_BSB_R(TT, 1); break;    \
-            case 2: KMB_BSB_R(TT, 2); break;    \
-            case 4: KMB_BSB_R(TT, 4); break;    \
-            default: KMB_BSB_R(TT, 8); break;   \
+            case 1: KMB_BSB_R(TT, 1, false); break;                       \
+            case 2: KMB_BSB_R(TT, 2, false); break;                       \
+            case 4: KMB_BSB_R(TT, 4, false); break;                       \
+            default:                                                        \
+                if (s.N % 16 == 0) KMB_BSB_R(TT, 8, true);                \
+                else KMB_BSB_R(TT, 8, false);                             \
+                break;                                                      \
         }                                       \
     } while (0)
     if (s.bf16) KMB_BSB_GP(__nv_bfloat16);
@@ -1918,19 +1922,22 @@ static bool bs_fwd_gstrips_launch(const BSDesc& s, cudaStream_t st) {
     const size_t sm = (size_t)nw * BSB_K * 4 * s.GP * sizeof(float) + 2 * nw * BSB_K * sizeof(uint64_t);
     const dim3 grid((unsigned)(s.batch * s.NG));
     auto go = [&](auto kern) { kern<<<grid, nw * 32, sm, st>>>(s, status); };
-#define KMB_BSF_R(TT, GPV)                                                    \
+#define KMB_BSF_R(TT, GPV, FL)                                                  \
     do {                                                                      \
-        if (s.R == 1) go(blockscan_fwd_gstrips<TT, GPV, 1, BSF_CW>);          \
-        else if (s.R == 2) go(blockscan_fwd_gstrips<TT, GPV, 2, BSF_CW>);     \
-        else go(blockscan_fwd_gstrips<TT, GPV, 4, BSF_CW>);                   \
+        if (s.R == 1) go(blockscan_fwd_gstrips<TT, GPV, 1, BSF_CW, FL>);      \
+        else if (s.R == 2) go(blockscan_fwd_gstrips<TT, GPV, 2, BSF_CW, FL>); \
+        else go(blockscan_fwd_gstrips<TT, GPV, 4, BSF_CW, FL>);               \
     } while (0)
 #define KMB_BSF_GP(TT)                          \
     do {                                        \
         switch (s.GP) {                         \
-            case 1: KMB_BSF_R(TT, 1); break;    \
-            case 2: KMB_BSF_R(TT, 2); break;    \
-            case 4: KMB_BSF_R(TT, 4); break;    \
-            default: KMB_BSF_R(TT, 8); break;   \
+            case 1: KMB_BSF_R(TT, 1, false); break;                       \
+            case 2: KMB_BSF_R(TT, 2, false); break;                       \
+            case 4: KMB_BSF_R(TT, 4, false); break;                       \
+            default:                                                        \
+                if (s.N % 16 == 0) KMB_BSF_R(TT, 8, true);                \
+                else KMB_BSF_R(TT, 8, false);                             \
+                break;                                                      \
         }                                       \
     } while (0)
     if (s.bf16) KMB_BSF_GP(__nv_bfloat16);
