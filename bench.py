@@ -74,6 +74,8 @@ def parse():
                     choices=["scan_fwd", "scan_bwd", "convnd", "block", "model"],
                     help="scan_fwd = the headline line; the others measure the other BASELINE configs")
     ap.add_argument("--bf16", action="store_true", help="block workload: bf16 storage, fp32 state (config 3)")
+    ap.add_argument("--exp2", type=int, default=0,
+                    help="exponential of the 2D forward: 0 default, 1 opt-in fast ex2.approx")
     a = ap.parse_args()
     set_workload(a.dims, a.D, a.M, a.batch)
     return a
@@ -244,6 +246,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     lib = kmb.lib()
+    lib.kmb_set_scan_exp2(args.exp2)
 
     def barrier():
         if world > 1:

@@ -117,6 +117,7 @@ CONVND_FORWARD, CONVND_BACKWARD, CONVND_COMPLETE = 1, 2, 3
 EXPORTS = [
     "scannd_validate", "scannd", "scannd_ref_with_plan", "om_scannd_forward", "om_scannd_backward",
     "scannd_batched", "scannd_backward_batched", "scannd_forward_async", "scannd_backward_async",
+    "scannd_backward_ex", "kmb_last_backward_path",
     "convnd_kernel_volume", "convnd_forward_wavefront", "convnd_backward_wavefront", "convnd",
     "om_convnd_forward", "om_convnd_backward", "convnd_status", "convnd_batched_async",
     "convnd_backward_noalloc", "convnd_backward_noalloc_error",
@@ -126,6 +127,7 @@ EXPORTS = [
     "km_wavefront_plan_matches_dims", "km_wavefront_plan_level_size", "km_wavefront_plan_level_offsets",
     "km_wavefront_plan_iter_forward", "km_wavefront_plan_iter_reverse",
     "kmb_last_error", "kmb_clear_error", "kmb_device_status", "kmb_last_forward_path", "kmb_set_force_generic",
+    "kmb_set_scan_exp2", "kmb_get_scan_exp2",
     "kmb_blockscan_forward", "kmb_blockscan_set_strips", "kmb_blockscan_last_forward_path", "kmb_blockscan_set_backward_strips",
     "kmb_blockscan_last_backward_path", "kmb_blockscan_backward", "kmb_blockscan_backward_ex", "kmb_block_activation_floats",
     "kmb_block_forward", "kmb_block_backward", "kmb_block_set_tensor_cores", "kmb_block_last_projection_path", "kmb_block_last_dx_path", "cuda_block_forward", "cuda_block_backward",
@@ -155,6 +157,7 @@ def lib():
         L.scannd_backward_batched.argtypes = [P, C.c_long, C.c_void_p]
         L.scannd_forward_async.argtypes = [P, C.c_long, C.c_void_p]
         L.scannd_backward_async.argtypes = [P, C.c_long, C.c_void_p, C.c_void_p]
+        L.scannd_backward_ex.argtypes = [P, C.c_long, C.c_void_p, C.c_int, C.c_void_p]
         L.scannd_ref_with_plan.argtypes = [P, C.c_void_p]
         L.convnd.argtypes = [Q, C.c_int]
         L.convnd.restype = None
@@ -219,6 +222,8 @@ def lib():
         L.kmb_blockscan_set_backward_strips.restype = None
         L.kmb_set_force_generic.argtypes = [C.c_int]
         L.kmb_set_force_generic.restype = None
+        L.kmb_set_scan_exp2.argtypes = [C.c_int]
+        L.kmb_set_scan_exp2.restype = None
         L.km_wavefront_plan_create.argtypes = [_l, C.c_long, C.c_long]
         L.km_wavefront_plan_create.restype = C.c_void_p
         L.km_wavefront_plan_free.argtypes = [C.c_void_p]

@@ -34,6 +34,10 @@ size_t scan_bwd_generic_scratch_bytes(const ScanDesc& s);
 size_t scan_bwd_wave_scratch_bytes(const ScanDesc& s);
 cudaError_t launch_scan_bwd_wave(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC, float* ddelta,
                                  float* dlambda, float* dtheta, float* dx, void* scratch, cudaStream_t st);
+cudaError_t launch_scan_bwd_strips(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC, float* ddelta,
+                                   float* dlambda, float* dtheta, float* dx, int overwrite, void* scratch, int* status,
+                                   cudaStream_t st);
+size_t scan_bwd_strips_scratch_bytes(const ScanDesc& s);
 cudaError_t launch_scan_bwd_generic(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC,
                                     float* ddelta, float* dlambda, float* dtheta, float* dx, void* scratch,
                                     cudaStream_t st);
@@ -57,7 +61,9 @@ namespace {
 thread_local std::string tl_err;
 thread_local int tl_conv_status = 0;
 thread_local int tl_fast_path = -1;   // 1 = last forward used the TMA kernel, 0 = generic
+thread_local int tl_bwd_path = -1;    // 2 = strips, 1 = wave, 0 = generic
 int g_force_generic = -1;             // KMB_FORCE_GENERIC=1 disables the TMA path (tests)
+int g_scan_ex2 = 0;                   // 1: the 2D strip forward evaluates alpha with ex2.approx
 
 int fail(const char* msg) {
     tl_err = msg;
@@ -174,6 +180,7 @@ bool fill_desc(const ScanNDParams* p, long batch, ScanDesc* s) {
     s->has_lambda = p->lambda != nullptr;
     s->fast_exp = p->use_fast_exp != 0;
     s->clamp = p->use_a_log_clamp != 0;
+    s->ex2 = g_scan_ex2;
     s->a_log_min = p->a_log_min;
     s->default_lambda = p->default_lambda;
     s->P = points_of(p->dims, p->ndims);
@@ -254,7 +261,10 @@ int kmb_device_status(void* stream) {
     return v;
 }
 int kmb_last_forward_path(void) { return tl_fast_path; }
+int kmb_last_backward_path(void) { return tl_bwd_path; }
 void kmb_set_force_generic(int on) { g_force_generic = on ? 1 : 0; }
+void kmb_set_scan_exp2(int on) { g_scan_ex2 = on ? 1 : 0; }
+int kmb_get_scan_exp2(void) { return g_scan_ex2; }
 
 int scannd_validate(const ScanNDParams* p) {
     if (!p || !p->dims) return 0;
@@ -464,33 +474,68 @@ int om_scannd_forward(ScanNDParams* p) {
     return sync_and_check(0);
 }
 
-int scannd_backward_async(ScanNDParams* p, long batch, float* dx, void* stream) {
+int scannd_backward_ex(ScanNDParams* p, long batch, float* dx, int overwrite, void* stream) {
     if (!scannd_validate(p) || batch < 1) return fail("invalid ScanNDParams");
     const void* ptrs[] = {p->x, p->A, p->B, p->C, p->delta, p->h, p->y, p->theta, p->lambda,
                           p->dA, p->dB, p->dC, p->ddelta, p->dlambda, p->dtheta, dx};
     if (common_kind(ptrs, 16) != PK_DEVICE) return fail("scannd backward needs device pointers");
     ScanDesc s;
     if (!fill_desc(p, batch, &s)) return fail("unsupported ndims / sizes");
+    cudaStream_t st = (cudaStream_t)stream;
+    float* dth = p->theta ? p->dtheta : nullptr;
+    if (!force_generic()) {
+        int* status = status_word();
+        void* ws = ws_get(WS_SCRATCH, scan_bwd_strips_scratch_bytes(s));
+        if (!ws || !status) return fail("workspace allocation failed");
+        cudaError_t es = cudaMemsetAsync(status, 0, sizeof(int), st);
+        if (es != cudaSuccess) return fail_cuda("memset", es);
+        es = launch_scan_bwd_strips(s, p->y, p->dA, p->dB, p->dC, p->ddelta, p->dlambda, dth, dx,
+                                                overwrite ? 1 : 0, ws, status, st);
+        if (es == cudaSuccess) {
+            tl_bwd_path = 2;
+            return 0;
+        }
+        if (es != cudaErrorNotSupported) return fail_cuda("scan_bwd_strips", es);
+        cudaGetLastError();
+    }
+    if (overwrite) {
+        // the other kernels accumulate: clear the outputs first
+        const size_t P = (size_t)s.P, D = s.D, M = s.M, nd = s.nd, b = batch;
+        struct { void* p; size_t n; } outs[] = {{p->dA, nd * D * M}, {p->dB, b * P * D * M}, {p->dC, b * P * D * M},
+                                                {p->ddelta, b * nd * P * D}, {p->dlambda, b * P},
+                                                {dth, D / 2}, {dx, b * P * D}};
+        for (auto& o : outs)
+            if (o.p) {
+                cudaError_t e = cudaMemsetAsync(o.p, 0, o.n * sizeof(float), st);
+                if (e != cudaSuccess) return fail_cuda("memset", e);
+            }
+    }
     if (!force_generic()) {
         void* ws = ws_get(WS_SCRATCH, scan_bwd_wave_scratch_bytes(s));
         if (!ws) return fail("workspace allocation failed");
-        cudaError_t ew = launch_scan_bwd_wave(s, p->y, p->dA, p->dB, p->dC, p->ddelta, p->dlambda,
-                                              p->theta ? p->dtheta : nullptr, dx, ws, (cudaStream_t)stream);
-        if (ew == cudaSuccess) return 0;
+        cudaError_t ew = launch_scan_bwd_wave(s, p->y, p->dA, p->dB, p->dC, p->ddelta, p->dlambda, dth, dx, ws, st);
+        if (ew == cudaSuccess) {
+            tl_bwd_path = 1;
+            return 0;
+        }
         if (ew != cudaErrorNotSupported) return fail_cuda("scan_bwd_wave", ew);
         cudaGetLastError();
     }
     void* scratch = ws_get(WS_SCRATCH, scan_bwd_generic_scratch_bytes(s));
     if (!scratch) return fail("workspace allocation failed");
-    cudaError_t e = launch_scan_bwd_generic(s, p->y, p->dA, p->dB, p->dC, p->ddelta, p->dlambda,
-                                            p->theta ? p->dtheta : nullptr, dx, scratch, (cudaStream_t)stream);
+    cudaError_t e = launch_scan_bwd_generic(s, p->y, p->dA, p->dB, p->dC, p->ddelta, p->dlambda, dth, dx, scratch, st);
     if (e != cudaSuccess) return fail_cuda("scan_bwd", e);
+    tl_bwd_path = 0;
     return 0;
+}
+
+int scannd_backward_async(ScanNDParams* p, long batch, float* dx, void* stream) {
+    return scannd_backward_ex(p, batch, dx, 0, stream);
 }
 
 int scannd_backward_batched(ScanNDParams* p, long batch, float* dx) {
     if (scannd_backward_async(p, batch, dx, nullptr)) return -1;
-    tl_fast_path = 0;
+    tl_fast_path = tl_bwd_path == 2 ? 1 : 0;   // the strips kernel records bounded-wait timeouts
     return sync_and_check(0);
 }
 

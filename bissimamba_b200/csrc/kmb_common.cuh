@@ -21,6 +21,7 @@ struct ScanDesc {
     int has_lambda;      // lambda != NULL
     int fast_exp;
     int clamp;
+    int ex2;             // opt-in: alpha by one ex2.approx in the 2D strip kernel
     float a_log_min;
     float default_lambda;
     long long P;         // points per item

@@ -1,0 +1,603 @@
+// scannd_bwd_strips.cu -- exact Scan-A adjoint for 2D grids on sm_100a: a
+// reverse systolic column-strip pipeline (the backward of the headline
+// geometry, 2D 64x64, D=512, M=64, and of BASELINE config 1).
+//
+// The forward of src/scan_nd.c:103-201 at point p with predecessors p - e_k:
+//   h(p) = sum_k a_k R h(p-e_k) + (1-lam) dt (sum_k a_k / n) (sum_k Bu(p-e_k) / n) + lam dt Bu(p)
+// with a_k = exp(delta_k A_k), dt = sum_k delta_k, Bu = B x, n = #predecessors.
+// Its adjoint is a recurrence running the other way: the state gradient of p
+// depends only on p's successors s_k = p + e_k,
+//   g_h(p)  = C dy + R^T sum_k P_k(s_k),      P_k(s) = a_k(s) g_h(s)
+//   g_Bu(p) = lam dt g_h(p) + sum_k Q(s_k),   Q(s) = (1-lam(s)) dt(s) mean_a(s) g_h(s) / n(s)
+// so every point passes (P_k, Q) to its predecessor along axis k.
+//
+// Work split (mirrors the forward strips kernel): a CTA owns a tile (item b,
+// CH channels, 32 states; M = 64 runs as two tiles of 32 states), the inner
+// axis (<= 64 columns) is cut into strips of 8 columns with one warp per strip,
+// and each lane carries two channels (the RoPE pair, or two independent
+// channels) of one state.  Rows are walked bottom to top and, within a row,
+// columns right to left.  The (P_in, Q) of a strip's first column goes to the
+// warp on its left through mbarrier-guarded shared-memory slots; the
+// (P_out, Q) of every column stays in registers for the row above.  Strips run
+// one row apart, so no adjoint is ever written to or read back from memory
+// (the level-parallel kernel's G scratch is gone).
+//
+// Per lane, h and B of three rows are in registers: the current row (own
+// values), the row above (the up-predecessors' values, loaded one row ahead)
+// and the row above that (in flight).  The left predecessor is the next column
+// of the same registers (its strip neighbour's last column at the strip edge,
+// loaded once per row).  The per-(point, channel) inputs x, delta, dy and
+// lambda go through a three-row shared-memory ring filled by cp.async.
+//
+// Sums over the states (ddelta, dx; dlambda also over the channels) are
+// written per column to a padded shared-memory table and added in a fixed
+// order at the end of each row; with M = 64 the two state halves leave
+// partials that a second kernel adds in a fixed order.  dA and dtheta leave
+// per-(item, strip) partials.  Everything is deterministic; dB, dC, ddelta, dx
+// and dlambda are accumulated (+=, one addition per element) or, with
+// overwrite, assigned.
+//
+// Traffic: reads h, B, C (12 B per state update) and, when accumulating,
+// dB, dC (8 B), writes dB, dC (8 B): 28 B (20 B with overwrite) per update,
+// plus x, delta, dy, lambda and ddelta, dx per (point, channel).
+#include "kmb_common.cuh"
+#include "kmb_sync.cuh"
+
+namespace kmb {
+
+constexpr int BS_WC = 8;   // columns per strip
+constexpr int BS_K = 4;    // handoff slots per strip boundary
+constexpr int BS_RS = 36;  // padded row stride (floats) of the per-row reduction table
+
+struct BwdStripDesc {
+    int D, M, Q, O, S;      // channels, states, columns, rows, strips
+    int G;                  // state halves per channel tile (2 when M = 64)
+    int ntd;                // channel tiles per item
+    long long ntiles;       // batch * ntd * G
+    int has_lambda, clamp, fast, overwrite;
+    float amin, deflam;
+    long long P;
+    const float *x, *A, *B, *C, *delta, *theta, *lambda, *h, *dy;
+    float *dB, *dC, *ddelta, *dx;
+    float* part;            // G > 1: [b][p][d][G][3] partial sums (ddelta inner, ddelta outer, dx)
+    float *pA, *pth, *plam; // [b*S + w][2][D][M], [(b*G + g)*S + w][D/2], [b][ntd*G][P]
+    int* status;
+};
+
+template <int MS>
+struct BsGeom {
+    static constexpr int SETS = 32 / MS;        // channel sets per warp (2 when MS = 16)
+    static constexpr int CH = 2 * SETS;         // channels per tile
+    static constexpr int NOUT = BS_WC * CH * 3 + BS_WC;  // per-row outputs of a warp
+    // small per-row inputs in the cp.async ring: x [WC+1][CH], dI, dO, dy [WC][CH], lam [WC]
+    static constexpr int XO = 0, DIO = (BS_WC + 1) * CH, DOO = DIO + BS_WC * CH, DYO = DOO + BS_WC * CH,
+                         LO = DYO + BS_WC * CH, SMALL = (LO + BS_WC + 3) / 4 * 4;
+    static constexpr int NSL = (SMALL + 31) / 32;  // small loads per lane per row
+};
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const float* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <int MS, bool ROPE>
+__global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant__ BwdStripDesc f) {
+    using Gm = BsGeom<MS>;
+    constexpr int WC = BS_WC, CH = Gm::CH, SM_ = Gm::SMALL;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int S = f.S, D = f.D, M = f.M, Q = f.Q, O = f.O, G = f.G, ntd = f.ntd;
+    const long long P = f.P;
+    // smem: small ring [S][3][SMALL] | reduction table [S][64][BS_RS] | handoff [S][K][2][32][2] | barriers
+    float* small = (float*)smem;
+    float* redt = small + S * 3 * SM_;
+    float* hand = redt + S * 64 * BS_RS;
+    uint64_t* bars = (uint64_t*)(hand + S * BS_K * 2 * 64);
+    uint64_t* b_full = bars;                // [S][K]  boundary w: written by strip w, read by strip w-1
+    uint64_t* b_empty = bars + S * BS_K;    // [S][K]
+    if (tid == 0) {
+        for (int i = 0; i < S * BS_K; i++) {
+            mbar_init(smem_u32(&b_full[i]), 1);
+            mbar_init(smem_u32(&b_empty[i]), 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (w >= S) return;
+
+    const int set = lane / MS, ml = lane % MS;     // channel set, state within the half
+    const int cl0 = 2 * set;                       // first local channel of this lane
+    const int q0 = w * WC;
+    const int ncol = min(WC, Q - q0);
+    float* my_small = small + w * 3 * SM_;
+    float* my_red = redt + w * 64 * BS_RS;
+    const long long DM = (long long)D * M;
+    const int ngl = ntd * G;
+
+    // per-lane small-load plan (relative to the item base and the row): array, column, channel
+    int sl_off[Gm::NSL];
+    int sl_dst[Gm::NSL];
+    int sl_kind[Gm::NSL];  // 0 x, 1 delta inner, 2 delta outer, 3 dy, 4 lambda, -1 none
+#pragma unroll
+    for (int t = 0; t < Gm::NSL; t++) {
+        const int i = lane + 32 * t;
+        sl_kind[t] = -1;
+        sl_off[t] = 0;
+        sl_dst[t] = i;
+        if (i < Gm::DIO) {
+            const int j = i / CH - 1, c = i % CH;   // column -1 .. WC-1
+            if (q0 + j >= 0 && j < ncol) { sl_kind[t] = 0; sl_off[t] = (q0 + j) * D + c; }
+        } else if (i < Gm::LO) {
+            const int r = i - Gm::DIO, a = r / (WC * CH), j = (r % (WC * CH)) / CH, c = r % CH;
+            if (j < ncol) { sl_kind[t] = 1 + a; sl_off[t] = (q0 + j) * D + c; }
+        } else if (i < SM_) {
+            const int j = i - Gm::LO;
+            if (j < ncol && f.has_lambda) { sl_kind[t] = 4; sl_off[t] = q0 + j; }
+        }
+    }
+
+    int row = 0;  // global row counter of this warp (handoff slot / phase)
+    for (long long tile = blockIdx.x; tile < f.ntiles; tile += gridDim.x) {
+        const int half = (int)(tile % G);
+        const long long bt = tile / G;
+        const int b = (int)(bt / ntd);
+        const int d0 = (int)(bt - (long long)b * ntd) * CH;
+        const int mg = half * 32 + ml;           // state index
+        const int dl0 = d0 + cl0;                // first channel of this lane
+        const float* hb = f.h + (long long)b * P * DM + (long long)dl0 * M + mg;
+        const float* Bb = f.B + (long long)b * P * DM + (long long)dl0 * M + mg;
+        const float* Cb = f.C + (long long)b * P * DM + (long long)dl0 * M + mg;
+        const float* xb = f.x + (long long)b * P * D + d0;
+        const float* dlb = f.delta + (long long)b * 2 * P * D + d0;
+        const float* dyb = f.dy + (long long)b * P * D + d0;
+        const float* lb = f.has_lambda ? f.lambda + (long long)b * P : nullptr;
+        float* dBb = f.dB ? f.dB + (long long)b * P * DM + (long long)dl0 * M + mg : nullptr;
+        float* dCb = f.dC ? f.dC + (long long)b * P * DM + (long long)dl0 * M + mg : nullptr;
+        const long long rowDM = (long long)Q * DM;   // one row of h / B / C
+        float AI[2], AO[2];
+        bool clI[2], clO[2];
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const int d = dl0 + c;
+            const float ai = f.A[((long long)1 * D + d) * M + mg], ao = f.A[((long long)0 * D + d) * M + mg];
+            clI[c] = f.clamp && ai > f.amin;
+            clO[c] = f.clamp && ao > f.amin;
+            AI[c] = clI[c] ? f.amin : ai;
+            AO[c] = clO[c] ? f.amin : ao;
+        }
+        float cth = 1.0f, sth = 0.0f;
+        if (ROPE) {
+            const float th = f.theta[dl0 >> 1];
+            cth = cosf(th);
+            sth = sinf(th);
+        }
+        // state ring: own row (o), predecessor row (o-1), row in flight (o-2)
+        float hO[WC][2], bO[WC][2], hP[WC][2], bP[WC][2], hN[WC][2], bN[WC][2], cO[WC][2], cN[WC][2];
+        auto load_hb = [&](int o, float (&hh)[WC][2], float (&bb)[WC][2]) {
+#pragma unroll
+            for (int j = 0; j < WC; j++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    if (j < ncol && o >= 0) {
+                        const long long off = (long long)o * rowDM + (long long)(q0 + j) * DM + c * M;
+                        hh[j][c] = __ldg(hb + off);
+                        bb[j][c] = __ldg(Bb + off);
+                    } else {
+                        hh[j][c] = 0.0f;
+                        bb[j][c] = 0.0f;
+                    }
+                }
+        };
+        auto load_c = [&](int o, float (&cc)[WC][2]) {
+#pragma unroll
+            for (int j = 0; j < WC; j++)
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+                    cc[j][c] = (j < ncol && o >= 0)
+                                   ? __ldg(Cb + (long long)o * rowDM + (long long)(q0 + j) * DM + c * M)
+                                   : 0.0f;
+        };
+        auto load_small = [&](int o) {
+            if (o < 0) return;
+            float* dst = my_small + (o % 3) * SM_;
+#pragma unroll
+            for (int t = 0; t < Gm::NSL; t++) {
+                const int k = sl_kind[t];
+                if (k < 0) continue;
+                const float* src = k == 0 ? xb : k == 1 ? dlb + P * D : k == 2 ? dlb : k == 3 ? dyb : lb;
+                const long long rs = k == 4 ? (long long)Q : (long long)Q * D;
+                cp_async4(smem_u32(dst + sl_dst[t]), src + (long long)o * rs + sl_off[t]);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        // prologue: rows O-1 (own) and O-2 (predecessors)
+        load_hb(O - 1, hO, bO);
+        load_hb(O - 2, hP, bP);
+        load_c(O - 1, cO);
+        load_small(O - 1);
+        load_small(O - 2);
+        float dP[WC][2], dQ[WC][2];
+#pragma unroll
+        for (int j = 0; j < WC; j++) dP[j][0] = dP[j][1] = dQ[j][0] = dQ[j][1] = 0.0f;
+        float gAI[2] = {0.f, 0.f}, gAO[2] = {0.f, 0.f}, gth = 0.0f;
+
+#pragma unroll 1
+        for (int o = O - 1; o >= 0; o--, row++) {
+            cp_async_wait_all();
+            __syncwarp();
+            // issue the row after next: h, B of o-2; C of o-1; small inputs of o-2
+            load_hb(o - 2, hN, bN);
+            load_c(o - 1, cN);
+            load_small(o - 2);
+            float hL[2] = {0.f, 0.f}, bL[2] = {0.f, 0.f};
+            if (q0 > 0) {
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const long long off = (long long)o * rowDM + (long long)(q0 - 1) * DM + c * M;
+                    hL[c] = __ldg(hb + off);
+                    bL[c] = __ldg(Bb + off);
+                }
+            }
+            const float* sO = my_small + (o % 3) * SM_;
+            const float* sP = my_small + ((o + 2) % 3) * SM_;   // row o-1
+            const int hs = row & (BS_K - 1);
+            const uint32_t hph = (uint32_t)((row / BS_K) & 1);
+            // right successor of the last column: strip w+1's first column
+            float rP[2] = {0.f, 0.f}, rQ[2] = {0.f, 0.f};
+            if (w + 1 < S) {
+                if (!mbar_wait(smem_u32(&b_full[(w + 1) * BS_K + hs]), hph)) {
+                    set_status(f.status, KMB_ERR_TIMEOUT_Y);
+                    cp_async_wait_all();
+                    return;
+                }
+                const float* src = hand + ((size_t)((w + 1) * BS_K + hs) * 2) * 64;
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    rP[c] = src[lane * 2 + c];
+                    rQ[c] = src[64 + lane * 2 + c];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&b_empty[(w + 1) * BS_K + hs]));
+            }
+            const float lamr = f.deflam;
+            const bool hasU = o > 0;
+#pragma unroll
+            for (int j = WC - 1; j >= 0; j--) {
+                if (j >= ncol) continue;
+                const bool hasL = (q0 + j) > 0;
+                const float lam = f.has_lambda ? sO[Gm::LO + j] : lamr;
+                const int npred = (int)hasL + (int)hasU;
+                const float inv = npred == 2 ? 0.5f : 1.0f;
+                float ah[2], ab[2], gh[2];
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    ah[c] = rP[c] + dP[j][c];
+                    ab[c] = rQ[c] + dQ[j][c];
+                }
+                const float h0 = hO[j][0], h1 = hO[j][1];
+                // predecessors' raw states (left: the next column, or the strip edge)
+                const float lh0 = j > 0 ? hO[j > 0 ? j - 1 : 0][0] : hL[0];
+                const float lh1 = j > 0 ? hO[j > 0 ? j - 1 : 0][1] : hL[1];
+                if (ROPE) {
+                    gh[0] = __fmaf_rn(cth, ah[0], __fmul_rn(sth, ah[1]));
+                    gh[1] = __fmaf_rn(cth, ah[1], -__fmul_rn(sth, ah[0]));
+                    const float hat0 = __fmaf_rn(cth, h0, -__fmul_rn(sth, h1));
+                    const float hat1 = __fmaf_rn(sth, h0, __fmul_rn(cth, h1));
+                    gth = __fmaf_rn(ah[1], hat0, __fmaf_rn(-ah[0], hat1, gth));
+                } else {
+                    gh[0] = ah[0];
+                    gh[1] = ah[1];
+                }
+                float* rr = my_red + (j * 2) * 4 * BS_RS + lane;
+                float glam_l = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const int cc = cl0 + c;
+                    const float xv = sO[Gm::XO + (j + 1) * CH + cc];
+                    const float dI = sO[Gm::DIO + j * CH + cc];
+                    const float dO = sO[Gm::DOO + j * CH + cc];
+                    const float dyv = sO[Gm::DYO + j * CH + cc];
+                    const float hv = c ? h1 : h0;
+                    const float Bv = bO[j][c];
+                    float g = __fmaf_rn(cO[j][c], dyv, gh[c]);
+                    const long long eo = (long long)o * rowDM + (long long)(q0 + j) * DM + c * M;
+                    if (dCb) {
+                        const float v = __fmul_rn(dyv, hv);
+                        if (f.overwrite) __stcs(dCb + eo, v);
+                        else atomicAdd(dCb + eo, v);
+                    }
+                    const float dt = __fadd_rn(dO, dI);
+                    const float bu = __fmul_rn(Bv, xv);
+                    const float gam = __fmul_rn(lam, dt);
+                    float PI = 0.0f, PO = 0.0f, Qv = 0.0f, eI = 0.0f, eO = 0.0f;
+                    float gdt = __fmul_rn(__fmul_rn(lam, bu), g);
+                    float gl = __fmul_rn(__fmul_rn(dt, bu), g);
+                    if (npred > 0) {
+                        float aI = 0.0f, aO = 0.0f, zI = 0.0f, zO = 0.0f, sbu = 0.0f;
+                        float hatL = 0.0f, hatU = 0.0f;
+                        if (hasL) {
+                            zI = __fmul_rn(dI, AI[c]);
+                            aI = kmb_exp(zI, f.fast);
+                            const float xl = sO[Gm::XO + j * CH + cc];
+                            const float bl = j > 0 ? bO[j > 0 ? j - 1 : 0][c] : bL[c];
+                            sbu = __fmul_rn(bl, xl);
+                            hatL = ROPE ? (c ? __fmaf_rn(sth, lh0, __fmul_rn(cth, lh1))
+                                             : __fmaf_rn(cth, lh0, -__fmul_rn(sth, lh1)))
+                                        : (c ? lh1 : lh0);
+                        }
+                        if (hasU) {
+                            zO = __fmul_rn(dO, AO[c]);
+                            aO = kmb_exp(zO, f.fast);
+                            const float xu = sP[Gm::XO + (j + 1) * CH + cc];
+                            sbu = __fmaf_rn(bP[j][c], xu, sbu);
+                            const float u0 = hP[j][0], u1 = hP[j][1];
+                            hatU = ROPE ? (c ? __fmaf_rn(sth, u0, __fmul_rn(cth, u1))
+                                             : __fmaf_rn(cth, u0, -__fmul_rn(sth, u1)))
+                                        : (c ? u1 : u0);
+                        }
+                        const float ma = __fmul_rn(__fadd_rn(aI, aO), inv);   // mean alpha
+                        const float mb = __fmul_rn(sbu, inv);                  // mean predecessor Bu
+                        const float oml = __fsub_rn(1.0f, lam);
+                        const float omdt = __fmul_rn(oml, dt);
+                        PI = __fmul_rn(aI, g);
+                        PO = __fmul_rn(aO, g);
+                        Qv = __fmul_rn(__fmul_rn(__fmul_rn(omdt, ma), inv), g);
+                        const float mab = __fmul_rn(ma, mb);
+                        gdt = __fmaf_rn(__fmul_rn(oml, mab), g, gdt);
+                        gl = __fmaf_rn(-__fmul_rn(dt, mab), g, gl);
+                        const float ka = __fmul_rn(__fmul_rn(omdt, inv), mb);   // d h / d a_k beyond the state term
+                        if (hasL) {
+                            const float dz = __fmul_rn(__fmul_rn(kmb_dexp(zI, aI, f.fast), g), __fadd_rn(hatL, ka));
+                            eI = __fmul_rn(dz, AI[c]);
+                            if (!clI[c]) gAI[c] = __fmaf_rn(dz, dI, gAI[c]);
+                        }
+                        if (hasU) {
+                            const float dz = __fmul_rn(__fmul_rn(kmb_dexp(zO, aO, f.fast), g), __fadd_rn(hatU, ka));
+                            eO = __fmul_rn(dz, AO[c]);
+                            if (!clO[c]) gAO[c] = __fmaf_rn(dz, dO, gAO[c]);
+                        }
+                    }
+                    const float gbu = __fmaf_rn(gam, g, ab[c]);
+                    if (dBb) {
+                        const float v = __fmul_rn(gbu, xv);
+                        if (f.overwrite) __stcs(dBb + eo, v);
+                        else atomicAdd(dBb + eo, v);
+                    }
+                    rr[(c * 4 + 0) * BS_RS] = __fadd_rn(eI, gdt);
+                    rr[(c * 4 + 1) * BS_RS] = __fadd_rn(eO, gdt);
+                    rr[(c * 4 + 2) * BS_RS] = __fmul_rn(gbu, Bv);
+                    glam_l = __fadd_rn(glam_l, gl);
+                    // pass to the predecessors: (P_in, Q) left, (P_out, Q) up
+                    dP[j][c] = PO;
+                    dQ[j][c] = Qv;
+                    rP[c] = PI;
+                    rQ[c] = Qv;
+                }
+                rr[3 * BS_RS] = glam_l;
+            }
+            // left edge: hand (P_in, Q) of column q0 to strip w-1
+            if (w > 0) {
+                if (row >= BS_K && !mbar_wait(smem_u32(&b_empty[w * BS_K + hs]), hph ^ 1)) {
+                    set_status(f.status, KMB_ERR_TIMEOUT_Y);
+                    cp_async_wait_all();
+                    return;
+                }
+                float* dst = hand + ((size_t)(w * BS_K + hs) * 2) * 64;
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    dst[lane * 2 + c] = rP[c];
+                    dst[64 + lane * 2 + c] = rQ[c];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&b_full[w * BS_K + hs]));
+            }
+            // sums over the states (fixed order) and their outputs
+            __syncwarp();
+            for (int t = lane; t < Gm::NOUT; t += 32) {
+                float acc = 0.0f;
+                int j, cc = 0, k = 3;
+                if (t < WC * CH * 3) {
+                    j = t / (CH * 3);
+                    cc = (t / 3) % CH;
+                    k = t % 3;
+                    const int s2 = cc / 2, c = cc % 2;
+                    const float* src = my_red + ((j * 2 + c) * 4 + k) * BS_RS + s2 * MS;
+#pragma unroll 4
+                    for (int l = 0; l < MS; l += 4) {
+                        const float4 v = *(const float4*)(src + l);
+                        acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+                    }
+                } else {
+                    j = t - WC * CH * 3;
+                    const float* src = my_red + (j * 2 * 4 + 3) * BS_RS;   // per-lane sums of both units
+#pragma unroll 4
+                    for (int l = 0; l < 32; l += 4) {
+                        const float4 v = *(const float4*)(src + l);
+                        acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+                    }
+                }
+                if (j >= ncol) continue;
+                const long long p = (long long)o * Q + q0 + j;
+                if (k == 3) {
+                    if (f.plam) f.plam[((long long)b * ngl + (bt - (long long)b * ntd) * G + half) * P + p] = acc;
+                    continue;
+                }
+                const long long pd = ((long long)b * P + p) * D + d0 + cc;
+                if (G > 1) {
+                    f.part[(pd * G + half) * 3 + k] = acc;
+                } else if (k < 2) {
+                    if (f.ddelta) {
+                        // inner axis is axis 1, outer axis 0
+                        float* dd = f.ddelta + (((long long)b * 2 + (k == 0 ? 1 : 0)) * P + p) * D + d0 + cc;
+                        if (f.overwrite) *dd = acc;
+                        else *dd = __fadd_rn(*dd, acc);
+                    }
+                } else if (f.dx) {
+                    float* dd = f.dx + pd;
+                    if (f.overwrite) *dd = acc;
+                    else *dd = __fadd_rn(*dd, acc);
+                }
+            }
+            __syncwarp();
+            // rotate the state ring
+#pragma unroll
+            for (int j = 0; j < WC; j++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    hO[j][c] = hP[j][c];
+                    bO[j][c] = bP[j][c];
+                    hP[j][c] = hN[j][c];
+                    bP[j][c] = bN[j][c];
+                    cO[j][c] = cN[j][c];
+                }
+        }
+        // per-(item, strip) partials of dA (this lane's (d, state)) and dtheta
+        {
+            const long long r = (long long)b * S + w;
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                const int d = dl0 + c;
+                f.pA[((r * 2 + 1) * D + d) * M + mg] = gAI[c];
+                f.pA[((r * 2 + 0) * D + d) * M + mg] = gAO[c];
+            }
+            if (ROPE) {
+                float v = gth;
+#pragma unroll
+                for (int off = MS / 2; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                if (ml == 0) f.pth[(((long long)b * G + half) * S + w) * (D / 2) + (dl0 >> 1)] = v;
+            }
+        }
+    }
+    cp_async_wait_all();
+}
+
+// ddelta / dx from the two state halves' partials (M = 64), fixed order.
+__global__ void bwd_strips_combine(const float* __restrict__ part, float* __restrict__ ddelta, float* __restrict__ dx,
+                                   long long batch, long long P, int D, int G, int overwrite) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * P * D) return;
+    const long long b = i / (P * D), pd = i - b * P * D;
+    float s[3] = {0.f, 0.f, 0.f};
+    for (int g = 0; g < G; g++)
+        for (int k = 0; k < 3; k++) s[k] = __fadd_rn(s[k], part[(i * G + g) * 3 + k]);
+    if (ddelta) {
+        float* d1 = ddelta + (b * 2 + 1) * P * D + pd;
+        float* d0 = ddelta + (b * 2 + 0) * P * D + pd;
+        *d1 = overwrite ? s[0] : __fadd_rn(*d1, s[0]);
+        *d0 = overwrite ? s[1] : __fadd_rn(*d0, s[1]);
+    }
+    if (dx) dx[i] = overwrite ? s[2] : __fadd_rn(dx[i], s[2]);
+}
+
+// out[i] (+)= sum_j part[j * stride + i], fixed order
+__global__ void bwd_strips_reduce(const float* __restrict__ part, float* __restrict__ out, long long count, long long n,
+                                  long long stride, int overwrite) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    float acc = 0.0f;
+    for (long long j = 0; j < n; j++) acc = __fadd_rn(acc, part[j * stride + i]);
+    out[i] = overwrite ? acc : __fadd_rn(out[i], acc);
+}
+
+// dlambda[b, p] (+)= sum_g plam[b, g, p], fixed order
+__global__ void bwd_strips_lambda(const float* __restrict__ plam, float* __restrict__ dl, long long batch, int ngroups,
+                                  long long P, int overwrite) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * P) return;
+    const long long b = i / P, p = i - b * P;
+    float acc = 0.0f;
+    for (int g = 0; g < ngroups; g++) acc = __fadd_rn(acc, plam[(b * ngroups + g) * P + p]);
+    dl[i] = overwrite ? acc : __fadd_rn(dl[i], acc);
+}
+
+// ------------------------------------------------------------------ host side
+static int bs_smem(int S, int small) {
+    return (S * 3 * small + S * 64 * BS_RS + S * BS_K * 2 * 64) * 4 + 2 * S * BS_K * 8;
+}
+
+size_t scan_bwd_strips_scratch_bytes(const ScanDesc& s) {
+    const long long G = s.M == 64 ? 2 : 1;
+    const long long S = 8;
+    const long long CH = s.M == 16 ? 4 : 2;
+    const long long ntd = s.D / CH;
+    size_t n = 0;
+    if (G > 1) n += (size_t)s.batch * s.P * s.D * G * 3;
+    n += (size_t)s.batch * S * 2 * s.D * s.M;            // pA
+    n += (size_t)s.batch * G * S * (s.D / 2 + 1);         // pth
+    n += (size_t)s.batch * ntd * G * s.P;                 // plam
+    return n * sizeof(float) + 4 * 256;
+}
+
+template <int MS, bool ROPE>
+static cudaError_t bs_launch(const BwdStripDesc& f, int smem, int threads, cudaStream_t st) {
+    auto k = scan_bwd_strips<MS, ROPE>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int dev, sms, per = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, threads, smem);
+    if (per < 1) return cudaErrorNotSupported;
+    long long grid = (long long)sms * per;
+    if (grid > f.ntiles) grid = f.ntiles;
+    k<<<(unsigned)grid, threads, smem, st>>>(f);
+    return cudaGetLastError();
+}
+
+// 2D grids whose inner (last) extent is <= 64, M in {16, 32, 64}, D a multiple
+// of the channel tile.  cudaErrorNotSupported outside that envelope.
+cudaError_t launch_scan_bwd_strips(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC, float* ddelta,
+                                   float* dlambda, float* dtheta, float* dx, int overwrite, void* scratch, int* status,
+                                   cudaStream_t st) {
+    if (s.nd != 2 || s.dims[1] > 64 || s.dims[1] < 1) return cudaErrorNotSupported;
+    if (s.M != 16 && s.M != 32 && s.M != 64) return cudaErrorNotSupported;
+    const int MS = s.M == 16 ? 16 : 32;
+    const int CH = MS == 16 ? 4 : 2;
+    if (s.D % CH != 0) return cudaErrorNotSupported;
+    if (s.batch * s.P * s.D * s.M >= (1LL << 62) || s.P > 0x7fffffffLL) return cudaErrorNotSupported;
+    BwdStripDesc f{};
+    f.D = s.D; f.M = s.M;
+    f.Q = (int)s.dims[1]; f.O = (int)s.dims[0];
+    f.S = (f.Q + BS_WC - 1) / BS_WC;
+    f.G = s.M == 64 ? 2 : 1;
+    f.ntd = s.D / CH;
+    f.ntiles = s.batch * f.ntd * f.G;
+    f.has_lambda = s.has_lambda; f.clamp = s.clamp; f.fast = s.fast_exp; f.overwrite = overwrite;
+    f.amin = s.a_log_min; f.deflam = s.default_lambda;
+    f.P = s.P;
+    f.x = s.x; f.A = s.A; f.B = s.B; f.C = s.C; f.delta = s.delta; f.theta = s.theta; f.lambda = s.lambda;
+    f.h = s.h; f.dy = dy;
+    f.dB = dB; f.dC = dC; f.ddelta = ddelta; f.dx = dx;
+    f.status = status;
+    auto align = [](char* p) { return (char*)(((uintptr_t)p + 255) & ~(uintptr_t)255); };
+    char* c = align((char*)scratch);
+    const long long S = 8;   // partial rows are laid out for 8 strips
+    if (f.G > 1) { f.part = (float*)c; c = align(c + (size_t)s.batch * s.P * s.D * f.G * 3 * 4); }
+    f.pA = (float*)c; c = align(c + (size_t)s.batch * S * 2 * s.D * s.M * 4);
+    f.pth = (float*)c; c = align(c + (size_t)s.batch * f.G * S * (s.D / 2 + 1) * 4);
+    f.plam = dlambda ? (float*)c : nullptr;
+    const int small = MS == 16 ? BsGeom<16>::SMALL : BsGeom<32>::SMALL;
+    const int smem = bs_smem(f.S, small);
+    const int threads = f.S * 32;
+    cudaError_t e;
+    if (MS == 16) e = s.rope ? bs_launch<16, true>(f, smem, threads, st) : bs_launch<16, false>(f, smem, threads, st);
+    else e = s.rope ? bs_launch<32, true>(f, smem, threads, st) : bs_launch<32, false>(f, smem, threads, st);
+    if (e != cudaSuccess) return e;
+    auto nb = [](long long n) { return (unsigned)((n + 255) / 256); };
+    if (f.G > 1 && (ddelta || dx))
+        bwd_strips_combine<<<nb(s.batch * s.P * s.D), 256, 0, st>>>(f.part, ddelta, dx, s.batch, s.P, s.D, f.G,
+                                                                    overwrite);
+    if (dA) {
+        const long long cnt = 2LL * s.D * s.M;
+        bwd_strips_reduce<<<nb(cnt), 256, 0, st>>>(f.pA, dA, cnt, s.batch * f.S, cnt, overwrite);
+    }
+    if (dtheta && s.rope && s.D >= 2) {
+        const long long cnt = s.D / 2;
+        bwd_strips_reduce<<<nb(cnt), 256, 0, st>>>(f.pth, dtheta, cnt, s.batch * f.G * f.S, s.D / 2, overwrite);
+    }
+    if (dlambda)
+        bwd_strips_lambda<<<nb(s.batch * s.P), 256, 0, st>>>(f.plam, dlambda, s.batch, f.ntd * f.G, s.P, overwrite);
+    return cudaGetLastError();
+}
+
+}  // namespace kmb

@@ -50,6 +50,7 @@ struct StripDesc {
     int st_bytes, offC, offX, offD, offL;
     unsigned tx_bytes;
     int red_y;              // 1: y is accumulated with red.add (two lane halves)
+    int ex2;                // 1: alpha by one ex2.approx (opt-in), 0: expf in the reference's order
     const float* A;
     const float* theta;
     float* h;
@@ -85,7 +86,7 @@ struct StripLayout {
     static constexpr int bytes = offL + 128;
 };
 
-template <int MT, bool ROPE, bool LAMB, bool KIN0, bool FULL>
+template <int MT, bool ROPE, bool LAMB, bool KIN0, bool FULL, int EXPM>  // EXPM 0: expf, reference order; 1: ex2.approx
 __global__ void __launch_bounds__(StripGeom<MT, ROPE>::MAXT, 1)
 scan_fwd_strips(const __grid_constant__ StripDesc f,
                 const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mC,
@@ -93,6 +94,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                 const __grid_constant__ CUtensorMap mL) {
     using Gm = StripGeom<MT, ROPE>;
     using Ly = StripLayout<MT, ROPE>;
+    constexpr bool EX2 = EXPM == 1;
     constexpr int CPT = Gm::CPT, HW = Gm::HW, CH = Gm::CH, GS = Gm::GS, U = Gm::U;
     constexpr int WC = SW_WC;
     constexpr int ST = Ly::bytes;
@@ -223,9 +225,11 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int d = d0 + cl0 + u % CPT, mu = m + 32 * (u / CPT);
-            // A log2 e: alpha = 2^(delta * A log2 e) is one multiply and one ex2 per update
-            AI[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + mu], f.clamp, f.amin), kKmbLog2e);
-            AO[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + mu], f.clamp, f.amin), kKmbLog2e);
+            // EX2: A log2 e, so alpha = 2^(delta * A log2 e) is one multiply and one ex2
+            // per update; otherwise A itself and alpha = expf(delta * A) as the reference
+            const float sc = EX2 ? kKmbLog2e : 1.0f;
+            AI[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + mu], f.clamp, f.amin), sc);
+            AO[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + mu], f.clamp, f.amin), sc);
         }
         if (ROPE) {
             const float th = f.theta[(d0 + cl0) >> 1];
@@ -293,14 +297,22 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     const float Bv = Bs[j * CH * MT + c * MT + sofs];
                     const float dt = __fadd_rn(dI, dO);
                     const float bu = __fmul_rn(Bv, x);
-                    const float aI = kmb_ex2(__fmul_rn(dI, AI[u]));
+                    const float aI = EX2 ? kmb_ex2(__fmul_rn(dI, AI[u])) : expf(__fmul_rn(dI, AI[u]));
                     float buacc, dacc, hacc, inv;
                     // inner predecessor: the previous column (strip w-1's last column when j == 0)
                     const float hatI = (j == 0) ? lh[u] : ring_h[j == 0 ? 0 : j - 1][u];
                     const float buI = (j == 0) ? lb[u] : ring_b[j == 0 ? 0 : j - 1][u];
                     if (HASO) {
-                        const float aO = kmb_ex2(__fmul_rn(dO, AO[u]));
-                        if (j > 0 || w > 0) {
+                        const float aO = EX2 ? kmb_ex2(__fmul_rn(dO, AO[u])) : expf(__fmul_rn(dO, AO[u]));
+                        if (!EX2 && (j > 0 || w > 0)) {
+                            // reference order (src/scan_nd.c:141-168): sums over the axes in
+                            // axis order, means as sum * 1/2 (exact), beta = ((1-lam) dt) mean(alpha)
+                            buacc = __fadd_rn(KIN0 ? buI : ring_b[j][u], KIN0 ? ring_b[j][u] : buI);
+                            dacc = __fadd_rn(KIN0 ? aI : aO, KIN0 ? aO : aI);
+                            hacc = KIN0 ? __fmaf_rn(aO, ring_h[j][u], __fmul_rn(aI, hatI))
+                                        : __fmaf_rn(aI, hatI, __fmul_rn(aO, ring_h[j][u]));
+                            inv = 0.5f;
+                        } else if (j > 0 || w > 0) {
                             // two predecessors: mean of two = sum * 0.5 (exact), so the
                             // coefficient (1-lam) dt (dacc/2) (buacc/2) is ((1-lam) dt / 4) (dacc buacc);
                             // h = (A-part + that) + gamma bu, as two fused multiply-adds
@@ -335,7 +347,8 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     {
                         const float beta = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt), __fmul_rn(dacc, inv));
                         const float gamma = __fmul_rn(lam, dt);
-                        hn[u] = __fadd_rn(__fmaf_rn(bu, gamma, __fmul_rn(__fmul_rn(buacc, inv), beta)), hacc);
+                        hn[u] = EX2 ? __fadd_rn(__fmaf_rn(bu, gamma, __fmul_rn(__fmul_rn(buacc, inv), beta)), hacc)
+                                    : __fadd_rn(__fmaf_rn(__fmul_rn(buacc, inv), beta, __fmul_rn(bu, gamma)), hacc);
                     }
                 have_h:
                     ring_b[j][u] = bu;
@@ -418,7 +431,10 @@ bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long
 
 template <int MT, bool ROPE, bool LAMB, bool KIN0>
 static cudaError_t strips_inst(const StripDesc& f, const CUtensorMap* maps, int smem, int threads, cudaStream_t st) {
-    auto k = (f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true> : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false>;
+    auto k = f.ex2 == 1 ? ((f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true, 1>
+                                              : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false, 1>)
+                        : ((f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true, 0>
+                                              : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false, 0>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int dev, sms, per = 0;
@@ -477,6 +493,7 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
     f.tx_bytes = (unsigned)(2 * bbox + 16 * f.Wc + 2 * 16 * f.Wc +
                             (s.has_lambda ? (f.lam_inner_fast ? 4 * f.Wc : 16 * f.Wc) : 0));
     f.red_y = HW > 1;
+    f.ex2 = s.ex2;
     f.A = s.A; f.theta = s.theta; f.h = s.h; f.y = s.y; f.status = status;
     const unsigned long long P = s.P, Bn = s.batch, DM = (unsigned long long)D * MT;
     const unsigned long long qs = f.qstride, os = f.ostride;

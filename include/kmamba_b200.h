@@ -17,8 +17,18 @@ int kmb_device_status(void *stream);
 /* Which Scan-A forward kernel the last forward call on this thread used:
  * 1 = persistent TMA kernel (1D/2D fast path), 0 = generic kernel, -1 = none. */
 int kmb_last_forward_path(void);
+/* Which Scan-A backward kernel the last backward call on this thread used:
+ * 2 = 2D systolic strips, 1 = level-parallel wave kernel, 0 = generic. */
+int kmb_last_backward_path(void);
 /* 1 = route every forward through the generic kernel (tests / comparison). */
 void kmb_set_force_generic(int on);
+/* Exponential of the 2D Scan-A forward (process-wide).  0 (default): expf of
+ * delta*A with the reference's operation order (src/scan_nd.c:126-168), within
+ * 1e-4 rel / 1e-5 abs of the reference's fp32 result.  1 (opt-in, faster):
+ * one ex2.approx of delta*(A log2 e) and a re-associated trapezoid term; it is
+ * a few ulp per update from expf, which the recurrence compounds. */
+void kmb_set_scan_exp2(int on);
+int kmb_get_scan_exp2(void);
 #ifdef __cplusplus
 }
 #endif

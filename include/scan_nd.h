@@ -97,6 +97,13 @@ int scannd_backward_batched(ScanNDParams *p, long batch, float *dx);
 int scannd_forward_async(ScanNDParams *p, long batch, void *stream);
 int scannd_backward_async(ScanNDParams *p, long batch, float *dx, void *stream);
 
+/* Backward with a choice of output semantics (no counterpart in the reference,
+ * whose GPU backward accumulates with atomicAdd, cuda/scan_nd.cu:367-537):
+ * overwrite = 0 accumulates into dA, dB, dC, ddelta, dlambda, dtheta and dx
+ * (+=, as scannd_backward_async); overwrite = 1 assigns them, so the caller
+ * need not clear them and the 2D kernel does not read them back. */
+int scannd_backward_ex(ScanNDParams *p, long batch, float *dx, int overwrite, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

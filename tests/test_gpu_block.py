@@ -45,7 +45,7 @@ def test_block_forward(kmb, cuda, dims, dim, N, R):
         lim = 1e-5 * np.linalg.norm(ex)
         if ref is not None:
             lim = max(lim, 4 * np.linalg.norm(ref - ex))
-            np.testing.assert_allclose(out[b], ref, rtol=1e-3, atol=1e-4 * np.abs(ref).max())
+            np.testing.assert_allclose(out[b], ref, rtol=1e-4, atol=1e-5)
         assert e_g <= lim + 1e-30, (e_g, lim)
 
 

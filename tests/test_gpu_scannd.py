@@ -15,24 +15,30 @@ from oracle import pyoracle as po
 pytestmark = pytest.mark.gpu
 
 
-def _run_both(kmb, cuda, inp, expect_path=None):
-    from gpu_util import scan_fwd, assert_scan_close
+def _run_both(kmb, cuda, inp, expect_path=None, zero_exempt=False):
+    from gpu_util import scan_fwd, assert_scan_close, assert_scan_strict
+    from oracle import pyoracle as po
     h, y, path = scan_fwd(inp, cuda)
     if expect_path is not None:
         assert path == expect_path, f"forward path {path}, expected {expect_path}"
-    return assert_scan_close(h, y, inp)
+    href, yref = po.oracle_scannd(inp)
+    r = assert_scan_strict(h, y, inp, href, yref, zero_exempt=zero_exempt)
+    print("strict parity:", r)
+    assert_scan_close(h, y, inp, href, yref)
+    return r
 
 
 @pytest.mark.parametrize("name", list(mg.SCAN_CASES))
 @pytest.mark.parametrize("generic", [False, True])
 def test_forward_matches_reference_fixture(kmb, cuda, name, generic):
-    from gpu_util import scan_fwd, assert_scan_close
+    from gpu_util import scan_fwd, assert_scan_close, assert_scan_strict
     kmb.lib().kmb_set_force_generic(1 if generic else 0)
     try:
         inp, href, yref = mg.load_scan(name)
         h, y, path = scan_fwd(inp, cuda)
         if generic:
             assert path == 0
+        assert_scan_strict(h, y, inp, href, yref)
         assert_scan_close(h, y, inp, href, yref)
     finally:
         kmb.lib().kmb_set_force_generic(0)
@@ -41,13 +47,32 @@ def test_forward_matches_reference_fixture(kmb, cuda, name, generic):
 def test_config0_1d(kmb, cuda):
     # dims {1024}, D 64, M 16, batch 1, no RoPE, lambda 0.5
     inp = po.gen_scan([1024], 64, 16, batch=1, seed=100)
-    _run_both(kmb, cuda, inp, expect_path=1)
+    _run_both(kmb, cuda, inp, expect_path=1, zero_exempt=True)
 
 
 def test_config1_2d_rope(kmb, cuda):
     # dims {32,32}, D 64, M 16, batch 8, RoPE on
     inp = po.gen_scan([32, 32], 64, 16, batch=8, seed=101, rope=True)
-    _run_both(kmb, cuda, inp, expect_path=1)
+    r = _run_both(kmb, cuda, inp, expect_path=1)
+    # the fp32 reference itself misses the bound against the exact result at
+    # ~0.17 % of the entries (cancellation); the GPU may not miss more often
+    assert r["exempt"] > 0 and r["gpu_miss"] <= 1.25 * r["ref_miss"]
+
+
+@pytest.mark.parametrize("dims,D,M,flags", [([32, 32], 64, 16, dict(rope=True)), ([64, 64], 16, 64, {}),
+                                            ([64, 64], 16, 64, dict(rope=True, lam=True))])
+def test_forward_exp2_opt_in(kmb, cuda, dims, D, M, flags):
+    """The opt-in ex2.approx exponential: within 1e-5 normwise of the exact
+    result (it is a few ulp per alpha off expf, compounded over the levels)."""
+    from gpu_util import scan_fwd, assert_scan_close
+    inp = po.gen_scan(dims, D, M, batch=2, seed=sum(dims) + D + 5, **flags)
+    kmb.lib().kmb_set_scan_exp2(1)
+    try:
+        h, y, path = scan_fwd(inp, cuda)
+    finally:
+        kmb.lib().kmb_set_scan_exp2(0)
+    assert path == 1
+    assert_scan_close(h, y, inp, norm_factor=32.0)
 
 
 @pytest.mark.parametrize("dims,D,M,flags,path", [
@@ -70,7 +95,7 @@ def test_headline_shape_channel_slice(kmb, cuda):
     """Headline geometry at full channel count (2D 64x64, D 512, M 64, batch 2):
     every (item, channel-pair) recurrence is independent, so a 16-channel
     slice of the oracle must match the same slice of the GPU result."""
-    from gpu_util import scan_fwd, assert_scan_close
+    from gpu_util import scan_fwd, assert_scan_close, assert_scan_strict
     inp = po.gen_scan([64, 64], 512, 64, batch=2, seed=7, rope=True)
     h, y, path = scan_fwd(inp, cuda)
     assert path == 1
@@ -81,8 +106,10 @@ def test_headline_shape_channel_slice(kmb, cuda):
         sl["delta"] = np.ascontiguousarray(inp["delta"][b:b + 1, :, :, c0:c0 + 16])
         sl["A"] = np.ascontiguousarray(inp["A"][:, c0:c0 + 16])
         sl["theta"] = np.ascontiguousarray(inp["theta"][c0 // 2:c0 // 2 + 8])
-        assert_scan_close(np.ascontiguousarray(h[b:b + 1, :, c0:c0 + 16]),
-                          np.ascontiguousarray(y[b:b + 1, :, c0:c0 + 16]), sl)
+        hs = np.ascontiguousarray(h[b:b + 1, :, c0:c0 + 16])
+        ys = np.ascontiguousarray(y[b:b + 1, :, c0:c0 + 16])
+        assert_scan_strict(hs, ys, sl)
+        assert_scan_close(hs, ys, sl)
 
 
 def test_host_pointer_entry(kmb, cuda):
@@ -123,8 +150,9 @@ def test_backward_matches_exact_adjoint(kmb, cuda, dims, D, M, flags, generic):
         kmb.lib().kmb_set_force_generic(0)
 
 
-def _check_backward(dims, D, M, flags, cuda):
+def _check_backward(dims, D, M, flags, cuda, expect_path=None):
     from gpu_util import scan_bwd, assert_grad_close
+    import bissimamba_b200 as k
     batch = 2
     inp = po.gen_scan(dims, D, M, batch=batch, seed=41 + D, **flags)
     href, _ = po.oracle_scannd(inp)
@@ -132,12 +160,63 @@ def _check_backward(dims, D, M, flags, cuda):
     P = int(np.prod(dims))
     dy = rng.standard_normal((batch, P, D)).astype(np.float32)
     got = scan_bwd(inp, href, dy, cuda)
+    if expect_path is not None:
+        assert k.lib().kmb_last_backward_path() == expect_path
     ref = po.oracle_scannd_bwd(inp, href, dy)
     names = ["dA", "dB", "dC", "ddelta", "dlambda", "dx"] + (["dtheta"] if flags.get("rope") else [])
     for k in names:
         r = ref[k] if k != "dtheta" else ref[k][: D // 2]
         g = got[k] if k != "dtheta" else got[k][: D // 2]
         assert_grad_close(g, r, k)
+
+
+@pytest.mark.parametrize("dims,D,M,flags", [
+    ([32, 32], 64, 16, dict(rope=True)),                       # BASELINE config 1 geometry
+    ([12, 20], 4, 64, dict(rope=True, lam=True)),              # M = 64: two state halves
+    ([9, 17], 6, 32, dict(lam=True)),                          # partial last strip
+    ([7, 64], 8, 16, {}),                                      # eight strips
+    ([5, 3], 4, 64, dict(fast_exp=True, clamp=True, a_log_min=-2.0)),
+    ([1, 8], 4, 32, dict(rope=True)),                          # one row
+    ([8, 1], 4, 16, dict(rope=True, lam=True)),                # one column
+    ([16, 16], 8, 64, dict(clamp=True, a_log_min=-3.0, lam=True)),
+])
+def test_backward_strips(kmb, cuda, dims, D, M, flags):
+    """The 2D reverse systolic backward (path 2) against the exact adjoint."""
+    _check_backward(dims, D, M, flags, cuda, expect_path=2)
+
+
+@pytest.mark.parametrize("dims,D,M,flags", [([12, 20], 4, 64, dict(rope=True, lam=True)), ([6, 5], 6, 4, dict(rope=True))])
+def test_backward_overwrite_and_determinism(kmb, cuda, dims, D, M, flags):
+    """scannd_backward_ex(overwrite=1) assigns every output (buffers full of
+    garbage beforehand give the same bits as accumulating into zeros), and two
+    calls give identical bits."""
+    import torch
+    from gpu_util import to_dev
+    inp = po.gen_scan(dims, D, M, batch=2, seed=5, **flags)
+    href, _ = po.oracle_scannd(inp)
+    P, nd = int(np.prod(dims)), len(dims)
+    dy = np.random.default_rng(3).standard_normal((2, P, D)).astype(np.float32)
+    d = to_dev(inp, cuda)
+    ht = torch.from_numpy(href).to(cuda)
+    dyt = torch.from_numpy(dy).to(cuda)
+    shapes = {"dA": (nd, D, M), "dB": (2, P, D, M), "dC": (2, P, D, M), "ddelta": (2, nd, P, D),
+              "dlambda": (2, P), "dtheta": (D // 2,), "dx": (2, P, D)}
+
+    def run(fill, overwrite):
+        g = {k: torch.full(s, fill, device=cuda) for k, s in shapes.items()}
+        p = kmb.scan_params(inp["dims"], D, M, d["x"], d["A"], d["B"], d["C"], d["delta"], ht, dyt,
+                            theta=d.get("theta"), lam=d.get("lambda"), grads={k: v for k, v in g.items() if k != "dx"})
+        kmb.check(kmb.lib().scannd_backward_ex(C.byref(p), 2, g["dx"].data_ptr(), overwrite, None))
+        torch.cuda.synchronize()
+        return {k: v.cpu().numpy() for k, v in g.items()}
+    a = run(0.0, 0)
+    b = run(123.0, 1)
+    c = run(0.0, 0)
+    for k in shapes:
+        if k == "dtheta" and not flags.get("rope"):
+            continue
+        assert np.array_equal(a[k], b[k]), k
+        assert np.array_equal(a[k], c[k]), k
 
 
 def test_backward_accumulates(kmb, cuda):
@@ -200,7 +279,7 @@ def test_headline_full_size(kmb, cuda):
     the same items of the batched call bit for bit; and the last channel tile
     of the last item matches the oracle."""
     import torch
-    from gpu_util import assert_scan_close
+    from gpu_util import assert_scan_close, assert_scan_strict
     if torch.cuda.get_device_properties(0).total_memory < 80 * 2 ** 30:
         pytest.skip("needs the B200's memory")
     g = torch.Generator(device=cuda).manual_seed(5)
@@ -233,8 +312,10 @@ def test_headline_full_size(kmb, cuda):
     sl["C"] = Cm[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy()
     sl["delta"] = delta[it:it + 1, :, :, c0:c0 + 4].contiguous().cpu().numpy()
     sl["A"] = A[:, c0:c0 + 4].contiguous().cpu().numpy()
-    assert_scan_close(h[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy(),
-                      y[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy(), sl)
+    hs = h[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy()
+    ys = y[it:it + 1, :, c0:c0 + 4].contiguous().cpu().numpy()
+    assert_scan_strict(hs, ys, sl)
+    assert_scan_close(hs, ys, sl)
 
 
 @pytest.mark.parametrize("dims,D,M,flags", [([1, 64], 8, 16, {}), ([64, 1], 8, 16, dict(rope=True)),
