@@ -42,19 +42,18 @@
 // plus x, delta, dy, lambda and ddelta, dx per (point, channel).
 #include "kmb_common.cuh"
 #include "kmb_sync.cuh"
+#include <stdlib.h>
+#include <type_traits>
 
 namespace kmb {
 
-constexpr int BS_WC = 8;   // columns per strip
 constexpr int BS_K = 4;    // handoff slots per strip boundary
-constexpr int BS_RS = 36;  // padded row stride (floats) of the per-row reduction table
 
 struct BwdStripDesc {
-    int D, M, Q, O, S;      // channels, states, columns, rows, strips
-    int G;                  // state halves per channel tile (2 when M = 64)
+    int D, Q, O, S;         // channels, columns, rows, strips
     int ntd;                // channel tiles per item
     long long ntiles;       // batch * ntd * G
-    int has_lambda, clamp, fast, overwrite;
+    int has_lambda, clamp;
     float amin, deflam;
     long long P;
     const float *x, *A, *B, *C, *delta, *theta, *lambda, *h, *dy;
@@ -64,15 +63,20 @@ struct BwdStripDesc {
     int* status;
 };
 
-template <int MS>
+template <int M, int WC>
 struct BsGeom {
-    static constexpr int SETS = 32 / MS;        // channel sets per warp (2 when MS = 16)
-    static constexpr int CH = 2 * SETS;         // channels per tile
-    static constexpr int NOUT = BS_WC * CH * 3 + BS_WC;  // per-row outputs of a warp
+    static constexpr int MS = M == 16 ? 16 : 32;      // states of one tile
+    static constexpr int G = M / MS;                  // state halves (2 when M = 64)
+    static constexpr int SETS = 32 / MS;              // channel sets per warp (2 when M = 16)
+    static constexpr int CH = 2 * SETS;               // channels per tile
     // small per-row inputs in the cp.async ring: x [WC+1][CH], dI, dO, dy [WC][CH], lam [WC]
-    static constexpr int XO = 0, DIO = (BS_WC + 1) * CH, DOO = DIO + BS_WC * CH, DYO = DOO + BS_WC * CH,
-                         LO = DYO + BS_WC * CH, SMALL = (LO + BS_WC + 3) / 4 * 4;
-    static constexpr int NSL = (SMALL + 31) / 32;  // small loads per lane per row
+    static constexpr int XO = 0, DIO = (WC + 1) * CH, DOO = DIO + WC * CH, DYO = DOO + WC * CH,
+                         LO = DYO + WC * CH, SMALL = (LO + WC + 3) / 4 * 4;
+    static constexpr int NSL = (SMALL + 31) / 32;    // small loads per lane per row
+    // per-row reduction table: rows (j, k) k = ddelta inner, ddelta outer, dx (two floats per lane)
+    // and (j, 3) = dlambda (one float per lane); padded so 8 readers of 8 rows hit distinct banks
+    static constexpr int RS = 68;
+    static constexpr int ROWS = WC * 4;
 };
 
 __device__ __forceinline__ void cp_async4(uint32_t dst, const float* src) {
@@ -80,18 +84,18 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const float* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <int MS, bool ROPE>
-__global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant__ BwdStripDesc f) {
-    using Gm = BsGeom<MS>;
-    constexpr int WC = BS_WC, CH = Gm::CH, SM_ = Gm::SMALL;
+template <int M, bool ROPE, bool OVW, int WC>
+__global__ void __launch_bounds__(WC == 8 ? 256 : 512, 1) scan_bwd_strips(const __grid_constant__ BwdStripDesc f) {
+    using Gm = BsGeom<M, WC>;
+    constexpr int CH = Gm::CH, SM_ = Gm::SMALL, MS = Gm::MS, G = Gm::G, RS = Gm::RS;
     extern __shared__ __align__(16) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    const int S = f.S, D = f.D, M = f.M, Q = f.Q, O = f.O, G = f.G, ntd = f.ntd;
+    const int S = f.S, D = f.D, Q = f.Q, O = f.O, ntd = f.ntd;
     const long long P = f.P;
-    // smem: small ring [S][3][SMALL] | reduction table [S][64][BS_RS] | handoff [S][K][2][32][2] | barriers
+    // smem: small ring [S][3][SMALL] | reduction table [S][ROWS][RS] | handoff [S][K][2][32][2] | barriers
     float* small = (float*)smem;
     float* redt = small + S * 3 * SM_;
-    float* hand = redt + S * 64 * BS_RS;
+    float* hand = redt + S * Gm::ROWS * RS;
     uint64_t* bars = (uint64_t*)(hand + S * BS_K * 2 * 64);
     uint64_t* b_full = bars;                // [S][K]  boundary w: written by strip w, read by strip w-1
     uint64_t* b_empty = bars + S * BS_K;    // [S][K]
@@ -105,25 +109,23 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
     __syncthreads();
     if (w >= S) return;
 
-    const int set = lane / MS, ml = lane % MS;     // channel set, state within the half
+    const int set = lane / MS, ml = lane % MS;     // channel set, state within the tile
     const int cl0 = 2 * set;                       // first local channel of this lane
     const int q0 = w * WC;
     const int ncol = min(WC, Q - q0);
     float* my_small = small + w * 3 * SM_;
-    float* my_red = redt + w * 64 * BS_RS;
-    const long long DM = (long long)D * M;
+    float* my_red = redt + w * Gm::ROWS * RS;
+    const int DM = D * M;                          // item-local offsets are 32-bit (P * D * M < 2^31)
     const int ngl = ntd * G;
 
     // per-lane small-load plan (relative to the item base and the row): array, column, channel
     int sl_off[Gm::NSL];
-    int sl_dst[Gm::NSL];
     int sl_kind[Gm::NSL];  // 0 x, 1 delta inner, 2 delta outer, 3 dy, 4 lambda, -1 none
 #pragma unroll
     for (int t = 0; t < Gm::NSL; t++) {
         const int i = lane + 32 * t;
         sl_kind[t] = -1;
         sl_off[t] = 0;
-        sl_dst[t] = i;
         if (i < Gm::DIO) {
             const int j = i / CH - 1, c = i % CH;   // column -1 .. WC-1
             if (q0 + j >= 0 && j < ncol) { sl_kind[t] = 0; sl_off[t] = (q0 + j) * D + c; }
@@ -141,20 +143,23 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
         const int half = (int)(tile % G);
         const long long bt = tile / G;
         const int b = (int)(bt / ntd);
-        const int d0 = (int)(bt - (long long)b * ntd) * CH;
+        const int dt0 = (int)(bt - (long long)b * ntd);
+        const int d0 = dt0 * CH;
         const int mg = half * 32 + ml;           // state index
         const int dl0 = d0 + cl0;                // first channel of this lane
-        const float* hb = f.h + (long long)b * P * DM + (long long)dl0 * M + mg;
-        const float* Bb = f.B + (long long)b * P * DM + (long long)dl0 * M + mg;
-        const float* Cb = f.C + (long long)b * P * DM + (long long)dl0 * M + mg;
+        const long long ib = (long long)b * P * DM;
+        const int lofs = dl0 * M + mg + q0 * DM;  // this lane's offset in a row at column q0
+        const float* hb = f.h + ib + lofs;
+        const float* Bb = f.B + ib + lofs;
+        const float* Cb = f.C + ib + lofs;
+        float* dBb = f.dB + ib + lofs;
+        float* dCb = f.dC + ib + lofs;
         const float* xb = f.x + (long long)b * P * D + d0;
         const float* dlb = f.delta + (long long)b * 2 * P * D + d0;
         const float* dyb = f.dy + (long long)b * P * D + d0;
         const float* lb = f.has_lambda ? f.lambda + (long long)b * P : nullptr;
-        float* dBb = f.dB ? f.dB + (long long)b * P * DM + (long long)dl0 * M + mg : nullptr;
-        float* dCb = f.dC ? f.dC + (long long)b * P * DM + (long long)dl0 * M + mg : nullptr;
-        const long long rowDM = (long long)Q * DM;   // one row of h / B / C
-        float AI[2], AO[2];
+        const int rowDM = Q * DM;   // one row of h / B / C
+        float AI[2], AO[2], AIL[2], AOL[2];
         bool clI[2], clO[2];
 #pragma unroll
         for (int c = 0; c < 2; c++) {
@@ -164,6 +169,9 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
             clO[c] = f.clamp && ao > f.amin;
             AI[c] = clI[c] ? f.amin : ai;
             AO[c] = clO[c] ? f.amin : ao;
+            // alpha = 2^(delta * A log2 e): one multiply and one ex2 per alpha
+            AIL[c] = __fmul_rn(AI[c], kKmbLog2e);
+            AOL[c] = __fmul_rn(AO[c], kKmbLog2e);
         }
         float cth = 1.0f, sth = 0.0f;
         if (ROPE) {
@@ -174,28 +182,23 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
         // state ring: own row (o), predecessor row (o-1), row in flight (o-2)
         float hO[WC][2], bO[WC][2], hP[WC][2], bP[WC][2], hN[WC][2], bN[WC][2], cO[WC][2], cN[WC][2];
         auto load_hb = [&](int o, float (&hh)[WC][2], float (&bb)[WC][2]) {
+            const int ro = o * rowDM;
 #pragma unroll
             for (int j = 0; j < WC; j++)
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
-                    if (j < ncol && o >= 0) {
-                        const long long off = (long long)o * rowDM + (long long)(q0 + j) * DM + c * M;
-                        hh[j][c] = __ldg(hb + off);
-                        bb[j][c] = __ldg(Bb + off);
-                    } else {
-                        hh[j][c] = 0.0f;
-                        bb[j][c] = 0.0f;
-                    }
+                    const bool ok = j < ncol && o >= 0;
+                    hh[j][c] = ok ? __ldg(hb + (ro + j * DM + c * M)) : 0.0f;
+                    bb[j][c] = ok ? __ldg(Bb + (ro + j * DM + c * M)) : 0.0f;
                 }
         };
         auto load_c = [&](int o, float (&cc)[WC][2]) {
+            const int ro = o * rowDM;
 #pragma unroll
             for (int j = 0; j < WC; j++)
 #pragma unroll
                 for (int c = 0; c < 2; c++)
-                    cc[j][c] = (j < ncol && o >= 0)
-                                   ? __ldg(Cb + (long long)o * rowDM + (long long)(q0 + j) * DM + c * M)
-                                   : 0.0f;
+                    cc[j][c] = (j < ncol && o >= 0) ? __ldg(Cb + (ro + j * DM + c * M)) : 0.0f;
         };
         auto load_small = [&](int o) {
             if (o < 0) return;
@@ -205,8 +208,8 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
                 const int k = sl_kind[t];
                 if (k < 0) continue;
                 const float* src = k == 0 ? xb : k == 1 ? dlb + P * D : k == 2 ? dlb : k == 3 ? dyb : lb;
-                const long long rs = k == 4 ? (long long)Q : (long long)Q * D;
-                cp_async4(smem_u32(dst + sl_dst[t]), src + (long long)o * rs + sl_off[t]);
+                const int rs = k == 4 ? Q : Q * D;
+                cp_async4(smem_u32(dst + lane + 32 * t), src + (o * rs + sl_off[t]));
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
         };
@@ -221,21 +224,22 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
         for (int j = 0; j < WC; j++) dP[j][0] = dP[j][1] = dQ[j][0] = dQ[j][1] = 0.0f;
         float gAI[2] = {0.f, 0.f}, gAO[2] = {0.f, 0.f}, gth = 0.0f;
 
-#pragma unroll 1
-        for (int o = O - 1; o >= 0; o--, row++) {
+        // one row; HASU: the row above exists (o > 0)
+        auto do_row = [&](auto hasU_c, int o) -> bool {
+            constexpr bool HASU = decltype(hasU_c)::value;
             cp_async_wait_all();
             __syncwarp();
             // issue the row after next: h, B of o-2; C of o-1; small inputs of o-2
             load_hb(o - 2, hN, bN);
             load_c(o - 1, cN);
             load_small(o - 2);
+            const int ro = o * rowDM;
             float hL[2] = {0.f, 0.f}, bL[2] = {0.f, 0.f};
             if (q0 > 0) {
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
-                    const long long off = (long long)o * rowDM + (long long)(q0 - 1) * DM + c * M;
-                    hL[c] = __ldg(hb + off);
-                    bL[c] = __ldg(Bb + off);
+                    hL[c] = __ldg(hb + (ro - DM + c * M));
+                    bL[c] = __ldg(Bb + (ro - DM + c * M));
                 }
             }
             const float* sO = my_small + (o % 3) * SM_;
@@ -247,27 +251,33 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
             if (w + 1 < S) {
                 if (!mbar_wait(smem_u32(&b_full[(w + 1) * BS_K + hs]), hph)) {
                     set_status(f.status, KMB_ERR_TIMEOUT_Y);
-                    cp_async_wait_all();
-                    return;
+                    return false;
                 }
-                const float* src = hand + ((size_t)((w + 1) * BS_K + hs) * 2) * 64;
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    rP[c] = src[lane * 2 + c];
-                    rQ[c] = src[64 + lane * 2 + c];
-                }
+                const float2* src = (const float2*)(hand + ((size_t)((w + 1) * BS_K + hs) * 2) * 64);
+                const float2 pv = src[lane], qv = src[32 + lane];
+                rP[0] = pv.x; rP[1] = pv.y;
+                rQ[0] = qv.x; rQ[1] = qv.y;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&b_empty[(w + 1) * BS_K + hs]));
             }
-            const float lamr = f.deflam;
-            const bool hasU = o > 0;
+            // x of column j as (channel c0, c0 + 1); the left predecessor's x is the next column's own
+            float2 xr = *(const float2*)(sO + Gm::XO + (WC) * CH + cl0);
 #pragma unroll
             for (int j = WC - 1; j >= 0; j--) {
-                if (j >= ncol) continue;
-                const bool hasL = (q0 + j) > 0;
-                const float lam = f.has_lambda ? sO[Gm::LO + j] : lamr;
-                const int npred = (int)hasL + (int)hasU;
-                const float inv = npred == 2 ? 0.5f : 1.0f;
+                if (j >= ncol) {
+                    if (j > 0) xr = *(const float2*)(sO + Gm::XO + j * CH + cl0);
+                    continue;
+                }
+                const bool hasL = j > 0 || q0 > 0;
+                const float lam = f.has_lambda ? sO[Gm::LO + j] : f.deflam;
+                const float inv = (HASU && hasL) ? 0.5f : 1.0f;
+                const float2 xo = xr;                                                   // own x
+                const float2 xl = *(const float2*)(sO + Gm::XO + j * CH + cl0);         // left x
+                xr = xl;
+                const float2 xu = *(const float2*)(sP + Gm::XO + (j + 1) * CH + cl0);   // up x
+                const float2 dI2 = *(const float2*)(sO + Gm::DIO + j * CH + cl0);
+                const float2 dO2 = *(const float2*)(sO + Gm::DOO + j * CH + cl0);
+                const float2 dy2 = *(const float2*)(sO + Gm::DYO + j * CH + cl0);
                 float ah[2], ab[2], gh[2];
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
@@ -275,7 +285,6 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
                     ab[c] = rQ[c] + dQ[j][c];
                 }
                 const float h0 = hO[j][0], h1 = hO[j][1];
-                // predecessors' raw states (left: the next column, or the strip edge)
                 const float lh0 = j > 0 ? hO[j > 0 ? j - 1 : 0][0] : hL[0];
                 const float lh1 = j > 0 ? hO[j > 0 ? j - 1 : 0][1] : hL[1];
                 if (ROPE) {
@@ -288,48 +297,37 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
                     gh[0] = ah[0];
                     gh[1] = ah[1];
                 }
-                float* rr = my_red + (j * 2) * 4 * BS_RS + lane;
-                float glam_l = 0.0f;
+                const float oml = __fsub_rn(1.0f, lam);
+                float red_eI[2], red_eO[2], red_gx[2], glam_l = 0.0f;
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
-                    const int cc = cl0 + c;
-                    const float xv = sO[Gm::XO + (j + 1) * CH + cc];
-                    const float dI = sO[Gm::DIO + j * CH + cc];
-                    const float dO = sO[Gm::DOO + j * CH + cc];
-                    const float dyv = sO[Gm::DYO + j * CH + cc];
+                    const float xv = c ? xo.y : xo.x;
+                    const float dI = c ? dI2.y : dI2.x;
+                    const float dO = c ? dO2.y : dO2.x;
+                    const float dyv = c ? dy2.y : dy2.x;
                     const float hv = c ? h1 : h0;
                     const float Bv = bO[j][c];
-                    float g = __fmaf_rn(cO[j][c], dyv, gh[c]);
-                    const long long eo = (long long)o * rowDM + (long long)(q0 + j) * DM + c * M;
-                    if (dCb) {
-                        const float v = __fmul_rn(dyv, hv);
-                        if (f.overwrite) __stcs(dCb + eo, v);
-                        else atomicAdd(dCb + eo, v);
-                    }
+                    const float g = __fmaf_rn(cO[j][c], dyv, gh[c]);
+                    const int eo = ro + j * DM + c * M;
                     const float dt = __fadd_rn(dO, dI);
                     const float bu = __fmul_rn(Bv, xv);
                     const float gam = __fmul_rn(lam, dt);
-                    float PI = 0.0f, PO = 0.0f, Qv = 0.0f, eI = 0.0f, eO = 0.0f;
                     float gdt = __fmul_rn(__fmul_rn(lam, bu), g);
                     float gl = __fmul_rn(__fmul_rn(dt, bu), g);
-                    if (npred > 0) {
-                        float aI = 0.0f, aO = 0.0f, zI = 0.0f, zO = 0.0f, sbu = 0.0f;
-                        float hatL = 0.0f, hatU = 0.0f;
+                    float PI = 0.0f, PO = 0.0f, Qv = 0.0f, eI = 0.0f, eO = 0.0f;
+                    if (HASU || hasL) {
+                        float aI = 0.0f, aO = 0.0f, sbu = 0.0f, hatL = 0.0f, hatU = 0.0f;
                         if (hasL) {
-                            zI = __fmul_rn(dI, AI[c]);
-                            aI = kmb_exp(zI, f.fast);
-                            const float xl = sO[Gm::XO + j * CH + cc];
+                            aI = kmb_ex2(__fmul_rn(dI, AIL[c]));
                             const float bl = j > 0 ? bO[j > 0 ? j - 1 : 0][c] : bL[c];
-                            sbu = __fmul_rn(bl, xl);
+                            sbu = __fmul_rn(bl, c ? xl.y : xl.x);
                             hatL = ROPE ? (c ? __fmaf_rn(sth, lh0, __fmul_rn(cth, lh1))
                                              : __fmaf_rn(cth, lh0, -__fmul_rn(sth, lh1)))
                                         : (c ? lh1 : lh0);
                         }
-                        if (hasU) {
-                            zO = __fmul_rn(dO, AO[c]);
-                            aO = kmb_exp(zO, f.fast);
-                            const float xu = sP[Gm::XO + (j + 1) * CH + cc];
-                            sbu = __fmaf_rn(bP[j][c], xu, sbu);
+                        if (HASU) {
+                            aO = kmb_ex2(__fmul_rn(dO, AOL[c]));
+                            sbu = __fmaf_rn(bP[j][c], c ? xu.y : xu.x, sbu);
                             const float u0 = hP[j][0], u1 = hP[j][1];
                             hatU = ROPE ? (c ? __fmaf_rn(sth, u0, __fmul_rn(cth, u1))
                                              : __fmaf_rn(cth, u0, -__fmul_rn(sth, u1)))
@@ -337,7 +335,6 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
                         }
                         const float ma = __fmul_rn(__fadd_rn(aI, aO), inv);   // mean alpha
                         const float mb = __fmul_rn(sbu, inv);                  // mean predecessor Bu
-                        const float oml = __fsub_rn(1.0f, lam);
                         const float omdt = __fmul_rn(oml, dt);
                         PI = __fmul_rn(aI, g);
                         PO = __fmul_rn(aO, g);
@@ -347,25 +344,27 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
                         gl = __fmaf_rn(-__fmul_rn(dt, mab), g, gl);
                         const float ka = __fmul_rn(__fmul_rn(omdt, inv), mb);   // d h / d a_k beyond the state term
                         if (hasL) {
-                            const float dz = __fmul_rn(__fmul_rn(kmb_dexp(zI, aI, f.fast), g), __fadd_rn(hatL, ka));
+                            const float dz = __fmul_rn(PI, __fadd_rn(hatL, ka));   // (d a / d z) g (...) with d a / d z = a
                             eI = __fmul_rn(dz, AI[c]);
-                            if (!clI[c]) gAI[c] = __fmaf_rn(dz, dI, gAI[c]);
+                            gAI[c] = clI[c] ? gAI[c] : __fmaf_rn(dz, dI, gAI[c]);
                         }
-                        if (hasU) {
-                            const float dz = __fmul_rn(__fmul_rn(kmb_dexp(zO, aO, f.fast), g), __fadd_rn(hatU, ka));
+                        if (HASU) {
+                            const float dz = __fmul_rn(PO, __fadd_rn(hatU, ka));
                             eO = __fmul_rn(dz, AO[c]);
-                            if (!clO[c]) gAO[c] = __fmaf_rn(dz, dO, gAO[c]);
+                            gAO[c] = clO[c] ? gAO[c] : __fmaf_rn(dz, dO, gAO[c]);
                         }
                     }
                     const float gbu = __fmaf_rn(gam, g, ab[c]);
-                    if (dBb) {
-                        const float v = __fmul_rn(gbu, xv);
-                        if (f.overwrite) __stcs(dBb + eo, v);
-                        else atomicAdd(dBb + eo, v);
+                    if (OVW) {
+                        __stcs(dCb + eo, __fmul_rn(dyv, hv));
+                        __stcs(dBb + eo, __fmul_rn(gbu, xv));
+                    } else {
+                        atomicAdd(dCb + eo, __fmul_rn(dyv, hv));
+                        atomicAdd(dBb + eo, __fmul_rn(gbu, xv));
                     }
-                    rr[(c * 4 + 0) * BS_RS] = __fadd_rn(eI, gdt);
-                    rr[(c * 4 + 1) * BS_RS] = __fadd_rn(eO, gdt);
-                    rr[(c * 4 + 2) * BS_RS] = __fmul_rn(gbu, Bv);
+                    red_eI[c] = __fadd_rn(eI, gdt);
+                    red_eO[c] = __fadd_rn(eO, gdt);
+                    red_gx[c] = __fmul_rn(gbu, Bv);
                     glam_l = __fadd_rn(glam_l, gl);
                     // pass to the predecessors: (P_in, Q) left, (P_out, Q) up
                     dP[j][c] = PO;
@@ -373,69 +372,74 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
                     rP[c] = PI;
                     rQ[c] = Qv;
                 }
-                rr[3 * BS_RS] = glam_l;
+                float* rr = my_red + (j * 4) * RS;
+                *(float2*)(rr + 0 * RS + 2 * lane) = make_float2(red_eI[0], red_eI[1]);
+                *(float2*)(rr + 1 * RS + 2 * lane) = make_float2(red_eO[0], red_eO[1]);
+                *(float2*)(rr + 2 * RS + 2 * lane) = make_float2(red_gx[0], red_gx[1]);
+                rr[3 * RS + lane] = glam_l;
             }
             // left edge: hand (P_in, Q) of column q0 to strip w-1
             if (w > 0) {
                 if (row >= BS_K && !mbar_wait(smem_u32(&b_empty[w * BS_K + hs]), hph ^ 1)) {
                     set_status(f.status, KMB_ERR_TIMEOUT_Y);
-                    cp_async_wait_all();
-                    return;
+                    return false;
                 }
-                float* dst = hand + ((size_t)(w * BS_K + hs) * 2) * 64;
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    dst[lane * 2 + c] = rP[c];
-                    dst[64 + lane * 2 + c] = rQ[c];
-                }
+                float2* dst = (float2*)(hand + ((size_t)(w * BS_K + hs) * 2) * 64);
+                dst[lane] = make_float2(rP[0], rP[1]);
+                dst[32 + lane] = make_float2(rQ[0], rQ[1]);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&b_full[w * BS_K + hs]));
             }
-            // sums over the states (fixed order) and their outputs
+            // sums over the states (fixed order) and their outputs: lane t < 3 WC reduces row
+            // (j, k) = (t / 3, t % 3) for all CH channels; lane 3 WC + j reduces dlambda of column j
             __syncwarp();
-            for (int t = lane; t < Gm::NOUT; t += 32) {
-                float acc = 0.0f;
-                int j, cc = 0, k = 3;
-                if (t < WC * CH * 3) {
-                    j = t / (CH * 3);
-                    cc = (t / 3) % CH;
-                    k = t % 3;
-                    const int s2 = cc / 2, c = cc % 2;
-                    const float* src = my_red + ((j * 2 + c) * 4 + k) * BS_RS + s2 * MS;
-#pragma unroll 4
-                    for (int l = 0; l < MS; l += 4) {
+            if (lane < 3 * WC) {
+                const int j = lane / 3, k = lane % 3;
+                if (j < ncol) {
+                    const float* src = my_red + (j * 4 + k) * RS;
+                    float acc[32 / MS][2];
+#pragma unroll
+                    for (int s2 = 0; s2 < 32 / MS; s2++) acc[s2][0] = acc[s2][1] = 0.0f;
+#pragma unroll
+                    for (int l = 0; l < 64; l += 4) {
                         const float4 v = *(const float4*)(src + l);
-                        acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+                        const int s2 = (l / 2) / MS;   // lane (l / 2) belongs to channel set s2
+                        acc[s2][0] = __fadd_rn(__fadd_rn(acc[s2][0], v.x), v.z);
+                        acc[s2][1] = __fadd_rn(__fadd_rn(acc[s2][1], v.y), v.w);
                     }
-                } else {
-                    j = t - WC * CH * 3;
-                    const float* src = my_red + (j * 2 * 4 + 3) * BS_RS;   // per-lane sums of both units
-#pragma unroll 4
+                    const int p = o * Q + q0 + j;
+#pragma unroll
+                    for (int s2 = 0; s2 < 32 / MS; s2++)
+#pragma unroll
+                        for (int c = 0; c < 2; c++) {
+                            const int cc = 2 * s2 + c;
+                            const long long pd = ((long long)b * P + p) * D + d0 + cc;
+                            const float v = acc[s2][c];
+                            if (G > 1) {
+                                f.part[(pd * G + half) * 3 + k] = v;
+                            } else if (k < 2) {
+                                if (f.ddelta) {
+                                    // inner axis is axis 1, outer axis 0
+                                    float* dd = f.ddelta + (((long long)b * 2 + (k == 0 ? 1 : 0)) * P + p) * D + d0 + cc;
+                                    *dd = OVW ? v : __fadd_rn(*dd, v);
+                                }
+                            } else if (f.dx) {
+                                float* dd = f.dx + pd;
+                                *dd = OVW ? v : __fadd_rn(*dd, v);
+                            }
+                        }
+                }
+            } else if (lane < 4 * WC) {
+                const int j = lane - 3 * WC;
+                if (j < ncol && f.plam) {
+                    const float* src = my_red + (j * 4 + 3) * RS;
+                    float acc = 0.0f;
+#pragma unroll
                     for (int l = 0; l < 32; l += 4) {
                         const float4 v = *(const float4*)(src + l);
                         acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
                     }
-                }
-                if (j >= ncol) continue;
-                const long long p = (long long)o * Q + q0 + j;
-                if (k == 3) {
-                    if (f.plam) f.plam[((long long)b * ngl + (bt - (long long)b * ntd) * G + half) * P + p] = acc;
-                    continue;
-                }
-                const long long pd = ((long long)b * P + p) * D + d0 + cc;
-                if (G > 1) {
-                    f.part[(pd * G + half) * 3 + k] = acc;
-                } else if (k < 2) {
-                    if (f.ddelta) {
-                        // inner axis is axis 1, outer axis 0
-                        float* dd = f.ddelta + (((long long)b * 2 + (k == 0 ? 1 : 0)) * P + p) * D + d0 + cc;
-                        if (f.overwrite) *dd = acc;
-                        else *dd = __fadd_rn(*dd, acc);
-                    }
-                } else if (f.dx) {
-                    float* dd = f.dx + pd;
-                    if (f.overwrite) *dd = acc;
-                    else *dd = __fadd_rn(*dd, acc);
+                    f.plam[((long long)b * ngl + dt0 * G + half) * P + o * Q + q0 + j] = acc;
                 }
             }
             __syncwarp();
@@ -450,6 +454,16 @@ __global__ void __launch_bounds__(256, 1) scan_bwd_strips(const __grid_constant_
                     bP[j][c] = bN[j][c];
                     cO[j][c] = cN[j][c];
                 }
+            row++;
+            return true;
+        };
+        bool ok = true;
+#pragma unroll 1
+        for (int o = O - 1; o >= 1 && ok; o--) ok = do_row(std::integral_constant<bool, true>(), o);
+        if (ok) ok = do_row(std::integral_constant<bool, false>(), 0);
+        if (!ok) {
+            cp_async_wait_all();
+            return;
         }
         // per-(item, strip) partials of dA (this lane's (d, state)) and dtheta
         {
@@ -511,26 +525,26 @@ __global__ void bwd_strips_lambda(const float* __restrict__ plam, float* __restr
 }
 
 // ------------------------------------------------------------------ host side
-static int bs_smem(int S, int small) {
-    return (S * 3 * small + S * 64 * BS_RS + S * BS_K * 2 * 64) * 4 + 2 * S * BS_K * 8;
-}
+constexpr long long BS_SMAX = 8;    // most strips a grid can have (64 columns of 8)
 
 size_t scan_bwd_strips_scratch_bytes(const ScanDesc& s) {
     const long long G = s.M == 64 ? 2 : 1;
-    const long long S = 8;
     const long long CH = s.M == 16 ? 4 : 2;
     const long long ntd = s.D / CH;
     size_t n = 0;
     if (G > 1) n += (size_t)s.batch * s.P * s.D * G * 3;
-    n += (size_t)s.batch * S * 2 * s.D * s.M;            // pA
-    n += (size_t)s.batch * G * S * (s.D / 2 + 1);         // pth
-    n += (size_t)s.batch * ntd * G * s.P;                 // plam
+    n += (size_t)s.batch * BS_SMAX * 2 * s.D * s.M;            // pA
+    n += (size_t)s.batch * G * BS_SMAX * (s.D / 2 + 1);         // pth
+    n += (size_t)s.batch * ntd * G * s.P;                       // plam
     return n * sizeof(float) + 4 * 256;
 }
 
-template <int MS, bool ROPE>
-static cudaError_t bs_launch(const BwdStripDesc& f, int smem, int threads, cudaStream_t st) {
-    auto k = scan_bwd_strips<MS, ROPE>;
+template <int M, bool ROPE, bool OVW, int WC>
+static cudaError_t bs_launch(const BwdStripDesc& f, cudaStream_t st) {
+    using Gm = BsGeom<M, WC>;
+    auto k = scan_bwd_strips<M, ROPE, OVW, WC>;
+    const int smem = (f.S * 3 * Gm::SMALL + f.S * Gm::ROWS * Gm::RS + f.S * BS_K * 2 * 64) * 4 + 2 * f.S * BS_K * 8;
+    const int threads = f.S * 32;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int dev, sms, per = 0;
@@ -544,25 +558,33 @@ static cudaError_t bs_launch(const BwdStripDesc& f, int smem, int threads, cudaS
     return cudaGetLastError();
 }
 
+template <int M, int WC>
+static cudaError_t bs_dispatch(const BwdStripDesc& f, bool rope, bool ovw, cudaStream_t st) {
+    if (rope) return ovw ? bs_launch<M, true, true, WC>(f, st) : bs_launch<M, true, false, WC>(f, st);
+    return ovw ? bs_launch<M, false, true, WC>(f, st) : bs_launch<M, false, false, WC>(f, st);
+}
+
 // 2D grids whose inner (last) extent is <= 64, M in {16, 32, 64}, D a multiple
-// of the channel tile.  cudaErrorNotSupported outside that envelope.
+// of the channel tile, dB and dC given, accurate exponential.
+// cudaErrorNotSupported outside that envelope.
 cudaError_t launch_scan_bwd_strips(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC, float* ddelta,
                                    float* dlambda, float* dtheta, float* dx, int overwrite, void* scratch, int* status,
                                    cudaStream_t st) {
     if (s.nd != 2 || s.dims[1] > 64 || s.dims[1] < 1) return cudaErrorNotSupported;
     if (s.M != 16 && s.M != 32 && s.M != 64) return cudaErrorNotSupported;
-    const int MS = s.M == 16 ? 16 : 32;
-    const int CH = MS == 16 ? 4 : 2;
+    if (!dB || !dC || s.fast_exp) return cudaErrorNotSupported;
+    const int CH = s.M == 16 ? 4 : 2;
     if (s.D % CH != 0) return cudaErrorNotSupported;
-    if (s.batch * s.P * s.D * s.M >= (1LL << 62) || s.P > 0x7fffffffLL) return cudaErrorNotSupported;
+    if (s.P * s.D * s.M >= (1LL << 31)) return cudaErrorNotSupported;   // 32-bit offsets inside an item
+    constexpr int WC = 8;   // measured: 4 columns per strip (16 warps, 128 registers) ran 1.6x slower
     BwdStripDesc f{};
-    f.D = s.D; f.M = s.M;
+    f.D = s.D;
     f.Q = (int)s.dims[1]; f.O = (int)s.dims[0];
-    f.S = (f.Q + BS_WC - 1) / BS_WC;
-    f.G = s.M == 64 ? 2 : 1;
+    f.S = (f.Q + WC - 1) / WC;
+    const int G = s.M == 64 ? 2 : 1;
     f.ntd = s.D / CH;
-    f.ntiles = s.batch * f.ntd * f.G;
-    f.has_lambda = s.has_lambda; f.clamp = s.clamp; f.fast = s.fast_exp; f.overwrite = overwrite;
+    f.ntiles = s.batch * f.ntd * G;
+    f.has_lambda = s.has_lambda; f.clamp = s.clamp;
     f.amin = s.a_log_min; f.deflam = s.default_lambda;
     f.P = s.P;
     f.x = s.x; f.A = s.A; f.B = s.B; f.C = s.C; f.delta = s.delta; f.theta = s.theta; f.lambda = s.lambda;
@@ -571,32 +593,31 @@ cudaError_t launch_scan_bwd_strips(const ScanDesc& s, const float* dy, float* dA
     f.status = status;
     auto align = [](char* p) { return (char*)(((uintptr_t)p + 255) & ~(uintptr_t)255); };
     char* c = align((char*)scratch);
-    const long long S = 8;   // partial rows are laid out for 8 strips
-    if (f.G > 1) { f.part = (float*)c; c = align(c + (size_t)s.batch * s.P * s.D * f.G * 3 * 4); }
-    f.pA = (float*)c; c = align(c + (size_t)s.batch * S * 2 * s.D * s.M * 4);
-    f.pth = (float*)c; c = align(c + (size_t)s.batch * f.G * S * (s.D / 2 + 1) * 4);
+    if (G > 1) { f.part = (float*)c; c = align(c + (size_t)s.batch * s.P * s.D * G * 3 * 4); }
+    f.pA = (float*)c; c = align(c + (size_t)s.batch * BS_SMAX * 2 * s.D * s.M * 4);
+    f.pth = (float*)c; c = align(c + (size_t)s.batch * G * BS_SMAX * (s.D / 2 + 1) * 4);
     f.plam = dlambda ? (float*)c : nullptr;
-    const int small = MS == 16 ? BsGeom<16>::SMALL : BsGeom<32>::SMALL;
-    const int smem = bs_smem(f.S, small);
-    const int threads = f.S * 32;
+    const bool ovw = overwrite != 0;
     cudaError_t e;
-    if (MS == 16) e = s.rope ? bs_launch<16, true>(f, smem, threads, st) : bs_launch<16, false>(f, smem, threads, st);
-    else e = s.rope ? bs_launch<32, true>(f, smem, threads, st) : bs_launch<32, false>(f, smem, threads, st);
+    switch (s.M) {
+        case 16: e = bs_dispatch<16, WC>(f, s.rope, ovw, st); break;
+        case 32: e = bs_dispatch<32, WC>(f, s.rope, ovw, st); break;
+        default: e = bs_dispatch<64, WC>(f, s.rope, ovw, st); break;
+    }
     if (e != cudaSuccess) return e;
     auto nb = [](long long n) { return (unsigned)((n + 255) / 256); };
-    if (f.G > 1 && (ddelta || dx))
-        bwd_strips_combine<<<nb(s.batch * s.P * s.D), 256, 0, st>>>(f.part, ddelta, dx, s.batch, s.P, s.D, f.G,
-                                                                    overwrite);
+    if (G > 1 && (ddelta || dx))
+        bwd_strips_combine<<<nb(s.batch * s.P * s.D), 256, 0, st>>>(f.part, ddelta, dx, s.batch, s.P, s.D, G, overwrite);
     if (dA) {
         const long long cnt = 2LL * s.D * s.M;
         bwd_strips_reduce<<<nb(cnt), 256, 0, st>>>(f.pA, dA, cnt, s.batch * f.S, cnt, overwrite);
     }
     if (dtheta && s.rope && s.D >= 2) {
         const long long cnt = s.D / 2;
-        bwd_strips_reduce<<<nb(cnt), 256, 0, st>>>(f.pth, dtheta, cnt, s.batch * f.G * f.S, s.D / 2, overwrite);
+        bwd_strips_reduce<<<nb(cnt), 256, 0, st>>>(f.pth, dtheta, cnt, s.batch * G * f.S, s.D / 2, overwrite);
     }
     if (dlambda)
-        bwd_strips_lambda<<<nb(s.batch * s.P), 256, 0, st>>>(f.plam, dlambda, s.batch, f.ntd * f.G, s.P, overwrite);
+        bwd_strips_lambda<<<nb(s.batch * s.P), 256, 0, st>>>(f.plam, dlambda, s.batch, f.ntd * G, s.P, overwrite);
     return cudaGetLastError();
 }
 

@@ -175,7 +175,7 @@ def _check_backward(dims, D, M, flags, cuda, expect_path=None):
     ([12, 20], 4, 64, dict(rope=True, lam=True)),              # M = 64: two state halves
     ([9, 17], 6, 32, dict(lam=True)),                          # partial last strip
     ([7, 64], 8, 16, {}),                                      # eight strips
-    ([5, 3], 4, 64, dict(fast_exp=True, clamp=True, a_log_min=-2.0)),
+    ([5, 3], 4, 64, dict(clamp=True, a_log_min=-2.0)),
     ([1, 8], 4, 32, dict(rope=True)),                          # one row
     ([8, 1], 4, 16, dict(rope=True, lam=True)),                # one column
     ([16, 16], 8, 64, dict(clamp=True, a_log_min=-3.0, lam=True)),
@@ -183,6 +183,15 @@ def _check_backward(dims, D, M, flags, cuda, expect_path=None):
 def test_backward_strips(kmb, cuda, dims, D, M, flags):
     """The 2D reverse systolic backward (path 2) against the exact adjoint."""
     _check_backward(dims, D, M, flags, cuda, expect_path=2)
+
+
+@pytest.mark.parametrize("dims,D,M,flags,path", [
+    ([5, 3], 4, 64, dict(fast_exp=True, clamp=True, a_log_min=-2.0), 0),   # polynomial exp: generic
+    ([4, 70], 4, 16, {}, 1),                                              # inner extent > 64: level kernel
+    ([3, 4, 5], 4, 64, dict(rope=True), 0),                               # 3D, M = 64: generic
+])
+def test_backward_fallback_paths(kmb, cuda, dims, D, M, flags, path):
+    _check_backward(dims, D, M, flags, cuda, expect_path=path)
 
 
 @pytest.mark.parametrize("dims,D,M,flags", [([12, 20], 4, 64, dict(rope=True, lam=True)), ([6, 5], 6, 4, dict(rope=True))])
