@@ -127,7 +127,7 @@ EXPORTS = [
     "km_wavefront_plan_matches_dims", "km_wavefront_plan_level_size", "km_wavefront_plan_level_offsets",
     "km_wavefront_plan_iter_forward", "km_wavefront_plan_iter_reverse",
     "kmb_last_error", "kmb_clear_error", "kmb_device_status", "kmb_last_forward_path", "kmb_set_force_generic",
-    "kmb_set_scan_exp2", "kmb_get_scan_exp2",
+    "kmb_set_scan_exp2", "kmb_get_scan_exp2", "kmb_init_tensor",
     "kmb_blockscan_forward", "kmb_blockscan_set_strips", "kmb_blockscan_last_forward_path", "kmb_blockscan_set_backward_strips",
     "kmb_blockscan_last_backward_path", "kmb_blockscan_backward", "kmb_blockscan_backward_ex", "kmb_block_activation_floats",
     "kmb_block_forward", "kmb_block_backward", "kmb_block_set_tensor_cores", "kmb_block_last_projection_path", "kmb_block_last_dx_path", "cuda_block_forward", "cuda_block_backward",
@@ -183,6 +183,8 @@ def lib():
         L.kmamba_free.argtypes = [C.c_void_p]
         L.kmamba_free.restype = None
         L.kmamba_init.argtypes = [C.c_void_p, C.c_uint32]
+        L.kmb_init_tensor.argtypes = [C.c_void_p, C.c_uint32, C.c_char_p, C.c_void_p, C.c_long]
+        L.kmb_init_tensor.restype = C.c_long
         L.kmamba_enable_training.argtypes = [C.c_void_p, C.POINTER(MBOptimConfig), C.c_float, C.c_float]
         L.kmamba_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
         L.kmamba_train_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]

@@ -110,8 +110,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_kernel(BSDesc s) {
     const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (pair) {
-        cth = cosf(s.theta[n0 >> 1]);
-        sth = sinf(s.theta[n0 >> 1]);
+        kmb_cos_sin(s.theta[n0 >> 1], &cth, &sth);
     }
     const long long L = s.L;
     const T* __restrict__ u = (const T*)s.u + b * L * R;
@@ -272,8 +271,7 @@ __global__ void __launch_bounds__(512) blockscan_fwd_ring(BSDesc s) {
     const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (pair) {
-        cth = cosf(s.theta[n0 >> 1]);
-        sth = sinf(s.theta[n0 >> 1]);
+        kmb_cos_sin(s.theta[n0 >> 1], &cth, &sth);
     }
     int strides[NDT];
 #pragma unroll
@@ -475,8 +473,7 @@ __global__ void __launch_bounds__(256, 1) blockscan_fwd_strips(BSDesc s, int* st
     const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (pair) {
-        cth = cosf(s.theta[lane]);
-        sth = sinf(s.theta[lane]);
+        kmb_cos_sin(s.theta[lane], &cth, &sth);
     }
     const long long L = s.L;
     const T* __restrict__ u = (const T*)s.u + b * L * R;
@@ -729,8 +726,7 @@ __global__ void __launch_bounds__(512) blockscan_bwd_generic(BSDesc s, BSGrad g)
     const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (pair) {
-        cth = cosf(s.theta[n0 >> 1]);
-        sth = sinf(s.theta[n0 >> 1]);
+        kmb_cos_sin(s.theta[n0 >> 1], &cth, &sth);
     }
     const long long L = s.L;
     const T* u = (const T*)s.u + b * L * R;
@@ -915,8 +911,7 @@ __global__ void __launch_bounds__(512) blockscan_bwd_kernel(BSDesc s, BSGrad g) 
     const float A0 = h0ok ? s.A[n0] : 0.0f, A1 = h1ok ? s.A[n1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (pair) {
-        cth = cosf(s.theta[n0 >> 1]);
-        sth = sinf(s.theta[n0 >> 1]);
+        kmb_cos_sin(s.theta[n0 >> 1], &cth, &sth);
     }
     const long long L = s.L;
     const T* __restrict__ u = (const T*)s.u + b * L * R;
@@ -1154,8 +1149,7 @@ __global__ void __launch_bounds__(256, 1) blockscan_bwd_strips(BSDesc s, BSGrad 
     const float A0 = hok ? s.A[n0] : 0.0f, A1 = hok ? s.A[n0 + 1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (hok) {
-        cth = cosf(s.theta[n0 >> 1]);
-        sth = sinf(s.theta[n0 >> 1]);
+        kmb_cos_sin(s.theta[n0 >> 1], &cth, &sth);
     }
     const long long L = s.L;
     const T* __restrict__ u = (const T*)s.u + b * L * R;
@@ -1455,8 +1449,7 @@ __global__ void __launch_bounds__(CW == 1 ? 512 : 256, 1) blockscan_fwd_gstrips(
     const float A0 = hok ? s.A[n0] : 0.0f, A1 = hok ? s.A[n0 + 1] : 0.0f;
     float cth = 1.0f, sth = 0.0f;
     if (hok) {
-        cth = cosf(s.theta[n0 >> 1]);
-        sth = sinf(s.theta[n0 >> 1]);
+        kmb_cos_sin(s.theta[n0 >> 1], &cth, &sth);
     }
     const long long L = s.L;
     const T* __restrict__ u = (const T*)s.u + b * L * R;

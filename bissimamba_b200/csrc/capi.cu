@@ -558,7 +558,12 @@ static bool conv_desc(const ConvNDParams* p, long batch, ConvDesc* c) {
     c->nd = (int)p->ndims;
     c->D = (int)p->D;
     c->K = (int)p->K;
-    c->V = (int)convnd_kernel_volume(p->ndims, p->K);
+    long long v = 1;   // K^ndims, rejected before it can overflow an int
+    for (long i = 0; i < p->ndims; i++) {
+        if (v > 0x7fffffffLL / p->K) return false;
+        v *= p->K;
+    }
+    c->V = (int)v;
     c->P = points_of(p->dims, p->ndims);
     c->batch = batch;
     long long st = 1;

@@ -536,7 +536,8 @@ static float* g_noalloc_ptr[kNoAllocMaxDevices];
 
 // Device address of the array on the current device.  The first call on a
 // device resolves it (cudaGetSymbolAddress); make that first call before any
-// stream capture.
+// stream capture.  The address is cached for the life of the process, so the
+// entry point must not be used across a cudaDeviceReset of that device.
 static cudaError_t noalloc_scratch_ptr(float** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -559,6 +560,10 @@ static cudaError_t launch_conv_bwd_noalloc(const ConvDesc& c, const float* in, c
     float* part = nullptr;
     cudaError_t e = noalloc_scratch_ptr(&part);
     if (e != cudaSuccess) return e;
+    // the fast kernels first, with as many partial-sum chunks as the array holds
+    e = conv_fast(c, false, in, ker, nullptr, nullptr, dy, din, dker, dbias, part, kNoAllocScratchFloats / per_chunk, st);
+    if (e != cudaErrorNotSupported) return e;
+    cudaGetLastError();
     long long nch = conv_chunks(c);
     if (nch > kNoAllocScratchFloats / per_chunk) nch = kNoAllocScratchFloats / per_chunk;
     const long long rows = c.batch * c.P;
@@ -612,10 +617,19 @@ extern "C" int convnd_backward_noalloc(ConvNDParams* p, long batch, void* stream
     c.nd = (int)p->ndims;
     c.D = (int)p->D;
     c.K = (int)p->K;
+    // (K^ndims + 1) * D must fit the array: check while multiplying, so a large K
+    // or ndims cannot wrap the product past the limit
+    const long long vmax = kmb::kNoAllocScratchFloats / p->D - 1;
     long long v = 1, P = 1;
     for (long i = 0; i < p->ndims; i++) {
         if (p->dims[i] <= 0) {
             snprintf(tl_noalloc_err, sizeof tl_noalloc_err, "invalid dims");
+            return -1;
+        }
+        if (v > vmax / p->K) {
+            snprintf(tl_noalloc_err, sizeof tl_noalloc_err,
+                     "convnd_backward_noalloc: (K^ndims + 1) * D exceeds the %lld-float scratch limit",
+                     kmb::kNoAllocScratchFloats);
             return -1;
         }
         v *= p->K;

@@ -49,6 +49,17 @@ __device__ __forceinline__ float kmb_exp(float z, int fast) {
     return expf(z);
 }
 
+// cos and sin of a RoPE angle, evaluated in double precision and rounded once
+// to float, so they are the correctly rounded values the reference's libm
+// cosf / sinf return (the rotation is applied at every point of a recurrence:
+// a one-ulp bias in it compounds over the levels).  Called once per tile.
+__device__ __forceinline__ void kmb_cos_sin(float th, float* c, float* s) {
+    double sd, cd;
+    sincos((double)th, &sd, &cd);
+    *c = (float)cd;
+    *s = (float)sd;
+}
+
 // 2^w as one hardware base-2 exponential (ex2.approx, a few ulp for |w| < 4;
 // results below 2^-126 flush to zero).  exp(delta * A) is evaluated as
 // kmb_ex2(delta * (A log2 e)) with A log2 e rounded once per channel, so the

@@ -279,23 +279,112 @@ void kmamba_free(KMamba* m) {
     delete m;
 }
 
+// ---- the reference's initialisation streams (bit for bit)
+// Seeds are finalised with the SplitMix64 mixer, draws are xorshift64 (13, 7, 17)
+// with 53-bit uniforms, as kernels/init_f32.c:17-45 and src/mamba_block.c:227-268.
+namespace {
+uint64_t init_mix(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    return z ^ (z >> 31);
+}
+inline uint64_t init_next(uint64_t& s) {
+    s ^= s << 13;
+    s ^= s >> 7;
+    s ^= s << 17;
+    return s;
+}
+inline double init_u53(uint64_t& s) { return (double)(init_next(s) >> 11) * (1.0 / 9007199254740992.0); }
+
+// embedding / head: Xavier-uniform over [-limit, limit), kmamba_init's stream
+// (src/kmamba.c:458-459: seed for the embedding, seed + 1 for the head)
+void init_xavier(float* w, size_t fan_in, size_t fan_out, uint32_t seed) {
+    uint64_t s = init_mix((uint64_t)seed + 0x9e3779b97f4a7c15ULL);
+    const float lim = sqrtf(6.0f / (float)(fan_in + fan_out));
+    const float lo = -lim, span = lim - lo;
+    for (size_t i = 0; i < fan_in * fan_out; i++) w[i] = fmaf((float)init_u53(s), span, lo);
+}
+
+// One block's tensors.  The reference seeds every block from its dimensions
+// (dim, state_size, seq_len), not from the model seed or the layer index, so
+// all layers start identical.  Order of the stream: W_in, W_out, W_B, W_C
+// (each Xavier over rows + cols), theta, delta_proj, lambda_proj.
+struct BlockInit {
+    std::vector<float> W_in, W_out, A_log, W_B, W_C, b_B, b_C, theta, delta_proj, lambda_proj;
+};
+BlockInit init_block(size_t D, size_t N, size_t R, size_t L) {
+    BlockInit b;
+    uint64_t s = init_mix((uint64_t)D ^ ((uint64_t)N << 16) ^ ((uint64_t)L << 32) ^ 0x9e3779b97f4a7c15ULL);
+    const size_t NR = N * R, TS = N / 2 > 0 ? N / 2 : 1;
+    b.A_log.assign(N, -1.0f);
+    auto mat = [&](std::vector<float>& v, size_t rows, size_t cols) {
+        v.resize(rows * cols);
+        const float scale = sqrtf(6.0f / (float)(rows + cols));
+        for (auto& x : v) x = ((float)init_u53(s) * 2.0f - 1.0f) * scale;
+    };
+    mat(b.W_in, R, D);
+    mat(b.W_out, D, R);
+    mat(b.W_B, NR, D);
+    mat(b.W_C, NR, D);
+    b.b_B.assign(NR, 0.0f);
+    b.b_C.assign(NR, 0.0f);
+    b.theta.resize(TS);
+    const float tsc = 2.0f * 3.14159f / (float)N;
+    for (auto& x : b.theta) x = (float)init_u53(s) * tsc;
+    b.delta_proj.resize(D);
+    for (auto& x : b.delta_proj) x = ((float)init_u53(s) - 0.5f) * 0.02f;
+    b.lambda_proj.resize(D);
+    for (auto& x : b.lambda_proj) x = ((float)init_u53(s) - 0.5f) * 0.02f;
+    return b;
+}
+const std::vector<float>* block_field(const BlockInit& b, const std::string& f) {
+    if (f == "W_in") return &b.W_in;
+    if (f == "W_out") return &b.W_out;
+    if (f == "A_log") return &b.A_log;
+    if (f == "W_B") return &b.W_B;
+    if (f == "W_C") return &b.W_C;
+    if (f == "b_B") return &b.b_B;
+    if (f == "b_C") return &b.b_C;
+    if (f == "theta") return &b.theta;
+    if (f == "delta_proj") return &b.delta_proj;
+    if (f == "lambda_proj") return &b.lambda_proj;
+    return nullptr;
+}
+}  // namespace
+
+long kmb_init_tensor(const KMambaConfig* cfg, uint32_t seed, const char* name, float* out, long n) {
+    if (!cfg || !name || !out) return -1;
+    const size_t V = cfg->vocab_size, D = cfg->dim, N = cfg->state_size, L = cfg->seq_len;
+    const size_t R = cfg->mimo_rank > 1 ? cfg->mimo_rank : 1;
+    const std::string nm(name);
+    if (nm == "embedding" || nm == "head") {
+        if ((size_t)n < V * D) return -1;
+        if (nm == "embedding") init_xavier(out, V, D, seed);
+        else init_xavier(out, D, V, seed + 1);
+        return (long)(V * D);
+    }
+    unsigned li = 0;
+    char field[32];
+    if (sscanf(name, "layers.%u.%31s", &li, field) != 2 || li >= cfg->n_layers) return -1;
+    const BlockInit b = init_block(D, N, R, L);
+    const std::vector<float>* v = block_field(b, field);
+    if (!v || (size_t)n < v->size()) return -1;
+    memcpy(out, v->data(), v->size() * sizeof(float));
+    return (long)v->size();
+}
+
 int kmamba_init(KMamba* m, uint32_t seed) {
     if (!m) return -1;
     std::vector<float> h(m->n_params, 0.0f);
-    std::mt19937_64 rng(seed);
-    std::uniform_real_distribution<float> U(-1.0f, 1.0f), U01(0.0f, 1.0f);
-    auto xav = [&](size_t off, size_t fi, size_t fo) {
-        const float lim = std::sqrt(6.0f / (float)(fi + fo));
-        for (size_t i = 0; i < fi * fo; i++) h[off + i] = U(rng) * lim;
-    };
-    xav(0, m->V, m->D);
-    xav((size_t)m->V * m->D, m->D, m->V);
+    init_xavier(h.data(), m->V, m->D, seed);
+    init_xavier(h.data() + (size_t)m->V * m->D, m->D, m->V, seed + 1);
+    const BlockInit b = init_block(m->D, m->N, m->R, m->L);
     for (auto& l : m->lo) {
-        for (long n = 0; n < m->N; n++) h[l.A_log + n] = -1.0f;
-        xav(l.W_in, m->R, m->D); xav(l.W_out, m->D, m->R); xav(l.W_B, m->NR, m->D); xav(l.W_C, m->NR, m->D);
-        for (long i = 0; i < m->TS; i++) h[l.theta + i] = U01(rng) * (2.0f * 3.14159f / (float)m->N);
-        for (long i = 0; i < m->D; i++) h[l.delta_proj + i] = (U01(rng) - 0.5f) * 0.02f;
-        for (long i = 0; i < m->D; i++) h[l.lambda_proj + i] = (U01(rng) - 0.5f) * 0.02f;
+        const std::pair<size_t, const std::vector<float>*> parts[] = {
+            {l.W_in, &b.W_in}, {l.W_out, &b.W_out}, {l.A_log, &b.A_log}, {l.W_B, &b.W_B}, {l.W_C, &b.W_C},
+            {l.delta_proj, &b.delta_proj}, {l.lambda_proj, &b.lambda_proj}, {l.b_B, &b.b_B}, {l.b_C, &b.b_C},
+            {l.theta, &b.theta}};
+        for (auto& pr : parts) memcpy(h.data() + pr.first, pr.second->data(), pr.second->size() * sizeof(float));
     }
     cudaSetDevice(m->dev);
     cudaError_t e = cudaMemcpy(m->params, h.data(), m->n_params * 4, cudaMemcpyHostToDevice);

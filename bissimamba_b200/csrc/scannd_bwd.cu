@@ -83,8 +83,7 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
         }
     float cth = 1.0f, sth = 0.0f;
     if (rot) {
-        cth = cosf(w.theta[g]);
-        sth = sinf(w.theta[g]);
+        kmb_cos_sin(w.theta[g], &cth, &sth);
     }
     float gA[ND][2], gth = 0.0f;
 #pragma unroll

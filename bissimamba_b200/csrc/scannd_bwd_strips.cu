@@ -176,8 +176,7 @@ __global__ void __launch_bounds__(WC == 8 ? 256 : 512, 1) scan_bwd_strips(const 
         float cth = 1.0f, sth = 0.0f;
         if (ROPE) {
             const float th = f.theta[dl0 >> 1];
-            cth = cosf(th);
-            sth = sinf(th);
+            kmb_cos_sin(th, &cth, &sth);
         }
         // state ring: own row (o), predecessor row (o-1), row in flight (o-2)
         float hO[WC][2], bO[WC][2], hP[WC][2], bP[WC][2], hN[WC][2], bN[WC][2], cO[WC][2], cN[WC][2];

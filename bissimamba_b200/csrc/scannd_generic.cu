@@ -42,8 +42,7 @@ __global__ void __launch_bounds__(128) scan_fwd_generic(ScanDesc s) {
     float cth = 1.0f, sth = 0.0f;
     if (ROPE && nc == 2) {
         const float th = s.theta[g];
-        cth = cosf(th);
-        sth = sinf(th);
+        kmb_cos_sin(th, &cth, &sth);
     }
     int idx[KMB_MAXND];
     for (int k = 0; k < nd; k++) idx[k] = 0;
@@ -135,8 +134,7 @@ __global__ void __launch_bounds__(64) scan_bwd_generic(ScanDesc s, BwdArgs a) {
     const long long P = s.P;
     float cth = 1.0f, sth = 0.0f;
     if (rot) {
-        cth = cosf(s.theta[g]);
-        sth = sinf(s.theta[g]);
+        kmb_cos_sin(s.theta[g], &cth, &sth);
     }
     const float* xb = s.x + b * P * D;
     const float* Bb = s.B + b * P * D * M;

@@ -233,8 +233,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
         }
         if (ROPE) {
             const float th = f.theta[(d0 + cl0) >> 1];
-            cth = cosf(th);
-            sth = sinf(th);
+            kmb_cos_sin(th, &cth, &sth);
         }
         // h and y of the current row, advanced by one outer step per row
         float* hrow = f.h + (long long)b * P * DM + (long long)(d0 + cl0) * MT + m + (long long)q0 * hq;

@@ -232,8 +232,7 @@ scan_fwd_tma(const __grid_constant__ FastDesc f,
         float cth = 1.0f, sth = 0.0f;
         if (ROPE) {
             const float th = f.theta[d >> 1];
-            cth = cosf(th);
-            sth = sinf(th);
+            kmb_cos_sin(th, &cth, &sth);
         }
         float* const hb = f.h + (long long)b * f.P * DM + (long long)d * MT + m;
         float* const yb = f.y + (long long)b * f.P * D + d0;

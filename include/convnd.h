@@ -58,14 +58,16 @@ int convnd_status(void);
 int convnd_batched_async(ConvNDParams *p, long batch, int mode, void *stream);
 
 /* No counterpart in the reference.  The backward of convnd_batched_async
- * (same results, same overwrite semantics, dkernel/dbias summed over the
- * batch) for callers that must not allocate device memory -- e.g. code
+ * (same results up to the order of the dkernel / dbias partial sums, same
+ * overwrite semantics, dkernel/dbias summed over the batch) for callers that must not allocate device memory -- e.g. code
  * running under a fixed memory pool or arena, inside allocator hooks, or on
  * paths that may not take the allocator's locks.  It calls no cudaMalloc /
  * cudaFree: its partial sums live in one 4 MiB device array that is part of
  * the loaded library (held on every GPU that loads it until exit), so it
  * rejects (K^ndims + 1) * D > 1048576 with -1.  The first call on a device
- * looks up that array's address; make it before any stream capture.  All
+ * looks up that array's address; make it before any stream capture, and do
+ * not use the entry point across a cudaDeviceReset of that device (the address
+ * is kept for the life of the process).  All
  * calls share the array: calls that overlap on the GPU race.  Device
  * pointers only; enqueued on `stream` without synchronising.  0 / -1; the
  * reason of a -1 is returned by convnd_backward_noalloc_error(). */

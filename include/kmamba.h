@@ -68,11 +68,18 @@ void kmamba_optim_config_set_defaults(MBOptimConfig *opt_cfg);
  * device arena on cfg->gpu_device (or the current device). */
 KMamba *kmamba_create(const KMambaConfig *cfg);
 void kmamba_free(KMamba *m);
-/* reference src/kmamba.c:453-466: Xavier-uniform embedding / head and block
- * matrices, A_log = -1, theta in [0, 2 pi / N), delta / lambda projections in
- * +-0.01, zero biases (seeded from `seed`; not bit-identical to the
- * reference's xorshift streams). */
+/* reference src/kmamba.c:453-466: the reference's own streams, bit for bit:
+ * Xavier-uniform embedding (seed) and head (seed + 1), kernels/init_f32.c:38-45;
+ * every block from the stream seeded by (dim, state_size, seq_len),
+ * src/mamba_block.c:227-268 (A_log = -1, Xavier W_in / W_out / W_B / W_C,
+ * theta in [0, 2 pi / N), delta / lambda projections in +-0.01, zero biases;
+ * all layers start identical, as in the reference). */
 int kmamba_init(KMamba *m, uint32_t seed);
+/* The values kmamba_init(seed) gives the tensor `name` ("embedding", "head",
+ * "layers.<i>.<field>") of a model with config `cfg`, computed on the host
+ * into out[0 .. n) (no device needed).  Returns the element count, or -1 for
+ * an unknown name or a short buffer.  No counterpart in the reference. */
+long kmb_init_tensor(const KMambaConfig *cfg, uint32_t seed, const char *name, float *out, long n);
 /* reference src/kmamba.c:468-486 */
 int kmamba_enable_training(KMamba *m, const MBOptimConfig *opt_blocks, float lr_embed_head, float weight_decay);
 /* reference src/kmamba.c:626-660: tokens[seq_len] (host) -> logits[seq_len, vocab] (host). */

@@ -597,6 +597,22 @@ def gen_model_params(V, dim, N, R, nl, seed=0):
     return p
 
 
+def ref_model_init(dims, V, dim, N, R, nl, seed, names, sizes):
+    """The reference's kmamba_init(seed) (src/kmamba.c:453-466) -> {name: array}."""
+    lib = _lib("ref")
+    dims_a = np.asarray(dims, np.int64)
+    outs = [np.zeros(n, np.float32) for n in sizes]
+    names_a = (C.c_char_p * len(names))(*[n.encode() for n in names])
+    ptrs = (C.c_void_p * len(names))(*[o.ctypes.data for o in outs])
+    lib.shim_model_init_tensors.restype = C.c_int
+    rc = lib.shim_model_init_tensors(dims_a.ctypes.data_as(_l), C.c_long(len(dims)), C.c_long(V), C.c_long(dim),
+                                     C.c_long(N), C.c_long(R), C.c_long(nl), C.c_uint32(seed), names_a, ptrs,
+                                     C.c_long(len(names)))
+    if rc != 0:
+        raise RuntimeError(f"shim_model_init_tensors rc={rc}")
+    return dict(zip(names, outs))
+
+
 def ref_model_forward(dims, V, dim, N, R, nl, params, tokens):
     """Reference kmamba_forward (CPU) logits[L, V] for one token sequence."""
     lib = _lib("ref")
@@ -615,6 +631,39 @@ def ref_model_forward(dims, V, dim, N, R, nl, params, tokens):
     if rc != 0:
         raise RuntimeError(f"reference model forward failed ({rc})")
     return logits
+
+
+def model_logits64(dims, V, dim, N, R, nl, params, tokens, dt_min=1e-3, dt_max=0.1):
+    """Double-precision logits[L, V] of one sequence (embedding, blocks, head)."""
+    emb = np.asarray(params["embedding"], np.float64)
+    tin = np.where(tokens >= V, 0, tokens).astype(np.int64)
+    h = emb[tin]
+    for i in range(nl):
+        lp = {k: params[f"layers.{i}.{k}"] for k in BLOCK_KEYS}
+        h = block_fwd64(lp, h, dims, N, R, dt_min, dt_max)
+    return h @ np.asarray(params["head"], np.float64)
+
+
+def perturbation_kappa(fn, arrays, n=2, eps=2.0 ** -24, seed=0, floor=1e-5):
+    """Condition estimate per output entry of the double-precision map
+    fn(**arrays): the change of each entry under a random relative
+    perturbation of every input by eps (fp32 input rounding), over its
+    magnitude: |f(x (1 + eps r)) - f(x)| / (eps max(|f(x)|, floor)), max over
+    n draws.  Entries near cancellation have large values."""
+    rng = np.random.default_rng(seed)
+    base = np.asarray(fn(**arrays), np.float64)
+    kap = np.zeros(base.shape)
+    for _ in range(n):
+        pert = {}
+        for k, v in arrays.items():
+            if isinstance(v, dict):
+                pert[k] = {kk: np.asarray(vv, np.float64) * (1 + eps * rng.uniform(-1, 1, np.shape(vv)))
+                           for kk, vv in v.items()}
+            else:
+                pert[k] = np.asarray(v, np.float64) * (1 + eps * rng.uniform(-1, 1, np.shape(v)))
+        d = np.abs(np.asarray(fn(**pert), np.float64) - base)
+        kap = np.maximum(kap, d / (eps * np.maximum(np.abs(base), floor)))
+    return base, kap
 
 
 def model_loss_and_grads(dims, V, dim, N, R, nl, params, batch_tokens, dt_min=1e-3, dt_max=0.1):

@@ -220,3 +220,50 @@ int shim_model_forward(const long *dims, long ndims, long V, long dim, long N, l
     kmamba_free(m);
     return rc;
 }
+
+/* Reference kmamba_init (src/kmamba.c:453-466) through its public API; every
+ * named tensor is copied out through the reference's structs (see above for
+ * why kmamba_get_tensor cannot be used). */
+int shim_model_init_tensors(const long *dims, long ndims, long V, long dim, long N, long R, long nl, uint32_t seed,
+                            const char *const *names, float *const *out, long ntensors) {
+    KMambaConfig cfg;
+    kmamba_config_set_defaults(&cfg);
+    long L = 1;
+    for (long i = 0; i < ndims; i++) L *= dims[i];
+    cfg.vocab_size = (size_t)V;
+    cfg.dim = (size_t)dim;
+    cfg.state_size = (size_t)N;
+    cfg.seq_len = (size_t)L;
+    cfg.n_layers = (size_t)nl;
+    cfg.mimo_rank = (size_t)R;
+    cfg.spatial_ndims = ndims;
+    for (long i = 0; i < ndims; i++) cfg.spatial_dims[i] = dims[i];
+    KMamba *m = kmamba_create(&cfg);
+    if (!m) return -1;
+    if (kmamba_init(m, seed) != 0) { kmamba_free(m); return -3; }
+    const size_t D = (size_t)dim, NR = (size_t)N * R, TS = N / 2 > 0 ? N / 2 : 1;
+    for (long i = 0; i < ntensors; i++) {
+        const float *src = NULL;
+        size_t n = 0, li;
+        char field[32];
+        if (!strcmp(names[i], "embedding")) { src = m->embedding; n = (size_t)V * D; }
+        else if (!strcmp(names[i], "head")) { src = m->head; n = D * (size_t)V; }
+        else if (sscanf(names[i], "layers.%zu.%31s", &li, field) == 2 && li < (size_t)nl) {
+            MambaBlock *b = m->layers[li];
+            if (!strcmp(field, "W_in")) { src = b->W_in.data; n = (size_t)R * D; }
+            else if (!strcmp(field, "W_out")) { src = b->W_out.data; n = D * (size_t)R; }
+            else if (!strcmp(field, "A_log")) { src = b->A_log.data; n = (size_t)N; }
+            else if (!strcmp(field, "W_B")) { src = b->W_B.data; n = NR * D; }
+            else if (!strcmp(field, "W_C")) { src = b->W_C.data; n = NR * D; }
+            else if (!strcmp(field, "delta_proj")) { src = b->delta_proj.data; n = D; }
+            else if (!strcmp(field, "lambda_proj")) { src = b->lambda_proj.data; n = D; }
+            else if (!strcmp(field, "b_B")) { src = b->b_B; n = NR; }
+            else if (!strcmp(field, "b_C")) { src = b->b_C; n = NR; }
+            else if (!strcmp(field, "theta")) { src = b->theta; n = TS; }
+        }
+        if (!src) { kmamba_free(m); return -2; }
+        memcpy(out[i], src, n * sizeof(float));
+    }
+    kmamba_free(m);
+    return 0;
+}

@@ -194,6 +194,38 @@ def assert_scan_strict(h, y, inp, href=None, yref=None, zero_exempt=False):
     return r
 
 
+KAPPA_PERT = 16.0
+
+
+def assert_close_strict(got, ref, exact, kappa, rtol=1e-4, atol=1e-5, name="", kappa_max=KAPPA_PERT):
+    """Elementwise parity bound |g - ref| <= atol + rtol |ref| against the
+    fp32 reference, asserted at every entry whose condition estimate kappa
+    (oracle.pyoracle.perturbation_kappa: the sensitivity to fp32 rounding of
+    the inputs) is <= kappa_max; at the ill-conditioned rest the GPU may miss
+    the bound against the exact result no more often than 1.5x the reference
+    itself (+16).  The input-perturbation estimate does not see the rounding
+    inside a recurrence, hence the low threshold: at kappa <= 16 (six draws)
+    the fp32 reference itself stays within 0.14 of the bound on the block
+    shapes tested, and such entries are ~88 % of the outputs."""
+    g = np.asarray(got, np.float64).ravel()
+    r = np.asarray(ref, np.float64).ravel()
+    e = np.asarray(exact, np.float64).ravel()
+    k = np.asarray(kappa, np.float64).ravel()
+    assert np.array_equal(np.isfinite(g), np.isfinite(r)), f"{name}: non-finite mask differs"
+    f = np.isfinite(r) & np.isfinite(e)
+    g, r, e, k = g[f], r[f], e[f], k[f]
+    well = k <= kappa_max
+    ratio = np.abs(g - r) / (atol + rtol * np.abs(r))
+    tol_e = atol + rtol * np.abs(e)
+    out = {"n": int(g.size), "well": int(well.sum()), "cond_viol": int((ratio[well] > 1).sum()),
+           "violations": int((ratio > 1).sum()), "gpu_miss": int((np.abs(g - e) > tol_e).sum()),
+           "ref_miss": int((np.abs(r - e) > tol_e).sum()),
+           "worst_well": float(ratio[well].max()) if well.any() else 0.0}
+    assert out["cond_viol"] == 0, f"{name}: strict parity on well-conditioned entries: {out}"
+    assert out["gpu_miss"] <= 1.5 * out["ref_miss"] + 16, f"{name}: strict parity against the exact result: {out}"
+    return out
+
+
 def assert_grad_close(got, ref, name, rtol=1e-3):
     """Gradients are compared against the double-precision adjoint:
     |g - g_ref| <= rtol * (|g_ref| + max|g_ref| * 1e-3)."""

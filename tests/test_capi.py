@@ -112,3 +112,30 @@ def test_model_config_layout_matches_reference(kmb):
     c = kmb.KMambaConfig()
     kmb.lib().kmamba_config_set_defaults(C.byref(c))
     assert (c.dim, c.state_size, c.seq_len, c.n_layers, c.vocab_size) == (512, 64, 1024, 12, 32768)
+
+
+@pytest.mark.parametrize("dims,V,dim,N,R,nl,seed", [([16, 32, 32], 256, 512, 64, 4, 2, 42),   # BASELINE config 4 shape
+                                                    ([64, 64], 256, 512, 64, 2, 1, 42),       # config 3 block
+                                                    ([6, 5], 37, 24, 6, 3, 2, 7)])
+def test_kmamba_init_matches_reference(dims, V, dim, N, R, nl, seed):
+    """kmamba_init(seed) gives the reference's weights bit for bit: every
+    tensor from kmb_init_tensor (the host stream kmamba_init uploads) equals
+    the reference's kmamba_init output (oracle/_ref, the reference sources)."""
+    import ctypes as C
+    from oracle import pyoracle as po
+    if not po.have_ref():
+        pytest.skip("reference build unavailable")
+    import bissimamba_b200 as kmb
+    cfg = kmb.model_config(dims, V, dim, N, R, nl)
+    NR, TS = N * R, max(N // 2, 1)
+    sizes = {"embedding": V * dim, "head": dim * V}
+    for i in range(nl):
+        for f, n in (("W_in", R * dim), ("W_out", dim * R), ("A_log", N), ("W_B", NR * dim), ("W_C", NR * dim),
+                     ("delta_proj", dim), ("lambda_proj", dim), ("b_B", NR), ("b_C", NR), ("theta", TS)):
+            sizes[f"layers.{i}.{f}"] = n
+    names = list(sizes)
+    ref = po.ref_model_init(dims, V, dim, N, R, nl, seed, names, [sizes[n] for n in names])
+    for n in names:
+        got = np.zeros(sizes[n], np.float32)
+        assert kmb.lib().kmb_init_tensor(C.byref(cfg), seed, n.encode(), got.ctypes.data, got.size) == got.size, n
+        assert np.array_equal(got.view(np.uint32), ref[n].view(np.uint32)), n

@@ -44,8 +44,11 @@ def test_block_forward(kmb, cuda, dims, dim, N, R):
         e_g = np.linalg.norm(out[b] - ex)
         lim = 1e-5 * np.linalg.norm(ex)
         if ref is not None:
+            from gpu_util import assert_close_strict
             lim = max(lim, 4 * np.linalg.norm(ref - ex))
-            np.testing.assert_allclose(out[b], ref, rtol=1e-4, atol=1e-5)
+            _, kap = po.perturbation_kappa(lambda params, x: po.block_fwd64(params, x, dims, N, R),
+                                           dict(params=params, x=x[b]), n=6)
+            assert_close_strict(out[b], ref, ex, kap, name=f"block out[{b}]")
         assert e_g <= lim + 1e-30, (e_g, lim)
 
 

@@ -35,7 +35,10 @@ def test_model_forward_matches_reference(kmb, cuda, dims, V, dim, N, R, nl):
     assert kmb.lib().kmamba_forward(m, tok.ctypes.data, logits.ctypes.data) == 0, kmb.last_error()
     kmb.lib().kmamba_free(m)
     ref = po.ref_model_forward(dims, V, dim, N, R, nl, params, tok)
-    np.testing.assert_allclose(logits, ref, rtol=1e-4, atol=1e-5)
+    from gpu_util import assert_close_strict
+    ex, kap = po.perturbation_kappa(lambda params: po.model_logits64(dims, V, dim, N, R, nl, params, tok),
+                                    dict(params=params), n=6)
+    assert_close_strict(logits, ref, ex, kap, name="logits")
 
 
 @pytest.mark.parametrize("dims,V,dim,N,R,nl", SHAPES)

@@ -38,7 +38,10 @@ def _run(kmb, dev, inp, noalloc):
 
 def test_noalloc_backward_matches_regular_twice(kmb, cuda):
     cases = [po.gen_conv([16, 16, 16], 256, 3, batch=4, seed=31),   # BASELINE config-2 shape
-             po.gen_conv([32, 32], 64, 3, batch=3, seed=32)]
+             po.gen_conv([32, 32], 64, 3, batch=3, seed=32),
+             # (K^3 + 1) * D = 126 * 2048 floats per partial-sum chunk: the array holds 4 chunks,
+             # fewer than the regular path uses, so the rows are regrouped into 4 chunks
+             po.gen_conv([16, 16, 16], 2048, 5, batch=1, seed=33)]
     for inp in cases:  # two calls in a row, different shapes: the shared array is reused
         got = _run(kmb, cuda, inp, noalloc=True)
         ref = _run(kmb, cuda, inp, noalloc=False)
@@ -51,5 +54,9 @@ def test_noalloc_rejects_oversize(kmb, cuda):
     buf = torch.zeros(16, device=cuda)
     # (K^nd + 1) * D = (5^4 + 1) * 2048 floats > the 1 Mi-float limit
     p = kmb.conv_params([5, 5, 5, 5], 2048, 5, buf, buf, None, None, buf, buf, buf, None)
+    assert kmb.lib().convnd_backward_noalloc(C.byref(p), 1, None) == -1
+    assert b"limit" in kmb.lib().convnd_backward_noalloc_error()
+    # K^ndims far beyond any integer width is rejected the same way, not wrapped
+    p = kmb.conv_params([2] * 16, 4, 1000, buf, buf, None, None, buf, buf, buf, None)
     assert kmb.lib().convnd_backward_noalloc(C.byref(p), 1, None) == -1
     assert b"limit" in kmb.lib().convnd_backward_noalloc_error()
