@@ -54,7 +54,6 @@ def set_workload(dims, d, m, batch):
 
 
 set_workload(DIMS, D, M, BATCH)
-PROFILE_MD = os.path.join(ROOT, "profiles", "scan_fwd_strips_headline.md")
 
 
 def parse():
@@ -71,9 +70,10 @@ def parse():
     ap.add_argument("--D", type=int, default=D)
     ap.add_argument("--M", type=int, default=M)
     ap.add_argument("--workload", default="scan_fwd",
-                    choices=["scan_fwd", "scan_bwd", "convnd", "block", "model"],
-                    help="scan_fwd = the headline line; the others measure the other BASELINE configs")
-    ap.add_argument("--bf16", action="store_true", help="block workload: bf16 storage, fp32 state (config 3)")
+                    choices=["scan_fwd", "scan_fwd_c0", "scan_fwd_c1", "scan_bwd", "scan_bwd_c1", "convnd2d",
+                             "convnd3d", "block", "block_bf16", "model", "all"],
+                    help="scan_fwd = the headline line; the others measure the other BASELINE configs "
+                         "(all = every other one, one line each)")
     ap.add_argument("--exp2", type=int, default=0,
                     help="exponential of the 2D forward: 0 default, 1 opt-in fast ex2.approx")
     a = ap.parse_args()
@@ -88,17 +88,6 @@ def peaks():
         return float(j["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
-
-
-def profiled_traffic_per_update():
-    """dram bytes per state update of the top kernel from the committed ncu summary."""
-    try:
-        for line in open(PROFILE_MD):
-            if line.strip().startswith("dram_bytes_per_update:"):
-                return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
 
 
 class ClockSampler:
@@ -302,11 +291,25 @@ def main():
 
     peak, peak_src = peaks()
     achieved = ALG_BYTES / mean_kern_s / 1e9
-    tpu = profiled_traffic_per_update()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                "traffic": (tpu * UPDATES if tpu else None),
+                # measured DRAM bytes of a launch come from ncu (profiles/scan_fwd_strips_headline.md),
+                # not from this run
+                "traffic": None,
                 "alg_bytes_per_launch": ALG_BYTES, "kernel": ("scan_fwd_strips" if len(DIMS) == 2 else "scan_fwd_tma") if path == 1 else "scan_fwd_generic"}
+
+    # the opt-in ex2.approx exponential on the same inputs (reported beside the default path)
+    variants = {}
+    if path == 1 and len(DIMS) == 2:
+        lib.kmb_set_scan_exp2(0 if args.exp2 else 1)
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        vms = _events(stream, step, max(args.steps // 3, 5)) / max(args.steps // 3, 5)
+        lib.kmb_set_scan_exp2(args.exp2)
+        variants["exp2" if not args.exp2 else "expf"] = {
+            "value": UPDATES * world / (vms / 1e3), "ms_per_step": vms,
+            "hbm_frac": round(ALG_BYTES / (vms / 1e3) / 1e9 / peak, 4)}
 
     # ------------------------------------------------------------- e2e
     e2e = None
@@ -361,6 +364,8 @@ def main():
                            "l2": f"inputs {ALG_BYTES / 1e9:.1f} GB/GPU >> 126 MB L2, no flush"},
                 "hbm_gbs": round(achieved, 1),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "exp": "expf, reference operation order" if not args.exp2 else "ex2.approx (opt-in)",
+                "variants": variants,
                 "gpu_launches": args.steps, "clocks": clk,
                 "kernel_ms": {"mean": statistics.mean(kern_ms), "min": min(kern_ms), "max": max(kern_ms)}}
         print(json.dumps(line), flush=True)
@@ -369,12 +374,18 @@ def main():
 
 
 # ---------------------------------------------------------------- other configs
-def _timed(step, steps, warmup, stream):
-    """CUDA-event time (ms) of `steps` calls after `warmup` calls."""
+# Every BASELINE config gets a full line: metric / value (device-resident
+# inputs, CUDA-event time), roofline of the step, cpu_baseline (the reference's
+# own CPU code on a bounded sample, rank 0 at N=1) and e2e (host buffers, the
+# H2D copies of the step's inputs and the D2H copies of its results inside the
+# timed region).  `--workload all` prints every line.
+OTHER = ("scan_fwd_c0", "scan_fwd_c1", "scan_bwd", "scan_bwd_c1", "convnd2d", "convnd3d", "block", "block_bf16",
+         "model")
+
+
+def _events(stream, step, steps):
+    """CUDA-event time (ms) of `steps` calls of step() on `stream`."""
     import torch
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     for _ in range(steps):
@@ -384,8 +395,371 @@ def _timed(step, steps, warmup, stream):
     return a.elapsed_time(b)
 
 
+def _timed(step, steps, warmup, stream):
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    return _events(stream, step, steps)
+
+
+def _e2e(stream, host_in, dev_in, dev_out, host_out, call, steps, unit_count, unit):
+    """Same metric through the C ABI with host buffers: every step copies the
+    inputs in from pinned host memory, calls, and copies the results out."""
+    import torch
+
+    def step():
+        for k in host_in:
+            dev_in[k].copy_(host_in[k], non_blocking=True)
+        call()
+        for k in dev_out:
+            host_out[k].copy_(dev_out[k], non_blocking=True)
+    step()
+    torch.cuda.synchronize()
+    ms = _events(stream, step, steps)
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+    return {"value": unit_count * steps / (ms / 1e3), "unit": unit, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms / steps, "steps": steps,
+            "path": "pinned host inputs -> device (cudaMemcpyAsync), C-ABI call, results -> pinned host, same stream"}
+
+
+def _pinned(t):
+    import torch
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t)
+    return h
+
+
+def _cpu_rate(fn, units, target_s=10.0, max_reps=5):
+    """Median seconds of fn() (after one warm-up) -> units/s."""
+    fn()
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(max_reps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > target_s:
+            break
+    return units / statistics.median(times), len(times)
+
+
+def _scan_inputs(g, dev, dims, D_, M_, B_, rope):
+    import torch
+    P_ = int(np.prod(dims))
+    nd = len(dims)
+    rn = lambda *s: torch.randn(s, generator=g, device=dev)
+    t = dict(x=rn(B_, P_, D_), delta=torch.nn.functional.softplus(rn(B_, nd, P_, D_) * 0.5 - 4.0),
+             A=-torch.exp(torch.rand((nd, D_, M_), generator=g, device=dev) * float(np.log(16.0))),
+             B=(rn(B_, P_, 1, M_) * 0.25).expand(B_, P_, D_, M_).contiguous(),
+             C=(rn(B_, P_, 1, M_) * 0.25).expand(B_, P_, D_, M_).contiguous())
+    t["theta"] = (torch.rand(D_ // 2, generator=g, device=dev) * 2 - 1) * float(np.pi) if rope else None
+    return t
+
+
+def wl_scan_fwd_small(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, world):
+    """BASELINE config 0 (1D {1024}, D 64, M 16, batch 1) or config 1 forward
+    (2D 32x32, D 64, M 16, batch 8, RoPE)."""
+    import torch
+    if which == "scan_fwd_c0":
+        dims, D_, M_, B_, rope, name = (1024,), 64, 16, 1, False, "scannd_fwd_1d1024_D64_M16_b1 (config 0)"
+    else:
+        dims, D_, M_, B_, rope, name = (32, 32), 64, 16, 8, True, "scannd_fwd_2d32x32_D64_M16_b8_rope (config 1)"
+    P_, nd = int(np.prod(dims)), len(dims)
+    t = _scan_inputs(g, dev, dims, D_, M_, B_, rope)
+    h, y = torch.empty(B_, P_, D_, M_, device=dev), torch.empty(B_, P_, D_, device=dev)
+    p = kmb.scan_params(list(dims), D_, M_, t["x"], t["A"], t["B"], t["C"], t["delta"], h, y, theta=t["theta"])
+    sp = C.c_void_p(stream.cuda_stream)
+    steps = max(args.steps, 20)
+    ms = _timed(lambda: kmb.check(lib.scannd_forward_async(C.byref(p), B_, sp)), steps, max(args.warmup, 3), stream)
+    upd = B_ * P_ * D_ * M_
+    alg = upd * 12 + B_ * P_ * D_ * (4 + 4 * nd + 4)
+    tt = ms / steps / 1e3
+    line = {"metric": "scanND state-updates/sec", "value": upd * world / tt, "unit": "state-updates/s",
+            "ms_per_step": ms / steps, "steps": steps, "config": {"workload": name, "l2": "inputs < L2: L2-resident"},
+            "roofline": {"bound": "hbm", "achieved": round(alg / tt / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(alg / tt / 1e9 / peak, 4), "peak_source": peak_src, "traffic": None,
+                         "alg_bytes_per_launch": alg,
+                         "kernel": "scan_fwd_tma" if nd == 1 else "scan_fwd_strips",
+                         "note": "inputs fit in L2 and one launch is a few microseconds: launch-latency bound"},
+            "gpu_launches": steps}
+    hin = {k: _pinned(v) for k, v in t.items() if v is not None and k != "A" and k != "theta"}
+    line["e2e"] = _e2e(stream, hin, {k: t[k] for k in hin}, {"h": h, "y": y},
+                       {"h": torch.empty(h.shape, pin_memory=True), "y": torch.empty(y.shape, pin_memory=True)},
+                       lambda: kmb.check(lib.scannd_forward_async(C.byref(p), B_, sp)), 20, upd * world,
+                       "state-updates/s")
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import pyoracle as po
+        threads = po.set_threads(len(os.sched_getaffinity(0)) or 1)
+        inp = po.gen_scan(list(dims), D_, M_, batch=B_, seed=3, rope=rope)
+        rate, n = _cpu_rate(lambda: po.ref_scannd(inp), upd)
+        line["cpu_baseline"] = {"value": rate, "unit": "state-updates/s", "cores": threads, "kind": "reference",
+                                "sample": f"scannd_ref (oracle/_ref) on the whole workload ({B_} items), median of {n}"}
+    return line
+
+
+def wl_scan_bwd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, world):
+    """Scan-A backward: the headline geometry (2D 64x64, D 512, M 64, batch 32)
+    or BASELINE config 1 (2D 32x32, D 64, M 16, batch 8, RoPE)."""
+    import torch
+    if which == "scan_bwd":
+        dims, D_, M_, B_, rope, name = (64, 64), 512, 64, 32, False, "scannd_bwd_2d64x64_D512_M64_b32 (headline geometry)"
+    else:
+        dims, D_, M_, B_, rope, name = (32, 32), 64, 16, 8, True, "scannd_bwd_2d32x32_D64_M16_b8_rope (config 1)"
+    P_, nd = int(np.prod(dims)), len(dims)
+    t = _scan_inputs(g, dev, dims, D_, M_, B_, rope)
+    h, y = torch.empty(B_, P_, D_, M_, device=dev), torch.empty(B_, P_, D_, device=dev)
+    p = kmb.scan_params(list(dims), D_, M_, t["x"], t["A"], t["B"], t["C"], t["delta"], h, y, theta=t["theta"])
+    sp = C.c_void_p(stream.cuda_stream)
+    kmb.check(lib.scannd_forward_async(C.byref(p), B_, sp))
+    torch.cuda.synchronize()
+    del y
+    dy = torch.randn((B_, P_, D_), generator=g, device=dev)
+    gr = {"dA": torch.zeros(nd, D_, M_, device=dev), "dB": torch.zeros(B_, P_, D_, M_, device=dev),
+          "dC": torch.zeros(B_, P_, D_, M_, device=dev), "ddelta": torch.zeros(B_, nd, P_, D_, device=dev),
+          "dlambda": torch.zeros(B_, P_, device=dev), "dtheta": torch.zeros(max(D_ // 2, 1), device=dev)}
+    dx = torch.zeros(B_, P_, D_, device=dev)
+    pb = kmb.scan_params(list(dims), D_, M_, t["x"], t["A"], t["B"], t["C"], t["delta"], h, dy, theta=t["theta"],
+                         grads=gr)
+    steps = max(args.steps // 6, 5) if which == "scan_bwd" else max(args.steps, 20)
+    call = lambda: kmb.check(lib.scannd_backward_async(C.byref(pb), B_, dx.data_ptr(), sp))
+    ms = _timed(call, steps, max(args.warmup, 3), stream)
+    path = lib.kmb_last_backward_path()
+    upd = B_ * P_ * D_ * M_
+    # accumulate (+=) semantics: read h, B, C, dB, dC; write dB, dC = 28 B per update; per (point, channel):
+    # read x, dy, delta[nd]; read + write ddelta[nd] and dx
+    alg = upd * 28 + B_ * P_ * D_ * (4 * (2 + nd) + 8 * (nd + 1)) + B_ * P_ * 8
+    tt = ms / steps / 1e3
+    line = {"metric": "scanND backward state-updates/sec", "value": upd * world / tt, "unit": "state-updates/s",
+            "ms_per_step": ms / steps, "steps": steps,
+            "config": {"workload": name, "semantics": "accumulate (+=) into every gradient, as the reference",
+                       "l2": "inputs >> L2" if which == "scan_bwd" else "inputs ~ L2 size"},
+            "roofline": {"bound": "hbm", "achieved": round(alg / tt / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(alg / tt / 1e9 / peak, 4), "peak_source": peak_src, "traffic": None,
+                         "alg_bytes_per_launch": alg,
+                         "kernel": {2: "scan_bwd_strips", 1: "scan_bwd_wave", 0: "scan_bwd_generic"}.get(path)},
+            "gpu_launches": steps * (5 if M_ == 64 else 4)}
+    # the same step with overwrite semantics (scannd_backward_ex): no read-back of the gradients
+    ovw = lambda: kmb.check(lib.scannd_backward_ex(C.byref(pb), B_, dx.data_ptr(), 1, sp))
+    ms_o = _timed(ovw, steps, 2, stream)
+    alg_o = upd * 20 + B_ * P_ * D_ * (4 * (2 + nd) + 4 * (nd + 1)) + B_ * P_ * 4
+    line["overwrite_variant"] = {"value": upd * world / (ms_o / steps / 1e3), "ms_per_step": ms_o / steps,
+                                 "hbm_frac": round(alg_o / (ms_o / steps / 1e3) / 1e9 / peak, 4)}
+    eb = B_ if which != "scan_bwd" else 4    # host RAM: 4 headline items (5.5 GB in, 4.4 GB out) per e2e step
+    hin = {"x": _pinned(t["x"][:eb]), "delta": _pinned(t["delta"][:eb]), "B": _pinned(t["B"][:eb]),
+           "C": _pinned(t["C"][:eb]), "h": _pinned(h[:eb]), "dy": _pinned(dy[:eb])}
+    din = {k: torch.empty_like(v, device=dev) for k, v in hin.items()}
+    gre = {k: (torch.zeros_like(v[:eb]) if v.dim() > 1 and k not in ("dA",) else torch.zeros_like(v)) for k, v in gr.items()}
+    dxe = torch.zeros((eb, P_, D_), device=dev)
+    pe = kmb.scan_params(list(dims), D_, M_, din["x"], t["A"], din["B"], din["C"], din["delta"], din["h"], din["dy"],
+                         theta=t["theta"], grads=gre)
+    outs = {"dB": gre["dB"], "dC": gre["dC"], "ddelta": gre["ddelta"], "dx": dxe, "dA": gre["dA"]}
+    line["e2e"] = _e2e(stream, hin, din, outs, {k: torch.empty(v.shape, pin_memory=True) for k, v in outs.items()},
+                       lambda: kmb.check(lib.scannd_backward_ex(C.byref(pe), eb, dxe.data_ptr(), 1, sp)), 3,
+                       eb * P_ * D_ * M_ * world, "state-updates/s")
+    line["e2e"]["batch_per_gpu"] = eb
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import pyoracle as po
+        d_s = 4 if which == "scan_bwd" else D_
+        inp = po.gen_scan(list(dims), d_s, M_, batch=1, seed=3, rope=rope)
+        hs, _ = po.oracle_scannd(inp)
+        dys = np.random.default_rng(1).standard_normal((1, P_, d_s)).astype(np.float32)
+        rate, n = _cpu_rate(lambda: po.oracle_scannd_bwd(inp, hs, dys), P_ * d_s * M_)
+        line["cpu_baseline"] = {"value": rate, "unit": "state-updates/s", "cores": 1, "kind": "port",
+                                "sample": f"the exact adjoint restated in C (oracle/scannd_oracle.c, double, one "
+                                          f"thread) on 1 item x {d_s} channels: the reference has no correct CPU "
+                                          f"Scan-A backward; median of {n}"}
+    return line
+
+
+def wl_convnd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, world):
+    """depthwise convND forward + backward, D 256, K 3, batch 16,
+    2D {32,32} or 3D {16,16,16}."""
+    import torch
+    dims = (32, 32) if which == "convnd2d" else (16, 16, 16)
+    D_, K_, B_ = 256, 3, 16
+    P_, V_ = int(np.prod(dims)), K_ ** len(dims)
+    rn = lambda *s: torch.randn(s, generator=g, device=dev)
+    xi, dy = rn(B_, P_, D_), rn(B_, P_, D_)
+    ker, bias = rn(V_, D_) / V_ ** 0.5, rn(D_) * 0.02 ** 0.5
+    out, din = torch.empty(B_, P_, D_, device=dev), torch.empty(B_, P_, D_, device=dev)
+    dk, db = torch.empty(V_, D_, device=dev), torch.empty(D_, device=dev)
+    p = kmb.conv_params(list(dims), D_, K_, xi, ker, bias, out, dy, din, dk, db)
+    sp = C.c_void_p(stream.cuda_stream)
+    steps = max(args.steps, 20)
+    call = lambda: kmb.check(lib.convnd_batched_async(C.byref(p), B_, 3, sp))
+    ms = _timed(call, steps, max(args.warmup, 3), stream)
+    tt = ms / steps / 1e3
+    units = B_ * P_ * D_
+    alg = units * 20    # forward: read input, write output; backward: read dy, input, write dinput
+    line = {"metric": "convND fwd+bwd outputs/sec", "value": units * world / tt, "unit": "outputs/s",
+            "ms_per_step": ms / steps, "steps": steps,
+            "config": {"workload": f"convnd_{'x'.join(map(str, dims))}_D256_K3_b16 (config 2)",
+                       "l2": "16 MB of inputs: L2-resident between steps"},
+            "roofline": {"bound": "hbm", "achieved": round(alg / tt / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(alg / tt / 1e9 / peak, 4), "peak_source": peak_src, "traffic": None,
+                         "alg_bytes_per_launch": alg},
+            "gpu_launches": steps * 3}
+    hin = {"input": _pinned(xi), "dy": _pinned(dy)}
+    dinp = {"input": xi, "dy": dy}
+    outs = {"output": out, "dinput": din, "dkernel": dk, "dbias": db}
+    line["e2e"] = _e2e(stream, hin, dinp, outs, {k: torch.empty(v.shape, pin_memory=True) for k, v in outs.items()},
+                       call, 20, units * world, "outputs/s")
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import pyoracle as po
+        threads = po.set_threads(len(os.sched_getaffinity(0)) or 1)
+        nb = 16 if len(dims) == 2 else 1
+        inp = po.gen_conv(list(dims), D_, K_, batch=nb, seed=3)
+        rate, n = _cpu_rate(lambda: po.conv_run(inp, "ref", 3), nb * P_ * D_)
+        line["cpu_baseline"] = {"value": rate, "unit": "outputs/s", "cores": threads, "kind": "reference",
+                                "sample": f"convnd_forward_wavefront + convnd_backward_wavefront (oracle/_ref) on "
+                                          f"{nb} item(s); the reference backward is serial; median of {n}"}
+    return line
+
+
+def _block_weights(lib, kmb, dims, dim, N, R, dev, g):
+    """Block parameters from kmamba_init(seed=42)'s stream (bit-identical to the
+    reference's), lambda_proj ~ N(0, 0.02) as BASELINE config 3 asks."""
+    import torch
+    cfg = kmb.model_config(list(dims), 256, dim, N, R, 1)
+    W = {}
+    for k in kmb.BLOCK_FIELDS:
+        n = {"W_in": R * dim, "W_out": dim * R, "A_log": N, "W_B": N * R * dim, "W_C": N * R * dim,
+             "delta_proj": dim, "lambda_proj": dim, "b_B": N * R, "b_C": N * R, "theta": max(N // 2, 1)}[k]
+        a = np.zeros(n, np.float32)
+        kmb.check(0 if lib.kmb_init_tensor(C.byref(cfg), 42, f"layers.0.{k}".encode(), a.ctypes.data, n) == n else -1)
+        W[k] = torch.from_numpy(a).to(dev)
+    W["lambda_proj"] = torch.randn(dim, generator=g, device=dev) * 0.02
+    return W
+
+
+def wl_block(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, world):
+    """Mamba-3 block forward + backward, dim 512, N 64, R 2,
+    2D 64x64, batch 32 (fp32 storage, or bf16 storage with fp32 state)."""
+    import torch
+    bf16 = which == "block_bf16"
+    dims, dim, N_, R_, B_ = (64, 64), 512, 64, 2, 32
+    L_ = 4096
+    W = _block_weights(lib, kmb, dims, dim, N_, R_, dev, g)
+    cfg = kmb.block_config(list(dims), dim, N_, R_, bf16=bf16)
+    w = kmb.KMBlockWeights(**{k: W[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+    G = {k: torch.zeros_like(v) for k, v in W.items()}
+    gw = kmb.KMBlockGrads(**{k: G[k].data_ptr() for k in kmb.BLOCK_FIELDS})
+    act_f = lib.kmb_block_activation_floats(C.byref(cfg), B_)
+    act = torch.empty(act_f, device=dev)
+    rn = lambda *s: torch.randn(s, generator=g, device=dev)
+    x, dout = rn(B_, L_, dim), rn(B_, L_, dim)
+    if bf16:
+        x, dout = x.to(torch.bfloat16), dout.to(torch.bfloat16)
+    out, dx = torch.empty_like(x), torch.empty_like(x)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def step():
+        kmb.check(lib.kmb_block_forward(C.byref(cfg), C.byref(w), x.data_ptr(), out.data_ptr(), B_, act.data_ptr(), sp))
+        kmb.check(lib.kmb_block_backward(C.byref(cfg), C.byref(w), x.data_ptr(), dout.data_ptr(), dx.data_ptr(),
+                                         C.byref(gw), B_, act.data_ptr(), sp))
+    steps = max(args.steps // 6, 10)
+    ms = _timed(step, steps, max(args.warmup, 3), stream)
+    tt = ms / steps / 1e3
+    esz = 2 if bf16 else 4
+    # compulsory traffic of the step: the saved activations written by the forward and read by the backward,
+    # x read twice, out, dout, dx once (weights and their gradients are < 1 MB)
+    alg = act_f * 4 * 2 + B_ * L_ * dim * esz * 5
+    line = {"metric": "Mamba-3 block fwd+bwd tokens/sec", "value": B_ * L_ * world / tt, "unit": "tokens/s",
+            "ms_per_step": ms / steps, "steps": steps,
+            "dtype": "bf16 storage / f32 state" if bf16 else "f32",
+            "config": {"workload": "block_dim512_N64_R2_2d64x64_b32 (config 3, "
+                                   + ("bf16 storage, fp32 state)" if bf16 else "fp32 storage)"),
+                       "init": "kmamba_init(seed=42) stream (reference-identical), lambda_proj ~ N(0, 0.02)"},
+            "scan_updates_per_s": B_ * L_ * N_ * R_ * world / tt,
+            "roofline": {"bound": "hbm", "achieved": round(alg / tt / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(alg / tt / 1e9 / peak, 4), "peak_source": peak_src, "traffic": None,
+                         "alg_bytes_per_launch": alg,
+                         "note": "whole-step compulsory bytes over the step time; per-kernel shares in profiles/"}}
+    hin = {"x": _pinned(x), "dout": _pinned(dout)}
+    outs = {"out": out, "dx": dx}
+    line["e2e"] = _e2e(stream, hin, {"x": x, "dout": dout}, outs,
+                       {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in outs.items()}, step, 5,
+                       B_ * L_ * world, "tokens/s")
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import pyoracle as po
+        threads = po.set_threads(len(os.sched_getaffinity(0)) or 1)
+        params = {k: v.cpu().numpy() for k, v in W.items()}
+        xs = np.random.default_rng(1).standard_normal((L_, dim)).astype(np.float32)
+        dys = np.random.default_rng(2).standard_normal((L_, dim)).astype(np.float32)
+        rate, n = _cpu_rate(lambda: po.ref_block_run(list(dims), dim, N_, R_, params, xs, dy=dys), L_, max_reps=3)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                "sample": f"mamba_block_forward_ws + mamba_backward_ws (oracle/_ref, fp32) on 1 item "
+                                          f"of the 32; median of {n}"}
+    return line
+
+
+def wl_model(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, world):
+    """12-layer k-mamba train step (forward, backward, AdamW),
+    dim 512, N 64, R 4, 3D {16,32,32}, batch 64, vocab 256."""
+    import torch
+    dims, V_, dim, N_, R_, nl, B_ = (16, 32, 32), 256, 512, 64, 4, 12, 64
+    B_ = int(os.environ.get("KMB_BENCH_MODEL_BATCH", B_))
+    cfgm = kmb.model_config(list(dims), V_, dim, N_, R_, nl)
+    m = lib.kmamba_create(C.byref(cfgm))
+    if not m:
+        raise RuntimeError(kmb.last_error())
+    kmb.check(lib.kmamba_init(m, 42))
+    opt = kmb.MBOptimConfig()
+    lib.kmamba_optim_config_set_defaults(C.byref(opt))
+    lib.kmamba_enable_training(m, C.byref(opt), 1e-3, 0.01)
+    L_ = 16384
+    tok = torch.randint(0, V_, (B_, L_ + 1), generator=g, device=dev, dtype=torch.int32)
+    sp = C.c_void_p(stream.cuda_stream)
+    losses = []
+
+    def step():
+        # NaN is a legitimate value at this scale (the 3D recurrence overflows fp32, as the reference's does)
+        loss = lib.kmb_model_forward_backward(m, tok.data_ptr(), B_, sp)
+        if loss != loss and kmb.last_error():
+            raise RuntimeError(kmb.last_error())
+        kmb.check(lib.kmb_model_optimizer_step(m, sp))
+        losses.append(loss if loss == loss else None)
+    steps = 3
+    ms = _timed(step, steps, 2, stream)
+    tt = ms / steps / 1e3
+    line = {"metric": "k-mamba train step tokens/sec", "value": B_ * L_ * world / tt, "unit": "tokens/s",
+            "ms_per_step": ms / steps, "steps": steps, "warmup": 2,
+            "config": {"workload": f"model_12x512_N64_R4_3d16x32x32_b{B_}_vocab256 (config 4)",
+                       "init": "kmamba_init(seed=42), reference-identical"},
+            "loss_first_last": [losses[0], losses[-1]],
+            "roofline": None}
+    # e2e: kmamba_train_batch with host tokens (copy in, forward, backward, AdamW, loss out)
+    htok = tok.cpu().numpy().astype(np.uint32)
+    eb = B_
+    lib.kmamba_train_batch(m, htok.ctypes.data, eb)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(2):
+        lib.kmamba_train_batch(m, htok.ctypes.data, eb)
+    dt = time.perf_counter() - t0
+    line["e2e"] = {"value": eb * L_ * world * 2 / dt, "unit": "tokens/s", "h2d_bytes_per_step": htok.nbytes,
+                   "d2h_bytes_per_step": 4, "steps": 2, "path": "kmamba_train_batch() with host tokens"}
+    lib.kmamba_free(m)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import pyoracle as po
+        threads = po.set_threads(len(os.sched_getaffinity(0)) or 1)
+        W = _block_weights(lib, kmb, dims, dim, N_, R_, dev, g)
+        params = {k: v.cpu().numpy() for k, v in W.items()}
+        xs = np.random.default_rng(1).standard_normal((L_, dim)).astype(np.float32) * 0.1
+        dys = np.random.default_rng(2).standard_normal((L_, dim)).astype(np.float32)
+        rate, n = _cpu_rate(lambda: po.ref_block_run(list(dims), dim, N_, R_, params, xs, dy=dys), L_, max_reps=2)
+        # one block of the 12, one sequence: tokens/s of the whole model is the block rate / 12 (the head,
+        # embedding and AdamW are a few percent of a layer and are not counted: an upper bound)
+        line["cpu_baseline"] = {"value": rate / nl, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                "sample": f"one reference block (mamba_block_forward_ws + mamba_backward_ws, "
+                                          f"oracle/_ref) on 1 sequence of 16384 tokens, rate / 12 layers; "
+                                          f"median of {n}"}
+    return line
+
+
 def run_other_workload(args, rank, world):
-    """BASELINE configs 1-4 on one GPU (per rank; weak scaling like the headline)."""
     import torch
     import torch.distributed as dist
     import bissimamba_b200 as kmb
@@ -397,133 +771,26 @@ def run_other_workload(args, rank, world):
         dist.init_process_group("nccl", device_id=dev)
     lib = kmb.lib()
     stream = torch.cuda.current_stream(dev)
-    sp = C.c_void_p(stream.cuda_stream)
-    g = torch.Generator(device=dev)
-    g.manual_seed(7 + rank)
-    rn = lambda *s: torch.randn(s, generator=g, device=dev)
-    steps, warm = max(args.steps // 6, 5), max(args.warmup, 3)
     peak, peak_src = peaks()
-    line = {"n_gpus": world, "steps": steps, "warmup": warm, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions), on device"}
-
-    if args.workload == "scan_bwd":
-        # BASELINE config 1 backward: 2D 32x32, D 64, M 16, batch 8, RoPE, dy ~ N(0,1)
-        dims, D_, M_, B_ = (32, 32), 64, 16, 8
-        P_ = 1024
-        x, dl = rn(B_, P_, D_), torch.nn.functional.softplus(rn(B_, 2, P_, D_) * 0.5 - 4.0)
-        A = -torch.exp(torch.rand((2, D_, M_), generator=g, device=dev) * torch.log(torch.tensor(16.0)))
-        Bm = (rn(B_, P_, 1, M_) * 0.25).expand(B_, P_, D_, M_).contiguous()
-        Cm = (rn(B_, P_, 1, M_) * 0.25).expand(B_, P_, D_, M_).contiguous()
-        th = torch.rand(D_ // 2, generator=g, device=dev) * 6.283 - 3.1416
-        h, y = torch.empty(B_, P_, D_, M_, device=dev), torch.empty(B_, P_, D_, device=dev)
-        p = kmb.scan_params(list(dims), D_, M_, x, A, Bm, Cm, dl, h, y, theta=th)
-        kmb.check(lib.scannd_forward_async(C.byref(p), B_, sp))
-        dy = rn(B_, P_, D_)
-        gr = {k: torch.zeros(s, device=dev) for k, s in (("dA", (2, D_, M_)), ("dB", (B_, P_, D_, M_)),
-                                                           ("dC", (B_, P_, D_, M_)), ("ddelta", (B_, 2, P_, D_)),
-                                                           ("dlambda", (B_, P_)), ("dtheta", (D_ // 2,)))}
-        dx = torch.zeros(B_, P_, D_, device=dev)
-        pb = kmb.scan_params(list(dims), D_, M_, x, A, Bm, Cm, dl, h, dy, theta=th, grads=gr)
-        ms = _timed(lambda: kmb.check(lib.scannd_backward_async(C.byref(pb), B_, dx.data_ptr(), sp)), steps, warm,
-                    stream)
-        upd = B_ * P_ * D_ * M_
-        alg = upd * 20 + B_ * P_ * D_ * 4 * 7
-        t = ms / steps / 1e3
-        line.update(metric="scanND backward state-updates/sec", value=upd * world / t, unit="state-updates/s",
-                    ms_per_step=ms / steps, config={"workload": "scannd_bwd_2d32x32_D64_M16_b8_rope (config 1)"},
-                    roofline={"bound": "hbm", "achieved": round(alg / t / 1e9, 1), "peak": peak, "unit": "GB/s",
-                              "frac": round(alg / t / 1e9 / peak, 4), "peak_source": peak_src},
-                    gpu_launches=steps * 4)
-    elif args.workload == "convnd":
-        # dims {32,32} and {16,16,16}, D 256, K 3, batch 16, forward + backward
-        res = {}
-        for dims in ((32, 32), (16, 16, 16)):
-            D_, K_, B_ = 256, 3, 16
-            P_ = int(np.prod(dims)) if False else (dims[0] * dims[1] * (dims[2] if len(dims) > 2 else 1))
-            V_ = K_ ** len(dims)
-            xi, dy = rn(B_, P_, D_), rn(B_, P_, D_)
-            ker, bias = rn(V_, D_) / V_ ** 0.5, rn(D_) * 0.14
-            out, din = torch.empty(B_, P_, D_, device=dev), torch.empty(B_, P_, D_, device=dev)
-            dk, db = torch.empty(V_, D_, device=dev), torch.empty(D_, device=dev)
-            p = kmb.conv_params(list(dims), D_, K_, xi, ker, bias, out, dy, din, dk, db)
-            ms = _timed(lambda: kmb.check(lib.convnd_batched_async(C.byref(p), B_, 3, sp)), steps, warm, stream)
-            t = ms / steps / 1e3
-            alg = B_ * P_ * D_ * 20
-            res["x".join(map(str, dims))] = {"outputs_per_s": B_ * P_ * D_ * world / t, "ms_per_step": ms / steps,
-                                             "hbm_gbs": round(alg / t / 1e9, 1),
-                                             "frac": round(alg / t / 1e9 / peak, 4)}
-        line.update(metric="convND fwd+bwd outputs/sec (config 2, 2D and 3D)",
-                    value=res["32x32"]["outputs_per_s"], unit="outputs/s", ms_per_step=res["32x32"]["ms_per_step"],
-                    config={"workload": "convnd_D256_K3_b16 (config 2)", "per_shape": res}, gpu_launches=None)
-    elif args.workload == "block":
-        # Mamba-3 block, dim 512, N 64, R 2, 2D 64x64, batch 32, forward + backward (fp32)
-        dims, dim, N_, R_, B_ = (64, 64), 512, 64, 2, 32
-        L_ = 4096
-        from oracle import pyoracle as po  # parameter init only (seeded numpy), not a compute path
-        params = po.gen_block_params(dim, N_, R_, seed=42)
-        W = {k: torch.from_numpy(v).to(dev) for k, v in params.items()}
-        cfg = kmb.block_config(list(dims), dim, N_, R_, bf16=args.bf16)
-        w = kmb.KMBlockWeights(**{k: W[k].data_ptr() for k in kmb.BLOCK_FIELDS})
-        G = {k: torch.zeros_like(v) for k, v in W.items()}
-        gw = kmb.KMBlockGrads(**{k: G[k].data_ptr() for k in kmb.BLOCK_FIELDS})
-        act = torch.empty(lib.kmb_block_activation_floats(C.byref(cfg), B_), device=dev)
-        x, dout = rn(B_, L_, dim), rn(B_, L_, dim)
-        if args.bf16:
-            x, dout = x.to(torch.bfloat16), dout.to(torch.bfloat16)
-        out, dx = torch.empty_like(x), torch.empty_like(x)
-
-        def step():
-            kmb.check(lib.kmb_block_forward(C.byref(cfg), C.byref(w), x.data_ptr(), out.data_ptr(), B_,
-                                            act.data_ptr(), sp))
-            kmb.check(lib.kmb_block_backward(C.byref(cfg), C.byref(w), x.data_ptr(), dout.data_ptr(), dx.data_ptr(),
-                                             C.byref(gw), B_, act.data_ptr(), sp))
-        ms = _timed(step, steps, warm, stream)
-        t = ms / steps / 1e3
-        line.update(metric="Mamba-3 block fwd+bwd tokens/sec (config 3)", value=B_ * L_ * world / t,
-                    unit="tokens/s", ms_per_step=ms / steps,
-                    config={"workload": "block_dim512_N64_R2_2d64x64_b32 (config 3, "
-                                        + ("bf16 storage, fp32 state)" if args.bf16 else "fp32 storage)")},
-                    dtype="bf16 storage / f32 state" if args.bf16 else "f32",
-                    scan_updates_per_s=B_ * L_ * N_ * R_ * world / t)
-    else:
-        # 12-layer model, dim 512, N 64, R 4, 3D {16,32,32}, batch 64, vocab 256, AdamW
-        dims, V_, dim, N_, R_, nl, B_ = (16, 32, 32), 256, 512, 64, 4, 12, 64
-        B_ = int(os.environ.get("KMB_BENCH_MODEL_BATCH", B_))
-        cfgm = kmb.model_config(list(dims), V_, dim, N_, R_, nl)
-        m = lib.kmamba_create(C.byref(cfgm))
-        if not m:
-            raise RuntimeError(kmb.last_error())
-        lib.kmamba_init(m, 42)
-        opt = kmb.MBOptimConfig()
-        lib.kmamba_optim_config_set_defaults(C.byref(opt))
-        lib.kmamba_enable_training(m, C.byref(opt), 1e-3, 0.01)
-        L_ = 16384
-        tok = torch.randint(0, V_, (B_, L_ + 1), generator=g, device=dev, dtype=torch.int32)
-        losses = []
-
-        def step():
-            # NaN is a legitimate value here (the recurrence overflows fp32 at this scale, as the
-            # reference's does); an error leaves a message in kmb_last_error()
-            loss = lib.kmb_model_forward_backward(m, tok.data_ptr(), B_, sp)
-            if loss != loss and kmb.last_error():
-                raise RuntimeError(kmb.last_error())
-            kmb.check(lib.kmb_model_optimizer_step(m, sp))
-            losses.append(loss if loss == loss else None)
-        steps = max(2, min(steps, 3))
-        ms = _timed(step, steps, 2, stream)
-        t = ms / steps / 1e3
-        line.update(metric="k-mamba train step tokens/sec (config 4)", value=B_ * L_ * world / t, unit="tokens/s",
-                    ms_per_step=ms / steps, steps=steps, warmup=2,
-                    config={"workload": f"model_12x512_N64_R4_3d16x32x32_b{B_}_vocab256 (config 4)"},
-                    loss_first_last=[losses[0], losses[-1]])
-        lib.kmamba_free(m)
+    names = OTHER if args.workload == "all" else (args.workload,)
+    fns = {"scan_fwd_c0": wl_scan_fwd_small, "scan_fwd_c1": wl_scan_fwd_small, "scan_bwd": wl_scan_bwd,
+           "scan_bwd_c1": wl_scan_bwd, "convnd2d": wl_convnd, "convnd3d": wl_convnd, "block": wl_block,
+           "block_bf16": wl_block, "model": wl_model}
+    for name in names:
+        g = torch.Generator(device=dev)
+        g.manual_seed(7 + rank)
+        line = {"n_gpus": world, "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions), on device"}
+        line.update(fns[name](args, dev, stream, lib, kmb, g, name, peak, peak_src, rank, world))
+        if world > 1:
+            t = torch.tensor([line["ms_per_step"]], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            line["ms_per_step"] = float(t.item())
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        torch.cuda.empty_cache()
     if world > 1:
-        t = torch.tensor([line["ms_per_step"]], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        line["ms_per_step"] = float(t.item())
         dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
