@@ -74,6 +74,8 @@ def parse():
                              "convnd3d", "block", "block_bf16", "model", "all"],
                     help="scan_fwd = the headline line; the others measure the other BASELINE configs "
                          "(all = every other one, one line each)")
+    ap.add_argument("--chunks", type=int, default=4, help="N > 1: item chunks of the scan / gather overlap")
+    ap.add_argument("--sm-reserve", type=int, default=8, help="N > 1: SMs the scan leaves to the NCCL kernels")
     ap.add_argument("--exp2", type=int, default=0,
                     help="exponential of the 2D forward: 0 default, 1 opt-in fast ex2.approx")
     a = ap.parse_args()
@@ -252,11 +254,44 @@ def main():
     p = kmb.scan_params(list(DIMS), D, M, t["x"], t["A"], t["B"], t["C"], t["delta"], t["h"], t["y"])
     stream = torch.cuda.current_stream(dev)
     sp = C.c_void_p(stream.cuda_stream)
+    gather = None
+    if world > 1:
+        # The final output gather of the north star: every rank receives every rank's y over NCCL
+        # (the library's own communicator, include/kmamba_distributed.h).  The batch is scanned in
+        # item chunks and each chunk's y is gathered on a second stream while the next chunk is
+        # scanned; the scan's persistent grid leaves a few SMs free for the NCCL kernels.
+        from bissimamba_b200.distributed import Context
+        ctx = Context(world, rank)
+        lib.kmb_set_sm_reserve(args.sm_reserve)
+        nch = max(1, min(args.chunks, BATCH))
+        ipc = (BATCH + nch - 1) // nch
+        chunks = []
+        for c0 in range(0, BATCH, ipc):
+            c1 = min(BATCH, c0 + ipc)
+            sl = lambda k: t[k][c0:c1]
+            chunks.append((c1 - c0, kmb.scan_params(list(DIMS), D, M, sl("x"), t["A"], sl("B"), sl("C"), sl("delta"),
+                                                    sl("h"), sl("y"))))
+        yall = torch.empty((world,) + tuple(t["y"].shape), device=dev)   # [chunk-major per rank] gathered y
+        comm = torch.cuda.Stream(dev)
+        cp = C.c_void_p(comm.cuda_stream)
+        evs = [torch.cuda.Event() for _ in chunks]
+        gather = dict(ctx=ctx, chunks=len(chunks), bytes_per_rank=t["y"].numel() * 4)
 
     def step():
-        rc = lib.scannd_forward_async(C.byref(p), BATCH, sp)
-        if rc != 0:
-            raise RuntimeError(kmb.last_error())
+        if world == 1:
+            rc = lib.scannd_forward_async(C.byref(p), BATCH, sp)
+            if rc != 0:
+                raise RuntimeError(kmb.last_error())
+            return
+        off = 0
+        for i, (nb, pc) in enumerate(chunks):
+            kmb.check(lib.scannd_forward_async(C.byref(pc), nb, sp))
+            evs[i].record(stream)
+            comm.wait_event(evs[i])
+            cnt = nb * P * D
+            ctx.allgather(t["y"].data_ptr() + off * 4, yall.data_ptr() + off * world * 4, cnt, cp)
+            off += cnt
+        stream.wait_stream(comm)
 
     for _ in range(max(args.warmup, 3) if args.warmup >= 3 else 3):
         step()
@@ -297,6 +332,23 @@ def main():
                 # not from this run
                 "traffic": None,
                 "alg_bytes_per_launch": ALG_BYTES, "kernel": ("scan_fwd_strips" if len(DIMS) == 2 else "scan_fwd_tma") if path == 1 else "scan_fwd_generic"}
+
+    gather_info = None
+    if gather is not None:
+        # the gathers alone (no scan running), for the collective's share of the step
+        def gathers():
+            off = 0
+            for nb, _ in chunks:
+                cnt = nb * P * D
+                gather["ctx"].allgather(t["y"].data_ptr() + off * 4, yall.data_ptr() + off * world * 4, cnt, sp)
+                off += cnt
+        gathers()
+        torch.cuda.synchronize()
+        g_ms = max_over_ranks(_events(stream, gathers, 5) / 5)
+        gather_info = {"op": "ncclAllGather of y (every rank's outputs to every rank)", "chunks": gather["chunks"],
+                       "bytes_received_per_rank_per_step": (world - 1) * gather["bytes_per_rank"],
+                       "alone_ms": g_ms, "share_of_step_if_serial": round(g_ms / ms_per_step, 4),
+                       "sm_reserve": args.sm_reserve}
 
     # the opt-in ex2.approx exponential on the same inputs (reported beside the default path)
     variants = {}
@@ -360,13 +412,16 @@ def main():
                 "data": "synthetic (seeded, BASELINE config-0 distributions), generated on device",
                 "config": {"workload": WORKLOAD, "dims": list(DIMS), "D": D, "M": M, "batch_per_gpu": BATCH,
                            "global_batch": BATCH * world, "rope": False, "lambda": "default 0.5",
-                           "parallelism": f"dp{world} (batch shards, no collective)",
+                           "parallelism": (f"dp{world}: batch shards; every rank's y all-gathered to every rank "
+                                           f"over NCCL inside the step, overlapped by item chunks")
+                           if world > 1 else "dp1",
                            "l2": f"inputs {ALG_BYTES / 1e9:.1f} GB/GPU >> 126 MB L2, no flush"},
                 "hbm_gbs": round(achieved, 1),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "exp": "expf, reference operation order" if not args.exp2 else "ex2.approx (opt-in)",
                 "variants": variants,
-                "gpu_launches": args.steps, "clocks": clk,
+                "gpu_launches": args.steps * (1 if world == 1 else gather["chunks"]), "clocks": clk,
+                "collective": gather_info,
                 "kernel_ms": {"mean": statistics.mean(kern_ms), "min": min(kern_ms), "max": max(kern_ms)}}
         print(json.dumps(line), flush=True)
     if world > 1:

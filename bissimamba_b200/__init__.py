@@ -127,7 +127,12 @@ EXPORTS = [
     "km_wavefront_plan_matches_dims", "km_wavefront_plan_level_size", "km_wavefront_plan_level_offsets",
     "km_wavefront_plan_iter_forward", "km_wavefront_plan_iter_reverse",
     "kmb_last_error", "kmb_clear_error", "kmb_device_status", "kmb_last_forward_path", "kmb_set_force_generic",
-    "kmb_set_scan_exp2", "kmb_get_scan_exp2", "kmb_init_tensor",
+    "kmb_set_scan_exp2", "kmb_get_scan_exp2", "kmb_init_tensor", "kmb_set_sm_reserve",
+    "kmamba_distributed_split_batch", "kmamba_distributed_split_layers", "kmamba_distributed_init_nccl",
+    "kmamba_distributed_fini_nccl", "kmamba_allreduce_gradients_nccl", "kmamba_broadcast_params_nccl",
+    "kmb_dist_unique_id", "kmb_dist_init", "kmb_dist_exchange_id", "kmb_dist_world_size", "kmb_dist_rank",
+    "kmb_dist_allreduce_async", "kmb_dist_allgather_async", "kmb_dist_broadcast_async", "kmb_dist_scannd_backward",
+    "kmb_dist_convnd_backward", "kmb_dist_model_train_step",
     "kmb_blockscan_forward", "kmb_blockscan_set_strips", "kmb_blockscan_last_forward_path", "kmb_blockscan_set_backward_strips",
     "kmb_blockscan_last_backward_path", "kmb_blockscan_backward", "kmb_blockscan_backward_ex", "kmb_block_activation_floats",
     "kmb_block_forward", "kmb_block_backward", "kmb_block_set_tensor_cores", "kmb_block_last_projection_path", "kmb_block_last_dx_path", "cuda_block_forward", "cuda_block_backward",
@@ -185,6 +190,30 @@ def lib():
         L.kmamba_init.argtypes = [C.c_void_p, C.c_uint32]
         L.kmb_init_tensor.argtypes = [C.c_void_p, C.c_uint32, C.c_char_p, C.c_void_p, C.c_long]
         L.kmb_init_tensor.restype = C.c_long
+        vp, sz = C.c_void_p, C.c_size_t
+        L.kmamba_distributed_split_batch.argtypes = [vp, sz, sz]
+        L.kmamba_distributed_split_batch.restype = None
+        L.kmamba_distributed_split_layers.argtypes = [vp, sz, sz]
+        L.kmamba_distributed_split_layers.restype = None
+        L.kmamba_distributed_init_nccl.argtypes = [C.c_int, C.c_int]
+        L.kmamba_distributed_init_nccl.restype = vp
+        L.kmamba_distributed_fini_nccl.argtypes = [vp]
+        L.kmamba_distributed_fini_nccl.restype = None
+        L.kmamba_allreduce_gradients_nccl.argtypes = [vp, vp, sz]
+        L.kmamba_broadcast_params_nccl.argtypes = [vp, vp, sz]
+        L.kmb_dist_unique_id.argtypes = [vp]
+        L.kmb_dist_init.argtypes = [vp, C.c_int, C.c_int, C.c_int]
+        L.kmb_dist_init.restype = vp
+        L.kmb_dist_exchange_id.argtypes = [vp, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        L.kmb_dist_world_size.argtypes = [vp]
+        L.kmb_dist_rank.argtypes = [vp]
+        L.kmb_dist_allreduce_async.argtypes = [vp, vp, sz, C.c_float, vp]
+        L.kmb_dist_allgather_async.argtypes = [vp, vp, vp, sz, vp]
+        L.kmb_dist_broadcast_async.argtypes = [vp, vp, sz, C.c_int, vp]
+        L.kmb_dist_scannd_backward.argtypes = [vp, vp, C.c_long, vp, C.c_int, vp]
+        L.kmb_dist_convnd_backward.argtypes = [vp, vp, C.c_long, vp]
+        L.kmb_dist_model_train_step.argtypes = [vp, vp, vp, sz, sz, vp]
+        L.kmb_dist_model_train_step.restype = C.c_float
         L.kmamba_enable_training.argtypes = [C.c_void_p, C.POINTER(MBOptimConfig), C.c_float, C.c_float]
         L.kmamba_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
         L.kmamba_train_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
@@ -226,6 +255,8 @@ def lib():
         L.kmb_set_force_generic.restype = None
         L.kmb_set_scan_exp2.argtypes = [C.c_int]
         L.kmb_set_scan_exp2.restype = None
+        L.kmb_set_sm_reserve.argtypes = [C.c_int]
+        L.kmb_set_sm_reserve.restype = None
         L.km_wavefront_plan_create.argtypes = [_l, C.c_long, C.c_long]
         L.km_wavefront_plan_create.restype = C.c_void_p
         L.km_wavefront_plan_free.argtypes = [C.c_void_p]

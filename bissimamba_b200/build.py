@@ -15,11 +15,32 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "libkmamba_b200.so")
 SOURCES = ["capi.cu", "scannd_generic.cu", "scannd_tma.cu", "scannd_strips.cu", "scannd_bwd.cu", "scannd_bwd_strips.cu", "convnd.cu",
-           "blockscan.cu", "block.cu", "proj_tc.cu", "model.cu", "wavefront.cpp"]
+           "blockscan.cu", "block.cu", "proj_tc.cu", "model.cu", "distributed.cu", "wavefront.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr", "-ccbin", "/usr/bin/g++"]
-LIBS = ["-lcublas"]
+
+
+def _nccl_dir():
+    """NCCL of the image: the copy PyTorch loads (nvidia-nccl wheel), so one
+    process never holds two NCCL versions; else the system one."""
+    try:
+        import nvidia.nccl
+        d = list(nvidia.nccl.__path__)[0]
+        if os.path.exists(os.path.join(d, "include", "nccl.h")):
+            return d
+    except ImportError:
+        pass
+    return None
+
+
+_NCCL = _nccl_dir()
+if _NCCL:
+    FLAGS += ["-I" + os.path.join(_NCCL, "include")]
+    LIBS = ["-lcublas", "-L" + os.path.join(_NCCL, "lib"), "-l:libnccl.so.2",
+            "-Xlinker", "-rpath=" + os.path.join(_NCCL, "lib")]
+else:
+    LIBS = ["-lcublas", "-lnccl"]
 
 
 def _headers():

@@ -63,7 +63,8 @@ thread_local int tl_conv_status = 0;
 thread_local int tl_fast_path = -1;   // 1 = last forward used the TMA kernel, 0 = generic
 thread_local int tl_bwd_path = -1;    // 2 = strips, 1 = wave, 0 = generic
 int g_force_generic = -1;             // KMB_FORCE_GENERIC=1 disables the TMA path (tests)
-int g_scan_ex2 = 0;                   // 1: the 2D strip forward evaluates alpha with ex2.approx
+int g_scan_ex2 = 0;
+int g_sm_reserve = 0;                 // SMs the persistent grids leave free for concurrent kernels                   // 1: the 2D strip forward evaluates alpha with ex2.approx
 
 int fail(const char* msg) {
     tl_err = msg;
@@ -123,6 +124,7 @@ namespace {
 
 namespace kmb {
 void* workspace(int slot, size_t bytes) { return ws_get(slot, bytes); }
+int persistent_sms(int sms) { return sms - g_sm_reserve > 1 ? sms - g_sm_reserve : 1; }
 int set_error(const char* msg) { return fail(msg); }
 void clear_error() { tl_err.clear(); }
 int set_cuda_error(const char* where, cudaError_t e) { return fail_cuda(where, e); }
@@ -265,6 +267,7 @@ int kmb_last_backward_path(void) { return tl_bwd_path; }
 void kmb_set_force_generic(int on) { g_force_generic = on ? 1 : 0; }
 void kmb_set_scan_exp2(int on) { g_scan_ex2 = on ? 1 : 0; }
 int kmb_get_scan_exp2(void) { return g_scan_ex2; }
+void kmb_set_sm_reserve(int n) { g_sm_reserve = n > 0 ? n : 0; }
 
 int scannd_validate(const ScanNDParams* p) {
     if (!p || !p->dims) return 0;

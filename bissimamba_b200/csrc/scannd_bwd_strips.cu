@@ -46,6 +46,7 @@
 #include <type_traits>
 
 namespace kmb {
+int persistent_sms(int sms);  // SMs a persistent grid may fill (capi.cu)
 
 constexpr int BS_K = 4;    // handoff slots per strip boundary
 
@@ -549,6 +550,7 @@ static cudaError_t bs_launch(const BwdStripDesc& f, cudaStream_t st) {
     int dev, sms, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sms = persistent_sms(sms);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, threads, smem);
     if (per < 1) return cudaErrorNotSupported;
     long long grid = (long long)sms * per;

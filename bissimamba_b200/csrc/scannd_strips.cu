@@ -30,6 +30,7 @@
 #include <type_traits>
 
 namespace kmb {
+int persistent_sms(int sms);  // SMs a persistent grid may fill (capi.cu)
 
 constexpr int SW_NSS_MAX = 4;  // stages per strip (fewer when shared memory is short)
 constexpr int SW_K = 4;        // handoff slots per strip boundary
@@ -439,6 +440,7 @@ static cudaError_t strips_inst(const StripDesc& f, const CUtensorMap* maps, int 
     int dev, sms, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sms = persistent_sms(sms);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, threads, smem);
     if (per < 1) return cudaErrorNotSupported;
     long long grid = (long long)sms * per;

@@ -35,6 +35,7 @@
 #include "kmb_sync.cuh"
 
 namespace kmb {
+int persistent_sms(int sms);  // SMs a persistent grid may fill (capi.cu)
 
 constexpr int TG = 8;      // points per stage
 constexpr int TNS = 6;     // stages in the ring
@@ -413,6 +414,7 @@ static cudaError_t launch_inst(const FastDesc& f, const CUtensorMap* maps, cudaS
     int dev, sms, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sms = persistent_sms(sms);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k, TTHREADS, smem);
     if (per < 1) return cudaErrorNotSupported;
     long long grid = (long long)sms * per;

@@ -1,39 +1,44 @@
-"""Batch / channel sharding across the GPUs of one node (rebuild of the
-reference's kmamba_distributed, src/kmamba_distributed.c and
-cuda/kmamba_distributed.cu, which were never called and broadcast no NCCL id).
+"""Python view of the library's multi-GPU layer (include/kmamba_distributed.h,
+csrc/distributed.cu): one process per GPU over NCCL, rebuilt from the
+reference's src/kmamba_distributed.c and cuda/kmamba_distributed.cu.
 
-One process per GPU over ``torch.distributed`` (NCCL on GPUs, gloo on CPU for
-tests).  The scans and convnd have no cross-rank exchange in the forward: each
-rank owns whole batch items (or whole RoPE channel pairs).  The only
-collectives are the parameter broadcast at start-up and the all-reduce of the
-gradient arena after the backward.  Each rank scales its gradients by its share
-of the batch before the sum, so the update equals the full-batch update even
-when the batch does not divide evenly.
-"""
+Everything here calls the C ABI; the collectives, the id exchange and the
+batch-split rule are native code.  Batch items are independent through the
+scans and convnd, so the forward has no exchange but the optional final output
+gather; the backward sums the weight gradients (Scan-A dA / dtheta, convnd
+dkernel / dbias, the model's gradient arena) over the ranks."""
 from __future__ import annotations
 
 import ctypes as C
 
-import torch
-import torch.distributed as dist
+from . import lib as _lib
+
+
+class DistConfig(C.Structure):
+    """reference include/kmamba_distributed.h:17-33"""
+    _fields_ = [("world_size", C.c_int), ("rank", C.c_int), ("local_rank", C.c_int),
+                ("layer_start", C.c_size_t), ("layer_end", C.c_size_t),
+                ("batch_start", C.c_size_t), ("batch_end", C.c_size_t),
+                ("use_nccl", C.c_int), ("use_p2p", C.c_int)]
 
 
 def split_batch(batch: int, world: int, rank: int) -> tuple[int, int]:
-    """[start, end) of this rank's batch items; earlier ranks take the extra
-    items (reference src/kmamba_distributed.c:120-139)."""
+    """[start, end) of this rank's items (reference src/kmamba_distributed.c:120-139,
+    kmamba_distributed_split_batch): earlier ranks take the extra items."""
     if world <= 0:
         raise ValueError("world must be > 0")
-    per, rem = divmod(batch, world)
-    if rank < rem:
-        start = rank * (per + 1)
-        return start, start + per + 1
-    start = rank * per + rem
-    return start, start + per
+    c = DistConfig(rank=rank)
+    _lib().kmamba_distributed_split_batch(C.byref(c), batch, world)
+    return c.batch_start, c.batch_end
 
 
 def split_layers(n_layers: int, world: int, rank: int) -> tuple[int, int]:
-    """Same rule over layers (reference src/kmamba_distributed.c:141-160)."""
-    return split_batch(n_layers, world, rank)
+    """The same rule over layers (reference src/kmamba_distributed.c:141-160)."""
+    if world <= 0:
+        raise ValueError("world must be > 0")
+    c = DistConfig(rank=rank)
+    _lib().kmamba_distributed_split_layers(C.byref(c), n_layers, world)
+    return c.layer_start, c.layer_end
 
 
 def split_channel_pairs(D: int, world: int, rank: int) -> tuple[int, int]:
@@ -44,65 +49,65 @@ def split_channel_pairs(D: int, world: int, rank: int) -> tuple[int, int]:
     return min(D, 2 * a), min(D, 2 * b)
 
 
-def scale_and_allreduce_(t: torch.Tensor, weight: float, group=None) -> torch.Tensor:
-    """t <- sum over ranks of weight_r * t_r (in place)."""
-    t.mul_(weight)
-    if dist.is_initialized() and dist.get_world_size(group) > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
-    return t
+def exchange_id(id128: bytes | None, world: int, rank: int, addr: str = "127.0.0.1", port: int = 0) -> bytes:
+    """kmb_dist_exchange_id: rank 0 sends its 128-byte id to the other ranks over TCP."""
+    buf = C.create_string_buffer(id128 if id128 is not None else b"", 128)
+    if _lib().kmb_dist_exchange_id(buf, world, rank, addr.encode(), port) != 0:
+        raise RuntimeError(_lib().kmb_last_error().decode())
+    return buf.raw
 
 
-class DataParallel:
-    """Data-parallel driver for anything that exposes a parameter buffer, a
-    gradient buffer and a local forward+backward:
+class Context:
+    """A KMambaDistributedContext: NCCL communicator + stream of this rank."""
 
-    * ``params`` / ``grads``: 1-D float32 tensors (views of the model arenas);
-    * ``forward_backward(local_batch) -> local mean loss``;
-    * ``step()``: the optimizer update on the reduced gradients.
-    """
+    def __init__(self, world: int, rank: int, device: int = -1, id128: bytes | None = None):
+        L = _lib()
+        if id128 is None:
+            # the reference's entry: rank 0 makes the id and sends it over TCP (MASTER_ADDR / MASTER_PORT + 1)
+            self.h = L.kmamba_distributed_init_nccl(world, rank)
+        else:
+            self.h = L.kmb_dist_init(C.create_string_buffer(id128, 128), world, rank, device)
+        if not self.h:
+            raise RuntimeError("distributed init failed: " + L.kmb_last_error().decode())
+        self.world, self.rank = world, rank
 
-    def __init__(self, params: torch.Tensor, grads: torch.Tensor, forward_backward, step, group=None):
-        self.params, self.grads = params, grads
-        self.forward_backward, self.step = forward_backward, step
-        self.group = group
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        if _lib().kmb_dist_unique_id(buf) != 0:
+            raise RuntimeError(_lib().kmb_last_error().decode())
+        return buf.raw
 
-    def broadcast_params(self, src: int = 0):
-        if self.world > 1:
-            dist.broadcast(self.params, src=src, group=self.group)
+    def _chk(self, rc, what):
+        if rc != 0:
+            raise RuntimeError(f"{what}: {_lib().kmb_last_error().decode()}")
 
-    def train_step(self, global_batch, global_size: int) -> float:
-        """global_batch: indexable by item; every rank passes the same global
-        batch and processes its own slice.  Returns the global mean loss."""
-        a, b = split_batch(global_size, self.world, self.rank)
-        share = (b - a) / global_size
-        loss = self.forward_backward(global_batch[a:b]) if b > a else 0.0
-        scale_and_allreduce_(self.grads, share, self.group)
-        lt = torch.tensor([loss * share], dtype=torch.float64, device=self.grads.device)
-        if self.world > 1:
-            dist.all_reduce(lt, op=dist.ReduceOp.SUM, group=self.group)
-        self.step()
-        return float(lt.item())
+    def allreduce(self, ptr: int, count: int, scale: float = 1.0, stream=None):
+        self._chk(_lib().kmb_dist_allreduce_async(self.h, ptr, count, scale, stream), "allreduce")
 
+    def allgather(self, send: int, recv: int, count: int, stream=None):
+        self._chk(_lib().kmb_dist_allgather_async(self.h, send, recv, count, stream), "allgather")
 
-def model_data_parallel(kmb, model, device, group=None) -> DataParallel:
-    """DataParallel over a library KMamba handle (GPU)."""
-    n = C.c_size_t()
-    gptr = kmb.lib().kmb_model_grad_arena(model, C.byref(n))
-    pptr = kmb.lib().kmb_model_param_arena(model, C.byref(n))
-    grads = torch.as_tensor(kmb.DeviceArray(gptr, n.value), device=device)
-    params = torch.as_tensor(kmb.DeviceArray(pptr, n.value), device=device)
-    stream = torch.cuda.current_stream(device)
+    def broadcast(self, ptr: int, count: int, root: int = 0, stream=None):
+        self._chk(_lib().kmb_dist_broadcast_async(self.h, ptr, count, root, stream), "broadcast")
 
-    def fb(tokens):
-        t = tokens.to(device=device, dtype=torch.int32).contiguous()
-        loss = kmb.lib().kmb_model_forward_backward(model, t.data_ptr(), t.shape[0], C.c_void_p(stream.cuda_stream))
-        if loss != loss:
-            raise RuntimeError(kmb.last_error())
-        return loss
+    def scannd_backward(self, params, local_batch: int, dx: int | None, overwrite: int = 0, stream=None):
+        self._chk(_lib().kmb_dist_scannd_backward(self.h, C.byref(params), local_batch, dx, overwrite, stream),
+                  "scannd backward")
 
-    def step():
-        kmb.check(kmb.lib().kmb_model_optimizer_step(model, C.c_void_p(stream.cuda_stream)), "optimizer step")
+    def convnd_backward(self, params, local_batch: int, stream=None):
+        self._chk(_lib().kmb_dist_convnd_backward(self.h, C.byref(params), local_batch, stream), "convnd backward")
 
-    return DataParallel(params, grads, fb, step, group)
+    def model_train_step(self, model, d_tokens: int, local_batch: int, global_batch: int, stream=None) -> float:
+        return _lib().kmb_dist_model_train_step(self.h, model, d_tokens, local_batch, global_batch, stream)
+
+    def close(self):
+        if self.h:
+            _lib().kmamba_distributed_fini_nccl(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -28,6 +28,11 @@ void kmb_set_force_generic(int on);
  * one ex2.approx of delta*(A log2 e) and a re-associated trapezoid term; it is
  * a few ulp per update from expf, which the recurrence compounds. */
 void kmb_set_scan_exp2(int on);
+/* Persistent kernels (the Scan-A strip and TMA kernels) size their grid to the
+ * SM count minus n (process-wide, default 0), so that a communication kernel
+ * enqueued on another stream (an NCCL gather overlapping the scan) finds SMs
+ * free instead of waiting for the scan to end. */
+void kmb_set_sm_reserve(int n);
 int kmb_get_scan_exp2(void);
 #ifdef __cplusplus
 }
