@@ -75,6 +75,8 @@ def parse():
                     help="scan_fwd = the headline line; the others measure the other BASELINE configs "
                          "(all = every other one, one line each)")
     ap.add_argument("--chunks", type=int, default=4, help="N > 1: item chunks of the scan / gather overlap")
+    ap.add_argument("--gather-mode", default="overlap", choices=["overlap", "after"],
+                    help="N > 1: gather each chunk's y while the next is scanned, or all of y after the scan")
     ap.add_argument("--sm-reserve", type=int, default=8, help="N > 1: SMs the scan leaves to the NCCL kernels")
     ap.add_argument("--exp2", type=int, default=0,
                     help="exponential of the 2D forward: 0 default, 1 opt-in fast ex2.approx")
@@ -261,8 +263,10 @@ def main():
         # item chunks and each chunk's y is gathered on a second stream while the next chunk is
         # scanned; the scan's persistent grid leaves a few SMs free for the NCCL kernels.
         from bissimamba_b200.distributed import Context
+        if args.sm_reserve > 0:
+            os.environ.setdefault("KMB_NCCL_MAX_CTAS", str(args.sm_reserve))   # NCCL fits in the SMs left free
         ctx = Context(world, rank)
-        lib.kmb_set_sm_reserve(args.sm_reserve)
+        lib.kmb_set_sm_reserve(args.sm_reserve if args.gather_mode == "overlap" else 0)
         nch = max(1, min(args.chunks, BATCH))
         ipc = (BATCH + nch - 1) // nch
         chunks = []
@@ -282,6 +286,10 @@ def main():
             rc = lib.scannd_forward_async(C.byref(p), BATCH, sp)
             if rc != 0:
                 raise RuntimeError(kmb.last_error())
+            return
+        if args.gather_mode == "after":
+            kmb.check(lib.scannd_forward_async(C.byref(p), BATCH, sp))
+            ctx.allgather(t["y"].data_ptr(), yall.data_ptr(), BATCH * P * D, sp)
             return
         off = 0
         for i, (nb, pc) in enumerate(chunks):
@@ -340,15 +348,16 @@ def main():
             off = 0
             for nb, _ in chunks:
                 cnt = nb * P * D
-                gather["ctx"].allgather(t["y"].data_ptr() + off * 4, yall.data_ptr() + off * world * 4, cnt, sp)
+                gather["ctx"].allgather(t["y"].data_ptr() + off * 4, yall.data_ptr() + off * world * 4, cnt, cp)
                 off += cnt
         gathers()
         torch.cuda.synchronize()
-        g_ms = max_over_ranks(_events(stream, gathers, 5) / 5)
+        g_ms = max_over_ranks(_events(comm, gathers, 5) / 5)
         gather_info = {"op": "ncclAllGather of y (every rank's outputs to every rank)", "chunks": gather["chunks"],
                        "bytes_received_per_rank_per_step": (world - 1) * gather["bytes_per_rank"],
                        "alone_ms": g_ms, "share_of_step_if_serial": round(g_ms / ms_per_step, 4),
-                       "sm_reserve": args.sm_reserve}
+                       "sm_reserve": args.sm_reserve, "mode": args.gather_mode,
+                       "nccl_max_ctas": os.environ.get("KMB_NCCL_MAX_CTAS")}
 
     # the opt-in ex2.approx exponential on the same inputs (reported beside the default path)
     variants = {}

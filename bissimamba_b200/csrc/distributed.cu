@@ -186,7 +186,17 @@ KMambaDistributedContext* kmb_dist_init(const void* id128, int world_size, int r
     if (world_size > 1) {
         ncclUniqueId id;
         memcpy(&id, id128, sizeof id);
-        ncclResult_t r = ncclCommInitRank(&c->comm, world_size, id, rank);
+        // KMB_NCCL_MAX_CTAS caps the CTAs of every NCCL kernel of this communicator, so that a
+        // collective overlapping a persistent scan (kmb_set_sm_reserve) fits in the SMs left free
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        if (const char* mc = getenv("KMB_NCCL_MAX_CTAS")) {
+            const int v = atoi(mc);
+            if (v > 0) {
+                cfg.maxCTAs = v;
+                cfg.minCTAs = 1;
+            }
+        }
+        ncclResult_t r = ncclCommInitRankConfig(&c->comm, world_size, id, rank, &cfg);
         if (r != ncclSuccess) {
             nccl_fail("ncclCommInitRank", r);
             cudaStreamDestroy(c->stream);
@@ -241,6 +251,20 @@ int kmb_dist_allgather_async(KMambaDistributedContext* ctx, const float* send, f
         if (send == recv) return 0;
         cudaError_t e = cudaMemcpyAsync(recv, send, count * sizeof(float), cudaMemcpyDeviceToDevice, st);
         return e == cudaSuccess ? 0 : kmb::set_cuda_error("allgather copy", e);
+    }
+    if (getenv("KMB_DIST_CHECK")) {
+        // every rank must pass the same count (a mismatch would hang NCCL): compare max and min first
+        double* chk = (double*)kmb::workspace(3, 256);
+        if (!chk) return kmb::set_error("kmb_dist_allgather_async: workspace allocation failed");
+        const double v[2] = {(double)count, -(double)count};
+        double got[2];
+        cudaMemcpyAsync(chk, v, sizeof v, cudaMemcpyHostToDevice, st);
+        ncclResult_t r = ncclAllReduce(chk, chk, 2, ncclDouble, ncclMax, ctx->comm, st);
+        if (r != ncclSuccess) return nccl_fail("ncclAllReduce (count check)", r);
+        cudaMemcpyAsync(got, chk, sizeof got, cudaMemcpyDeviceToHost, st);
+        cudaStreamSynchronize(st);
+        if (got[0] != (double)count || -got[1] != (double)count)
+            return kmb::set_error("kmb_dist_allgather_async: ranks passed different counts");
     }
     ncclResult_t r = ncclAllGather(send, recv, count, ncclFloat, ctx->comm, st);
     return r == ncclSuccess ? 0 : nccl_fail("ncclAllGather", r);

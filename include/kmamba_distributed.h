@@ -71,7 +71,10 @@ int kmb_dist_world_size(const KMambaDistributedContext *ctx);
 int kmb_dist_rank(const KMambaDistributedContext *ctx);
 /* Asynchronous collectives on `stream` (NULL = the context's own stream).
  * allreduce: buf <- scale * sum over ranks (scale applied after the sum).
- * allgather: recv[r * count .. (r + 1) * count) <- rank r's send[0 .. count). */
+ * allgather: recv[r * count .. (r + 1) * count) <- rank r's send[0 .. count);
+ * every rank must pass the same count (pad uneven shards), as NCCL requires;
+ * with KMB_DIST_CHECK set in the environment the counts are compared first and
+ * a mismatch returns -1 instead of hanging. */
 int kmb_dist_allreduce_async(KMambaDistributedContext *ctx, float *buf, size_t count, float scale, void *stream);
 int kmb_dist_allgather_async(KMambaDistributedContext *ctx, const float *send, float *recv, size_t count,
                              void *stream);

@@ -51,6 +51,7 @@ def main():
     tok = np.random.default_rng(0).integers(0, V, (gb, 33)).astype(np.int32)
     a, b = split_batch(gb, world, rank)
     dtok = torch.from_numpy(np.ascontiguousarray(tok[a:b])).to(dev)
+    torch.cuda.synchronize()
     losses = [ctx.model_train_step(m, dtok.data_ptr(), b - a, gb) for _ in range(2)]
     params = arena(m, "p", dev).clone()
     ref = make(dims, V, dim, N, R, nl, seed=42)
@@ -90,6 +91,7 @@ def main():
     sl = lambda t: t[a:b].contiguous()
     pl = kmb.scan_params([H, W], D, M, sl(full["x"]), full["A"], sl(full["B"]), sl(full["C"]), sl(full["delta"]),
                          sl(h), sl(full["dy"]), theta=full["theta"], grads=gl)
+    torch.cuda.synchronize()   # the context's stream does not order after torch's
     ctx.scannd_backward(pl, b - a, None, 0)
     torch.cuda.synchronize()
     for k in ("dA", "dtheta"):
@@ -97,15 +99,19 @@ def main():
         ok &= e < 1e-5
         print(f"[{rank}] scan {k} rel diff {e:.3g}", flush=True)
     ok &= torch.equal(gl["dB"], gref["dB"][a:b])
-    # ---- output gather: every rank's y, in rank order
-    cnt = (b - a) * P * D
-    yall = torch.empty(world * cnt, device=dev)
-    ctx.allgather(sl(y).data_ptr(), yall.data_ptr(), cnt)
+    # ---- output gather: every rank's y, in rank order (shards padded to the largest, as NCCL needs
+    # one count on every rank)
+    per = (B_ + world - 1) // world
+    cnt = per * P * D
+    ysend = torch.zeros(per, P, D, device=dev)
+    ysend[:b - a] = y[a:b]
+    yall = torch.empty(world, per, P, D, device=dev)
     torch.cuda.synchronize()
-    if B_ % world == 0:
-        ok &= torch.equal(yall.view(B_, P, D), y)
-    else:
-        ok &= torch.equal(yall[rank * cnt:(rank + 1) * cnt].view(b - a, P, D), y[a:b])
+    ctx.allgather(ysend.data_ptr(), yall.data_ptr(), cnt)
+    torch.cuda.synchronize()
+    for r in range(world):
+        ra, rb = split_batch(B_, world, r)
+        ok &= torch.equal(yall[r, :rb - ra], y[ra:rb])
     # ---- convnd backward, batch-sharded
     cdims, CD, K = [6, 7], 16, 3
     xi = torch.randn(B_, 42, CD, generator=g, device=dev)
@@ -117,6 +123,7 @@ def main():
     kmb.check(kmb.lib().convnd_batched_async(C.byref(cp), B_, 2, None))
     dk, db, din = torch.empty(9, CD, device=dev), torch.empty(CD, device=dev), torch.empty(b - a, 42, CD, device=dev)
     cl = kmb.conv_params(cdims, CD, K, sl(xi), ker, None, None, sl(cdy), din, dk, db)
+    torch.cuda.synchronize()
     ctx.convnd_backward(cl, b - a)
     torch.cuda.synchronize()
     e = ((dk - dk_ref).abs().max() / dk_ref.abs().max()).item()

@@ -1,5 +1,7 @@
-"""Multi-GPU (one process per GPU, NCCL): the data-parallel model step equals
-the single-GPU full-batch step; skipped with fewer than 2 GPUs."""
+"""Multi-GPU (one process per GPU, the library's NCCL layer): the data-parallel
+model step equals the single-GPU full-batch step, the batch-sharded Scan-A /
+convnd backward reductions equal the full-batch gradients, the output gather
+assembles every rank's y (tests/mp_model_dp.py); skipped with fewer than 2 GPUs."""
 import os
 import socket
 import subprocess
@@ -25,5 +27,6 @@ def test_data_parallel_model_two_gpus(cuda):
         pytest.skip("needs 2 GPUs")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(ROOT, "tests", "mp_model_dp.py")]
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=240,
+                       env=dict(os.environ, NCCL_NVLS_ENABLE="0", KMB_DIST_CHECK="1"))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
