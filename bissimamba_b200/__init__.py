@@ -133,6 +133,11 @@ EXPORTS = [
     "kmb_dist_unique_id", "kmb_dist_init", "kmb_dist_exchange_id", "kmb_dist_world_size", "kmb_dist_rank",
     "kmb_dist_allreduce_async", "kmb_dist_allgather_async", "kmb_dist_broadcast_async", "kmb_dist_scannd_backward",
     "kmb_dist_convnd_backward", "kmb_dist_model_train_step",
+    "kser_writer_create", "kser_writer_add_vocab", "kser_writer_add_tensor", "kser_writer_finalize", "kser_writer_free",
+    "kser_reader_open", "kser_reader_config", "kser_reader_is_valid", "kser_reader_load_vocab", "kser_reader_load_tensor",
+    "kser_reader_count_tensors", "kser_reader_get_tensor_info", "kser_reader_close", "kser_file_info", "kser_quantize",
+    "kser_dequantize", "kser_dtype_size", "kser_sha256", "kmamba_save_ser", "kmamba_load_ser", "kmb_load_ser_ex",
+    "kmamba_ser_info", "kmamba_save_checkpoint_ser", "kmamba_load_checkpoint_ser",
     "kmb_blockscan_forward", "kmb_blockscan_set_strips", "kmb_blockscan_last_forward_path", "kmb_blockscan_set_backward_strips",
     "kmb_blockscan_last_backward_path", "kmb_blockscan_backward", "kmb_blockscan_backward_ex", "kmb_block_activation_floats",
     "kmb_block_forward", "kmb_block_backward", "kmb_block_set_tensor_cores", "kmb_block_last_projection_path", "kmb_block_last_dx_path", "cuda_block_forward", "cuda_block_backward",
@@ -214,6 +219,31 @@ def lib():
         L.kmb_dist_convnd_backward.argtypes = [vp, vp, C.c_long, vp]
         L.kmb_dist_model_train_step.argtypes = [vp, vp, vp, sz, sz, vp]
         L.kmb_dist_model_train_step.restype = C.c_float
+        for fn in ("kser_writer_create", "kser_reader_open", "kser_reader_config", "kser_reader_load_tensor",
+                   "kser_reader_get_tensor_info", "kmamba_load_ser", "kmb_load_ser_ex"):
+            getattr(L, fn).restype = vp
+        L.kser_writer_create.argtypes = [C.c_char_p, vp]
+        L.kser_writer_add_vocab.argtypes = [vp, C.c_uint32, C.c_char_p, C.c_uint16]
+        L.kser_writer_add_tensor.argtypes = [vp, C.c_char_p, vp, vp, C.c_int, C.c_int]
+        L.kser_writer_finalize.argtypes = [vp]
+        L.kser_writer_free.argtypes = [vp]
+        L.kser_writer_free.restype = None
+        L.kser_reader_open.argtypes = [C.c_char_p]
+        L.kser_reader_config.argtypes = [vp]
+        L.kser_reader_is_valid.argtypes = [vp]
+        L.kser_reader_load_tensor.argtypes = [vp, C.c_char_p]
+        L.kser_reader_count_tensors.argtypes = [vp]
+        L.kser_reader_count_tensors.restype = C.c_uint64
+        L.kser_reader_get_tensor_info.argtypes = [vp, C.c_uint64]
+        L.kser_reader_close.argtypes = [vp]
+        L.kser_reader_close.restype = None
+        L.kser_quantize.argtypes = [vp, vp, C.c_uint64, C.c_int]
+        L.kser_dequantize.argtypes = [vp, vp, C.c_uint64, C.c_int]
+        L.kser_sha256.argtypes = [vp, sz, vp]
+        L.kser_sha256.restype = None
+        L.kmamba_save_ser.argtypes = [vp, C.c_char_p, C.c_int]
+        L.kmamba_load_ser.argtypes = [C.c_char_p, C.c_int]
+        L.kmb_load_ser_ex.argtypes = [C.c_char_p, C.c_int, vp]
         L.kmamba_enable_training.argtypes = [C.c_void_p, C.POINTER(MBOptimConfig), C.c_float, C.c_float]
         L.kmamba_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
         L.kmamba_train_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]

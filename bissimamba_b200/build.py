@@ -15,7 +15,7 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "libkmamba_b200.so")
 SOURCES = ["capi.cu", "scannd_generic.cu", "scannd_tma.cu", "scannd_strips.cu", "scannd_bwd.cu", "scannd_bwd_strips.cu", "convnd.cu",
-           "blockscan.cu", "block.cu", "proj_tc.cu", "model.cu", "distributed.cu", "wavefront.cpp"]
+           "blockscan.cu", "block.cu", "proj_tc.cu", "model.cu", "distributed.cu", "kser.cpp", "wavefront.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr", "-ccbin", "/usr/bin/g++"]

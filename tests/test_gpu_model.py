@@ -97,3 +97,51 @@ def test_train_batch_reduces_loss(kmb, cuda):
     assert losses[-1] < losses[0], losses
     assert kmb.lib().kmamba_step_count(m) == 20
     kmb.lib().kmamba_free(m)
+
+
+def test_ser_save_load_round_trip(kmb, cuda, tmp_path):
+    """kmamba_save_ser writes the reference's .ser layout (embedding, per-layer
+    W_in .. theta, head) byte for byte as the reference's own kser writer does
+    for the same tensors; kmamba_load_ser / kmb_load_ser_ex bring back a model
+    whose logits equal the saved model's bit for bit (bf16 storage: to bf16)."""
+    import sys
+    sys.path.insert(0, __import__("os").path.dirname(__file__))
+    from test_kser import FP32, BF16, KSerConfig, _bind, _write
+    if not po.have_ref():
+        pytest.skip("reference build unavailable")
+    dims, V, dim, N, R, nl = [4, 8], 16, 16, 8, 2, 2
+    params = po.gen_model_params(V, dim, N, R, nl, seed=11)
+    m = _model(kmb, dims, V, dim, N, R, nl, params)
+    L = int(np.prod(dims))
+    tok = np.random.default_rng(4).integers(0, V, L).astype(np.uint32)
+    ref_logits = np.zeros((L, V), np.float32)
+    assert kmb.lib().kmamba_forward(m, tok.ctypes.data, ref_logits.ctypes.data) == 0
+    cfg = kmb.model_config(dims, V, dim, N, R, nl)
+    for dt in (FP32, BF16):
+        ours = str(tmp_path / f"ours{dt}.ser")
+        assert kmb.lib().kmamba_save_ser(m, ours.encode(), dt) == 0, kmb.last_error()
+        # the same tensors through the reference's writer, in kmamba_save_ser's order and shapes
+        sc = KSerConfig(vocab_size=V, dim=dim, state_size=N, n_layers=nl, seq_len=L, d_conv=cfg.d_conv,
+                        expand_factor=cfg.expand_factor, dtype=dt, model_name=bytes(cfg.model_name))
+        NR, TS = N * R, max(N // 2, 1)
+        shapes = {"W_in": (R, dim), "W_out": (dim, R), "A_log": (N, 0), "W_B": (NR, dim), "W_C": (NR, dim),
+                  "delta_proj": (dim, 0), "lambda_proj": (dim, 0), "b_B": (NR, 0), "b_C": (NR, 0), "theta": (TS, 0)}
+        tens = [("embedding", params["embedding"], (V, dim, 0, 0), dt)]
+        for i in range(nl):
+            for f in shapes:
+                tens.append((f"layers.{i}.{f}", np.ascontiguousarray(params[f"layers.{i}.{f}"], np.float32),
+                             shapes[f] + (0, 0), dt))
+        tens.append(("head", params["head"], (dim, V, 0, 0), dt))
+        refp = str(tmp_path / f"ref{dt}.ser")
+        _write(_bind(C.CDLL(po.REF_SO)), refp, sc, [], tens)
+        assert open(ours, "rb").read() == open(refp, "rb").read()
+        m2 = kmb.lib().kmb_load_ser_ex(ours.encode(), 2, C.byref(cfg))   # KM_SER_VERIFY
+        assert m2, kmb.last_error()
+        got = np.zeros((L, V), np.float32)
+        assert kmb.lib().kmamba_forward(m2, tok.ctypes.data, got.ctypes.data) == 0
+        kmb.lib().kmamba_free(m2)
+        if dt == FP32:
+            assert np.array_equal(got, ref_logits)
+        else:
+            np.testing.assert_allclose(got, ref_logits, rtol=0.05, atol=0.05 * np.abs(ref_logits).max())
+    kmb.lib().kmamba_free(m)
