@@ -41,15 +41,11 @@ size_t scan_bwd_strips_scratch_bytes(const ScanDesc& s);
 cudaError_t launch_scan_bwd_generic(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC,
                                     float* ddelta, float* dlambda, float* dtheta, float* dx, void* scratch,
                                     cudaStream_t st);
-struct ConvDesc {
-    int nd, D, K, V;
-    long long P, batch;
-    long long dims[KMB_MAXND];
-    long long strides[KMB_MAXND];
-};
 cudaError_t launch_conv_fwd(const ConvDesc& c, const float* in, const float* ker, const float* bias, float* out,
                             cudaStream_t st);
 size_t conv_bwd_scratch_bytes(const ConvDesc& c);
+cudaError_t launch_conv_both(const ConvDesc& c, const float* in, const float* ker, const float* bias, float* out,
+                             const float* dy, float* din, float* dker, float* dbias, void* scratch, cudaStream_t st);
 cudaError_t launch_conv_bwd(const ConvDesc& c, const float* in, const float* ker, const float* dy, float* din,
                             float* dker, float* dbias, void* scratch, cudaStream_t st);
 }  // namespace kmb
@@ -583,6 +579,18 @@ int convnd_batched_async(ConvNDParams* p, long batch, int mode, void* stream) {
     if (batch < 1 || !conv_desc(p, batch, &c)) return fail("invalid ConvNDParams");
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e;
+    if ((mode & CONVND_FORWARD) && (mode & CONVND_BACKWARD) && p->input && p->kernel && p->output && p->dy &&
+        p->dinput && p->dkernel) {
+        // forward and backward together: one pass over input and dy when the fused kernel takes the shape
+        const void* ptrs[] = {p->input, p->kernel, p->bias, p->output, p->dy, p->dinput, p->dkernel, p->dbias};
+        if (common_kind(ptrs, 8) != PK_DEVICE) return fail("convnd needs device pointers");
+        void* scratch = ws_get(WS_SCRATCH, conv_bwd_scratch_bytes(c));
+        if (!scratch) return fail("workspace allocation failed");
+        if ((e = launch_conv_both(c, p->input, p->kernel, p->bias, p->output, p->dy, p->dinput, p->dkernel, p->dbias,
+                                  scratch, st)) != cudaSuccess)
+            return fail_cuda("conv_fwd_bwd", e);
+        return 0;
+    }
     if (mode & CONVND_FORWARD) {
         if (!p->input || !p->kernel || !p->output) return fail("convnd forward needs input, kernel, output");
         const void* ptrs[] = {p->input, p->kernel, p->bias, p->output};

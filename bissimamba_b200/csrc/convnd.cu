@@ -17,13 +17,6 @@
 
 namespace kmb {
 
-struct ConvDesc {
-    int nd, D, K, V;          // V = K^nd
-    long long P, batch;
-    long long dims[KMB_MAXND];
-    long long strides[KMB_MAXND];
-};
-
 __global__ void __launch_bounds__(256) conv_fwd_kernel(ConvDesc c, const float* __restrict__ in,
                                                        const float* __restrict__ ker,
                                                        const float* __restrict__ bias,
@@ -468,13 +461,24 @@ static cudaError_t conv_fast(const ConvDesc& c, bool fwd, const float* in, const
 }
 
 
+cudaError_t launch_conv_fused(const ConvDesc& c, int mode, const float* in, const float* ker, const float* bias,
+                              float* out, const float* dy, float* din, float* dker, float* dbias, float* part,
+                              long long nch_max, cudaStream_t st);
+long long conv_fused_chunks(const ConvDesc& c, int mode);
+
 cudaError_t launch_conv_fwd(const ConvDesc& c, const float* in, const float* ker, const float* bias,
                             float* out, cudaStream_t st) {
-    cudaError_t ef = conv_fast(c, true, in, ker, bias, out, nullptr, nullptr, nullptr, nullptr, nullptr, 0, st);
+    cudaError_t ef = launch_conv_fused(c, 1, in, ker, bias, out, nullptr, nullptr, nullptr, nullptr, nullptr, 0, st);
+    if (ef != cudaErrorNotSupported) return ef;
+    ef = conv_fast(c, true, in, ker, bias, out, nullptr, nullptr, nullptr, nullptr, nullptr, 0, st);
     if (ef != cudaErrorNotSupported) return ef;
     conv_fwd_kernel<<<cblk(c.batch * c.P * c.D, 256), 256, 0, st>>>(c, in, ker, bias, out);
     return cudaGetLastError();
 }
+
+// forward and backward together: one fused launch when the shape allows it
+cudaError_t launch_conv_both(const ConvDesc& c, const float* in, const float* ker, const float* bias, float* out,
+                             const float* dy, float* din, float* dker, float* dbias, void* scratch, cudaStream_t st);
 
 static long long conv_chunks(const ConvDesc& c) {
     const long long rows = c.batch * c.P;
@@ -483,12 +487,18 @@ static long long conv_chunks(const ConvDesc& c) {
 }
 
 size_t conv_bwd_scratch_bytes(const ConvDesc& c) {
-    return (size_t)conv_chunks(c) * (c.V + 1) * c.D * sizeof(float);
+    long long n = conv_chunks(c);
+    const long long nf = conv_fused_chunks(c, 3);
+    if (nf > n) n = nf;
+    return (size_t)n * (c.V + 1) * c.D * sizeof(float);
 }
 
 cudaError_t launch_conv_bwd(const ConvDesc& c, const float* in, const float* ker, const float* dy,
                             float* din, float* dker, float* dbias, void* scratch, cudaStream_t st) {
-    cudaError_t ef = conv_fast(c, false, in, ker, nullptr, nullptr, dy, din, dker, dbias, (float*)scratch,
+    cudaError_t ef = launch_conv_fused(c, 2, in, ker, nullptr, nullptr, dy, din, dker, dbias, (float*)scratch,
+                                       conv_fused_chunks(c, 2), st);
+    if (ef != cudaErrorNotSupported) return ef;
+    ef = conv_fast(c, false, in, ker, nullptr, nullptr, dy, din, dker, dbias, (float*)scratch,
                                conv_chunks(c), st);
     if (ef != cudaErrorNotSupported) return ef;
     conv_bwd_input_kernel<<<cblk(c.batch * c.P * c.D, 256), 256, 0, st>>>(c, dy, ker, din);
@@ -510,6 +520,15 @@ cudaError_t launch_conv_bwd(const ConvDesc& c, const float* in, const float* ker
 }
 
 
+
+cudaError_t launch_conv_both(const ConvDesc& c, const float* in, const float* ker, const float* bias, float* out,
+                             const float* dy, float* din, float* dker, float* dbias, void* scratch, cudaStream_t st) {
+    cudaError_t e = launch_conv_fused(c, 3, in, ker, bias, out, dy, din, dker, dbias, (float*)scratch,
+                                      conv_fused_chunks(c, 3), st);
+    if (e != cudaErrorNotSupported) return e;
+    if ((e = launch_conv_fwd(c, in, ker, bias, out, st)) != cudaSuccess) return e;
+    return launch_conv_bwd(c, in, ker, dy, din, dker, dbias, scratch, st);
+}
 
 // ---------------------------------------------------------------------------
 // convnd backward without any allocation.
@@ -561,6 +580,10 @@ static cudaError_t launch_conv_bwd_noalloc(const ConvDesc& c, const float* in, c
     cudaError_t e = noalloc_scratch_ptr(&part);
     if (e != cudaSuccess) return e;
     // the fast kernels first, with as many partial-sum chunks as the array holds
+    e = launch_conv_fused(c, 2, in, ker, nullptr, nullptr, dy, din, dker, dbias, part,
+                          kNoAllocScratchFloats / per_chunk, st);
+    if (e != cudaErrorNotSupported) return e;
+    cudaGetLastError();
     e = conv_fast(c, false, in, ker, nullptr, nullptr, dy, din, dker, dbias, part, kNoAllocScratchFloats / per_chunk, st);
     if (e != cudaErrorNotSupported) return e;
     cudaGetLastError();

@@ -1,0 +1,398 @@
+// convnd_fused.cu -- depthwise causal convND forward + backward in one launch
+// (reference src/convnd.c:396-531) for ndims <= 3, K <= 4,
+// D a multiple of 8.
+//
+// A CTA owns (item b, slab of T0 planes of the outermost axis, 8 channels).
+// It stages the input slab with its K-1 causal halo planes / rows / columns
+// on the low side, and the dy slab with the halo on the high side, into
+// shared memory, zero-padded, so no tap needs a bounds test.  Then each
+// thread walks runs of R consecutive points along the innermost axis for one
+// float4 of channels:
+//   forward  out[x]  = bias + sum_k in[x - s_k] ker[k]   (taps in ascending
+//            kernel-linear order, the reference's order: bit-identical)
+//   dinput   din[x]  = sum_k dy[x + s_k] ker[k]          (gather, no atomics)
+//   dkernel  acc[k] += dy[x] in[x - s_k]                  (per-CTA partials)
+// A row of R + K - 1 values along the innermost axis serves all K taps of that
+// axis for the R points, so shared-memory reads per point fall from K^nd to
+// K^(nd-1) (R + K - 1) / R.  The input values read for the forward are the
+// ones the dkernel products need, so they are read once for both.  The
+// per-CTA dkernel / dbias partials are summed over the CTA in a fixed order
+// and written to part[(b * nslab + slab)][V + 1][D]; a second launch adds the
+// chunks in order (deterministic).  Global traffic: input and dy read once
+// (plus the halo planes of the next slab), out and dinput written once.
+#include "kmb_common.cuh"
+
+namespace kmb {
+
+constexpr int CF_THREADS = 256;
+constexpr int CF_SMEM_MAX = 110 * 1024;   // two CTAs per SM
+
+struct FusedGeom {
+    int T0, nslab;              // planes of axis 0 per slab, slabs per item
+    int pd[3];                  // padded extents of the slab (axis 0 includes the K - 1 halo planes)
+    int ps[3];                  // padded strides (in points)
+    int slab_pts;               // points of one padded slab
+    int slab_slots;             // point slots allocated (one spare slot after every 4 points)
+};
+
+template <int ND, int K>
+struct CfTaps {
+    static constexpr int V = ND == 1 ? K : (ND == 2 ? K * K : K * K * K);
+    static constexpr int ROWS = V / K;   // taps of the outer axes: one shared-memory row each
+};
+
+// N channels per thread (1, 2 or 4 floats)
+template <int N> struct CfVec;
+template <> struct CfVec<4> { using T = float4; };
+template <> struct CfVec<2> { using T = float2; };
+template <> struct CfVec<1> { using T = float; };
+__device__ __forceinline__ void cf_fma(float4& a, const float4 x, const float4 y) {
+    a.x = __fmaf_rn(x.x, y.x, a.x);
+    a.y = __fmaf_rn(x.y, y.y, a.y);
+    a.z = __fmaf_rn(x.z, y.z, a.z);
+    a.w = __fmaf_rn(x.w, y.w, a.w);
+}
+__device__ __forceinline__ void cf_fma(float2& a, const float2 x, const float2 y) {
+    a.x = __fmaf_rn(x.x, y.x, a.x);
+    a.y = __fmaf_rn(x.y, y.y, a.y);
+}
+__device__ __forceinline__ void cf_fma(float& a, const float x, const float y) { a = __fmaf_rn(x, y, a); }
+__device__ __forceinline__ void cf_add(float4& a, const float4 x) { a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w; }
+__device__ __forceinline__ void cf_add(float2& a, const float2 x) { a.x += x.x; a.y += x.y; }
+__device__ __forceinline__ void cf_add(float& a, const float x) { a += x; }
+template <typename V> __device__ __forceinline__ V cf_zero();
+template <> __device__ __forceinline__ float4 cf_zero<float4>() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+template <> __device__ __forceinline__ float2 cf_zero<float2>() { return make_float2(0.f, 0.f); }
+template <> __device__ __forceinline__ float cf_zero<float>() { return 0.0f; }
+__device__ __forceinline__ float4 cf_shfl(float4 v, int o) {
+    return make_float4(__shfl_xor_sync(~0u, v.x, o), __shfl_xor_sync(~0u, v.y, o), __shfl_xor_sync(~0u, v.z, o),
+                       __shfl_xor_sync(~0u, v.w, o));
+}
+__device__ __forceinline__ float2 cf_shfl(float2 v, int o) {
+    return make_float2(__shfl_xor_sync(~0u, v.x, o), __shfl_xor_sync(~0u, v.y, o));
+}
+__device__ __forceinline__ float cf_shfl(float v, int o) { return __shfl_xor_sync(~0u, v, o); }
+
+// Shared-memory slot of padded point pt: one spare slot after every four points,
+// so the runs of four points that the threads of a warp read start in different
+// banks (no conflicts for 4-, 8- or 16-byte reads).
+__device__ __forceinline__ int cf_slot(int pt) { return pt + (pt >> 2); }
+
+// MODE bit 0: forward (out); bit 1: backward (dinput, dkernel / dbias partials).
+// CG float4 channel lanes (4 CG channels) per CTA; N channels per thread.
+template <int ND, int K, int R, int MODE, int N, int CG>
+__global__ void __launch_bounds__(CF_THREADS, 2) conv_fused_kernel(ConvDesc c, FusedGeom g,
+                                                                   const float4* __restrict__ in,
+                                                                   const float* __restrict__ ker,
+                                                                   const float* __restrict__ bias,
+                                                                   const float4* __restrict__ dy,
+                                                                   float* __restrict__ out, float* __restrict__ din,
+                                                                   float* __restrict__ part) {
+    using T = CfTaps<ND, K>;
+    using V = typename CfVec<N>::T;
+    constexpr bool FWD = MODE & 1, BWD = (MODE & 2) != 0;
+    constexpr int NL = CG * 4 / N;                           // threads per point (channel lanes of N)
+    constexpr int H = K - 1;
+    extern __shared__ __align__(16) float4 cf_smem[];
+    float4* sIN = cf_smem;                                   // [slot][CG]
+    float4* sDY = cf_smem + g.slab_slots * CG;
+    const int D4 = c.D >> 2;
+    const int slab = blockIdx.x % g.nslab;
+    const long long b = blockIdx.x / g.nslab;
+    const int lane0 = blockIdx.y * CG;                       // first float4 channel lane of this CTA
+    const int z0 = slab * g.T0;
+    const int dims0 = (int)c.dims[0];
+    const int nz = min(g.T0, dims0 - z0);                    // planes this CTA produces
+    const int d1 = ND > 1 ? (int)c.dims[ND > 1 ? 1 : 0] : 1;
+    const int d2 = ND > 2 ? (int)c.dims[ND > 2 ? 2 : 0] : 1;
+    const long long ibase = b * c.P;                         // item base in points
+    const int tid = threadIdx.x, wl = tid & 31, warp = tid >> 5;
+
+    // ---- stage the slabs, one padded row of the innermost axis at a time (zero halo):
+    // padded (pz, py, px) <- input (z0 + pz - H, py - H, px - H) and dy (z0 + pz, py, px)
+    {
+        const int pdl = g.pd[ND - 1];                        // padded innermost extent
+        const int nrows = g.slab_pts / pdl;
+        const int dl_ = ND == 1 ? dims0 : (ND == 2 ? d1 : d2);
+        for (int row = warp; row < nrows; row += CF_THREADS / 32) {
+            int c0 = row, c1 = 0;
+            if (ND == 3) {
+                c0 = row / g.pd[1];
+                c1 = row - c0 * g.pd[1];
+            }
+            // source row coordinates (outer axes) for the input and for dy
+            const int si0 = ND == 1 ? 0 : z0 + c0 - H, si1 = c1 - H;
+            const int sd0 = ND == 1 ? 0 : z0 + c0, sd1 = c1;
+            const bool in_ok = ND == 1 || (si0 >= 0 && si0 < dims0 && (ND < 3 || (si1 >= 0 && si1 < d1)));
+            const bool dy_ok = ND == 1 || (sd0 < dims0 && (ND < 3 || sd1 < d1));
+            const long long rbase_in = ND == 1 ? 0 : (ND == 2 ? (long long)si0 * d1 : ((long long)si0 * d1 + si1) * d2);
+            const long long rbase_dy = ND == 1 ? 0 : (ND == 2 ? (long long)sd0 * d1 : ((long long)sd0 * d1 + sd1) * d2);
+            for (int e = wl; e < pdl * CG; e += 32) {
+                const int px = e / CG, l = e - px * CG;
+                const int slot = cf_slot(row * pdl + px) * CG + l;
+                // innermost source coordinate (for 1D the innermost axis is axis 0, offset by the slab)
+                const int xi = (ND == 1 ? z0 : 0) + px - H, xd = (ND == 1 ? z0 : 0) + px;
+                if (FWD || BWD) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (in_ok && xi >= 0 && xi < dl_) v = in[(ibase + rbase_in + xi) * D4 + lane0 + l];
+                    sIN[slot] = v;
+                }
+                if (BWD) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (dy_ok && xd < dl_) v = dy[(ibase + rbase_dy + xd) * D4 + lane0 + l];
+                    sDY[slot] = v;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- compute: work item = (run of R points along the innermost axis, N channels)
+    const int lane = tid % NL;
+    const int ch = lane0 * 4 + lane * N;                     // first channel of this thread
+    const float* sINf = (const float*)sIN;
+    const float* sDYf = (const float*)sDY;
+    const int lo = lane * N;                                 // float offset inside a point's 4 CG channels
+    auto ldin = [&](int pt) { return *(const V*)(sINf + cf_slot(pt) * (CG * 4) + lo); };
+    auto lddy = [&](int pt) { return *(const V*)(sDYf + cf_slot(pt) * (CG * 4) + lo); };
+    V kv[T::V];
+#pragma unroll
+    for (int k = 0; k < T::V; k++) kv[k] = *(const V*)(ker + (long long)k * c.D + ch);
+    const V b0 = (FWD && bias) ? *(const V*)(bias + ch) : cf_zero<V>();
+    V dk[BWD ? T::V + 1 : 1];
+#pragma unroll
+    for (int k = 0; k < (BWD ? T::V + 1 : 1); k++) dk[k] = cf_zero<V>();
+    const int dlast = ND == 1 ? dims0 : (ND == 2 ? d1 : d2);   // innermost extent
+    const int nrun_line = dlast / R;
+    const int lines = ND == 1 ? 1 : (ND == 2 ? nz : nz * d1);
+    const int nwork = (ND == 1 ? (nz / R) : lines * nrun_line);
+    for (int wi = tid / NL; wi < nwork; wi += CF_THREADS / NL) {
+        // coordinates of the run's first point (relative to the slab for axis 0)
+        int zr, y = 0, x0;
+        if (ND == 1) {
+            zr = wi * R;
+            x0 = zr;
+        } else if (ND == 2) {
+            zr = wi / nrun_line;
+            x0 = (wi - zr * nrun_line) * R;
+        } else {
+            const int ln = wi / nrun_line;
+            zr = ln / d1;
+            y = ln - zr * d1;
+            x0 = (wi - ln * nrun_line) * R;
+        }
+        // padded base index of the run (the same expression for the input, whose halo is on the low
+        // side of every axis, and for dy, whose halo is on the high side)
+        int base;
+        if (ND == 1) base = zr;
+        else if (ND == 2) base = zr * g.ps[0] + x0;
+        else base = zr * g.ps[0] + y * g.ps[1] + x0;
+        V acc[R], adin[R], dyo[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            acc[r] = b0;
+            adin[r] = cf_zero<V>();
+        }
+        if (BWD) {
+#pragma unroll
+            for (int r = 0; r < R; r++) dyo[r] = lddy(base + r);
+        }
+#pragma unroll
+        for (int row = 0; row < T::ROWS; row++) {
+            // outer digits of this row: (k0) for 2D, (k0, k1) for 3D; shift of an axis = H - digit
+            const int k0 = ND == 3 ? row / K : row;
+            const int k1 = ND == 3 ? row % K : 0;
+            int rin, rdy;
+            if (ND == 1) {
+                rin = base;
+                rdy = base;
+            } else if (ND == 2) {
+                rin = base + k0 * g.ps[0];
+                rdy = base + (H - k0) * g.ps[0];
+            } else {
+                rin = base + k0 * g.ps[0] + k1 * g.ps[1];
+                rdy = base + (H - k0) * g.ps[0] + (H - k1) * g.ps[1];
+            }
+            {
+                V w[R + H];
+#pragma unroll
+                for (int j = 0; j < R + H; j++) w[j] = ldin(rin + j);
+#pragma unroll
+                for (int kx = 0; kx < K; kx++) {
+                    const int k = row * K + kx;
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        // in[x - (H - kx)] with x = x0 + r sits at padded x0 + r + kx
+                        if (FWD) cf_fma(acc[r], w[r + kx], kv[k]);
+                        if (BWD) cf_fma(dk[k], dyo[r], w[r + kx]);
+                    }
+                }
+            }
+            if (BWD) {
+                V w[R + H];
+#pragma unroll
+                for (int j = 0; j < R + H; j++) w[j] = lddy(rdy + j);
+#pragma unroll
+                for (int kx = 0; kx < K; kx++) {
+                    const int k = row * K + kx;
+#pragma unroll
+                    for (int r = 0; r < R; r++) cf_fma(adin[r], w[r + H - kx], kv[k]);   // dy[x + (H - kx)]
+                }
+            }
+        }
+        // global point index of the run's first point
+        long long p;
+        if (ND == 1) p = z0 + zr;
+        else if (ND == 2) p = (long long)(z0 + zr) * d1 + x0;
+        else p = ((long long)(z0 + zr) * d1 + y) * d2 + x0;
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const long long gi = (ibase + p + r) * c.D + ch;
+            if (FWD) *(V*)(out + gi) = acc[r];
+            if (BWD) {
+                *(V*)(din + gi) = adin[r];
+                cf_add(dk[T::V], dyo[r]);
+            }
+        }
+    }
+    if (!BWD) return;
+    // ---- dkernel / dbias partials of the CTA, a fixed-order tree: the threads of a warp that share a
+    // channel lane (xor shuffles over the lane-stride offsets), then the warps in order
+    constexpr int NV = T::V + 1;
+#pragma unroll
+    for (int k = 0; k < NV; k++)
+#pragma unroll
+        for (int o = NL; o < 32; o <<= 1) cf_add(dk[k], cf_shfl(dk[k], o));
+    __syncthreads();
+    V* red = (V*)cf_smem;   // reuse the staging area: [warp][NV][NL]
+    if (wl < NL) {
+#pragma unroll
+        for (int k = 0; k < NV; k++) red[(warp * NV + k) * NL + wl] = dk[k];
+    }
+    __syncthreads();
+    const long long chunk = b * g.nslab + slab;
+    for (int i = tid; i < NV * NL; i += CF_THREADS) {
+        const int k = i / NL, l = i - k * NL;
+        V s2 = red[k * NL + l];
+        for (int wv = 1; wv < CF_THREADS / 32; wv++) cf_add(s2, red[(wv * NV + k) * NL + l]);
+        *(V*)(part + (chunk * NV + k) * c.D + lane0 * 4 + l * N) = s2;
+    }
+}
+
+__global__ void reduce_rows_set(const float* __restrict__ part, float* __restrict__ out, long long count, long long n,
+                                long long stride);
+
+// Channel lanes per CTA: 8 channels (one 32-byte sector per point) for 1D / 2D,
+// 4 for 3D, whose padded planes are larger.
+static int cf_cg(int nd) { return nd == 3 ? 1 : 2; }
+
+// Plans the slab split; false when the shape is outside the kernel's set.
+static bool cf_plan(const ConvDesc& c, int mode, FusedGeom* g, int* smem, int* R) {
+    if (c.nd < 1 || c.nd > 3 || c.K < 2 || c.K > 4 || c.D % 8 != 0 || (c.nd == 3 && c.K == 4)) return false;
+    const int H = c.K - 1, CG = cf_cg(c.nd);
+    const int dlast = (int)c.dims[c.nd - 1];
+    *R = (dlast % 4 == 0) ? 4 : 1;
+    int rest = 1;   // padded points of one plane of axis 0
+    for (int a = 1; a < c.nd; a++) rest *= (int)c.dims[a] + H;
+    const int ntens = (mode & 2) ? 2 : 1;
+    auto bytes = [&](int T0) {
+        const int pts = (T0 + H) * rest;
+        return (pts + pts / 4 + 1) * CG * 16 * ntens;
+    };
+    int T0 = (int)c.dims[0];
+    if (c.nd == 1) {
+        T0 = (int)c.dims[0] < 1024 ? (int)c.dims[0] : 1024;
+        T0 = T0 / *R * *R;
+        if (T0 < *R) T0 = *R;
+    }
+    while (T0 > 1 && bytes(T0) > CF_SMEM_MAX) T0 = c.nd == 1 ? T0 / 2 / *R * *R : T0 - 1;
+    if (T0 < 1 || bytes(T0) > CF_SMEM_MAX) return false;
+    if (c.nd == 1 && T0 % *R) return false;
+    g->T0 = T0;
+    g->nslab = (int)((c.dims[0] + T0 - 1) / T0);
+    if (c.nd == 1 && c.dims[0] % T0 != 0 && (c.dims[0] % T0) % *R != 0) return false;
+    g->pd[0] = T0 + H;
+    for (int a = 1; a < c.nd; a++) g->pd[a] = (int)c.dims[a] + H;
+    for (int a = c.nd; a < 3; a++) g->pd[a] = 1;
+    g->ps[c.nd - 1] = 1;
+    for (int a = c.nd - 2; a >= 0; a--) g->ps[a] = g->ps[a + 1] * g->pd[a + 1];
+    g->slab_pts = g->pd[0] * g->ps[0];
+    g->slab_slots = g->slab_pts + g->slab_pts / 4 + 1;
+    int sm = bytes(T0);
+    const int vol = (int)(std::pow((double)c.K, (double)c.nd) + 0.5) + 1;
+    const int red = (CF_THREADS / 32) * vol * 16 * 4;   // [warp][V + 1][lanes] partials, at most 16 B x 4 lanes
+    if ((mode & 2) && red > sm) sm = red;
+    *smem = sm;
+    return true;
+}
+
+long long conv_fused_chunks(const ConvDesc& c, int mode) {
+    FusedGeom g;
+    int sm, R;
+    if (!cf_plan(c, mode, &g, &sm, &R)) return -1;
+    return c.batch * g.nslab;
+}
+
+template <int ND, int K, int R, int MODE>
+static cudaError_t cf_launch_t(const ConvDesc& c, const FusedGeom& g, int smem, const float* in, const float* ker,
+                               const float* bias, const float* dy, float* out, float* din, float* part,
+                               cudaStream_t st) {
+    // one channel per thread in 3D (27 taps of kernel values and dkernel accumulators in registers,
+    // two CTAs per SM), two elsewhere
+    constexpr int N = ND == 3 ? 1 : 2;
+    constexpr int CG = ND == 3 ? 1 : 2;
+    auto k = conv_fused_kernel<ND, K, R, MODE, N, CG>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    dim3 grid((unsigned)(c.batch * g.nslab), (unsigned)(c.D / 4 / CG));
+    k<<<grid, CF_THREADS, smem, st>>>(c, g, (const float4*)in, ker, bias, (const float4*)dy, out, din, part);
+    return cudaGetLastError();
+}
+
+template <int ND, int K, int R>
+static cudaError_t cf_mode(int mode, const ConvDesc& c, const FusedGeom& g, int smem, const float* in,
+                           const float* ker, const float* bias, const float* dy, float* out, float* din, float* part,
+                           cudaStream_t st) {
+    switch (mode) {
+        case 1: return cf_launch_t<ND, K, R, 1>(c, g, smem, in, ker, bias, dy, out, din, part, st);
+        case 2: return cf_launch_t<ND, K, R, 2>(c, g, smem, in, ker, bias, dy, out, din, part, st);
+        default: return cf_launch_t<ND, K, R, 3>(c, g, smem, in, ker, bias, dy, out, din, part, st);
+    }
+}
+
+// mode 1: forward; 2: backward; 3: both.  part: >= conv_fused_chunks * (V + 1) * D floats (backward).
+// cudaErrorNotSupported outside the kernel's set or when nch_max is too small.
+cudaError_t launch_conv_fused(const ConvDesc& c, int mode, const float* in, const float* ker, const float* bias,
+                              float* out, const float* dy, float* din, float* dker, float* dbias, float* part,
+                              long long nch_max, cudaStream_t st) {
+    FusedGeom g;
+    int smem, R;
+    if (!cf_plan(c, mode, &g, &smem, &R)) return cudaErrorNotSupported;
+    const long long nch = c.batch * g.nslab;
+    if ((mode & 2) && nch > nch_max) return cudaErrorNotSupported;
+    if (c.batch * g.nslab > 0x7fffffffLL) return cudaErrorNotSupported;
+    const uintptr_t al = (uintptr_t)in | (uintptr_t)ker | (uintptr_t)(bias ? bias : ker) |
+                         (uintptr_t)(out ? out : ker) | (uintptr_t)(dy ? dy : ker) | (uintptr_t)(din ? din : ker) |
+                         (uintptr_t)(part ? part : ker);
+    if (al & 15) return cudaErrorNotSupported;
+    cudaError_t e;
+#define KMB_CF(ND_, K_)                                                                                        \
+    if (c.nd == ND_ && c.K == K_)                                                                              \
+        e = R == 4 ? cf_mode<ND_, K_, 4>(mode, c, g, smem, in, ker, bias, dy, out, din, part, st)              \
+                   : cf_mode<ND_, K_, 1>(mode, c, g, smem, in, ker, bias, dy, out, din, part, st);             \
+    else
+    // (3D with K = 4 is left to the other kernels: 64 dkernel accumulators per thread do not fit)
+    KMB_CF(1, 2) KMB_CF(1, 3) KMB_CF(1, 4) KMB_CF(2, 2) KMB_CF(2, 3) KMB_CF(2, 4) KMB_CF(3, 2) KMB_CF(3, 3)
+    return cudaErrorNotSupported;
+#undef KMB_CF
+    if (e != cudaSuccess || !(mode & 2)) return e;
+    const long long V = (long long)(std::pow((double)c.K, (double)c.nd) + 0.5);
+    const long long cnt = V * c.D;
+    reduce_rows_set<<<(unsigned)((cnt + 255) / 256), 256, 0, st>>>(part, dker, cnt, nch, (V + 1) * c.D);
+    if (dbias)
+        reduce_rows_set<<<(unsigned)((c.D + 255) / 256), 256, 0, st>>>(part + V * c.D, dbias, c.D, nch, (V + 1) * c.D);
+    return cudaGetLastError();
+}
+
+}  // namespace kmb

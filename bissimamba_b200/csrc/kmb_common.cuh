@@ -39,6 +39,16 @@ struct ScanDesc {
     float* y;
 };
 
+namespace kmb {
+// convND problem description (batch of items, row-major points, channels last).
+struct ConvDesc {
+    int nd, D, K, V;          // V = K^nd
+    long long P, batch;
+    long long dims[KMB_MAXND];
+    long long strides[KMB_MAXND];
+};
+}  // namespace kmb
+
 // Clamped cubic Taylor exponential of the reference (include/km_topology.h:52-56)
 // or CUDA's accurate expf.
 __device__ __forceinline__ float kmb_exp(float z, int fast) {

@@ -101,3 +101,34 @@ def test_conv_rejects_invalid(kmb, cuda):
     for dims, K, batch in (([4, 0], 3, 1), ([4, 4], 0, 1), ([4, 4], 3, 0)):
         p = kmb.conv_params(dims, 1, K, z, z, None, z, z, z, z, None)
         assert kmb.lib().convnd_batched_async(C.byref(p), batch, 3, None) == -1
+
+
+@pytest.mark.parametrize("dims,D,K", [([1024], 8, 4), ([36], 16, 3), ([37], 8, 2), ([32, 32], 64, 3),
+                                      ([13, 30], 8, 2), ([6, 10], 16, 4), ([48, 64], 8, 3), ([16, 16, 16], 16, 3),
+                                      ([20, 16, 16], 8, 3), ([5, 7, 6], 8, 2)])
+def test_fused_kernel_shapes(kmb, cuda, dims, D, K):
+    """The fused forward + backward kernel (D a multiple of 8, ndims <= 3):
+    slabs with their causal halos, runs of 4 and of 1 along the innermost
+    axis.  The forward is bit-identical to the reference's tap order; mode 1
+    and mode 2 alone give the same bits as mode 3."""
+    import torch
+    inp = po.gen_conv(dims, D, K, batch=3, seed=sum(dims) + K, bias=True)
+    o, di, dk, db = _gpu_conv(kmb, cuda, inp)
+    ro, rdi, rdk, rdb = po.conv_run(inp, "oracle")
+    assert np.array_equal(o, ro)
+    np.testing.assert_allclose(di, rdi, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(dk, rdk, rtol=1e-4, atol=1e-5 * max(np.abs(rdk).max(), 1e-30))
+    np.testing.assert_allclose(db, rdb, rtol=1e-4, atol=1e-5 * max(np.abs(rdb).max(), 1e-30))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    P, V = int(np.prod(dims)), K ** len(dims)
+    out = torch.zeros((3, P, D), device=cuda)
+    din = torch.zeros((3, P, D), device=cuda)
+    dk2, db2 = torch.zeros((V, D), device=cuda), torch.zeros((D,), device=cuda)
+    p = kmb.conv_params(dims, D, K, t(inp["input"]), t(inp["kernel"]), t(inp["bias"]), out, t(inp["dy"]), din, dk2, db2)
+    kmb.check(kmb.lib().convnd_batched_async(C.byref(p), 3, 1, None))
+    kmb.check(kmb.lib().convnd_batched_async(C.byref(p), 3, 2, None))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), o)
+    assert np.array_equal(din.cpu().numpy(), di)
+    assert np.array_equal(dk2.cpu().numpy(), dk)
+    assert np.array_equal(db2.cpu().numpy(), db)
