@@ -569,7 +569,9 @@ def wl_scan_bwd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, wor
     or BASELINE config 1 (2D 32x32, D 64, M 16, batch 8, RoPE)."""
     import torch
     if which == "scan_bwd":
-        dims, D_, M_, B_, rope, name = (64, 64), 512, 64, 32, False, "scannd_bwd_2d64x64_D512_M64_b32 (headline geometry)"
+        B_ = args.batch   # 32 unless --batch overrides it (profiling)
+        dims, D_, M_, rope = (64, 64), 512, 64, False
+        name = f"scannd_bwd_2d64x64_D512_M64_b{B_} (headline geometry)"
     else:
         dims, D_, M_, B_, rope, name = (32, 32), 64, 16, 8, True, "scannd_bwd_2d32x32_D64_M16_b8_rope (config 1)"
     P_, nd = int(np.prod(dims)), len(dims)
@@ -611,7 +613,7 @@ def wl_scan_bwd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, wor
     alg_o = upd * 20 + B_ * P_ * D_ * (4 * (2 + nd) + 4 * (nd + 1)) + B_ * P_ * 4
     line["overwrite_variant"] = {"value": upd * world / (ms_o / steps / 1e3), "ms_per_step": ms_o / steps,
                                  "hbm_frac": round(alg_o / (ms_o / steps / 1e3) / 1e9 / peak, 4)}
-    eb = B_ if which != "scan_bwd" else 4    # host RAM: 4 headline items (5.5 GB in, 4.4 GB out) per e2e step
+    eb = B_ if which != "scan_bwd" else min(4, B_)   # host RAM: 4 headline items (5.5 GB in, 4.4 GB out) per e2e step
     hin = {"x": _pinned(t["x"][:eb]), "delta": _pinned(t["delta"][:eb]), "B": _pinned(t["B"][:eb]),
            "C": _pinned(t["C"][:eb]), "h": _pinned(h[:eb]), "dy": _pinned(dy[:eb])}
     din = {k: torch.empty_like(v, device=dev) for k, v in hin.items()}

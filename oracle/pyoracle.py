@@ -22,7 +22,24 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(HERE, "_ref", "libkmamba_ref.so")
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
-REF_SRC = "/root/reference"
+
+
+def _reference_dir():
+    """Where the reference sources are: KMB_REFERENCE_DIR, else the
+    `reference_path` that BASELINE.json records (absent on the GPU box, which
+    uses the prebuilt _ref library)."""
+    d = os.environ.get("KMB_REFERENCE_DIR")
+    if d:
+        return d
+    try:
+        import json
+        with open(os.path.join(HERE, "..", "BASELINE.json")) as f:
+            return json.load(f).get("reference_path") or ""
+    except (OSError, ValueError):
+        return ""
+
+
+REF_SRC = _reference_dir()
 
 _f = C.POINTER(C.c_float)
 _l = C.POINTER(C.c_long)
@@ -55,10 +72,10 @@ def build(force: bool = False) -> None:
     targets = []
     if force or not os.path.exists(ORACLE_SO):
         targets.append("oracle")
-    if os.path.isdir(REF_SRC) and (force or not os.path.exists(REF_SO)):
+    if REF_SRC and os.path.isdir(REF_SRC) and (force or not os.path.exists(REF_SO)):
         targets.append("ref")
     if targets:
-        subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+        subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_SRC}"] + targets, check=True)
 
 
 _libs: dict = {}
