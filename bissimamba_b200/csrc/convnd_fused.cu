@@ -279,8 +279,17 @@ __global__ void __launch_bounds__(CF_THREADS, 2) conv_fused_kernel(ConvDesc c, F
     }
 }
 
-__global__ void reduce_rows_set(const float* __restrict__ part, float* __restrict__ out, long long count, long long n,
-                                long long stride);
+// dkernel[i] (i < V D) and dbias[i - V D] = sum over the chunks of part[chunk][i], fixed order (one launch)
+__global__ void cf_reduce_dk(const float* __restrict__ part, float* __restrict__ dker, float* __restrict__ dbias,
+                             long long VD, int D, long long nch) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long stride = VD + D;
+    if (i >= (dbias ? stride : VD)) return;
+    float acc = 0.0f;
+    for (long long j = 0; j < nch; j++) acc += part[j * stride + i];
+    if (i < VD) dker[i] = acc;
+    else dbias[i - VD] = acc;
+}
 
 // Channel lanes per CTA: 8 channels (one 32-byte sector per point) for 1D / 2D,
 // 4 for 3D, whose padded planes are larger.
@@ -388,10 +397,8 @@ cudaError_t launch_conv_fused(const ConvDesc& c, int mode, const float* in, cons
 #undef KMB_CF
     if (e != cudaSuccess || !(mode & 2)) return e;
     const long long V = (long long)(std::pow((double)c.K, (double)c.nd) + 0.5);
-    const long long cnt = V * c.D;
-    reduce_rows_set<<<(unsigned)((cnt + 255) / 256), 256, 0, st>>>(part, dker, cnt, nch, (V + 1) * c.D);
-    if (dbias)
-        reduce_rows_set<<<(unsigned)((c.D + 255) / 256), 256, 0, st>>>(part + V * c.D, dbias, c.D, nch, (V + 1) * c.D);
+    const long long cnt = (V + 1) * c.D;
+    cf_reduce_dk<<<(unsigned)((cnt + 255) / 256), 256, 0, st>>>(part, dker, dbias, V * c.D, c.D, nch);
     return cudaGetLastError();
 }
 
