@@ -145,6 +145,7 @@ EXPORTS = [
     "kmamba_init", "kmamba_enable_training", "kmamba_forward", "kmamba_train_batch", "kmamba_train_step",
     "kmamba_get_config", "kmamba_step_count", "kmamba_update_lr", "kmamba_get_tensor", "kmamba_set_tensor",
     "kmb_model_forward_backward", "kmb_model_optimizer_step", "kmb_model_grad_arena", "kmb_model_param_arena", "kmb_model_tensor_offset",
+    "kmb_gemm_f32", "kmb_gemm_bf16", "kmb_gemm_set_f32_kind", "kmb_gemm_get_f32_kind", "kmb_gemm_set_f32_flush", "kmb_gemm_last_path",
 ]
 
 _lib = None
@@ -257,6 +258,11 @@ def lib():
         L.kmamba_step_count.restype = C.c_size_t
         L.kmamba_update_lr.argtypes = [C.c_void_p, C.c_float, C.c_float]
         L.kmamba_update_lr.restype = None
+        ll = C.c_longlong
+        L.kmb_gemm_f32.argtypes = [C.c_int, C.c_int, ll, ll, ll, vp, ll, vp, ll, vp, ll, C.c_int, vp]
+        L.kmb_gemm_bf16.argtypes = [C.c_int, ll, ll, ll, vp, ll, vp, ll, vp, ll, C.c_int, vp]
+        L.kmb_gemm_set_f32_kind.argtypes = [C.c_int]
+        L.kmb_gemm_set_f32_flush.argtypes = [C.c_int]
         L.kmamba_get_config.argtypes = [C.c_void_p]
         L.kmamba_get_config.restype = KC
         L.kmb_model_forward_backward.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]

@@ -15,7 +15,7 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "libkmamba_b200.so")
 SOURCES = ["capi.cu", "scannd_generic.cu", "scannd_tma.cu", "scannd_strips.cu", "scannd_bwd.cu", "scannd_bwd_strips.cu", "convnd.cu", "convnd_fused.cu",
-           "blockscan.cu", "block.cu", "proj_tc.cu", "model.cu", "distributed.cu", "kser.cpp", "wavefront.cpp"]
+           "blockscan.cu", "block.cu", "proj_tc.cu", "gemm_tc.cu", "block_gemm.cu", "model.cu", "distributed.cu", "kser.cpp", "wavefront.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo",
          "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr", "-ccbin", "/usr/bin/g++"]
@@ -37,10 +37,10 @@ def _nccl_dir():
 _NCCL = _nccl_dir()
 if _NCCL:
     FLAGS += ["-I" + os.path.join(_NCCL, "include")]
-    LIBS = ["-lcublas", "-L" + os.path.join(_NCCL, "lib"), "-l:libnccl.so.2",
+    LIBS = ["-L" + os.path.join(_NCCL, "lib"), "-l:libnccl.so.2",
             "-Xlinker", "-rpath=" + os.path.join(_NCCL, "lib")]
 else:
-    LIBS = ["-lcublas", "-lnccl"]
+    LIBS = ["-lnccl"]
 
 
 def _headers():

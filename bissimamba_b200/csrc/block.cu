@@ -9,7 +9,6 @@
 // epilogue applies silu / softplus+clamp / sigmoid / biases and writes the
 // block-scan inputs; the backward mirrors it.  The backward is exact: it also
 // produces dW_in and the projection paths of dx, which the reference skips.
-#include <cublas_v2.h>
 #include <cuda_bf16.h>
 #include <algorithm>
 #include <cstring>
@@ -234,9 +233,9 @@ __global__ void block_out_bf16(const __nv_bfloat16* __restrict__ x, const float*
     out[i] = __float2bfloat16_rn(__bfloat162float(x[i]) + acc);
 }
 
-__global__ void fill_value(float* p, long long n, float v) {
+__global__ void sub_inplace(float* __restrict__ y, const float* __restrict__ x, long long n) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) p[i] = v;
+    if (i < n) y[i] -= x[i];
 }
 
 int* device_status();
@@ -253,18 +252,24 @@ cudaError_t launch_dx_tc(const __nv_bfloat16* dP, int ldp, const float* Win, con
                          const float* WB, const float* WC, __nv_bfloat16* Wt, long long BL, int dim, int R, int NR,
                          const __nv_bfloat16* dout, __nv_bfloat16* dx, int* status, cudaStream_t st);
 
-static thread_local std::map<int, cublasHandle_t> tl_cublas;
-static cublasHandle_t cublas_for(cudaStream_t st) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cublasHandle_t& h = tl_cublas[dev];
-    if (!h) {
-        if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return nullptr;
-        cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH);  // strict fp32: no TF32 or reduced-precision paths
-    }
-    cublasSetStream(h, st);
-    return h;
-}
+// matrix products of the block (block_gemm.cu): tensor cores for the large ones, own kernels for rank R
+cudaError_t mm_nt(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
+                  long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st);
+cudaError_t mm_tn(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
+                  long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st);
+cudaError_t rank_rows(bool bf16, const void* X, const float* W, long long rows, int dim, int R, float* out,
+                      cudaStream_t st);
+cudaError_t rank_outer(bool bf16, const void* X, const float* Y, long long rows, int dim, int R, float* G,
+                       cudaStream_t st);
+cudaError_t col_sums(const float* X, long long rows, int dim, float* g, cudaStream_t st);
+cudaError_t rank_bwd(bool bf16, const void* X, const float* W, const float* Y, long long rows, int dim, int R,
+                     float* dy, float* G, cudaStream_t st);
+cudaError_t out_rank(const float* x, const float* y, const float* W, long long rows, int dim, int R, float* out,
+                     cudaStream_t st);
+cudaError_t gemm_transpose_f32(const float* in, float* out, long long R, long long Cn, long long ldi, long long ldo,
+                               cudaStream_t st);
+cudaError_t launch_pack_wcat_t(const float* Win, const float* dp, const float* lp, const float* WB, const float* WC,
+                               int R, int NR, int dim, int ldp, __nv_bfloat16* out, cudaStream_t st);
 
 static inline unsigned nb(long long n, int t) { return (unsigned)((n + t - 1) / t); }
 
@@ -312,12 +317,9 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     if (check_cfg(c, w, batch)) return -1;
     if (!x || !out || !act) return set_error("kmb_block_forward: x, out, act required");
     cudaStream_t st = (cudaStream_t)stream;
-    cublasHandle_t hb = cublas_for(st);
-    if (!hb) return set_error("cuBLAS initialisation failed");
     const ActLayout a = act_layout(c, batch);
     float* W = pack_wcat(c, w, st);
     if (!W) return set_error("kmb_block_forward: weight packing failed");
-    const float one = 1.0f, zero = 0.0f;
     const int dim = (int)c->dim;
     const bool bf = c->bf16_storage != 0;
     cudaError_t e;
@@ -326,7 +328,7 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
         __nv_bfloat16* Wb = (__nv_bfloat16*)workspace(WS_BLK_WBF, (size_t)a.Rt * dim * sizeof(__nv_bfloat16));
         if (!Wb) return set_error("workspace allocation failed");
         typedef __nv_bfloat16 H;
-        // tensor-core projection with the epilogue fused (tcgen05); cuBLAS + epilogue otherwise
+        // tensor-core projection with the epilogue fused (tcgen05); the plain tensor-core GEMM + epilogue otherwise
         int* status = device_status();
         if (status && !tl_no_tc) {
             cudaMemsetAsync(status, 0, sizeof(int), st);
@@ -342,18 +344,15 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
         if (e == cudaSuccess) goto scan;
         cudaGetLastError();
         to_bf16<<<nb(a.Rt * dim, 256), 256, 0, st>>>(W, Wb, a.Rt * dim);
-        if (cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, (int)a.Rt, (int)a.BL, dim, &one, Wb, CUDA_R_16BF, dim, x,
-                         CUDA_R_16BF, dim, &zero, act + a.proj, CUDA_R_32F, (int)a.Rt, CUBLAS_COMPUTE_32F,
-                         CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
-            return set_error("bf16 projection GEMM failed");
+        if ((e = mm_nt(true, a.BL, a.Rt, dim, x, dim, Wb, dim, act + a.proj, a.Rt, false, st)) != cudaSuccess)
+            return set_cuda_error("bf16 projection GEMM", e);
         block_fwd_epilogue<H><<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(
             act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, (H*)(act + a.u),
             (H*)(act + a.dt), (H*)(act + a.lam), (H*)(act + a.B), (H*)(act + a.C));
     } else {
-        // P^T[Rt, BL] = Wcat[Rt, dim] . X^T
-        if (cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, (int)a.Rt, (int)a.BL, dim, &one, W, dim, x, dim, &zero,
-                        act + a.proj, (int)a.Rt) != CUBLAS_STATUS_SUCCESS)
-            return set_error("projection GEMM failed");
+        // P[BL, Rt] = X[BL, dim] . Wcat^T on the tensor cores at fp32 accuracy (3xTF32)
+        if ((e = mm_nt(false, a.BL, a.Rt, dim, x, dim, W, dim, act + a.proj, a.Rt, false, st)) != cudaSuccess)
+            return set_cuda_error("projection GEMM", e);
         block_fwd_epilogue<float><<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(
             act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, act + a.u, act + a.dt,
             act + a.lam, act + a.B, act + a.C);
@@ -386,12 +385,9 @@ scan:
         e = cudaGetLastError();
         return e == cudaSuccess ? 0 : set_cuda_error("bf16 output", e);
     }
-    // out = x + y . W_out^T
-    if ((e = cudaMemcpyAsync(out, x, (size_t)a.BL * dim * sizeof(float), cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
-        return set_cuda_error("residual copy", e);
-    if (cublasSgemm(hb, CUBLAS_OP_T, CUBLAS_OP_N, dim, (int)a.BL, (int)c->R, &one, w->W_out, (int)c->R,
-                    act + a.y, (int)c->R, &one, out, dim) != CUBLAS_STATUS_SUCCESS)
-        return set_error("output projection GEMM failed");
+    // out = x + y . W_out^T (rank R: one elementwise pass)
+    if ((e = out_rank(x, act + a.y, w->W_out, a.BL, dim, (int)c->R, out, st)) != cudaSuccess)
+        return set_cuda_error("output projection", e);
     return 0;
 }
 
@@ -399,30 +395,24 @@ scan:
 static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, const float* x, const float* dout,
                               float* dx, const KMBlockGrads* g, long batch, const float* act, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
-    cublasHandle_t hb = cublas_for(st);
-    if (!hb) return set_error("cuBLAS initialisation failed");
     const ActLayout a = act_layout(c, batch);
     const int dim = (int)c->dim, R = (int)c->R;
     const long long BL = a.BL, NR = a.NR, Rt = a.Rt;
-    // scratch: dy[BL,R] | du[BL,R] | ddt[BL] | dlam[BL] | dB[BL,NR] | dC[BL,NR] | dP[BL,Rt] | G[Rt,dim] | ones[BL]
+    // scratch: dy[BL,R] | du[BL,R] | ddt[BL] | dlam[BL] | dB[BL,NR] | dC[BL,NR] | dP[BL,Rt] | G[Rt,dim] | Wcat^T
     size_t o = 0;
     auto take = [&](size_t n) { size_t r = o; o += (n + 63) & ~(size_t)63; return r; };
     const size_t s_dy = take(BL * R), s_du = take(BL * R), s_ddt = take(BL), s_dlam = take(BL);
-    const size_t s_dB = take(BL * NR), s_dC = take(BL * NR), s_dP = take(BL * Rt), s_G = take(Rt * dim);
-    const size_t s_one = take(BL);
+    const long long ldq = (Rt + 3) & ~3LL;   // dP and Wcat^T row stride: 16-byte rows for the tensor-core loads
+    const size_t s_dB = take(BL * NR), s_dC = take(BL * NR), s_dP = take(BL * ldq), s_G = take(Rt * dim);
+    const size_t s_WT = take((size_t)dim * ldq);
     float* S = (float*)workspace(WS_BLK_SCRATCH, o * sizeof(float));
     if (!S) return set_error("workspace allocation failed");
     float* W = pack_wcat(c, w, st);
     if (!W) return set_error("kmb_block_backward: weight packing failed");
-    const float one = 1.0f, zero = 0.0f;
     cudaError_t e;
-    // d_y[BL,R] = dout . W_out ; gW_out += dout^T . y
-    if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_N, R, (int)BL, dim, &one, w->W_out, R, dout, dim, &zero, S + s_dy, R) !=
-        CUBLAS_STATUS_SUCCESS)
-        return set_error("dy GEMM failed");
-    if (g->W_out && cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_T, R, dim, (int)BL, &one, act + a.y, R, dout, dim, &one,
-                                g->W_out, R) != CUBLAS_STATUS_SUCCESS)
-        return set_error("dW_out GEMM failed");
+    // d_y[BL,R] = dout . W_out ; gW_out += dout^T . y   (rank R, one pass over dout)
+    if ((e = rank_bwd(false, dout, w->W_out, act + a.y, BL, dim, R, S + s_dy, g->W_out, st)) != cudaSuccess)
+        return set_cuda_error("dy / dW_out", e);
     KMBlockScanParams p;
     memset(&p, 0, sizeof p);
     p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;
@@ -434,37 +424,31 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
     // du, ddt, dlambda, dB, dC are assigned (no clearing of the scratch first)
     if (kmb_blockscan_backward_ex(&p, batch, S + s_dy, &sg, 1, stream)) return -1;
-    block_bwd_epilogue<float, float><<<nb(BL * Rt, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
-                                                                    (int)NR, c->dt_min, c->dt_max, S + s_du,
-                                                                    S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
-                                                                    S + s_dP, (int)Rt);
+    block_bwd_epilogue<float, float><<<nb(BL * ldq, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
+                                                                     (int)NR, c->dt_min, c->dt_max, S + s_du,
+                                                                     S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
+                                                                     S + s_dP, (int)ldq);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
-    // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
-    if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, &one, x, dim, S + s_dP, (int)Rt, &zero,
-                    S + s_G, dim) != CUBLAS_STATUS_SUCCESS)
-        return set_error("dWcat GEMM failed");
+    // G[Rt, dim] = dP^T . X (tensor cores, K = BL split over the SMs) -> scatter into the projection gradients
+    if ((e = mm_tn(false, Rt, dim, BL, S + s_dP, ldq, x, dim, S + s_G, dim, false, st)) != cudaSuccess)
+        return set_cuda_error("dWcat GEMM", e);
     block_scatter_grads<<<nb(Rt * dim, 256), 256, 0, st>>>(S + s_G, R, (int)NR, dim, g->W_in, g->delta_proj,
                                                            g->lambda_proj, g->W_B, g->W_C);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("grad scatter", e);
-    // bias gradients: column sums of dB, dC (GEMV with a ones vector, += into the gradients)
-    if (g->b_B || g->b_C) {
-        fill_value<<<nb(BL, 256), 256, 0, st>>>(S + s_one, BL, 1.0f);
-        if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("fill", e);
-        if (g->b_B && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dB, (int)NR, S + s_one, 1, &one,
-                                  g->b_B, 1) != CUBLAS_STATUS_SUCCESS)
-            return set_error("db_B GEMV failed");
-        if (g->b_C && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dC, (int)NR, S + s_one, 1, &one,
-                                  g->b_C, 1) != CUBLAS_STATUS_SUCCESS)
-            return set_error("db_C GEMV failed");
-    }
+    // bias gradients: column sums of dB, dC (+= into the gradients)
+    if (g->b_B && (e = col_sums(S + s_dB, BL, (int)NR, g->b_B, st)) != cudaSuccess) return set_cuda_error("db_B", e);
+    if (g->b_C && (e = col_sums(S + s_dC, BL, (int)NR, g->b_C, st)) != cudaSuccess) return set_cuda_error("db_C", e);
     if (dx) {
         // dx may alias dout (the reference model passes one buffer for both): dout is last read above
         if (dx != dout && (e = cudaMemcpyAsync(dx, dout, (size_t)BL * dim * sizeof(float), cudaMemcpyDeviceToDevice, st)) !=
             cudaSuccess)
             return set_cuda_error("dx copy", e);
-        if (cublasSgemm(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, &one, W, dim, S + s_dP, (int)Rt, &one, dx,
-                        dim) != CUBLAS_STATUS_SUCCESS)
-            return set_error("dx GEMM failed");
+        // dx += dP[BL, Rt] . Wcat[Rt, dim]: the B operand is Wcat^T [dim, Rt] (row stride ldq; the loads
+        // past column Rt read zeros)
+        if ((e = gemm_transpose_f32(W, S + s_WT, Rt, dim, dim, ldq, st)) != cudaSuccess)
+            return set_cuda_error("Wcat^T", e);
+        if ((e = mm_nt(false, BL, dim, Rt, S + s_dP, ldq, S + s_WT, ldq, dx, dim, true, st)) != cudaSuccess)
+            return set_cuda_error("dx GEMM", e);
     }
     return 0;
 }
@@ -485,23 +469,15 @@ __global__ void residual_bf16(const __nv_bfloat16* dout, const float* __restrict
     }
 }
 
-static cublasStatus_t gemm_bf16(cublasHandle_t hb, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
-                                const void* A, int lda, const void* B, int ldb, float beta, float* C, int ldc) {
-    const float one = 1.0f;
-    return cublasGemmEx(hb, ta, tb, m, n, k, &one, A, CUDA_R_16BF, lda, B, CUDA_R_16BF, ldb, &beta, C, CUDA_R_32F,
-                        ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-}
-
-// bf16-storage backward: x, dout, dx bf16; the four gradient GEMMs run as
-// bf16 x bf16 -> fp32 on the tensor cores (dP and the small operands y, W_out
-// rounded to bf16), the scan backward and every gradient accumulate in fp32.
+// bf16-storage backward: x, dout, dx bf16; dWcat and dx run as bf16 x bf16 ->
+// fp32 on the tensor cores (dP rounded to bf16), the rank-R products (dy, dW_out)
+// read the bf16 dout with fp32 y and W_out; the scan backward and every
+// gradient accumulate in fp32.
 static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, const __nv_bfloat16* x,
                                const __nv_bfloat16* dout, __nv_bfloat16* dx, const KMBlockGrads* g, long batch,
                                const float* act, void* stream) {
     typedef __nv_bfloat16 H;
     cudaStream_t st = (cudaStream_t)stream;
-    cublasHandle_t hb = cublas_for(st);
-    if (!hb) return set_error("cuBLAS initialisation failed");
     const ActLayout a = act_layout(c, batch);
     const int dim = (int)c->dim, R = (int)c->R;
     const long long BL = a.BL, NR = a.NR, Rt = a.Rt;
@@ -518,15 +494,11 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     if (!S) return set_error("workspace allocation failed");
     H *dPb = (H*)(S + s_dP), *yb = (H*)(S + s_yb), *wob = (H*)(S + s_wo), *Wb = (H*)(S + s_wb);
     cudaError_t e;
-    to_bf16<<<nb(BL * R, 256), 256, 0, st>>>(act + a.y, yb, BL * R);
-    to_bf16<<<nb((long long)dim * R, 256), 256, 0, st>>>(w->W_out, wob, (long long)dim * R);
-    // d_y[BL,R] = dout . W_out ; gW_out += dout^T . y
-    if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_N, R, (int)BL, dim, wob, R, dout, dim, 0.0f, S + s_dy, R) !=
-        CUBLAS_STATUS_SUCCESS)
-        return set_error("dy GEMM failed");
-    if (g->W_out && gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, R, dim, (int)BL, yb, R, dout, dim, 1.0f, g->W_out, R) !=
-                        CUBLAS_STATUS_SUCCESS)
-        return set_error("dW_out GEMM failed");
+    (void)yb;
+    (void)wob;
+    // d_y[BL,R] = dout . W_out ; gW_out += dout^T . y   (rank R, one pass over dout)
+    if ((e = rank_bwd(true, dout, w->W_out, act + a.y, BL, dim, R, S + s_dy, g->W_out, st)) != cudaSuccess)
+        return set_cuda_error("dy / dW_out", e);
     KMBlockScanParams p;
     memset(&p, 0, sizeof p);
     p.ndims = c->ndims; p.dims = c->dims; p.L = c->L; p.N = c->N; p.R = c->R;
@@ -544,26 +516,18 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
         act + a.proj, (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max, S + s_du, S + s_ddt,
         S + s_dlam, S + s_dB, S + s_dC, dPb, ldp);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
-    // G[Rt, dim] = dP^T . X  -> scatter into the projection gradients
-    if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_T, dim, (int)Rt, (int)BL, x, dim, dPb, ldp, 0.0f, S + s_G, dim) !=
-        CUBLAS_STATUS_SUCCESS)
-        return set_error("dWcat GEMM failed");
+    // G[Rt, dim] = dP^T . X (tensor cores, K = BL split over the SMs) -> scatter into the projection gradients
+    if ((e = mm_tn(true, Rt, dim, BL, dPb, ldp, x, dim, S + s_G, dim, false, st)) != cudaSuccess)
+        return set_cuda_error("dWcat GEMM", e);
     block_scatter_grads<<<nb(Rt * dim, 256), 256, 0, st>>>(S + s_G, R, (int)NR, dim, g->W_in, g->delta_proj,
                                                            g->lambda_proj, g->W_B, g->W_C);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("grad scatter", e);
-    const float one = 1.0f;
-    if (g->b_B || g->b_C) {
-        fill_value<<<nb(BL, 256), 256, 0, st>>>(S + s_one, BL, 1.0f);
-        if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("fill", e);
-        if (g->b_B && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dB, (int)NR, S + s_one, 1, &one,
-                                  g->b_B, 1) != CUBLAS_STATUS_SUCCESS)
-            return set_error("db_B GEMV failed");
-        if (g->b_C && cublasSgemv(hb, CUBLAS_OP_N, (int)NR, (int)BL, &one, S + s_dC, (int)NR, S + s_one, 1, &one,
-                                  g->b_C, 1) != CUBLAS_STATUS_SUCCESS)
-            return set_error("db_C GEMV failed");
-    }
+    (void)s_one;
+    if (g->b_B && (e = col_sums(S + s_dB, BL, (int)NR, g->b_B, st)) != cudaSuccess) return set_cuda_error("db_B", e);
+    if (g->b_C && (e = col_sums(S + s_dC, BL, (int)NR, g->b_C, st)) != cudaSuccess) return set_cuda_error("db_C", e);
     if (dx) {
-        // dx = dout + dP Wcat: tensor cores with the residual fused (tcgen05), else cuBLAS + residual kernel
+        // dx = dout + dP Wcat: tensor cores with the residual fused (tcgen05), else the plain tensor-core GEMM
+        // and a residual kernel
         int* status = device_status();
         if (status && !tl_no_tc) {
             cudaMemsetAsync(status, 0, sizeof(int), st);
@@ -576,12 +540,12 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
         tl_dx_path = e == cudaSuccess ? 1 : 0;
         if (e != cudaSuccess) {
             cudaGetLastError();
-            float* W = pack_wcat(c, w, st);
-            if (!W) return set_error("kmb_block_backward: weight packing failed");
-            to_bf16<<<nb(Rt * dim, 256), 256, 0, st>>>(W, Wb, Rt * dim);
-            if (gemm_bf16(hb, CUBLAS_OP_N, CUBLAS_OP_N, dim, (int)BL, (int)Rt, Wb, dim, dPb, ldp, 0.0f, S + s_D,
-                          dim) != CUBLAS_STATUS_SUCCESS)
-                return set_error("dx GEMM failed");
+            // Wt = Wcat^T [dim, ldp] bf16 (zero columns past Rt), then D[BL, dim] = dP . Wt^T
+            if ((e = launch_pack_wcat_t(w->W_in, w->delta_proj, w->lambda_proj, w->W_B, w->W_C, R, (int)NR, dim, ldp,
+                                        Wb, st)) != cudaSuccess)
+                return set_cuda_error("Wcat^T", e);
+            if ((e = mm_nt(true, BL, dim, ldp, dPb, ldp, Wb, ldp, S + s_D, dim, false, st)) != cudaSuccess)
+                return set_cuda_error("dx GEMM", e);
             residual_bf16<<<nb((BL * dim + 7) / 8, 256), 256, 0, st>>>(dout, S + s_D, dx, BL * dim);
         }
     }
@@ -677,9 +641,7 @@ extern "C" void cuda_block_forward(void* cublas, const float* d_W_in, const floa
     cudaMemcpyAsync(d_y_scan, act + a.y, (size_t)L * c.R * f, cudaMemcpyDeviceToDevice, 0);
     if (d_y_proj) {  // y_proj = y - x
         cudaMemcpyAsync(d_y_proj, d_y, (size_t)L * dim * f, cudaMemcpyDeviceToDevice, 0);
-        const float m1 = -1.0f;
-        cublasHandle_t hb = cublas_for(0);
-        if (hb) cublasSaxpy(hb, L * dim, &m1, d_x, 1, d_y_proj, 1);
+        sub_inplace<<<nb((long long)L * dim, 256), 256>>>(d_y_proj, d_x, (long long)L * dim);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) set_cuda_error("cuda_block_forward", e);

@@ -80,7 +80,7 @@ bool force_generic() {
 }
 
 // ---------------------------------------------------------------- workspace
-enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 12 };  // 4: blockscan, 5-10: block
+enum WsSlot { WS_SCRATCH = 0, WS_STAGE = 1, WS_STATUS = 2, WS_NSLOTS = 20 };  // 3-4: blockscan, 5-10: block, 11 + 14: distributed, 12, 13, 15, 16: GEMMs
 struct Ws {
     void* p = nullptr;
     size_t n = 0;

@@ -254,7 +254,7 @@ int kmb_dist_allgather_async(KMambaDistributedContext* ctx, const float* send, f
     }
     if (getenv("KMB_DIST_CHECK")) {
         // every rank must pass the same count (a mismatch would hang NCCL): compare max and min first
-        double* chk = (double*)kmb::workspace(3, 256);
+        double* chk = (double*)kmb::workspace(14, 256);
         if (!chk) return kmb::set_error("kmb_dist_allgather_async: workspace allocation failed");
         const double v[2] = {(double)count, -(double)count};
         double got[2];
@@ -350,7 +350,7 @@ float kmb_dist_model_train_step(KMambaDistributedContext* ctx, KMamba* m, const 
     // gradient of the global mean loss: each rank's local mean weighted by its share, summed
     dist_scale<<<blocks(n), 256, 0, st>>>(g, n, share);
     if (kmb_dist_allreduce_async(ctx, g, n, 1.0f, st)) return NAN;
-    float* lt = (float*)kmb::workspace(3, 256);
+    float* lt = (float*)kmb::workspace(14, 256);
     if (!lt) {
         kmb::set_error("kmb_dist_model_train_step: workspace allocation failed");
         return NAN;

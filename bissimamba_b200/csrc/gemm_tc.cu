@@ -1,0 +1,641 @@
+// gemm_tc.cu -- the block and model GEMMs on the sm_100a tensor cores
+// (tcgen05), in place of library GEMMs:
+//
+//   D[m, n] (+)= sum_k A[m, k] B[n, k]
+//
+// Operands are K-major ([rows, K] row-major) or, for 16-bit kinds, MN-major
+// ([K, rows] row-major: the transposed product A^T B of two row-major
+// matrices needs no transposition pass).  Kinds, by the pieces each operand
+// is given as:
+//   KIND_BF16    one bf16 piece, kind::f16 MMAs;
+//   KIND_TF32X3  fp32 at fp32 accuracy, two fp32 pieces hi = rna_tf32(x) and
+//                lo = rna_tf32(x - hi): hi_a lo_b + lo_a hi_b + hi_a hi_b
+//                (kind::tf32), a relative error of about 2^-22 per product;
+//   KIND_BF16X6  fp32 at fp32 accuracy, three bf16 pieces x = b0 + b1 + b2
+//                (each the bf16 rounding of what the previous ones leave; the
+//                remainder is below 2^-26 |x|), the six products of order
+//                <= 2, smallest first, kind::f16 (the split-bf16 emulation of
+//                an fp32 GEMM: Henry, Tang, Heinecke, "Leveraging the bfloat16
+//                artificial intelligence datatype for higher-precision
+//                computations", ARITH 2019);
+//   KIND_BF16X9  the same with all nine products.
+// One CTA per 128-row tile of A and up to 256 columns of B (one TMEM
+// accumulator); grid.x walks the column tiles, so the CTAs that share an A
+// tile run together and read it from L2.  Warp 0 issues TMA loads (128-byte
+// swizzled tiles, 128 bytes of K per K-major row or 64 K rows per MN-major
+// tile, a ring of stages), warp 1 allocates TMEM and issues the MMAs, warps
+// 2-5 read the accumulator back (tcgen05.ld) and store.
+// The fp32 kinds do not let one TMEM accumulator run over all of K: the
+// tensor core's accumulation drifts with the number of products it adds (its
+// error grows about as sqrt(K) relative to sum |a b|, where an fp32 FMA loop's
+// stays flat).  The MMA warp accumulates `kflush` MMA K steps (16 bf16 or 8
+// tf32 K each) into one of two TMEM buffers, and the epilogue warps add every
+// finished buffer into an fp32 running sum in registers while the next one
+// accumulates.
+// Split-K: grid.z cuts K into chunks; each split writes its own partial
+// (EPI_STORE at D + split * split_stride), summed later in a fixed order.
+// EPI_ADD adds the accumulator into D (one split).  Every wait is bounded; on a
+// timeout the kernel records a status, drains its copies and frees its TMEM.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include "kmb_common.cuh"
+#include "kmb_sync.cuh"
+#include "kmb_gemm.cuh"
+
+namespace kmb {
+
+bool tmap_encode_ex(CUtensorMap* m, const void* base, int dtype, int rank, const unsigned long long* dims,
+                    const unsigned long long* strides_bytes, const unsigned* box, int swizzle);
+
+enum { KIND_BF16 = 0, KIND_TF32X3 = 1, KIND_BF16X6 = 2, KIND_BF16X9 = 3 };
+enum { EPI_STORE = 0, EPI_ADD = 1 };
+
+struct GemmTCDesc {
+    long long M, N, K;
+    long long kchunk;          // K per split (a multiple of the stage depth)
+    int ncols_max;             // columns per CTA (<= 256)
+    int stages, a_bytes, b_bytes, stage_bytes;
+    unsigned mn_lbo, mn_sbo;   // MN-major descriptor strides (bytes)
+    int kflush;                // fp32 kinds: MMA K steps per TMEM buffer (1, 2 or 4)
+    float* D;
+    long long ldd;
+    long long split_stride;    // elements between the splits' partial outputs
+    int* status;
+};
+
+namespace {
+
+template <int KIND> struct KindTraits;
+template <> struct KindTraits<KIND_BF16> { static constexpr int NP = 1, ESZ = 2, NPROD = 1; };
+template <> struct KindTraits<KIND_TF32X3> { static constexpr int NP = 2, ESZ = 4, NPROD = 3; };
+template <> struct KindTraits<KIND_BF16X6> { static constexpr int NP = 3, ESZ = 2, NPROD = 6; };
+template <> struct KindTraits<KIND_BF16X9> { static constexpr int NP = 3, ESZ = 2, NPROD = 9; };
+
+// piece pairs (a, b), smallest products first, the leading product last
+__device__ __forceinline__ void prod_pair(int kind, int i, int& pa, int& pb) {
+    if (kind == KIND_BF16) { pa = 0; pb = 0; return; }
+    if (kind == KIND_TF32X3) {
+        const int a[3] = {1, 0, 0}, b[3] = {0, 1, 0};
+        pa = a[i]; pb = b[i];
+        return;
+    }
+    // x9: (2,2) (2,1) (1,2) then the x6 list (2,0) (1,1) (0,2) (1,0) (0,1) (0,0)
+    const int a[9] = {2, 2, 1, 2, 1, 0, 1, 0, 0}, b[9] = {2, 1, 2, 0, 1, 2, 0, 1, 0};
+    const int off = kind == KIND_BF16X9 ? 0 : 3;
+    pa = a[off + i]; pb = b[off + i];
+}
+
+__device__ __forceinline__ void g_tma_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(c0), "r"(c1) : "memory");
+}
+// 128-byte swizzled shared-memory matrix descriptor (sm_100 form: bit 46 set, swizzle mode 2 in bits 61-63).
+// K-major: 8-row groups 1024 B apart (SBO), LBO unused.  MN-major: LBO = bytes between 64-element
+// MN blocks, SBO = bytes between 8-row K groups.
+__device__ __forceinline__ uint64_t g_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    const uint64_t lo = (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16);
+    const uint64_t hi = (uint64_t)((sbo >> 4) & 0x3FFF) | ((uint64_t)1 << 14) | ((uint64_t)2 << 29);
+    return lo | (hi << 32);
+}
+// instruction descriptor: fp32 accumulator, A / B format (1 = bf16, 2 = tf32), major-ness (bit 15 A,
+// bit 16 B: 1 = MN-major), N, M = 128
+__device__ __forceinline__ uint32_t g_idesc(int fmt, int n, bool mn) {
+    return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | (mn ? (3u << 15) : 0u) |
+           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+template <int KIND>
+__device__ __forceinline__ void g_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, bool acc) {
+    if constexpr (KIND == KIND_TF32X3)
+        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                     "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                     ::"r"(d), "l"(a), "l"(b), "r"(id), "r"((uint32_t)acc) : "memory");
+    else
+        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                     "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                     ::"r"(d), "l"(a), "l"(b), "r"(id), "r"((uint32_t)acc) : "memory");
+}
+__device__ __forceinline__ void g_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void g_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// 64 consecutive TMEM columns of this warp's 32 lanes, waited for inside the same asm
+__device__ __forceinline__ void g_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, "
+        "%36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, "
+        "%57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// The epilogue's 128 threads (warps 2-5) write a 128 x 128 fp32 block through shared memory so that
+// global stores are whole 128-byte rows: row-major tile with a 129-float stride (conflict-free both ways).
+constexpr int EPI_LD = 129;
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+template <int EPI>
+__device__ __forceinline__ void epi_flush(float* tile, int q, const float* vals, int cols_here, float* D, long long ldd,
+                                          long long m0, long long M, long long col0, long long N, int lane,
+                                          bool write) {
+    // every epilogue thread reaches both barriers; `write` only gates the stores
+    const int rl = q * 32 + lane;
+#pragma unroll
+    for (int c = 0; c < 128; c++)
+        if (c < cols_here) tile[rl * EPI_LD + c] = vals[c];
+    epi_bar();
+    // warp q writes rows q*32 .. q*32+31, lanes along the columns
+    for (int i = 0; i < 32 && write; i++) {
+        const int r = q * 32 + i;
+        const long long row = m0 + r;
+        if (row >= M) break;
+        float* drow = D + row * ldd;
+        for (int c = lane; c < cols_here; c += 32) {
+            const long long col = col0 + c;
+            if (col < N) {
+                if (EPI == EPI_ADD) drow[col] += tile[r * EPI_LD + c];
+                else drow[col] = tile[r * EPI_LD + c];
+            }
+        }
+    }
+    epi_bar();
+}
+
+constexpr int GT_THREADS = 192;
+
+// Stage layout: A pieces 0..NP-1 (a_bytes each), then B pieces (b_bytes each).
+// K-major: one TMA box per piece and operand ([128 or ncols rows] x 128 B).
+// MN-major: boxes of 64 elements (128 B) x 64 K rows, 8 KB each, side by side.
+template <int KIND, int EPI, bool MN>
+__global__ void __launch_bounds__(GT_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUtensorMap mA0,
+               const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mA2,
+               const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1,
+               const __grid_constant__ CUtensorMap mB2) {
+    using TR = KindTraits<KIND>;
+    constexpr int NP = TR::NP;
+    constexpr int KS = MN ? 64 : 128 / TR::ESZ;   // K elements per stage
+    extern __shared__ __align__(1024) unsigned char g_smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)g_smem_raw + 1023) & ~(uintptr_t)1023);
+    const int S = d.stages;
+    uint64_t* full = (uint64_t*)(smem + (size_t)S * d.stage_bytes);
+    uint64_t* empty = full + S;
+    uint64_t* done = empty + S;
+    uint32_t* tmem_slot = (uint32_t*)(done + 5);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long n0 = (long long)blockIdx.x * d.ncols_max;
+    const long long m0 = (long long)blockIdx.y * 128;
+    const int ncols = (int)min((long long)d.ncols_max, ((d.N + 15) & ~15LL) - n0);   // multiple of 16
+    const long long k0 = (long long)blockIdx.z * d.kchunk;
+    const long long k1 = min(d.K, k0 + d.kchunk);
+    const int nkb = k1 > k0 ? (int)((k1 - k0 + KS - 1) / KS) : 0;
+    constexpr bool FL = KIND != KIND_BF16;   // stage-wise accumulator flush (ncols <= 128)
+    const int tcols = FL ? 256 : ncols <= 32 ? 32 : ncols <= 64 ? 64 : ncols <= 128 ? 128 : 256;
+    uint64_t* tfull = done + 1;     // FL: TMEM buffer b holds a finished stage
+    uint64_t* tempty = done + 3;    // FL: the epilogue has read TMEM buffer b
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) {
+            mbar_init(smem_u32(&full[i]), 1);
+            mbar_init(smem_u32(&empty[i]), 1);
+        }
+        mbar_init(smem_u32(done), 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(smem_u32(&tfull[b]), 1);
+            mbar_init(smem_u32(&tempty[b]), 4);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(tcols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // rows past M or N and K past the end arrive zero-filled and count in the transaction bytes
+            const CUtensorMap* ma[3] = {&mA0, &mA1, &mA2};
+            const CUtensorMap* mb[3] = {&mB0, &mB1, &mB2};
+            const int nbb = MN ? (ncols + 63) / 64 : 1;   // MN-major B boxes of this CTA
+            const unsigned bytes = (unsigned)(NP * (d.a_bytes + (MN ? nbb * 8192 : d.b_bytes)));
+            int issued = 0;
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % S;
+                if (kb >= S && !mbar_wait(smem_u32(&empty[s]), (uint32_t)(((kb / S) - 1) & 1))) {
+                    set_status(d.status, KMB_ERR_TIMEOUT_EMPTY);
+                    break;
+                }
+                unsigned char* st = smem + (size_t)s * d.stage_bytes;
+                const uint32_t fb = smem_u32(&full[s]);
+                const int kc = (int)(k0 + (long long)kb * KS);
+                mbar_expect_tx(fb, bytes);
+#pragma unroll
+                for (int p = 0; p < NP; p++) {
+                    unsigned char* sa = st + p * d.a_bytes;
+                    unsigned char* sb = st + NP * d.a_bytes + p * d.b_bytes;
+                    if (MN) {
+                        g_tma_2d(smem_u32(sa), ma[p], fb, (int)m0, kc);
+                        g_tma_2d(smem_u32(sa + 8192), ma[p], fb, (int)m0 + 64, kc);
+                        for (int bx = 0; bx < nbb; bx++)
+                            g_tma_2d(smem_u32(sb + bx * 8192), mb[p], fb, (int)(n0 + 64 * bx), kc);
+                    } else {
+                        g_tma_2d(smem_u32(sa), ma[p], fb, kc, (int)m0);
+                        g_tma_2d(smem_u32(sb), mb[p], fb, kc, (int)n0);
+                    }
+                }
+                issued = kb + 1;
+            }
+            for (int kb = (issued > S ? issued - S : 0); kb < issued; kb++)
+                mbar_wait(smem_u32(&full[kb % S]), (uint32_t)((kb / S) & 1));
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const int fmt = KIND == KIND_TF32X3 ? 2 : 1;
+            const uint32_t id = g_idesc(fmt, ncols, MN);
+            const uint32_t lbo = MN ? d.mn_lbo : 16u, sbo = MN ? d.mn_sbo : 1024u;
+            const int kf = d.kflush;
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % S;
+                if (!mbar_wait(smem_u32(&full[s]), (uint32_t)((kb / S) & 1))) {
+                    set_status(d.status, KMB_ERR_TIMEOUT_FULL);
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t st = smem_u32(smem + (size_t)s * d.stage_bytes);
+                bool stop = false;
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++) {   // K-major: 32 bytes of K per MMA; MN-major: 16 K rows
+                    const uint32_t o = MN ? ks * 2048 : ks * 32;
+                    const int g = kb * 4 + ks, unit = g / kf;
+                    const bool first = !FL ? (kb == 0 && ks == 0) : (g % kf == 0);
+                    if (FL && first && unit >= 2 &&
+                        !mbar_wait(smem_u32(&tempty[unit & 1]), (uint32_t)(((unit >> 1) - 1) & 1))) {
+                        set_status(d.status, KMB_ERR_TIMEOUT_EMPTY);
+                        stop = true;
+                        break;
+                    }
+                    if (FL && first) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t dt = FL ? tmem + (uint32_t)((unit & 1) * 128) : tmem;
+#pragma unroll
+                    for (int i = 0; i < TR::NPROD; i++) {
+                        int pa, pb;
+                        prod_pair(KIND, i, pa, pb);
+                        const uint32_t a = st + pa * d.a_bytes + o;
+                        const uint32_t b = st + NP * d.a_bytes + pb * d.b_bytes + o;
+                        g_mma<KIND>(dt, g_desc(a, lbo, sbo), g_desc(b, lbo, sbo), id, !first || i > 0);
+                    }
+                    if (FL && g % kf == kf - 1) g_commit(smem_u32(&tfull[unit & 1]));
+                }
+                g_commit(smem_u32(&empty[s]));
+                if (stop) break;
+            }
+            g_commit(smem_u32(done));
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile
+        const int q = warp & 3;
+        if constexpr (FL) {
+            float acc[128];
+#pragma unroll
+            for (int c = 0; c < 128; c++) acc[c] = 0.0f;
+            bool ok = true;
+            const int nunits = nkb * 4 / d.kflush;
+            for (int u = 0; u < nunits; u++) {
+                if (!mbar_wait(smem_u32(&tfull[u & 1]), (uint32_t)((u >> 1) & 1))) {
+                    set_status(d.status, KMB_ERR_TIMEOUT_Y);
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((u & 1) * 128);
+#pragma unroll
+                for (int h = 0; h < 128; h += 64) {
+                    if (h < ncols) {
+                        float v[64];
+                        g_ld64(tb + (uint32_t)h, v);
+#pragma unroll
+                        for (int j = 0; j < 64; j++) acc[h + j] += v[j];
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tempty[u & 1]));
+            }
+            // the last unit's commit covers every MMA; the stages are free for the store tile
+            if (!mbar_wait(smem_u32(done), 0)) { set_status(d.status, KMB_ERR_TIMEOUT_Y); ok = false; }
+            epi_flush<EPI>((float*)smem, q, acc, ncols, d.D + (long long)blockIdx.z * d.split_stride, d.ldd, m0, d.M,
+                           n0, d.N, lane, ok);
+        } else {
+            const bool got = mbar_wait(smem_u32(done), 0);
+            if (!got) set_status(d.status, KMB_ERR_TIMEOUT_Y);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            for (int h = 0; h < ncols; h += 128) {
+                float v[128];
+#pragma unroll
+                for (int j = 0; j < 128; j += 64) {
+                    if (h + j < ncols) g_ld64(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h + j), v + j);
+                    else
+#pragma unroll
+                        for (int i = 0; i < 64; i++) v[j + i] = 0.0f;   // nkb == 0: an empty split stores zeros
+                }
+                if (nkb == 0)
+#pragma unroll
+                    for (int i = 0; i < 128; i++) v[i] = 0.0f;
+                const int cols_here = min(128, ncols - h);
+                epi_flush<EPI>((float*)smem, q, v, cols_here, d.D + (long long)blockIdx.z * d.split_stride, d.ldd, m0,
+                               d.M, n0 + h, d.N, lane, got);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+}
+
+__device__ __forceinline__ float rna_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// hi = rna_tf32(x), lo = rna_tf32(x - hi) (x - hi is exact in fp32); four columns per thread
+// (cols, ldx, ldo multiples of 4)
+__global__ void split_tf32(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                           long long rows, int cols4, long long ldx, long long ldo) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * cols4) return;
+    const long long r = i / cols4;
+    const int c = (int)(i - r * cols4) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    float h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        h[k] = rna_tf32(e[k]);
+        l[k] = rna_tf32(e[k] - h[k]);
+    }
+    *reinterpret_cast<float4*>(hi + r * ldo + c) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + r * ldo + c) = make_float4(l[0], l[1], l[2], l[3]);
+}
+
+// x = b0 + b1 + b2 (+ a remainder below 2^-26 |x|): each piece the bf16 rounding of what is left;
+// four columns per thread (cols, ldx, ldo multiples of 4)
+__global__ void split_bf16x3(const float* __restrict__ x, __nv_bfloat16* __restrict__ b0,
+                             __nv_bfloat16* __restrict__ b1, __nv_bfloat16* __restrict__ b2, long long rows,
+                             int cols4, long long ldx, long long ldo) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * cols4) return;
+    const long long r = i / cols4;
+    const int c = (int)(i - r * cols4) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    __align__(8) __nv_bfloat16 p0[4], p1[4], p2[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        p0[k] = __float2bfloat16_rn(e[k]);
+        const float r1 = e[k] - __bfloat162float(p0[k]);
+        p1[k] = __float2bfloat16_rn(r1);
+        p2[k] = __float2bfloat16_rn(r1 - __bfloat162float(p1[k]));
+    }
+    *reinterpret_cast<uint2*>(b0 + r * ldo + c) = *reinterpret_cast<const uint2*>(p0);
+    *reinterpret_cast<uint2*>(b1 + r * ldo + c) = *reinterpret_cast<const uint2*>(p1);
+    *reinterpret_cast<uint2*>(b2 + r * ldo + c) = *reinterpret_cast<const uint2*>(p2);
+}
+
+// the same one element per thread, for any shape
+__global__ void split_any(int kind, const float* __restrict__ x, void* o0, void* o1, void* o2, long long rows,
+                          long long cols, long long ldx, long long ldo) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * cols) return;
+    const long long r = i / cols, c = i - r * cols;
+    const float v = x[r * ldx + c];
+    if (kind == KIND_TF32X3) {
+        const float h = rna_tf32(v);
+        ((float*)o0)[r * ldo + c] = h;
+        ((float*)o1)[r * ldo + c] = rna_tf32(v - h);
+    } else {
+        const __nv_bfloat16 p0 = __float2bfloat16_rn(v);
+        const float r1 = v - __bfloat162float(p0);
+        const __nv_bfloat16 p1 = __float2bfloat16_rn(r1);
+        ((__nv_bfloat16*)o0)[r * ldo + c] = p0;
+        ((__nv_bfloat16*)o1)[r * ldo + c] = p1;
+        ((__nv_bfloat16*)o2)[r * ldo + c] = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+    }
+}
+
+// out[c, r] = in[r, c]: in is R x Cn (row stride ldi), out Cn x R (row stride ldo); 32 x 32 tiles
+template <typename T>
+__global__ void transpose_2d(const T* __restrict__ in, T* __restrict__ out, long long R, long long Cn, long long ldi,
+                             long long ldo) {
+    __shared__ T t[32][33];
+    const long long r0 = (long long)blockIdx.y * 32, c0 = (long long)blockIdx.x * 32;
+    for (int j = threadIdx.y; j < 32; j += 8) {
+        const long long r = r0 + j, c = c0 + threadIdx.x;
+        if (r < R && c < Cn) t[j][threadIdx.x] = in[r * ldi + c];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += 8) {
+        const long long c = c0 + j, r = r0 + threadIdx.x;   // out row c, column r
+        if (r < R && c < Cn) out[c * ldo + r] = t[threadIdx.x][j];
+    }
+}
+
+// out[i] (+)= sum_s part[s * stride + i], fixed order
+__global__ void gt_reduce_splits(const float* __restrict__ part, float* __restrict__ out, long long n, int nsplit,
+                                 long long stride, int accumulate, long long ldp, long long ldo, long long cols) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const long long r = i / cols, c = i - r * cols;
+    float acc = 0.0f;
+    for (int s = 0; s < nsplit; s++) acc += part[s * stride + r * ldp + c];
+    float* o = out + r * ldo + c;
+    *o = accumulate ? *o + acc : acc;
+}
+
+int g_kflush = 2;
+
+int kind_pieces(int kind) { return kind == KIND_BF16 ? 1 : kind == KIND_TF32X3 ? 2 : 3; }
+
+
+}  // namespace
+
+// D = A B^T on the tensor cores (operands as in GemmOperand; MN-major only for
+// the 16-bit kinds).  nsplit > 1 writes partials to D + s * split_stride.
+// cudaErrorNotSupported when the shapes or alignments do not fit (rows of 16
+// bytes: ld a multiple of 8 bf16 / 4 fp32, pieces 16-byte aligned).
+cudaError_t gemm_tc(int kind, int epi, long long M, long long N, long long K, const GemmOperand& A,
+                    const GemmOperand& B, float* D, long long ldd, int nsplit, long long split_stride, int* status,
+                    cudaStream_t st) {
+    const int NP = kind_pieces(kind);
+    const int esz = kind == KIND_TF32X3 ? 4 : 2;
+    const bool mn = A.mn_major != 0;
+    if (M < 1 || N < 1 || K < 1 || nsplit < 1 || (A.mn_major != B.mn_major) || (mn && esz != 2) ||
+        (A.ld * esz) % 16 || (B.ld * esz) % 16 || (epi == EPI_ADD && nsplit != 1) || M > 0x7fffffffLL ||
+        N > 0x7fffffffLL || K > 0x7fffffffLL)
+        return cudaErrorNotSupported;
+    for (int p = 0; p < NP; p++)
+        if (!A.p[p] || !B.p[p] || ((uintptr_t)A.p[p] & 15) || ((uintptr_t)B.p[p] & 15)) return cudaErrorNotSupported;
+    const int KS = mn ? 64 : 128 / esz;
+    GemmTCDesc d{};
+    d.M = M; d.N = N; d.K = K;
+    // columns per CTA: the (padded) width up to 256, fewer while two stages do not fit the budget
+    // (bf16: two CTAs and two 256-column accumulators per SM, so one tile's epilogue overlaps another's
+    // MMAs; the multi-piece kinds one CTA per SM)
+    const long long npad = mn ? (N + 63) & ~63LL : (N + 15) & ~15LL;
+    const int budget = (kind == KIND_BF16 ? 110 : 200) * 1024;
+    d.a_bytes = 128 * 128;
+    // (the fp32 kinds keep two 128-column TMEM buffers: at most 128 columns)
+    const int ncap = kind == KIND_BF16 ? 256 : 128;
+    int nc = (int)(npad <= ncap ? npad : ncap);
+    for (;;) {
+        d.b_bytes = mn ? ((nc + 63) / 64) * 8192 : nc * 128;
+        d.stage_bytes = NP * (d.a_bytes + d.b_bytes);
+        if (2 * d.stage_bytes <= budget || nc <= 64) break;
+        nc = mn ? nc - 64 : ((nc / 2 + 15) & ~15);
+    }
+    d.ncols_max = nc;
+    d.stages = budget / d.stage_bytes;
+    if (d.stages > 6) d.stages = 6;
+    if (d.stages < 2 || d.stages * d.stage_bytes < 128 * EPI_LD * 4) return cudaErrorNotSupported;
+    const long long kb_total = (K + KS - 1) / KS;
+    d.kchunk = ((kb_total + nsplit - 1) / nsplit) * KS;
+    d.mn_lbo = 8192u;   // the two 64-element halves of a 128-row tile / the B boxes: one 8 KB box apart
+    d.mn_sbo = 1024u;   // 8 K rows of 128 B
+    d.kflush = g_kflush;
+    d.D = D; d.ldd = ldd; d.split_stride = split_stride; d.status = status;
+    const int dt = kind == KIND_TF32X3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap ma[3], mb[3];
+    auto enc = [&](CUtensorMap* m, const void* p, long long rows, long long ld, unsigned boxrows) {
+        if (mn) {   // [K, rows] row-major: inner dimension = rows
+            const unsigned long long dims[2] = {(unsigned long long)rows, (unsigned long long)K};
+            const unsigned long long str[1] = {(unsigned long long)(ld * esz)};
+            const unsigned box[2] = {64u, (unsigned)KS};
+            return tmap_encode_ex(m, p, dt, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        }
+        const unsigned long long dims[2] = {(unsigned long long)K, (unsigned long long)rows};
+        const unsigned long long str[1] = {(unsigned long long)(ld * esz)};
+        const unsigned box[2] = {(unsigned)KS, boxrows};
+        return tmap_encode_ex(m, p, dt, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    };
+    for (int p = 0; p < 3; p++) {
+        if (p < NP) {
+            if (!enc(&ma[p], A.p[p], M, A.ld, 128) || !enc(&mb[p], B.p[p], N, B.ld, (unsigned)d.ncols_max))
+                return cudaErrorNotSupported;
+        } else {
+            ma[p] = ma[0];
+            mb[p] = mb[0];
+        }
+    }
+    const int smem = 1024 + d.stages * d.stage_bytes + (2 * d.stages + 5) * 8 + 16;
+    const dim3 grid((unsigned)((npad + d.ncols_max - 1) / d.ncols_max), (unsigned)((M + 127) / 128), (unsigned)nsplit);
+    if (grid.y > 65535u || grid.z > 65535u) return cudaErrorNotSupported;
+    cudaError_t e = cudaErrorNotSupported;
+#define KMB_GT(KI, EP, MNV)                                                                                 \
+    do {                                                                                                    \
+        e = cudaFuncSetAttribute(gemm_tc_kernel<KI, EP, MNV>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                 smem);                                                                     \
+        if (e != cudaSuccess) return e;                                                                     \
+        gemm_tc_kernel<KI, EP, MNV><<<grid, GT_THREADS, smem, st>>>(d, ma[0], ma[1], ma[2], mb[0], mb[1],   \
+                                                                    mb[2]);                                 \
+        e = cudaGetLastError();                                                                             \
+    } while (0)
+#define KMB_GT_EPI(KI, MNV)                      \
+    do {                                         \
+        if (epi == EPI_ADD) KMB_GT(KI, EPI_ADD, MNV); \
+        else KMB_GT(KI, EPI_STORE, MNV);         \
+    } while (0)
+    switch (kind) {
+        case KIND_BF16: if (mn) KMB_GT_EPI(KIND_BF16, true); else KMB_GT_EPI(KIND_BF16, false); break;
+        case KIND_TF32X3: KMB_GT_EPI(KIND_TF32X3, false); break;
+        case KIND_BF16X6: if (mn) KMB_GT_EPI(KIND_BF16X6, true); else KMB_GT_EPI(KIND_BF16X6, false); break;
+        case KIND_BF16X9: if (mn) KMB_GT_EPI(KIND_BF16X9, true); else KMB_GT_EPI(KIND_BF16X9, false); break;
+        default: return cudaErrorNotSupported;
+    }
+#undef KMB_GT_EPI
+#undef KMB_GT
+    return e;
+}
+
+// Pieces of an fp32 matrix [rows, cols] (row stride ldx) for `kind`, written with row stride ldo:
+// TF32X3 into out[0..1] (fp32), BF16X6 / BF16X9 into out[0..2] (bf16).
+cudaError_t gemm_split(int kind, const float* x, void* const* out, long long rows, long long cols, long long ldx,
+                       long long ldo, cudaStream_t st) {
+    if (rows * cols <= 0) return cudaSuccess;
+    if (kind != KIND_TF32X3 && kind != KIND_BF16X6 && kind != KIND_BF16X9) return cudaErrorInvalidValue;
+    bool vec = cols % 4 == 0 && ldx % 4 == 0 && ldo % 4 == 0 && !((uintptr_t)x & 15);
+    for (int p = 0; p < (kind == KIND_TF32X3 ? 2 : 3); p++) vec = vec && !((uintptr_t)out[p] & 15);
+    if (vec) {
+        const long long n = rows * (cols / 4);
+        const unsigned g = (unsigned)((n + 255) / 256);
+        if (kind == KIND_TF32X3)
+            split_tf32<<<g, 256, 0, st>>>(x, (float*)out[0], (float*)out[1], rows, (int)(cols / 4), ldx, ldo);
+        else
+            split_bf16x3<<<g, 256, 0, st>>>(x, (__nv_bfloat16*)out[0], (__nv_bfloat16*)out[1],
+                                            (__nv_bfloat16*)out[2], rows, (int)(cols / 4), ldx, ldo);
+    } else {
+        const long long n = rows * cols;
+        split_any<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(kind, x, out[0], out[1], out[2], rows, cols, ldx, ldo);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t gemm_transpose_f32(const float* in, float* out, long long R, long long Cn, long long ldi, long long ldo,
+                               cudaStream_t st) {
+    dim3 grid((unsigned)((Cn + 31) / 32), (unsigned)((R + 31) / 32));
+    transpose_2d<float><<<grid, dim3(32, 8), 0, st>>>(in, out, R, Cn, ldi, ldo);
+    return cudaGetLastError();
+}
+cudaError_t gemm_transpose_bf16(const __nv_bfloat16* in, __nv_bfloat16* out, long long R, long long Cn,
+                                long long ldi, long long ldo, cudaStream_t st) {
+    dim3 grid((unsigned)((Cn + 31) / 32), (unsigned)((R + 31) / 32));
+    transpose_2d<__nv_bfloat16><<<grid, dim3(32, 8), 0, st>>>(in, out, R, Cn, ldi, ldo);
+    return cudaGetLastError();
+}
+
+// out[r, c] (+)= sum over splits of part[s][r, c]
+cudaError_t gemm_reduce_splits(const float* part, float* out, long long rows, long long cols, int nsplit,
+                               long long split_stride, long long ldp, long long ldo, int accumulate, cudaStream_t st) {
+    const long long n = rows * cols;
+    gt_reduce_splits<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, out, n, nsplit, split_stride, accumulate, ldp,
+                                                                   ldo, cols);
+    return cudaGetLastError();
+}
+
+// MMA K steps per TMEM buffer of the fp32 kinds (1, 2 or 4); fewer = closer to fp32 FMA accuracy
+int gemm_set_kflush(int k) {
+    if (k != 1 && k != 2 && k != 4) return -1;
+    g_kflush = k;
+    return 0;
+}
+
+}  // namespace kmb

@@ -7,7 +7,6 @@
 // one elementwise launch over the arena and a data-parallel caller all-reduces
 // one contiguous buffer.  The reference trains one sequence at a time
 // (src/kmamba.c:534); here the whole batch goes through each block at once.
-#include <cublas_v2.h>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -23,8 +22,16 @@ namespace kmb {
 int set_error(const char* msg);
 int set_cuda_error(const char* where, cudaError_t e);
 void clear_error();
+void* workspace(int slot, size_t bytes);
+cudaError_t mm_nt(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
+                  long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st);
+cudaError_t mm_tn(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
+                  long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st);
+cudaError_t gemm_transpose_f32(const float* in, float* out, long long R, long long Cn, long long ldi, long long ldo,
+                               cudaStream_t st);
 }
 using namespace kmb;
+enum { WS_HEAD_T = 17 };   // head^T [V, D] for the logits GEMM
 
 struct LayerOfs {
     size_t W_in, W_out, A_log, W_B, W_C, delta_proj, lambda_proj, b_B, b_C, theta;
@@ -48,7 +55,6 @@ struct KMamba {
           *loss = nullptr;
     uint32_t* tok = nullptr;
     size_t act_floats = 0;
-    cublasHandle_t cublas = nullptr;
     std::map<std::string, std::vector<float>> mirror;
 };
 
@@ -261,12 +267,6 @@ KMamba* kmamba_create(const KMambaConfig* cfg) {
     }
     cudaMemset(m->params, 0, o * 4);
     cudaMemset(m->grads, 0, o * 4);
-    if (cublasCreate(&m->cublas) != CUBLAS_STATUS_SUCCESS) {
-        set_error("cuBLAS initialisation failed");
-        kmamba_free(m);
-        return nullptr;
-    }
-    cublasSetMathMode(m->cublas, CUBLAS_PEDANTIC_MATH);
     return m;
 }
 
@@ -275,7 +275,6 @@ void kmamba_free(KMamba* m) {
     cudaFree(m->params); cudaFree(m->grads); cudaFree(m->mom1); cudaFree(m->mom2);
     cudaFree(m->hid); cudaFree(m->blk_act); cudaFree(m->logits); cudaFree(m->dh); cudaFree(m->dh2);
     cudaFree(m->rowloss); cudaFree(m->loss); cudaFree(m->tok);
-    if (m->cublas) cublasDestroy(m->cublas);
     delete m;
 }
 
@@ -409,7 +408,6 @@ int kmamba_enable_training(KMamba* m, const MBOptimConfig* opt, float lr_embed_h
 // forward of `batch` sequences already in m->tok; leaves logits in m->logits
 static int model_forward(KMamba* m, size_t batch, cudaStream_t st) {
     const long long BL = (long long)batch * m->L;
-    const float one = 1.0f, zero = 0.0f;
     embed_gather<<<nblk(BL * m->D, 256), 256, 0, st>>>(m->params, m->tok, BL, (int)m->L, (int)m->D, (int)m->V,
                                                        m->hid);
     KMBlockConfig c = layer_cfg(m);
@@ -419,13 +417,14 @@ static int model_forward(KMamba* m, size_t batch, cudaStream_t st) {
                               (long)batch, m->blk_act + (size_t)i * m->act_floats, st))
             return -1;
     }
-    cublasSetStream(m->cublas, st);
-    // logits[BL, V] = h[BL, D] . head[D, V]
-    if (cublasSgemm(m->cublas, CUBLAS_OP_N, CUBLAS_OP_N, (int)m->V, (int)BL, (int)m->D, &one,
-                    m->params + (size_t)m->V * m->D, (int)m->V, m->hid + (size_t)m->nl * BL * m->D, (int)m->D, &zero,
-                    m->logits, (int)m->V) != CUBLAS_STATUS_SUCCESS)
-        return set_error("head GEMM failed");
-    return 0;
+    // logits[BL, V] = h[BL, D] . head[D, V] on the tensor cores at fp32 accuracy (3xTF32): B operand head^T
+    float* hT = (float*)workspace(WS_HEAD_T, (size_t)m->V * m->D * sizeof(float));
+    if (!hT) return set_error("workspace allocation failed");
+    cudaError_t e = gemm_transpose_f32(m->params + (size_t)m->V * m->D, hT, m->D, m->V, m->V, m->D, st);
+    if (e == cudaSuccess)
+        e = mm_nt(false, BL, m->V, m->D, m->hid + (size_t)m->nl * BL * m->D, m->D, hT, m->D, m->logits, m->V, false,
+                  st);
+    return e == cudaSuccess ? 0 : set_cuda_error("head GEMM", e);
 }
 
 int kmamba_forward(KMamba* m, const uint32_t* tokens, float* logits_out) {
@@ -456,17 +455,18 @@ float kmb_model_forward_backward(KMamba* m, const uint32_t* d_tokens, size_t bat
     }
     cudaMemsetAsync(m->grads, 0, m->n_params * 4, st);
     if (model_forward(m, batch, st)) return NAN;
-    const float inv = 1.0f / (float)BL, one = 1.0f, zero = 0.0f;
+    const float inv = 1.0f / (float)BL;
     softmax_xent<<<nblk(BL, 8), 256, 0, st>>>(m->logits, m->tok, BL, (int)m->L, (int)m->V, inv, m->rowloss);
     sum_rows<<<1, 256, 0, st>>>(m->rowloss, BL, inv, m->loss);
     float* hN = m->hid + (size_t)m->nl * BL * m->D;
     // g_head[D, V] += h^T . dlogits ; dh[BL, D] = dlogits . head^T
-    if (cublasSgemm(m->cublas, CUBLAS_OP_N, CUBLAS_OP_T, (int)m->V, (int)m->D, (int)BL, &one, m->logits, (int)m->V,
-                    hN, (int)m->D, &one, m->grads + (size_t)m->V * m->D, (int)m->V) != CUBLAS_STATUS_SUCCESS ||
-        cublasSgemm(m->cublas, CUBLAS_OP_T, CUBLAS_OP_N, (int)m->D, (int)BL, (int)m->V, &one,
-                    m->params + (size_t)m->V * m->D, (int)m->V, m->logits, (int)m->V, &zero,
-                    m->dh, (int)m->D) != CUBLAS_STATUS_SUCCESS) {
-        set_error("head backward GEMM failed");
+    cudaError_t e = mm_tn(false, m->D, m->V, BL, hN, m->D, m->logits, m->V, m->grads + (size_t)m->V * m->D, m->V,
+                          true, st);
+    if (e == cudaSuccess)
+        e = mm_nt(false, BL, m->D, m->V, m->logits, m->V, m->params + (size_t)m->V * m->D, m->V, m->dh, m->D, false,
+                  st);
+    if (e != cudaSuccess) {
+        set_cuda_error("head backward GEMM", e);
         return NAN;
     }
     KMBlockConfig c = layer_cfg(m);
@@ -481,7 +481,7 @@ float kmb_model_forward_backward(KMamba* m, const uint32_t* d_tokens, size_t bat
     embed_scatter_grad<<<nblk(BL * m->D, 256), 256, 0, st>>>(m->dh, m->tok, BL, (int)m->L, (int)m->D, (int)m->V,
                                                              m->grads);
     float loss = NAN;
-    cudaError_t e = cudaMemcpyAsync(&loss, m->loss, 4, cudaMemcpyDeviceToHost, st);
+    e = cudaMemcpyAsync(&loss, m->loss, 4, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) {
         set_cuda_error("kmb_model_forward_backward", e);

@@ -275,6 +275,13 @@ __global__ void pack_wcat_t(const float* __restrict__ Win, const float* __restri
     out[i] = __float2bfloat16_rn(v);
 }
 
+cudaError_t launch_pack_wcat_t(const float* Win, const float* dp, const float* lp, const float* WB, const float* WC,
+                               int R, int NR, int dim, int ldp, __nv_bfloat16* out, cudaStream_t st) {
+    pack_wcat_t<<<(unsigned)(((long long)dim * ldp + 255) / 256), 256, 0, st>>>(Win, dp, lp, WB, WC, R, NR, dim, ldp,
+                                                                               out);
+    return cudaGetLastError();
+}
+
 // Stage sizing, tensor maps and launch shared by both epilogues.  A [M, K] and
 // Bm [N, K] are bf16, K-major, with row strides lda / ldb elements.
 template <int EPI>
