@@ -132,74 +132,84 @@ __global__ void add_partials(const float* __restrict__ part, long long n, int nc
 }
 
 // The rank-R products of the block backward in one pass over X [rows, dim]
-// (dout, or dB / dC for the bias sums), for ranks r0 .. r0 + rc - 1 (rc <= 4):
-//   dy[row, r]           = sum_j X[row, j] W[j, r]              (DY)
+// (dout, or dB / dC for the bias sums), for ranks r0 .. r0 + rc - 1 (rc <= RM):
+//   dy[row, r]           = sum_j X[row, j] W[j, r]              (dy non-null)
 //   part[blk][j][r - r0] = sum over the block's rows of X[row, j] Y[row, r]
-//                          (Y == nullptr: Y = 1, rc = 1)
+//                          (part non-null; Y == nullptr: Y = 1, rc = 1)
 // One warp per row; lane l holds NC chunks of V consecutive columns (16-byte
-// loads) at (c * 32 + l) * V.  dy is a butterfly over the lanes; the block's
-// eight warps add their column partials into shared memory in warp order.
-// Every sum has a fixed order.
-template <typename T, int NC>
+// loads) at (c * 32 + l) * V, and the next row's chunks are loaded before the
+// current row is used.  dy is a butterfly over the lanes; the block's eight
+// warps add their column partials into shared memory in warp order.  Every
+// sum has a fixed order.
+template <typename T, int NC, int RM>
 __global__ void __launch_bounds__(256)
 rank_pass(const T* __restrict__ X, const float* __restrict__ W, const float* __restrict__ Y, long long rows, int dim,
           int R, int r0, int rc, float* __restrict__ dy, float* __restrict__ part) {
     constexpr int V = 16 / sizeof(T);
-    extern __shared__ float rp_buf[];   // [dim][4]
+    extern __shared__ float rp_buf[];   // [dim][RM]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float acc[NC][V][4];
-    float wv[NC][V][4];
+    float acc[NC][V][RM];
+    float wv[NC][V][RM];
 #pragma unroll
     for (int c = 0; c < NC; c++)
 #pragma unroll
         for (int v = 0; v < V; v++)
 #pragma unroll
-            for (int r = 0; r < 4; r++) {
+            for (int r = 0; r < RM; r++) {
                 acc[c][v][r] = 0.0f;
                 const int j = (c * 32 + lane) * V + v;
                 wv[c][v][r] = (dy && j < dim && r < rc) ? W[(long long)j * R + r0 + r] : 0.0f;
             }
     const long long stride = (long long)gridDim.x * 8;
-    for (long long row = (long long)blockIdx.x * 8 + warp; row < rows; row += stride) {
-        float xv[NC][V];
+    long long row = (long long)blockIdx.x * 8 + warp;
+    uint4 nxt[NC];
+    auto load = [&](long long rw) {
 #pragma unroll
         for (int c = 0; c < NC; c++) {
             const int j0 = (c * 32 + lane) * V;
-            if (j0 < dim) {
-                const uint4 q = *reinterpret_cast<const uint4*>(X + row * dim + j0);
-                const T* e = reinterpret_cast<const T*>(&q);
-#pragma unroll
-                for (int v = 0; v < V; v++) xv[c][v] = ldf(e + v);
-            } else {
-#pragma unroll
-                for (int v = 0; v < V; v++) xv[c][v] = 0.0f;
-            }
+            nxt[c] = (rw < rows && j0 < dim) ? __ldcs(reinterpret_cast<const uint4*>(X + rw * dim + j0))
+                                             : make_uint4(0u, 0u, 0u, 0u);
         }
-        float yr[4];
+    };
+    load(row);
+    for (; row < rows; row += stride) {
+        float xv[NC][V];
 #pragma unroll
-        for (int r = 0; r < 4; r++)
+        for (int c = 0; c < NC; c++) {
+            const T* e = reinterpret_cast<const T*>(&nxt[c]);
+#pragma unroll
+            for (int v = 0; v < V; v++) xv[c][v] = ldf(e + v);
+        }
+        float yr[RM];
+#pragma unroll
+        for (int r = 0; r < RM; r++)
             yr[r] = Y ? (r < rc ? Y[row * R + r0 + r] : 0.0f) : (r == 0 ? 1.0f : 0.0f);
+        load(row + stride);   // the next row's chunks are in flight while this one is used
         if (part) {
 #pragma unroll
             for (int c = 0; c < NC; c++)
 #pragma unroll
                 for (int v = 0; v < V; v++)
 #pragma unroll
-                    for (int r = 0; r < 4; r++) acc[c][v][r] = __fmaf_rn(xv[c][v], yr[r], acc[c][v][r]);
+                    for (int r = 0; r < RM; r++) acc[c][v][r] = __fmaf_rn(xv[c][v], yr[r], acc[c][v][r]);
         }
         if (dy) {
-            float sr[4] = {0.f, 0.f, 0.f, 0.f};
+            float sr[RM];
+#pragma unroll
+            for (int r = 0; r < RM; r++) sr[r] = 0.0f;
 #pragma unroll
             for (int c = 0; c < NC; c++)
 #pragma unroll
                 for (int v = 0; v < V; v++)
 #pragma unroll
-                    for (int r = 0; r < 4; r++) sr[r] = __fmaf_rn(xv[c][v], wv[c][v][r], sr[r]);
+                    for (int r = 0; r < RM; r++) sr[r] = __fmaf_rn(xv[c][v], wv[c][v][r], sr[r]);
 #pragma unroll
-            for (int r = 0; r < 4; r++)
+            for (int r = 0; r < RM; r++)
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) sr[r] += __shfl_xor_sync(~0u, sr[r], o);
-            if (lane < rc) dy[row * R + r0 + lane] = lane == 0 ? sr[0] : lane == 1 ? sr[1] : lane == 2 ? sr[2] : sr[3];
+#pragma unroll
+            for (int r = 0; r < RM; r++)
+                if (lane == r && r < rc) dy[row * R + r0 + r] = sr[r];
         }
     }
     if (!part) return;
@@ -213,8 +223,8 @@ rank_pass(const T* __restrict__ X, const float* __restrict__ W, const float* __r
                     const int j = (c * 32 + lane) * V + v;
                     if (j < dim)
 #pragma unroll
-                        for (int r = 0; r < 4; r++) {
-                            float* b = rp_buf + j * 4 + r;
+                        for (int r = 0; r < RM; r++) {
+                            float* b = rp_buf + j * RM + r;
                             *b = w == 0 ? acc[c][v][r] : *b + acc[c][v][r];
                         }
                 }
@@ -223,18 +233,29 @@ rank_pass(const T* __restrict__ X, const float* __restrict__ W, const float* __r
     }
     const int rr = Y ? rc : 1;
     float* out = part + (long long)blockIdx.x * dim * rr;   // [dim][rr]
-    for (int i = threadIdx.x; i < dim * rr; i += blockDim.x) out[i] = rp_buf[(i / rr) * 4 + (i % rr)];
+    for (int i = threadIdx.x; i < dim * rr; i += blockDim.x) out[i] = rp_buf[(i / rr) * RM + (i % rr)];
 }
 
-// G[j, r0 + r] += sum_b part[b][j][r]  (fixed order over the blocks)
+// G[j, r0 + r] += sum_b part[b][j][r]: 32 elements per block, warp w adds the blocks w, w + 8, ...
+// in order, then warp 0 adds the eight warp sums in order (a fixed order overall)
 __global__ void add_rank_partials(const float* __restrict__ part, int nblk, int dim, int rr, int R, int r0,
                                   float* __restrict__ G) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= dim * rr) return;
+    __shared__ float ws[8][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x * 32 + lane;
+    const int n = dim * rr;
     float acc = 0.0f;
-    for (int b = 0; b < nblk; b++) acc += part[(long long)b * dim * rr + i];
-    const int j = i / rr, r = i - j * rr;
-    G[(long long)j * R + r0 + r] += acc;
+    if (i < n)
+        for (int b = warp; b < nblk; b += 8) acc += part[(long long)b * n + i];
+    ws[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0 && i < n) {
+        float t = ws[0][lane];
+#pragma unroll
+        for (int w = 1; w < 8; w++) t += ws[w][lane];
+        const int j = i / rr, r = i - j * rr;
+        G[(long long)j * R + r0 + r] += t;
+    }
 }
 
 // out[row, j] = x[row, j] + sum_r y[row, r] W[j, r], four columns per thread (dim % 4 == 0)
@@ -438,19 +459,26 @@ static cudaError_t rank_pass_run(bool bf16, const void* X, const float* W, const
     const size_t smem = G ? (size_t)dim * 4 * sizeof(float) : 0;
     for (int r0 = 0; r0 < RR; r0 += 4) {
         const int rc = RR - r0 < 4 ? RR - r0 : 4;
-#define KMB_RP(TT, NCV)                                                                                       \
-    rank_pass<TT, NCV><<<(unsigned)nb, 256, smem, st>>>((const TT*)X, W, Y, rows, dim, R, r0, rc, dy, part)
+#define KMB_RP3(TT, NCV, RMV)                                                                          \
+    rank_pass<TT, NCV, RMV><<<(unsigned)nb, 256, smem, st>>>((const TT*)X, W, Y, rows, dim, R, r0, rc, dy, part)
+#define KMB_RP(TT, NCV)                      \
+    do {                                     \
+        if (rc <= 1) KMB_RP3(TT, NCV, 1);    \
+        else if (rc <= 2) KMB_RP3(TT, NCV, 2); \
+        else KMB_RP3(TT, NCV, 4);            \
+    } while (0)
         if (bf16) {
             if (nc == 1) KMB_RP(__nv_bfloat16, 1); else if (nc == 2) KMB_RP(__nv_bfloat16, 2); else KMB_RP(__nv_bfloat16, 4);
         } else {
             if (nc == 1) KMB_RP(float, 1); else if (nc == 2) KMB_RP(float, 2); else KMB_RP(float, 4);
         }
+#undef KMB_RP3
 #undef KMB_RP
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         if (G) {
             const int rr = Y ? rc : 1;
-            add_rank_partials<<<nblk(dim * rr, 256), 256, 0, st>>>(part, (int)nb, dim, rr, Y ? R : 1, Y ? r0 : 0, G);
+            add_rank_partials<<<nblk(dim * rr, 32), 256, 0, st>>>(part, (int)nb, dim, rr, Y ? R : 1, Y ? r0 : 0, G);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
             if (!Y && !dy) break;
         }

@@ -168,18 +168,32 @@ __device__ __forceinline__ void epi_flush(float* tile, int q, const float* vals,
     for (int c = 0; c < 128; c++)
         if (c < cols_here) tile[rl * EPI_LD + c] = vals[c];
     epi_bar();
-    // warp q writes rows q*32 .. q*32+31, lanes along the columns
-    for (int i = 0; i < 32 && write; i++) {
-        const int r = q * 32 + i;
-        const long long row = m0 + r;
-        if (row >= M) break;
-        float* drow = D + row * ldd;
-        for (int c = lane; c < cols_here; c += 32) {
-            const long long col = col0 + c;
-            if (col < N) {
-                if (EPI == EPI_ADD) drow[col] += tile[r * EPI_LD + c];
-                else drow[col] = tile[r * EPI_LD + c];
+    // warp q writes rows q*32 .. q*32+31, lanes along the columns; EPI_ADD loads eight rows' worth
+    // of D before it stores any, so the loads overlap
+    if (write) {
+        for (int i0 = 0; i0 < 32; i0 += 8) {
+            float g[8][4];
+            if (EPI == EPI_ADD) {
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const int r = q * 32 + i0 + i, c = lane + 32 * k;
+                        const long long row = m0 + r, col = col0 + c;
+                        g[i][k] = (row < M && c < cols_here && col < N) ? D[row * ldd + col] : 0.0f;
+                    }
             }
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int r = q * 32 + i0 + i, c = lane + 32 * k;
+                    const long long row = m0 + r, col = col0 + c;
+                    if (row < M && c < cols_here && col < N) {
+                        const float t = tile[r * EPI_LD + c];
+                        D[row * ldd + col] = EPI == EPI_ADD ? g[i][k] + t : t;
+                    }
+                }
         }
     }
     epi_bar();
