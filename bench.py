@@ -70,7 +70,7 @@ def parse():
     ap.add_argument("--D", type=int, default=D)
     ap.add_argument("--M", type=int, default=M)
     ap.add_argument("--workload", default="scan_fwd",
-                    choices=["scan_fwd", "scan_fwd_c0", "scan_fwd_c1", "scan_bwd", "scan_bwd_c1", "convnd2d",
+                    choices=["scan_fwd", "scan_fwd_c0", "scan_fwd_c1", "scan_fwd_3d", "scan_bwd", "scan_bwd_c1", "convnd2d",
                              "convnd3d", "block", "block_bf16", "model", "all"],
                     help="scan_fwd = the headline line; the others measure the other BASELINE configs "
                          "(all = every other one, one line each)")
@@ -444,7 +444,7 @@ def main():
 # own CPU code on a bounded sample, rank 0 at N=1) and e2e (host buffers, the
 # H2D copies of the step's inputs and the D2H copies of its results inside the
 # timed region).  `--workload all` prints every line.
-OTHER = ("scan_fwd_c0", "scan_fwd_c1", "scan_bwd", "scan_bwd_c1", "convnd2d", "convnd3d", "block", "block_bf16",
+OTHER = ("scan_fwd_c0", "scan_fwd_c1", "scan_fwd_3d", "scan_bwd", "scan_bwd_c1", "convnd2d", "convnd3d", "block", "block_bf16",
          "model")
 
 
@@ -561,6 +561,49 @@ def wl_scan_fwd_small(args, dev, stream, lib, kmb, g, which, peak, peak_src, ran
         rate, n = _cpu_rate(lambda: po.ref_scannd(inp), upd)
         line["cpu_baseline"] = {"value": rate, "unit": "state-updates/s", "cores": threads, "kind": "reference",
                                 "sample": f"scannd_ref (oracle/_ref) on the whole workload ({B_} items), median of {n}"}
+    return line
+
+
+def wl_scan_fwd_3d(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, world):
+    """Scan-A forward on the 3D grid {16,32,32} (the model config's spatial
+    grid) at the headline's channel and state counts: D 512, M 64, RoPE,
+    batch 2 (13 GB of B, C and h: inputs > L2)."""
+    import torch
+    dims, D_, M_, B_ = (16, 32, 32), 512, 64, 2
+    P_, nd = int(np.prod(dims)), len(dims)
+    t = _scan_inputs(g, dev, dims, D_, M_, B_, True)
+    h, y = torch.empty(B_, P_, D_, M_, device=dev), torch.empty(B_, P_, D_, device=dev)
+    p = kmb.scan_params(list(dims), D_, M_, t["x"], t["A"], t["B"], t["C"], t["delta"], h, y, theta=t["theta"])
+    sp = C.c_void_p(stream.cuda_stream)
+    call = lambda: kmb.check(lib.scannd_forward_async(C.byref(p), B_, sp))
+    steps = max(args.steps, 5)
+    ms = _timed(call, steps, max(args.warmup, 3), stream)
+    path = lib.kmb_last_forward_path()
+    upd = B_ * P_ * D_ * M_
+    # B, C read + h written per update, plus the plane predecessor's h and B read back (L2 or HBM)
+    alg = upd * 12 + B_ * P_ * D_ * (4 + 4 * nd + 4)
+    tt = ms / steps / 1e3
+    line = {"metric": "scanND state-updates/sec", "value": upd * world / tt, "unit": "state-updates/s",
+            "ms_per_step": ms / steps, "steps": steps,
+            "config": {"workload": "scannd_fwd_3d16x32x32_D512_M64_b2_rope", "l2": "inputs > L2 (13 GB)"},
+            "roofline": {"bound": "hbm", "achieved": round(alg / tt / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(alg / tt / 1e9 / peak, 4), "peak_source": peak_src, "traffic": None,
+                         "alg_bytes_per_launch": alg, "kernel": "scan_fwd_strips (3D: plane predecessor by TMA)",
+                         "note": "algorithmic bytes count B, C, h once; the plane predecessor's h and B are "
+                                 "re-read (8 B per update more when they miss L2)"},
+            "fast_path": path, "gpu_launches": steps}
+    hin = {k: _pinned(v) for k, v in t.items() if v is not None and k != "A" and k != "theta"}
+    line["e2e"] = _e2e(stream, hin, {k: t[k] for k in hin}, {"h": h, "y": y},
+                       {"h": torch.empty(h.shape, pin_memory=True), "y": torch.empty(y.shape, pin_memory=True)},
+                       call, 3, upd * world, "state-updates/s")
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import pyoracle as po
+        threads = po.set_threads(len(os.sched_getaffinity(0)) or 1)
+        inp = po.gen_scan(list(dims), 16, M_, batch=1, seed=3, rope=True)
+        units = P_ * 16 * M_
+        rate, n = _cpu_rate(lambda: po.ref_scannd(inp), units)
+        line["cpu_baseline"] = {"value": rate, "unit": "state-updates/s", "cores": threads, "kind": "reference",
+                                "sample": f"scannd_ref (oracle/_ref): one item, 16 of the 512 channels, median of {n}"}
     return line
 
 
@@ -840,7 +883,8 @@ def run_other_workload(args, rank, world):
     stream = torch.cuda.current_stream(dev)
     peak, peak_src = peaks()
     names = OTHER if args.workload == "all" else (args.workload,)
-    fns = {"scan_fwd_c0": wl_scan_fwd_small, "scan_fwd_c1": wl_scan_fwd_small, "scan_bwd": wl_scan_bwd,
+    fns = {"scan_fwd_c0": wl_scan_fwd_small, "scan_fwd_c1": wl_scan_fwd_small, "scan_fwd_3d": wl_scan_fwd_3d,
+           "scan_bwd": wl_scan_bwd,
            "scan_bwd_c1": wl_scan_bwd, "convnd2d": wl_convnd, "convnd3d": wl_convnd, "block": wl_block,
            "block_bf16": wl_block, "model": wl_model}
     for name in names:

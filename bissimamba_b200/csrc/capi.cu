@@ -200,7 +200,7 @@ int run_scan_fwd(const ScanDesc& s, cudaStream_t st) {
         int* status = status_word();
         if (!status) return fail("workspace allocation failed");
         if ((e = cudaMemsetAsync(status, 0, sizeof(int), st)) != cudaSuccess) return fail_cuda("memset", e);
-        e = (s.nd == 2) ? launch_scan_fwd_strips(s, status, st) : launch_scan_fwd_tma(s, status, st);
+        e = (s.nd == 2 || s.nd == 3) ? launch_scan_fwd_strips(s, status, st) : launch_scan_fwd_tma(s, status, st);
         if (e == cudaSuccess) {
             tl_fast_path = 1;
             return 0;
@@ -376,7 +376,8 @@ static int scan_host_pipelined(ScanNDParams* p, long batch, const ScanDesc& s0) 
         s.y = (float*)(base + soff[6]);
         cudaError_t ek = cudaErrorNotSupported;
         if (!force_generic())
-            ek = (s.nd == 2) ? launch_scan_fwd_strips(s, status, ps->comp) : launch_scan_fwd_tma(s, status, ps->comp);
+            ek = (s.nd == 2 || s.nd == 3) ? launch_scan_fwd_strips(s, status, ps->comp)
+                                         : launch_scan_fwd_tma(s, status, ps->comp);
         if (ek == cudaSuccess) {
             fast = fast < 0 ? 1 : fast;
         } else {

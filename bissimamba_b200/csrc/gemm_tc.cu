@@ -154,40 +154,43 @@ __device__ __forceinline__ void g_ld64(uint32_t taddr, float* v) {
     for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// The epilogue's 128 threads (warps 2-5) write a 128 x 128 fp32 block through shared memory so that
-// global stores are whole 128-byte rows: row-major tile with a 129-float stride (conflict-free both ways).
+// The epilogue's 256 threads (warps 2-9: lane quarter q = warp % 4 of TMEM, column half hh) write a
+// 128 x 128 fp32 block through shared memory so that global stores are whole 128-byte rows: row-major
+// tile with a 129-float stride (conflict-free both ways).  Each thread holds 64 columns of its row.
 constexpr int EPI_LD = 129;
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+constexpr int EPI_THREADS = 256;
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 template <int EPI>
-__device__ __forceinline__ void epi_flush(float* tile, int q, const float* vals, int cols_here, float* D, long long ldd,
-                                          long long m0, long long M, long long col0, long long N, int lane,
-                                          bool write) {
+__device__ __forceinline__ void epi_flush(float* tile, int q, int hh, const float* vals, int cols_here, float* D,
+                                          long long ldd, long long m0, long long M, long long col0, long long N,
+                                          int lane, bool write) {
     // every epilogue thread reaches both barriers; `write` only gates the stores
     const int rl = q * 32 + lane;
 #pragma unroll
-    for (int c = 0; c < 128; c++)
-        if (c < cols_here) tile[rl * EPI_LD + c] = vals[c];
+    for (int c = 0; c < 64; c++)
+        if (hh * 64 + c < cols_here) tile[rl * EPI_LD + hh * 64 + c] = vals[c];
     epi_bar();
-    // warp q writes rows q*32 .. q*32+31, lanes along the columns; EPI_ADD loads eight rows' worth
-    // of D before it stores any, so the loads overlap
+    // epilogue warp e = hh * 4 + q writes rows 16 e .. 16 e + 15, lanes along the columns; EPI_ADD loads
+    // four rows' worth of D before it stores any, so the loads overlap
+    const int e = hh * 4 + q;
     if (write) {
-        for (int i0 = 0; i0 < 32; i0 += 8) {
-            float g[8][4];
+        for (int i0 = 0; i0 < 16; i0 += 4) {
+            float g[4][4];
             if (EPI == EPI_ADD) {
 #pragma unroll
-                for (int i = 0; i < 8; i++)
+                for (int i = 0; i < 4; i++)
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        const int r = q * 32 + i0 + i, c = lane + 32 * k;
+                        const int r = e * 16 + i0 + i, c = lane + 32 * k;
                         const long long row = m0 + r, col = col0 + c;
                         g[i][k] = (row < M && c < cols_here && col < N) ? D[row * ldd + col] : 0.0f;
                     }
             }
 #pragma unroll
-            for (int i = 0; i < 8; i++)
+            for (int i = 0; i < 4; i++)
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
-                    const int r = q * 32 + i0 + i, c = lane + 32 * k;
+                    const int r = e * 16 + i0 + i, c = lane + 32 * k;
                     const long long row = m0 + r, col = col0 + c;
                     if (row < M && c < cols_here && col < N) {
                         const float t = tile[r * EPI_LD + c];
@@ -199,13 +202,13 @@ __device__ __forceinline__ void epi_flush(float* tile, int q, const float* vals,
     epi_bar();
 }
 
-constexpr int GT_THREADS = 192;
+constexpr int GT_THREADS = 64 + EPI_THREADS;   // TMA warp, MMA warp, 8 epilogue warps
 
 // Stage layout: A pieces 0..NP-1 (a_bytes each), then B pieces (b_bytes each).
 // K-major: one TMA box per piece and operand ([128 or ncols rows] x 128 B).
 // MN-major: boxes of 64 elements (128 B) x 64 K rows, 8 KB each, side by side.
 template <int KIND, int EPI, bool MN>
-__global__ void __launch_bounds__(GT_THREADS, 1)
+__global__ void __launch_bounds__(GT_THREADS, KIND == KIND_BF16 ? 2 : 1)
 gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUtensorMap mA0,
                const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mA2,
                const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1,
@@ -240,7 +243,7 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
         mbar_init(smem_u32(done), 1);
         for (int b = 0; b < 2; b++) {
             mbar_init(smem_u32(&tfull[b]), 1);
-            mbar_init(smem_u32(&tempty[b]), 4);
+            mbar_init(smem_u32(&tempty[b]), EPI_THREADS / 32);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -335,12 +338,12 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
             g_commit(smem_u32(done));
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile
-        const int q = warp & 3;
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile, columns of half hh
+        const int q = warp & 3, hh = (warp - 2) >> 2;
         if constexpr (FL) {
-            float acc[128];
+            float acc[64];
 #pragma unroll
-            for (int c = 0; c < 128; c++) acc[c] = 0.0f;
+            for (int c = 0; c < 64; c++) acc[c] = 0.0f;
             bool ok = true;
             const int nunits = nkb * 4 / d.kflush;
             for (int u = 0; u < nunits; u++) {
@@ -350,15 +353,11 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((u & 1) * 128);
+                if (hh * 64 < ncols) {
+                    float v[64];
+                    g_ld64(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((u & 1) * 128 + hh * 64), v);
 #pragma unroll
-                for (int h = 0; h < 128; h += 64) {
-                    if (h < ncols) {
-                        float v[64];
-                        g_ld64(tb + (uint32_t)h, v);
-#pragma unroll
-                        for (int j = 0; j < 64; j++) acc[h + j] += v[j];
-                    }
+                    for (int j = 0; j < 64; j++) acc[j] += v[j];
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
@@ -366,27 +365,22 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
             }
             // the last unit's commit covers every MMA; the stages are free for the store tile
             if (!mbar_wait(smem_u32(done), 0)) { set_status(d.status, KMB_ERR_TIMEOUT_Y); ok = false; }
-            epi_flush<EPI>((float*)smem, q, acc, ncols, d.D + (long long)blockIdx.z * d.split_stride, d.ldd, m0, d.M,
-                           n0, d.N, lane, ok);
+            epi_flush<EPI>((float*)smem, q, hh, acc, ncols, d.D + (long long)blockIdx.z * d.split_stride, d.ldd, m0,
+                           d.M, n0, d.N, lane, ok);
         } else {
             const bool got = mbar_wait(smem_u32(done), 0);
             if (!got) set_status(d.status, KMB_ERR_TIMEOUT_Y);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             for (int h = 0; h < ncols; h += 128) {
-                float v[128];
+                float v[64];
+                if (h + hh * 64 < ncols && nkb > 0)
+                    g_ld64(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h + hh * 64), v);
+                else
 #pragma unroll
-                for (int j = 0; j < 128; j += 64) {
-                    if (h + j < ncols) g_ld64(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h + j), v + j);
-                    else
-#pragma unroll
-                        for (int i = 0; i < 64; i++) v[j + i] = 0.0f;   // nkb == 0: an empty split stores zeros
-                }
-                if (nkb == 0)
-#pragma unroll
-                    for (int i = 0; i < 128; i++) v[i] = 0.0f;
+                    for (int i = 0; i < 64; i++) v[i] = 0.0f;   // nkb == 0: an empty split stores zeros
                 const int cols_here = min(128, ncols - h);
-                epi_flush<EPI>((float*)smem, q, v, cols_here, d.D + (long long)blockIdx.z * d.split_stride, d.ldd, m0,
-                               d.M, n0 + h, d.N, lane, got);
+                epi_flush<EPI>((float*)smem, q, hh, v, cols_here, d.D + (long long)blockIdx.z * d.split_stride, d.ldd,
+                               m0, d.M, n0 + h, d.N, lane, got);
             }
         }
     }

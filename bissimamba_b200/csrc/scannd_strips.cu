@@ -28,6 +28,7 @@
 #include "kmb_sync.cuh"
 #include "kmb_butterfly.cuh"
 #include <type_traits>
+#include <cstdlib>
 
 namespace kmb {
 int persistent_sms(int sms);  // SMs a persistent grid may fill (capi.cu)
@@ -39,6 +40,8 @@ constexpr int SW_WC = 8;       // max columns per strip
 struct StripDesc {
     int D, nd;
     int Q, O, Wc, S;        // inner extent, outer extent, columns per strip, strips
+    int O1;                 // 3D: rows per plane (the outer extent O is planes x O1)
+    int fence_period;       // 3D: rows between proxy fences (<= O1 - look-ahead + 1)
     int k_in;               // axis of the inner dimension
     int lam_inner_fast;     // lambda box (Wc,1,1) at (q0,o,b) vs (4,Wc,1) at (o&~3,q0,b)
     int clamp;
@@ -76,28 +79,37 @@ struct StripGeom {
     static constexpr int MAXT = 8 * HW * 32;              // threads of the largest CTA (8 strips)
 };
 
-template <int MT, bool ROPE>
+template <int MT, bool ROPE, bool P3 = false, int WCT = SW_WC>
 struct StripLayout {
     using Gm = StripGeom<MT, ROPE>;
-    static constexpr int BBOX = MT * Gm::CH * SW_WC * 4;   // bytes of one B / C box
+    static constexpr int BBOX = MT * Gm::CH * WCT * 4;     // bytes of one B / C box
     static constexpr int offC = BBOX;
     static constexpr int offX = 2 * BBOX;                  // x box [WC][4]
-    static constexpr int offD = offX + 128;                // delta box [2][WC][4]
-    static constexpr int offL = offD + 256;                // lambda box [WC] or [WC][4]
-    static constexpr int bytes = offL + 128;
+    static constexpr int offD = offX + 128;                // delta box [nd][WC][4]
+    static constexpr int offL = offD + (P3 ? 384 : 256);   // lambda box [WC] or [WC][4]
+    // 3D: the previous plane's h, B and x boxes (the plane predecessor of every point of the row)
+    static constexpr int offHp = offL + 128;
+    static constexpr int offBp = offHp + BBOX;
+    static constexpr int offXp = offBp + BBOX;
+    static constexpr int bytes = P3 ? offXp + 128 : offL + 128;
 };
 
-template <int MT, bool ROPE, bool LAMB, bool KIN0, bool FULL, int EXPM>  // EXPM 0: expf, reference order; 1: ex2.approx
+// EXPM 0: expf, reference order; 1: ex2.approx.  P3: 3D grids (planes x rows x inner, inner = the last
+// axis): rows are (plane, row) pairs walked in order, the row predecessor comes from the register ring
+// (none on a plane's first row) and the plane predecessor's h, B and x arrive as TMA boxes of the row
+// O1 rows back, which this warp wrote itself (a proxy fence after every row orders its h stores before
+// the bulk loads that read them; the issuer runs at most O1 rows ahead).
+template <int MT, bool ROPE, bool LAMB, bool KIN0, bool FULL, int EXPM, bool P3 = false, int WCT = SW_WC>
 __global__ void __launch_bounds__(StripGeom<MT, ROPE>::MAXT, 1)
 scan_fwd_strips(const __grid_constant__ StripDesc f,
                 const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mC,
                 const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mD,
-                const __grid_constant__ CUtensorMap mL) {
+                const __grid_constant__ CUtensorMap mL, const __grid_constant__ CUtensorMap mH) {
     using Gm = StripGeom<MT, ROPE>;
-    using Ly = StripLayout<MT, ROPE>;
+    using Ly = StripLayout<MT, ROPE, P3, WCT>;
     constexpr bool EX2 = EXPM == 1;
     constexpr int CPT = Gm::CPT, HW = Gm::HW, CH = Gm::CH, GS = Gm::GS, U = Gm::U;
-    constexpr int WC = SW_WC;
+    constexpr int WC = WCT;   // columns per strip
     constexpr int ST = Ly::bytes;
     extern __shared__ __align__(1024) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, wi = tid >> 5;
@@ -164,6 +176,11 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             if (!KIN0) tma_load_3d(smem_u32(st + Ly::offL), &mL, full, q0, o, b);
             else tma_load_3d(smem_u32(st + Ly::offL), &mL, full, o & ~3, q0, b);
         }
+        if (P3) {   // plane predecessor row (negative rows of the first plane read zeros)
+            tma_load_5d(smem_u32(st + Ly::offHp), &mH, full, 0, d0, q0, o - f.O1, b);
+            tma_load_5d(smem_u32(st + Ly::offBp), &mB, full, 0, d0, q0, o - f.O1, b);
+            tma_load_4d(smem_u32(st + Ly::offXp), &mX, full, d0 & ~3, q0, o - f.O1, b);
+        }
     };
     auto advance_issue = [&]() {
         next_issue++;
@@ -174,8 +191,9 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
         if (++is_slot == NSS) { is_slot = 0; is_phase ^= 1u; }
     };
     // Keep up to NSS rows in flight; block only for the row about to be consumed.
+    const int ahead = P3 ? min(NSS, f.O1) : NSS;   // P3: row r reads row r - O1, finished only when r < cur + O1
     auto top_up = [&](int cur) -> bool {
-        while (next_issue < total_rows && next_issue < cur + NSS) {
+        while (next_issue < total_rows && next_issue < cur + ahead) {
             if (next_issue >= NSS) {
                 // the slot's previous use (row next_issue - NSS) must have been released
                 const uint32_t eb = smem_u32(&b_empty[w * NSS + is_slot]);
@@ -222,15 +240,17 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int b = (int)(tile / ntd);
         const int d0 = (int)(tile - (long long)b * ntd) * CH;
-        float AI[U], AO[U], cth = 1.0f, sth = 0.0f;
+        float AI[U], AO[U], AP[U], cth = 1.0f, sth = 0.0f;
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const int d = d0 + cl0 + u % CPT, mu = m + 32 * (u / CPT);
             // EX2: A log2 e, so alpha = 2^(delta * A log2 e) is one multiply and one ex2
             // per update; otherwise A itself and alpha = expf(delta * A) as the reference
             const float sc = EX2 ? kKmbLog2e : 1.0f;
-            AI[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 0 : 1) * D + d) * MT + mu], f.clamp, f.amin), sc);
-            AO[u] = __fmul_rn(kmb_clampA(f.A[((long long)(KIN0 ? 1 : 0) * D + d) * MT + mu], f.clamp, f.amin), sc);
+            const int axI = P3 ? 2 : (KIN0 ? 0 : 1), axO = P3 ? 1 : (KIN0 ? 1 : 0);
+            AI[u] = __fmul_rn(kmb_clampA(f.A[((long long)axI * D + d) * MT + mu], f.clamp, f.amin), sc);
+            AO[u] = __fmul_rn(kmb_clampA(f.A[((long long)axO * D + d) * MT + mu], f.clamp, f.amin), sc);
+            AP[u] = P3 ? __fmul_rn(kmb_clampA(f.A[(long long)d * MT + mu], f.clamp, f.amin), sc) : 0.0f;
         }
         if (ROPE) {
             const float th = f.theta[(d0 + cl0) >> 1];
@@ -242,9 +262,10 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
         const int xo = (d0 & 3) + xofs;
         float ring_h[WC][U], ring_b[WC][U];
 
-        // one row of this strip; HASO: the row above exists (o > 0)
-        auto do_row = [&](auto hasO_c, int o) -> bool {
+        // one row of this strip; HASO: the row above exists; HASP (3D): the plane before exists
+        auto do_row = [&](auto hasO_c, auto hasP_c, int o) -> bool {
             constexpr bool HASO = decltype(hasO_c)::value;
+            constexpr bool HASP = decltype(hasP_c)::value;
             if (issuer && !top_up(row)) {
                 set_status(f.status, KMB_ERR_TIMEOUT_EMPTY);
                 drain();
@@ -260,8 +281,12 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             const float* Bs = (const float*)(st + bofs);
             const float* Cs = (const float*)(st + Ly::offC + bofs);
             const float* Xs = (const float*)(st + Ly::offX) + xo;
-            const float* DsI = (const float*)(st + Ly::offD) + (KIN0 ? 0 : WC * 4) + xo;
-            const float* DsO = (const float*)(st + Ly::offD) + (KIN0 ? WC * 4 : 0) + xo;
+            const float* DsI = (const float*)(st + Ly::offD) + (P3 ? 2 * WC * 4 : KIN0 ? 0 : WC * 4) + xo;
+            const float* DsO = (const float*)(st + Ly::offD) + (P3 ? WC * 4 : KIN0 ? WC * 4 : 0) + xo;
+            const float* DsP = (const float*)(st + Ly::offD) + xo;
+            const float* Hp = (const float*)(st + Ly::offHp + bofs);
+            const float* Bp = (const float*)(st + Ly::offBp + bofs);
+            const float* Xp = (const float*)(st + Ly::offXp) + xo;
             const float* Ls = (const float*)(st + Ly::offL) + (KIN0 ? (o & 3) : 0);
             const int hs = row & (SW_K - 1);
             const uint32_t hph = (uint32_t)((row / SW_K) & 1);
@@ -302,6 +327,58 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     // inner predecessor: the previous column (strip w-1's last column when j == 0)
                     const float hatI = (j == 0) ? lh[u] : ring_h[j == 0 ? 0 : j - 1][u];
                     const float buI = (j == 0) ? lb[u] : ring_b[j == 0 ? 0 : j - 1][u];
+                    if constexpr (P3) {
+                        // reference order over the axes (plane, row, inner): dt = sum of the three
+                        // deltas; sums of the present predecessors' Bu, alpha and alpha * h in axis
+                        // order; means as sum / n (n = 3 an IEEE division)
+                        const float dP = DsP[j * 4 + c];
+                        const float dt3 = __fadd_rn(__fadd_rn(dP, dO), dI);
+                        int n = 0;
+                        buacc = 0.0f; dacc = 0.0f; hacc = 0.0f;
+                        if (HASP) {
+                            const float aP = expf(__fmul_rn(dP, AP[u]));
+                            const float* hb = Hp + j * CH * MT + sofs;
+                            float hatP;
+                            if (ROPE) {
+                                const float h0 = hb[0], h1 = hb[MT];
+                                hatP = c == 0 ? __fmaf_rn(cth, h0, -__fmul_rn(sth, h1))
+                                              : __fmaf_rn(sth, h0, __fmul_rn(cth, h1));
+                            } else {
+                                hatP = hb[c * MT];
+                            }
+                            buacc = __fmul_rn(Bp[j * CH * MT + c * MT + sofs], Xp[j * 4 + c]);
+                            dacc = aP;
+                            hacc = __fmul_rn(aP, hatP);
+                            n = 1;
+                        }
+                        if (HASO) {
+                            const float aO = expf(__fmul_rn(dO, AO[u]));
+                            if (n == 0) {
+                                buacc = ring_b[j][u]; dacc = aO; hacc = __fmul_rn(aO, ring_h[j][u]);
+                            } else {
+                                buacc = __fadd_rn(buacc, ring_b[j][u]);
+                                dacc = __fadd_rn(dacc, aO);
+                                hacc = __fmaf_rn(aO, ring_h[j][u], hacc);
+                            }
+                            n++;
+                        }
+                        if (j > 0 || w > 0) {
+                            if (n == 0) {
+                                buacc = buI; dacc = aI; hacc = __fmul_rn(aI, hatI);
+                            } else {
+                                buacc = __fadd_rn(buacc, buI);
+                                dacc = __fadd_rn(dacc, aI);
+                                hacc = __fmaf_rn(aI, hatI, hacc);
+                            }
+                            n++;
+                        }
+                        const float buavg = n == 3 ? __fdiv_rn(buacc, 3.0f) : n == 2 ? __fmul_rn(buacc, 0.5f) : buacc;
+                        const float alavg = n == 3 ? __fdiv_rn(dacc, 3.0f) : n == 2 ? __fmul_rn(dacc, 0.5f) : dacc;
+                        const float beta = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, lam), dt3), alavg);
+                        const float gamma = __fmul_rn(lam, dt3);
+                        hn[u] = __fadd_rn(__fmaf_rn(buavg, beta, __fmul_rn(bu, gamma)), hacc);
+                        goto have_h;
+                    }
                     if (HASO) {
                         const float aO = EX2 ? kmb_ex2(__fmul_rn(dO, AO[u])) : expf(__fmul_rn(dO, AO[u]));
                         if (!EX2 && (j > 0 || w > 0)) {
@@ -352,7 +429,10 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     }
                 have_h:
                     ring_b[j][u] = bu;
-                    if (j < ncol) __stcs(hp + (long long)c * MT + sofs, hn[u]);
+                    if (j < ncol) {
+                        if (P3) hp[(long long)c * MT + sofs] = hn[u];   // read back by the next plane (keep in L2)
+                        else __stcs(hp + (long long)c * MT + sofs, hn[u]);
+                    }
                     const float cy = __fmul_rn(Cs[j * CH * MT + c * MT + sofs], hn[u]);
                     prod[j][c] = sofs == 0 ? cy : __fadd_rn(prod[j][c], cy);
                 }
@@ -408,6 +488,9 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     else *yrow = sum;
                 }
             }
+            // 3D: order this warp's h stores before the bulk loads that read them back O1 rows later;
+            // one fence every fence_period rows covers the rows before it
+            if (P3 && (row + 1) % f.fence_period == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&b_empty[w * NSS + slot]));
             row++;
@@ -417,10 +500,25 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             return true;
         };
 
-        if (!do_row(std::integral_constant<bool, false>(), 0)) return;
+        using T_ = std::integral_constant<bool, true>;
+        using F_ = std::integral_constant<bool, false>;
+        if constexpr (P3) {
+            const int O1 = f.O1;
+            int a1 = 0;
 #pragma unroll 1
-        for (int o = 1; o < O; o++)
-            if (!do_row(std::integral_constant<bool, true>(), o)) return;
+            for (int o = 0; o < O; o++) {
+                bool ok;
+                if (o < O1) ok = a1 == 0 ? do_row(F_(), F_(), o) : do_row(T_(), F_(), o);
+                else ok = a1 == 0 ? do_row(F_(), T_(), o) : do_row(T_(), T_(), o);
+                if (!ok) return;
+                if (++a1 == O1) a1 = 0;
+            }
+        } else {
+            if (!do_row(F_(), F_(), 0)) return;
+#pragma unroll 1
+            for (int o = 1; o < O; o++)
+                if (!do_row(T_(), F_(), o)) return;
+        }
     }
 }
 
@@ -429,12 +527,17 @@ bool tmap_encode(CUtensorMap* m, const void* base, int rank, const unsigned long
                  const unsigned long long* strides_bytes, const unsigned* box);
 
 
-template <int MT, bool ROPE, bool LAMB, bool KIN0>
+template <int MT, bool ROPE, bool LAMB, bool KIN0, bool P3>
 static cudaError_t strips_inst(const StripDesc& f, const CUtensorMap* maps, int smem, int threads, cudaStream_t st) {
-    auto k = f.ex2 == 1 ? ((f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true, 1>
-                                              : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false, 1>)
-                        : ((f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true, 0>
-                                              : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false, 0>);
+    // 3D: four-column strips when the inner extent is <= 32, so up to eight strips (warps) share the SM
+    auto k = P3 ? (f.Wc == 4 ? ((f.Q % 4 == 0) ? scan_fwd_strips<MT, ROPE, LAMB, false, true, 0, P3, 4>
+                                               : scan_fwd_strips<MT, ROPE, LAMB, false, false, 0, P3, 4>)
+                             : ((f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, false, true, 0, P3, SW_WC>
+                                                   : scan_fwd_strips<MT, ROPE, LAMB, false, false, 0, P3, SW_WC>))
+         : f.ex2 == 1 ? ((f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true, 1>
+                                            : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false, 1>)
+                      : ((f.Q % SW_WC == 0) ? scan_fwd_strips<MT, ROPE, LAMB, KIN0, true, 0>
+                                            : scan_fwd_strips<MT, ROPE, LAMB, KIN0, false, 0>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int dev, sms, per = 0;
@@ -445,19 +548,22 @@ static cudaError_t strips_inst(const StripDesc& f, const CUtensorMap* maps, int 
     if (per < 1) return cudaErrorNotSupported;
     long long grid = (long long)sms * per;
     if (grid > f.ntiles) grid = f.ntiles;
-    k<<<(unsigned)grid, threads, smem, st>>>(f, maps[0], maps[1], maps[2], maps[3], maps[4]);
+    k<<<(unsigned)grid, threads, smem, st>>>(f, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5]);
     return cudaGetLastError();
 }
 
 template <int MT, bool ROPE>
 static cudaError_t strips_flags(const ScanDesc& s, const StripDesc& f, const CUtensorMap* maps, int smem,
                                 int threads, cudaStream_t st) {
+    if (f.nd == 3)
+        return s.has_lambda ? strips_inst<MT, ROPE, true, false, true>(f, maps, smem, threads, st)
+                            : strips_inst<MT, ROPE, false, false, true>(f, maps, smem, threads, st);
     const bool k0 = f.k_in == 0;
     if (s.has_lambda)
-        return k0 ? strips_inst<MT, ROPE, true, true>(f, maps, smem, threads, st)
-                  : strips_inst<MT, ROPE, true, false>(f, maps, smem, threads, st);
-    return k0 ? strips_inst<MT, ROPE, false, true>(f, maps, smem, threads, st)
-              : strips_inst<MT, ROPE, false, false>(f, maps, smem, threads, st);
+        return k0 ? strips_inst<MT, ROPE, true, true, false>(f, maps, smem, threads, st)
+                  : strips_inst<MT, ROPE, true, false, false>(f, maps, smem, threads, st);
+    return k0 ? strips_inst<MT, ROPE, false, true, false>(f, maps, smem, threads, st)
+              : strips_inst<MT, ROPE, false, false, false>(f, maps, smem, threads, st);
 }
 
 template <int MT, bool ROPE>
@@ -466,11 +572,17 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
     const int CH = Gm::CH, HW = Gm::HW;
     const int D = s.D;
     if (D % CH != 0) return cudaErrorNotSupported;
-    const long long H = s.dims[0], W = s.dims[1];
+    const bool p3 = s.nd == 3;
+    const long long H = p3 ? s.dims[0] * s.dims[1] : s.dims[0], W = p3 ? s.dims[2] : s.dims[1];
     StripDesc f{};
     f.D = D;
-    f.nd = 2;
-    if (W <= 64) {
+    f.nd = s.nd;
+    f.O1 = p3 ? (int)s.dims[1] : 1;
+    if (p3) {
+        // inner axis = the last one; rows = (plane, row) pairs
+        if (W > 64 || H > 0x7fffffffLL) return cudaErrorNotSupported;
+        f.Q = (int)W; f.O = (int)H; f.k_in = 2; f.qstride = 1; f.ostride = W; f.lam_inner_fast = 1;
+    } else if (W <= 64) {
         f.Q = (int)W; f.O = (int)H; f.k_in = 1; f.qstride = 1; f.ostride = W; f.lam_inner_fast = 1;
     } else if (H <= 64) {
         f.Q = (int)H; f.O = (int)W; f.k_in = 0; f.qstride = W; f.ostride = 1; f.lam_inner_fast = 0;
@@ -478,27 +590,30 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
         return cudaErrorNotSupported;
     }
     if (s.has_lambda && (W % 4) != 0) return cudaErrorNotSupported;
-    f.Wc = SW_WC;
+    f.Wc = (p3 && W <= 32) ? 4 : SW_WC;
     f.S = (f.Q + f.Wc - 1) / f.Wc;
     f.clamp = s.clamp; f.amin = s.a_log_min; f.deflam = s.default_lambda;
     f.P = s.P;
     f.ntd = D / CH;
     f.ntiles = s.batch * f.ntd;
     using Ly = StripLayout<MT, ROPE>;
-    const int bbox = Ly::BBOX;
+    using Ly3 = StripLayout<MT, ROPE, true>;
+    using Ly34 = StripLayout<MT, ROPE, true, 4>;
+    const int bbox = Ly::BBOX / SW_WC * f.Wc;   // B / C box bytes at this strip width
     f.offC = Ly::offC;
     f.offX = Ly::offX;
-    f.offD = Ly::offD;
-    f.offL = Ly::offL;
-    f.st_bytes = Ly::bytes;
-    f.tx_bytes = (unsigned)(2 * bbox + 16 * f.Wc + 2 * 16 * f.Wc +
-                            (s.has_lambda ? (f.lam_inner_fast ? 4 * f.Wc : 16 * f.Wc) : 0));
+    f.offD = p3 ? Ly3::offD : Ly::offD;
+    f.offL = p3 ? Ly3::offL : Ly::offL;
+    f.st_bytes = p3 ? (f.Wc == 4 ? Ly34::bytes : Ly3::bytes) : Ly::bytes;
+    f.tx_bytes = (unsigned)(2 * bbox + 16 * f.Wc + s.nd * 16 * f.Wc +
+                            (s.has_lambda ? (f.lam_inner_fast ? 4 * f.Wc : 16 * f.Wc) : 0) +
+                            (p3 ? 2 * bbox + 16 * f.Wc : 0));
     f.red_y = HW > 1;
     f.ex2 = s.ex2;
     f.A = s.A; f.theta = s.theta; f.h = s.h; f.y = s.y; f.status = status;
     const unsigned long long P = s.P, Bn = s.batch, DM = (unsigned long long)D * MT;
     const unsigned long long qs = f.qstride, os = f.ostride;
-    CUtensorMap maps[5];
+    CUtensorMap maps[6];
     memset(maps, 0, sizeof(maps));
     {
         const unsigned long long dims[5] = {(unsigned long long)MT, (unsigned long long)D, (unsigned long long)f.Q,
@@ -507,6 +622,7 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
         const unsigned box[5] = {(unsigned)MT, (unsigned)CH, (unsigned)f.Wc, 1, 1};
         if (!tmap_encode(&maps[0], s.B, 5, dims, str, box)) return cudaErrorNotSupported;
         if (!tmap_encode(&maps[1], s.C, 5, dims, str, box)) return cudaErrorNotSupported;
+        if (p3 && !tmap_encode(&maps[5], s.h, 5, dims, str, box)) return cudaErrorNotSupported;
     }
     {
         const unsigned long long dims[4] = {(unsigned long long)D, (unsigned long long)f.Q, (unsigned long long)f.O, Bn};
@@ -515,12 +631,13 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
         if (!tmap_encode(&maps[2], s.x, 4, dims, str, box)) return cudaErrorNotSupported;
     }
     {
-        const unsigned long long dims[5] = {(unsigned long long)D, (unsigned long long)f.Q, (unsigned long long)f.O, 2, Bn};
-        const unsigned long long str[4] = {qs * D * 4, os * D * 4, P * D * 4, 2 * P * D * 4};
-        const unsigned box[5] = {4, (unsigned)f.Wc, 1, 2, 1};
+        const unsigned long long nd = (unsigned long long)s.nd;
+        const unsigned long long dims[5] = {(unsigned long long)D, (unsigned long long)f.Q, (unsigned long long)f.O, nd, Bn};
+        const unsigned long long str[4] = {qs * D * 4, os * D * 4, P * D * 4, nd * P * D * 4};
+        const unsigned box[5] = {4, (unsigned)f.Wc, 1, (unsigned)nd, 1};
         if (!tmap_encode(&maps[3], s.delta, 5, dims, str, box)) return cudaErrorNotSupported;
     }
-    if (s.has_lambda) {
+    if (s.has_lambda) {   // [H][W] per item (3D: H = planes x rows)
         const unsigned long long dims[3] = {(unsigned long long)W, (unsigned long long)H, Bn};
         const unsigned long long str[2] = {(unsigned long long)W * 4, P * 4};
         const unsigned box[3] = {f.lam_inner_fast ? (unsigned)f.Wc : 4u, f.lam_inner_fast ? 1u : (unsigned)f.Wc, 1};
@@ -528,6 +645,7 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
     } else {
         maps[4] = maps[2];
     }
+    if (!p3) maps[5] = maps[0];
     const int threads = f.S * HW * 32;
     const int hv = 32 * Gm::U;
     const int fixed = f.S * HW * SW_K * 2 * hv * 4 + (2 * f.S * SW_NSS_MAX + 2 * f.S * HW * SW_K) * 8;
@@ -535,6 +653,16 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
     while (f.nss > 2 && fixed + f.S * f.nss * f.st_bytes > 227 * 1024) f.nss--;
     const int smem = fixed + f.S * f.nss * f.st_bytes;
     if (smem > 227 * 1024) return cudaErrorNotSupported;
+    {
+        // the issuer runs min(nss, O1) rows ahead: row r (read back at row r + O1) must be fenced before
+        // the issue of row r + O1, which happens at the start of row r + O1 - ahead + 1
+        const int ahead = f.nss < f.O1 ? f.nss : f.O1;
+        int per = f.O1 - ahead + 1;
+        if (per > 16) per = 16;
+        if (per < 1) per = 1;
+        if (const char* e = getenv("KMB_FENCE_PERIOD")) per = atoi(e) > 0 ? atoi(e) : per;
+        f.fence_period = per;
+    }
     if (f.red_y) {
         cudaError_t e = cudaMemsetAsync(s.y, 0, (size_t)s.batch * s.P * D * sizeof(float), st);
         if (e != cudaSuccess) return e;
@@ -542,9 +670,10 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
     return strips_flags<MT, ROPE>(s, f, maps, smem, threads, st);
 }
 
-// 2D grids with an inner extent <= 64 and M in {16, 32, 64}.
+// 2D grids with an inner extent <= 64 and 3D grids whose last extent is <= 64 (reference-order expf
+// only), M in {16, 32, 64}.
 cudaError_t launch_scan_fwd_strips(const ScanDesc& s, int* status, cudaStream_t st) {
-    if (s.nd != 2 || s.fast_exp) return cudaErrorNotSupported;
+    if ((s.nd != 2 && s.nd != 3) || s.fast_exp || (s.nd == 3 && s.ex2)) return cudaErrorNotSupported;
     if (s.batch > 0x7fffffff || s.P > 0x7fffffffLL) return cudaErrorNotSupported;
     if (s.D % 4 != 0) return cudaErrorNotSupported;
     switch (s.M) {

@@ -91,6 +91,21 @@ def test_forward_shapes(kmb, cuda, dims, D, M, flags, path):
     _run_both(kmb, cuda, inp, expect_path=path)
 
 
+@pytest.mark.parametrize("dims,D,M,flags", [
+    ([4, 6, 8], 8, 16, dict(rope=True)),
+    ([3, 5, 16], 4, 32, dict(lam=True)),
+    ([5, 4, 12], 4, 64, dict(rope=True, lam=True)),   # partial last strip
+    ([3, 1, 8], 4, 16, {}),                            # one row per plane: no look-ahead
+    ([1, 8, 8], 4, 16, dict(rope=True)),               # one plane
+    ([16, 32, 32], 8, 16, dict(rope=True)),            # the {16,32,32} grid, fewer channels
+    ([6, 7, 40], 4, 32, dict(clamp=True, a_log_min=-2.0)),
+])
+def test_forward_3d_strips(kmb, cuda, dims, D, M, flags):
+    """3D grids run the strip kernel with the plane predecessor staged by TMA."""
+    inp = po.gen_scan(dims, D, M, batch=2, seed=sum(dims) * 3 + D, **flags)
+    _run_both(kmb, cuda, inp, expect_path=1)
+
+
 def test_headline_shape_channel_slice(kmb, cuda):
     """Headline geometry at full channel count (2D 64x64, D 512, M 64, batch 2):
     every (item, channel-pair) recurrence is independent, so a 16-channel
