@@ -4,8 +4,9 @@
 // activations), :509-528 (forward), :746-773 (backward).  On the B200 the L
 // per-point GEMVs of the reference become one packed GEMM over all batch rows:
 // P[BL, Rt] = X[BL, dim] . Wcat^T with Wcat = [W_in; delta_proj; lambda_proj;
-// W_B; W_C] (Rt = R + 2 + 2 N R rows), in fp32 through cuBLAS (plain library
-// GEMM; no TF32, the parity target is the fp32 reference).  One elementwise
+// W_B; W_C] (Rt = R + 2 + 2 N R rows), on the tensor cores at fp32 accuracy
+// (block_gemm.cu / gemm_tc.cu: split-bf16 pieces, stage-wise fp32 accumulation;
+// the parity target is the fp32 reference).  One elementwise
 // epilogue applies silu / softplus+clamp / sigmoid / biases and writes the
 // block-scan inputs; the backward mirrors it.  The backward is exact: it also
 // produces dW_in and the projection paths of dx, which the reference skips.
@@ -244,10 +245,10 @@ cudaError_t launch_proj_fwd_tc(const __nv_bfloat16* X, const float* Win, const f
                                int NR, float dt_min, float dt_max, const float* bB, const float* bC, float* P,
                                __nv_bfloat16* u, __nv_bfloat16* dt, __nv_bfloat16* lam, __nv_bfloat16* B,
                                __nv_bfloat16* C, int* status, cudaStream_t st);
-// 1: route the bf16 projections through cuBLAS + separate epilogues (tests / comparison)
+// 1: route the bf16 projections through the plain tensor-core GEMM + separate epilogues (tests / comparison)
 static thread_local int tl_no_tc = 0;
-static thread_local int tl_proj_path = -1;  // projection of the last bf16 forward: 1 tensor cores, 0 cuBLAS
-static thread_local int tl_dx_path = -1;    // dx GEMM of the last bf16 backward: 1 tensor cores, 0 cuBLAS
+static thread_local int tl_proj_path = -1;  // projection of the last bf16 forward: 1 fused tensor-core kernel, 0 plain GEMM
+static thread_local int tl_dx_path = -1;    // dx GEMM of the last bf16 backward: 1 fused tensor-core kernel, 0 plain GEMM
 cudaError_t launch_dx_tc(const __nv_bfloat16* dP, int ldp, const float* Win, const float* dp, const float* lp,
                          const float* WB, const float* WC, __nv_bfloat16* Wt, long long BL, int dim, int R, int NR,
                          const __nv_bfloat16* dout, __nv_bfloat16* dx, int* status, cudaStream_t st);
@@ -324,7 +325,7 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
     const bool bf = c->bf16_storage != 0;
     cudaError_t e;
     if (bf) {
-        // bf16 x bf16 -> fp32 projection GEMM (tensor cores through cuBLAS)
+        // bf16 x bf16 -> fp32 projection GEMM on the tensor cores
         __nv_bfloat16* Wb = (__nv_bfloat16*)workspace(WS_BLK_WBF, (size_t)a.Rt * dim * sizeof(__nv_bfloat16));
         if (!Wb) return set_error("workspace allocation failed");
         typedef __nv_bfloat16 H;

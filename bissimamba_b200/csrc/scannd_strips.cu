@@ -28,10 +28,22 @@
 #include "kmb_sync.cuh"
 #include "kmb_butterfly.cuh"
 #include <type_traits>
-#include <cstdlib>
 
 namespace kmb {
 int persistent_sms(int sms);  // SMs a persistent grid may fill (capi.cu)
+
+// packed fp32 pairs (per component exactly __fadd_rn / __fmul_rn / __fmaf_rn)
+#ifdef KMB_F2_EMUL
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)); }
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) { return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)); }
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+    return make_float2(__fmaf_rn(a.x, b.x, c.x), __fmaf_rn(a.y, b.y, c.y));
+}
+#else
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+#endif
 
 constexpr int SW_NSS_MAX = 4;  // stages per strip (fewer when shared memory is short)
 constexpr int SW_K = 4;        // handoff slots per strip boundary
@@ -313,6 +325,70 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             for (int j = 0; j < WC; j++) {
                 const float lam = LAMB ? Ls[j * (KIN0 ? 4 : 1)] : deflam;
                 float hn[U];
+                if constexpr (!EX2 && !P3) {
+                    // The lane's two channels as one float2 (.x = channel cl0, .y = cl0 + 1): the
+                    // reference-order operations of the scalar path below, two per packed
+                    // instruction (same IEEE rounding per component); expf stays per channel.
+                    const float2 x2 = *reinterpret_cast<const float2*>(Xs + j * 4);
+                    const float2 dI2 = *reinterpret_cast<const float2*>(DsI + j * 4);
+                    const float2 dO2 = *reinterpret_cast<const float2*>(DsO + j * 4);
+                    const float2 dt2 = f2add(dI2, dO2);
+                    const float2 omdt2 = f2mul(f2add(make_float2(1.0f, 1.0f), make_float2(-lam, -lam)), dt2);
+                    const float2 gam2 = f2mul(make_float2(lam, lam), dt2);
+#pragma unroll
+                    for (int sl = 0; sl < Gm::SPT; sl++) {
+                        const int u0 = sl * CPT, sofs = 32 * sl;
+                        const float2 bu2 = f2mul(make_float2(Bs[j * CH * MT + sofs], Bs[j * CH * MT + MT + sofs]), x2);
+                        const float2 zI = f2mul(dI2, make_float2(AI[u0], AI[u0 + 1]));
+                        const float2 aI2 = make_float2(expf(zI.x), expf(zI.y));
+                        const float2 hatI2 = (j == 0) ? make_float2(lh[u0], lh[u0 + 1])
+                                                      : make_float2(ring_h[j == 0 ? 0 : j - 1][u0], ring_h[j == 0 ? 0 : j - 1][u0 + 1]);
+                        const float2 buI2 = (j == 0) ? make_float2(lb[u0], lb[u0 + 1])
+                                                     : make_float2(ring_b[j == 0 ? 0 : j - 1][u0], ring_b[j == 0 ? 0 : j - 1][u0 + 1]);
+                        const float2 rh2 = make_float2(ring_h[j][u0], ring_h[j][u0 + 1]);
+                        const float2 rb2 = make_float2(ring_b[j][u0], ring_b[j][u0 + 1]);
+                        float2 buacc2, dacc2, hacc2;
+                        float inv;
+                        if (HASO) {
+                            const float2 zO = f2mul(dO2, make_float2(AO[u0], AO[u0 + 1]));
+                            const float2 aO2 = make_float2(expf(zO.x), expf(zO.y));
+                            if (j > 0 || w > 0) {
+                                buacc2 = KIN0 ? f2add(buI2, rb2) : f2add(rb2, buI2);
+                                dacc2 = KIN0 ? f2add(aI2, aO2) : f2add(aO2, aI2);
+                                hacc2 = KIN0 ? f2fma(aO2, rh2, f2mul(aI2, hatI2))
+                                             : f2fma(aI2, hatI2, f2mul(aO2, rh2));
+                                inv = 0.5f;
+                            } else {
+                                buacc2 = rb2;
+                                dacc2 = aO2;
+                                hacc2 = f2mul(aO2, rh2);
+                                inv = 1.0f;
+                            }
+                        } else if (j > 0 || w > 0) {
+                            buacc2 = buI2;
+                            dacc2 = aI2;
+                            hacc2 = f2mul(aI2, hatI2);
+                            inv = 1.0f;
+                        } else {
+                            buacc2 = dacc2 = hacc2 = make_float2(0.0f, 0.0f);
+                            inv = 0.0f;
+                        }
+                        const float2 inv2 = make_float2(inv, inv);
+                        const float2 beta2 = f2mul(omdt2, f2mul(dacc2, inv2));
+                        const float2 hn2 = f2add(f2fma(f2mul(buacc2, inv2), beta2, f2mul(bu2, gam2)), hacc2);
+                        hn[u0] = hn2.x;
+                        hn[u0 + 1] = hn2.y;
+                        ring_b[j][u0] = bu2.x;
+                        ring_b[j][u0 + 1] = bu2.y;
+                        if (j < ncol) {
+                            __stcs(hp + sofs, hn2.x);
+                            __stcs(hp + MT + sofs, hn2.y);
+                        }
+                        const float2 cy2 = f2mul(make_float2(Cs[j * CH * MT + sofs], Cs[j * CH * MT + MT + sofs]), hn2);
+                        prod[j][0] = sl == 0 ? cy2.x : __fadd_rn(prod[j][0], cy2.x);
+                        prod[j][1] = sl == 0 ? cy2.y : __fadd_rn(prod[j][1], cy2.y);
+                    }
+                } else {
 #pragma unroll
                 for (int u = 0; u < U; u++) {
                     const int c = u % CPT, sofs = 32 * (u / CPT);  // channel, state offset
@@ -436,6 +512,7 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                     const float cy = __fmul_rn(Cs[j * CH * MT + c * MT + sofs], hn[u]);
                     prod[j][c] = sofs == 0 ? cy : __fadd_rn(prod[j][c], cy);
                 }
+                }   // scalar path
                 if (ROPE) {
                     // the pair (2i, 2i+1) of state slot s is units (s CPT, s CPT + 1)
 #pragma unroll
@@ -660,7 +737,6 @@ static cudaError_t strips_launch(const ScanDesc& s, int* status, cudaStream_t st
         int per = f.O1 - ahead + 1;
         if (per > 16) per = 16;
         if (per < 1) per = 1;
-        if (const char* e = getenv("KMB_FENCE_PERIOD")) per = atoi(e) > 0 ? atoi(e) : per;
         f.fence_period = per;
     }
     if (f.red_y) {

@@ -101,17 +101,19 @@ size_t kmb_block_activation_floats(const KMBlockConfig *c, long batch);
 /* Reference mamba_block_forward_ws (src/mamba_block.c:509-528) for `batch`
  * items: x, out [batch, L, dim].  u = silu(W_in x), dt = clamp(softplus(
  * delta_proj.x), dt_min, dt_max), lambda = sigmoid(lambda_proj.x), B = W_B x + b_B,
- * C = W_C x + b_C, block scan, out = x + W_out y.  Projections are fp32 cuBLAS
- * GEMMs (no TF32).  act: kmb_block_activation_floats() floats. */
+ * C = W_C x + b_C, block scan, out = x + W_out y.  Projections run on the
+ * tensor cores at fp32 accuracy (split-bf16 pieces, fp32 accumulation; see
+ * kmamba_gemm.h).  act: kmb_block_activation_floats() floats. */
 /* bf16 storage: 1 (default) = block projections on the tensor cores with the
- * input epilogue fused (tcgen05); 0 = cuBLAS GEMMs and separate epilogues.
+ * input epilogue fused (tcgen05); 0 = the plain tensor-core GEMM and separate
+ * epilogues.
  * Per host thread; for comparison and tests. */
 void kmb_block_set_tensor_cores(int on);
 /* Projection used by this thread's last bf16 block forward: 1 = tensor cores,
- * 0 = cuBLAS, -1 = none yet. */
+ * 0 = plain GEMM + epilogue, -1 = none yet. */
 int kmb_block_last_projection_path(void);
 /* dx GEMM of this thread's last bf16 block backward: 1 = tensor cores (residual
- * fused), 0 = cuBLAS, -1 = none yet. */
+ * fused), 0 = plain GEMM + residual kernel, -1 = none yet. */
 int kmb_block_last_dx_path(void);
 int kmb_block_forward(const KMBlockConfig *c, const KMBlockWeights *w, const float *x, float *out,
                       long batch, float *act, void *stream);
