@@ -48,6 +48,11 @@
 namespace kmb {
 int persistent_sms(int sms);  // SMs a persistent grid may fill (capi.cu)
 
+// packed fp32 pairs (per component exactly __fadd_rn / __fmul_rn / __fmaf_rn)
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
 constexpr int BS_K = 4;    // handoff slots per strip boundary
 
 struct BwdStripDesc {
@@ -278,100 +283,106 @@ __global__ void __launch_bounds__(WC == 8 ? 256 : 512, 1) scan_bwd_strips(const 
                 const float2 dI2 = *(const float2*)(sO + Gm::DIO + j * CH + cl0);
                 const float2 dO2 = *(const float2*)(sO + Gm::DOO + j * CH + cl0);
                 const float2 dy2 = *(const float2*)(sO + Gm::DYO + j * CH + cl0);
-                float ah[2], ab[2], gh[2];
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    ah[c] = rP[c] + dP[j][c];
-                    ab[c] = rQ[c] + dQ[j][c];
-                }
-                const float h0 = hO[j][0], h1 = hO[j][1];
-                const float lh0 = j > 0 ? hO[j > 0 ? j - 1 : 0][0] : hL[0];
-                const float lh1 = j > 0 ? hO[j > 0 ? j - 1 : 0][1] : hL[1];
+                // Both channels of the lane as packed fp32 pairs (.x = channel dl0, .y = dl0 + 1): the
+                // same IEEE operations per channel as a scalar loop over the two, half the instructions.
+                const float2 ah2 = f2add(make_float2(rP[0], rP[1]), make_float2(dP[j][0], dP[j][1]));
+                const float2 ab2 = f2add(make_float2(rQ[0], rQ[1]), make_float2(dQ[j][0], dQ[j][1]));
+                const float2 h2 = make_float2(hO[j][0], hO[j][1]);
+                const float2 lh2 = j > 0 ? make_float2(hO[j > 0 ? j - 1 : 0][0], hO[j > 0 ? j - 1 : 0][1])
+                                         : make_float2(hL[0], hL[1]);
+                // R v for the pair v: (cth v0 - sth v1, sth v0 + cth v1); R^T a: (cth a0 + sth a1, cth a1 - sth a0)
+                auto rot = [&](float2 v) {
+                    const float2 m = f2mul(make_float2(sth, cth), make_float2(v.y, v.y));
+                    return f2fma(make_float2(cth, sth), make_float2(v.x, v.x), make_float2(-m.x, m.y));
+                };
+                float2 gh2;
                 if (ROPE) {
-                    gh[0] = __fmaf_rn(cth, ah[0], __fmul_rn(sth, ah[1]));
-                    gh[1] = __fmaf_rn(cth, ah[1], -__fmul_rn(sth, ah[0]));
-                    const float hat0 = __fmaf_rn(cth, h0, -__fmul_rn(sth, h1));
-                    const float hat1 = __fmaf_rn(sth, h0, __fmul_rn(cth, h1));
-                    gth = __fmaf_rn(ah[1], hat0, __fmaf_rn(-ah[0], hat1, gth));
+                    const float2 m = f2mul(make_float2(sth, sth), make_float2(ah2.y, ah2.x));
+                    gh2 = f2fma(make_float2(cth, cth), ah2, make_float2(m.x, -m.y));
+                    const float2 hat = rot(h2);
+                    gth = __fmaf_rn(ah2.y, hat.x, __fmaf_rn(-ah2.x, hat.y, gth));
                 } else {
-                    gh[0] = ah[0];
-                    gh[1] = ah[1];
+                    gh2 = ah2;
                 }
                 const float oml = __fsub_rn(1.0f, lam);
-                float red_eI[2], red_eO[2], red_gx[2], glam_l = 0.0f;
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    const float xv = c ? xo.y : xo.x;
-                    const float dI = c ? dI2.y : dI2.x;
-                    const float dO = c ? dO2.y : dO2.x;
-                    const float dyv = c ? dy2.y : dy2.x;
-                    const float hv = c ? h1 : h0;
-                    const float Bv = bO[j][c];
-                    const float g = __fmaf_rn(cO[j][c], dyv, gh[c]);
-                    const int eo = ro + j * DM + c * M;
-                    const float dt = __fadd_rn(dO, dI);
-                    const float bu = __fmul_rn(Bv, xv);
-                    const float gam = __fmul_rn(lam, dt);
-                    float gdt = __fmul_rn(__fmul_rn(lam, bu), g);
-                    float gl = __fmul_rn(__fmul_rn(dt, bu), g);
-                    float PI = 0.0f, PO = 0.0f, Qv = 0.0f, eI = 0.0f, eO = 0.0f;
-                    if (HASU || hasL) {
-                        float aI = 0.0f, aO = 0.0f, sbu = 0.0f, hatL = 0.0f, hatU = 0.0f;
-                        if (hasL) {
-                            aI = kmb_ex2(__fmul_rn(dI, AIL[c]));
-                            const float bl = j > 0 ? bO[j > 0 ? j - 1 : 0][c] : bL[c];
-                            sbu = __fmul_rn(bl, c ? xl.y : xl.x);
-                            hatL = ROPE ? (c ? __fmaf_rn(sth, lh0, __fmul_rn(cth, lh1))
-                                             : __fmaf_rn(cth, lh0, -__fmul_rn(sth, lh1)))
-                                        : (c ? lh1 : lh0);
-                        }
-                        if (HASU) {
-                            aO = kmb_ex2(__fmul_rn(dO, AOL[c]));
-                            sbu = __fmaf_rn(bP[j][c], c ? xu.y : xu.x, sbu);
-                            const float u0 = hP[j][0], u1 = hP[j][1];
-                            hatU = ROPE ? (c ? __fmaf_rn(sth, u0, __fmul_rn(cth, u1))
-                                             : __fmaf_rn(cth, u0, -__fmul_rn(sth, u1)))
-                                        : (c ? u1 : u0);
-                        }
-                        const float ma = __fmul_rn(__fadd_rn(aI, aO), inv);   // mean alpha
-                        const float mb = __fmul_rn(sbu, inv);                  // mean predecessor Bu
-                        const float omdt = __fmul_rn(oml, dt);
-                        PI = __fmul_rn(aI, g);
-                        PO = __fmul_rn(aO, g);
-                        Qv = __fmul_rn(__fmul_rn(__fmul_rn(omdt, ma), inv), g);
-                        const float mab = __fmul_rn(ma, mb);
-                        gdt = __fmaf_rn(__fmul_rn(oml, mab), g, gdt);
-                        gl = __fmaf_rn(-__fmul_rn(dt, mab), g, gl);
-                        const float ka = __fmul_rn(__fmul_rn(omdt, inv), mb);   // d h / d a_k beyond the state term
-                        if (hasL) {
-                            const float dz = __fmul_rn(PI, __fadd_rn(hatL, ka));   // (d a / d z) g (...) with d a / d z = a
-                            eI = __fmul_rn(dz, AI[c]);
-                            gAI[c] = clI[c] ? gAI[c] : __fmaf_rn(dz, dI, gAI[c]);
-                        }
-                        if (HASU) {
-                            const float dz = __fmul_rn(PO, __fadd_rn(hatU, ka));
-                            eO = __fmul_rn(dz, AO[c]);
-                            gAO[c] = clO[c] ? gAO[c] : __fmaf_rn(dz, dO, gAO[c]);
-                        }
+                const float2 oml2 = make_float2(oml, oml), lam2 = make_float2(lam, lam);
+                const float2 B2 = make_float2(bO[j][0], bO[j][1]);
+                const float2 g2 = f2fma(make_float2(cO[j][0], cO[j][1]), dy2, gh2);
+                const float2 dt2 = f2add(dO2, dI2);
+                const float2 bu2 = f2mul(B2, xo);
+                const float2 gam2 = f2mul(lam2, dt2);
+                float2 gdt2 = f2mul(f2mul(lam2, bu2), g2);
+                float2 gl2 = f2mul(f2mul(dt2, bu2), g2);
+                const float2 z2 = make_float2(0.0f, 0.0f);
+                float2 PI2 = z2, PO2 = z2, Qv2 = z2, eI2 = z2, eO2 = z2;
+                if (HASU || hasL) {
+                    float2 aI2 = z2, aO2 = z2, sbu2 = z2, hatL2 = z2, hatU2 = z2;
+                    if (hasL) {
+                        const float2 za = f2mul(dI2, make_float2(AIL[0], AIL[1]));
+                        aI2 = make_float2(kmb_ex2(za.x), kmb_ex2(za.y));
+                        const float2 bl2 = j > 0 ? make_float2(bO[j > 0 ? j - 1 : 0][0], bO[j > 0 ? j - 1 : 0][1])
+                                                 : make_float2(bL[0], bL[1]);
+                        sbu2 = f2mul(bl2, xl);
+                        hatL2 = ROPE ? rot(lh2) : lh2;
                     }
-                    const float gbu = __fmaf_rn(gam, g, ab[c]);
-                    if (OVW) {
-                        __stcs(dCb + eo, __fmul_rn(dyv, hv));
-                        __stcs(dBb + eo, __fmul_rn(gbu, xv));
-                    } else {
-                        atomicAdd(dCb + eo, __fmul_rn(dyv, hv));
-                        atomicAdd(dBb + eo, __fmul_rn(gbu, xv));
+                    if (HASU) {
+                        const float2 za = f2mul(dO2, make_float2(AOL[0], AOL[1]));
+                        aO2 = make_float2(kmb_ex2(za.x), kmb_ex2(za.y));
+                        sbu2 = f2fma(make_float2(bP[j][0], bP[j][1]), xu, sbu2);
+                        const float2 u2 = make_float2(hP[j][0], hP[j][1]);
+                        hatU2 = ROPE ? rot(u2) : u2;
                     }
-                    red_eI[c] = __fadd_rn(eI, gdt);
-                    red_eO[c] = __fadd_rn(eO, gdt);
-                    red_gx[c] = __fmul_rn(gbu, Bv);
-                    glam_l = __fadd_rn(glam_l, gl);
-                    // pass to the predecessors: (P_in, Q) left, (P_out, Q) up
-                    dP[j][c] = PO;
-                    dQ[j][c] = Qv;
-                    rP[c] = PI;
-                    rQ[c] = Qv;
+                    const float2 inv2 = make_float2(inv, inv);
+                    const float2 ma2 = f2mul(f2add(aI2, aO2), inv2);   // mean alpha
+                    const float2 mb2 = f2mul(sbu2, inv2);                 // mean predecessor Bu
+                    const float2 omdt2 = f2mul(oml2, dt2);
+                    PI2 = f2mul(aI2, g2);
+                    PO2 = f2mul(aO2, g2);
+                    Qv2 = f2mul(f2mul(f2mul(omdt2, ma2), inv2), g2);
+                    const float2 mab2 = f2mul(ma2, mb2);
+                    gdt2 = f2fma(f2mul(oml2, mab2), g2, gdt2);
+                    const float2 dm = f2mul(dt2, mab2);
+                    gl2 = f2fma(make_float2(-dm.x, -dm.y), g2, gl2);
+                    const float2 ka2 = f2mul(f2mul(omdt2, inv2), mb2);   // d h / d a_k beyond the state term
+                    if (hasL) {
+                        const float2 dz = f2mul(PI2, f2add(hatL2, ka2));   // (d a / d z) g (...) with d a / d z = a
+                        eI2 = f2mul(dz, make_float2(AI[0], AI[1]));
+                        const float2 t = f2fma(dz, dI2, make_float2(gAI[0], gAI[1]));
+                        gAI[0] = clI[0] ? gAI[0] : t.x;
+                        gAI[1] = clI[1] ? gAI[1] : t.y;
+                    }
+                    if (HASU) {
+                        const float2 dz = f2mul(PO2, f2add(hatU2, ka2));
+                        eO2 = f2mul(dz, make_float2(AO[0], AO[1]));
+                        const float2 t = f2fma(dz, dO2, make_float2(gAO[0], gAO[1]));
+                        gAO[0] = clO[0] ? gAO[0] : t.x;
+                        gAO[1] = clO[1] ? gAO[1] : t.y;
+                    }
                 }
+                const float2 gbu2 = f2fma(gam2, g2, ab2);
+                const float2 vC = f2mul(dy2, h2), vB = f2mul(gbu2, xo);
+                {
+                    const int eo = ro + j * DM;
+                    if (OVW) {
+                        __stcs(dCb + eo, vC.x);
+                        __stcs(dBb + eo, vB.x);
+                        __stcs(dCb + eo + M, vC.y);
+                        __stcs(dBb + eo + M, vB.y);
+                    } else {
+                        atomicAdd(dCb + eo, vC.x);
+                        atomicAdd(dBb + eo, vB.x);
+                        atomicAdd(dCb + eo + M, vC.y);
+                        atomicAdd(dBb + eo + M, vB.y);
+                    }
+                }
+                const float2 reI = f2add(eI2, gdt2), reO = f2add(eO2, gdt2), rgx = f2mul(gbu2, B2);
+                const float glam_l = __fadd_rn(__fadd_rn(0.0f, gl2.x), gl2.y);
+                // pass to the predecessors: (P_in, Q) left, (P_out, Q) up
+                dP[j][0] = PO2.x; dP[j][1] = PO2.y;
+                dQ[j][0] = Qv2.x; dQ[j][1] = Qv2.y;
+                rP[0] = PI2.x; rP[1] = PI2.y;
+                rQ[0] = Qv2.x; rQ[1] = Qv2.y;
+                const float red_eI[2] = {reI.x, reI.y}, red_eO[2] = {reO.x, reO.y}, red_gx[2] = {rgx.x, rgx.y};
                 float* rr = my_red + (j * 4) * RS;
                 *(float2*)(rr + 0 * RS + 2 * lane) = make_float2(red_eI[0], red_eI[1]);
                 *(float2*)(rr + 1 * RS + 2 * lane) = make_float2(red_eO[0], red_eO[1]);

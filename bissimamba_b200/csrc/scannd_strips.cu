@@ -325,14 +325,16 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
             for (int j = 0; j < WC; j++) {
                 const float lam = LAMB ? Ls[j * (KIN0 ? 4 : 1)] : deflam;
                 float hn[U];
-                if constexpr (!EX2 && !P3) {
+                if constexpr (!EX2) {
                     // The lane's two channels as one float2 (.x = channel cl0, .y = cl0 + 1): the
                     // reference-order operations of the scalar path below, two per packed
                     // instruction (same IEEE rounding per component); expf stays per channel.
                     const float2 x2 = *reinterpret_cast<const float2*>(Xs + j * 4);
                     const float2 dI2 = *reinterpret_cast<const float2*>(DsI + j * 4);
                     const float2 dO2 = *reinterpret_cast<const float2*>(DsO + j * 4);
-                    const float2 dt2 = f2add(dI2, dO2);
+                    // dt: the deltas summed in axis order (2D: inner + outer, commutative; 3D: plane, row, inner)
+                    const float2 dP2 = P3 ? *reinterpret_cast<const float2*>(DsP + j * 4) : make_float2(0.0f, 0.0f);
+                    const float2 dt2 = P3 ? f2add(f2add(dP2, dO2), dI2) : f2add(dI2, dO2);
                     const float2 omdt2 = f2mul(f2add(make_float2(1.0f, 1.0f), make_float2(-lam, -lam)), dt2);
                     const float2 gam2 = f2mul(make_float2(lam, lam), dt2);
 #pragma unroll
@@ -349,7 +351,56 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                         const float2 rb2 = make_float2(ring_b[j][u0], ring_b[j][u0 + 1]);
                         float2 buacc2, dacc2, hacc2;
                         float inv;
-                        if (HASO) {
+                        if constexpr (P3) {
+                            // three axes in axis order (plane, row, inner); means as sum / n, n = 3 an
+                            // IEEE division; hn as in the scalar 3D path
+                            int n = 0;
+                            buacc2 = dacc2 = hacc2 = make_float2(0.0f, 0.0f);
+                            if (HASP) {
+                                const float2 zP = f2mul(dP2, make_float2(AP[u0], AP[u0 + 1]));
+                                const float2 aP2 = make_float2(expf(zP.x), expf(zP.y));
+                                const float* hb = Hp + j * CH * MT + sofs;
+                                float2 hatP2 = make_float2(hb[0], hb[MT]);
+                                if (ROPE) {
+                                    const float2 m = f2mul(make_float2(sth, cth), make_float2(hatP2.y, hatP2.y));
+                                    hatP2 = f2fma(make_float2(cth, sth), make_float2(hatP2.x, hatP2.x), make_float2(-m.x, m.y));
+                                }
+                                buacc2 = f2mul(make_float2(Bp[j * CH * MT + sofs], Bp[j * CH * MT + MT + sofs]),
+                                               make_float2(Xp[j * 4], Xp[j * 4 + 1]));
+                                dacc2 = aP2;
+                                hacc2 = f2mul(aP2, hatP2);
+                                n = 1;
+                            }
+                            if (HASO) {
+                                const float2 zO = f2mul(dO2, make_float2(AO[u0], AO[u0 + 1]));
+                                const float2 aO2 = make_float2(expf(zO.x), expf(zO.y));
+                                if (n == 0) {
+                                    buacc2 = rb2; dacc2 = aO2; hacc2 = f2mul(aO2, rh2);
+                                } else {
+                                    buacc2 = f2add(buacc2, rb2);
+                                    dacc2 = f2add(dacc2, aO2);
+                                    hacc2 = f2fma(aO2, rh2, hacc2);
+                                }
+                                n++;
+                            }
+                            if (j > 0 || w > 0) {
+                                if (n == 0) {
+                                    buacc2 = buI2; dacc2 = aI2; hacc2 = f2mul(aI2, hatI2);
+                                } else {
+                                    buacc2 = f2add(buacc2, buI2);
+                                    dacc2 = f2add(dacc2, aI2);
+                                    hacc2 = f2fma(aI2, hatI2, hacc2);
+                                }
+                                n++;
+                            }
+                            const float2 buavg = n == 3 ? make_float2(__fdiv_rn(buacc2.x, 3.0f), __fdiv_rn(buacc2.y, 3.0f))
+                                               : n == 2 ? f2mul(buacc2, make_float2(0.5f, 0.5f)) : buacc2;
+                            const float2 alavg = n == 3 ? make_float2(__fdiv_rn(dacc2.x, 3.0f), __fdiv_rn(dacc2.y, 3.0f))
+                                               : n == 2 ? f2mul(dacc2, make_float2(0.5f, 0.5f)) : dacc2;
+                            const float2 hn3 = f2add(f2fma(buavg, f2mul(omdt2, alavg), f2mul(bu2, gam2)), hacc2);
+                            buacc2 = hn3;   // carried to the stores below
+                            inv = -1.0f;
+                        } else if (HASO) {
                             const float2 zO = f2mul(dO2, make_float2(AO[u0], AO[u0 + 1]));
                             const float2 aO2 = make_float2(expf(zO.x), expf(zO.y));
                             if (j > 0 || w > 0) {
@@ -374,15 +425,21 @@ scan_fwd_strips(const __grid_constant__ StripDesc f,
                             inv = 0.0f;
                         }
                         const float2 inv2 = make_float2(inv, inv);
-                        const float2 beta2 = f2mul(omdt2, f2mul(dacc2, inv2));
-                        const float2 hn2 = f2add(f2fma(f2mul(buacc2, inv2), beta2, f2mul(bu2, gam2)), hacc2);
+                        const float2 hn2 = P3 ? buacc2
+                                              : f2add(f2fma(f2mul(buacc2, inv2), f2mul(omdt2, f2mul(dacc2, inv2)),
+                                                            f2mul(bu2, gam2)), hacc2);
                         hn[u0] = hn2.x;
                         hn[u0 + 1] = hn2.y;
                         ring_b[j][u0] = bu2.x;
                         ring_b[j][u0 + 1] = bu2.y;
                         if (j < ncol) {
-                            __stcs(hp + sofs, hn2.x);
-                            __stcs(hp + MT + sofs, hn2.y);
+                            if (P3) {   // read back by the next plane (keep in L2)
+                                hp[sofs] = hn2.x;
+                                hp[MT + sofs] = hn2.y;
+                            } else {
+                                __stcs(hp + sofs, hn2.x);
+                                __stcs(hp + MT + sofs, hn2.y);
+                            }
                         }
                         const float2 cy2 = f2mul(make_float2(Cs[j * CH * MT + sofs], Cs[j * CH * MT + MT + sofs]), hn2);
                         prod[j][0] = sl == 0 ? cy2.x : __fadd_rn(prod[j][0], cy2.x);
