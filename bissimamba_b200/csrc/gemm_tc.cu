@@ -600,16 +600,19 @@ cudaError_t gemm_split(int kind, const float* x, void* const* out, long long row
                        long long ldo, cudaStream_t st) {
     if (rows * cols <= 0) return cudaSuccess;
     if (kind != KIND_TF32X3 && kind != KIND_BF16X6 && kind != KIND_BF16X9) return cudaErrorInvalidValue;
-    bool vec = cols % 4 == 0 && ldx % 4 == 0 && ldo % 4 == 0 && !((uintptr_t)x & 15);
+    // the four-column form may also split the row padding up to a multiple of 4 when both row strides
+    // cover it: the GEMM's tensor maps stop at the true K, so padded pieces are never read
+    const long long cols4 = (cols + 3) & ~3LL;
+    bool vec = ldx % 4 == 0 && ldo % 4 == 0 && ldx >= cols4 && ldo >= cols4 && !((uintptr_t)x & 15);
     for (int p = 0; p < (kind == KIND_TF32X3 ? 2 : 3); p++) vec = vec && !((uintptr_t)out[p] & 15);
     if (vec) {
-        const long long n = rows * (cols / 4);
+        const long long n = rows * (cols4 / 4);
         const unsigned g = (unsigned)((n + 255) / 256);
         if (kind == KIND_TF32X3)
-            split_tf32<<<g, 256, 0, st>>>(x, (float*)out[0], (float*)out[1], rows, (int)(cols / 4), ldx, ldo);
+            split_tf32<<<g, 256, 0, st>>>(x, (float*)out[0], (float*)out[1], rows, (int)(cols4 / 4), ldx, ldo);
         else
             split_bf16x3<<<g, 256, 0, st>>>(x, (__nv_bfloat16*)out[0], (__nv_bfloat16*)out[1],
-                                            (__nv_bfloat16*)out[2], rows, (int)(cols / 4), ldx, ldo);
+                                            (__nv_bfloat16*)out[2], rows, (int)(cols4 / 4), ldx, ldo);
     } else {
         const long long n = rows * cols;
         split_any<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(kind, x, out[0], out[1], out[2], rows, cols, ldx, ldo);
