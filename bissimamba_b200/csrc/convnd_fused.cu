@@ -46,19 +46,20 @@ template <int N> struct CfVec;
 template <> struct CfVec<4> { using T = float4; };
 template <> struct CfVec<2> { using T = float2; };
 template <> struct CfVec<1> { using T = float; };
+// packed fp32 pairs: per component exactly __fmaf_rn / __fadd_rn, two channels per instruction
 __device__ __forceinline__ void cf_fma(float4& a, const float4 x, const float4 y) {
-    a.x = __fmaf_rn(x.x, y.x, a.x);
-    a.y = __fmaf_rn(x.y, y.y, a.y);
-    a.z = __fmaf_rn(x.z, y.z, a.z);
-    a.w = __fmaf_rn(x.w, y.w, a.w);
+    const float2 lo = __ffma2_rn(make_float2(x.x, x.y), make_float2(y.x, y.y), make_float2(a.x, a.y));
+    const float2 hi = __ffma2_rn(make_float2(x.z, x.w), make_float2(y.z, y.w), make_float2(a.z, a.w));
+    a = make_float4(lo.x, lo.y, hi.x, hi.y);
 }
-__device__ __forceinline__ void cf_fma(float2& a, const float2 x, const float2 y) {
-    a.x = __fmaf_rn(x.x, y.x, a.x);
-    a.y = __fmaf_rn(x.y, y.y, a.y);
-}
+__device__ __forceinline__ void cf_fma(float2& a, const float2 x, const float2 y) { a = __ffma2_rn(x, y, a); }
 __device__ __forceinline__ void cf_fma(float& a, const float x, const float y) { a = __fmaf_rn(x, y, a); }
-__device__ __forceinline__ void cf_add(float4& a, const float4 x) { a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w; }
-__device__ __forceinline__ void cf_add(float2& a, const float2 x) { a.x += x.x; a.y += x.y; }
+__device__ __forceinline__ void cf_add(float4& a, const float4 x) {
+    const float2 lo = __fadd2_rn(make_float2(a.x, a.y), make_float2(x.x, x.y));
+    const float2 hi = __fadd2_rn(make_float2(a.z, a.w), make_float2(x.z, x.w));
+    a = make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ void cf_add(float2& a, const float2 x) { a = __fadd2_rn(a, x); }
 __device__ __forceinline__ void cf_add(float& a, const float x) { a += x; }
 template <typename V> __device__ __forceinline__ V cf_zero();
 template <> __device__ __forceinline__ float4 cf_zero<float4>() { return make_float4(0.f, 0.f, 0.f, 0.f); }
@@ -314,8 +315,9 @@ static bool cf_plan(const ConvDesc& c, int mode, FusedGeom* g, int* smem, int* R
         T0 = T0 / *R * *R;
         if (T0 < *R) T0 = *R;
     }
-    while (T0 > 1 && bytes(T0) > CF_SMEM_MAX) T0 = c.nd == 1 ? T0 / 2 / *R * *R : T0 - 1;
-    if (T0 < 1 || bytes(T0) > CF_SMEM_MAX) return false;
+    const int smax = CF_SMEM_MAX;
+    while (T0 > 1 && bytes(T0) > smax) T0 = c.nd == 1 ? T0 / 2 / *R * *R : T0 - 1;
+    if (T0 < 1 || bytes(T0) > smax) return false;
     if (c.nd == 1 && T0 % *R) return false;
     g->T0 = T0;
     g->nslab = (int)((c.dims[0] + T0 - 1) / T0);
@@ -347,7 +349,8 @@ static cudaError_t cf_launch_t(const ConvDesc& c, const FusedGeom& g, int smem, 
                                const float* bias, const float* dy, float* out, float* din, float* part,
                                cudaStream_t st) {
     // one channel per thread in 3D (27 taps of kernel values and dkernel accumulators in registers,
-    // two CTAs per SM), two elsewhere
+    // two CTAs per SM; two channels as packed pairs need ~240 registers and one CTA per SM, measured
+    // 0.42 ms against 0.31 ms), two channels as packed fp32 pairs elsewhere
     constexpr int N = ND == 3 ? 1 : 2;
     constexpr int CG = ND == 3 ? 1 : 2;
     auto k = conv_fused_kernel<ND, K, R, MODE, N, CG>;
