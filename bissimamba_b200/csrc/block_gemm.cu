@@ -366,7 +366,7 @@ static cudaError_t mm_tn_kind(int kind, bool bf16, long long M, long long N, lon
                               cudaStream_t st) {
     const bool pieces_mn = !bf16 && (kind == KIND_BF16X6_ || kind == KIND_BF16X9_);
     const bool direct = bf16 || pieces_mn;   // MN-major operands read in place
-    const long long tiles = ((M + 127) / 128) * ((N + (direct && !bf16 ? 127 : 255)) / (direct && !bf16 ? 128 : 256));
+    const long long tiles = ((M + 127) / 128) * ((N + (bf16 ? 255 : 191)) / (bf16 ? 256 : 192));
     int nsplit = (int)((148 + tiles - 1) / tiles);
     const long long kb = (K + 63) / 64;
     if (nsplit > kb) nsplit = (int)kb;

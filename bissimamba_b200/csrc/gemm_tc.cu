@@ -19,12 +19,14 @@
 //                artificial intelligence datatype for higher-precision
 //                computations", ARITH 2019);
 //   KIND_BF16X9  the same with all nine products.
-// One CTA per 128-row tile of A and up to 256 columns of B (one TMEM
-// accumulator); grid.x walks the column tiles, so the CTAs that share an A
-// tile run together and read it from L2.  Warp 0 issues TMA loads (128-byte
-// swizzled tiles, 128 bytes of K per K-major row or 64 K rows per MN-major
-// tile, a ring of stages), warp 1 allocates TMEM and issues the MMAs, warps
-// 2-5 read the accumulator back (tcgen05.ld) and store.
+// One CTA per 128-row tile of A and a column tile of B; grid.x walks the
+// column tiles, so the CTAs that share an A tile run together and read it
+// from L2.  Warp 0 issues TMA loads into a ring of stages, warp 1 allocates
+// TMEM and issues the MMAs, warps 2-9 read the accumulator back (tcgen05.ld)
+// and store through shared memory.  bf16: 128-byte swizzled rows (64 K per
+// stage), up to 256 columns, two CTAs per SM.  fp32 kinds: 64-byte swizzled
+// rows (32 K per stage), up to 192 columns, three stages of the operand
+// pieces, one CTA per SM.
 // The fp32 kinds do not let one TMEM accumulator run over all of K: the
 // tensor core's accumulation drifts with the number of products it adds (its
 // error grows about as sqrt(K) relative to sum |a b|, where an fp32 FMA loop's
@@ -55,8 +57,8 @@ struct GemmTCDesc {
     long long kchunk;          // K per split (a multiple of the stage depth)
     int ncols_max;             // columns per CTA (<= 256)
     int stages, a_bytes, b_bytes, stage_bytes;
-    unsigned mn_lbo, mn_sbo;   // MN-major descriptor strides (bytes)
     int kflush;                // fp32 kinds: MMA K steps per TMEM buffer (1, 2 or 4)
+    int tbuf;                  // fp32 kinds: TMEM columns per buffer (128 or 192)
     float* D;
     long long ldd;
     long long split_stride;    // elements between the splits' partial outputs
@@ -90,12 +92,12 @@ __device__ __forceinline__ void g_tma_2d(uint32_t dst, const CUtensorMap* map, u
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
         ::"r"(dst), "l"((unsigned long long)map), "r"(bar), "r"(c0), "r"(c1) : "memory");
 }
-// 128-byte swizzled shared-memory matrix descriptor (sm_100 form: bit 46 set, swizzle mode 2 in bits 61-63).
-// K-major: 8-row groups 1024 B apart (SBO), LBO unused.  MN-major: LBO = bytes between 64-element
-// MN blocks, SBO = bytes between 8-row K groups.
-__device__ __forceinline__ uint64_t g_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Swizzled shared-memory matrix descriptor (sm_100 form: bit 46 set; layout type in bits 61-63: 2 = 128-byte,
+// 4 = 64-byte swizzle).  K-major: 8-row groups SBO apart (8 rows of the swizzle width), LBO unused.  MN-major:
+// LBO = bytes between MN blocks (one TMA box apart), SBO = bytes between 8-row K groups.
+__device__ __forceinline__ uint64_t g_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t mode) {
     const uint64_t lo = (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16);
-    const uint64_t hi = (uint64_t)((sbo >> 4) & 0x3FFF) | ((uint64_t)1 << 14) | ((uint64_t)2 << 29);
+    const uint64_t hi = (uint64_t)((sbo >> 4) & 0x3FFF) | ((uint64_t)1 << 14) | ((uint64_t)mode << 29);
     return lo | (hi << 32);
 }
 // instruction descriptor: fp32 accumulator, A / B format (1 = bf16, 2 = tf32), major-ness (bit 15 A,
@@ -154,46 +156,66 @@ __device__ __forceinline__ void g_ld64(uint32_t taddr, float* v) {
     for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// The epilogue's 256 threads (warps 2-9: lane quarter q = warp % 4 of TMEM, column half hh) write a
-// 128 x 128 fp32 block through shared memory so that global stores are whole 128-byte rows: row-major
-// tile with a 129-float stride (conflict-free both ways).  Each thread holds 64 columns of its row.
-constexpr int EPI_LD = 129;
-constexpr int EPI_THREADS = 256;
+// 32 consecutive TMEM columns of this warp's 32 lanes, waited for inside the same asm
+__device__ __forceinline__ void g_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// The epilogue's 256 threads (warps 2-9: lane quarter q = warp % 4 of TMEM, column group hh) write the CTA's
+// fp32 block through shared memory so that global stores are whole 128-byte rows: a row-major tile of TW
+// columns with a TW + 1 float stride (conflict-free both ways; bf16 passes 128 columns at a time, the fp32
+// kinds all of their <= 192 columns at once).
+constexpr int EPI_WARPS = 8;
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-template <int EPI>
-__device__ __forceinline__ void epi_flush(float* tile, int q, int hh, const float* vals, int cols_here, float* D,
-                                          long long ldd, long long m0, long long M, long long col0, long long N,
-                                          int lane, bool write) {
-    // every epilogue thread reaches both barriers; `write` only gates the stores
+template <int EPI, int NV, int TW>
+__device__ __forceinline__ void epi_flush(float* tile, int q, int hh, const float* vals, int nv, int cb,
+                                          int cols_here, float* D, long long ldd, long long m0, long long M,
+                                          long long col0, long long N, int lane, bool write) {
+    // every epilogue thread reaches both barriers; `write` only gates the stores.  This thread holds
+    // tile columns cb .. cb + nv - 1 of its row (nv <= NV).
+    constexpr int LD = TW + 1;
     const int rl = q * 32 + lane;
 #pragma unroll
-    for (int c = 0; c < 64; c++)
-        if (hh * 64 + c < cols_here) tile[rl * EPI_LD + hh * 64 + c] = vals[c];
+    for (int c = 0; c < NV; c++)
+        if (c < nv && cb + c < cols_here) tile[rl * LD + cb + c] = vals[c];
     epi_bar();
     // epilogue warp e = hh * 4 + q writes rows 16 e .. 16 e + 15, lanes along the columns; EPI_ADD loads
-    // four rows' worth of D before it stores any, so the loads overlap
+    // two rows' worth of D before it stores any, so the loads overlap
     const int e = hh * 4 + q;
+    constexpr int KW = TW / 32;
     if (write) {
-        for (int i0 = 0; i0 < 16; i0 += 4) {
-            float g[4][4];
+        for (int i0 = 0; i0 < 16; i0 += 2) {
+            float g[2][KW];
             if (EPI == EPI_ADD) {
 #pragma unroll
-                for (int i = 0; i < 4; i++)
+                for (int i = 0; i < 2; i++)
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
+                    for (int k = 0; k < KW; k++) {
                         const int r = e * 16 + i0 + i, c = lane + 32 * k;
                         const long long row = m0 + r, col = col0 + c;
                         g[i][k] = (row < M && c < cols_here && col < N) ? D[row * ldd + col] : 0.0f;
                     }
             }
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < 2; i++)
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
+                for (int k = 0; k < KW; k++) {
                     const int r = e * 16 + i0 + i, c = lane + 32 * k;
                     const long long row = m0 + r, col = col0 + c;
                     if (row < M && c < cols_here && col < N) {
-                        const float t = tile[r * EPI_LD + c];
+                        const float t = tile[r * LD + c];
                         D[row * ldd + col] = EPI == EPI_ADD ? g[i][k] + t : t;
                     }
                 }
@@ -202,11 +224,27 @@ __device__ __forceinline__ void epi_flush(float* tile, int q, int hh, const floa
     epi_bar();
 }
 
-constexpr int GT_THREADS = 64 + EPI_THREADS;   // TMA warp, MMA warp, 8 epilogue warps
+constexpr int GT_THREADS = 64 + 32 * EPI_WARPS;   // TMA warp, MMA warp, 8 epilogue warps
+
+// Geometry of one instantiation.  bf16: 128-byte swizzle, 64 K per stage, up to 256 columns, one TMEM
+// accumulator.  fp32 kinds: 64-byte swizzle, 32 K per stage (so three stages of three pieces fit with
+// 256-column tiles), two TMEM buffers of up to 256 columns each.
+template <int KIND, bool MN>
+struct GtGeom {
+    static constexpr bool FL = KIND != KIND_BF16;
+    static constexpr int ESZ = KindTraits<KIND>::ESZ;
+    static constexpr int ROWB = FL ? 64 : 128;                 // bytes of one swizzled row
+    static constexpr uint32_t MODE = FL ? 4u : 2u;             // descriptor layout type
+    static constexpr int MNB = ROWB / 2;                       // MN-major: elements per box row
+    static constexpr int KS = MN ? ROWB / 2 : ROWB / ESZ;      // K per stage
+    static constexpr int KSTEPS = MN ? KS / 16 : ROWB / 32;    // MMAs (K steps) per stage and product
+    static constexpr int BOXB = ROWB * KS;                     // MN-major: bytes of one box (MNB x KS)
+    static constexpr uint32_t SBO = 8 * ROWB;
+};
 
 // Stage layout: A pieces 0..NP-1 (a_bytes each), then B pieces (b_bytes each).
-// K-major: one TMA box per piece and operand ([128 or ncols rows] x 128 B).
-// MN-major: boxes of 64 elements (128 B) x 64 K rows, 8 KB each, side by side.
+// K-major: one TMA box per piece and operand ([128 or ncols rows] x ROWB).
+// MN-major: boxes of MNB elements x KS K rows, side by side.
 template <int KIND, int EPI, bool MN>
 __global__ void __launch_bounds__(GT_THREADS, KIND == KIND_BF16 ? 2 : 1)
 gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUtensorMap mA0,
@@ -214,14 +252,18 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1,
                const __grid_constant__ CUtensorMap mB2) {
     using TR = KindTraits<KIND>;
+    using GG = GtGeom<KIND, MN>;
     constexpr int NP = TR::NP;
-    constexpr int KS = MN ? 64 : 128 / TR::ESZ;   // K elements per stage
+    constexpr int KS = GG::KS, KSTEPS = GG::KSTEPS, MNB = GG::MNB, BOXB = GG::BOXB;
+    constexpr bool FL = GG::FL;   // accumulator flush every kflush K steps
     extern __shared__ __align__(1024) unsigned char g_smem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)g_smem_raw + 1023) & ~(uintptr_t)1023);
     const int S = d.stages;
     uint64_t* full = (uint64_t*)(smem + (size_t)S * d.stage_bytes);
     uint64_t* empty = full + S;
     uint64_t* done = empty + S;
+    uint64_t* tfull = done + 1;     // FL: TMEM buffer b holds a finished unit
+    uint64_t* tempty = done + 3;    // FL: the epilogue has read TMEM buffer b
     uint32_t* tmem_slot = (uint32_t*)(done + 5);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long n0 = (long long)blockIdx.x * d.ncols_max;
@@ -230,10 +272,9 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
     const long long k0 = (long long)blockIdx.z * d.kchunk;
     const long long k1 = min(d.K, k0 + d.kchunk);
     const int nkb = k1 > k0 ? (int)((k1 - k0 + KS - 1) / KS) : 0;
-    constexpr bool FL = KIND != KIND_BF16;   // stage-wise accumulator flush (ncols <= 128)
-    const int tcols = FL ? 256 : ncols <= 32 ? 32 : ncols <= 64 ? 64 : ncols <= 128 ? 128 : 256;
-    uint64_t* tfull = done + 1;     // FL: TMEM buffer b holds a finished stage
-    uint64_t* tempty = done + 3;    // FL: the epilogue has read TMEM buffer b
+    const int TB = d.tbuf;          // FL: columns between the two TMEM buffers (128 or 192)
+    // (TMEM allocations are powers of two: two 192-column buffers take 512 columns)
+    const int tcols = FL ? (TB <= 128 ? 256 : 512) : ncols <= 32 ? 32 : ncols <= 64 ? 64 : ncols <= 128 ? 128 : 256;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
@@ -243,7 +284,7 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
         mbar_init(smem_u32(done), 1);
         for (int b = 0; b < 2; b++) {
             mbar_init(smem_u32(&tfull[b]), 1);
-            mbar_init(smem_u32(&tempty[b]), EPI_THREADS / 32);
+            mbar_init(smem_u32(&tempty[b]), EPI_WARPS);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -256,14 +297,15 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    const int total = nkb * KSTEPS;                    // MMA K steps of this CTA
+    const int kf = FL ? d.kflush : 1;
+    const int nunits = FL ? (total + kf - 1) / kf : 0;
 
     if (warp == 0) {
         if (lane == 0) {
             // rows past M or N and K past the end arrive zero-filled and count in the transaction bytes
-            const CUtensorMap* ma[3] = {&mA0, &mA1, &mA2};
-            const CUtensorMap* mb[3] = {&mB0, &mB1, &mB2};
-            const int nbb = MN ? (ncols + 63) / 64 : 1;   // MN-major B boxes of this CTA
-            const unsigned bytes = (unsigned)(NP * (d.a_bytes + (MN ? nbb * 8192 : d.b_bytes)));
+            const int nbb = MN ? (ncols + MNB - 1) / MNB : 1;   // MN-major B boxes of this CTA
+            const unsigned bytes = (unsigned)(NP * (d.a_bytes + (MN ? nbb * BOXB : d.b_bytes)));
             int issued = 0;
             for (int kb = 0; kb < nkb; kb++) {
                 const int s = kb % S;
@@ -277,16 +319,19 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                 mbar_expect_tx(fb, bytes);
 #pragma unroll
                 for (int p = 0; p < NP; p++) {
+                    const CUtensorMap* mpa = p == 0 ? &mA0 : p == 1 ? &mA1 : &mA2;
+                    const CUtensorMap* mpb = p == 0 ? &mB0 : p == 1 ? &mB1 : &mB2;
                     unsigned char* sa = st + p * d.a_bytes;
                     unsigned char* sb = st + NP * d.a_bytes + p * d.b_bytes;
                     if (MN) {
-                        g_tma_2d(smem_u32(sa), ma[p], fb, (int)m0, kc);
-                        g_tma_2d(smem_u32(sa + 8192), ma[p], fb, (int)m0 + 64, kc);
+#pragma unroll
+                        for (int i = 0; i < 128 / MNB; i++)
+                            g_tma_2d(smem_u32(sa + i * BOXB), mpa, fb, (int)m0 + i * MNB, kc);
                         for (int bx = 0; bx < nbb; bx++)
-                            g_tma_2d(smem_u32(sb + bx * 8192), mb[p], fb, (int)(n0 + 64 * bx), kc);
+                            g_tma_2d(smem_u32(sb + bx * BOXB), mpb, fb, (int)(n0 + MNB * bx), kc);
                     } else {
-                        g_tma_2d(smem_u32(sa), ma[p], fb, kc, (int)m0);
-                        g_tma_2d(smem_u32(sb), mb[p], fb, kc, (int)n0);
+                        g_tma_2d(smem_u32(sa), mpa, fb, kc, (int)m0);
+                        g_tma_2d(smem_u32(sb), mpb, fb, kc, (int)n0);
                     }
                 }
                 issued = kb + 1;
@@ -298,9 +343,9 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
         if (lane == 0) {
             const int fmt = KIND == KIND_TF32X3 ? 2 : 1;
             const uint32_t id = g_idesc(fmt, ncols, MN);
-            const uint32_t lbo = MN ? d.mn_lbo : 16u, sbo = MN ? d.mn_sbo : 1024u;
-            const int kf = d.kflush;
-            for (int kb = 0; kb < nkb; kb++) {
+            const uint32_t lbo = MN ? (uint32_t)BOXB : 16u, sbo = GG::SBO;
+            bool stop = false;
+            for (int kb = 0; kb < nkb && !stop; kb++) {
                 const int s = kb % S;
                 if (!mbar_wait(smem_u32(&full[s]), (uint32_t)((kb / S) & 1))) {
                     set_status(d.status, KMB_ERR_TIMEOUT_FULL);
@@ -308,11 +353,10 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t st = smem_u32(smem + (size_t)s * d.stage_bytes);
-                bool stop = false;
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++) {   // K-major: 32 bytes of K per MMA; MN-major: 16 K rows
-                    const uint32_t o = MN ? ks * 2048 : ks * 32;
-                    const int g = kb * 4 + ks, unit = g / kf;
+                for (int ks = 0; ks < KSTEPS; ks++) {   // K-major: 32 bytes of K per MMA; MN-major: 16 K rows
+                    const uint32_t o = MN ? ks * 16 * GG::ROWB : ks * 32;
+                    const int g = kb * KSTEPS + ks, unit = g / kf;
                     const bool first = !FL ? (kb == 0 && ks == 0) : (g % kf == 0);
                     if (FL && first && unit >= 2 &&
                         !mbar_wait(smem_u32(&tempty[unit & 1]), (uint32_t)(((unit >> 1) - 1) & 1))) {
@@ -321,31 +365,34 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                         break;
                     }
                     if (FL && first) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t dt = FL ? tmem + (uint32_t)((unit & 1) * 128) : tmem;
+                    const uint32_t dt = FL ? tmem + (uint32_t)((unit & 1) * TB) : tmem;
 #pragma unroll
                     for (int i = 0; i < TR::NPROD; i++) {
                         int pa, pb;
                         prod_pair(KIND, i, pa, pb);
                         const uint32_t a = st + pa * d.a_bytes + o;
                         const uint32_t b = st + NP * d.a_bytes + pb * d.b_bytes + o;
-                        g_mma<KIND>(dt, g_desc(a, lbo, sbo), g_desc(b, lbo, sbo), id, !first || i > 0);
+                        g_mma<KIND>(dt, g_desc(a, lbo, sbo, GG::MODE), g_desc(b, lbo, sbo, GG::MODE), id,
+                                    !first || i > 0);
                     }
-                    if (FL && g % kf == kf - 1) g_commit(smem_u32(&tfull[unit & 1]));
+                    if (FL && (g % kf == kf - 1 || g == total - 1)) g_commit(smem_u32(&tfull[unit & 1]));
                 }
                 g_commit(smem_u32(&empty[s]));
-                if (stop) break;
             }
             g_commit(smem_u32(done));
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile, columns of half hh
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile; column group hh
         const int q = warp & 3, hh = (warp - 2) >> 2;
+        float* dout = d.D + (long long)blockIdx.z * d.split_stride;
         if constexpr (FL) {
-            float acc[64];
+            // group hh (0, 1) holds columns hh * CG .. hh * CG + CG - 1 (CG = TB / 2 <= 96) as an fp32
+            // running sum
+            const int CG = TB >> 1;
+            float acc[96];
 #pragma unroll
-            for (int c = 0; c < 64; c++) acc[c] = 0.0f;
+            for (int c = 0; c < 96; c++) acc[c] = 0.0f;
             bool ok = true;
-            const int nunits = nkb * 4 / d.kflush;
             for (int u = 0; u < nunits; u++) {
                 if (!mbar_wait(smem_u32(&tfull[u & 1]), (uint32_t)((u >> 1) & 1))) {
                     set_status(d.status, KMB_ERR_TIMEOUT_Y);
@@ -353,20 +400,24 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                if (hh * 64 < ncols) {
-                    float v[64];
-                    g_ld64(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((u & 1) * 128 + hh * 64), v);
+                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((u & 1) * TB + hh * CG);
 #pragma unroll
-                    for (int j = 0; j < 64; j++) acc[j] += v[j];
+                for (int c = 0; c < 96; c += 16) {
+                    if (c < CG && hh * CG + c < ncols) {
+                        float v[16];
+                        g_ld16(tb + (uint32_t)c, v);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) acc[c + j] += v[j];
+                    }
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&tempty[u & 1]));
             }
-            // the last unit's commit covers every MMA; the stages are free for the store tile
+            // the last commit covers every MMA; the stages are free for the store tile
             if (!mbar_wait(smem_u32(done), 0)) { set_status(d.status, KMB_ERR_TIMEOUT_Y); ok = false; }
-            epi_flush<EPI>((float*)smem, q, hh, acc, ncols, d.D + (long long)blockIdx.z * d.split_stride, d.ldd, m0,
-                           d.M, n0, d.N, lane, ok);
+            epi_flush<EPI, 96, 192>((float*)smem, q, hh, acc, CG, hh * CG, ncols, dout, d.ldd, m0, d.M, n0, d.N,
+                                    lane, ok);
         } else {
             const bool got = mbar_wait(smem_u32(done), 0);
             if (!got) set_status(d.status, KMB_ERR_TIMEOUT_Y);
@@ -378,9 +429,8 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                 else
 #pragma unroll
                     for (int i = 0; i < 64; i++) v[i] = 0.0f;   // nkb == 0: an empty split stores zeros
-                const int cols_here = min(128, ncols - h);
-                epi_flush<EPI>((float*)smem, q, hh, v, cols_here, d.D + (long long)blockIdx.z * d.split_stride, d.ldd,
-                               m0, d.M, n0 + h, d.N, lane, got);
+                epi_flush<EPI, 64, 128>((float*)smem, q, hh, v, 64, hh * 64, min(128, ncols - h), dout, d.ldd, m0,
+                                        d.M, n0 + h, d.N, lane, got);
             }
         }
     }
@@ -513,47 +563,51 @@ cudaError_t gemm_tc(int kind, int epi, long long M, long long N, long long K, co
         return cudaErrorNotSupported;
     for (int p = 0; p < NP; p++)
         if (!A.p[p] || !B.p[p] || ((uintptr_t)A.p[p] & 15) || ((uintptr_t)B.p[p] & 15)) return cudaErrorNotSupported;
-    const int KS = mn ? 64 : 128 / esz;
+    // geometry (GtGeom): bf16 128-byte rows, the fp32 kinds 64-byte rows
+    const bool fl = kind != KIND_BF16;
+    const int rowb = fl ? 64 : 128;
+    const int KS = mn ? rowb / 2 : rowb / esz;
+    const int mnb = rowb / 2, boxb = rowb * KS;
     GemmTCDesc d{};
     d.M = M; d.N = N; d.K = K;
-    // columns per CTA: the (padded) width up to 256, fewer while two stages do not fit the budget
-    // (bf16: two CTAs and two 256-column accumulators per SM, so one tile's epilogue overlaps another's
-    // MMAs; the multi-piece kinds one CTA per SM)
-    const long long npad = mn ? (N + 63) & ~63LL : (N + 15) & ~15LL;
-    const int budget = (kind == KIND_BF16 ? 110 : 200) * 1024;
-    d.a_bytes = 128 * 128;
-    // (the fp32 kinds keep two 128-column TMEM buffers: at most 128 columns)
-    const int ncap = kind == KIND_BF16 ? 256 : 128;
+    // columns per CTA: the (padded) width up to 256, fewer while the stages do not fit the budget (bf16:
+    // two stages and two CTAs per SM, so one tile's epilogue overlaps another's MMAs; the fp32 kinds three
+    // stages and one CTA per SM, two TMEM buffers of up to 256 columns)
+    const long long npad = mn ? (N + mnb - 1) / mnb * mnb : (N + 15) & ~15LL;
+    const int budget = (fl ? 216 : 110) * 1024;
+    const int min_stages = fl ? 3 : 2;
+    d.a_bytes = 128 * rowb;
+    const int ncap = fl ? 192 : 256;   // fp32 kinds: two TMEM buffers of <= 192 columns, 96 per epilogue thread
     int nc = (int)(npad <= ncap ? npad : ncap);
     for (;;) {
-        d.b_bytes = mn ? ((nc + 63) / 64) * 8192 : nc * 128;
+        d.b_bytes = mn ? ((nc + mnb - 1) / mnb) * boxb : nc * rowb;
         d.stage_bytes = NP * (d.a_bytes + d.b_bytes);
-        if (2 * d.stage_bytes <= budget || nc <= 64) break;
-        nc = mn ? nc - 64 : ((nc / 2 + 15) & ~15);
+        if (min_stages * d.stage_bytes <= budget || nc <= 64) break;
+        nc = mn ? nc - mnb : ((nc / 2 + 15) & ~15);
     }
     d.ncols_max = nc;
+    d.tbuf = nc <= 128 ? 128 : 192;
     d.stages = budget / d.stage_bytes;
     if (d.stages > 6) d.stages = 6;
-    if (d.stages < 2 || d.stages * d.stage_bytes < 128 * EPI_LD * 4) return cudaErrorNotSupported;
+    if (d.stages < 2 || d.stages * d.stage_bytes < 128 * ((fl ? 192 : 128) + 1) * 4) return cudaErrorNotSupported;
     const long long kb_total = (K + KS - 1) / KS;
     d.kchunk = ((kb_total + nsplit - 1) / nsplit) * KS;
-    d.mn_lbo = 8192u;   // the two 64-element halves of a 128-row tile / the B boxes: one 8 KB box apart
-    d.mn_sbo = 1024u;   // 8 K rows of 128 B
     d.kflush = g_kflush;
     d.D = D; d.ldd = ldd; d.split_stride = split_stride; d.status = status;
     const int dt = kind == KIND_TF32X3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     CUtensorMap ma[3], mb[3];
+    const int swz = fl ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
     auto enc = [&](CUtensorMap* m, const void* p, long long rows, long long ld, unsigned boxrows) {
         if (mn) {   // [K, rows] row-major: inner dimension = rows
             const unsigned long long dims[2] = {(unsigned long long)rows, (unsigned long long)K};
             const unsigned long long str[1] = {(unsigned long long)(ld * esz)};
-            const unsigned box[2] = {64u, (unsigned)KS};
-            return tmap_encode_ex(m, p, dt, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+            const unsigned box[2] = {(unsigned)mnb, (unsigned)KS};
+            return tmap_encode_ex(m, p, dt, 2, dims, str, box, swz);
         }
         const unsigned long long dims[2] = {(unsigned long long)K, (unsigned long long)rows};
         const unsigned long long str[1] = {(unsigned long long)(ld * esz)};
         const unsigned box[2] = {(unsigned)KS, boxrows};
-        return tmap_encode_ex(m, p, dt, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        return tmap_encode_ex(m, p, dt, 2, dims, str, box, swz);
     };
     for (int p = 0; p < 3; p++) {
         if (p < NP) {
@@ -573,8 +627,8 @@ cudaError_t gemm_tc(int kind, int epi, long long M, long long N, long long K, co
         e = cudaFuncSetAttribute(gemm_tc_kernel<KI, EP, MNV>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
                                  smem);                                                                     \
         if (e != cudaSuccess) return e;                                                                     \
-        gemm_tc_kernel<KI, EP, MNV><<<grid, GT_THREADS, smem, st>>>(d, ma[0], ma[1], ma[2], mb[0], mb[1],   \
-                                                                    mb[2]);                                 \
+        gemm_tc_kernel<KI, EP, MNV><<<grid, GT_THREADS, smem, st>>>(d, ma[0], ma[1], ma[2], mb[0],            \
+                                                                              mb[1], mb[2]);                \
         e = cudaGetLastError();                                                                             \
     } while (0)
 #define KMB_GT_EPI(KI, MNV)                      \
