@@ -565,7 +565,7 @@ int kmb_gemm_set_f32_kind(int kind) {
 }
 int kmb_gemm_get_f32_kind(void) { return g_f32_kind; }
 int kmb_gemm_set_f32_flush(int ksteps) {
-    return gemm_set_kflush(ksteps) ? set_error("kmb_gemm_set_f32_flush: 1, 2 or 4") : 0;
+    return gemm_set_kflush(ksteps) ? set_error("kmb_gemm_set_f32_flush: 1 .. 64") : 0;
 }
 int kmb_gemm_last_path(void) { return tl_gemm_path; }
 

@@ -30,10 +30,12 @@
 // The fp32 kinds do not let one TMEM accumulator run over all of K: the
 // tensor core's accumulation drifts with the number of products it adds (its
 // error grows about as sqrt(K) relative to sum |a b|, where an fp32 FMA loop's
-// stays flat).  The MMA warp accumulates `kflush` MMA K steps (16 bf16 or 8
-// tf32 K each) into one of two TMEM buffers, and the epilogue warps add every
-// finished buffer into an fp32 running sum in registers while the next one
-// accumulates.
+// stays flat).  The leading product (a0 b0, or hi hi) accumulates in one TMEM
+// buffer for `kflush` MMA K steps (16 bf16 or 8 tf32 K each) at a time, after
+// which the epilogue warps add it into an fp32 running sum in registers; the
+// smaller products, 2^-8 (2^-11) of its size and smaller, accumulate over all
+// of K in a second buffer whose drift stays below fp32 rounding, added once at
+// the end.
 // Split-K: grid.z cuts K into chunks; each split writes its own partial
 // (EPI_STORE at D + split * split_stride), summed later in a fixed order.
 // EPI_ADD adds the accumulator into D (one split).  Every wait is bounded; on a
@@ -358,24 +360,28 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                     const uint32_t o = MN ? ks * 16 * GG::ROWB : ks * 32;
                     const int g = kb * KSTEPS + ks, unit = g / kf;
                     const bool first = !FL ? (kb == 0 && ks == 0) : (g % kf == 0);
-                    if (FL && first && unit >= 2 &&
-                        !mbar_wait(smem_u32(&tempty[unit & 1]), (uint32_t)(((unit >> 1) - 1) & 1))) {
+                    // FL: the leading product accumulates in the buffer at column 0, flushed every kflush K
+                    // steps (wait until the epilogue has read the previous unit); the smaller products
+                    // accumulate over all of K in the buffer at column TB
+                    if (FL && first && unit >= 1 &&
+                        !mbar_wait(smem_u32(&tempty[0]), (uint32_t)((unit - 1) & 1))) {
                         set_status(d.status, KMB_ERR_TIMEOUT_EMPTY);
                         stop = true;
                         break;
                     }
                     if (FL && first) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t dt = FL ? tmem + (uint32_t)((unit & 1) * TB) : tmem;
 #pragma unroll
                     for (int i = 0; i < TR::NPROD; i++) {
                         int pa, pb;
                         prod_pair(KIND, i, pa, pb);
                         const uint32_t a = st + pa * d.a_bytes + o;
                         const uint32_t b = st + NP * d.a_bytes + pb * d.b_bytes + o;
-                        g_mma<KIND>(dt, g_desc(a, lbo, sbo, GG::MODE), g_desc(b, lbo, sbo, GG::MODE), id,
-                                    !first || i > 0);
+                        const bool lead = i == TR::NPROD - 1;
+                        const uint32_t dt = (FL && !lead) ? tmem + (uint32_t)TB : tmem;
+                        const bool acc = !FL ? (!first || i > 0) : lead ? !first : (g > 0 || i > 0);
+                        g_mma<KIND>(dt, g_desc(a, lbo, sbo, GG::MODE), g_desc(b, lbo, sbo, GG::MODE), id, acc);
                     }
-                    if (FL && (g % kf == kf - 1 || g == total - 1)) g_commit(smem_u32(&tfull[unit & 1]));
+                    if (FL && (g % kf == kf - 1 || g == total - 1)) g_commit(smem_u32(&tfull[0]));
                 }
                 g_commit(smem_u32(&empty[s]));
             }
@@ -387,20 +393,14 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
         float* dout = d.D + (long long)blockIdx.z * d.split_stride;
         if constexpr (FL) {
             // group hh (0, 1) holds columns hh * CG .. hh * CG + CG - 1 (CG = TB / 2 <= 96) as an fp32
-            // running sum
+            // running sum of the leading product's units, then adds the smaller products' accumulator
             const int CG = TB >> 1;
             float acc[96];
 #pragma unroll
             for (int c = 0; c < 96; c++) acc[c] = 0.0f;
             bool ok = true;
-            for (int u = 0; u < nunits; u++) {
-                if (!mbar_wait(smem_u32(&tfull[u & 1]), (uint32_t)((u >> 1) & 1))) {
-                    set_status(d.status, KMB_ERR_TIMEOUT_Y);
-                    ok = false;
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((u & 1) * TB + hh * CG);
+            auto add_tmem = [&](uint32_t col0) {
+                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + col0 + (uint32_t)(hh * CG);
 #pragma unroll
                 for (int c = 0; c < 96; c += 16) {
                     if (c < CG && hh * CG + c < ncols) {
@@ -410,12 +410,23 @@ gemm_tc_kernel(const __grid_constant__ GemmTCDesc d, const __grid_constant__ CUt
                         for (int j = 0; j < 16; j++) acc[c + j] += v[j];
                     }
                 }
+            };
+            for (int u = 0; u < nunits; u++) {
+                if (!mbar_wait(smem_u32(&tfull[0]), (uint32_t)(u & 1))) {
+                    set_status(d.status, KMB_ERR_TIMEOUT_Y);
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                add_tmem(0);
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&tempty[u & 1]));
+                if (lane == 0) mbar_arrive(smem_u32(&tempty[0]));
             }
             // the last commit covers every MMA; the stages are free for the store tile
             if (!mbar_wait(smem_u32(done), 0)) { set_status(d.status, KMB_ERR_TIMEOUT_Y); ok = false; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (ok && nkb > 0) add_tmem((uint32_t)TB);   // the smaller products, accumulated over all of K
             epi_flush<EPI, 96, 192>((float*)smem, q, hh, acc, CG, hh * CG, ncols, dout, d.ldd, m0, d.M, n0, d.N,
                                     lane, ok);
         } else {
@@ -540,7 +551,7 @@ __global__ void gt_reduce_splits(const float* __restrict__ part, float* __restri
     *o = accumulate ? *o + acc : acc;
 }
 
-int g_kflush = 2;
+int g_kflush = 8;
 
 int kind_pieces(int kind) { return kind == KIND_BF16 ? 1 : kind == KIND_TF32X3 ? 2 : 3; }
 
@@ -696,9 +707,10 @@ cudaError_t gemm_reduce_splits(const float* part, float* out, long long rows, lo
     return cudaGetLastError();
 }
 
-// MMA K steps per TMEM buffer of the fp32 kinds (1, 2 or 4); fewer = closer to fp32 FMA accuracy
+// MMA K steps of the leading product per TMEM flush of the fp32 kinds (1 .. 64); fewer = closer to
+// fp32 FMA accuracy
 int gemm_set_kflush(int k) {
-    if (k != 1 && k != 2 && k != 4) return -1;
+    if (k < 1 || k > 64) return -1;
     g_kflush = k;
     return 0;
 }

@@ -30,9 +30,11 @@ int kmb_gemm_bf16(int trans, long long M, long long N, long long K, const void *
 /* The kind every fp32 product of the block and the model uses. */
 int kmb_gemm_set_f32_kind(int kind);
 int kmb_gemm_get_f32_kind(void);
-/* Tensor-core MMA K steps (16 bf16 / 8 tf32 K each) the fp32 kinds accumulate in
- * one TMEM buffer before the epilogue adds it into an fp32 running sum: 1, 2 or
- * 4.  Fewer = closer to an fp32 FMA loop's accuracy, more = fewer TMEM reads. */
+/* Tensor-core MMA K steps (16 bf16 / 8 tf32 K each) over which the fp32 kinds let
+ * the leading product accumulate in TMEM before the epilogue adds it into an
+ * fp32 running sum: 1 .. 64, default 8.  Fewer = closer to an fp32 FMA loop's
+ * accuracy, more = fewer TMEM reads.  The smaller products accumulate over all
+ * of K and are added once. */
 int kmb_gemm_set_f32_flush(int ksteps);
 /* Path of this thread's last product: 1 tensor cores, 0 CUDA cores, -1 none yet. */
 int kmb_gemm_last_path(void);

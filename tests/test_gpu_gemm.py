@@ -15,6 +15,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 SIMT, TF32X3, BF16X6, BF16X9 = 4, 1, 2, 3
+DEFAULT_FLUSH = 8
 
 # (M, N, K): block projection / dx / dWcat shapes at reduced batch, head shapes, ragged ones
 SHAPES = [(1024, 260, 512), (2048, 512, 260), (260, 512, 4096), (512, 256, 64), (300, 100, 77),
@@ -51,7 +52,7 @@ def test_f32_kinds_reach_fp32_accuracy(kmb, cuda, M, N, K, trans):
     scale = np.abs(am) @ np.abs(bm)
     A, B = a.to(cuda), b.to(cuda)
     errs = {}
-    for flush in (1, 2, 4):
+    for flush in (1, 2, 8, 16):
         kmb.check(kmb.lib().kmb_gemm_set_f32_flush(flush), "flush")
         for kind in (SIMT, TF32X3, BF16X6, BF16X9):
             D = _run_f32(kmb, kind, trans, A, B, M, N, K)
@@ -62,10 +63,13 @@ def test_f32_kinds_reach_fp32_accuracy(kmb, cuda, M, N, K, trans):
               " ".join(f"{n}={errs[k, flush] * 2**24:.2f},{errs[k, flush, 'bias'] * 2**24:+.3f}"
                        f"(p{errs[k, flush, 'path']})" for n, k in
                        (("simt", SIMT), ("tf32x3", TF32X3), ("bf16x6", BF16X6), ("bf16x9", BF16X9))))
-    kmb.check(kmb.lib().kmb_gemm_set_f32_flush(1), "flush")
+    kmb.check(kmb.lib().kmb_gemm_set_f32_flush(DEFAULT_FLUSH), "flush")
     base = max(errs[SIMT, 1], 2.0 ** -24)
-    for kind in (TF32X3, BF16X6, BF16X9):
-        assert errs[kind, 1] <= 2 * base, (kind, errs[kind, 1], base)
+    for kind in (BF16X6, BF16X9):
+        # the default flush interval is within 2x of the fp32 FMA loop's error (below it on most shapes)
+        assert errs[kind, DEFAULT_FLUSH] <= 2 * base, (kind, errs[kind, DEFAULT_FLUSH], base)
+    # 3xTF32 keeps the tf32 rounding of its low pieces (about 2^-22 relative per product): 4 units more
+    assert errs[TF32X3, DEFAULT_FLUSH] <= 2 * base + 4 * 2.0 ** -24, (errs[TF32X3, DEFAULT_FLUSH], base)
 
 
 @pytest.mark.parametrize("trans", [0, 1])
