@@ -142,7 +142,7 @@ __global__ void add_partials(const float* __restrict__ part, long long n, int nc
 // warps add their column partials into shared memory in warp order.  Every
 // sum has a fixed order.
 template <typename T, int NC, int RM>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, (NC * (16 / (int)sizeof(T)) * RM <= 16 || (sizeof(T) == 2 && NC <= 2 && NC * RM <= 4)) ? 2 : 1)
 rank_pass(const T* __restrict__ X, const float* __restrict__ W, const float* __restrict__ Y, long long rows, int dim,
           int R, int r0, int rc, float* __restrict__ dy, float* __restrict__ part) {
     constexpr int V = 16 / sizeof(T);
@@ -162,29 +162,38 @@ rank_pass(const T* __restrict__ X, const float* __restrict__ W, const float* __r
             }
     const long long stride = (long long)gridDim.x * 8;
     long long row = (long long)blockIdx.x * 8 + warp;
-    uint4 nxt[NC];
-    auto load = [&](long long rw) {
+    // two rows in flight ahead of the one in use: X chunks and the row's Y values
+    uint4 b0[NC], b1[NC];
+    float y0[RM], y1[RM];
+    auto load = [&](uint4 (&dst)[NC], float (&yd)[RM], long long rw) {
 #pragma unroll
         for (int c = 0; c < NC; c++) {
             const int j0 = (c * 32 + lane) * V;
-            nxt[c] = (rw < rows && j0 < dim) ? __ldcs(reinterpret_cast<const uint4*>(X + rw * dim + j0))
+            dst[c] = (rw < rows && j0 < dim) ? __ldcs(reinterpret_cast<const uint4*>(X + rw * dim + j0))
                                              : make_uint4(0u, 0u, 0u, 0u);
         }
-    };
-    load(row);
-    for (; row < rows; row += stride) {
-        float xv[NC][V];
-#pragma unroll
-        for (int c = 0; c < NC; c++) {
-            const T* e = reinterpret_cast<const T*>(&nxt[c]);
-#pragma unroll
-            for (int v = 0; v < V; v++) xv[c][v] = ldf(e + v);
-        }
-        float yr[RM];
 #pragma unroll
         for (int r = 0; r < RM; r++)
-            yr[r] = Y ? (r < rc ? Y[row * R + r0 + r] : 0.0f) : (r == 0 ? 1.0f : 0.0f);
-        load(row + stride);   // the next row's chunks are in flight while this one is used
+            yd[r] = Y ? ((r < rc && rw < rows) ? Y[rw * R + r0 + r] : 0.0f) : (r == 0 ? 1.0f : 0.0f);
+    };
+    load(b0, y0, row);
+    load(b1, y1, row + stride);
+    for (; row < rows; row += stride) {
+        float xv[NC][V];
+        float yr[RM];
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            const T* e = reinterpret_cast<const T*>(&b0[c]);
+#pragma unroll
+            for (int v = 0; v < V; v++) xv[c][v] = ldf(e + v);
+            b0[c] = b1[c];
+        }
+#pragma unroll
+        for (int r = 0; r < RM; r++) {
+            yr[r] = y0[r];
+            y0[r] = y1[r];
+        }
+        load(b1, y1, row + 2 * stride);
         if (part) {
 #pragma unroll
             for (int c = 0; c < NC; c++)
@@ -245,8 +254,18 @@ __global__ void add_rank_partials(const float* __restrict__ part, int nblk, int 
     const int i = blockIdx.x * 32 + lane;
     const int n = dim * rr;
     float acc = 0.0f;
-    if (i < n)
-        for (int b = warp; b < nblk; b += 8) acc += part[(long long)b * n + i];
+    if (i < n) {
+        // blocks warp, warp + 8, ... added in that order; eight loads issued before their adds
+        int b = warp;
+        for (; b + 56 < nblk; b += 64) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[k] = part[(long long)(b + 8 * k) * n + i];
+#pragma unroll
+            for (int k = 0; k < 8; k++) acc += v[k];
+        }
+        for (; b < nblk; b += 8) acc += part[(long long)b * n + i];
+    }
     ws[warp][lane] = acc;
     __syncthreads();
     if (warp == 0 && i < n) {
