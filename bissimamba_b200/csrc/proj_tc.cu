@@ -84,6 +84,29 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 64 consecutive TMEM columns of this warp's 32 lanes, waited for inside the same asm
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, "
+        "%36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, "
+        "%57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+
 constexpr int PTC_THREADS = 192;
 constexpr int PTC_WROWS = 16;   // rows of Wcat per TMA box
 
@@ -181,23 +204,19 @@ proj_fwd_tc(const __grid_constant__ ProjTCDesc d, const __grid_constant__ CUtens
         if (!got) set_status(d.status, KMB_ERR_TIMEOUT_Y);
         tc_fence_after();
         const int R = d.R, NR = d.NR, Rt = d.Rt;
-        for (int c = 0; c < ncols; c += 16) {
-            float v[16];
-            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-            if (!got || row >= d.BL) continue;
+        // one 16-column chunk of this row: v = the accumulator, dv = the dout chunk (EPI 1)
+        auto chunk = [&](int c, const float* v, const uint4* dv) {
             const int col = n0 + c;
             if constexpr (EPI == 1) {
-                // dx = bf16(dout + D): 16 columns, two 16-byte loads and stores (dx may alias dout)
+                // dx = bf16(dout + D): 16 columns, two 16-byte stores (dx may alias dout: read before)
                 const long long o = row * d.N + col;
-                uint4 pk[2];
-                pk[0] = ((const uint4*)(d.dout + o))[0];
-                pk[1] = ((const uint4*)(d.dout + o))[1];
+                uint4 pk[2] = {dv[0], dv[1]};
                 __nv_bfloat16* e = (__nv_bfloat16*)pk;
 #pragma unroll
                 for (int j = 0; j < 16; j++) e[j] = __float2bfloat16_rn(__bfloat162float(e[j]) + v[j]);
                 ((uint4*)(d.dx + o))[0] = pk[0];
                 ((uint4*)(d.dx + o))[1] = pk[1];
-                continue;
+                return;
             }
             if (col < 2 * NR) {
                 // 16 columns of B or C: bias, round, two 16-byte stores
@@ -229,6 +248,34 @@ proj_fwd_tc(const __grid_constant__ ProjTCDesc d, const __grid_constant__ CUtens
                     }
                 }
             }
+        };
+        const bool live = got && row < d.BL;
+        int c = 0;
+        // 64 columns at a time: the row's dout loads (EPI 1) and one TMEM load in flight together
+        for (; c + 64 <= ncols; c += 64) {
+            uint4 dv[8];
+            if (EPI == 1 && live) {
+                const uint4* src = (const uint4*)(d.dout + row * d.N + n0 + c);
+#pragma unroll
+                for (int i = 0; i < 8; i++) dv[i] = src[i];
+            }
+            float v[64];
+            tmem_ld64(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+            if (!live) continue;
+#pragma unroll
+            for (int i = 0; i < 4; i++) chunk(c + 16 * i, v + 16 * i, dv + 2 * i);
+        }
+        for (; c < ncols; c += 16) {
+            uint4 dv[2];
+            if (EPI == 1 && live) {
+                const uint4* src = (const uint4*)(d.dout + row * d.N + n0 + c);
+                dv[0] = src[0];
+                dv[1] = src[1];
+            }
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+            if (!live) continue;
+            chunk(c, v, dv);
         }
     }
     tc_fence_before();
