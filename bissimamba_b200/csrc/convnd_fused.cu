@@ -280,6 +280,223 @@ __global__ void __launch_bounds__(CF_THREADS, 2) conv_fused_kernel(ConvDesc c, F
     }
 }
 
+// ---------------------------------------------------------------------------
+// 3D variant (K = 2 or 3, D a multiple of 4).  A CTA owns (item, slab of T0
+// planes of axis 0, 4 channels).  The padded slabs are laid out as
+// [plane][row][PX] points of 16 bytes with PX = d2 + K - 1 rounded up to an odd
+// number.  A warp takes 8 consecutive rows (axis 1) at one run of R points
+// along axis 2, 4 threads per point (one channel each): the 8 rows of a warp
+// sit PX points apart, and with PX odd their 16-byte points fall in 8
+// different bank groups, so every shared-memory read is conflict-free and its
+// address is the thread's run base plus a per-row constant.  The slabs are
+// staged with cp.async (16 bytes per point, zero-filled outside the grid).
+// Arithmetic per point and its order are those of the generic fused kernel.
+// ---------------------------------------------------------------------------
+struct Fused3Geom {
+    int T0, nslab;   // planes of axis 0 per slab, slabs per item
+    int PX, PY;      // padded row pitch (odd) and rows per plane, in points
+    int plane;       // PX * PY
+};
+
+__device__ __forceinline__ void cf_cp16(void* sdst, const void* gsrc, bool ok) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(sdst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gsrc), "r"(ok ? 16 : 0)
+                 : "memory");
+}
+
+template <int K, int R, int MODE>
+__global__ void __launch_bounds__(CF_THREADS, 2) conv_fused3d_kernel(ConvDesc c, Fused3Geom g,
+                                                                     const float4* __restrict__ in,
+                                                                     const float* __restrict__ ker,
+                                                                     const float* __restrict__ bias,
+                                                                     const float4* __restrict__ dy,
+                                                                     float* __restrict__ out,
+                                                                     float* __restrict__ din,
+                                                                     float* __restrict__ part) {
+    constexpr int H = K - 1, V = K * K * K, ROWS = K * K;
+    constexpr bool FWD = MODE & 1, BWD = (MODE & 2) != 0;
+    extern __shared__ __align__(16) float4 cf_smem[];
+    float4* sIN = cf_smem;
+    float4* sDY = cf_smem + (g.T0 + H) * g.plane;
+    const int D4 = c.D >> 2;
+    const int slab = blockIdx.x % g.nslab;
+    const long long b = blockIdx.x / g.nslab;
+    const int q = blockIdx.y;                                // float4 channel lane of this CTA
+    const int d0 = (int)c.dims[0], d1 = (int)c.dims[1], d2 = (int)c.dims[2];
+    const int z0 = slab * g.T0;
+    const int nz = min(g.T0, d0 - z0);
+    const long long ibase = b * c.P;
+    const int tid = threadIdx.x, wl = tid & 31, warp = tid >> 5;
+
+    // ---- stage: padded (pz, py, px) <- input (z0 + pz - H, py - H, px - H), dy (z0 + pz, py, px)
+    {
+        const int pdx = d2 + H, pdy = d1 + H;
+        const int n = (nz + H) * pdy * pdx;
+        const float4* inb = in + ibase * D4 + q;
+        const float4* dyb = dy ? dy + ibase * D4 + q : inb;
+        for (int i = tid; i < n; i += CF_THREADS) {
+            const int row = i / pdx, px = i - row * pdx;
+            const int pz = row / pdy, py = row - pz * pdy;
+            const int slot = pz * g.plane + py * g.PX + px;
+            if (FWD || BWD) {
+                const int zi = z0 + pz - H, yi = py - H, xi = px - H;
+                const bool ok = zi >= 0 && yi >= 0 && xi >= 0 && zi < d0;
+                cf_cp16(sIN + slot, ok ? inb + (((long long)zi * d1 + yi) * d2 + xi) * D4 : inb, ok);
+            }
+            if (BWD) {
+                const int zd = z0 + pz;
+                const bool ok = zd < d0 && py < d1 && px < d2;
+                cf_cp16(sDY + slot, ok ? dyb + (((long long)zd * d1 + py) * d2 + px) * D4 : dyb, ok);
+            }
+        }
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
+    }
+    __syncthreads();
+
+    const int l = tid & 3, iy = (tid >> 2) & 7;
+    const int ch = q * 4 + l;
+    float kv[V];
+#pragma unroll
+    for (int k = 0; k < V; k++) kv[k] = ker[(long long)k * c.D + ch];
+    const float b0 = (FWD && bias) ? bias[ch] : 0.0f;
+    float dk[BWD ? V + 1 : 1];
+#pragma unroll
+    for (int k = 0; k < (BWD ? V + 1 : 1); k++) dk[k] = 0.0f;
+    const float* sINf = (const float*)sIN + l;
+    const float* sDYf = (const float*)sDY + l;
+    const int PL = g.plane, PX = g.PX;
+    const int nrun = d2 / R, nyb = (d1 + 7) >> 3;
+    const int ntask = nz * nyb * nrun;
+    for (int t = warp; t < ntask; t += CF_THREADS / 32) {
+        const int xr = t % nrun, rest = t / nrun;
+        const int zr = rest / nyb, y = (rest - zr * nyb) * 8 + iy;
+        if (y >= d1) continue;
+        const int x0 = xr * R;
+        const int base = zr * PL + y * PX + x0;
+        const float* pin = sINf + base * 4;
+        const float* pdy = sDYf + base * 4;
+        float acc[R], adin[R], dyo[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            acc[r] = b0;
+            adin[r] = 0.0f;
+            if (BWD) dyo[r] = pdy[r * 4];
+        }
+#pragma unroll
+        for (int row = 0; row < ROWS; row++) {
+            const int k0 = row / K, k1 = row % K;
+            {
+                const float* pr = pin + (k0 * PL + k1 * PX) * 4;
+                float w[R + H];
+#pragma unroll
+                for (int j = 0; j < R + H; j++) w[j] = pr[j * 4];
+#pragma unroll
+                for (int kx = 0; kx < K; kx++) {
+                    const int k = row * K + kx;
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        if (FWD) acc[r] = __fmaf_rn(w[r + kx], kv[k], acc[r]);
+                        if (BWD) dk[k] = __fmaf_rn(dyo[r], w[r + kx], dk[k]);
+                    }
+                }
+            }
+            if (BWD) {
+                const float* pr = pdy + ((H - k0) * PL + (H - k1) * PX) * 4;
+                float w[R + H];
+#pragma unroll
+                for (int j = 0; j < R + H; j++) w[j] = pr[j * 4];
+#pragma unroll
+                for (int kx = 0; kx < K; kx++) {
+                    const int k = row * K + kx;
+#pragma unroll
+                    for (int r = 0; r < R; r++) adin[r] = __fmaf_rn(w[r + H - kx], kv[k], adin[r]);
+                }
+            }
+        }
+        const long long p = ((long long)(z0 + zr) * d1 + y) * d2 + x0;
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const long long gi = (ibase + p + r) * c.D + ch;
+            if (FWD) out[gi] = acc[r];
+            if (BWD) {
+                din[gi] = adin[r];
+                dk[V] += dyo[r];
+            }
+        }
+    }
+    if (!BWD) return;
+    // ---- dkernel / dbias partials of the CTA: the 8 threads of a warp that share a channel
+    // (xor shuffles 4, 8, 16), then the warps in order
+    constexpr int NV = V + 1;
+#pragma unroll
+    for (int k = 0; k < NV; k++)
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) dk[k] += __shfl_xor_sync(~0u, dk[k], o);
+    __syncthreads();
+    float* red = (float*)cf_smem;   // [warp][NV][4]
+    if (wl < 4) {
+#pragma unroll
+        for (int k = 0; k < NV; k++) red[(warp * NV + k) * 4 + wl] = dk[k];
+    }
+    __syncthreads();
+    const long long chunk = b * g.nslab + slab;
+    for (int i = tid; i < NV * 4; i += CF_THREADS) {
+        const int k = i >> 2, l2 = i & 3;
+        float s2 = red[k * 4 + l2];
+        for (int wv = 1; wv < CF_THREADS / 32; wv++) s2 += red[(wv * NV + k) * 4 + l2];
+        part[(chunk * NV + k) * c.D + q * 4 + l2] = s2;
+    }
+}
+
+static bool cf3_plan(const ConvDesc& c, int mode, Fused3Geom* g, int* smem, int* R) {
+    if (c.nd != 3 || c.K < 2 || c.K > 3 || c.D % 4 != 0) return false;
+    const int H = c.K - 1;
+    const long long d0 = c.dims[0], d1 = c.dims[1], d2 = c.dims[2];
+    if (d1 + H > 4096 || d2 + H > 4096) return false;
+    int PX = (int)d2 + H;
+    if (PX % 2 == 0) PX++;
+    const int PY = (int)d1 + H;
+    const long long plane_bytes = (long long)PX * PY * 16 * ((mode & 2) ? 2 : 1);
+    const long long t0max = CF_SMEM_MAX / plane_bytes - H;
+    if (t0max < 1) return false;
+    const long long nslab = (d0 + t0max - 1) / t0max;
+    g->nslab = (int)nslab;
+    g->T0 = (int)((d0 + nslab - 1) / nslab);
+    g->PX = PX;
+    g->PY = PY;
+    g->plane = PX * PY;
+    *R = (d2 % 4 == 0) ? 4 : 1;
+    int sm = (int)((g->T0 + H) * plane_bytes);
+    const int red = (CF_THREADS / 32) * (c.K * c.K * c.K + 1) * 4 * 4;
+    if ((mode & 2) && red > sm) sm = red;
+    *smem = sm;
+    return true;
+}
+
+template <int K, int R, int MODE>
+static cudaError_t cf3_launch_t(const ConvDesc& c, const Fused3Geom& g, int smem, const float* in, const float* ker,
+                                const float* bias, const float* dy, float* out, float* din, float* part,
+                                cudaStream_t st) {
+    auto k = conv_fused3d_kernel<K, R, MODE>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    dim3 grid((unsigned)(c.batch * g.nslab), (unsigned)(c.D / 4));
+    k<<<grid, CF_THREADS, smem, st>>>(c, g, (const float4*)in, ker, bias, (const float4*)dy, out, din, part);
+    return cudaGetLastError();
+}
+
+template <int K, int R>
+static cudaError_t cf3_mode(int mode, const ConvDesc& c, const Fused3Geom& g, int smem, const float* in,
+                            const float* ker, const float* bias, const float* dy, float* out, float* din,
+                            float* part, cudaStream_t st) {
+    switch (mode) {
+        case 1: return cf3_launch_t<K, R, 1>(c, g, smem, in, ker, bias, dy, out, din, part, st);
+        case 2: return cf3_launch_t<K, R, 2>(c, g, smem, in, ker, bias, dy, out, din, part, st);
+        default: return cf3_launch_t<K, R, 3>(c, g, smem, in, ker, bias, dy, out, din, part, st);
+    }
+}
+
 // dkernel[i] (i < V D) and dbias[i - V D] = sum over the chunks of part[chunk][i], fixed order (one launch)
 __global__ void cf_reduce_dk(const float* __restrict__ part, float* __restrict__ dker, float* __restrict__ dbias,
                              long long VD, int D, long long nch) {
@@ -338,8 +555,13 @@ static bool cf_plan(const ConvDesc& c, int mode, FusedGeom* g, int* smem, int* R
 }
 
 long long conv_fused_chunks(const ConvDesc& c, int mode) {
-    FusedGeom g;
     int sm, R;
+    if (c.nd == 3) {
+        Fused3Geom g3;
+        if (!cf3_plan(c, mode, &g3, &sm, &R)) return -1;
+        return c.batch * g3.nslab;
+    }
+    FusedGeom g;
     if (!cf_plan(c, mode, &g, &sm, &R)) return -1;
     return c.batch * g.nslab;
 }
@@ -379,8 +601,14 @@ cudaError_t launch_conv_fused(const ConvDesc& c, int mode, const float* in, cons
                               float* out, const float* dy, float* din, float* dker, float* dbias, float* part,
                               long long nch_max, cudaStream_t st) {
     FusedGeom g;
+    Fused3Geom g3;
     int smem, R;
-    if (!cf_plan(c, mode, &g, &smem, &R)) return cudaErrorNotSupported;
+    if (c.nd == 3) {
+        if (!cf3_plan(c, mode, &g3, &smem, &R)) return cudaErrorNotSupported;
+        g.nslab = g3.nslab;
+    } else if (!cf_plan(c, mode, &g, &smem, &R)) {
+        return cudaErrorNotSupported;
+    }
     const long long nch = c.batch * g.nslab;
     if ((mode & 2) && nch > nch_max) return cudaErrorNotSupported;
     if (c.batch * g.nslab > 0x7fffffffLL) return cudaErrorNotSupported;
@@ -394,8 +622,16 @@ cudaError_t launch_conv_fused(const ConvDesc& c, int mode, const float* in, cons
         e = R == 4 ? cf_mode<ND_, K_, 4>(mode, c, g, smem, in, ker, bias, dy, out, din, part, st)              \
                    : cf_mode<ND_, K_, 1>(mode, c, g, smem, in, ker, bias, dy, out, din, part, st);             \
     else
-    // (3D with K = 4 is left to the other kernels: 64 dkernel accumulators per thread do not fit)
-    KMB_CF(1, 2) KMB_CF(1, 3) KMB_CF(1, 4) KMB_CF(2, 2) KMB_CF(2, 3) KMB_CF(2, 4) KMB_CF(3, 2) KMB_CF(3, 3)
+    // 3D: the conflict-free variant (K = 4 is left to the other kernels: 64 dkernel accumulators
+    // per thread do not fit)
+    if (c.nd == 3 && c.K == 2)
+        e = R == 4 ? cf3_mode<2, 4>(mode, c, g3, smem, in, ker, bias, dy, out, din, part, st)
+                   : cf3_mode<2, 1>(mode, c, g3, smem, in, ker, bias, dy, out, din, part, st);
+    else if (c.nd == 3 && c.K == 3)
+        e = R == 4 ? cf3_mode<3, 4>(mode, c, g3, smem, in, ker, bias, dy, out, din, part, st)
+                   : cf3_mode<3, 1>(mode, c, g3, smem, in, ker, bias, dy, out, din, part, st);
+    else
+    KMB_CF(1, 2) KMB_CF(1, 3) KMB_CF(1, 4) KMB_CF(2, 2) KMB_CF(2, 3) KMB_CF(2, 4)
     return cudaErrorNotSupported;
 #undef KMB_CF
     if (e != cudaSuccess || !(mode & 2)) return e;

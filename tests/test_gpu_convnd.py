@@ -105,9 +105,11 @@ def test_conv_rejects_invalid(kmb, cuda):
 
 @pytest.mark.parametrize("dims,D,K", [([1024], 8, 4), ([36], 16, 3), ([37], 8, 2), ([32, 32], 64, 3),
                                       ([13, 30], 8, 2), ([6, 10], 16, 4), ([48, 64], 8, 3), ([16, 16, 16], 16, 3),
-                                      ([20, 16, 16], 8, 3), ([5, 7, 6], 8, 2)])
+                                      ([20, 16, 16], 8, 3), ([5, 7, 6], 8, 2), ([16, 16, 16], 4, 2),
+                                      ([7, 9, 13], 12, 3), ([33, 5, 20], 4, 3), ([3, 11, 8], 20, 2)])
 def test_fused_kernel_shapes(kmb, cuda, dims, D, K):
-    """The fused forward + backward kernel (D a multiple of 8, ndims <= 3):
+    """The fused forward + backward kernels (D a multiple of 8 for ndims <= 2,
+    of 4 for the 3D variant):
     slabs with their causal halos, runs of 4 and of 1 along the innermost
     axis.  The forward is bit-identical to the reference's tap order; mode 1
     and mode 2 alone give the same bits as mode 3."""
