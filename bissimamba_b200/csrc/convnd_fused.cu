@@ -1,6 +1,7 @@
 // convnd_fused.cu -- depthwise causal convND forward + backward in one launch
-// (reference src/convnd.c:396-531) for ndims <= 3, K <= 4,
-// D a multiple of 8.
+// (reference src/convnd.c:396-531): ndims <= 2 with K <= 4
+// and D a multiple of 8 on the kernel below; ndims = 3 with K <= 3 and D a
+// multiple of 4 on the streaming 3D kernel further down.
 //
 // A CTA owns (item b, slab of T0 planes of the outermost axis, 8 channels).
 // It stages the input slab with its K-1 causal halo planes / rows / columns
@@ -21,6 +22,7 @@
 // chunks in order (deterministic).  Global traffic: input and dy read once
 // (plus the halo planes of the next slab), out and dinput written once.
 #include "kmb_common.cuh"
+#include "kmb_sync.cuh"
 
 namespace kmb {
 
@@ -281,26 +283,33 @@ __global__ void __launch_bounds__(CF_THREADS, 2) conv_fused_kernel(ConvDesc c, F
 }
 
 // ---------------------------------------------------------------------------
-// 3D variant (K = 2 or 3, D a multiple of 4).  A CTA owns (item, slab of T0
-// planes of axis 0, 4 channels).  The padded slabs are laid out as
-// [plane][row][PX] points of 16 bytes with PX = d2 + K - 1 rounded up to an odd
-// number.  A warp takes 8 consecutive rows (axis 1) at one run of R points
+// 3D variant (K = 2 or 3, D a multiple of 4), streaming along axis 0.  A CTA
+// owns (item, slab of T0 planes of axis 0, 4 channels) and walks its output
+// planes in order.  Planes are staged with cp.async (16 bytes = 4 channels per
+// point, zero-filled outside the grid) into a ring of NS plane slots per
+// tensor: stage s holds the input plane z0 - H + s and the dy plane z0 + s,
+// each laid out as [row][PX] points with PX = d2 + K - 1 rounded up to an odd
+// number.  Output plane zr uses stages zr .. zr + H; stage zr + NS - 1 is
+// issued at the top of iteration zr, into the slot that output zr - 1 freed,
+// so the copies of the next planes overlap the arithmetic of this one, and
+// every input and dy plane is read once per slab.
+// Per plane, a warp takes 8 consecutive rows (axis 1) at one run of R points
 // along axis 2, 4 threads per point (one channel each): the 8 rows of a warp
 // sit PX points apart, and with PX odd their 16-byte points fall in 8
 // different bank groups, so every shared-memory read is conflict-free and its
-// address is the thread's run base plus a per-row constant.  The slabs are
-// staged with cp.async (16 bytes per point, zero-filled outside the grid).
-// Arithmetic per point and its order are those of the generic fused kernel.
+// address is the thread's run base plus a per-row constant.  Arithmetic per
+// point and its order are those of the generic fused kernel.
 // ---------------------------------------------------------------------------
+constexpr int CF3_NS = 8;   // plane slots per tensor
+
 struct Fused3Geom {
     int T0, nslab;   // planes of axis 0 per slab, slabs per item
     int PX, PY;      // padded row pitch (odd) and rows per plane, in points
-    int plane;       // PX * PY
+    int slot;        // floats of one plane slot (128-byte multiple)
 };
 
-__device__ __forceinline__ void cf_cp16(void* sdst, const void* gsrc, bool ok) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(sdst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gsrc), "r"(ok ? 16 : 0)
+__device__ __forceinline__ void cf_cp16(uint32_t sdst, const void* gsrc, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sdst), "l"(gsrc), "r"(ok ? 16 : 0)
                  : "memory");
 }
 
@@ -313,45 +322,56 @@ __global__ void __launch_bounds__(CF_THREADS, 2) conv_fused3d_kernel(ConvDesc c,
                                                                      float* __restrict__ out,
                                                                      float* __restrict__ din,
                                                                      float* __restrict__ part) {
-    constexpr int H = K - 1, V = K * K * K, ROWS = K * K;
+    constexpr int H = K - 1, V = K * K * K, ROWS = K * K, NS = CF3_NS;
     constexpr bool FWD = MODE & 1, BWD = (MODE & 2) != 0;
-    extern __shared__ __align__(16) float4 cf_smem[];
-    float4* sIN = cf_smem;
-    float4* sDY = cf_smem + (g.T0 + H) * g.plane;
-    const int D4 = c.D >> 2;
+    extern __shared__ __align__(128) float cf3_smem[];
+    float* sIN = cf3_smem;                                   // [NS][slot]
+    float* sDY = cf3_smem + NS * g.slot;
     const int slab = blockIdx.x % g.nslab;
-    const long long b = blockIdx.x / g.nslab;
+    const int b = blockIdx.x / g.nslab;
     const int q = blockIdx.y;                                // float4 channel lane of this CTA
     const int d0 = (int)c.dims[0], d1 = (int)c.dims[1], d2 = (int)c.dims[2];
     const int z0 = slab * g.T0;
     const int nz = min(g.T0, d0 - z0);
-    const long long ibase = b * c.P;
+    const int nstage = nz + H;
+    const int D4 = c.D >> 2;
     const int tid = threadIdx.x, wl = tid & 31, warp = tid >> 5;
+    const int pdx = d2 + H, npt = (d1 + H) * pdx;            // staged points of one padded plane
+    const long long zstride = (long long)d1 * d2 * D4;       // float4s per plane of axis 0
+    const float4* inb = in + (long long)b * c.P * D4 + q;
+    const float4* dyb = BWD ? dy + (long long)b * c.P * D4 + q : inb;
+    const uint32_t uin = smem_u32(sIN), udy = smem_u32(sDY);
 
-    // ---- stage: padded (pz, py, px) <- input (z0 + pz - H, py - H, px - H), dy (z0 + pz, py, px)
-    {
-        const int pdx = d2 + H, pdy = d1 + H;
-        const int n = (nz + H) * pdy * pdx;
-        const float4* inb = in + ibase * D4 + q;
-        const float4* dyb = dy ? dy + ibase * D4 + q : inb;
-        for (int i = tid; i < n; i += CF_THREADS) {
-            const int row = i / pdx, px = i - row * pdx;
-            const int pz = row / pdy, py = row - pz * pdy;
-            const int slot = pz * g.plane + py * g.PX + px;
-            if (FWD || BWD) {
-                const int zi = z0 + pz - H, yi = py - H, xi = px - H;
-                const bool ok = zi >= 0 && yi >= 0 && xi >= 0 && zi < d0;
-                cf_cp16(sIN + slot, ok ? inb + (((long long)zi * d1 + yi) * d2 + xi) * D4 : inb, ok);
-            }
-            if (BWD) {
-                const int zd = z0 + pz;
-                const bool ok = zd < d0 && py < d1 && px < d2;
-                cf_cp16(sDY + slot, ok ? dyb + (((long long)zd * d1 + py) * d2 + px) * D4 : dyb, ok);
+    // stage st -> slot st % NS: padded (py, px) <- input (z0 - H + st, py - H, px - H), dy (z0 + st, py, px)
+    auto stage = [&](int st) {
+        if (st < nstage) {
+            const int sl = st % NS;
+            const int zi = z0 - H + st, zd = z0 + st;
+            const bool zi_ok = zi >= 0, zd_ok = zd < d0;
+            int py = tid / pdx, px = tid - py * pdx;
+            const int sy = CF_THREADS / pdx, sx = CF_THREADS - sy * pdx;
+            for (int i = tid; i < npt; i += CF_THREADS) {
+                const uint32_t so = (uint32_t)((sl * g.slot + (py * g.PX + px) * 4) * 4);
+                {
+                    const int yi = py - H, xi = px - H;
+                    const bool ok = zi_ok && yi >= 0 && xi >= 0;
+                    cf_cp16(uin + so, ok ? inb + zi * zstride + ((long long)yi * d2 + xi) * D4 : inb, ok);
+                }
+                if (BWD) {
+                    const bool ok = zd_ok && py < d1 && px < d2;
+                    cf_cp16(udy + so, ok ? dyb + zd * zstride + ((long long)py * d2 + px) * D4 : dyb, ok);
+                }
+                px += sx;
+                py += sy;
+                if (px >= pdx) {
+                    px -= pdx;
+                    py++;
+                }
             }
         }
-        asm volatile("cp.async.wait_all;\n" ::: "memory");
-    }
-    __syncthreads();
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    for (int st = 0; st < NS - 1; st++) stage(st);
 
     const int l = tid & 3, iy = (tid >> 2) & 7;
     const int ch = q * 4 + l;
@@ -362,68 +382,78 @@ __global__ void __launch_bounds__(CF_THREADS, 2) conv_fused3d_kernel(ConvDesc c,
     float dk[BWD ? V + 1 : 1];
 #pragma unroll
     for (int k = 0; k < (BWD ? V + 1 : 1); k++) dk[k] = 0.0f;
-    const float* sINf = (const float*)sIN + l;
-    const float* sDYf = (const float*)sDY + l;
-    const int PL = g.plane, PX = g.PX;
+    const int PX = g.PX;
     const int nrun = d2 / R, nyb = (d1 + 7) >> 3;
-    const int ntask = nz * nyb * nrun;
-    for (int t = warp; t < ntask; t += CF_THREADS / 32) {
-        const int xr = t % nrun, rest = t / nrun;
-        const int zr = rest / nyb, y = (rest - zr * nyb) * 8 + iy;
-        if (y >= d1) continue;
-        const int x0 = xr * R;
-        const int base = zr * PL + y * PX + x0;
-        const float* pin = sINf + base * 4;
-        const float* pdy = sDYf + base * 4;
-        float acc[R], adin[R], dyo[R];
+    const int ntask = nyb * nrun;
+    const long long ibase = (long long)b * c.P;
+    for (int zr = 0; zr < nz; zr++) {
+        // stages <= zr + H have landed once at most NS - 2 - H of the later groups are pending
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(NS - 2 - H) : "memory");
+        __syncthreads();   // ... for every thread's copies; and every warp is done with output zr - 1
+        stage(zr + NS - 1);   // into the slot of stage zr - 1
+        const float* pin[K];
+        const float* pdy[K];
 #pragma unroll
-        for (int r = 0; r < R; r++) {
-            acc[r] = b0;
-            adin[r] = 0.0f;
-            if (BWD) dyo[r] = pdy[r * 4];
+        for (int k0 = 0; k0 < K; k0++) {
+            pin[k0] = sIN + ((zr + k0) % NS) * g.slot + l;              // input plane z - H + k0
+            pdy[k0] = sDY + ((zr + H - k0) % NS) * g.slot + l;          // dy plane z + H - k0
         }
+        for (int t = warp; t < ntask; t += CF_THREADS / 32) {
+            const int yb = t / nrun;
+            const int y = yb * 8 + iy;
+            if (y >= d1) continue;
+            const int x0 = (t - yb * nrun) * R;
+            const int base = (y * PX + x0) * 4;
+            float acc[R], adin[R], dyo[R];
 #pragma unroll
-        for (int row = 0; row < ROWS; row++) {
-            const int k0 = row / K, k1 = row % K;
-            {
-                const float* pr = pin + (k0 * PL + k1 * PX) * 4;
-                float w[R + H];
+            for (int r = 0; r < R; r++) {
+                acc[r] = b0;
+                adin[r] = 0.0f;
+                if (BWD) dyo[r] = pdy[H][base + r * 4];
+            }
 #pragma unroll
-                for (int j = 0; j < R + H; j++) w[j] = pr[j * 4];
+            for (int row = 0; row < ROWS; row++) {
+                const int k0 = row / K, k1 = row % K;
+                {
+                    const float* pr = pin[k0] + base + k1 * PX * 4;
+                    float w[R + H];
 #pragma unroll
-                for (int kx = 0; kx < K; kx++) {
-                    const int k = row * K + kx;
+                    for (int j = 0; j < R + H; j++) w[j] = pr[j * 4];
 #pragma unroll
-                    for (int r = 0; r < R; r++) {
-                        if (FWD) acc[r] = __fmaf_rn(w[r + kx], kv[k], acc[r]);
-                        if (BWD) dk[k] = __fmaf_rn(dyo[r], w[r + kx], dk[k]);
+                    for (int kx = 0; kx < K; kx++) {
+                        const int k = row * K + kx;
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            if (FWD) acc[r] = __fmaf_rn(w[r + kx], kv[k], acc[r]);
+                            if (BWD) dk[k] = __fmaf_rn(dyo[r], w[r + kx], dk[k]);
+                        }
+                    }
+                }
+                if (BWD) {
+                    const float* pr = pdy[k0] + base + (H - k1) * PX * 4;
+                    float w[R + H];
+#pragma unroll
+                    for (int j = 0; j < R + H; j++) w[j] = pr[j * 4];
+#pragma unroll
+                    for (int kx = 0; kx < K; kx++) {
+                        const int k = row * K + kx;
+#pragma unroll
+                        for (int r = 0; r < R; r++) adin[r] = __fmaf_rn(w[r + H - kx], kv[k], adin[r]);
                     }
                 }
             }
-            if (BWD) {
-                const float* pr = pdy + ((H - k0) * PL + (H - k1) * PX) * 4;
-                float w[R + H];
+            const long long gi0 = (ibase + ((long long)(z0 + zr) * d1 + y) * d2 + x0) * c.D + ch;
 #pragma unroll
-                for (int j = 0; j < R + H; j++) w[j] = pr[j * 4];
-#pragma unroll
-                for (int kx = 0; kx < K; kx++) {
-                    const int k = row * K + kx;
-#pragma unroll
-                    for (int r = 0; r < R; r++) adin[r] = __fmaf_rn(w[r + H - kx], kv[k], adin[r]);
+            for (int r = 0; r < R; r++) {
+                if (FWD) out[gi0 + (long long)r * c.D] = acc[r];
+                if (BWD) {
+                    din[gi0 + (long long)r * c.D] = adin[r];
+                    dk[V] += dyo[r];
                 }
             }
         }
-        const long long p = ((long long)(z0 + zr) * d1 + y) * d2 + x0;
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-            const long long gi = (ibase + p + r) * c.D + ch;
-            if (FWD) out[gi] = acc[r];
-            if (BWD) {
-                din[gi] = adin[r];
-                dk[V] += dyo[r];
-            }
-        }
     }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
     if (!BWD) return;
     // ---- dkernel / dbias partials of the CTA: the 8 threads of a warp that share a channel
     // (xor shuffles 4, 8, 16), then the warps in order
@@ -432,14 +462,14 @@ __global__ void __launch_bounds__(CF_THREADS, 2) conv_fused3d_kernel(ConvDesc c,
     for (int k = 0; k < NV; k++)
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) dk[k] += __shfl_xor_sync(~0u, dk[k], o);
-    __syncthreads();
-    float* red = (float*)cf_smem;   // [warp][NV][4]
+    __syncthreads();   // every warp is done with the ring
+    float* red = cf3_smem;   // [warp][NV][4]
     if (wl < 4) {
 #pragma unroll
         for (int k = 0; k < NV; k++) red[(warp * NV + k) * 4 + wl] = dk[k];
     }
     __syncthreads();
-    const long long chunk = b * g.nslab + slab;
+    const long long chunk = (long long)b * g.nslab + slab;
     for (int i = tid; i < NV * 4; i += CF_THREADS) {
         const int k = i >> 2, l2 = i & 3;
         float s2 = red[k * 4 + l2];
@@ -452,21 +482,25 @@ static bool cf3_plan(const ConvDesc& c, int mode, Fused3Geom* g, int* smem, int*
     if (c.nd != 3 || c.K < 2 || c.K > 3 || c.D % 4 != 0) return false;
     const int H = c.K - 1;
     const long long d0 = c.dims[0], d1 = c.dims[1], d2 = c.dims[2];
-    if (d1 + H > 4096 || d2 + H > 4096) return false;
+    if (d1 + H > 4096 || d2 + H > 4096 || c.batch > 0x7fffffffLL) return false;
     int PX = (int)d2 + H;
     if (PX % 2 == 0) PX++;
     const int PY = (int)d1 + H;
-    const long long plane_bytes = (long long)PX * PY * 16 * ((mode & 2) ? 2 : 1);
-    const long long t0max = CF_SMEM_MAX / plane_bytes - H;
-    if (t0max < 1) return false;
-    const long long nslab = (d0 + t0max - 1) / t0max;
+    const int ntens = (mode & 2) ? 2 : 1;
+    const long long slot = ((long long)PX * PY * 16 + 127) / 128 * 128;
+    if (CF3_NS * slot * ntens > CF_SMEM_MAX) return false;
+    // slabs along axis 0: enough CTAs for about six waves at two per SM, at least 4 planes per slab
+    long long nslab = 1;
+    const long long per_slab = c.batch * (c.D / 4);
+    while (nslab < d0 / 4 && per_slab * nslab < 6 * 148 * 2) nslab++;
     g->nslab = (int)nslab;
     g->T0 = (int)((d0 + nslab - 1) / nslab);
+    g->nslab = (int)((d0 + g->T0 - 1) / g->T0);
     g->PX = PX;
     g->PY = PY;
-    g->plane = PX * PY;
+    g->slot = (int)(slot / 4);
     *R = (d2 % 4 == 0) ? 4 : 1;
-    int sm = (int)((g->T0 + H) * plane_bytes);
+    int sm = (int)(CF3_NS * slot * ntens);
     const int red = (CF_THREADS / 32) * (c.K * c.K * c.K + 1) * 4 * 4;
     if ((mode & 2) && red > sm) sm = red;
     *smem = sm;
@@ -509,13 +543,12 @@ __global__ void cf_reduce_dk(const float* __restrict__ part, float* __restrict__
     else dbias[i - VD] = acc;
 }
 
-// Channel lanes per CTA: 8 channels (one 32-byte sector per point) for 1D / 2D,
-// 4 for 3D, whose padded planes are larger.
-static int cf_cg(int nd) { return nd == 3 ? 1 : 2; }
+// Channel lanes per CTA: 8 channels (one 32-byte sector per point).
+static int cf_cg(int) { return 2; }
 
 // Plans the slab split; false when the shape is outside the kernel's set.
 static bool cf_plan(const ConvDesc& c, int mode, FusedGeom* g, int* smem, int* R) {
-    if (c.nd < 1 || c.nd > 3 || c.K < 2 || c.K > 4 || c.D % 8 != 0 || (c.nd == 3 && c.K == 4)) return false;
+    if (c.nd < 1 || c.nd > 2 || c.K < 2 || c.K > 4 || c.D % 8 != 0) return false;
     const int H = c.K - 1, CG = cf_cg(c.nd);
     const int dlast = (int)c.dims[c.nd - 1];
     *R = (dlast % 4 == 0) ? 4 : 1;
@@ -570,11 +603,9 @@ template <int ND, int K, int R, int MODE>
 static cudaError_t cf_launch_t(const ConvDesc& c, const FusedGeom& g, int smem, const float* in, const float* ker,
                                const float* bias, const float* dy, float* out, float* din, float* part,
                                cudaStream_t st) {
-    // one channel per thread in 3D (27 taps of kernel values and dkernel accumulators in registers,
-    // two CTAs per SM; two channels as packed pairs need ~240 registers and one CTA per SM, measured
-    // 0.42 ms against 0.31 ms), two channels as packed fp32 pairs elsewhere
-    constexpr int N = ND == 3 ? 1 : 2;
-    constexpr int CG = ND == 3 ? 1 : 2;
+    // two channels per thread as packed fp32 pairs, 8 channels per CTA (1D and 2D; 3D has its own kernel)
+    constexpr int N = 2;
+    constexpr int CG = 2;
     auto k = conv_fused_kernel<ND, K, R, MODE, N, CG>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
