@@ -14,6 +14,10 @@ batch 32 per GPU, reported as state-updates/s.
 * cpu_baseline: the reference's own scannd_ref (oracle/_ref, compiled from the
            reference sources) on a bounded sample of the same workload, all
            host threads, rank 0, N=1.
+* other_configs (N=1): every other BASELINE config (--workload all: configs
+           0-4 forward / backward / block / model), run in a child process
+           after the headline and summarised in the same line (value, ms per
+           step, roofline fraction, e2e, CPU-baseline rate).
 Multi-GPU: one process per GPU (torchrun), every rank scans its own batch of
 32 items (weak scaling); the scan has no cross-rank exchange in forward.
 """
@@ -74,6 +78,8 @@ def parse():
                              "convnd3d", "block", "block_bf16", "model", "all"],
                     help="scan_fwd = the headline line; the others measure the other BASELINE configs "
                          "(all = every other one, one line each)")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="N=1 headline run: skip the summary of the other BASELINE configs (one child process, ~35 s)")
     ap.add_argument("--chunks", type=int, default=4, help="N > 1: item chunks of the scan / gather overlap")
     ap.add_argument("--gather-mode", default="overlap", choices=["overlap", "after"],
                     help="N > 1: gather each chunk's y while the next is scanned, or all of y after the scan")
@@ -407,6 +413,7 @@ def main():
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                "ms_per_step": 1e3 * dt / args.e2e_steps, "batch_per_gpu": eb,
                "path": "scannd_batched() with pinned host buffers: H2D inputs, kernel, D2H h and y, pipelined by item chunks over three streams (PCIe-bound)"}
+        del hb, ph
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -414,6 +421,14 @@ def main():
             cpu, _ = cpu_reference_rate()
         except Exception as exc:  # the reference build is test infrastructure: report, do not fail
             cpu = {"value": None, "error": str(exc)[:200]}
+
+    others = None
+    if rank == 0 and world == 1 and not args.no_other_configs:
+        host = None   # the child pins its own host buffers: release the headline's first  # noqa: F841
+        torch.cuda.empty_cache()
+        if hasattr(torch._C, "_host_emptyCache"):
+            torch._C._host_emptyCache()
+        others = other_configs(args)
 
     if rank == 0:
         line = {"metric": "scanND state-updates/sec", "value": value, "unit": "state-updates/s",
@@ -432,7 +447,8 @@ def main():
                 "variants": variants,
                 "gpu_launches": args.steps * (1 if world == 1 else gather["chunks"]), "clocks": clk,
                 "collective": gather_info,
-                "kernel_ms": {"mean": statistics.mean(kern_ms), "min": min(kern_ms), "max": max(kern_ms)}}
+                "kernel_ms": {"mean": statistics.mean(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
+                "other_configs": others}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -867,6 +883,35 @@ def wl_model(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, world)
                                           f"oracle/_ref) on 1 sequence of 16384 tokens, rate / 12 layers; "
                                           f"median of {n}"}
     return line
+
+
+def other_configs(args):
+    """The other BASELINE configs (every workload of --workload all), measured in
+    a child process after the headline and summarised into the headline line:
+    value, ms per step, roofline fraction, e2e and CPU-baseline rates."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--workload", "all", "--steps", "10", "--warmup", "3"]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
+    except Exception as exc:
+        return {"error": str(exc)[:200]}
+    out = {}
+    for ln in r.stdout.splitlines():
+        if not ln.startswith("{"):
+            continue
+        try:
+            d = json.loads(ln)
+        except ValueError:
+            continue
+        rf, e2, cb = d.get("roofline") or {}, d.get("e2e") or {}, d.get("cpu_baseline") or {}
+        out[d["config"]["workload"]] = {
+            "metric": d.get("metric"), "value": d.get("value"), "unit": d.get("unit"),
+            "ms_per_step": d.get("ms_per_step"), "dtype": d.get("dtype"), "steps": d.get("steps"),
+            "roofline_frac": rf.get("frac"), "roofline_bound": rf.get("bound"), "e2e": e2.get("value"),
+            "cpu_baseline": cb.get("value"), "cpu_baseline_kind": cb.get("kind"), "cpu_cores": cb.get("cores")}
+    if r.returncode != 0:
+        out["error"] = (r.stderr or "")[-300:]
+    return out
 
 
 def run_other_workload(args, rank, world):
