@@ -58,80 +58,87 @@ __device__ __forceinline__ void stv(__nv_bfloat16* p, float v) { *p = __float2bf
 __device__ __forceinline__ float ldv(const float* p) { return *p; }
 __device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-// Forward epilogue over P[BL, Rt]; T = storage type of the scan inputs
+// Forward epilogue over P[BL, Rt]; T = storage type of the scan inputs.  A CTA walks rows (rpi rows at a time,
+// tpr threads per row, grid-stride): thread j of a row writes B[j] and C[j] and, for j < R + 2, the u / dt /
+// lambda column j (coalesced row segments, no per-element index division).
 template <typename T>
 __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, int R, int NR, float dt_min,
                                    float dt_max, const float* __restrict__ bB, const float* __restrict__ bC,
                                    T* __restrict__ u, T* __restrict__ dt, T* __restrict__ lam,
                                    T* __restrict__ B, T* __restrict__ C) {
-    const long long Rt = R + 2 + 2LL * NR;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= BL * Rt) return;
-    // 32-bit division when the index fits (the common case), 64-bit otherwise
-    const long long row = BL * Rt <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)Rt) : i / Rt;
-    const int col = (int)(i - row * Rt);
-    const float v = P[i];
-    if (col < R) {
-        stv(u + row * R + col, v / (1.0f + expf(-v)));          // silu
-    } else if (col == R) {
-        float d = logf(1.0f + expf(v));                           // softplus
-        if (d < dt_min) d = dt_min;
-        if (d > dt_max) d = dt_max;
-        stv(dt + row, d);
-    } else if (col == R + 1) {
-        stv(lam + row, sigm(v));
-    } else if (col < R + 2 + NR) {
-        const int j = col - R - 2;
-        stv(B + row * NR + j, v + bB[j]);
-    } else {
-        const int j = col - R - 2 - NR;
-        stv(C + row * NR + j, v + bC[j]);
+    const int Rt = R + 2 + 2 * NR;
+    const int W = NR > R + 2 ? NR : R + 2;
+    const int tpr = W < (int)blockDim.x ? W : (int)blockDim.x, rpi = blockDim.x / tpr;
+    const int sub = threadIdx.x / tpr, c0 = threadIdx.x - sub * tpr;
+    if (sub >= rpi) return;
+    for (long long row = (long long)blockIdx.x * rpi + sub; row < BL; row += (long long)gridDim.x * rpi) {
+        const float* pr = P + row * Rt;
+        for (int j = c0; j < W; j += tpr) {
+            if (j < NR) {
+                stv(B + row * NR + j, pr[R + 2 + j] + bB[j]);
+                stv(C + row * NR + j, pr[R + 2 + NR + j] + bC[j]);
+            }
+            if (j < R) {
+                const float v = pr[j];
+                stv(u + row * R + j, v / (1.0f + expf(-v)));          // silu
+            } else if (j == R) {
+                float d = logf(1.0f + expf(pr[j]));                     // softplus
+                if (d < dt_min) d = dt_min;
+                if (d > dt_max) d = dt_max;
+                stv(dt + row, d);
+            } else if (j == R + 1) {
+                stv(lam + row, sigm(pr[j]));
+            }
+        }
     }
 }
 
 // Backward epilogue: dP[BL, Rt] from the scan gradients (O = float, or bf16
-// as the operand of the bf16 tensor-core gradient GEMMs)
+// as the operand of the bf16 tensor-core gradient GEMMs).  dP rows have ldo >= Rt
+// columns; columns Rt .. ldo-1 are written as zero.  Rows are walked as in the
+// forward epilogue: thread j of a row writes dP[R + 2 + j] (from dB), dP[R + 2 + NR + j]
+// (from dC), the column j < R + 2 and the padding column Rt + j.
 template <typename T, typename O>
 __global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restrict__ dtv,
                                    const T* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
                                    float dt_max, const float* __restrict__ du, const float* __restrict__ ddt,
                                    const float* __restrict__ dlam, const float* __restrict__ dB,
                                    const float* __restrict__ dC, O* __restrict__ dP, int ldo) {
-    // dP rows have ldo >= Rt columns; columns Rt .. ldo-1 are written as zero
-    const long long Rt = R + 2 + 2LL * NR;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= BL * ldo) return;
-    // 32-bit division when the index fits (the common case), 64-bit otherwise
-    const long long row = BL * ldo <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)ldo) : i / ldo;
-    const int col = (int)(i - row * ldo);
-    if (col >= Rt) {
-        stv(dP + i, 0.0f);
-        return;
+    const int Rt = R + 2 + 2 * NR, pad = ldo - Rt;
+    int W = NR > R + 2 ? NR : R + 2;
+    if (pad > W) W = pad;
+    const int tpr = W < (int)blockDim.x ? W : (int)blockDim.x, rpi = blockDim.x / tpr;
+    const int sub = threadIdx.x / tpr, c0 = threadIdx.x - sub * tpr;
+    (void)dtv;
+    if (sub >= rpi) return;
+    for (long long row = (long long)blockIdx.x * rpi + sub; row < BL; row += (long long)gridDim.x * rpi) {
+        const float* pr = P + row * Rt;
+        O* dr = dP + row * ldo;
+        for (int j = c0; j < W; j += tpr) {
+            if (j < NR) {
+                stv(dr + R + 2 + j, dB[row * NR + j]);
+                stv(dr + R + 2 + NR + j, dC[row * NR + j]);
+            }
+            if (j < pad) stv(dr + Rt + j, 0.0f);
+            if (j < R) {
+                const float z = pr[j], s = sigm(z);
+                stv(dr + j, du[row * R + j] * s * (1.0f + z * (1.0f - s)));   // silu'
+            } else if (j == R) {
+                // clamp test on the unrounded softplus (identical to the stored dt in fp32 mode)
+                const float z = pr[j];
+                const float d = fminf(fmaxf(logf(1.0f + expf(z)), dt_min), dt_max);
+                stv(dr + j, (d > dt_min && d < dt_max) ? ddt[row] * sigm(z) : 0.0f);   // softplus' inside the clamp
+            } else if (j == R + 1) {
+                const float l = ldv(lamv + row);
+                stv(dr + j, dlam[row] * l * (1.0f - l));
+            }
+        }
     }
-    const long long ip = row * Rt + col;   // index into P
-    float g;
-    if (col < R) {
-        const float z = P[ip], s = sigm(z);
-        g = du[row * R + col] * s * (1.0f + z * (1.0f - s));          // silu'
-    } else if (col == R) {
-        // clamp test on the unrounded softplus (identical to the stored dt in fp32 mode)
-        const float d = fminf(fmaxf(logf(1.0f + expf(P[ip])), dt_min), dt_max);
-        (void)dtv;
-        g = (d > dt_min && d < dt_max) ? ddt[row] * sigm(P[ip]) : 0.0f;  // softplus' inside the clamp
-    } else if (col == R + 1) {
-        const float l = ldv(lamv + row);
-        g = dlam[row] * l * (1.0f - l);
-    } else if (col < R + 2 + NR) {
-        g = dB[row * NR + (col - R - 2)];
-    } else {
-        g = dC[row * NR + (col - R - 2 - NR)];
-    }
-    stv(dP + i, g);
 }
 
 // The bf16 form of block_bwd_epilogue: 8 consecutive dP columns of one row per
-// thread (one index division per 8 elements, one 16-byte store); ldo % 8 == 0 and
-// a 16-byte-aligned dP.  Same per-element arithmetic.
+// thread (one 16-byte store), rows walked as above; ldo % 8 == 0 and a
+// 16-byte-aligned dP.  Same per-element arithmetic.
 template <typename T>
 __global__ void block_bwd_epilogue_v8(const float* __restrict__ P, const T* __restrict__ lamv, long long BL, int R,
                                       int NR, float dt_min, float dt_max, const float* __restrict__ du,
@@ -139,10 +146,12 @@ __global__ void block_bwd_epilogue_v8(const float* __restrict__ P, const T* __re
                                       const float* __restrict__ dB, const float* __restrict__ dC,
                                       __nv_bfloat16* __restrict__ dP, int ldo) {
     const int Rt = R + 2 + 2 * NR, ch = ldo >> 3;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= BL * ch) return;
-    const long long row = BL * ch <= 0xffffffffLL ? (long long)((unsigned)i / (unsigned)ch) : i / ch;
-    const int c0 = (int)(i - row * ch) * 8;
+    const int tpr = ch < (int)blockDim.x ? ch : (int)blockDim.x, rpi = blockDim.x / tpr;
+    const int sub = threadIdx.x / tpr, k0 = threadIdx.x - sub * tpr;
+    if (sub >= rpi) return;
+    for (long long row = (long long)blockIdx.x * rpi + sub; row < BL; row += (long long)gridDim.x * rpi)
+    for (int k = k0; k < ch; k += tpr) {
+    const int c0 = k * 8;
     uint4 pk;
     __nv_bfloat16* e = (__nv_bfloat16*)&pk;
 #pragma unroll
@@ -167,6 +176,7 @@ __global__ void block_bwd_epilogue_v8(const float* __restrict__ P, const T* __re
         e[j] = __float2bfloat16_rn(g);
     }
     *(uint4*)(dP + row * ldo + c0) = pk;
+    }
 }
 
 // grads += slices of G[Rt, dim]
@@ -274,6 +284,25 @@ cudaError_t launch_pack_wcat_t(const float* Win, const float* dp, const float* l
 
 static inline unsigned nb(long long n, int t) { return (unsigned)((n + t - 1) / t); }
 
+// Grid of the row-walking epilogues: rows / (rows per CTA pass), at most 8 CTAs of 256 threads per SM
+static unsigned row_grid(long long rows, int per_row) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+    }
+    const int tpr = per_row < 256 ? (per_row < 1 ? 1 : per_row) : 256, rpi = 256 / tpr;
+    long long g = (rows + rpi - 1) / rpi;
+    if (g > 8LL * sms) g = 8LL * sms;
+    return (unsigned)(g < 1 ? 1 : g);
+}
+static int epi_width(int R, long long NR, long long pad = 0) {
+    long long w = NR > R + 2 ? NR : R + 2;
+    if (pad > w) w = pad;
+    return (int)w;
+}
+
 static int check_cfg(const KMBlockConfig* c, const KMBlockWeights* w, long batch) {
     if (!c || !w || batch < 1 || c->dim < 1 || c->N < 1 || c->N > 64 || c->R < 1 || c->L < 1)
         return set_error("invalid KMBlockConfig (N must be 1..64)");
@@ -347,14 +376,14 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
         to_bf16<<<nb(a.Rt * dim, 256), 256, 0, st>>>(W, Wb, a.Rt * dim);
         if ((e = mm_nt(true, a.BL, a.Rt, dim, x, dim, Wb, dim, act + a.proj, a.Rt, false, st)) != cudaSuccess)
             return set_cuda_error("bf16 projection GEMM", e);
-        block_fwd_epilogue<H><<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(
+        block_fwd_epilogue<H><<<row_grid(a.BL, epi_width((int)c->R, a.NR)), 256, 0, st>>>(
             act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, (H*)(act + a.u),
             (H*)(act + a.dt), (H*)(act + a.lam), (H*)(act + a.B), (H*)(act + a.C));
     } else {
         // P[BL, Rt] = X[BL, dim] . Wcat^T on the tensor cores at fp32 accuracy (3xTF32)
         if ((e = mm_nt(false, a.BL, a.Rt, dim, x, dim, W, dim, act + a.proj, a.Rt, false, st)) != cudaSuccess)
             return set_cuda_error("projection GEMM", e);
-        block_fwd_epilogue<float><<<nb(a.BL * a.Rt, 256), 256, 0, st>>>(
+        block_fwd_epilogue<float><<<row_grid(a.BL, epi_width((int)c->R, a.NR)), 256, 0, st>>>(
             act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, act + a.u, act + a.dt,
             act + a.lam, act + a.B, act + a.C);
     }
@@ -425,7 +454,7 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
     // du, ddt, dlambda, dB, dC are assigned (no clearing of the scratch first)
     if (kmb_blockscan_backward_ex(&p, batch, S + s_dy, &sg, 1, stream)) return -1;
-    block_bwd_epilogue<float, float><<<nb(BL * ldq, 256), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
+    block_bwd_epilogue<float, float><<<row_grid(BL, epi_width(R, NR, ldq - Rt)), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
                                                                      (int)NR, c->dt_min, c->dt_max, S + s_du,
                                                                      S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
                                                                      S + s_dP, (int)ldq);
@@ -513,7 +542,7 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     // du, ddt, dlambda, dB, dC are assigned (no clearing of the scratch first)
     if (kmb_blockscan_backward_ex(&p, batch, S + s_dy, &sg, 1, stream)) return -1;
     // ldp is a multiple of 16 and dPb 256-byte aligned: the 8-column form applies
-    block_bwd_epilogue_v8<H><<<nb(BL * (ldp / 8), 256), 256, 0, st>>>(
+    block_bwd_epilogue_v8<H><<<row_grid(BL, (int)(ldp / 8)), 256, 0, st>>>(
         act + a.proj, (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max, S + s_du, S + s_ddt,
         S + s_dlam, S + s_dB, S + s_dC, dPb, ldp);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);

@@ -277,23 +277,53 @@ __global__ void add_rank_partials(const float* __restrict__ part, int nblk, int 
     }
 }
 
-// out[row, j] = x[row, j] + sum_r y[row, r] W[j, r], four columns per thread (dim % 4 == 0)
+// out[row, j] = x[row, j] + sum_r y[row, r] W[j, r], four columns per thread (dim % 4 == 0).
+// W (dim x R) is staged once per CTA in shared memory as its transpose [R][dim], so a thread reads its four
+// columns of each rank as one conflict-free 16-byte load (read from W directly, the R x 4 scalars of a
+// thread sit 16 R bytes apart across the warp and each load touched ~16 sectors).  A CTA walks rows
+// (rpi rows at a time, tpr threads per row, grid-stride); the sum over r is in ascending order.
 __global__ void out_rank_f32x4(const float4* __restrict__ x, const float* __restrict__ y, const float* __restrict__ W,
                                long long rows, int dim4, int R, float4* __restrict__ out) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= rows * dim4) return;
-    const long long row = i / dim4;
-    const int j = (int)(i - row * dim4) * 4;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int r = 0; r < R; r++) {
-        const float yv = y[row * R + r];
-        a0 = __fmaf_rn(yv, W[(long long)(j + 0) * R + r], a0);
-        a1 = __fmaf_rn(yv, W[(long long)(j + 1) * R + r], a1);
-        a2 = __fmaf_rn(yv, W[(long long)(j + 2) * R + r], a2);
-        a3 = __fmaf_rn(yv, W[(long long)(j + 3) * R + r], a3);
+    extern __shared__ float4 ork_wt[];   // [R][dim4]
+    const int dim = dim4 * 4;
+    float* wt = (float*)ork_wt;
+    for (int i = threadIdx.x; i < dim * R; i += blockDim.x) {
+        const int j = i / R, r = i - j * R;
+        wt[r * dim + j] = W[i];
     }
-    const float4 xv = x[i];
-    out[i] = make_float4(xv.x + a0, xv.y + a1, xv.z + a2, xv.w + a3);
+    __syncthreads();
+    const int tpr = dim4 < (int)blockDim.x ? dim4 : (int)blockDim.x;
+    const int rpi = blockDim.x / tpr;
+    const int sub = threadIdx.x / tpr, c0 = threadIdx.x - sub * tpr;
+    if (sub >= rpi) return;
+    // two rows per step (their loads in flight together)
+    const long long rstep = (long long)gridDim.x * rpi;
+    for (long long row = (long long)blockIdx.x * rpi + sub; row < rows; row += 2 * rstep) {
+        const long long row2 = row + rstep;
+        const bool two = row2 < rows;
+        const float* yr = y + row * R;
+        const float* yr2 = y + (two ? row2 : row) * R;
+        for (int j4 = c0; j4 < dim4; j4 += tpr) {
+            const long long i = row * dim4 + j4, i2 = (two ? row2 : row) * dim4 + j4;
+            const float4 xv = x[i];
+            const float4 xv2 = x[i2];
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+            for (int r = 0; r < R; r++) {
+                const float yv = yr[r], yv2 = yr2[r];
+                const float4 w = ork_wt[r * dim4 + j4];
+                a0 = __fmaf_rn(yv, w.x, a0);
+                a1 = __fmaf_rn(yv, w.y, a1);
+                a2 = __fmaf_rn(yv, w.z, a2);
+                a3 = __fmaf_rn(yv, w.w, a3);
+                b0 = __fmaf_rn(yv2, w.x, b0);
+                b1 = __fmaf_rn(yv2, w.y, b1);
+                b2 = __fmaf_rn(yv2, w.z, b2);
+                b3 = __fmaf_rn(yv2, w.w, b3);
+            }
+            out[i] = make_float4(xv.x + a0, xv.y + a1, xv.z + a2, xv.w + a3);
+            if (two) out[i2] = make_float4(xv2.x + b0, xv2.y + b1, xv2.z + b2, xv2.w + b3);
+        }
+    }
 }
 
 // out[row, j] = x[row, j] + sum_r y[row, r] W[j, r]   (fp32 residual stream)
@@ -562,9 +592,16 @@ cudaError_t col_sums(const float* X, long long rows, int dim, float* g, cudaStre
 
 cudaError_t out_rank(const float* x, const float* y, const float* W, long long rows, int dim, int R, float* out,
                      cudaStream_t st) {
-    if (dim % 4 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)out & 15)) {
-        out_rank_f32x4<<<nblk(rows * (dim / 4), 256), 256, 0, st>>>((const float4*)x, y, W, rows, dim / 4, R,
-                                                                    (float4*)out);
+    const size_t wbytes = (size_t)dim * R * sizeof(float);
+    if (dim % 4 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)out & 15) && wbytes <= 48 * 1024) {
+        const int dim4 = dim / 4, tpr = dim4 < 256 ? dim4 : 256, rpi = 256 / tpr;
+        long long grid = (rows + rpi - 1) / rpi;
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (grid > 8LL * sms) grid = 8LL * sms;
+        if (grid < 1) grid = 1;
+        out_rank_f32x4<<<(unsigned)grid, 256, wbytes, st>>>((const float4*)x, y, W, rows, dim4, R, (float4*)out);
         return cudaGetLastError();
     }
     out_rank_f32<<<nblk(rows * dim, 256), 256, 0, st>>>(x, y, W, rows, dim, R, out);
