@@ -59,8 +59,8 @@ __device__ __forceinline__ float ldv(const float* p) { return *p; }
 __device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
 // Forward epilogue over P[BL, Rt]; T = storage type of the scan inputs.  A CTA walks rows (rpi rows at a time,
-// tpr threads per row, grid-stride): thread j of a row writes B[j] and C[j] and, for j < R + 2, the u / dt /
-// lambda column j (coalesced row segments, no per-element index division).
+// tpr threads per row, grid-stride): thread j of a row writes B[j] and C[j] (coalesced row segments, no
+// per-element index division); the u / dt / lambda columns go to lane 0 of as many warps.
 template <typename T>
 __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, int R, int NR, float dt_min,
                                    float dt_max, const float* __restrict__ bB, const float* __restrict__ bC,
@@ -78,6 +78,10 @@ __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, in
                 stv(B + row * NR + j, pr[R + 2 + j] + bB[j]);
                 stv(C + row * NR + j, pr[R + 2 + NR + j] + bC[j]);
             }
+        }
+        // u / dt / lambda: column k on lane 0 of warp k of the row's threads (spread over warps)
+        for (int k = c0 >> 5; (c0 & 31) == 0 && k < R + 2; k += (tpr + 31) >> 5) {
+            const int j = k;
             if (j < R) {
                 const float v = pr[j];
                 stv(u + row * R + j, v / (1.0f + expf(-v)));          // silu
@@ -97,7 +101,7 @@ __global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, in
 // as the operand of the bf16 tensor-core gradient GEMMs).  dP rows have ldo >= Rt
 // columns; columns Rt .. ldo-1 are written as zero.  Rows are walked as in the
 // forward epilogue: thread j of a row writes dP[R + 2 + j] (from dB), dP[R + 2 + NR + j]
-// (from dC), the column j < R + 2 and the padding column Rt + j.
+// (from dC) and the padding column Rt + j; the columns j < R + 2 go to lane 0 of as many warps.
 template <typename T, typename O>
 __global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restrict__ dtv,
                                    const T* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
@@ -120,6 +124,10 @@ __global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restr
                 stv(dr + R + 2 + NR + j, dC[row * NR + j]);
             }
             if (j < pad) stv(dr + Rt + j, 0.0f);
+        }
+        // columns j < R + 2: column k on lane 0 of warp k of the row's threads (spread over warps)
+        for (int k = c0 >> 5; (c0 & 31) == 0 && k < R + 2; k += (tpr + 31) >> 5) {
+            const int j = k;
             if (j < R) {
                 const float z = pr[j], s = sigm(z);
                 stv(dr + j, du[row * R + j] * s * (1.0f + z * (1.0f - s)));   // silu'

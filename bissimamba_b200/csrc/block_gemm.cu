@@ -296,32 +296,36 @@ __global__ void out_rank_f32x4(const float4* __restrict__ x, const float* __rest
     const int rpi = blockDim.x / tpr;
     const int sub = threadIdx.x / tpr, c0 = threadIdx.x - sub * tpr;
     if (sub >= rpi) return;
-    // two rows per step (their loads in flight together)
+    // four rows per step (their loads in flight together)
     const long long rstep = (long long)gridDim.x * rpi;
-    for (long long row = (long long)blockIdx.x * rpi + sub; row < rows; row += 2 * rstep) {
-        const long long row2 = row + rstep;
-        const bool two = row2 < rows;
-        const float* yr = y + row * R;
-        const float* yr2 = y + (two ? row2 : row) * R;
+    for (long long row0 = (long long)blockIdx.x * rpi + sub; row0 < rows; row0 += 4 * rstep) {
         for (int j4 = c0; j4 < dim4; j4 += tpr) {
-            const long long i = row * dim4 + j4, i2 = (two ? row2 : row) * dim4 + j4;
-            const float4 xv = x[i];
-            const float4 xv2 = x[i2];
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-            for (int r = 0; r < R; r++) {
-                const float yv = yr[r], yv2 = yr2[r];
-                const float4 w = ork_wt[r * dim4 + j4];
-                a0 = __fmaf_rn(yv, w.x, a0);
-                a1 = __fmaf_rn(yv, w.y, a1);
-                a2 = __fmaf_rn(yv, w.z, a2);
-                a3 = __fmaf_rn(yv, w.w, a3);
-                b0 = __fmaf_rn(yv2, w.x, b0);
-                b1 = __fmaf_rn(yv2, w.y, b1);
-                b2 = __fmaf_rn(yv2, w.z, b2);
-                b3 = __fmaf_rn(yv2, w.w, b3);
+            float4 xv[4], a[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const long long row = row0 + q * rstep;
+                a[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (row < rows) xv[q] = x[row * dim4 + j4];
             }
-            out[i] = make_float4(xv.x + a0, xv.y + a1, xv.z + a2, xv.w + a3);
-            if (two) out[i2] = make_float4(xv2.x + b0, xv2.y + b1, xv2.z + b2, xv2.w + b3);
+            for (int r = 0; r < R; r++) {
+                const float4 w = ork_wt[r * dim4 + j4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const long long row = row0 + q * rstep;
+                    const float yv = row < rows ? y[row * R + r] : 0.0f;
+                    a[q].x = __fmaf_rn(yv, w.x, a[q].x);
+                    a[q].y = __fmaf_rn(yv, w.y, a[q].y);
+                    a[q].z = __fmaf_rn(yv, w.z, a[q].z);
+                    a[q].w = __fmaf_rn(yv, w.w, a[q].w);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const long long row = row0 + q * rstep;
+                if (row < rows)
+                    out[row * dim4 + j4] = make_float4(xv[q].x + a[q].x, xv[q].y + a[q].y, xv[q].z + a[q].z,
+                                                       xv[q].w + a[q].w);
+            }
         }
     }
 }
