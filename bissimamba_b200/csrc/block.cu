@@ -58,132 +58,159 @@ __device__ __forceinline__ void stv(__nv_bfloat16* p, float v) { *p = __float2bf
 __device__ __forceinline__ float ldv(const float* p) { return *p; }
 __device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-// Forward epilogue over P[BL, Rt]; T = storage type of the scan inputs.  A CTA walks rows (rpi rows at a time,
-// tpr threads per row, grid-stride): thread j of a row writes B[j] and C[j] (coalesced row segments, no
-// per-element index division); the u / dt / lambda columns go to lane 0 of as many warps.
+// The epilogues below walk blocks of 32 rows (grid-stride over blocks, 256 threads).  The per-row columns
+// (u / dt / lambda and their gradients: R + 2 of them, each with an exp / log) are computed lane-parallel:
+// warp k takes column k of the block's 32 rows, one row per lane, so no warp carries them alone.  The wide
+// parts (B / C and their gradients) are copied by all threads as coalesced row segments, four rows in flight.
+constexpr int EPI_RB = 32;
+
+// Forward epilogue over P[BL, Rt]; T = storage type of the scan inputs.
 template <typename T>
-__global__ void block_fwd_epilogue(const float* __restrict__ P, long long BL, int R, int NR, float dt_min,
-                                   float dt_max, const float* __restrict__ bB, const float* __restrict__ bC,
-                                   T* __restrict__ u, T* __restrict__ dt, T* __restrict__ lam,
-                                   T* __restrict__ B, T* __restrict__ C) {
+__global__ void __launch_bounds__(256) block_fwd_epilogue(const float* __restrict__ P, long long BL, int R, int NR,
+                                                          float dt_min, float dt_max, const float* __restrict__ bB,
+                                                          const float* __restrict__ bC, T* __restrict__ u,
+                                                          T* __restrict__ dt, T* __restrict__ lam, T* __restrict__ B,
+                                                          T* __restrict__ C) {
     const int Rt = R + 2 + 2 * NR;
-    const int W = NR > R + 2 ? NR : R + 2;
-    const int tpr = W < (int)blockDim.x ? W : (int)blockDim.x, rpi = blockDim.x / tpr;
+    const int tpr = NR < 256 ? NR : 256, rpi = 256 / tpr;
     const int sub = threadIdx.x / tpr, c0 = threadIdx.x - sub * tpr;
-    if (sub >= rpi) return;
-    for (long long row = (long long)blockIdx.x * rpi + sub; row < BL; row += (long long)gridDim.x * rpi) {
-        const float* pr = P + row * Rt;
-        for (int j = c0; j < W; j += tpr) {
-            if (j < NR) {
-                stv(B + row * NR + j, pr[R + 2 + j] + bB[j]);
-                stv(C + row * NR + j, pr[R + 2 + NR + j] + bC[j]);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (long long r0 = (long long)blockIdx.x * EPI_RB; r0 < BL; r0 += (long long)gridDim.x * EPI_RB) {
+        const int nrow = BL - r0 < EPI_RB ? (int)(BL - r0) : EPI_RB;
+        if (sub < rpi) {
+#pragma unroll 4
+            for (int rr = sub; rr < nrow; rr += rpi) {
+                const long long row = r0 + rr;
+                const float* pr = P + row * Rt + R + 2;
+                for (int j = c0; j < NR; j += tpr) {
+                    stv(B + row * NR + j, pr[j] + bB[j]);
+                    stv(C + row * NR + j, pr[NR + j] + bC[j]);
+                }
             }
         }
-        // u / dt / lambda: column k on lane 0 of warp k of the row's threads (spread over warps)
-        for (int k = c0 >> 5; (c0 & 31) == 0 && k < R + 2; k += (tpr + 31) >> 5) {
-            const int j = k;
-            if (j < R) {
-                const float v = pr[j];
-                stv(u + row * R + j, v / (1.0f + expf(-v)));          // silu
-            } else if (j == R) {
-                float d = logf(1.0f + expf(pr[j]));                     // softplus
-                if (d < dt_min) d = dt_min;
-                if (d > dt_max) d = dt_max;
-                stv(dt + row, d);
-            } else if (j == R + 1) {
-                stv(lam + row, sigm(pr[j]));
+        if (lane < nrow) {
+            const long long row = r0 + lane;
+            for (int j = warp; j < R + 2; j += 8) {
+                const float v = P[row * Rt + j];
+                if (j < R) {
+                    stv(u + row * R + j, v / (1.0f + expf(-v)));          // silu
+                } else if (j == R) {
+                    float d = logf(1.0f + expf(v));                         // softplus
+                    if (d < dt_min) d = dt_min;
+                    if (d > dt_max) d = dt_max;
+                    stv(dt + row, d);
+                } else {
+                    stv(lam + row, sigm(v));
+                }
             }
         }
     }
+}
+
+// Gradient of the per-row column j < R + 2 of P (silu', softplus' inside the clamp, sigmoid')
+template <typename T>
+__device__ __forceinline__ float epi_grad_col(const float* __restrict__ P, const T* __restrict__ lamv, long long row,
+                                              int Rt, int R, int j, float dt_min, float dt_max,
+                                              const float* __restrict__ du, const float* __restrict__ ddt,
+                                              const float* __restrict__ dlam) {
+    if (j < R) {
+        const float z = P[row * Rt + j], s = sigm(z);
+        return du[row * R + j] * s * (1.0f + z * (1.0f - s));
+    }
+    if (j == R) {
+        // clamp test on the unrounded softplus (identical to the stored dt in fp32 mode)
+        const float z = P[row * Rt + j];
+        const float d = fminf(fmaxf(logf(1.0f + expf(z)), dt_min), dt_max);
+        return (d > dt_min && d < dt_max) ? ddt[row] * sigm(z) : 0.0f;
+    }
+    const float l = ldv(lamv + row);
+    return dlam[row] * l * (1.0f - l);
 }
 
 // Backward epilogue: dP[BL, Rt] from the scan gradients (O = float, or bf16
 // as the operand of the bf16 tensor-core gradient GEMMs).  dP rows have ldo >= Rt
-// columns; columns Rt .. ldo-1 are written as zero.  Rows are walked as in the
-// forward epilogue: thread j of a row writes dP[R + 2 + j] (from dB), dP[R + 2 + NR + j]
-// (from dC) and the padding column Rt + j; the columns j < R + 2 go to lane 0 of as many warps.
+// columns; columns Rt .. ldo-1 are written as zero.
 template <typename T, typename O>
-__global__ void block_bwd_epilogue(const float* __restrict__ P, const T* __restrict__ dtv,
-                                   const T* __restrict__ lamv, long long BL, int R, int NR, float dt_min,
-                                   float dt_max, const float* __restrict__ du, const float* __restrict__ ddt,
-                                   const float* __restrict__ dlam, const float* __restrict__ dB,
-                                   const float* __restrict__ dC, O* __restrict__ dP, int ldo) {
+__global__ void __launch_bounds__(256) block_bwd_epilogue(const float* __restrict__ P, const T* __restrict__ dtv,
+                                                          const T* __restrict__ lamv, long long BL, int R, int NR,
+                                                          float dt_min, float dt_max, const float* __restrict__ du,
+                                                          const float* __restrict__ ddt,
+                                                          const float* __restrict__ dlam,
+                                                          const float* __restrict__ dB,
+                                                          const float* __restrict__ dC, O* __restrict__ dP,
+                                                          int ldo) {
     const int Rt = R + 2 + 2 * NR, pad = ldo - Rt;
-    int W = NR > R + 2 ? NR : R + 2;
-    if (pad > W) W = pad;
-    const int tpr = W < (int)blockDim.x ? W : (int)blockDim.x, rpi = blockDim.x / tpr;
+    const int W = NR > pad ? NR : pad;
+    const int tpr = W < 256 ? W : 256, rpi = 256 / tpr;
     const int sub = threadIdx.x / tpr, c0 = threadIdx.x - sub * tpr;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     (void)dtv;
-    if (sub >= rpi) return;
-    for (long long row = (long long)blockIdx.x * rpi + sub; row < BL; row += (long long)gridDim.x * rpi) {
-        const float* pr = P + row * Rt;
-        O* dr = dP + row * ldo;
-        for (int j = c0; j < W; j += tpr) {
-            if (j < NR) {
-                stv(dr + R + 2 + j, dB[row * NR + j]);
-                stv(dr + R + 2 + NR + j, dC[row * NR + j]);
+    for (long long r0 = (long long)blockIdx.x * EPI_RB; r0 < BL; r0 += (long long)gridDim.x * EPI_RB) {
+        const int nrow = BL - r0 < EPI_RB ? (int)(BL - r0) : EPI_RB;
+        if (sub < rpi) {
+#pragma unroll 4
+            for (int rr = sub; rr < nrow; rr += rpi) {
+                const long long row = r0 + rr;
+                O* dr = dP + row * ldo;
+                for (int j = c0; j < W; j += tpr) {
+                    if (j < NR) {
+                        stv(dr + R + 2 + j, dB[row * NR + j]);
+                        stv(dr + R + 2 + NR + j, dC[row * NR + j]);
+                    }
+                    if (j < pad) stv(dr + Rt + j, 0.0f);
+                }
             }
-            if (j < pad) stv(dr + Rt + j, 0.0f);
         }
-        // columns j < R + 2: column k on lane 0 of warp k of the row's threads (spread over warps)
-        for (int k = c0 >> 5; (c0 & 31) == 0 && k < R + 2; k += (tpr + 31) >> 5) {
-            const int j = k;
-            if (j < R) {
-                const float z = pr[j], s = sigm(z);
-                stv(dr + j, du[row * R + j] * s * (1.0f + z * (1.0f - s)));   // silu'
-            } else if (j == R) {
-                // clamp test on the unrounded softplus (identical to the stored dt in fp32 mode)
-                const float z = pr[j];
-                const float d = fminf(fmaxf(logf(1.0f + expf(z)), dt_min), dt_max);
-                stv(dr + j, (d > dt_min && d < dt_max) ? ddt[row] * sigm(z) : 0.0f);   // softplus' inside the clamp
-            } else if (j == R + 1) {
-                const float l = ldv(lamv + row);
-                stv(dr + j, dlam[row] * l * (1.0f - l));
-            }
+        if (lane < nrow) {
+            const long long row = r0 + lane;
+            for (int j = warp; j < R + 2; j += 8)
+                stv(dP + row * ldo + j, epi_grad_col(P, lamv, row, Rt, R, j, dt_min, dt_max, du, ddt, dlam));
         }
     }
 }
 
-// The bf16 form of block_bwd_epilogue: 8 consecutive dP columns of one row per
-// thread (one 16-byte store), rows walked as above; ldo % 8 == 0 and a
-// 16-byte-aligned dP.  Same per-element arithmetic.
+// The bf16 form of block_bwd_epilogue: 8 consecutive dP columns per thread (one 16-byte store);
+// ldo % 8 == 0 and a 16-byte-aligned dP.  The chunks holding per-row columns (the first
+// ceil((R + 2) / 8)) are computed lane-parallel (warp k: chunk k of the block's rows, a row per lane);
+// the others are copies.  Same per-element arithmetic.
 template <typename T>
-__global__ void block_bwd_epilogue_v8(const float* __restrict__ P, const T* __restrict__ lamv, long long BL, int R,
-                                      int NR, float dt_min, float dt_max, const float* __restrict__ du,
-                                      const float* __restrict__ ddt, const float* __restrict__ dlam,
-                                      const float* __restrict__ dB, const float* __restrict__ dC,
-                                      __nv_bfloat16* __restrict__ dP, int ldo) {
-    const int Rt = R + 2 + 2 * NR, ch = ldo >> 3;
-    const int tpr = ch < (int)blockDim.x ? ch : (int)blockDim.x, rpi = blockDim.x / tpr;
+__global__ void __launch_bounds__(256) block_bwd_epilogue_v8(const float* __restrict__ P,
+                                                             const T* __restrict__ lamv, long long BL, int R,
+                                                             int NR, float dt_min, float dt_max,
+                                                             const float* __restrict__ du,
+                                                             const float* __restrict__ ddt,
+                                                             const float* __restrict__ dlam,
+                                                             const float* __restrict__ dB,
+                                                             const float* __restrict__ dC,
+                                                             __nv_bfloat16* __restrict__ dP, int ldo) {
+    const int Rt = R + 2 + 2 * NR, ch = ldo >> 3, nsc = (R + 2 + 7) >> 3;
+    const int W = ch - nsc;   // copy chunks per row
+    const int tpr = W < 256 ? (W < 1 ? 1 : W) : 256, rpi = 256 / tpr;
     const int sub = threadIdx.x / tpr, k0 = threadIdx.x - sub * tpr;
-    if (sub >= rpi) return;
-    for (long long row = (long long)blockIdx.x * rpi + sub; row < BL; row += (long long)gridDim.x * rpi)
-    for (int k = k0; k < ch; k += tpr) {
-    const int c0 = k * 8;
-    uint4 pk;
-    __nv_bfloat16* e = (__nv_bfloat16*)&pk;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    auto chunk = [&](long long row, int c0, bool special) {
+        uint4 pk;
+        __nv_bfloat16* e = (__nv_bfloat16*)&pk;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int col = c0 + j;
-        float g;
-        if (col >= Rt) {
-            g = 0.0f;
-        } else if (col >= R + 2) {
-            g = col < R + 2 + NR ? dB[row * NR + (col - R - 2)] : dC[row * NR + (col - R - 2 - NR)];
-        } else if (col < R) {
-            const float z = P[row * Rt + col], s = sigm(z);
-            g = du[row * R + col] * s * (1.0f + z * (1.0f - s));
-        } else if (col == R) {
-            const float z = P[row * Rt + col];
-            const float d = fminf(fmaxf(logf(1.0f + expf(z)), dt_min), dt_max);
-            g = (d > dt_min && d < dt_max) ? ddt[row] * sigm(z) : 0.0f;
-        } else {
-            const float l = ldv(lamv + row);
-            g = dlam[row] * l * (1.0f - l);
+        for (int j = 0; j < 8; j++) {
+            const int col = c0 + j;
+            float g;
+            if (col >= Rt) g = 0.0f;
+            else if (col >= R + 2) g = col < R + 2 + NR ? dB[row * NR + (col - R - 2)] : dC[row * NR + (col - R - 2 - NR)];
+            else g = special ? epi_grad_col(P, lamv, row, Rt, R, col, dt_min, dt_max, du, ddt, dlam) : 0.0f;
+            e[j] = __float2bfloat16_rn(g);
         }
-        e[j] = __float2bfloat16_rn(g);
-    }
-    *(uint4*)(dP + row * ldo + c0) = pk;
+        *(uint4*)(dP + row * ldo + c0) = pk;
+    };
+    for (long long r0 = (long long)blockIdx.x * EPI_RB; r0 < BL; r0 += (long long)gridDim.x * EPI_RB) {
+        const int nrow = BL - r0 < EPI_RB ? (int)(BL - r0) : EPI_RB;
+        if (sub < rpi && W > 0) {
+#pragma unroll 2
+            for (int rr = sub; rr < nrow; rr += rpi)
+                for (int k = nsc + k0; k < ch; k += tpr) chunk(r0 + rr, k * 8, false);
+        }
+        if (lane < nrow)
+            for (int k = warp; k < nsc; k += 8) chunk(r0 + lane, k * 8, true);
     }
 }
 
@@ -292,23 +319,17 @@ cudaError_t launch_pack_wcat_t(const float* Win, const float* dp, const float* l
 
 static inline unsigned nb(long long n, int t) { return (unsigned)((n + t - 1) / t); }
 
-// Grid of the row-walking epilogues: rows / (rows per CTA pass), at most 8 CTAs of 256 threads per SM
-static unsigned row_grid(long long rows, int per_row) {
+// Grid of the epilogues: one CTA per 32-row block, at most 8 CTAs of 256 threads per SM (grid-stride)
+static unsigned epi_grid(long long rows) {
     static int sms = 0;
     if (!sms) {
         int dev = 0;
         cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
     }
-    const int tpr = per_row < 256 ? (per_row < 1 ? 1 : per_row) : 256, rpi = 256 / tpr;
-    long long g = (rows + rpi - 1) / rpi;
+    long long g = (rows + EPI_RB - 1) / EPI_RB;
     if (g > 8LL * sms) g = 8LL * sms;
     return (unsigned)(g < 1 ? 1 : g);
-}
-static int epi_width(int R, long long NR, long long pad = 0) {
-    long long w = NR > R + 2 ? NR : R + 2;
-    if (pad > w) w = pad;
-    return (int)w;
 }
 
 static int check_cfg(const KMBlockConfig* c, const KMBlockWeights* w, long batch) {
@@ -384,14 +405,14 @@ extern "C" int kmb_block_forward(const KMBlockConfig* c, const KMBlockWeights* w
         to_bf16<<<nb(a.Rt * dim, 256), 256, 0, st>>>(W, Wb, a.Rt * dim);
         if ((e = mm_nt(true, a.BL, a.Rt, dim, x, dim, Wb, dim, act + a.proj, a.Rt, false, st)) != cudaSuccess)
             return set_cuda_error("bf16 projection GEMM", e);
-        block_fwd_epilogue<H><<<row_grid(a.BL, epi_width((int)c->R, a.NR)), 256, 0, st>>>(
+        block_fwd_epilogue<H><<<epi_grid(a.BL), 256, 0, st>>>(
             act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, (H*)(act + a.u),
             (H*)(act + a.dt), (H*)(act + a.lam), (H*)(act + a.B), (H*)(act + a.C));
     } else {
         // P[BL, Rt] = X[BL, dim] . Wcat^T on the tensor cores at fp32 accuracy (3xTF32)
         if ((e = mm_nt(false, a.BL, a.Rt, dim, x, dim, W, dim, act + a.proj, a.Rt, false, st)) != cudaSuccess)
             return set_cuda_error("projection GEMM", e);
-        block_fwd_epilogue<float><<<row_grid(a.BL, epi_width((int)c->R, a.NR)), 256, 0, st>>>(
+        block_fwd_epilogue<float><<<epi_grid(a.BL), 256, 0, st>>>(
             act + a.proj, a.BL, (int)c->R, (int)a.NR, c->dt_min, c->dt_max, w->b_B, w->b_C, act + a.u, act + a.dt,
             act + a.lam, act + a.B, act + a.C);
     }
@@ -462,7 +483,7 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
     sg.dA_log = g->A_log; sg.dtheta = g->theta;
     // du, ddt, dlambda, dB, dC are assigned (no clearing of the scratch first)
     if (kmb_blockscan_backward_ex(&p, batch, S + s_dy, &sg, 1, stream)) return -1;
-    block_bwd_epilogue<float, float><<<row_grid(BL, epi_width(R, NR, ldq - Rt)), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
+    block_bwd_epilogue<float, float><<<epi_grid(BL), 256, 0, st>>>(act + a.proj, act + a.dt, act + a.lam, BL, R,
                                                                      (int)NR, c->dt_min, c->dt_max, S + s_du,
                                                                      S + s_ddt, S + s_dlam, S + s_dB, S + s_dC,
                                                                      S + s_dP, (int)ldq);
@@ -550,7 +571,7 @@ static int block_backward_bf16(const KMBlockConfig* c, const KMBlockWeights* w, 
     // du, ddt, dlambda, dB, dC are assigned (no clearing of the scratch first)
     if (kmb_blockscan_backward_ex(&p, batch, S + s_dy, &sg, 1, stream)) return -1;
     // ldp is a multiple of 16 and dPb 256-byte aligned: the 8-column form applies
-    block_bwd_epilogue_v8<H><<<row_grid(BL, (int)(ldp / 8)), 256, 0, st>>>(
+    block_bwd_epilogue_v8<H><<<epi_grid(BL), 256, 0, st>>>(
         act + a.proj, (const H*)(act + a.lam), BL, R, (int)NR, c->dt_min, c->dt_max, S + s_du, S + s_ddt,
         S + s_dlam, S + s_dB, S + s_dC, dPb, ldp);
     if ((e = cudaGetLastError()) != cudaSuccess) return set_cuda_error("block bwd epilogue", e);
