@@ -74,7 +74,7 @@ def parse():
     ap.add_argument("--D", type=int, default=D)
     ap.add_argument("--M", type=int, default=M)
     ap.add_argument("--workload", default="scan_fwd",
-                    choices=["scan_fwd", "scan_fwd_c0", "scan_fwd_c1", "scan_fwd_3d", "scan_bwd", "scan_bwd_c1", "convnd2d",
+                    choices=["scan_fwd", "scan_fwd_c0", "scan_fwd_c1", "scan_fwd_3d", "scan_bwd", "scan_bwd_c1", "scan_bwd_3d", "convnd2d",
                              "convnd3d", "block", "block_bf16", "model", "all"],
                     help="scan_fwd = the headline line; the others measure the other BASELINE configs "
                          "(all = every other one, one line each)")
@@ -460,7 +460,7 @@ def main():
 # own CPU code on a bounded sample, rank 0 at N=1) and e2e (host buffers, the
 # H2D copies of the step's inputs and the D2H copies of its results inside the
 # timed region).  `--workload all` prints every line.
-OTHER = ("scan_fwd_c0", "scan_fwd_c1", "scan_fwd_3d", "scan_bwd", "scan_bwd_c1", "convnd2d", "convnd3d", "block", "block_bf16",
+OTHER = ("scan_fwd_c0", "scan_fwd_c1", "scan_fwd_3d", "scan_bwd", "scan_bwd_c1", "scan_bwd_3d", "convnd2d", "convnd3d", "block", "block_bf16",
          "model")
 
 
@@ -631,6 +631,8 @@ def wl_scan_bwd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, wor
         B_ = args.batch   # 32 unless --batch overrides it (profiling)
         dims, D_, M_, rope = (64, 64), 512, 64, False
         name = f"scannd_bwd_2d64x64_D512_M64_b{B_} (headline geometry)"
+    elif which == "scan_bwd_3d":
+        dims, D_, M_, B_, rope, name = (16, 32, 32), 512, 64, 2, True, "scannd_bwd_3d16x32x32_D512_M64_b2_rope"
     else:
         dims, D_, M_, B_, rope, name = (32, 32), 64, 16, 8, True, "scannd_bwd_2d32x32_D64_M16_b8_rope (config 1)"
     P_, nd = int(np.prod(dims)), len(dims)
@@ -648,7 +650,7 @@ def wl_scan_bwd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, wor
     dx = torch.zeros(B_, P_, D_, device=dev)
     pb = kmb.scan_params(list(dims), D_, M_, t["x"], t["A"], t["B"], t["C"], t["delta"], h, dy, theta=t["theta"],
                          grads=gr)
-    steps = max(args.steps // 6, 5) if which == "scan_bwd" else max(args.steps, 20)
+    steps = max(args.steps // 6, 5) if which != "scan_bwd_c1" else max(args.steps, 20)
     call = lambda: kmb.check(lib.scannd_backward_async(C.byref(pb), B_, dx.data_ptr(), sp))
     ms = _timed(call, steps, max(args.warmup, 3), stream)
     path = lib.kmb_last_backward_path()
@@ -660,12 +662,12 @@ def wl_scan_bwd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, wor
     line = {"metric": "scanND backward state-updates/sec", "value": upd * world / tt, "unit": "state-updates/s",
             "ms_per_step": ms / steps, "steps": steps,
             "config": {"workload": name, "semantics": "accumulate (+=) into every gradient, as the reference",
-                       "l2": "inputs >> L2" if which == "scan_bwd" else "inputs ~ L2 size"},
+                       "l2": "inputs ~ L2 size" if which == "scan_bwd_c1" else "inputs >> L2"},
             "roofline": {"bound": "hbm", "achieved": round(alg / tt / 1e9, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(alg / tt / 1e9 / peak, 4), "peak_source": peak_src, "traffic": None,
                          "alg_bytes_per_launch": alg,
                          "kernel": {2: "scan_bwd_strips", 1: "scan_bwd_wave", 0: "scan_bwd_generic"}.get(path)},
-            "gpu_launches": steps * (5 if M_ == 64 else 4)}
+            "gpu_launches": steps * {2: 5 if M_ == 64 else 4, 1: 2 + 3 * max(M_ // 32, 1)}.get(path, 4)}
     # the same step with overwrite semantics (scannd_backward_ex): no read-back of the gradients
     ovw = lambda: kmb.check(lib.scannd_backward_ex(C.byref(pb), B_, dx.data_ptr(), 1, sp))
     ms_o = _timed(ovw, steps, 2, stream)
@@ -687,7 +689,7 @@ def wl_scan_bwd(args, dev, stream, lib, kmb, g, which, peak, peak_src, rank, wor
     line["e2e"]["batch_per_gpu"] = eb
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import pyoracle as po
-        d_s = 4 if which == "scan_bwd" else D_
+        d_s = D_ if which == "scan_bwd_c1" else 4
         inp = po.gen_scan(list(dims), d_s, M_, batch=1, seed=3, rope=rope)
         hs, _ = po.oracle_scannd(inp)
         dys = np.random.default_rng(1).standard_normal((1, P_, d_s)).astype(np.float32)
@@ -930,7 +932,7 @@ def run_other_workload(args, rank, world):
     names = OTHER if args.workload == "all" else (args.workload,)
     fns = {"scan_fwd_c0": wl_scan_fwd_small, "scan_fwd_c1": wl_scan_fwd_small, "scan_fwd_3d": wl_scan_fwd_3d,
            "scan_bwd": wl_scan_bwd,
-           "scan_bwd_c1": wl_scan_bwd, "convnd2d": wl_convnd, "convnd3d": wl_convnd, "block": wl_block,
+           "scan_bwd_c1": wl_scan_bwd, "scan_bwd_3d": wl_scan_bwd, "convnd2d": wl_convnd, "convnd3d": wl_convnd, "block": wl_block,
            "block_bf16": wl_block, "model": wl_model}
     for name in names:
         g = torch.Generator(device=dev)

@@ -1,5 +1,6 @@
 // scannd_bwd.cu -- exact Scan-A adjoint, parallel over the points of each
-// wavefront level (any ndims <= 4, M a power of two <= 32).
+// wavefront level (any ndims <= 4; M a power of two <= 32, or a multiple of 32
+// run as state tiles of 32, one launch per tile in order).
 //
 // Grid: one CTA per (item, channel group); a group is the RoPE pair
 // (2g, 2g+1) when theta is set, one channel otherwise.  Threads are
@@ -15,7 +16,10 @@
 // a_k(s), beta(s) are recomputed from delta(s), lambda(s).  No atomics: dA,
 // dtheta and dlambda leave per-(item, group) partials that fixed-order
 // reductions add into the outputs.  Reads B, C, h, x, delta, dy; writes G and
-// accumulates dB, dC, ddelta, dx.
+// accumulates dB, dC, ddelta, dx.  The states of a point are independent
+// except for the sums over m (ddelta, dx, dlambda, dtheta), so M > 32 runs
+// tiles of 32 states one after another: each tile adds its partial sums, in
+// tile order (deterministic).
 #include <vector>
 #include "kmb_common.cuh"
 
@@ -29,7 +33,8 @@ __global__ void reduce_lambda(const float* __restrict__ plam, float* __restrict_
                               long long P);
 
 struct WaveBwd {
-    int D, M, has_lambda, fast, clamp;
+    int D, M, has_lambda, fast, clamp;   // M: states of this launch (the tile)
+    int MF, m0;                          // all states (the layout's stride) and the tile's first state
     float amin, deflam;
     long long P;
     int dims[4], strides[4];
@@ -47,7 +52,7 @@ struct WaveBwd {
 // latency; the small register spill costs less than that gains.
 template <int ND, bool ROPE>
 __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
-    const int D = w.D, M = w.M;
+    const int D = w.D, M = w.M, MF = w.MF, m0 = w.m0;
     const int ngroups = ROPE ? (D + 1) / 2 : D;
     const int b = blockIdx.x / ngroups, g = blockIdx.x % ngroups;
     const int c0 = ROPE ? 2 * g : g;
@@ -56,8 +61,8 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
     const int tid = threadIdx.x, m = tid % M, slot = tid / M;
     const int nslots = blockDim.x / M;
     // item bases in 64-bit; indices inside an item in 32-bit (P * D * M < 2^31, checked by the launcher)
-    const long long P = w.P, DM = (long long)D * M;
-    const int Pi = (int)P, DMi = D * M;
+    const long long P = w.P, DM = (long long)D * MF;
+    const int Pi = (int)P, DMi = D * MF;
     const float* __restrict__ x = w.x + b * P * D;
     const float* __restrict__ Bp = w.B + b * P * DM;
     const float* __restrict__ Cp = w.C + b * P * DM;
@@ -77,7 +82,7 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
     for (int k = 0; k < ND; k++)
 #pragma unroll
         for (int c = 0; c < 2; c++) {
-            const float a = (c < nc) ? w.A[((long long)k * D + c0 + c) * M + m] : 0.0f;
+            const float a = (c < nc) ? w.A[((long long)k * D + c0 + c) * MF + m0 + m] : 0.0f;
             clk[k][c] = w.clamp && a > w.amin;
             Ak[k][c] = clk[k][c] ? w.amin : a;
         }
@@ -126,15 +131,15 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
                                 if (k2 == k) alk = a;
                             }
                         }
-                        const float Gs = G[s * DMi + (c0 + c) * M + m];
+                        const float Gs = G[s * DMi + (c0 + c) * MF + m0 + m];
                         const float beta = (1.0f - lams) * dts * (sal / (float)ns);
                         ah[c] += alk * Gs;
                         ab[c] += beta / (float)ns * Gs;
                     }
                 }
                 float gh[2];
-                const int o = p * DMi + c0 * M + m;
-                const float h0 = hp[o], h1 = rot ? hp[o + M] : 0.0f;
+                const int o = p * DMi + c0 * MF + m0 + m;
+                const float h0 = hp[o], h1 = rot ? hp[o + MF] : 0.0f;
                 if (rot) {
                     gh[0] = cth * ah[0] + sth * ah[1];
                     gh[1] = -sth * ah[0] + cth * ah[1];
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     if (c >= nc) continue;
-                    const int oc = o + c * M;
+                    const int oc = o + c * MF;
                     const int d = c0 + c;
                     const float dyv = dyp[p * D + d];
                     const float hv = c ? h1 : h0;
@@ -177,12 +182,12 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
                             hat[k] = 0.0f;
                             if (!((nb >> k) & 1)) continue;
                             const int q = p - w.strides[k];
-                            const int oq = q * DMi + c0 * M + m;
+                            const int oq = q * DMi + c0 * MF + m0 + m;
                             al[k] = kmb_exp(dk[k] * Ak[k][c], w.fast);
                             sal += al[k];
-                            sbu += Bp[oq + c * M] * x[q * D + d];
+                            sbu += Bp[oq + c * MF] * x[q * D + d];
                             if (rot) {
-                                const float q0 = hp[oq], q1 = hp[oq + M];
+                                const float q0 = hp[oq], q1 = hp[oq + MF];
                                 hat[k] = c ? sth * q0 + cth * q1 : cth * q0 - sth * q1;
                             } else {
                                 hat[k] = hp[oq];
@@ -243,7 +248,7 @@ __global__ void __launch_bounds__(512, 2) scan_bwd_wave(WaveBwd w) {
             if (slot == 0 && c < nc) {
                 float acc = 0.0f;
                 for (int s2 = 0; s2 < nslots; s2++) acc += red[s2 * M + m];
-                w.pA[(((long long)b * ND + k) * D + c0 + c) * M + m] = acc;
+                w.pA[(((long long)b * ND + k) * D + c0 + c) * MF + m0 + m] = acc;
             }
             __syncthreads();
         }
@@ -276,7 +281,9 @@ size_t scan_bwd_wave_scratch_bytes(const ScanDesc& s) {
 // cudaErrorNotSupported when the shape is outside the kernel's envelope.
 cudaError_t launch_scan_bwd_wave(const ScanDesc& s, const float* dy, float* dA, float* dB, float* dC, float* ddelta,
                                  float* dlambda, float* dtheta, float* dx, void* scratch, cudaStream_t st) {
-    if (s.nd < 1 || s.nd > 4 || s.M > 32 || (s.M & (s.M - 1)) != 0 || s.P > 0x7fffffffLL || s.batch * s.D > 0x7fffffffLL ||
+    const bool tiles = s.M > 32 && s.M % 32 == 0;
+    if (s.nd < 1 || s.nd > 4 || (!tiles && (s.M > 32 || (s.M & (s.M - 1)) != 0)) || s.P > 0x7fffffffLL ||
+        s.batch * s.D > 0x7fffffffLL ||
         s.P * s.D * s.M * s.nd >= (1LL << 31))   // 32-bit indexing inside an item
         return cudaErrorNotSupported;
     std::vector<long> dims(s.dims, s.dims + s.nd);
@@ -285,7 +292,8 @@ cudaError_t launch_scan_bwd_wave(const ScanDesc& s, const float* dy, float* dA, 
     if (device_plan(dims, (long)s.P, &plan, &nlev, st)) return cudaErrorUnknown;
     WaveBwd w;
     memset(&w, 0, sizeof w);
-    w.D = s.D; w.M = s.M; w.has_lambda = s.has_lambda; w.fast = s.fast_exp; w.clamp = s.clamp;
+    const int Mt = tiles ? 32 : s.M;
+    w.D = s.D; w.M = Mt; w.MF = s.M; w.m0 = 0; w.has_lambda = s.has_lambda; w.fast = s.fast_exp; w.clamp = s.clamp;
     w.amin = s.a_log_min; w.deflam = s.default_lambda; w.P = s.P;
     for (int k = 0; k < s.nd; k++) { w.dims[k] = (int)s.dims[k]; w.strides[k] = (int)s.strides[k]; }
     w.nlev = nlev; w.lev_start = plan; w.lev_pts = plan + nlev + 1;
@@ -299,27 +307,32 @@ cudaError_t launch_scan_bwd_wave(const ScanDesc& s, const float* dy, float* dA, 
     w.pA = (float*)c; c = align(c + (size_t)s.batch * s.nd * s.D * s.M * 4);
     w.pth = (float*)c; c = align(c + (size_t)s.batch * (s.D / 2 + 1) * 4);
     w.plam = (float*)c;
-    // threads: up to 512, whole points (multiples of M), at least one warp
-    int threads = 512 / s.M * s.M;
+    // threads: up to 512, whole points (multiples of the tile's M), at least one warp
+    int threads = 512 / Mt * Mt;
     if (threads < 32) threads = 32;
-    cudaError_t e;
-    switch (s.nd) {
-        case 1: e = wave_launch<1>(w, s.rope, s.batch, threads, st); break;
-        case 2: e = wave_launch<2>(w, s.rope, s.batch, threads, st); break;
-        case 3: e = wave_launch<3>(w, s.rope, s.batch, threads, st); break;
-        default: e = wave_launch<4>(w, s.rope, s.batch, threads, st); break;
-    }
-    if (e != cudaSuccess) return e;
     auto nb = [](long long n) { return (unsigned)((n + 255) / 256); };
+    // one launch per state tile, in order; each adds its sums over m (ddelta, dx by one atomic addition per
+    // element and launch; dtheta, dlambda through their partials, reduced before the next tile's launch)
+    for (int m0 = 0; m0 < s.M; m0 += Mt) {
+        w.m0 = m0;
+        cudaError_t e;
+        switch (s.nd) {
+            case 1: e = wave_launch<1>(w, s.rope, s.batch, threads, st); break;
+            case 2: e = wave_launch<2>(w, s.rope, s.batch, threads, st); break;
+            case 3: e = wave_launch<3>(w, s.rope, s.batch, threads, st); break;
+            default: e = wave_launch<4>(w, s.rope, s.batch, threads, st); break;
+        }
+        if (e != cudaSuccess) return e;
+        if (dtheta && s.rope && s.D >= 2) {
+            const long long cnt = s.D / 2;
+            reduce_rows_add<<<nb(cnt), 256, 0, st>>>(w.pth, dtheta, cnt, s.batch, cnt);
+        }
+        if (dlambda) reduce_lambda<<<nb(s.batch * s.P), 256, 0, st>>>(w.plam, dlambda, s.batch, (int)ngroups, s.P);
+    }
     if (dA) {
         const long long cnt = (long long)s.nd * s.D * s.M;
         reduce_rows_add<<<nb(cnt), 256, 0, st>>>(w.pA, dA, cnt, s.batch, cnt);
     }
-    if (dtheta && s.rope && s.D >= 2) {
-        const long long cnt = s.D / 2;
-        reduce_rows_add<<<nb(cnt), 256, 0, st>>>(w.pth, dtheta, cnt, s.batch, cnt);
-    }
-    if (dlambda) reduce_lambda<<<nb(s.batch * s.P), 256, 0, st>>>(w.plam, dlambda, s.batch, (int)ngroups, s.P);
     return cudaGetLastError();
 }
 

@@ -201,15 +201,19 @@ def test_backward_strips(kmb, cuda, dims, D, M, flags):
 
 
 @pytest.mark.parametrize("dims,D,M,flags,path", [
-    ([5, 3], 4, 64, dict(fast_exp=True, clamp=True, a_log_min=-2.0), 0),   # polynomial exp: generic
+    ([5, 3], 4, 64, dict(fast_exp=True, clamp=True, a_log_min=-2.0), 1),   # polynomial exp: level kernel, 2 tiles
     ([4, 70], 4, 16, {}, 1),                                              # inner extent > 64: level kernel
-    ([3, 4, 5], 4, 64, dict(rope=True), 0),                               # 3D, M = 64: generic
-])
+    ([3, 4, 5], 4, 64, dict(rope=True), 1),                               # 3D, M = 64: two state tiles
+    ([3, 4, 5], 6, 96, dict(rope=True, lam=True), 1),                     # 3D, M = 96: three state tiles
+    ([2, 3, 2, 3], 4, 64, dict(lam=True), 1),                             # 4D, M = 64
+    ([3, 4, 5], 4, 48, dict(rope=True), 0),                               # M neither a power of two <= 32 nor
+])                                                                        # a multiple of 32: generic
 def test_backward_fallback_paths(kmb, cuda, dims, D, M, flags, path):
     _check_backward(dims, D, M, flags, cuda, expect_path=path)
 
 
-@pytest.mark.parametrize("dims,D,M,flags", [([12, 20], 4, 64, dict(rope=True, lam=True)), ([6, 5], 6, 4, dict(rope=True))])
+@pytest.mark.parametrize("dims,D,M,flags", [([12, 20], 4, 64, dict(rope=True, lam=True)), ([6, 5], 6, 4, dict(rope=True)),
+                                            ([4, 5, 6], 4, 64, dict(rope=True, lam=True))])
 def test_backward_overwrite_and_determinism(kmb, cuda, dims, D, M, flags):
     """scannd_backward_ex(overwrite=1) assigns every output (buffers full of
     garbage beforehand give the same bits as accumulating into zeros), and two
