@@ -301,6 +301,8 @@ cudaError_t launch_dx_tc(const __nv_bfloat16* dP, int ldp, const float* Win, con
 // matrix products of the block (block_gemm.cu): tensor cores for the large ones, own kernels for rank R
 cudaError_t mm_nt(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
                   long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st);
+cudaError_t mm_nt_same_a(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
+                         long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st);
 cudaError_t mm_tn(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
                   long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st);
 cudaError_t rank_rows(bool bf16, const void* X, const float* W, long long rows, int dim, int R, float* out,
@@ -506,7 +508,8 @@ static int block_backward_f32(const KMBlockConfig* c, const KMBlockWeights* w, c
         // past column Rt read zeros)
         if ((e = gemm_transpose_f32(W, S + s_WT, Rt, dim, dim, ldq, st)) != cudaSuccess)
             return set_cuda_error("Wcat^T", e);
-        if ((e = mm_nt(false, BL, dim, Rt, S + s_dP, ldq, S + s_WT, ldq, dx, dim, true, st)) != cudaSuccess)
+        // dP's pieces from the dWcat product above are still in the workspace: not split again
+        if ((e = mm_nt_same_a(false, BL, dim, Rt, S + s_dP, ldq, S + s_WT, ldq, dx, dim, true, st)) != cudaSuccess)
             return set_cuda_error("dx GEMM", e);
     }
     return 0;

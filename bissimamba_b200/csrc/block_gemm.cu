@@ -351,10 +351,21 @@ cudaError_t rank_bwd(bool bf16, const void* X, const float* W, const float* Y, l
 
 static int npieces(int kind) { return kind == KIND_BF16_ ? 1 : kind == KIND_TF32X3_ ? 2 : 3; }
 
+// What the last split of this host thread left in the A / B piece workspaces
+struct PieceKey {
+    const float* x;
+    long long rows, cols, ldx, ldo;
+    int kind;
+    const void* buf;
+};
+static thread_local PieceKey tl_pieces[2];
+
 // The pieces of the fp32 matrix x [rows, cols] (stride ldx) in workspace `slot`, row stride ldo
-// (a multiple of 8 elements, so rows are 16-byte aligned for either element size).
+// (a multiple of 8 elements, so rows are 16-byte aligned for either element size).  With `unchanged`
+// (the caller guarantees x was not written since this thread's previous split of it), pieces still in
+// the workspace from a split of the same matrix in the same layout are used as they are.
 static cudaError_t make_pieces(int kind, int slot, const float* x, long long rows, long long cols, long long ldx,
-                               long long ldo, GemmOperand& op, cudaStream_t st) {
+                               long long ldo, GemmOperand& op, cudaStream_t st, bool unchanged = false) {
     const int np = npieces(kind);
     const size_t esz = kind == KIND_TF32X3_ ? 4 : 2;
     const size_t one = ((size_t)rows * ldo * esz + 255) & ~(size_t)255;
@@ -363,7 +374,15 @@ static cudaError_t make_pieces(int kind, int slot, const float* x, long long row
     void* out[3] = {w, np > 1 ? w + one : nullptr, np > 2 ? w + 2 * one : nullptr};
     for (int p = 0; p < 3; p++) op.p[p] = out[p];
     op.ld = ldo;
-    return gemm_split(kind, x, out, rows, cols, ldx, ldo, st);
+    PieceKey& key = tl_pieces[slot == WS_GEMM_A ? 0 : 1];
+    const PieceKey now{x, rows, cols, ldx, ldo, kind, w};
+    if (unchanged && key.x == now.x && key.rows == rows && key.cols == cols && key.ldx == ldx && key.ldo == ldo &&
+        key.kind == kind && key.buf == w)
+        return cudaSuccess;
+    key = PieceKey{};
+    const cudaError_t e = gemm_split(kind, x, out, rows, cols, ldx, ldo, st);
+    if (e == cudaSuccess) key = now;
+    return e;
 }
 
 static cudaError_t simt_nt(bool bf16, long long M, long long N, long long K, const void* A, long long lda,
@@ -385,7 +404,7 @@ static inline long long round8(long long v) { return (v + 7) & ~7LL; }
 // KIND_SIMT_ for the CUDA-core kernel).  A [M, K] (lda), B [N, K] (ldb).
 static cudaError_t mm_nt_kind(int kind, bool bf16, long long M, long long N, long long K, const void* A,
                               long long lda, const void* B, long long ldb, float* D, long long ldd, bool accumulate,
-                              cudaStream_t st) {
+                              cudaStream_t st, bool a_unchanged = false) {
     int* status = device_status();
     cudaError_t e = cudaErrorNotSupported;
     if (status && (bf16 || kind != KIND_SIMT_)) {
@@ -395,7 +414,8 @@ static cudaError_t mm_nt_kind(int kind, bool bf16, long long M, long long N, lon
         } else {
             GemmOperand a{}, b{};
             const long long ldk = round8(K);
-            if ((e = make_pieces(kind, WS_GEMM_A, (const float*)A, M, K, lda, ldk, a, st)) != cudaSuccess) return e;
+            if ((e = make_pieces(kind, WS_GEMM_A, (const float*)A, M, K, lda, ldk, a, st, a_unchanged)) != cudaSuccess)
+                return e;
             if ((e = make_pieces(kind, WS_GEMM_B, (const float*)B, N, K, ldb, ldk, b, st)) != cudaSuccess) return e;
             e = gemm_tc(kind, accumulate ? 1 : 0, M, N, K, a, b, D, ldd, 1, 0, status, st);
         }
@@ -409,6 +429,13 @@ static cudaError_t mm_nt_kind(int kind, bool bf16, long long M, long long N, lon
 cudaError_t mm_nt(bool bf16, long long M, long long N, long long K, const void* A, long long lda, const void* B,
                   long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st) {
     return mm_nt_kind(g_f32_kind, bf16, M, N, K, A, lda, B, ldb, D, ldd, accumulate, st);
+}
+
+// mm_nt whose A the previous product of this thread split in the same layout (an mm_tn's A [K, M] split
+// rows = K is the same matrix as an mm_nt's A [M, K]) and nothing wrote since: its pieces are reused.
+cudaError_t mm_nt_same_a(bool bf16, long long M, long long N, long long K, const void* A, long long lda,
+                         const void* B, long long ldb, float* D, long long ldd, bool accumulate, cudaStream_t st) {
+    return mm_nt_kind(g_f32_kind, bf16, M, N, K, A, lda, B, ldb, D, ldd, accumulate, st, true);
 }
 
 // D[M, N] (+)= A^T B with A [K, M] (lda), B [K, N] (ldb).  K is split over
